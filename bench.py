@@ -1,0 +1,363 @@
+"""Benchmark: batch-1 greedy decode of the synthetic 4B Q4_0 model on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl spark|reference]
+
+Workload: 36 layers, hidden 2560, 32 q / 8 kv heads of 128,
+SwiGLU 9728, vocab 151936, random N(0, 0.02) weights quantized to Q4_0, a prompt of
+2048 uniform-random token ids, then greedy decode.  One "step" is one decode token
+(one CUDA-graph replay of the whole model).  The K timed steps run at context
+2048 .. 2048+K-1 (the default K = 4096 is the reference's 4096-token protocol).
+
+Printed (rank 0, one JSON line): decode tokens/s (whole job), ms per step (TPOT),
+e2e tokens/s through the public API with a host<->device token copy every step,
+the roofline of the dominant kernel (Q4 gate_up GEMV) against the measured HBM
+peak, the whole-step roofline (weights + KV bytes / TPOT), clocks sampled during the
+timed region, and the CPU baseline (the C oracle on the host cores).
+
+Multi-GPU (torchrun): every rank decodes its own replica (no collective on the data
+path; "scaling": "weak"); timing is the max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (str(ROOT), str(ROOT / "spark-vllm-ascend_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "batch-1 decode tokens/s (synthetic 4B Q4_0, ctx 2048->2048+K)"
+PROMPT_LEN = 2048
+
+
+def _peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+        self.t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.t = threading.Thread(target=self._read, daemon=True)
+        self.t.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.t:
+            self.t.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[3:7]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def build_engine(args, device, seed):
+    import torch
+    from spark_b200.config import SparkConfig
+    from spark_b200.model import DecodeEngine, SyntheticWeights
+    cfg = SparkConfig()
+    w = SyntheticWeights(cfg, device=device, seed=seed)
+    max_seq = PROMPT_LEN + max(args.steps, args.warmup) + 1
+    eng = DecodeEngine(w, max_seq_len=max_seq, splits=args.splits, num_blocks=(max_seq + 127) // 128 + 8,
+                       max_steps=max(max_seq, args.steps + args.warmup + 8), seed=seed)
+    torch.cuda.synchronize()
+    return cfg, w, eng
+
+
+def time_kernels(eng, reps: int = 3) -> dict:
+    """Per-kernel average device time, each kernel replayed over all 36 layers' weights
+    (cold L2: 36 distinct weight sets) inside a CUDA graph, timed with CUDA events."""
+    import torch
+    calls = eng._calls
+    by_name: dict[str, list] = {}
+    for fn, name, a in calls:
+        by_name.setdefault(name, []).append((fn, a))
+    out = {}
+    stream = torch.cuda.Stream()
+    for name in ("qkv", "attn", "combine", "o_proj", "gate_up", "down", "head"):
+        seq = by_name[name]
+        if name == "head":
+            seq = seq * 8
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            for fn, a in seq:  # warm
+                fn(*a, torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g, stream=stream):
+            for fn, a in seq:
+                fn(*a, torch.cuda.current_stream().cuda_stream)
+        best = None
+        for _ in range(reps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(stream):
+                e0.record()
+                g.replay()
+                e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / len(seq)
+            best = ms if best is None else min(best, ms)
+        out[name] = best * 1e3  # us per launch
+        del g
+    # the key / token state was disturbed by the head replays: reset by caller
+    return out
+
+
+def kernel_bytes(cfg, ctx: int) -> dict:
+    h, i, nq, nkv, D = cfg.hidden_size, cfg.intermediate_size, cfg.num_q_heads, cfg.num_kv_heads, cfg.head_dim
+    q4 = lambda n, k: n * k // 32 * 18  # noqa: E731
+    return {
+        "qkv": q4(cfg.qkv_rows, h) + 2 * h * 3 + nq * D * 2 + 2 * nkv * D * 2,
+        "attn": 2 * ctx * nkv * D * 2 + nq * D * 2,
+        "o_proj": q4(h, nq * D) + nq * D * 2 + h * 2,
+        "gate_up": q4(2 * i, h) + 3 * h * 2 + i * 2,
+        "down": q4(h, i) + i * 2 + h * 2,
+        "head": q4(cfg.vocab_size, h) + 2 * h * 2 + cfg.vocab_size * 2,
+    }
+
+
+def cpu_baseline(eng, w, cfg, n_tokens: int, threads: int) -> dict:
+    """The C oracle (a restatement of the reference's CPU path) timed on the host cores:
+    decode steps at context 2048 from the GPU's prefilled KV cache."""
+    import numpy as np
+    import oracle
+    oracle.set_threads(threads)
+    om = oracle.OracleModel(cfg, w.to_numpy(), num_blocks=eng.num_blocks, splits=eng.splits)
+    om.kc[...] = eng.k_cache.view(__import__("torch").int16).cpu().numpy().view(np.uint16)
+    om.vc[...] = eng.v_cache.view(__import__("torch").int16).cpu().numpy().view(np.uint16)
+    table = eng.block_table.cpu().numpy()
+    tok = 1
+    om.step(table, tok, PROMPT_LEN)  # warm (page in)
+    t0 = time.perf_counter()
+    for s in range(n_tokens):
+        tok = om.step(table, tok, PROMPT_LEN + s)
+    dt = time.perf_counter() - t0
+    return {"value": round(n_tokens / dt, 4), "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{n_tokens} decode tokens of the full 36-layer model at ctx {PROMPT_LEN} "
+                      f"(C oracle, OpenMP {threads} threads, {dt:.1f} s)"}
+
+
+def run_spark(args):
+    import torch
+    world, rank, local = dist_setup()
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    cfg, w, eng = build_engine(args, device, seed=rank)
+    gen = torch.Generator().manual_seed(1234 + rank)
+    prompt = torch.randint(0, cfg.vocab_size, (PROMPT_LEN,), generator=gen, dtype=torch.int32)
+    eng.capture()
+    first = eng.prefill(prompt)
+    torch.cuda.synchronize()
+    # snapshot the state after prefill, warm up, then rewind so the timed steps run at ctx 2048..
+    saved_tok = first.clone()
+    eng.step_idx.zero_()
+    for _ in range(args.warmup):
+        eng.step()
+    torch.cuda.synchronize()
+
+    def rewind():
+        eng.pos.fill_(PROMPT_LEN)
+        eng.step_idx.zero_()
+        eng.key.zero_()
+        eng.token.copy_(saved_tok)
+        torch.cuda.synchronize()
+
+    rewind()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(device.index if device.index is not None else 0) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.4)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        eng.graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    clocks = sampler.stop() if sampler else None
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    assert int(eng.error.item()) == 0, "attention split overflow"
+    tokens_timed = eng.token_log[:args.steps].cpu()
+
+    # e2e through the public API: host token in (pinned H2D), one step, token out (D2H), every step
+    rewind()
+    tok_host = torch.empty(1, dtype=torch.int32, pin_memory=True)
+    out_host = torch.empty(1, dtype=torch.int32, pin_memory=True)
+    tok_host.copy_(saved_tok.cpu())
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    x0.record()
+    for _ in range(args.steps):
+        eng.token.copy_(tok_host, non_blocking=True)
+        eng.graph.replay()
+        out_host.copy_(eng.token, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        tok_host.copy_(out_host)
+    x1.record()
+    torch.cuda.synchronize()
+    e2e_ms = x0.elapsed_time(x1)
+    wall_e2e = time.perf_counter() - t0
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_tokens_match = bool(torch.equal(eng.token_log[:args.steps].cpu(), tokens_timed))
+
+    # per-kernel device times (rank 0) and roofline of the dominant kernel
+    kern = time_kernels(eng) if rank == 0 else {}
+    peak, peak_kind = _peaks()
+    result = None
+    if rank == 0:
+        ctx_mid = PROMPT_LEN + args.steps // 2
+        kb = kernel_bytes(cfg, ctx_mid)
+        layers = cfg.num_layers
+        per_step_us = {k: kern[k] * (1 if k == "head" else layers) for k in kern}
+        dom = max(("qkv", "o_proj", "gate_up", "down", "attn"), key=lambda k: per_step_us[k])
+        achieved = kb[dom] / (kern[dom] * 1e-6) / 1e9
+        tpot = ms / args.steps
+        step_bytes = w.q4_bytes() + cfg.hidden_size * 2 + cfg.kv_bytes_per_token() * ctx_mid
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            try:
+                cpu = cpu_baseline(eng, w, cfg, args.cpu_tokens, os.cpu_count() or 1)
+            except Exception as exc:  # reported, not fatal
+                cpu = {"value": None, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+                       "sample": f"failed: {exc}"}
+        result = {
+            "metric": METRIC,
+            "value": round(args.steps * world / (ms / 1e3), 3),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(tpot, 5),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "q4_0 weights x fp32 accumulate, bf16 activations / KV",
+            "data": "synthetic: seeded N(0,0.02) weights -> Q4_0, 2048 uniform-random prompt ids",
+            "config": {"workload": "configs[2]: synthetic 4B Q4_0 batch-1 decode, 2048 prompt, greedy",
+                       "layers": layers, "hidden": cfg.hidden_size, "vocab": cfg.vocab_size, "prompt": PROMPT_LEN,
+                       "ctx_range": [PROMPT_LEN, PROMPT_LEN + args.steps - 1], "splits": args.splits,
+                       "kernels_per_step": eng.kernels_per_step(), "parallelism": f"replicas x{world}",
+                       "l2": "inputs larger than L2 (2.26 GB of weights per step)"},
+            "e2e": {"value": round(args.steps * world / (e2e_ms / 1e3), 3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4, "wall_s": round(wall_e2e, 3),
+                    "tokens_match_device_loop": e2e_tokens_match},
+            "gpu_launches": eng.kernels_per_step() * args.steps,
+            "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": peak,
+                         "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "bytes_per_launch": kb[dom], "us_per_launch": round(kern[dom], 3), "traffic": None},
+            "step_roofline": {"bytes_per_step": step_bytes, "achieved_gbs": round(step_bytes / (tpot * 1e-3) / 1e9, 1),
+                              "frac": round(step_bytes / (tpot * 1e-3) / 1e9 / peak, 4),
+                              "roofline_ms": round(step_bytes / (peak * 1e9) * 1e3, 4)},
+            "kernel_us": {k: round(v, 3) for k, v in kern.items()},
+            "kernel_share": {k: round(per_step_us[k] / (tpot * 1e3), 4) for k in per_step_us},
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+        }
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    return result
+
+
+def run_reference(args):
+    world, rank, _ = dist_setup()
+    if rank != 0:
+        return None
+    from reference_cpu import run as ref_run  # noqa: WPS433 (module beside bench.py)
+    return ref_run(args, METRIC, PROMPT_LEN)
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=4096)
+    ap.add_argument("--warmup", type=int, default=16)
+    ap.add_argument("--impl", choices=["spark", "reference"], default="spark")
+    ap.add_argument("--splits", type=int, default=16)
+    ap.add_argument("--cpu-tokens", type=int, default=4)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args(argv)
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    res = run_reference(args) if args.impl == "reference" else run_spark(args)
+    if res is not None:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

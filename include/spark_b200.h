@@ -1,0 +1,159 @@
+/*
+ * spark_b200.h -- C ABI of the B200 (sm_100a) batch-1 decode hot path.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t (passed
+ * as void*), launches on that stream, never synchronises, never allocates, and
+ * returns a status code (0 = success, see SPARK_* below).  All entry points are
+ * safe to capture into a CUDA graph.  bf16 / fp16 tensors are passed as uint16_t
+ * bit patterns.
+ *
+ * Q4_0 weights are stored as two planes (a lossless split of the gguf block
+ * layout [rows][K/32][2-byte fp16 d | 16 nibble bytes]):
+ *   qs  uint8  [rows][K/2]   nibble bytes, gguf order (byte j: low = element j,
+ *                            high = element j+16 of the 32-element block)
+ *   d   fp16   [rows][K/32]  block scale, w = d * (q - 8)
+ *
+ * The reference's host boundary is the torch custom op spark_v43::layer_run
+ * (src/spark_vllm_ascend/integration/model.py:46-82) which hands a flat tensor
+ * list to the compiled DecodeLayer megakernel (integration/model.py:118-139,
+ * kernels/layer.py:48-109).  This ABI replaces that monolith with one entry
+ * point per fused stage; each declaration names the reference code it replaces.
+ */
+#ifndef SPARK_B200_H
+#define SPARK_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SPARK_OK 0
+#define SPARK_ERR_INVALID_ARG 1
+#define SPARK_ERR_UNSUPPORTED_SHAPE 2
+#define SPARK_ERR_ALIGNMENT 3
+#define SPARK_ERR_LAUNCH 4
+#define SPARK_ERR_TOO_LARGE 5
+
+/* Library version (major * 10000 + minor * 100 + patch). */
+int spark_version(void);
+
+/* Human readable text for a status code. */
+const char* spark_status_string(int status);
+
+/* Q4_0 quantization of fp32 weights [rows][k] on the device, bit-identical to
+ * gguf 0.19.0 quants.Q4_0.quantize_blocks (third-party; the reference calls it
+ * through gguf.quants at integration/weights.py:30 and
+ * tools/deployment/prepare_model.py:63).  k % 32 == 0. */
+int spark_q4_quantize(const float* w, int64_t rows, int64_t k, uint8_t* qs, uint16_t* d, void* stream);
+
+/* Split gguf Q4_0 block bytes [rows][k/32][18] into the qs / d planes.
+ * Replaces the repack in integration/weights.py:34-54 (unpack_q4 + pack). */
+int spark_q4_split_gguf(const uint8_t* blocks, int64_t rows, int64_t k, uint8_t* qs, uint16_t* d, void* stream);
+
+/* Dequantize to bf16 [rows][k] (w = d * (q - 8), rounded to bf16).  Used by
+ * prefill-side matmuls; replaces gguf dequantize -> bf16 at integration/weights.py:28-32. */
+int spark_q4_dequantize_bf16(const uint8_t* qs, const uint16_t* d, int64_t rows, int64_t k, uint16_t* w,
+                             void* stream);
+
+/* y[b][n] = bf16(sum_k W[n][k] * x[b][k]) for b < batch (1..8); fp32 accumulation
+ * in the fixed order documented in q4_gemv.cuh.  n even, k % 32 == 0.
+ * Replaces GemvStage.calculate (kernels/linear.py:17-200) as used by
+ * NativeLinear.execute_o / execute_down (linear.py:339-370). */
+int spark_q4_gemv(const uint16_t* x, const uint8_t* qs, const uint16_t* d, uint16_t* y, int n, int k, int batch,
+                  void* stream);
+
+/* Fused add + RMSNorm prologue + Q4_0 GEMV: s = a + b (b may be NULL),
+ * res_out = bf16(s) (may be NULL), x = bf16(s / rms(s) * gamma), y = W x.
+ * Replaces norm_ub (kernels/linear.py:202-224) feeding the gate_up GEMV
+ * (NativeUp.execute, linear.py:585-611) and the next layer's input norm
+ * (NativePool.final_norm, linear.py:298-305). */
+int spark_rmsnorm_q4_gemv(const uint16_t* a, const uint16_t* b, const uint16_t* gamma, float eps, uint16_t* res_out,
+                          const uint8_t* qs, const uint16_t* d, uint16_t* y, int n, int k, void* stream);
+
+/* Fused add + RMSNorm + gate_up Q4_0 GEMV + SiLU*mul: rows [0, n/2) are gate,
+ * [n/2, n) up; mid[i] = bf16(bf16(silu(g_i)) * u_i).
+ * Replaces NativeUp.execute + FusedUpStage.activate (kernels/linear.py:228-260,
+ * 540-611; the reference's activation is GELU, the synthetic model's SwiGLU). */
+int spark_rmsnorm_gate_up_silu(const uint16_t* a, const uint16_t* b, const uint16_t* gamma, float eps,
+                               uint16_t* res_out, const uint8_t* qs, const uint16_t* d, uint16_t* mid, int n, int k,
+                               void* stream);
+
+/* Fused input norm + QKV Q4_0 GEMV + neox RoPE + paged K/V store.
+ * a: bf16 [k] or, when embed != NULL, the row embed[token[0]] (token int32 on device).
+ * Rows of W: nq*head_dim query rows, then nkv*head_dim key rows, then value rows.
+ * cos_sin: bf16 [max_pos][head_dim] (cos in the first half, sin in the second).
+ * Position from pos (int64 on device).  The KV slot is slot_mapping[0] when
+ * slot_mapping != NULL, else block_table[pos / block_size] * block_size + pos % block_size
+ * (a negative slot skips the store).  q_out: bf16 [nq][head_dim] (rotated).
+ * Replaces FusedQkvStage.execute_fused + calculate_rotated + store8
+ * (kernels/qkv.py:25-236) and the slot computation of integration/slot_mapping.py:8-22. */
+int spark_qkv_rope_kvstore(const uint16_t* a, const uint16_t* b, const uint16_t* embed, const int32_t* token,
+                           const uint16_t* gamma, float eps, uint16_t* res_out, const uint8_t* qs, const uint16_t* d,
+                           int k, int nq, int nkv, int head_dim, const uint16_t* cos_sin, const int64_t* pos,
+                           const int32_t* block_table, const int64_t* slot_mapping, int block_size,
+                           uint16_t* k_cache, uint16_t* v_cache, uint16_t* q_out, void* stream);
+
+/* Split-KV paged GQA decode attention (partials).  q bf16 [nq][head_dim];
+ * caches bf16 [num_blocks][nkv][block_size][head_dim]; sequence length =
+ * seq_len[0] (int32) when seq_len != NULL else pos[0] + 1 (int64).
+ * Split s covers tokens [s*T, min((s+1)*T, L)), T = roundup16(ceil(L / splits)),
+ * and T must not exceed max_split_tokens (sizes shared memory; <= 2048).
+ * part_o fp32 [splits][nq][head_dim], part_lse fp32 [splits][nq] (-inf for
+ * empty splits).  error (int on device, may be NULL) is set to 1 when a split
+ * exceeds max_split_tokens at run time; the split is then written as empty.
+ * head_dim 128 and nq / nkv == 4 are supported.
+ * Replaces AttentionStage.execute_serial / execute_pipeline (kernels/attention.py:120-286). */
+int spark_attn_splitkv(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
+                       const int32_t* block_table, const int64_t* pos, const int32_t* seq_len, int nq, int nkv,
+                       int head_dim, int block_size, int splits, int max_split_tokens, float scale, float* part_o,
+                       float* part_lse, int* error, void* stream);
+
+/* Log-sum-exp combine of split partials -> bf16 [nq][head_dim].
+ * Replaces merge_attention (kernels/vector.py:154-192) without the output gate. */
+int spark_attn_combine(const float* part_o, const float* part_lse, int splits, int nq, int head_dim, uint16_t* out,
+                       void* stream);
+
+/* Final norm + LM head Q4_0 GEMV + greedy argmax.  logits bf16 [n]; argmax_key
+ * (uint64 on device) must hold 0 before the call; afterwards its low 32 bits are
+ * ~index of the largest logit (lowest index on ties).  Replaces the head GEMV path
+ * (integration/head.py:6-16, native/head/extension.cpp:7-14) for a Q4_0 head. */
+int spark_rmsnorm_q4_head_argmax(const uint16_t* a, const uint16_t* b, const uint16_t* gamma, float eps,
+                                 const uint8_t* qs, const uint16_t* d, uint16_t* logits, int n, int k,
+                                 unsigned long long* argmax_key, void* stream);
+
+/* Decode bookkeeping after the head: token = index in argmax_key; writes
+ * token_out[0] (int32, the next step's input) and, when token_log != NULL,
+ * token_log[step[0]]; resets argmax_key to 0; increments pos[0] and step[0]
+ * when they are non-NULL. */
+int spark_decode_finalize(unsigned long long* argmax_key, int32_t* token_out, int32_t* token_log, int32_t* step,
+                          int64_t* pos, void* stream);
+
+/* Standalone fused add + RMSNorm (hidden <= 16384): res_out = bf16(a + b),
+ * y = bf16((a+b) / rms * gamma).  Replaces norm_ub (kernels/linear.py:202-224). */
+int spark_add_rmsnorm(const uint16_t* a, const uint16_t* b, const uint16_t* gamma, float eps, int hidden,
+                      uint16_t* res_out, uint16_t* y, void* stream);
+
+/* SiLU * mul over n elements: out = bf16(bf16(silu(g)) * u).  The synthetic
+ * model's SwiGLU counterpart of FusedUpStage.activate (kernels/linear.py:228-260). */
+int spark_silu_mul(const uint16_t* g, const uint16_t* u, int64_t n, uint16_t* out, void* stream);
+
+/* In-place neox RoPE on bf16 heads [nh][head_dim] at position pos[0] (int64).
+ * Replaces the rotation in FusedQkvStage.calculate_rotated (kernels/qkv.py:179-189). */
+int spark_rope_neox(uint16_t* x, int nh, int head_dim, const uint16_t* cos_sin, const int64_t* pos, void* stream);
+
+/* Paged-KV slot mapping for one request (single KV group):
+ * out[i] = table[pos[i] / block_size] * block_size + pos[i] % block_size for
+ * i in [query_start[0], query_start[1]) and i < num_tokens, else -1, for all
+ * i < max_tokens.  Replaces _slot_one (integration/slot_mapping.py:8-22). */
+int spark_slot_mapping(int64_t num_tokens, int64_t max_tokens, const int32_t* query_start, const int64_t* positions,
+                       const int32_t* block_table, int64_t block_size, int64_t* out, void* stream);
+
+/* Enable / disable programmatic dependent launch on the kernels above (default on). */
+int spark_set_pdl(int enabled);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPARK_B200_H */

@@ -1,0 +1,273 @@
+"""CPU oracle for the Spark decode hot path -- TEST INFRASTRUCTURE ONLY.
+
+This package wraps ``spark_oracle.c`` (a plain-C restatement of the reference
+algorithm, see that file's header for the reference anchors) with ctypes and
+numpy.  Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU
+baseline legs may import it; the product package ``spark_b200`` never does, and
+it fails loudly when its CUDA library is missing instead of falling back here.
+
+All bf16 arrays are numpy ``uint16`` bit patterns; fp16 scales are ``uint16``.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+_HERE = Path(__file__).resolve().parent
+_LIB_PATH = _HERE / "_build" / "libspark_oracle.so"
+_lib = None
+
+_P = ctypes.c_void_p
+_I64 = ctypes.c_int64
+_I = ctypes.c_int
+_F = ctypes.c_float
+
+
+def build(force: bool = False) -> Path:
+    """Compile the oracle with its Makefile (gcc, no GPU needed)."""
+    if force or not _LIB_PATH.exists() or _LIB_PATH.stat().st_mtime < (_HERE / "spark_oracle.c").stat().st_mtime:
+        subprocess.run(["make", "-C", str(_HERE), "-s"], check=True)
+    return _LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not _LIB_PATH.exists():
+            build()
+        flags = Path("/proc/cpuinfo").read_text() if Path("/proc/cpuinfo").exists() else ""
+        if " fma " not in flags or " avx2 " not in flags:
+            raise RuntimeError("the oracle is compiled for x86-64 with AVX2+FMA; this CPU lacks them")
+        L = ctypes.CDLL(str(_LIB_PATH))
+        sig = {
+            "orc_exp": (_F, [_F]),
+            "orc_log": (_F, [_F]),
+            "orc_q4_quantize": (None, [_P, _I64, _I64, _P, _P]),
+            "orc_q4_split": (None, [_P, _I64, _I64, _P, _P]),
+            "orc_q4_join": (None, [_P, _P, _I64, _I64, _P]),
+            "orc_q4_dequantize": (None, [_P, _P, _I64, _I64, _P]),
+            "orc_q4_gemv_f32": (None, [_P, _P, _P, _I64, _I64, _I, _P]),
+            "orc_q4_gemv": (None, [_P, _P, _P, _I64, _I64, _I, _P]),
+            "orc_add_rmsnorm": (None, [_P, _P, _P, _I, _F, _P, _P]),
+            "orc_rope_neox": (None, [_P, _I, _I, _P]),
+            "orc_silu_mul": (None, [_P, _P, _I64, _P]),
+            "orc_slot_mapping": (None, [_I64, _I64, _I64, _I64, _P, _P, _I64, _P]),
+            "orc_split_tokens": (_I64, [_I64, _I]),
+            "orc_attn_split": (None, [_P, _P, _P, _P, _I64, _I, _I, _I, _I, _I, _F, _P, _P]),
+            "orc_attn_combine": (None, [_P, _P, _I, _I, _I, _P]),
+            "orc_argmax_bf16": (_I64, [_P, _I64]),
+            "orc_decode_step": (_I64, [_P, _P, _P, _P, _P, _I64, _P, _I64, _I64, _F, _F, _P]),
+            "orc_set_threads": (None, [_I]),
+            "orc_get_threads": (_I, []),
+        }
+        for name, (res, args) in sig.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def _p(a: np.ndarray | None):
+    if a is None:
+        return None
+    assert a.flags["C_CONTIGUOUS"], "oracle arrays must be C-contiguous"
+    return a.ctypes.data
+
+
+# ----------------------------------------------------------------- bf16 helpers
+def f32_to_bf16(a) -> np.ndarray:
+    """Round-to-nearest-even fp32 -> bf16 bits (uint16)."""
+    u = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    nan = (u & 0x7FFFFFFF) > 0x7F800000
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    r[nan] = 0x7FFF
+    return r
+
+
+def bf16_to_f32(b) -> np.ndarray:
+    return (np.ascontiguousarray(b, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+# ----------------------------------------------------------------- Q4_0
+def q4_quantize(w: np.ndarray):
+    """fp32 [rows, k] -> (qs uint8 [rows, k/2], d uint16 [rows, k/32]) (gguf Q4_0)."""
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    rows, k = w.shape
+    assert k % 32 == 0
+    qs = np.empty((rows, k // 2), np.uint8)
+    d = np.empty((rows, k // 32), np.uint16)
+    lib().orc_q4_quantize(_p(w), rows, k, _p(qs), _p(d))
+    return qs, d
+
+
+def q4_split(blocks: np.ndarray, rows: int, k: int):
+    blocks = np.ascontiguousarray(blocks, dtype=np.uint8)
+    qs = np.empty((rows, k // 2), np.uint8)
+    d = np.empty((rows, k // 32), np.uint16)
+    lib().orc_q4_split(_p(blocks), rows, k, _p(qs), _p(d))
+    return qs, d
+
+
+def q4_join(qs: np.ndarray, d: np.ndarray) -> np.ndarray:
+    rows, k = qs.shape[0], qs.shape[1] * 2
+    out = np.empty((rows, k // 32 * 18), np.uint8)
+    lib().orc_q4_join(_p(np.ascontiguousarray(qs)), _p(np.ascontiguousarray(d)), rows, k, _p(out))
+    return out
+
+
+def q4_dequantize(qs: np.ndarray, d: np.ndarray) -> np.ndarray:
+    rows, k = qs.shape[0], qs.shape[1] * 2
+    w = np.empty((rows, k), np.float32)
+    lib().orc_q4_dequantize(_p(np.ascontiguousarray(qs)), _p(np.ascontiguousarray(d)), rows, k, _p(w))
+    return w
+
+
+def q4_gemv(x_bf16: np.ndarray, qs: np.ndarray, d: np.ndarray) -> np.ndarray:
+    """x bf16 [batch, k] (uint16) -> y bf16 [batch, n] in the canonical order."""
+    x = np.ascontiguousarray(np.atleast_2d(x_bf16), dtype=np.uint16)
+    n, k = qs.shape[0], qs.shape[1] * 2
+    batch = x.shape[0]
+    assert x.shape[1] == k
+    y = np.empty((batch, n), np.uint16)
+    lib().orc_q4_gemv(_p(x), _p(np.ascontiguousarray(qs)), _p(np.ascontiguousarray(d)), n, k, batch, _p(y))
+    return y
+
+
+def q4_gemv_f32(x_f32: np.ndarray, qs: np.ndarray, d: np.ndarray) -> np.ndarray:
+    """Unrounded fp32 sums (same order) -- used to study rounding boundaries."""
+    x = np.ascontiguousarray(np.atleast_2d(x_f32), dtype=np.float32)
+    n, k = qs.shape[0], qs.shape[1] * 2
+    y = np.empty((x.shape[0], n), np.float32)
+    lib().orc_q4_gemv_f32(_p(x), _p(np.ascontiguousarray(qs)), _p(np.ascontiguousarray(d)), n, k, x.shape[0], _p(y))
+    return y
+
+
+# ----------------------------------------------------------------- elementwise
+def add_rmsnorm(a, b, gamma, eps: float, want_res: bool = True):
+    a = np.ascontiguousarray(a, dtype=np.uint16)
+    h = a.shape[-1]
+    bb = None if b is None else np.ascontiguousarray(b, dtype=np.uint16)
+    g = np.ascontiguousarray(gamma, dtype=np.uint16)
+    res = np.empty(h, np.uint16) if want_res else None
+    y = np.empty(h, np.uint16)
+    lib().orc_add_rmsnorm(_p(a), _p(bb), _p(g), h, eps, _p(res), _p(y))
+    return res, y
+
+
+def rope_neox(x_bf16: np.ndarray, cs_row: np.ndarray) -> np.ndarray:
+    x = np.array(x_bf16, dtype=np.uint16, copy=True, order="C")
+    nh, dim = x.shape
+    lib().orc_rope_neox(_p(x), nh, dim, _p(np.ascontiguousarray(cs_row, dtype=np.uint16)))
+    return x
+
+
+def silu_mul(g, u) -> np.ndarray:
+    g = np.ascontiguousarray(g, dtype=np.uint16)
+    u = np.ascontiguousarray(u, dtype=np.uint16)
+    out = np.empty_like(g)
+    lib().orc_silu_mul(_p(g), _p(u), g.size, _p(out))
+    return out
+
+
+def exp(x: float) -> float:
+    return lib().orc_exp(x)
+
+
+def log(x: float) -> float:
+    return lib().orc_log(x)
+
+
+# ----------------------------------------------------------------- paged KV / attention
+def slot_mapping(positions: np.ndarray, table: np.ndarray, block_size: int, max_tokens: int,
+                 start: int = 0, end: int | None = None) -> np.ndarray:
+    pos = np.ascontiguousarray(positions, dtype=np.int64)
+    n = pos.size
+    end = n if end is None else end
+    out = np.empty(max_tokens, np.int64)
+    lib().orc_slot_mapping(n, max_tokens, start, end, _p(pos), _p(np.ascontiguousarray(table, dtype=np.int32)),
+                           block_size, _p(out))
+    return out
+
+
+def split_tokens(length: int, splits: int) -> int:
+    return lib().orc_split_tokens(length, splits)
+
+
+def attn_split(q, kc, vc, table, length: int, splits: int, scale: float):
+    """q bf16 [nq, D]; kc/vc bf16 [blocks, nkv, bs, D]; returns (part_o [S,nq,D], part_lse [S,nq])."""
+    q = np.ascontiguousarray(q, dtype=np.uint16)
+    kc = np.ascontiguousarray(kc, dtype=np.uint16)
+    vc = np.ascontiguousarray(vc, dtype=np.uint16)
+    nq, dim = q.shape
+    _, nkv, bs, _ = kc.shape
+    po = np.empty((splits, nq, dim), np.float32)
+    pl = np.empty((splits, nq), np.float32)
+    lib().orc_attn_split(_p(q), _p(kc), _p(vc), _p(np.ascontiguousarray(table, dtype=np.int32)), length, nq, nkv,
+                         dim, bs, splits, scale, _p(po), _p(pl))
+    return po, pl
+
+
+def attn_combine(part_o, part_lse) -> np.ndarray:
+    po = np.ascontiguousarray(part_o, dtype=np.float32)
+    pl = np.ascontiguousarray(part_lse, dtype=np.float32)
+    splits, nq, dim = po.shape
+    out = np.empty((nq, dim), np.uint16)
+    lib().orc_attn_combine(_p(po), _p(pl), splits, nq, dim, _p(out))
+    return out
+
+
+def argmax_bf16(logits) -> int:
+    lg = np.ascontiguousarray(logits, dtype=np.uint16)
+    return int(lib().orc_argmax_bf16(_p(lg), lg.size))
+
+
+def set_threads(n: int) -> None:
+    lib().orc_set_threads(n)
+
+
+def get_threads() -> int:
+    return lib().orc_get_threads()
+
+
+# ----------------------------------------------------------------- whole model
+class OracleModel:
+    """Host copy of a synthetic Spark decoder for the C decode step.
+
+    ``weights`` is a dict of numpy arrays with the keys produced by
+    ``spark_b200.model.SyntheticWeights.to_numpy()``.
+    """
+
+    def __init__(self, cfg, weights: dict, num_blocks: int, splits: int):
+        self.cfg = cfg
+        self.w = weights
+        self.splits = splits
+        self.num_blocks = num_blocks
+        L, nkv, bs, D = cfg.num_layers, cfg.num_kv_heads, cfg.block_size, cfg.head_dim
+        self.kc = np.zeros((L, num_blocks, nkv, bs, D), np.uint16)
+        self.vc = np.zeros_like(self.kc)
+        self.dims = np.array([cfg.hidden_size, cfg.num_q_heads, cfg.num_kv_heads, cfg.head_dim,
+                              cfg.intermediate_size, cfg.vocab_size, cfg.num_layers, cfg.block_size,
+                              splits, cfg.max_position], dtype=np.int64)
+        self._keep = []
+        mp = [weights["embed"], weights["final_norm"], weights["head_qs"], weights["head_d"], weights["cos_sin"]]
+        self.model_ptrs = (ctypes.c_void_p * 5)(*[_p(a) for a in mp])
+        lp = []
+        for li in range(L):
+            for key in ("in_norm", "post_norm", "qkv_qs", "qkv_d", "o_qs", "o_d", "gu_qs", "gu_d",
+                        "down_qs", "down_d"):
+                lp.append(_p(weights[f"layers.{li}.{key}"]))
+        self.layer_ptrs = (ctypes.c_void_p * len(lp))(*lp)
+
+    def step(self, table: np.ndarray, token: int, pos: int, want_logits: bool = False):
+        cfg = self.cfg
+        logits = np.empty(cfg.vocab_size, np.uint16) if want_logits else None
+        table = np.ascontiguousarray(table, dtype=np.int32)
+        tok = lib().orc_decode_step(_p(self.dims), self.model_ptrs, self.layer_ptrs, _p(self.kc), _p(self.vc),
+                                    self.num_blocks, _p(table), token, pos, cfg.rms_norm_eps,
+                                    cfg.attn_scale, _p(logits))
+        return (int(tok), logits) if want_logits else int(tok)

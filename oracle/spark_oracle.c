@@ -1,0 +1,553 @@
+/*
+ * spark_oracle.c -- CPU restatement of the batch-1 decode hot path of the
+ * Spark-vllm-ascend plugin.  TEST INFRASTRUCTURE ONLY: this file is the checker
+ * that the CUDA kernels are compared against (tests/, __graft_entry__.smoke()
+ * and bench.py's cpu_baseline / --impl reference legs).  The product path never
+ * links, loads or calls it.
+ *
+ * Every function restates one piece of the reference algorithm and fixes ONE
+ * fp32 evaluation order.  The CUDA kernels evaluate exactly the same order, so
+ * outputs are bit-identical, and greedy tokens of a whole model agree.
+ *
+ * Reference anchors (paths inside hxmmxh/Spark-vllm-ascend, src/spark_vllm_ascend/):
+ *   Q4_0 block format ........ third-party gguf 0.19.0 quants.Q4_0.{quantize,dequantize}_blocks,
+ *                              called at integration/weights.py:30 and unpacked at weights.py:34-40
+ *   Q4 GEMV .................. kernels/linear.py:17-200 (fp32 accumulation of dequantized
+ *                              int4 x fp32 activation, lane reduction, round-to-nearest bf16 out)
+ *   add + RMSNorm ............ kernels/linear.py:202-224 (norm_ub)
+ *   RoPE (neox) .............. kernels/qkv.py:179-189 (bf16 inputs, separate fp32 products, bf16 out)
+ *   split-KV attention ....... kernels/attention.py:59-117 (fp32 scores, max, exp, fp32 sum,
+ *                              bf16 P for PV, out = acc / l, lse = log(l) + m)
+ *   LSE combine .............. kernels/vector.py:154-192 (softmax over lse, weights divided
+ *                              first, acc += w * O without fusion, bf16 round)
+ *   slot mapping ............. integration/slot_mapping.py:8-22 and
+ *                              tools/validation/test_slot_mapping.py:26-28
+ *   SiLU * mul ............... the synthetic model's SwiGLU (vLLM SiluAndMul semantics:
+ *                              bf16(silu(g)) * u rounded to bf16); the reference's GELU
+ *                              variant is linear.py:228-260.
+ *
+ * Canonical orders (shared with the CUDA kernels):
+ *   GEMV row: a row is split over 16 lanes; lane l owns Q4_0 blocks l, l+16, l+32, ...
+ *     For each block: a0 = fma chain over elements 0..15, a1 = fma chain over 16..31
+ *     (value (q-8) * x, starting from 0), block sum = a0 + a1,
+ *     lane acc = fma(d, block sum, acc).  The 16 lane sums are combined by an
+ *     xor butterfly with offsets 8,4,2,1 (v[l] = v[l] + v[l^off]).
+ *   RMSNorm: 32 lanes, lane l sums s_i*s_i (product, then add) for i = l mod 32 in
+ *     ascending order, xor butterfly 16,8,4,2,1.
+ *   Attention scores: a0 over even dims, a1 over odd dims (fma), score = (a0+a1)*scale.
+ *     l: 32 lanes over split-local token index mod 32, ascending adds, butterfly 16..1.
+ *     PV: per output dim, fma over tokens in ascending order with bf16-rounded p.
+ *   exp: Cody-Waite reduction (ln2 split in a 16-bit head and a tail) + degree-7
+ *     Taylor polynomial (Horner, fma), scaled by 2^n in two steps when n is outside
+ *     the normal exponent range.  log: x = 2^e * m, m in [sqrt(1/2), sqrt(2)),
+ *     log m = 2 atanh((m-1)/(m+1)) by its odd power series through f^11.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+#define ORC_API __attribute__((visibility("default")))
+
+/* ------------------------------------------------------------------ */
+/* scalar conversions                                                  */
+/* ------------------------------------------------------------------ */
+static inline float u2f(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
+static inline uint32_t f2u(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
+
+static inline float bf2f(uint16_t h) { return u2f((uint32_t)h << 16); }
+
+/* round-to-nearest-even fp32 -> bf16; NaN -> canonical 0x7fff */
+static inline uint16_t f2bf(float f) {
+    uint32_t u = f2u(f);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return 0x7fff;
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+
+static inline float h2f(uint16_t h) {
+    uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+    uint32_t exp = (h >> 10) & 0x1fu, man = h & 0x3ffu;
+    if (exp == 0) {
+        if (man == 0) return u2f(sign);
+        /* subnormal half: man * 2^-24, exact in fp32 */
+        float v = (float)man * 5.9604644775390625e-08f;
+        return sign ? -v : v;
+    }
+    if (exp == 31) return u2f(sign | 0x7f800000u | (man << 13));
+    return u2f(sign | ((exp + 112u) << 23) | (man << 13));
+}
+
+/* round-to-nearest-even fp32 -> fp16 (numpy astype(float16) semantics) */
+static inline uint16_t f2h(float f) {
+    uint32_t u = f2u(f);
+    uint16_t sign = (uint16_t)((u >> 16) & 0x8000u);
+    uint32_t a = u & 0x7fffffffu;
+    if (a > 0x7f800000u) return sign | 0x7e00u;
+    if (a >= 0x477ff000u) return sign | 0x7c00u; /* rounds to >= 65520 -> inf */
+    if (a < 0x38800000u) {
+        /* result is subnormal (or zero) in half: value / 2^-24, rounded to int (RNE) */
+        if (a < 0x33000000u) return sign; /* < 2^-25 rounds to 0 */
+        uint32_t e = a >> 23, m = (a & 0x7fffffu) | 0x800000u;
+        int shift = 126 - (int)e; /* value = m * 2^(e-150); half units 2^-24 -> shift = 150-24-e = 126-e */
+        uint32_t q = m >> shift, rem = m & ((1u << shift) - 1u), half = 1u << (shift - 1);
+        if (rem > half || (rem == half && (q & 1u))) q++;
+        return sign | (uint16_t)q;
+    }
+    uint32_t e = (a >> 23) - 112u, m = a & 0x7fffffu;
+    uint32_t q = (e << 10) | (m >> 13), rem = m & 0x1fffu;
+    if (rem > 0x1000u || (rem == 0x1000u && (q & 1u))) q++;
+    return sign | (uint16_t)q;
+}
+
+/* ------------------------------------------------------------------ */
+/* exp / log (own implementation, see header)                          */
+/* ------------------------------------------------------------------ */
+#define SPARK_LOG2E 1.44269502162933349609375f  /* fp32(log2 e) */
+#define SPARK_LN2_HI 0.693145751953125f           /* ln 2 to 16 significant bits */
+#define SPARK_LN2_LO 1.428606765330187e-06f       /* ln 2 - SPARK_LN2_HI */
+
+ORC_API float orc_exp(float x) {
+    if (x != x) return x;
+    if (x > 88.7228394f) return INFINITY;
+    if (x < -104.0f) return 0.0f;
+    float n = rintf(x * SPARK_LOG2E);
+    float r = fmaf(-n, SPARK_LN2_HI, x);
+    r = fmaf(-n, SPARK_LN2_LO, r);
+    float p = 1.98412698e-04f;                /* 1/5040 */
+    p = fmaf(p, r, 1.38888889e-03f);          /* 1/720 */
+    p = fmaf(p, r, 8.33333377e-03f);          /* 1/120 */
+    p = fmaf(p, r, 4.16666679e-02f);          /* 1/24 */
+    p = fmaf(p, r, 1.66666672e-01f);          /* 1/6 */
+    p = fmaf(p, r, 0.5f);
+    p = fmaf(p, r, 1.0f);
+    p = fmaf(p, r, 1.0f);
+    int ni = (int)n;
+    if (ni >= -126 && ni <= 127) return p * u2f((uint32_t)(ni + 127) << 23);
+    int n1 = ni / 2, n2 = ni - n1;
+    return (p * u2f((uint32_t)(n1 + 127) << 23)) * u2f((uint32_t)(n2 + 127) << 23);
+}
+
+ORC_API float orc_log(float x) {
+    if (x != x || x < 0.0f) return NAN;
+    if (x == 0.0f) return -INFINITY;
+    if (x == INFINITY) return INFINITY;
+    uint32_t u = f2u(x);
+    int e = (int)(u >> 23) - 127;
+    if ((u >> 23) == 0) { /* subnormal: scale by 2^23 */
+        x = x * 8388608.0f;
+        u = f2u(x);
+        e = (int)(u >> 23) - 127 - 23;
+    }
+    float m = u2f((u & 0x7fffffu) | 0x3f800000u);
+    if (m > 1.41421354f) { m = m * 0.5f; e += 1; }
+    float f = (m - 1.0f) / (m + 1.0f);
+    float f2 = f * f;
+    float s = 9.09090936e-02f;               /* 1/11 */
+    s = fmaf(s, f2, 1.11111112e-01f);        /* 1/9 */
+    s = fmaf(s, f2, 1.42857149e-01f);        /* 1/7 */
+    s = fmaf(s, f2, 2.00000003e-01f);        /* 1/5 */
+    s = fmaf(s, f2, 3.33333343e-01f);        /* 1/3 */
+    s = fmaf(s, f2, 1.0f);
+    float lm = (2.0f * f) * s;
+    float fe = (float)e;
+    return fmaf(fe, SPARK_LN2_HI, fmaf(fe, SPARK_LN2_LO, lm));
+}
+
+/* ------------------------------------------------------------------ */
+/* Q4_0 block format (gguf 0.19.0 quants.Q4_0)                         */
+/* ------------------------------------------------------------------ */
+
+/* Quantize rows x k fp32 weights into the split planes: qs [rows][k/2], d [rows][k/32].
+ * Restates gguf Q4_0.quantize_blocks: signed absmax (first index on ties),
+ * d = max / -8, id = 1/d (0 when d == 0), q = clip(trunc(w*id + 8.5), 0, 15),
+ * byte j = q[j] | q[j+16] << 4, d stored as fp16 (round to nearest even). */
+ORC_API void orc_q4_quantize(const float* w, int64_t rows, int64_t k, uint8_t* qs, uint16_t* d) {
+    int64_t nb = k / 32;
+#pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < rows; r++) {
+        for (int64_t b = 0; b < nb; b++) {
+            const float* v = w + r * k + b * 32;
+            int imax = 0;
+            float amax = fabsf(v[0]);
+            for (int j = 1; j < 32; j++) {
+                float a = fabsf(v[j]);
+                if (a > amax) { amax = a; imax = j; }
+            }
+            float mx = v[imax];
+            float dd = mx / -8.0f;
+            float id = (dd == 0.0f) ? 0.0f : 1.0f / dd;
+            uint8_t q[32];
+            for (int j = 0; j < 32; j++) {
+                float t = truncf(v[j] * id + 8.5f);
+                int qi = (int)t;
+                if (qi > 15) qi = 15;
+                if (qi < 0) qi = 0;
+                q[j] = (uint8_t)qi;
+            }
+            uint8_t* o = qs + r * (k / 2) + b * 16;
+            for (int j = 0; j < 16; j++) o[j] = (uint8_t)(q[j] | (q[j + 16] << 4));
+            d[r * nb + b] = f2h(dd);
+        }
+    }
+}
+
+/* gguf block bytes [rows][k/32][18] <-> split planes (lossless) */
+ORC_API void orc_q4_split(const uint8_t* blocks, int64_t rows, int64_t k, uint8_t* qs, uint16_t* d) {
+    int64_t nb = k / 32;
+    for (int64_t r = 0; r < rows; r++)
+        for (int64_t b = 0; b < nb; b++) {
+            const uint8_t* src = blocks + (r * nb + b) * 18;
+            d[r * nb + b] = (uint16_t)(src[0] | (src[1] << 8));
+            memcpy(qs + r * (k / 2) + b * 16, src + 2, 16);
+        }
+}
+
+ORC_API void orc_q4_join(const uint8_t* qs, const uint16_t* d, int64_t rows, int64_t k, uint8_t* blocks) {
+    int64_t nb = k / 32;
+    for (int64_t r = 0; r < rows; r++)
+        for (int64_t b = 0; b < nb; b++) {
+            uint8_t* dst = blocks + (r * nb + b) * 18;
+            uint16_t s = d[r * nb + b];
+            dst[0] = (uint8_t)(s & 0xff);
+            dst[1] = (uint8_t)(s >> 8);
+            memcpy(dst + 2, qs + r * (k / 2) + b * 16, 16);
+        }
+}
+
+/* gguf Q4_0.dequantize_blocks: w = fp32(d) * (q - 8) */
+ORC_API void orc_q4_dequantize(const uint8_t* qs, const uint16_t* d, int64_t rows, int64_t k, float* w) {
+    int64_t nb = k / 32;
+#pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < rows; r++)
+        for (int64_t b = 0; b < nb; b++) {
+            float s = h2f(d[r * nb + b]);
+            const uint8_t* q = qs + r * (k / 2) + b * 16;
+            float* o = w + r * k + b * 32;
+            for (int j = 0; j < 16; j++) {
+                o[j] = s * (float)((int)(q[j] & 15) - 8);
+                o[j + 16] = s * (float)((int)(q[j] >> 4) - 8);
+            }
+        }
+}
+
+/* ------------------------------------------------------------------ */
+/* GEMV                                                                */
+/* ------------------------------------------------------------------ */
+static inline void butterfly(float* v, int n) {
+    float t[32];
+    for (int off = n / 2; off >= 1; off /= 2) {
+        for (int l = 0; l < n; l++) t[l] = v[l] + v[l ^ off];
+        memcpy(v, t, sizeof(float) * n);
+    }
+}
+
+/* one row dot product in the canonical order; x is fp32 [k] */
+static float q4_row_dot(const uint8_t* qs, const uint16_t* d, const float* x, int64_t nb) {
+    float lane[16];
+    for (int l = 0; l < 16; l++) {
+        float acc = 0.0f;
+        for (int64_t b = l; b < nb; b += 16) {
+            const uint8_t* q = qs + b * 16;
+            const float* xb = x + b * 32;
+            float a0 = 0.0f, a1 = 0.0f;
+            for (int e = 0; e < 16; e++) {
+                a0 = fmaf((float)((int)(q[e] & 15) - 8), xb[e], a0);
+                a1 = fmaf((float)((int)(q[e] >> 4) - 8), xb[e + 16], a1);
+            }
+            acc = fmaf(h2f(d[b]), a0 + a1, acc);
+        }
+        lane[l] = acc;
+    }
+    butterfly(lane, 16);
+    return lane[0];
+}
+
+/* y[bt][n] = bf16( sum_k W[n][k] * x[bt][k] ), batch rows of x */
+ORC_API void orc_q4_gemv_f32(const float* x, const uint8_t* qs, const uint16_t* d, int64_t n, int64_t k,
+                             int batch, float* y) {
+    int64_t nb = k / 32;
+#pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < n; r++)
+        for (int bt = 0; bt < batch; bt++)
+            y[(int64_t)bt * n + r] = q4_row_dot(qs + r * (k / 2), d + r * nb, x + (int64_t)bt * k, nb);
+}
+
+ORC_API void orc_q4_gemv(const uint16_t* x, const uint8_t* qs, const uint16_t* d, int64_t n, int64_t k,
+                         int batch, uint16_t* y) {
+    float* xf = (float*)malloc(sizeof(float) * k * batch);
+    float* yf = (float*)malloc(sizeof(float) * n * batch);
+    for (int64_t i = 0; i < k * batch; i++) xf[i] = bf2f(x[i]);
+    orc_q4_gemv_f32(xf, qs, d, n, k, batch, yf);
+    for (int64_t i = 0; i < n * batch; i++) y[i] = f2bf(yf[i]);
+    free(xf);
+    free(yf);
+}
+
+/* ------------------------------------------------------------------ */
+/* add + RMSNorm (norm_ub)                                             */
+/* ------------------------------------------------------------------ */
+/* s = a + b (b may be NULL: s = a), res_out = bf16(s) (may be NULL),
+ * y = bf16((s * inv) * gamma), inv = 1 / sqrt(ss * inv_h + eps) */
+ORC_API void orc_add_rmsnorm(const uint16_t* a, const uint16_t* b, const uint16_t* gamma, int h, float eps,
+                             uint16_t* res_out, uint16_t* y) {
+    float* s = (float*)malloc(sizeof(float) * h);
+    for (int i = 0; i < h; i++) s[i] = b ? bf2f(a[i]) + bf2f(b[i]) : bf2f(a[i]);
+    float lane[32];
+    for (int l = 0; l < 32; l++) {
+        float acc = 0.0f;
+        for (int i = l; i < h; i += 32) acc = acc + s[i] * s[i];
+        lane[l] = acc;
+    }
+    butterfly(lane, 32);
+    float inv_h = (float)(1.0 / (double)h);
+    float root = sqrtf(lane[0] * inv_h + eps);
+    float inv = 1.0f / root;
+    for (int i = 0; i < h; i++) {
+        if (res_out) res_out[i] = f2bf(s[i]);
+        y[i] = f2bf((s[i] * inv) * bf2f(gamma[i]));
+    }
+    free(s);
+}
+
+/* ------------------------------------------------------------------ */
+/* RoPE (neox), SiLU*mul                                               */
+/* ------------------------------------------------------------------ */
+/* in-place on bf16 heads [nh][dim]; cos_sin row [dim]: cos[0..dim/2), sin[dim/2..dim) */
+ORC_API void orc_rope_neox(uint16_t* x, int nh, int dim, const uint16_t* cs_row) {
+    int half = dim / 2;
+    for (int hh = 0; hh < nh; hh++) {
+        uint16_t* v = x + (int64_t)hh * dim;
+        for (int i = 0; i < half; i++) {
+            float a = bf2f(v[i]), bb = bf2f(v[i + half]);
+            float c = bf2f(cs_row[i]), s = bf2f(cs_row[i + half]);
+            float u = (a * c) - (bb * s);
+            float w = (bb * c) + (a * s);
+            v[i] = f2bf(u);
+            v[i + half] = f2bf(w);
+        }
+    }
+}
+
+ORC_API void orc_silu_mul(const uint16_t* g, const uint16_t* u, int64_t n, uint16_t* out) {
+    for (int64_t i = 0; i < n; i++) {
+        float gf = bf2f(g[i]);
+        float act = bf2f(f2bf(gf / (1.0f + orc_exp(-gf))));
+        out[i] = f2bf(act * bf2f(u[i]));
+    }
+}
+
+/* ------------------------------------------------------------------ */
+/* paged KV + split-KV attention                                       */
+/* ------------------------------------------------------------------ */
+/* slot = table[pos / bs] * bs + pos % bs; positions outside [start,end) or beyond n -> -1,
+ * outputs padded with -1 up to max_tokens (slot_mapping.py:8-22). */
+ORC_API void orc_slot_mapping(int64_t n, int64_t max_tokens, int64_t start, int64_t end, const int64_t* pos,
+                              const int32_t* table, int64_t bs, int64_t* out) {
+    for (int64_t i = 0; i < max_tokens; i++) {
+        if (i < n && i >= start && i < end) {
+            int64_t p = pos[i], blk = p / bs;
+            out[i] = (int64_t)table[blk] * bs + (p - blk * bs);
+        } else {
+            out[i] = -1;
+        }
+    }
+}
+
+static inline int64_t split_tokens(int64_t len, int splits) {
+    int64_t t = (len + splits - 1) / splits;
+    return (t + 15) / 16 * 16;
+}
+
+ORC_API int64_t orc_split_tokens(int64_t len, int splits) { return split_tokens(len, splits); }
+
+/* q bf16 [nq][dim]; caches bf16 [blocks][nkv][bs][dim]; table int32;
+ * part_o fp32 [splits][nq][dim]; part_lse fp32 [splits][nq] */
+ORC_API void orc_attn_split(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const int32_t* table,
+                            int64_t len, int nq, int nkv, int dim, int bs, int splits, float scale,
+                            float* part_o, float* part_lse) {
+    int group = nq / nkv;
+    int64_t T = split_tokens(len, splits);
+    float* scores = (float*)malloc(sizeof(float) * (T > 0 ? T : 1));
+    float* qf = (float*)malloc(sizeof(float) * dim);
+    float* o = (float*)malloc(sizeof(float) * dim);
+    for (int s = 0; s < splits; s++) {
+        int64_t t0 = (int64_t)s * T, t1 = t0 + T < len ? t0 + T : len;
+        int64_t n = t1 - t0;
+        for (int hq = 0; hq < nq; hq++) {
+            int hk = hq / group;
+            float* po = part_o + ((int64_t)s * nq + hq) * dim;
+            if (n <= 0) {
+                for (int dd = 0; dd < dim; dd++) po[dd] = 0.0f;
+                part_lse[(int64_t)s * nq + hq] = -INFINITY;
+                continue;
+            }
+            for (int dd = 0; dd < dim; dd++) qf[dd] = bf2f(q[(int64_t)hq * dim + dd]);
+            float m = -INFINITY;
+            for (int64_t i = 0; i < n; i++) {
+                int64_t t = t0 + i, blk = table[t / bs], off = t % bs;
+                const uint16_t* kr = kc + ((blk * nkv + hk) * bs + off) * dim;
+                float a0 = 0.0f, a1 = 0.0f;
+                for (int dd = 0; dd < dim; dd += 2) {
+                    a0 = fmaf(qf[dd], bf2f(kr[dd]), a0);
+                    a1 = fmaf(qf[dd + 1], bf2f(kr[dd + 1]), a1);
+                }
+                float sc = (a0 + a1) * scale;
+                scores[i] = sc;
+                if (sc > m) m = sc;
+            }
+            float lane[32];
+            for (int l = 0; l < 32; l++) lane[l] = 0.0f;
+            for (int64_t i = 0; i < n; i++) {
+                float p = orc_exp(scores[i] - m);
+                lane[i % 32] = lane[i % 32] + p;
+                scores[i] = bf2f(f2bf(p));
+            }
+            butterfly(lane, 32);
+            float l = lane[0];
+            for (int dd = 0; dd < dim; dd++) o[dd] = 0.0f;
+            for (int64_t i = 0; i < n; i++) {
+                int64_t t = t0 + i, blk = table[t / bs], off = t % bs;
+                const uint16_t* vr = vc + ((blk * nkv + hk) * bs + off) * dim;
+                for (int dd = 0; dd < dim; dd++) o[dd] = fmaf(scores[i], bf2f(vr[dd]), o[dd]);
+            }
+            for (int dd = 0; dd < dim; dd++) po[dd] = o[dd] / l;
+            part_lse[(int64_t)s * nq + hq] = orc_log(l) + m;
+        }
+    }
+    free(scores);
+    free(qf);
+    free(o);
+}
+
+/* out bf16 [nq][dim] = sum_s softmax(lse)_s * part_o[s] */
+ORC_API void orc_attn_combine(const float* part_o, const float* part_lse, int splits, int nq, int dim,
+                              uint16_t* out) {
+    float* w = (float*)malloc(sizeof(float) * splits);
+    for (int hq = 0; hq < nq; hq++) {
+        float mx = -INFINITY;
+        for (int s = 0; s < splits; s++) {
+            float v = part_lse[(int64_t)s * nq + hq];
+            if (v > mx) mx = v;
+        }
+        if (mx == -INFINITY) {
+            for (int dd = 0; dd < dim; dd++) out[(int64_t)hq * dim + dd] = 0;
+            continue;
+        }
+        float den = 0.0f;
+        for (int s = 0; s < splits; s++) {
+            float v = part_lse[(int64_t)s * nq + hq];
+            w[s] = (v == -INFINITY) ? 0.0f : orc_exp(v - mx);
+            den = den + w[s];
+        }
+        for (int s = 0; s < splits; s++) w[s] = w[s] / den;
+        for (int dd = 0; dd < dim; dd++) {
+            float acc = 0.0f;
+            for (int s = 0; s < splits; s++) {
+                if (part_lse[(int64_t)s * nq + hq] == -INFINITY) continue; /* empty split */
+                acc = acc + w[s] * part_o[((int64_t)s * nq + hq) * dim + dd];
+            }
+            out[(int64_t)hq * dim + dd] = f2bf(acc);
+        }
+    }
+    free(w);
+}
+
+/* ------------------------------------------------------------------ */
+/* argmax over bf16 logits: largest value, lowest index on ties        */
+/* ------------------------------------------------------------------ */
+ORC_API int64_t orc_argmax_bf16(const uint16_t* logits, int64_t n) {
+    int64_t best = 0;
+    float bv = bf2f(logits[0]);
+    for (int64_t i = 1; i < n; i++) {
+        float v = bf2f(logits[i]);
+        if (v > bv) { bv = v; best = i; }
+    }
+    return best;
+}
+
+/* ------------------------------------------------------------------ */
+/* full synthetic decoder: one decode step                             */
+/* ------------------------------------------------------------------ */
+/* dims: [hidden, n_q_heads, n_kv_heads, head_dim, intermediate, vocab, layers, block_size,
+ *        splits, max_pos]
+ * model pointers: [embed bf16 [V][H], final_norm bf16 [H], head_qs, head_d, cos_sin bf16 [max_pos][D]]
+ * layer pointers, 10 per layer: [in_norm, post_norm, qkv_qs, qkv_d, o_qs, o_d, gu_qs, gu_d, down_qs, down_d]
+ *   qkv rows: q heads, then k heads, then v heads; gu rows: gate [I] then up [I].
+ * kc / vc: bf16 [layers][blocks][nkv][bs][D]; table int32 shared by all layers.
+ * Returns the greedy token; logits (bf16 [V]) written when non-NULL. */
+ORC_API int64_t orc_decode_step(const int64_t* dims, const void* const* model, const void* const* layers,
+                                uint16_t* kc, uint16_t* vc, int64_t nblocks, const int32_t* table, int64_t token,
+                                int64_t pos, float eps, float scale, uint16_t* logits) {
+    int H = (int)dims[0], nq = (int)dims[1], nkv = (int)dims[2], D = (int)dims[3];
+    int I = (int)dims[4];
+    int64_t V = dims[5];
+    int L = (int)dims[6], bs = (int)dims[7], splits = (int)dims[8];
+    const uint16_t* embed = (const uint16_t*)model[0];
+    const uint16_t* fnorm = (const uint16_t*)model[1];
+    const uint8_t* hqs = (const uint8_t*)model[2];
+    const uint16_t* hd = (const uint16_t*)model[3];
+    const uint16_t* cs = (const uint16_t*)model[4];
+    int64_t nqkv = (int64_t)(nq + 2 * nkv) * D;
+    uint16_t* a = (uint16_t*)malloc(2 * H);
+    uint16_t* b = (uint16_t*)malloc(2 * H);
+    uint16_t* res = (uint16_t*)malloc(2 * H);
+    uint16_t* x = (uint16_t*)malloc(2 * H);
+    uint16_t* qkv = (uint16_t*)malloc(2 * nqkv);
+    uint16_t* attn = (uint16_t*)malloc(2 * (int64_t)nq * D);
+    uint16_t* gu = (uint16_t*)malloc(2 * 2 * (int64_t)I);
+    uint16_t* mid = (uint16_t*)malloc(2 * (int64_t)I);
+    float* po = (float*)malloc(sizeof(float) * splits * nq * D);
+    float* pl = (float*)malloc(sizeof(float) * splits * nq);
+    int have_b = 0;
+    memcpy(a, embed + token * H, 2 * H);
+    int64_t blk = table[pos / bs], off = pos % bs;
+    for (int li = 0; li < L; li++) {
+        const void* const* lp = layers + (int64_t)li * 10;
+        int64_t lkv = (int64_t)li * nblocks * nkv * bs * D;
+        /* input norm: s = a + b; res = bf16(s) */
+        orc_add_rmsnorm(a, have_b ? b : NULL, (const uint16_t*)lp[0], H, eps, res, x);
+        orc_q4_gemv(x, (const uint8_t*)lp[2], (const uint16_t*)lp[3], nqkv, H, 1, qkv);
+        orc_rope_neox(qkv, nq + nkv, D, cs + pos * D);
+        for (int hk = 0; hk < nkv; hk++) {
+            memcpy(kc + lkv + ((blk * nkv + hk) * bs + off) * D, qkv + (int64_t)(nq + hk) * D, 2 * D);
+            memcpy(vc + lkv + ((blk * nkv + hk) * bs + off) * D, qkv + (int64_t)(nq + nkv + hk) * D, 2 * D);
+        }
+        orc_attn_split(qkv, kc + lkv, vc + lkv, table, pos + 1, nq, nkv, D, bs, splits, scale, po, pl);
+        orc_attn_combine(po, pl, splits, nq, D, attn);
+        uint16_t* oproj = a; /* reuse */
+        orc_q4_gemv(attn, (const uint8_t*)lp[4], (const uint16_t*)lp[5], H, (int64_t)nq * D, 1, oproj);
+        /* post-attention norm: s = oproj + res -> resmid */
+        orc_add_rmsnorm(oproj, res, (const uint16_t*)lp[1], H, eps, b, x);
+        orc_q4_gemv(x, (const uint8_t*)lp[6], (const uint16_t*)lp[7], 2 * (int64_t)I, H, 1, gu);
+        orc_silu_mul(gu, gu + I, I, mid);
+        orc_q4_gemv(mid, (const uint8_t*)lp[8], (const uint16_t*)lp[9], H, I, 1, a);
+        have_b = 1; /* next layer: a = down, b = resmid */
+    }
+    orc_add_rmsnorm(a, b, fnorm, H, eps, NULL, x);
+    uint16_t* lg = logits ? logits : (uint16_t*)malloc(2 * V);
+    orc_q4_gemv(x, hqs, hd, V, H, 1, lg);
+    int64_t tok = orc_argmax_bf16(lg, V);
+    if (!logits) free(lg);
+    free(a); free(b); free(res); free(x); free(qkv); free(attn); free(gu); free(mid); free(po); free(pl);
+    return tok;
+}
+
+ORC_API void orc_set_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}
+
+ORC_API int orc_get_threads(void) {
+#ifdef _OPENMP
+    return omp_get_max_threads();
+#else
+    return 1;
+#endif
+}

@@ -1,0 +1,177 @@
+// misc.cuh -- Q4_0 format kernels, standalone elementwise stages and decode bookkeeping.
+#pragma once
+
+#include "common.cuh"
+
+namespace spark {
+
+// ------------------------------------------------------------------ Q4_0 quantize
+// One thread per 32-weight block; restates gguf 0.19.0 quants.Q4_0.quantize_blocks:
+// signed absmax (first index on ties), d = max / -8, id = 1 / d (0 if d == 0),
+// q = clip(trunc(w * id + 8.5), 0, 15), byte j = q[j] | q[j+16] << 4, d -> fp16 (RNE).
+__global__ void q4_quantize_kernel(const float* __restrict__ w, int64_t nblocks, uint8_t* __restrict__ qs,
+                                   uint16_t* __restrict__ d) {
+  for (int64_t blk = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; blk < nblocks;
+       blk += (int64_t)gridDim.x * blockDim.x) {
+    const float4* src = reinterpret_cast<const float4*>(w + blk * 32);
+    float v[32];
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      float4 t = src[i];
+      v[4 * i] = t.x;
+      v[4 * i + 1] = t.y;
+      v[4 * i + 2] = t.z;
+      v[4 * i + 3] = t.w;
+    }
+    int imax = 0;
+    float amax = fabsf(v[0]);
+#pragma unroll
+    for (int j = 1; j < 32; j++) {
+      float a = fabsf(v[j]);
+      if (a > amax) {
+        amax = a;
+        imax = j;
+      }
+    }
+    float mx = v[0];
+#pragma unroll
+    for (int j = 1; j < 32; j++)
+      if (j == imax) mx = v[j];
+    const float dd = __fdiv_rn(mx, -8.0f);
+    const float id = (dd == 0.0f) ? 0.0f : __fdiv_rn(1.0f, dd);
+    uint32_t words[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+    for (int j = 0; j < 16; j++) {
+      int lo = (int)truncf(__fadd_rn(__fmul_rn(v[j], id), 8.5f));
+      int hi = (int)truncf(__fadd_rn(__fmul_rn(v[j + 16], id), 8.5f));
+      lo = lo > 15 ? 15 : (lo < 0 ? 0 : lo);
+      hi = hi > 15 ? 15 : (hi < 0 ? 0 : hi);
+      words[j >> 2] |= (uint32_t)(lo | (hi << 4)) << (8 * (j & 3));
+    }
+    // qs row layout == block-major within a row, so block blk's bytes are at blk*16
+    *reinterpret_cast<uint4*>(qs + blk * 16) = make_uint4(words[0], words[1], words[2], words[3]);
+    d[blk] = __half_as_ushort(__float2half_rn(dd));
+  }
+}
+
+// gguf bytes [nblocks][18] -> planes
+__global__ void q4_split_kernel(const uint8_t* __restrict__ blocks, int64_t nblocks, uint8_t* __restrict__ qs,
+                                uint16_t* __restrict__ d) {
+  for (int64_t blk = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; blk < nblocks;
+       blk += (int64_t)gridDim.x * blockDim.x) {
+    const uint8_t* src = blocks + blk * 18;
+    d[blk] = (uint16_t)(src[0] | (src[1] << 8));
+    uint32_t words[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+      words[i] = (uint32_t)src[2 + 4 * i] | ((uint32_t)src[3 + 4 * i] << 8) | ((uint32_t)src[4 + 4 * i] << 16) |
+                 ((uint32_t)src[5 + 4 * i] << 24);
+    *reinterpret_cast<uint4*>(qs + blk * 16) = make_uint4(words[0], words[1], words[2], words[3]);
+  }
+}
+
+__global__ void q4_dequant_bf16_kernel(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ d, int64_t nblocks,
+                                       uint16_t* __restrict__ w) {
+  for (int64_t blk = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; blk < nblocks;
+       blk += (int64_t)gridDim.x * blockDim.x) {
+    const float s = h2f(d[blk]);
+    const uint4 q = *reinterpret_cast<const uint4*>(qs + blk * 16);
+    const uint32_t words[4] = {q.x, q.y, q.z, q.w};
+    uint16_t* o = w + blk * 32;
+#pragma unroll
+    for (int j = 0; j < 16; j++) {
+      uint32_t byte = (words[j >> 2] >> (8 * (j & 3))) & 0xffu;
+      o[j] = f2bf(__fmul_rn(s, (float)((int)(byte & 15u) - 8)));
+      o[j + 16] = f2bf(__fmul_rn(s, (float)((int)(byte >> 4) - 8)));
+    }
+  }
+}
+
+// ------------------------------------------------------------------ standalone add + RMSNorm
+// One CTA of 1024 threads; same canonical order as the GEMV prologue.
+__global__ void __launch_bounds__(1024) add_rmsnorm_kernel(const uint16_t* __restrict__ a,
+                                                           const uint16_t* __restrict__ b,
+                                                           const uint16_t* __restrict__ gamma, float eps, float inv_h,
+                                                           int h, uint16_t* res_out, uint16_t* y) {
+  extern __shared__ float s_sm[];
+  __shared__ float inv_s;
+  pdl_launch_dependents();
+  pdl_wait();
+  for (int i = threadIdx.x; i < h; i += blockDim.x) {
+    float s = b ? __fadd_rn(bf2f(a[i]), bf2f(b[i])) : bf2f(a[i]);
+    s_sm[i] = s;
+    if (res_out) res_out[i] = f2bf(s);
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float acc = 0.0f;
+    for (int i = threadIdx.x; i < h; i += 32) acc = __fadd_rn(acc, __fmul_rn(s_sm[i], s_sm[i]));
+    acc = butterfly_sum<32>(acc);
+    if (threadIdx.x == 0) inv_s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(acc, inv_h), eps)));
+  }
+  __syncthreads();
+  const float inv = inv_s;
+  for (int i = threadIdx.x; i < h; i += blockDim.x) y[i] = f2bf(__fmul_rn(__fmul_rn(s_sm[i], inv), bf2f(gamma[i])));
+}
+
+__global__ void silu_mul_kernel(const uint16_t* __restrict__ g, const uint16_t* __restrict__ u, int64_t n,
+                                uint16_t* __restrict__ out) {
+  pdl_launch_dependents();
+  pdl_wait();
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    float gf = bf2f(g[i]);
+    float act = bf2f(f2bf(__fdiv_rn(gf, __fadd_rn(1.0f, spark_exp(-gf)))));
+    out[i] = f2bf(__fmul_rn(act, bf2f(u[i])));
+  }
+}
+
+__global__ void rope_neox_kernel(uint16_t* x, int nh, int dim, const uint16_t* __restrict__ cos_sin,
+                                 const int64_t* __restrict__ pos) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int half = dim >> 1;
+  const uint16_t* cs = cos_sin + (size_t)pos[0] * dim;
+  for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < nh * half; idx += gridDim.x * blockDim.x) {
+    int h = idx / half, i = idx - h * half;
+    uint16_t* v = x + (size_t)h * dim;
+    float a = bf2f(v[i]), b = bf2f(v[i + half]);
+    float c = bf2f(cs[i]), s = bf2f(cs[i + half]);
+    v[i] = f2bf(__fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s)));
+    v[i + half] = f2bf(__fadd_rn(__fmul_rn(b, c), __fmul_rn(a, s)));
+  }
+}
+
+// ------------------------------------------------------------------ slot mapping (integration/slot_mapping.py:8-22)
+__global__ void slot_mapping_kernel(int64_t n, int64_t max_tokens, const int32_t* __restrict__ query_start,
+                                    const int64_t* __restrict__ positions, const int32_t* __restrict__ table,
+                                    int64_t bs, int64_t* __restrict__ out) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int64_t start = query_start[0], end = query_start[1];
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < max_tokens; i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t v = -1;
+    if (i < n && i >= start && i < end) {
+      int64_t p = positions[i], blk = p / bs;
+      v = (int64_t)table[blk] * bs + (p - blk * bs);
+    }
+    out[i] = v;
+  }
+}
+
+// ------------------------------------------------------------------ decode bookkeeping
+__global__ void decode_finalize_kernel(unsigned long long* key, int32_t* token_out, int32_t* token_log,
+                                       int32_t* step, int64_t* pos) {
+  pdl_launch_dependents();
+  pdl_wait();
+  if (threadIdx.x == 0 && blockIdx.x == 0) {
+    unsigned long long k = *key;
+    int32_t tok = (int32_t)(0xffffffffu - (uint32_t)(k & 0xffffffffull));
+    token_out[0] = tok;
+    if (token_log) token_log[step ? step[0] : 0] = tok;
+    *key = 0ull;
+    if (pos) pos[0] += 1;
+    if (step) step[0] += 1;
+  }
+}
+
+}  // namespace spark

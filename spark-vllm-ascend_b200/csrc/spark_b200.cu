@@ -1,0 +1,399 @@
+// spark_b200.cu -- C ABI entry points (declared in include/spark_b200.h).
+//
+// Argument validation happens here, on the host, before any launch: shapes,
+// alignment and sizes that the kernels rely on are checked and reported as
+// status codes.  Launches use cudaLaunchKernelEx with programmatic stream
+// serialization (PDL) so that consecutive kernels of a decode step overlap their
+// launch and prologue with the tail of the previous kernel.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+#include <utility>
+
+#include "attention.cuh"
+#include "misc.cuh"
+#include "q4_gemv.cuh"
+#include "spark_b200.h"
+
+using namespace spark;
+
+namespace {
+
+int g_pdl = 1;
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+// cudaFuncSetAttribute is per (function, device).  Remember which pairs are done so
+// that launches during stream capture make no further attribute calls.
+struct SmemDone {
+  const void* fn;
+  int dev;
+  size_t bytes;
+};
+SmemDone g_smem_done[512];
+int g_smem_count = 0;
+std::mutex g_smem_mu;
+
+int set_smem(const void* kernel, size_t smem) {
+  if (smem <= 48 * 1024) return kOk;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return kErrLaunch;
+  std::lock_guard<std::mutex> lock(g_smem_mu);
+  for (int i = 0; i < g_smem_count; i++)
+    if (g_smem_done[i].fn == kernel && g_smem_done[i].dev == dev && g_smem_done[i].bytes >= smem) return kOk;
+  // always request the maximum so one call serves every later size
+  const int max_bytes = 227 * 1024;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, max_bytes) != cudaSuccess)
+    return kErrLaunch;
+  for (int i = 0; i < g_smem_count; i++)
+    if (g_smem_done[i].fn == kernel && g_smem_done[i].dev == dev) {
+      g_smem_done[i].bytes = max_bytes;
+      return kOk;
+    }
+  if (g_smem_count < 512) g_smem_done[g_smem_count++] = {kernel, dev, (size_t)max_bytes};
+  return kOk;
+}
+
+template <typename... KArgs, typename... Args>
+int launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, Args&&... args) {
+  if (set_smem(reinterpret_cast<const void*>(kernel), smem) != kOk) return kErrLaunch;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = g_pdl;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  return e == cudaSuccess ? kOk : kErrLaunch;
+}
+
+int num_sms() {
+  static int cached[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return kNumSMs;
+  if (!cached[dev]) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    cached[dev] = v > 0 ? v : kNumSMs;
+  }
+  return cached[dev];
+}
+
+// ------------------------------------------------------------------ GEMV dispatch
+template <class Pro, class Epi, int BATCH>
+int gemv_launch_b(const GemvArgs& g, cudaStream_t st) {
+  const int nb = g.k / 32;
+  const int bpl = (nb + 15) / 16;  // blocks per lane
+  const int npairs = g.n / 2;
+  const int duos = (npairs + 1) / 2;
+  const int sms = num_sms();
+  const int ctas_per_sm = 2;
+  const int cap = sms * ctas_per_sm;
+  int grid = (duos + 7) / 8;  // CTAs of 8 busy warps
+  if (grid < sms) grid = duos < sms ? duos : sms;  // spread thin work over all SMs
+  if (grid > cap) grid = cap;
+  if (grid < 1) grid = 1;
+  const size_t smem = (size_t)BATCH * g.k * sizeof(float) + 128;
+  if (smem > 227 * 1024) return kErrTooLarge;
+  if (bpl <= 2) return launch(q4_gemv_kernel<Pro, Epi, BATCH, 2>, dim3(grid), dim3(256), smem, st, g);
+  if (bpl <= 5) return launch(q4_gemv_kernel<Pro, Epi, BATCH, 5>, dim3(grid), dim3(256), smem, st, g);
+  if (bpl <= 8) return launch(q4_gemv_kernel<Pro, Epi, BATCH, 8>, dim3(grid), dim3(256), smem, st, g);
+  return launch(q4_gemv_kernel<Pro, Epi, BATCH, 10>, dim3(grid), dim3(256), smem, st, g);
+}
+
+int check_q4(const uint8_t* qs, const uint16_t* d, int n, int k) {
+  if (!qs || !d) return kErrInvalidArg;
+  if (n <= 0 || k <= 0 || (n & 1) || (k % 32)) return kErrUnsupportedShape;
+  if (!aligned(qs, 16) || !aligned(d, 2)) return kErrAlignment;
+  return kOk;
+}
+
+GemvArgs blank_args() {
+  GemvArgs g;
+  memset(&g, 0, sizeof(g));
+  g.batch = 1;
+  return g;
+}
+
+}  // namespace
+
+extern "C" {
+
+int spark_version(void) { return 100; }
+
+const char* spark_status_string(int status) {
+  switch (status) {
+    case SPARK_OK: return "ok";
+    case SPARK_ERR_INVALID_ARG: return "invalid argument (null pointer or bad value)";
+    case SPARK_ERR_UNSUPPORTED_SHAPE: return "unsupported shape";
+    case SPARK_ERR_ALIGNMENT: return "pointer alignment violated";
+    case SPARK_ERR_LAUNCH: return "CUDA launch failed";
+    case SPARK_ERR_TOO_LARGE: return "size exceeds the kernel's limit";
+    default: return "unknown status";
+  }
+}
+
+int spark_set_pdl(int enabled) {
+  g_pdl = enabled ? 1 : 0;
+  return SPARK_OK;
+}
+
+int spark_q4_quantize(const float* w, int64_t rows, int64_t k, uint8_t* qs, uint16_t* d, void* stream) {
+  if (!w || !qs || !d) return SPARK_ERR_INVALID_ARG;
+  if (rows <= 0 || k <= 0 || k % 32) return SPARK_ERR_UNSUPPORTED_SHAPE;
+  if (!aligned(w, 16) || !aligned(qs, 16) || !aligned(d, 2)) return SPARK_ERR_ALIGNMENT;
+  const int64_t nblocks = rows * (k / 32);
+  int64_t grid = (nblocks + 255) / 256;
+  if (grid > 65535 * 16) grid = 65535 * 16;
+  q4_quantize_kernel<<<(unsigned)grid, 256, 0, as_stream(stream)>>>(w, nblocks, qs, d);
+  return cudaGetLastError() == cudaSuccess ? SPARK_OK : SPARK_ERR_LAUNCH;
+}
+
+int spark_q4_split_gguf(const uint8_t* blocks, int64_t rows, int64_t k, uint8_t* qs, uint16_t* d, void* stream) {
+  if (!blocks || !qs || !d) return SPARK_ERR_INVALID_ARG;
+  if (rows <= 0 || k <= 0 || k % 32) return SPARK_ERR_UNSUPPORTED_SHAPE;
+  if (!aligned(qs, 16) || !aligned(d, 2)) return SPARK_ERR_ALIGNMENT;
+  const int64_t nblocks = rows * (k / 32);
+  int64_t grid = (nblocks + 255) / 256;
+  if (grid > 65535 * 16) grid = 65535 * 16;
+  q4_split_kernel<<<(unsigned)grid, 256, 0, as_stream(stream)>>>(blocks, nblocks, qs, d);
+  return cudaGetLastError() == cudaSuccess ? SPARK_OK : SPARK_ERR_LAUNCH;
+}
+
+int spark_q4_dequantize_bf16(const uint8_t* qs, const uint16_t* d, int64_t rows, int64_t k, uint16_t* w,
+                             void* stream) {
+  if (!qs || !d || !w) return SPARK_ERR_INVALID_ARG;
+  if (rows <= 0 || k <= 0 || k % 32) return SPARK_ERR_UNSUPPORTED_SHAPE;
+  if (!aligned(qs, 16) || !aligned(d, 2) || !aligned(w, 2)) return SPARK_ERR_ALIGNMENT;
+  const int64_t nblocks = rows * (k / 32);
+  int64_t grid = (nblocks + 255) / 256;
+  if (grid > 65535 * 16) grid = 65535 * 16;
+  q4_dequant_bf16_kernel<<<(unsigned)grid, 256, 0, as_stream(stream)>>>(qs, d, nblocks, w);
+  return cudaGetLastError() == cudaSuccess ? SPARK_OK : SPARK_ERR_LAUNCH;
+}
+
+int spark_q4_gemv(const uint16_t* x, const uint8_t* qs, const uint16_t* d, uint16_t* y, int n, int k, int batch,
+                  void* stream) {
+  int st = check_q4(qs, d, n, k);
+  if (st) return st;
+  if (!x || !y) return SPARK_ERR_INVALID_ARG;
+  if (batch < 1 || batch > 8) return SPARK_ERR_UNSUPPORTED_SHAPE;
+  if (!aligned(x, 4) || !aligned(y, 4)) return SPARK_ERR_ALIGNMENT;
+  GemvArgs g = blank_args();
+  g.qs = qs;
+  g.d = d;
+  g.n = n;
+  g.k = k;
+  g.batch = batch;
+  g.x = x;
+  g.y = y;
+  cudaStream_t s = as_stream(stream);
+  if (batch == 1) return gemv_launch_b<ProPlain, EpiPlain, 1>(g, s);
+  if (batch == 2) return gemv_launch_b<ProPlain, EpiPlain, 2>(g, s);
+  if (batch <= 4) return gemv_launch_b<ProPlain, EpiPlain, 4>(g, s);
+  return gemv_launch_b<ProPlain, EpiPlain, 8>(g, s);
+}
+
+static int fill_norm(GemvArgs& g, const uint16_t* a, const uint16_t* b, const uint16_t* gamma, float eps,
+                     uint16_t* res_out, int k) {
+  if (!gamma) return SPARK_ERR_INVALID_ARG;
+  if (!aligned(gamma, 2) || (a && !aligned(a, 4)) || (b && !aligned(b, 4)) || (res_out && !aligned(res_out, 4)))
+    return SPARK_ERR_ALIGNMENT;
+  if (!(eps >= 0.0f)) return SPARK_ERR_INVALID_ARG;
+  g.a = a;
+  g.b = b;
+  g.gamma = gamma;
+  g.eps = eps;
+  g.inv_k = (float)(1.0 / (double)k);
+  g.res_out = res_out;
+  return SPARK_OK;
+}
+
+int spark_rmsnorm_q4_gemv(const uint16_t* a, const uint16_t* b, const uint16_t* gamma, float eps, uint16_t* res_out,
+                          const uint8_t* qs, const uint16_t* d, uint16_t* y, int n, int k, void* stream) {
+  int st = check_q4(qs, d, n, k);
+  if (st) return st;
+  if (!a || !y) return SPARK_ERR_INVALID_ARG;
+  if (!aligned(y, 4)) return SPARK_ERR_ALIGNMENT;
+  GemvArgs g = blank_args();
+  if ((st = fill_norm(g, a, b, gamma, eps, res_out, k))) return st;
+  g.qs = qs;
+  g.d = d;
+  g.n = n;
+  g.k = k;
+  g.y = y;
+  return gemv_launch_b<ProNorm, EpiPlain, 1>(g, as_stream(stream));
+}
+
+int spark_rmsnorm_gate_up_silu(const uint16_t* a, const uint16_t* b, const uint16_t* gamma, float eps,
+                               uint16_t* res_out, const uint8_t* qs, const uint16_t* d, uint16_t* mid, int n, int k,
+                               void* stream) {
+  int st = check_q4(qs, d, n, k);
+  if (st) return st;
+  if (!a || !mid) return SPARK_ERR_INVALID_ARG;
+  GemvArgs g = blank_args();
+  if ((st = fill_norm(g, a, b, gamma, eps, res_out, k))) return st;
+  g.qs = qs;
+  g.d = d;
+  g.n = n;
+  g.k = k;
+  g.y = mid;
+  return gemv_launch_b<ProNorm, EpiSiluMul, 1>(g, as_stream(stream));
+}
+
+int spark_qkv_rope_kvstore(const uint16_t* a, const uint16_t* b, const uint16_t* embed, const int32_t* token,
+                           const uint16_t* gamma, float eps, uint16_t* res_out, const uint8_t* qs, const uint16_t* d,
+                           int k, int nq, int nkv, int head_dim, const uint16_t* cos_sin, const int64_t* pos,
+                           const int32_t* block_table, const int64_t* slot_mapping, int block_size,
+                           uint16_t* k_cache, uint16_t* v_cache, uint16_t* q_out, void* stream) {
+  if (nq <= 0 || nkv <= 0 || head_dim <= 0 || (head_dim & 3) || block_size <= 0) return SPARK_ERR_UNSUPPORTED_SHAPE;
+  const int n = (nq + 2 * nkv) * head_dim;
+  int st = check_q4(qs, d, n, k);
+  if (st) return st;
+  if ((!a && !(embed && token)) || !cos_sin || !pos || !k_cache || !v_cache || !q_out) return SPARK_ERR_INVALID_ARG;
+  if (!slot_mapping && !block_table) return SPARK_ERR_INVALID_ARG;
+  if (!aligned(v_cache, 4) || !aligned(k_cache, 2) || !aligned(q_out, 2) || (embed && !aligned(embed, 4)))
+    return SPARK_ERR_ALIGNMENT;
+  GemvArgs g = blank_args();
+  if ((st = fill_norm(g, a, b, gamma, eps, res_out, k))) return st;
+  g.embed = embed;
+  g.token = token;
+  g.qs = qs;
+  g.d = d;
+  g.n = n;
+  g.k = k;
+  g.y = q_out;
+  g.nq = nq;
+  g.nkv = nkv;
+  g.head_dim = head_dim;
+  g.block_size = block_size;
+  g.cos_sin = cos_sin;
+  g.pos64 = pos;
+  g.block_table = block_table;
+  g.slot_mapping = slot_mapping;
+  g.k_cache = k_cache;
+  g.v_cache = v_cache;
+  return gemv_launch_b<ProNorm, EpiRope, 1>(g, as_stream(stream));
+}
+
+int spark_rmsnorm_q4_head_argmax(const uint16_t* a, const uint16_t* b, const uint16_t* gamma, float eps,
+                                 const uint8_t* qs, const uint16_t* d, uint16_t* logits, int n, int k,
+                                 unsigned long long* argmax_key, void* stream) {
+  int st = check_q4(qs, d, n, k);
+  if (st) return st;
+  if (!a || !logits || !argmax_key) return SPARK_ERR_INVALID_ARG;
+  if (!aligned(logits, 4) || !aligned(argmax_key, 8)) return SPARK_ERR_ALIGNMENT;
+  GemvArgs g = blank_args();
+  if ((st = fill_norm(g, a, b, gamma, eps, nullptr, k))) return st;
+  g.qs = qs;
+  g.d = d;
+  g.n = n;
+  g.k = k;
+  g.y = logits;
+  g.argmax_key = argmax_key;
+  return gemv_launch_b<ProNorm, EpiArgmax, 1>(g, as_stream(stream));
+}
+
+int spark_attn_splitkv(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
+                       const int32_t* block_table, const int64_t* pos, const int32_t* seq_len, int nq, int nkv,
+                       int head_dim, int block_size, int splits, int max_split_tokens, float scale, float* part_o,
+                       float* part_lse, int* error, void* stream) {
+  if (!q || !k_cache || !v_cache || !block_table || !part_o || !part_lse || (!pos && !seq_len))
+    return SPARK_ERR_INVALID_ARG;
+  if (head_dim != 128 || nkv <= 0 || nq != 4 * nkv || block_size <= 0) return SPARK_ERR_UNSUPPORTED_SHAPE;
+  if (splits <= 0 || splits > 4096) return SPARK_ERR_UNSUPPORTED_SHAPE;
+  if (max_split_tokens <= 0 || max_split_tokens > kAttnMaxSplitTokens) return SPARK_ERR_TOO_LARGE;
+  if (!aligned(k_cache, 16) || !aligned(v_cache, 16) || !aligned(part_o, 8) || !aligned(q, 4))
+    return SPARK_ERR_ALIGNMENT;
+  AttnArgs a;
+  a.q = q;
+  a.k_cache = k_cache;
+  a.v_cache = v_cache;
+  a.block_table = block_table;
+  a.pos64 = seq_len ? nullptr : pos;
+  a.pos32 = nullptr;
+  a.seq_len32 = seq_len;
+  a.nq = nq;
+  a.nkv = nkv;
+  a.block_size = block_size;
+  a.splits = splits;
+  a.t_alloc = (max_split_tokens + 15) / 16 * 16;
+  a.scale = scale;
+  a.part_o = part_o;
+  a.part_lse = part_lse;
+  a.error = error;
+  const int G = 4, D = 128;
+  const size_t smem = (size_t)(G * D + G * a.t_alloc + 2 * G + 8) * sizeof(float) +
+                      (size_t)kAttnStages * kAttnChunk * D * sizeof(uint16_t);
+  return launch(attn_split_kernel<128, 4>, dim3(splits, nkv), dim3(kAttnThreads), smem, as_stream(stream), a);
+}
+
+int spark_attn_combine(const float* part_o, const float* part_lse, int splits, int nq, int head_dim, uint16_t* out,
+                       void* stream) {
+  if (!part_o || !part_lse || !out) return SPARK_ERR_INVALID_ARG;
+  if (splits <= 0 || splits > 4096 || nq <= 0 || head_dim <= 0) return SPARK_ERR_UNSUPPORTED_SHAPE;
+  CombineArgs c;
+  c.part_o = part_o;
+  c.part_lse = part_lse;
+  c.splits = splits;
+  c.nq = nq;
+  c.dim = head_dim;
+  c.out = out;
+  return launch(attn_combine_kernel, dim3(nq), dim3(128), (size_t)splits * sizeof(float), as_stream(stream), c);
+}
+
+int spark_decode_finalize(unsigned long long* argmax_key, int32_t* token_out, int32_t* token_log, int32_t* step,
+                          int64_t* pos, void* stream) {
+  if (!argmax_key || !token_out) return SPARK_ERR_INVALID_ARG;
+  if (token_log && !step) return SPARK_ERR_INVALID_ARG;
+  return launch(decode_finalize_kernel, dim3(1), dim3(32), 0, as_stream(stream), argmax_key, token_out, token_log,
+                step, pos);
+}
+
+int spark_add_rmsnorm(const uint16_t* a, const uint16_t* b, const uint16_t* gamma, float eps, int hidden,
+                      uint16_t* res_out, uint16_t* y, void* stream) {
+  if (!a || !gamma || !y) return SPARK_ERR_INVALID_ARG;
+  if (hidden <= 0 || hidden > 16384) return SPARK_ERR_UNSUPPORTED_SHAPE;
+  if (!(eps >= 0.0f)) return SPARK_ERR_INVALID_ARG;
+  const float inv_h = (float)(1.0 / (double)hidden);
+  return launch(add_rmsnorm_kernel, dim3(1), dim3(1024), (size_t)hidden * sizeof(float), as_stream(stream), a, b,
+                gamma, eps, inv_h, hidden, res_out, y);
+}
+
+int spark_silu_mul(const uint16_t* g, const uint16_t* u, int64_t n, uint16_t* out, void* stream) {
+  if (!g || !u || !out) return SPARK_ERR_INVALID_ARG;
+  if (n <= 0) return SPARK_ERR_UNSUPPORTED_SHAPE;
+  int64_t grid = (n + 255) / 256;
+  if (grid > 4 * num_sms()) grid = 4 * num_sms();
+  return launch(silu_mul_kernel, dim3((unsigned)grid), dim3(256), 0, as_stream(stream), g, u, n, out);
+}
+
+int spark_rope_neox(uint16_t* x, int nh, int head_dim, const uint16_t* cos_sin, const int64_t* pos, void* stream) {
+  if (!x || !cos_sin || !pos) return SPARK_ERR_INVALID_ARG;
+  if (nh <= 0 || head_dim <= 0 || (head_dim & 1)) return SPARK_ERR_UNSUPPORTED_SHAPE;
+  const int total = nh * head_dim / 2;
+  const int grid = (total + 255) / 256;
+  return launch(rope_neox_kernel, dim3(grid), dim3(256), 0, as_stream(stream), x, nh, head_dim, cos_sin, pos);
+}
+
+int spark_slot_mapping(int64_t num_tokens, int64_t max_tokens, const int32_t* query_start, const int64_t* positions,
+                       const int32_t* block_table, int64_t block_size, int64_t* out, void* stream) {
+  if (!query_start || !out || (num_tokens > 0 && (!positions || !block_table))) return SPARK_ERR_INVALID_ARG;
+  if (num_tokens < 0 || max_tokens <= 0 || num_tokens > max_tokens || block_size <= 0)
+    return SPARK_ERR_UNSUPPORTED_SHAPE;
+  int64_t grid = (max_tokens + 255) / 256;
+  if (grid > 4 * num_sms()) grid = 4 * num_sms();
+  return launch(slot_mapping_kernel, dim3((unsigned)grid), dim3(256), 0, as_stream(stream), num_tokens, max_tokens,
+                query_start, positions, block_table, block_size, out);
+}
+
+}  // extern "C"

@@ -1,0 +1,80 @@
+"""ctypes binding of ``libspark_b200.so`` (the C ABI in include/spark_b200.h).
+
+There is no fallback: if the shared library is missing or cannot be loaded,
+``lib()`` raises, so no caller can silently run something other than the sm_100a
+kernels.
+"""
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+_LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libspark_b200.so"
+_lib = None
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_I64 = ctypes.c_int64
+_F = ctypes.c_float
+
+# name -> argument types (all return int status)
+SIGNATURES: dict[str, list] = {
+    "spark_q4_quantize": [_P, _I64, _I64, _P, _P, _P],
+    "spark_q4_split_gguf": [_P, _I64, _I64, _P, _P, _P],
+    "spark_q4_dequantize_bf16": [_P, _P, _I64, _I64, _P, _P],
+    "spark_q4_gemv": [_P, _P, _P, _P, _I, _I, _I, _P],
+    "spark_rmsnorm_q4_gemv": [_P, _P, _P, _F, _P, _P, _P, _P, _I, _I, _P],
+    "spark_rmsnorm_gate_up_silu": [_P, _P, _P, _F, _P, _P, _P, _P, _I, _I, _P],
+    "spark_qkv_rope_kvstore": [_P, _P, _P, _P, _P, _F, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P, _I, _P, _P, _P,
+                               _P],
+    "spark_attn_splitkv": [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _F, _P, _P, _P, _P],
+    "spark_attn_combine": [_P, _P, _I, _I, _I, _P, _P],
+    "spark_rmsnorm_q4_head_argmax": [_P, _P, _P, _F, _P, _P, _P, _I, _I, _P, _P],
+    "spark_decode_finalize": [_P, _P, _P, _P, _P, _P],
+    "spark_add_rmsnorm": [_P, _P, _P, _F, _I, _P, _P, _P],
+    "spark_silu_mul": [_P, _P, _I64, _P, _P],
+    "spark_rope_neox": [_P, _I, _I, _P, _P, _P],
+    "spark_slot_mapping": [_I64, _I64, _P, _P, _P, _I64, _P, _P],
+    "spark_set_pdl": [_I],
+}
+
+
+class SparkError(RuntimeError):
+    """A C-ABI entry point returned a non-zero status."""
+
+    def __init__(self, fn: str, status: int, text: str):
+        super().__init__(f"{fn} failed with status {status}: {text}")
+        self.fn = fn
+        self.status = status
+
+
+def library_path() -> Path:
+    return _LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not _LIB_PATH.exists():
+            raise RuntimeError(
+                f"spark_b200 CUDA library not found at {_LIB_PATH}; build it with "
+                "`python spark-vllm-ascend_b200/build.py` (there is no CPU fallback)")
+        L = ctypes.CDLL(str(_LIB_PATH))
+        for name, args in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = _I
+            fn.argtypes = args
+        L.spark_status_string.restype = ctypes.c_char_p
+        L.spark_status_string.argtypes = [_I]
+        L.spark_version.restype = _I
+        L.spark_version.argtypes = []
+        _lib = L
+    return _lib
+
+
+def call(name: str, *args) -> None:
+    """Call an entry point and raise SparkError on a non-zero status."""
+    L = lib()
+    status = getattr(L, name)(*args)
+    if status != 0:
+        raise SparkError(name, status, L.spark_status_string(status).decode())

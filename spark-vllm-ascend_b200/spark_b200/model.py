@@ -1,0 +1,316 @@
+"""Synthetic Spark decoder on B200: weights in HBM, paged KV cache and the decode engine.
+
+Structure of one decode step (the reference's per-layer megakernel,
+kernels/layer.py:48-103, re-cut into stream-ordered sm_100a kernels launched with
+programmatic dependent launch and replayed as one CUDA graph):
+
+  per layer i:
+    qkv      : s = a + b -> res_attn; x = RMSNorm(s) * in_norm; QKV Q4 GEMV; RoPE;
+               q -> q_buf, k / v -> paged cache at the step's slot
+               (layer 0: a = embedding row of the input token, b = none)
+    attn     : split-KV partials over the sequence
+    combine  : log-sum-exp merge -> attn_out (bf16)
+    o_proj   : Q4 GEMV attn_out -> oproj
+    gate_up  : s = oproj + res_attn -> resmid; x = RMSNorm(s) * post_norm;
+               gate/up Q4 GEMV; SiLU(g) * u -> mid
+    down     : Q4 GEMV mid -> down          (next layer: a = down, b = resmid)
+  head       : s = down + resmid; x = RMSNorm(s) * final_norm; LM-head Q4 GEMV;
+               bf16 logits + greedy argmax key
+  finalize   : token = argmax; token_log[step] = token; pos += 1; step += 1
+
+This is the same dataflow as the reference's layer_run custom op
+(integration/model.py:46-82), whose inputs are the normalised hidden state and the
+residual and whose outputs are the next layer's normalised input and residual.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import ops
+from ._lib import lib
+from .config import SparkConfig
+
+BF16 = torch.bfloat16
+
+
+# ---------------------------------------------------------------------------- RoPE table
+def rope_cos_sin(cfg: SparkConfig, max_position: int | None = None) -> torch.Tensor:
+    """bf16 [max_pos, head_dim]: cos(pos * inv_freq) | sin(pos * inv_freq), neox layout.
+
+    Same construction as vLLM's RotaryEmbedding._compute_cos_sin_cache (fp32 on the
+    CPU, then cast to the model dtype), which the reference feeds to its kernel as
+    ``cs`` (integration/model.py:71)."""
+    max_pos = max_position or cfg.max_position
+    d = cfg.head_dim
+    inv_freq = 1.0 / (cfg.rope_theta ** (torch.arange(0, d, 2, dtype=torch.float32) / d))
+    t = torch.arange(max_pos, dtype=torch.float32)
+    freqs = torch.einsum("i,j->ij", t, inv_freq)
+    return torch.cat((freqs.cos(), freqs.sin()), dim=-1).to(BF16).contiguous()
+
+
+# ---------------------------------------------------------------------------- weights
+@dataclass
+class Q4Linear:
+    qs: torch.Tensor  # uint8 [n, k/2]
+    d: torch.Tensor   # fp16 [n, k/32]
+
+    @property
+    def n(self) -> int:
+        return self.qs.shape[0]
+
+    @property
+    def k(self) -> int:
+        return self.qs.shape[1] * 2
+
+    def nbytes(self) -> int:
+        return self.qs.numel() + self.d.numel() * 2
+
+
+@dataclass
+class LayerWeights:
+    in_norm: torch.Tensor
+    post_norm: torch.Tensor
+    qkv: Q4Linear
+    o: Q4Linear
+    gate_up: Q4Linear
+    down: Q4Linear
+
+
+class SyntheticWeights:
+    """Seeded random-init weights of the synthetic model, generated on the GPU.
+
+    Linear weights are N(0, init_std) in fp32, quantized to Q4_0 on the device by
+    ``spark_q4_quantize`` (bit-identical to gguf's quantizer).  Embeddings are bf16
+    N(0, init_std).  RMSNorm weights are bf16(1 + N(0, init_std)).
+    """
+
+    def __init__(self, cfg: SparkConfig, device="cuda", seed: int = 0):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        gen = torch.Generator(device=self.device)
+        gen.manual_seed(seed)
+        std = cfg.init_std
+        h, i = cfg.hidden_size, cfg.intermediate_size
+
+        def q4(n, k):
+            qs = torch.empty((n, k // 2), dtype=torch.uint8, device=self.device)
+            d = torch.empty((n, k // 32), dtype=torch.float16, device=self.device)
+            rows_per_chunk = max(1, (1 << 27) // k)  # <= 512 MB of fp32 at a time
+            for r0 in range(0, n, rows_per_chunk):
+                r1 = min(n, r0 + rows_per_chunk)
+                w = torch.randn((r1 - r0, k), generator=gen, device=self.device, dtype=torch.float32) * std
+                q, s = ops.q4_quantize(w)
+                qs[r0:r1].copy_(q)
+                d[r0:r1].copy_(s)
+            return Q4Linear(qs, d)
+
+        def norm(n):
+            return (1.0 + std * torch.randn((n,), generator=gen, device=self.device)).to(BF16)
+
+        self.embed = (torch.randn((cfg.vocab_size, h), generator=gen, device=self.device) * std).to(BF16)
+        self.layers: list[LayerWeights] = []
+        for _ in range(cfg.num_layers):
+            self.layers.append(LayerWeights(
+                in_norm=norm(h), post_norm=norm(h),
+                qkv=q4(cfg.qkv_rows, h), o=q4(h, cfg.num_q_heads * cfg.head_dim),
+                gate_up=q4(2 * i, h), down=q4(h, i)))
+        self.final_norm = norm(h)
+        self.head = q4(cfg.vocab_size, h)
+        self.cos_sin = rope_cos_sin(cfg).to(self.device)
+
+    def q4_bytes(self) -> int:
+        return sum(l.qkv.nbytes() + l.o.nbytes() + l.gate_up.nbytes() + l.down.nbytes() for l in self.layers) + \
+            self.head.nbytes()
+
+    def to_numpy(self) -> dict:
+        """Host copies (uint16 bit patterns for bf16 / fp16) for the CPU checker."""
+        def u16(t):
+            return t.detach().contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+
+        def u8(t):
+            return t.detach().contiguous().cpu().numpy()
+
+        out = {"embed": u16(self.embed), "final_norm": u16(self.final_norm), "head_qs": u8(self.head.qs),
+               "head_d": u16(self.head.d), "cos_sin": u16(self.cos_sin)}
+        for li, l in enumerate(self.layers):
+            p = f"layers.{li}."
+            out[p + "in_norm"] = u16(l.in_norm)
+            out[p + "post_norm"] = u16(l.post_norm)
+            for key, lin in (("qkv", l.qkv), ("o", l.o), ("gu", l.gate_up), ("down", l.down)):
+                out[p + key + "_qs"] = u8(lin.qs)
+                out[p + key + "_d"] = u16(lin.d)
+        return out
+
+
+# ---------------------------------------------------------------------------- engine
+def _vp(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+class DecodeEngine:
+    """Batch-1 greedy decode of the synthetic model with a paged BF16 KV cache.
+
+    All state lives in HBM; one decode step is one CUDA-graph replay with no host
+    synchronisation.  ``block_table`` maps logical KV blocks to physical blocks of
+    the cache (a random permutation by default, as in the attention parity cases).
+    """
+
+    def __init__(self, weights: SyntheticWeights, max_seq_len: int, splits: int = 16, num_blocks: int | None = None,
+                 block_table: torch.Tensor | None = None, use_graph: bool = True, max_steps: int | None = None,
+                 seed: int = 0):
+        cfg = weights.cfg
+        self.cfg, self.w = cfg, weights
+        dev = weights.device
+        self.device = dev
+        self.splits = splits
+        self.max_seq_len = max_seq_len
+        bs = cfg.block_size
+        nblk_seq = (max_seq_len + bs - 1) // bs
+        self.num_blocks = num_blocks or nblk_seq
+        if self.num_blocks < nblk_seq:
+            raise ValueError("num_blocks too small for max_seq_len")
+        self.max_split_tokens = ((max_seq_len + splits - 1) // splits + 15) // 16 * 16
+        if self.max_split_tokens > 2048:
+            raise ValueError(f"{splits} splits give {self.max_split_tokens}-token splits; use more splits (limit 2048)")
+        if block_table is None:
+            g = torch.Generator().manual_seed(seed)
+            block_table = torch.randperm(self.num_blocks, generator=g)[:nblk_seq].to(torch.int32)
+        self.block_table = block_table.to(dev, torch.int32).contiguous()
+        L, nkv, D = cfg.num_layers, cfg.num_kv_heads, cfg.head_dim
+        self.k_cache = torch.zeros((L, self.num_blocks, nkv, bs, D), dtype=BF16, device=dev)
+        self.v_cache = torch.zeros_like(self.k_cache)
+        h, i, nq = cfg.hidden_size, cfg.intermediate_size, cfg.num_q_heads
+        e = lambda *s, dt=BF16: torch.zeros(s, dtype=dt, device=dev)  # noqa: E731
+        self.res_attn, self.resmid, self.oproj, self.down = e(h), e(h), e(h), e(h)
+        self.mid = e(i)
+        self.q = e(nq, D)
+        self.attn_out = e(nq, D)
+        self.part_o = e(splits, nq, D, dt=torch.float32)
+        self.part_lse = e(splits, nq, dt=torch.float32)
+        self.logits = e(cfg.vocab_size)
+        self.key = e(1, dt=torch.int64)
+        self.token = e(1, dt=torch.int32)
+        self.pos = e(1, dt=torch.int64)
+        self.step_idx = e(1, dt=torch.int32)
+        self.max_steps = max_steps or max_seq_len
+        self.token_log = e(self.max_steps, dt=torch.int32)
+        self.error = e(1, dt=torch.int32)
+        self.use_graph = use_graph
+        self.graph = None
+        self._calls = self._build_calls()
+
+    # -- the kernel sequence of one step, as prepared ctypes calls (no allocation)
+    def _build_calls(self):
+        cfg, w = self.cfg, self.w
+        L = lib()
+        eps = ctypes.c_float(cfg.rms_norm_eps)
+        h, i, nq, nkv, D, bs = (cfg.hidden_size, cfg.intermediate_size, cfg.num_q_heads, cfg.num_kv_heads,
+                                cfg.head_dim, cfg.block_size)
+        scale = ctypes.c_float(cfg.attn_scale)
+        layer_stride = self.k_cache[0].numel() * 2
+        kc0, vc0 = self.k_cache.data_ptr(), self.v_cache.data_ptr()
+        calls = []
+        for li, lw in enumerate(w.layers):
+            kc = ctypes.c_void_p(kc0 + li * layer_stride)
+            vc = ctypes.c_void_p(vc0 + li * layer_stride)
+            if li == 0:
+                a, b, embed, tok = None, None, _vp(w.embed), _vp(self.token)
+            else:
+                a, b, embed, tok = _vp(self.down), _vp(self.resmid), None, None
+            calls.append((L.spark_qkv_rope_kvstore, "qkv", (
+                a, b, embed, tok, _vp(lw.in_norm), eps, _vp(self.res_attn), _vp(lw.qkv.qs), _vp(lw.qkv.d), h, nq,
+                nkv, D, _vp(w.cos_sin), _vp(self.pos), _vp(self.block_table), None, bs, kc, vc, _vp(self.q))))
+            calls.append((L.spark_attn_splitkv, "attn", (
+                _vp(self.q), kc, vc, _vp(self.block_table), _vp(self.pos), None, nq, nkv, D, bs, self.splits,
+                self.max_split_tokens, scale, _vp(self.part_o), _vp(self.part_lse), _vp(self.error))))
+            calls.append((L.spark_attn_combine, "combine", (
+                _vp(self.part_o), _vp(self.part_lse), self.splits, nq, D, _vp(self.attn_out))))
+            calls.append((L.spark_q4_gemv, "o_proj", (
+                _vp(self.attn_out), _vp(lw.o.qs), _vp(lw.o.d), _vp(self.oproj), h, nq * D, 1)))
+            calls.append((L.spark_rmsnorm_gate_up_silu, "gate_up", (
+                _vp(self.oproj), _vp(self.res_attn), _vp(lw.post_norm), eps, _vp(self.resmid), _vp(lw.gate_up.qs),
+                _vp(lw.gate_up.d), _vp(self.mid), 2 * i, h)))
+            calls.append((L.spark_q4_gemv, "down", (
+                _vp(self.mid), _vp(lw.down.qs), _vp(lw.down.d), _vp(self.down), h, i, 1)))
+        calls.append((L.spark_rmsnorm_q4_head_argmax, "head", (
+            _vp(self.down), _vp(self.resmid), _vp(w.final_norm), eps, _vp(w.head.qs), _vp(w.head.d),
+            _vp(self.logits), cfg.vocab_size, h, _vp(self.key))))
+        calls.append((L.spark_decode_finalize, "finalize", (
+            _vp(self.key), _vp(self.token), _vp(self.token_log), _vp(self.step_idx), _vp(self.pos))))
+        return calls
+
+    def kernels_per_step(self) -> int:
+        return len(self._calls)
+
+    def _enqueue(self):
+        stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        for fn, name, args in self._calls:
+            st = fn(*args, stream)
+            if st != 0:
+                raise RuntimeError(f"{name}: spark status {st}")
+
+    def capture(self):
+        """Capture one decode step into a CUDA graph (state is restored afterwards)."""
+        saved = [t.clone() for t in (self.pos, self.step_idx, self.token, self.key)]
+        kv_saved = None
+        s = torch.cuda.Stream(device=self.device)
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            self._enqueue()  # warm-up outside capture (also sets smem attributes)
+        torch.cuda.current_stream().wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self._enqueue()
+        torch.cuda.synchronize()
+        for dst, src in zip((self.pos, self.step_idx, self.token, self.key), saved):
+            dst.copy_(src)
+        del kv_saved
+        self.graph = g
+        return g
+
+    def reset(self, pos: int = 0):
+        self.pos.fill_(pos)
+        self.step_idx.zero_()
+        self.key.zero_()
+        self.error.zero_()
+
+    def step(self):
+        """Enqueue one decode step on the current stream (graph replay when captured)."""
+        if self.use_graph:
+            if self.graph is None:
+                self.capture()
+            self.graph.replay()
+        else:
+            self._enqueue()
+
+    def set_token(self, token: int | torch.Tensor):
+        if isinstance(token, torch.Tensor):
+            self.token.copy_(token.reshape(1), non_blocking=True)
+        else:
+            self.token.fill_(int(token))
+
+    def prefill(self, prompt: torch.Tensor | list[int], start_pos: int = 0):
+        """Feed prompt tokens one decode step each (KV cache fill through the decode path)."""
+        prompt = torch.as_tensor(prompt, dtype=torch.int32).to(self.device)
+        self.reset(start_pos)
+        for t in range(prompt.numel()):
+            self.token.copy_(prompt[t:t + 1])
+            self.step()
+        # the last step's argmax is the first generated token
+        return self.token.clone()
+
+    def generate(self, prompt, max_new_tokens: int) -> list[int]:
+        """Greedy decode: returns the generated token ids (host list)."""
+        first = self.prefill(prompt)
+        out = [first]
+        self.step_idx.zero_()
+        for _ in range(max_new_tokens - 1):
+            self.step()
+        torch.cuda.synchronize()
+        toks = self.token_log[:max_new_tokens - 1].cpu().tolist()
+        return [int(first.item())] + toks
