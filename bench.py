@@ -35,7 +35,7 @@ for _p in (str(ROOT), str(ROOT / "spark-vllm-ascend_b200")):
         sys.path.insert(0, _p)
 
 METRIC = "batch-1 decode tokens/s (synthetic 4B Q4_0, ctx 2048->2048+K)"
-PROMPT_LEN = 2048
+PROMPT_LEN = 2048  # overridable with --prompt (profiling runs use a short prompt)
 
 
 def _peaks():
@@ -234,11 +234,13 @@ def run_spark(args):
         sampler.start()
         time.sleep(0.4)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("timed")
     e0.record()
     for _ in range(args.steps):
         eng.graph.replay()
     e1.record()
     torch.cuda.synchronize()
+    torch.cuda.nvtx.range_pop()
     clocks = sampler.stop() if sampler else None
     ms = e0.elapsed_time(e1)
     if world > 1:
@@ -335,11 +337,82 @@ def run_spark(args):
 
 
 def run_reference(args):
+    """The reference's CPU implementation of the path, timed on the host cores.
+
+    The reference's own kernels need cannbotdsl + an Ascend NPU and cannot be built
+    or run here, so the reference arm runs the C restatement of its algorithm
+    (oracle/, OpenMP over all host threads).  One step is a bounded sample: one
+    decoder layer (layers taken in turn) or the final norm + LM head, at context
+    2048; 37 samples make one whole token, so tokens/s = (K / 37) / time.
+    Weights and the KV prefix are random bytes of the real shapes (values do not
+    change CPU time), generated with numpy; no GPU code is touched."""
     world, rank, _ = dist_setup()
     if rank != 0:
         return None
-    from reference_cpu import run as ref_run  # noqa: WPS433 (module beside bench.py)
-    return ref_run(args, METRIC, PROMPT_LEN)
+    import numpy as np
+    import oracle
+    from spark_b200.config import SparkConfig
+    cfg = SparkConfig()
+    threads = os.cpu_count() or 1
+    oracle.set_threads(threads)
+    rng = np.random.default_rng(0)
+    h, i, V = cfg.hidden_size, cfg.intermediate_size, cfg.vocab_size
+
+    def q4(n, k):
+        qs = rng.integers(0, 256, size=(n, k // 2), dtype=np.uint8)
+        d = rng.uniform(0.002, 0.01, size=(n, k // 32)).astype(np.float16).view(np.uint16)
+        return qs, d
+
+    def bfv(n, scale=1.0, base=0.0):
+        return oracle.f32_to_bf16((base + scale * rng.standard_normal(n)).astype(np.float32))
+
+    t_setup = time.perf_counter()
+    w = {"embed": bfv(V * h, 0.02).reshape(V, h), "final_norm": bfv(h, 0.02, 1.0)}
+    w["head_qs"], w["head_d"] = q4(V, h)
+    w["cos_sin"] = np.zeros((cfg.max_position, cfg.head_dim), np.uint16)
+    for li in range(cfg.num_layers):
+        p_ = f"layers.{li}."
+        w[p_ + "in_norm"], w[p_ + "post_norm"] = bfv(h, 0.02, 1.0), bfv(h, 0.02, 1.0)
+        for key, (n, k) in (("qkv", (cfg.qkv_rows, h)), ("o", (h, cfg.num_q_heads * cfg.head_dim)),
+                            ("gu", (2 * i, h)), ("down", (h, i))):
+            w[p_ + key + "_qs"], w[p_ + key + "_d"] = q4(n, k)
+    nblk = (PROMPT_LEN + 1 + 127) // 128
+    om = oracle.OracleModel(cfg, w, num_blocks=nblk, splits=args.splits)
+    om.kc[...] = rng.integers(0, 65536, size=om.kc.shape, dtype=np.uint16) & 0xBFFF  # finite bf16
+    om.vc[...] = rng.integers(0, 65536, size=om.vc.shape, dtype=np.uint16) & 0xBFFF
+    table = np.arange(nblk, dtype=np.int32)
+    a = w["embed"][1].copy()
+    b = np.zeros(h, np.uint16)
+    setup_s = time.perf_counter() - t_setup
+    units = cfg.num_layers + 1
+
+    def sample(j):
+        u = j % units
+        if u < cfg.num_layers:
+            om.layer(u, a, b, u > 0, table, PROMPT_LEN)
+        else:
+            om.head(a, b)
+
+    for j in range(args.warmup):
+        sample(j)
+    t0 = time.perf_counter()
+    for j in range(args.steps):
+        sample(j)
+    dt = time.perf_counter() - t0
+    tps = (args.steps / units) / dt
+    return {
+        "impl": "reference", "metric": METRIC, "value": round(tps, 4), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "q4_0 weights x fp32 accumulate, bf16 activations / KV",
+        "data": "synthetic: random Q4_0 codes / scales and bf16 KV prefix of the real shapes",
+        "config": {"workload": "configs[2]: synthetic 4B Q4_0 batch-1 decode, 2048 prompt, greedy",
+                   "layers": cfg.num_layers, "ctx": PROMPT_LEN, "splits": args.splits, "setup_s": round(setup_s, 1)},
+        "cpu_baseline": {"value": round(tps, 4), "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": f"{args.steps} samples of one layer (or the LM head) of a ctx-{PROMPT_LEN} "
+                                   f"decode step; {units} samples = 1 token"},
+        "e2e": {"value": round(tps, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
 
 
 def main(argv=None):
@@ -351,7 +424,10 @@ def main(argv=None):
     ap.add_argument("--splits", type=int, default=16)
     ap.add_argument("--cpu-tokens", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--prompt", type=int, default=2048, help="prompt length (2048 = the benchmark protocol)")
     args = ap.parse_args(argv)
+    global PROMPT_LEN
+    PROMPT_LEN = args.prompt
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     res = run_reference(args) if args.impl == "reference" else run_spark(args)

@@ -61,6 +61,8 @@ def lib():
             "orc_attn_combine": (None, [_P, _P, _I, _I, _I, _P]),
             "orc_argmax_bf16": (_I64, [_P, _I64]),
             "orc_decode_step": (_I64, [_P, _P, _P, _P, _P, _I64, _P, _I64, _I64, _F, _F, _P]),
+            "orc_decode_layer": (None, [_P, _P, _P, _P, _P, _P, _I64, _F, _F, _P, _P, _I]),
+            "orc_decode_head": (_I64, [_P, _P, _P, _P, _F, _P]),
             "orc_set_threads": (None, [_I]),
             "orc_get_threads": (_I, []),
         }
@@ -262,6 +264,19 @@ class OracleModel:
                         "down_qs", "down_d"):
                 lp.append(_p(weights[f"layers.{li}.{key}"]))
         self.layer_ptrs = (ctypes.c_void_p * len(lp))(*lp)
+
+    def layer(self, li: int, a: np.ndarray, b: np.ndarray, has_b: bool, table: np.ndarray, pos: int) -> None:
+        """One decoder layer in place: a <- down projection, b <- residual (resmid)."""
+        cfg = self.cfg
+        kc, vc = self.kc[li], self.vc[li]
+        lp = ctypes.cast(ctypes.byref(self.layer_ptrs, li * 10 * ctypes.sizeof(ctypes.c_void_p)),
+                         ctypes.POINTER(ctypes.c_void_p))
+        lib().orc_decode_layer(_p(self.dims), lp, _p(self.w["cos_sin"]), _p(kc), _p(vc),
+                               _p(np.ascontiguousarray(table, dtype=np.int32)), pos, cfg.rms_norm_eps,
+                               cfg.attn_scale, _p(a), _p(b), 1 if has_b else 0)
+
+    def head(self, a: np.ndarray, b: np.ndarray) -> int:
+        return int(lib().orc_decode_head(_p(self.dims), self.model_ptrs, _p(a), _p(b), self.cfg.rms_norm_eps, None))
 
     def step(self, table: np.ndarray, token: int, pos: int, want_logits: bool = False):
         cfg = self.cfg

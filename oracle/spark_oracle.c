@@ -477,23 +477,17 @@ ORC_API int64_t orc_argmax_bf16(const uint16_t* logits, int64_t n) {
  * model pointers: [embed bf16 [V][H], final_norm bf16 [H], head_qs, head_d, cos_sin bf16 [max_pos][D]]
  * layer pointers, 10 per layer: [in_norm, post_norm, qkv_qs, qkv_d, o_qs, o_d, gu_qs, gu_d, down_qs, down_d]
  *   qkv rows: q heads, then k heads, then v heads; gu rows: gate [I] then up [I].
- * kc / vc: bf16 [layers][blocks][nkv][bs][D]; table int32 shared by all layers.
- * Returns the greedy token; logits (bf16 [V]) written when non-NULL. */
-ORC_API int64_t orc_decode_step(const int64_t* dims, const void* const* model, const void* const* layers,
-                                uint16_t* kc, uint16_t* vc, int64_t nblocks, const int32_t* table, int64_t token,
-                                int64_t pos, float eps, float scale, uint16_t* logits) {
+ * kc / vc: bf16 [layers][blocks][nkv][bs][D]; table int32 shared by all layers. */
+
+/* One decoder layer.  In: a (bf16 [H]) and b (bf16 [H]; ignored for layer 0).
+ * Out: a <- down projection, b <- residual after attention (resmid).  kc / vc are
+ * this layer's caches [blocks][nkv][bs][D]; the new token is stored at pos. */
+ORC_API void orc_decode_layer(const int64_t* dims, const void* const* lp, const uint16_t* cos_sin, uint16_t* kc,
+                              uint16_t* vc, const int32_t* table, int64_t pos, float eps, float scale, uint16_t* a,
+                              uint16_t* b, int has_b) {
     int H = (int)dims[0], nq = (int)dims[1], nkv = (int)dims[2], D = (int)dims[3];
-    int I = (int)dims[4];
-    int64_t V = dims[5];
-    int L = (int)dims[6], bs = (int)dims[7], splits = (int)dims[8];
-    const uint16_t* embed = (const uint16_t*)model[0];
-    const uint16_t* fnorm = (const uint16_t*)model[1];
-    const uint8_t* hqs = (const uint8_t*)model[2];
-    const uint16_t* hd = (const uint16_t*)model[3];
-    const uint16_t* cs = (const uint16_t*)model[4];
+    int I = (int)dims[4], bs = (int)dims[7], splits = (int)dims[8];
     int64_t nqkv = (int64_t)(nq + 2 * nkv) * D;
-    uint16_t* a = (uint16_t*)malloc(2 * H);
-    uint16_t* b = (uint16_t*)malloc(2 * H);
     uint16_t* res = (uint16_t*)malloc(2 * H);
     uint16_t* x = (uint16_t*)malloc(2 * H);
     uint16_t* qkv = (uint16_t*)malloc(2 * nqkv);
@@ -502,37 +496,60 @@ ORC_API int64_t orc_decode_step(const int64_t* dims, const void* const* model, c
     uint16_t* mid = (uint16_t*)malloc(2 * (int64_t)I);
     float* po = (float*)malloc(sizeof(float) * splits * nq * D);
     float* pl = (float*)malloc(sizeof(float) * splits * nq);
-    int have_b = 0;
-    memcpy(a, embed + token * H, 2 * H);
     int64_t blk = table[pos / bs], off = pos % bs;
-    for (int li = 0; li < L; li++) {
-        const void* const* lp = layers + (int64_t)li * 10;
-        int64_t lkv = (int64_t)li * nblocks * nkv * bs * D;
-        /* input norm: s = a + b; res = bf16(s) */
-        orc_add_rmsnorm(a, have_b ? b : NULL, (const uint16_t*)lp[0], H, eps, res, x);
-        orc_q4_gemv(x, (const uint8_t*)lp[2], (const uint16_t*)lp[3], nqkv, H, 1, qkv);
-        orc_rope_neox(qkv, nq + nkv, D, cs + pos * D);
-        for (int hk = 0; hk < nkv; hk++) {
-            memcpy(kc + lkv + ((blk * nkv + hk) * bs + off) * D, qkv + (int64_t)(nq + hk) * D, 2 * D);
-            memcpy(vc + lkv + ((blk * nkv + hk) * bs + off) * D, qkv + (int64_t)(nq + nkv + hk) * D, 2 * D);
-        }
-        orc_attn_split(qkv, kc + lkv, vc + lkv, table, pos + 1, nq, nkv, D, bs, splits, scale, po, pl);
-        orc_attn_combine(po, pl, splits, nq, D, attn);
-        uint16_t* oproj = a; /* reuse */
-        orc_q4_gemv(attn, (const uint8_t*)lp[4], (const uint16_t*)lp[5], H, (int64_t)nq * D, 1, oproj);
-        /* post-attention norm: s = oproj + res -> resmid */
-        orc_add_rmsnorm(oproj, res, (const uint16_t*)lp[1], H, eps, b, x);
-        orc_q4_gemv(x, (const uint8_t*)lp[6], (const uint16_t*)lp[7], 2 * (int64_t)I, H, 1, gu);
-        orc_silu_mul(gu, gu + I, I, mid);
-        orc_q4_gemv(mid, (const uint8_t*)lp[8], (const uint16_t*)lp[9], H, I, 1, a);
-        have_b = 1; /* next layer: a = down, b = resmid */
+    /* input norm: s = a + b; res = bf16(s) */
+    orc_add_rmsnorm(a, has_b ? b : NULL, (const uint16_t*)lp[0], H, eps, res, x);
+    orc_q4_gemv(x, (const uint8_t*)lp[2], (const uint16_t*)lp[3], nqkv, H, 1, qkv);
+    orc_rope_neox(qkv, nq + nkv, D, cos_sin + pos * D);
+    for (int hk = 0; hk < nkv; hk++) {
+        memcpy(kc + ((blk * nkv + hk) * bs + off) * D, qkv + (int64_t)(nq + hk) * D, 2 * D);
+        memcpy(vc + ((blk * nkv + hk) * bs + off) * D, qkv + (int64_t)(nq + nkv + hk) * D, 2 * D);
     }
-    orc_add_rmsnorm(a, b, fnorm, H, eps, NULL, x);
+    orc_attn_split(qkv, kc, vc, table, pos + 1, nq, nkv, D, bs, splits, scale, po, pl);
+    orc_attn_combine(po, pl, splits, nq, D, attn);
+    /* o_proj -> a */
+    orc_q4_gemv(attn, (const uint8_t*)lp[4], (const uint16_t*)lp[5], H, (int64_t)nq * D, 1, a);
+    /* post-attention norm: s = oproj + res -> resmid (into b) */
+    orc_add_rmsnorm(a, res, (const uint16_t*)lp[1], H, eps, b, x);
+    orc_q4_gemv(x, (const uint8_t*)lp[6], (const uint16_t*)lp[7], 2 * (int64_t)I, H, 1, gu);
+    orc_silu_mul(gu, gu + I, I, mid);
+    orc_q4_gemv(mid, (const uint8_t*)lp[8], (const uint16_t*)lp[9], H, I, 1, a);
+    free(res); free(x); free(qkv); free(attn); free(gu); free(mid); free(po); free(pl);
+}
+
+/* Final norm of (a + b), LM head, greedy argmax; logits written when non-NULL. */
+ORC_API int64_t orc_decode_head(const int64_t* dims, const void* const* model, const uint16_t* a, const uint16_t* b,
+                                float eps, uint16_t* logits) {
+    int H = (int)dims[0];
+    int64_t V = dims[5];
+    uint16_t* x = (uint16_t*)malloc(2 * H);
+    orc_add_rmsnorm(a, b, (const uint16_t*)model[1], H, eps, NULL, x);
     uint16_t* lg = logits ? logits : (uint16_t*)malloc(2 * V);
-    orc_q4_gemv(x, hqs, hd, V, H, 1, lg);
+    orc_q4_gemv(x, (const uint8_t*)model[2], (const uint16_t*)model[3], V, H, 1, lg);
     int64_t tok = orc_argmax_bf16(lg, V);
     if (!logits) free(lg);
-    free(a); free(b); free(res); free(x); free(qkv); free(attn); free(gu); free(mid); free(po); free(pl);
+    free(x);
+    return tok;
+}
+
+/* One decode step of the whole model; returns the greedy token. */
+ORC_API int64_t orc_decode_step(const int64_t* dims, const void* const* model, const void* const* layers,
+                                uint16_t* kc, uint16_t* vc, int64_t nblocks, const int32_t* table, int64_t token,
+                                int64_t pos, float eps, float scale, uint16_t* logits) {
+    int H = (int)dims[0], nkv = (int)dims[2], D = (int)dims[3], L = (int)dims[6], bs = (int)dims[7];
+    const uint16_t* embed = (const uint16_t*)model[0];
+    const uint16_t* cs = (const uint16_t*)model[4];
+    uint16_t* a = (uint16_t*)malloc(2 * H);
+    uint16_t* b = (uint16_t*)malloc(2 * H);
+    memcpy(a, embed + token * H, 2 * H);
+    for (int li = 0; li < L; li++) {
+        int64_t lkv = (int64_t)li * nblocks * nkv * bs * D;
+        orc_decode_layer(dims, layers + (int64_t)li * 10, cs, kc + lkv, vc + lkv, table, pos, eps, scale, a, b,
+                         li > 0);
+    }
+    int64_t tok = orc_decode_head(dims, model, a, b, eps, logits);
+    free(a);
+    free(b);
     return tok;
 }
 
