@@ -152,6 +152,18 @@ int spark_slot_mapping(int64_t num_tokens, int64_t max_tokens, const int32_t* qu
 /* Enable / disable programmatic dependent launch on the kernels above (default on). */
 int spark_set_pdl(int enabled);
 
+/* Select the Q4_0 GEMV implementation for shapes with K % 512 == 0 and batch 1:
+ * 1 (default) = persistent kernel streaming weights through a cp.async.bulk
+ * shared-memory ring, 0 = register-direct kernel.  Both compute the same order
+ * and give bit-identical results. */
+int spark_set_gemv_ring(int enabled);
+
+/* Copy the library's device error word to *value (synchronous; diagnostics only)
+ * and clear it when reset != 0.  Non-zero means a kernel gave up a bounded wait
+ * (2/3: producer side, 4: consumer side of the ring GEMV); outputs of that launch
+ * are then incomplete. */
+int spark_read_device_error(int* value, int reset);
+
 #ifdef __cplusplus
 }
 #endif

@@ -52,6 +52,7 @@ def lib():
             "orc_q4_dequantize": (None, [_P, _P, _I64, _I64, _P]),
             "orc_q4_gemv_f32": (None, [_P, _P, _P, _I64, _I64, _I, _P]),
             "orc_q4_gemv": (None, [_P, _P, _P, _I64, _I64, _I, _P]),
+            "orc_q4_stage_x": (None, [_P, _I64, _P, _P, _P]),
             "orc_add_rmsnorm": (None, [_P, _P, _P, _I, _F, _P, _P]),
             "orc_rope_neox": (None, [_P, _I, _I, _P]),
             "orc_silu_mul": (None, [_P, _P, _I64, _P]),
@@ -138,6 +139,17 @@ def q4_gemv(x_bf16: np.ndarray, qs: np.ndarray, d: np.ndarray) -> np.ndarray:
     y = np.empty((batch, n), np.uint16)
     lib().orc_q4_gemv(_p(x), _p(np.ascontiguousarray(qs)), _p(np.ascontiguousarray(d)), n, k, batch, _p(y))
     return y
+
+
+def q4_stage_x(x_f32: np.ndarray):
+    """Per-block 16-bit fixed point of x: (X int16 [k], sx fp32 [k/32], C int32 [k/32])."""
+    x = np.ascontiguousarray(x_f32, dtype=np.float32)
+    k = x.size
+    X = np.empty(k, np.int16)
+    sx = np.empty(k // 32, np.float32)
+    C = np.empty(k // 32, np.int32)
+    lib().orc_q4_stage_x(_p(x), k, _p(X), _p(sx), _p(C))
+    return X, sx, C
 
 
 def q4_gemv_f32(x_f32: np.ndarray, qs: np.ndarray, d: np.ndarray) -> np.ndarray:

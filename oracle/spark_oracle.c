@@ -27,11 +27,11 @@
  *                              variant is linear.py:228-260.
  *
  * Canonical orders (shared with the CUDA kernels):
- *   GEMV row: a row is split over 16 lanes; lane l owns Q4_0 blocks l, l+16, l+32, ...
- *     For each block: a0 = fma chain over elements 0..15, a1 = fma chain over 16..31
- *     (value (q-8) * x, starting from 0), block sum = a0 + a1,
- *     lane acc = fma(d, block sum, acc).  The 16 lane sums are combined by an
- *     xor butterfly with offsets 8,4,2,1 (v[l] = v[l] + v[l^off]).
+ *   GEMV: x is staged once per call as exact 16-bit fixed point per 32-element
+ *     block (power-of-two scale from the block maximum, see stage_block).  A row is
+ *     split over 16 lanes; lane l owns Q4_0 blocks l, l+16, ...  A block's dot
+ *     product sum (q-8) * X is an exact integer P; lane acc = fma(d * 2^-S, P, acc).
+ *     The 16 lane sums are combined by an xor butterfly 8,4,2,1 (v[l] += v[l^off]).
  *   RMSNorm: 32 lanes, lane l sums s_i*s_i (product, then add) for i = l mod 32 in
  *     ascending order, xor butterfly 16,8,4,2,1.
  *   Attention scores: a0 over even dims, a1 over odd dims (fma), score = (a0+a1)*scale.
@@ -245,20 +245,71 @@ static inline void butterfly(float* v, int n) {
     }
 }
 
-/* one row dot product in the canonical order; x is fp32 [k] */
-static float q4_row_dot(const uint8_t* qs, const uint16_t* d, const float* x, int64_t nb) {
+/* Activation staging (once per GEMV call, shared by all rows).  Each 32-element
+ * block b of x becomes exact 16-bit fixed point with a power-of-two scale:
+ *   M = max_j |x_j|; blocks with M < 2^-100 (or M not finite) are all zero;
+ *   e = floor(log2 M), S = 14 - e, X_j = rint(x_j * 2^S) (|X_j| <= 32640),
+ *   sx = 2^-S, C = 8 * sum_j X_j.
+ * Elements within 2^7 of the block maximum are represented exactly (x is bf16,
+ * 8 significant bits); smaller ones are rounded to nearest-even at 2^(e-14). */
+typedef struct {
+    int16_t X[32];
+    float sx;
+    int32_t C;
+} xq_block;
+
+static inline float pow2f(int e) { return u2f((uint32_t)(e + 127) << 23); } /* -126 <= e <= 127 */
+
+static void stage_block(const float* x, xq_block* o) {
+    float M = 0.0f;
+    for (int j = 0; j < 32; j++) {
+        float a = fabsf(x[j]);
+        if (a > M) M = a;
+    }
+    if (!(M >= 7.888609052210118e-31f) || M == INFINITY) { /* M < 2^-100 or NaN / inf */
+        memset(o->X, 0, sizeof(o->X));
+        o->sx = 1.0f;
+        o->C = 0;
+        return;
+    }
+    int e = (int)((f2u(M) >> 23) & 0xff) - 127; /* M is normal here */
+    int S = 14 - e;
+    float sc = pow2f(S);
+    int32_t sum = 0;
+    for (int j = 0; j < 32; j++) {
+        int v = (int)rintf(x[j] * sc);
+        o->X[j] = (int16_t)v;
+        sum += v;
+    }
+    o->sx = pow2f(-S);
+    o->C = 8 * sum;
+}
+
+ORC_API void orc_q4_stage_x(const float* x, int64_t k, int16_t* X, float* sx, int32_t* C) {
+    for (int64_t b = 0; b < k / 32; b++) {
+        xq_block blk;
+        stage_block(x + b * 32, &blk);
+        memcpy(X + b * 32, blk.X, sizeof(blk.X));
+        sx[b] = blk.sx;
+        C[b] = blk.C;
+    }
+}
+
+/* One row in the canonical order.  Per block: P = sum_j q_j X_j - C (exact int32,
+ * |P| < 2^24), ds = fp32(d) * sx, lane acc = fma(ds, (float)P, acc); lane l owns
+ * blocks l, l+16, ...; the 16 lane sums are combined by an xor butterfly 8,4,2,1. */
+static float q4_row_dot(const uint8_t* qs, const uint16_t* d, const xq_block* xb, int64_t nb) {
     float lane[16];
     for (int l = 0; l < 16; l++) {
         float acc = 0.0f;
         for (int64_t b = l; b < nb; b += 16) {
             const uint8_t* q = qs + b * 16;
-            const float* xb = x + b * 32;
-            float a0 = 0.0f, a1 = 0.0f;
-            for (int e = 0; e < 16; e++) {
-                a0 = fmaf((float)((int)(q[e] & 15) - 8), xb[e], a0);
-                a1 = fmaf((float)((int)(q[e] >> 4) - 8), xb[e + 16], a1);
-            }
-            acc = fmaf(h2f(d[b]), a0 + a1, acc);
+            const xq_block* xx = xb + b;
+            int32_t P = 0;
+            for (int e = 0; e < 16; e++) P += (int32_t)(q[e] & 15) * xx->X[e] + (int32_t)(q[e] >> 4) * xx->X[e + 16];
+            P -= xx->C;
+            float ds = h2f(d[b]) * xx->sx;
+            acc = fmaf(ds, (float)P, acc);
         }
         lane[l] = acc;
     }
@@ -266,14 +317,18 @@ static float q4_row_dot(const uint8_t* qs, const uint16_t* d, const float* x, in
     return lane[0];
 }
 
-/* y[bt][n] = bf16( sum_k W[n][k] * x[bt][k] ), batch rows of x */
+/* y[bt][n] = sum_k W[n][k] * x[bt][k] (unrounded fp32), batch rows of x */
 ORC_API void orc_q4_gemv_f32(const float* x, const uint8_t* qs, const uint16_t* d, int64_t n, int64_t k,
                              int batch, float* y) {
     int64_t nb = k / 32;
+    xq_block* xb = (xq_block*)malloc(sizeof(xq_block) * nb * batch);
+    for (int bt = 0; bt < batch; bt++)
+        for (int64_t b = 0; b < nb; b++) stage_block(x + (int64_t)bt * k + b * 32, xb + (int64_t)bt * nb + b);
 #pragma omp parallel for schedule(static)
     for (int64_t r = 0; r < n; r++)
         for (int bt = 0; bt < batch; bt++)
-            y[(int64_t)bt * n + r] = q4_row_dot(qs + r * (k / 2), d + r * nb, x + (int64_t)bt * k, nb);
+            y[(int64_t)bt * n + r] = q4_row_dot(qs + r * (k / 2), d + r * nb, xb + (int64_t)bt * nb, nb);
+    free(xb);
 }
 
 ORC_API void orc_q4_gemv(const uint16_t* x, const uint8_t* qs, const uint16_t* d, int64_t n, int64_t k,

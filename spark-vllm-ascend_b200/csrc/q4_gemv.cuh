@@ -11,56 +11,96 @@
 // A row is read by 16 lanes (a half warp) with 128-bit loads: lane l owns blocks
 // l, l+16, ... so one load instruction of a half warp covers 256 contiguous bytes.
 //
-// Arithmetic per block (canonical order, mirrored by the CPU oracle):
-//   nibble -> exact (q - 8) in fp32 with one LOP3 per value (a magic exponent chosen
-//   per nibble position) and one packed f32x2 subtract per pair, then packed f32x2
-//   FMAs: lane .x accumulates elements 0..15, lane .y elements 16..31, in ascending
-//   order; block sum = .x + .y; row acc = fma(d, block sum, acc).  The 16 per-lane
-//   row sums are combined with an xor butterfly (8, 4, 2, 1) and rounded to bf16.
+// Arithmetic (canonical order, mirrored by the CPU oracle):
+//   * once per call the activation x is staged in shared memory as exact 16-bit
+//     fixed point per 32-element block: M = max |x_j|, S = 14 - floor(log2 M),
+//     X_j = rint(x_j * 2^S), sx = 2^-S, C = 8 * sum X_j (blocks with M < 2^-100
+//     are zero).  X_j is split into a signed high byte and an unsigned low byte,
+//     packed four elements per 32-bit word in the order the nibble words need;
+//   * per weight block: P = sum_j (q_j - 8) X_j is computed exactly with dp4a
+//     (low nibbles v & 0x0f0f0f0f, high nibbles v & 0xf0f0f0f0 = 16 q), then
+//     lane acc = fma(fp32(d) * sx, float(P), acc) -- |P| < 2^24, so float(P) is exact;
+//   * the 16 per-lane row sums are combined with an xor butterfly (8, 4, 2, 1) and
+//     rounded to bf16.
 #pragma once
 
 #include "common.cuh"
 
 namespace spark {
 
-// x staging in shared memory (fp32), per batch row: float4 slot (w*2+h)*nb + b holds
-// (x[32b+4w+2h], x[32b+4w+2h+16], x[32b+4w+2h+1], x[32b+4w+2h+17]), i.e. the two
-// (element, element+16) pairs that word w of block b multiplies with.
-__device__ __forceinline__ int xs_index(int e, int nb) {
-  int b = e >> 5, j = e & 31, hi = j >> 4, lo = j & 15;
-  int w = lo >> 2, k = lo & 3, h = k >> 1;
-  return (((w * 2 + h) * nb + b) << 2) + ((k & 1) << 1) + hi;
-}
+// ------------------------------------------------------------------ fixed-point x staging
+// Shared-memory layout of one staged activation row with nb blocks:
+//   xq  uint4 [4][nb]: xq[w*nb + b] = (hi bytes of X[4w..4w+3], lo bytes of X[4w..4w+3],
+//                                     hi bytes of X[16+4w..16+4w+3], lo bytes of the same)
+//   xm  float2 [nb]:   (sx, C as int bits)
+constexpr float kStageMinMax = 7.888609052210118e-31f;  // 2^-100
 
-// dequantize one 32-bit word (8 nibbles) into 4 exact (q-8) pairs
-__device__ __forceinline__ void dequant_word(uint32_t v, float2& w0, float2& w1, float2& w2, float2& w3) {
-  const uint32_t u = v >> 12;
-  w0 = make_float2(__uint_as_float((v & 0x0000000fu) | 0x4b000000u), __uint_as_float((v & 0x000000f0u) | 0x49000000u));
-  w1 = make_float2(__uint_as_float((v & 0x00000f00u) | 0x47000000u), __uint_as_float((v & 0x0000f000u) | 0x45000000u));
-  w2 = make_float2(__uint_as_float((v & 0x000f0000u) | 0x43000000u), __uint_as_float((u & 0x00000f00u) | 0x47000000u));
-  w3 = make_float2(__uint_as_float((u & 0x0000f000u) | 0x45000000u), __uint_as_float((u & 0x000f0000u) | 0x43000000u));
-  w0 = __fadd2_rn(w0, make_float2(-8388616.0f, -524296.0f));
-  w1 = __fadd2_rn(w1, make_float2(-32776.0f, -2056.0f));
-  w2 = __fadd2_rn(w2, make_float2(-136.0f, -32776.0f));
-  w3 = __fadd2_rn(w3, make_float2(-2056.0f, -136.0f));
-}
-
-// block sum (a0 + a1) of one 32-weight block against staged x
-__device__ __forceinline__ float block_dot(const uint4 q, const float4* __restrict__ xs, int nb, int b) {
-  float2 a = make_float2(0.0f, 0.0f);
-  const uint32_t words[4] = {q.x, q.y, q.z, q.w};
+__device__ __forceinline__ void stage_block_q(const float (&v)[32], uint4* xq, float2* xm, int nb, int b) {
+  float M = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 32; j++) M = fmaxf(M, fabsf(v[j]));
+  int X[32];
+  float sx = 1.0f;
+  int sum = 0;
+  if (M >= kStageMinMax && M != __int_as_float(0x7f800000)) {
+    const int e = (int)((__float_as_uint(M) >> 23) & 0xffu) - 127;
+    const int S = 14 - e;
+    const float sc = __uint_as_float((uint32_t)(S + 127) << 23);
+#pragma unroll
+    for (int j = 0; j < 32; j++) {
+      X[j] = __float2int_rn(__fmul_rn(v[j], sc));
+      sum += X[j];
+    }
+    sx = __uint_as_float((uint32_t)(127 - S) << 23);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; j++) X[j] = 0;
+  }
 #pragma unroll
   for (int w = 0; w < 4; w++) {
-    float2 w0, w1, w2, w3;
-    dequant_word(words[w], w0, w1, w2, w3);
-    const float4 x01 = xs[(w * 2 + 0) * nb + b];
-    const float4 x23 = xs[(w * 2 + 1) * nb + b];
-    a = __ffma2_rn(w0, make_float2(x01.x, x01.y), a);
-    a = __ffma2_rn(w1, make_float2(x01.z, x01.w), a);
-    a = __ffma2_rn(w2, make_float2(x23.x, x23.y), a);
-    a = __ffma2_rn(w3, make_float2(x23.z, x23.w), a);
+    uint32_t hl = 0, ll = 0, hh = 0, lh = 0;
+#pragma unroll
+    for (int t = 0; t < 4; t++) {
+      const int a = X[4 * w + t], c = X[16 + 4 * w + t];
+      hl |= (uint32_t)((a >> 8) & 0xff) << (8 * t);
+      ll |= (uint32_t)(a & 0xff) << (8 * t);
+      hh |= (uint32_t)((c >> 8) & 0xff) << (8 * t);
+      lh |= (uint32_t)(c & 0xff) << (8 * t);
+    }
+    xq[w * nb + b] = make_uint4(hl, ll, hh, lh);
   }
-  return __fadd_rn(a.x, a.y);
+  xm[b] = make_float2(sx, __int_as_float(8 * sum));
+}
+
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+// exact integer dot product of one Q4_0 block with its staged x block (before -C):
+// xb points at xq[b]; consecutive words of the block are `stride` uint4 apart
+__device__ __forceinline__ int block_int_dot(const uint4 q, const uint4* __restrict__ xb, int stride) {
+  const uint32_t words[4] = {q.x, q.y, q.z, q.w};
+  int A = 0, Cc = 0;
+  uint32_t B = 0, D = 0;
+#pragma unroll
+  for (int w = 0; w < 4; w++) {
+    const uint32_t lo = words[w] & 0x0f0f0f0fu, hi = words[w] & 0xf0f0f0f0u;
+    const uint4 xw = xb[w * stride];
+    A = dp4a_us(lo, xw.x, A);
+    B = __dp4a(lo, xw.y, B);
+    Cc = dp4a_us(hi, xw.z, Cc);
+    D = __dp4a(hi, xw.w, D);
+  }
+  return A * 256 + (int)B + Cc * 16 + (int)(D >> 4);
+}
+
+// lane accumulation of one block: acc = fma(fp32(d) * sx, float(P - C), acc)
+__device__ __forceinline__ float block_accum(float acc, uint16_t d, const uint4 q, const uint4* __restrict__ xb,
+                                             int stride, const float2 m) {
+  const int P = block_int_dot(q, xb, stride) - __float_as_int(m.y);
+  return __fmaf_rn(__fmul_rn(h2f(d), m.x), __int2float_rn(P), acc);
 }
 
 // ------------------------------------------------------------------ argument block
@@ -93,14 +133,26 @@ struct GemvArgs {
   // silu-mul epilogue: gate rows [0, n/2), up rows [n/2, n)
   // argmax epilogue
   unsigned long long* argmax_key;
+  int* error;  // device error word (ring kernel: bounded-wait timeouts), may be null
 };
 
 // ------------------------------------------------------------------ prologues
+// Prologues.  sync(n) is the barrier among the n staging threads: all threads of
+// the CTA for the register-direct kernel (n == blockDim.x), the consumer warps
+// (named barrier 1) for the ring kernel.
+__device__ __forceinline__ void staging_sync(int n) {
+  if (n == (int)blockDim.x)
+    __syncthreads();
+  else
+    asm volatile("bar.sync 1, %0;" ::"r"(n) : "memory");
+}
 struct ProPlain {
   static constexpr bool kNorm = false;
+  __device__ static void sync(int n) { staging_sync(n); }
 };
 struct ProNorm {
   static constexpr bool kNorm = true;
+  __device__ static void sync(int n) { staging_sync(n); }
 };
 
 // ------------------------------------------------------------------ epilogues
@@ -117,6 +169,9 @@ struct EpiPlain {
   __device__ static void store(const GemvArgs& g, EpiState& st, int bt, int p, int r0, int r1, float s0, float s1) {
     uint32_t packed = (uint32_t)f2bf(s0) | ((uint32_t)f2bf(s1) << 16);
     *reinterpret_cast<uint32_t*>(g.y + (size_t)bt * g.n + r0) = packed;
+  }
+  __device__ static void store_row(const GemvArgs& g, EpiState& st, int bt, int r, float s) {
+    g.y[(size_t)bt * g.n + r] = f2bf(s);
   }
   template <int BATCH>
   __device__ static void finish(const GemvArgs& g, EpiState& st, unsigned long long* red) {}
@@ -141,6 +196,12 @@ struct EpiArgmax {
     *reinterpret_cast<uint32_t*>(g.y + (size_t)bt * g.n + r0) = (uint32_t)b0 | ((uint32_t)b1 << 16);
     unsigned long long k0 = key(b0, r0), k1 = key(b1, r1);
     unsigned long long k = k0 > k1 ? k0 : k1;
+    if (k > st.best[bt]) st.best[bt] = k;
+  }
+  __device__ static void store_row(const GemvArgs& g, EpiState& st, int bt, int r, float s) {
+    uint16_t b = f2bf(s);
+    g.y[(size_t)bt * g.n + r] = b;
+    unsigned long long k = key(b, r);
     if (k > st.best[bt]) st.best[bt] = k;
   }
   template <int BATCH>
@@ -184,7 +245,9 @@ struct EpiSiluMul {
 
 struct EpiRope {
   // rows: q heads [0, nq*D), k heads [nq*D, (nq+nkv)*D), v heads after.
-  // q/k pairs rotate (i, i + D/2) of one head (neox); v pairs are adjacent rows.
+  // q/k pairs rotate (i, i + D/2) of one head (neox).  v pairs are
+  // (vbase + t, vbase + t + nkv*D/2): any pairing works for v, and this one keeps
+  // each side of a run of pairs contiguous in memory.
   __device__ static int num_pairs(const GemvArgs& g) { return g.n >> 1; }
   __device__ static void rows(const GemvArgs& g, int p, int& r0, int& r1) {
     const int half = g.head_dim >> 1;
@@ -194,8 +257,8 @@ struct EpiRope {
       r0 = h * g.head_dim + i;
       r1 = r0 + half;
     } else {
-      r0 = (g.nq + g.nkv) * g.head_dim + 2 * (p - rot_pairs);
-      r1 = r0 + 1;
+      r0 = (g.nq + g.nkv) * g.head_dim + (p - rot_pairs);
+      r1 = r0 + g.nkv * half;
     }
   }
   __device__ static int64_t position(const GemvArgs& g) { return g.pos64 ? g.pos64[0] : (int64_t)g.pos32[0]; }
@@ -203,6 +266,13 @@ struct EpiRope {
     if (g.slot_mapping) return g.slot_mapping[0];
     int64_t blk = pos / g.block_size;
     return (int64_t)g.block_table[blk] * g.block_size + (pos - blk * g.block_size);
+  }
+  __device__ static void store_v(const GemvArgs& g, int64_t sl, int r, float s) {
+    const int D = g.head_dim;
+    int e = r - (g.nq + g.nkv) * D;
+    int hk = e / D, dd = e - hk * D;
+    int64_t blk = sl / g.block_size, off = sl - blk * g.block_size;
+    g.v_cache[((blk * g.nkv + hk) * g.block_size + off) * D + dd] = f2bf(s);
   }
   __device__ static void store(const GemvArgs& g, EpiState& st, int bt, int p, int r0, int r1, float s0, float s1) {
     const int D = g.head_dim, half = D >> 1;
@@ -232,11 +302,8 @@ struct EpiRope {
     } else {
       int64_t sl = slot(g, pos);
       if (sl >= 0) {
-        int e = r0 - (g.nq + g.nkv) * D;
-        int hk = e / D, dd = e - hk * D;
-        int64_t blk = sl / g.block_size, off = sl - blk * g.block_size;
-        uint16_t* dst = g.v_cache + ((blk * g.nkv + hk) * g.block_size + off) * D + dd;
-        *reinterpret_cast<uint32_t*>(dst) = (uint32_t)f2bf(s0) | ((uint32_t)f2bf(s1) << 16);
+        store_v(g, sl, r0, s0);
+        store_v(g, sl, r1, s1);
       }
     }
   }
@@ -245,67 +312,82 @@ struct EpiRope {
 };
 
 // ------------------------------------------------------------------ x staging
-// Plain: x bf16 [batch][k] -> xs.  Norm: s = a + b, res_out = bf16(s) (CTA 0),
-// ss by warp 0 in the canonical 32-lane order, y = bf16((s * inv) * gamma).
+// smem per batch row: xq (64 * nb bytes) then xm (8 * nb bytes); after all batch
+// rows: red (40 floats) and, for the norm prologue, slin (k floats).
+// Plain: x bf16 [batch][k].  Norm: s = a + b, res_out = bf16(s) (CTA 0), ss by
+// warp 0 in the canonical 32-lane order, x = bf16((s * inv) * gamma).
 template <class Pro, int BATCH>
-__device__ __forceinline__ void stage_x(const GemvArgs& g, float* xs, float* red) {
+__device__ __forceinline__ void stage_x(const GemvArgs& g, unsigned char* smem, float* red, float* slin, int tid,
+                                        int nthreads) {
   const int k = g.k, nb = k >> 5;
   if constexpr (!Pro::kNorm) {
     for (int bt = 0; bt < BATCH; bt++) {
-      const uint32_t* src = reinterpret_cast<const uint32_t*>(g.x + (size_t)bt * k);
-      float* dst = xs + (size_t)bt * k;
-      for (int i = threadIdx.x; i < (k >> 1); i += blockDim.x) {
-        uint32_t v = bt < g.batch ? src[i] : 0u;
-        dst[xs_index(2 * i, nb)] = bf_lo(v);
-        dst[xs_index(2 * i + 1, nb)] = bf_hi(v);
+      uint4* xq = reinterpret_cast<uint4*>(smem + (size_t)bt * 72 * nb);
+      float2* xm = reinterpret_cast<float2*>(smem + (size_t)bt * 72 * nb + 64 * nb);
+      const uint4* src = reinterpret_cast<const uint4*>(g.x + (size_t)bt * k);
+      for (int b = tid; b < nb; b += nthreads) {
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const uint4 u = bt < g.batch ? src[b * 4 + i] : make_uint4(0, 0, 0, 0);
+          const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+          for (int t = 0; t < 4; t++) {
+            v[8 * i + 2 * t] = bf_lo(w4[t]);
+            v[8 * i + 2 * t + 1] = bf_hi(w4[t]);
+          }
+        }
+        stage_block_q(v, xq, xm, nb, b);
       }
     }
-    __syncthreads();
   } else {
-    // phase 1: s = a + b into xs (fp32), residual out
     const uint16_t* arow = g.embed ? g.embed + (size_t)g.token[0] * k : g.a;
     const uint32_t* pa = reinterpret_cast<const uint32_t*>(arow);
     const uint32_t* pb = reinterpret_cast<const uint32_t*>(g.b);
     const bool write_res = (g.res_out != nullptr) && blockIdx.x == 0;
-    for (int i = threadIdx.x; i < (k >> 1); i += blockDim.x) {
-      uint32_t va = pa[i];
+    for (int i = tid; i < (k >> 1); i += nthreads) {
+      const uint32_t va = pa[i];
       float s0, s1;
       if (pb) {
-        uint32_t vb = pb[i];
+        const uint32_t vb = pb[i];
         s0 = __fadd_rn(bf_lo(va), bf_lo(vb));
         s1 = __fadd_rn(bf_hi(va), bf_hi(vb));
       } else {
         s0 = bf_lo(va);
         s1 = bf_hi(va);
       }
-      xs[xs_index(2 * i, nb)] = s0;
-      xs[xs_index(2 * i + 1, nb)] = s1;
-      if (write_res)
-        reinterpret_cast<uint32_t*>(g.res_out)[i] = (uint32_t)f2bf(s0) | ((uint32_t)f2bf(s1) << 16);
+      reinterpret_cast<float2*>(slin)[i] = make_float2(s0, s1);
+      if (write_res) reinterpret_cast<uint32_t*>(g.res_out)[i] = (uint32_t)f2bf(s0) | ((uint32_t)f2bf(s1) << 16);
     }
-    __syncthreads();
-    // phase 2: canonical sum of squares (warp 0)
-    if (threadIdx.x < 32) {
+    Pro::sync(nthreads);
+    if (tid < 32) {
       float acc = 0.0f;
-      for (int i = threadIdx.x; i < k; i += 32) {
-        float s = xs[xs_index(i, nb)];
-        acc = __fadd_rn(acc, __fmul_rn(s, s));
+#pragma unroll 8
+      for (int i = tid; i < k; i += 32) {
+        const float sv = slin[i];
+        acc = __fadd_rn(acc, __fmul_rn(sv, sv));
       }
       acc = butterfly_sum<32>(acc);
-      if (threadIdx.x == 0) {
-        float root = __fsqrt_rn(__fadd_rn(__fmul_rn(acc, g.inv_k), g.eps));
-        red[0] = __fdiv_rn(1.0f, root);
-      }
+      if (tid == 0) red[0] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(acc, g.inv_k), g.eps)));
     }
-    __syncthreads();
-    // phase 3: y = bf16((s * inv) * gamma) in place
+    Pro::sync(nthreads);
     const float inv = red[0];
-    for (int i = threadIdx.x; i < k; i += blockDim.x) {
-      int idx = xs_index(i, nb);
-      xs[idx] = bf2f(f2bf(__fmul_rn(__fmul_rn(xs[idx], inv), bf2f(g.gamma[i]))));
+    uint4* xq = reinterpret_cast<uint4*>(smem);
+    float2* xm = reinterpret_cast<float2*>(smem + 64 * nb);
+    const uint32_t* pg = reinterpret_cast<const uint32_t*>(g.gamma);
+    for (int b = tid; b < nb; b += nthreads) {
+      float v[32];
+#pragma unroll
+      for (int j = 0; j < 16; j++) {
+        const uint32_t gv = pg[b * 16 + j];
+        const float2 sv = reinterpret_cast<const float2*>(slin)[b * 16 + j];
+        v[2 * j] = bf2f(f2bf(__fmul_rn(__fmul_rn(sv.x, inv), bf_lo(gv))));
+        v[2 * j + 1] = bf2f(f2bf(__fmul_rn(__fmul_rn(sv.y, inv), bf_hi(gv))));
+      }
+      stage_block_q(v, xq, xm, nb, b);
     }
-    __syncthreads();
   }
+  Pro::sync(nthreads);
 }
 
 // ------------------------------------------------------------------ the kernel
@@ -315,19 +397,18 @@ __device__ __forceinline__ void stage_x(const GemvArgs& g, float* xs, float* red
 // interleaved across CTAs so that every SM gets an even share.
 template <class Pro, class Epi, int BATCH, int NBL>
 __global__ void __launch_bounds__(256) q4_gemv_kernel(const GemvArgs g) {
-  extern __shared__ __align__(16) float smem[];
-  float* xs = smem;
-  float* red = smem + (size_t)BATCH * g.k;
+  extern __shared__ __align__(16) unsigned char smem_u8[];
+  const int nb = g.k >> 5;
+  float* red = reinterpret_cast<float*>(smem_u8 + (size_t)BATCH * 72 * nb);
+  float* slin = red + 40;
 
   pdl_launch_dependents();
   pdl_wait();
-  stage_x<Pro, BATCH>(g, xs, red);
+  stage_x<Pro, BATCH>(g, smem_u8, red, slin, threadIdx.x, blockDim.x);
 
   const int lane = threadIdx.x & 31, hl = lane & 15, half = lane >> 4, warp = threadIdx.x >> 5;
-  const int nb = g.k >> 5;
   const int npairs = Epi::num_pairs(g);
   const int warps_total = gridDim.x * (blockDim.x >> 5);
-  const float4* xs4 = reinterpret_cast<const float4*>(xs);
   const size_t row_bytes = (size_t)g.k >> 1;
   const int my_blocks = nb > hl ? (nb - hl + 15) >> 4 : 0;
   EpiState st;
@@ -366,12 +447,12 @@ __global__ void __launch_bounds__(256) q4_gemv_kernel(const GemvArgs g) {
       for (int j = 0; j < NBL; j++) {
         const int b = hl + 16 * (j0 + j);
         if (j0 + j < nblk) {
-          const float sc0 = h2f(s0[j]), sc1 = h2f(s1[j]);
 #pragma unroll
           for (int bt = 0; bt < BATCH; bt++) {
-            const float4* xb = xs4 + (size_t)bt * (g.k >> 2);
-            acc0[bt] = __fmaf_rn(sc0, block_dot(wq0[j], xb, nb, b), acc0[bt]);
-            acc1[bt] = __fmaf_rn(sc1, block_dot(wq1[j], xb, nb, b), acc1[bt]);
+            const uint4* xq = reinterpret_cast<const uint4*>(smem_u8 + (size_t)bt * 72 * nb);
+            const float2 m = reinterpret_cast<const float2*>(smem_u8 + (size_t)bt * 72 * nb + 64 * nb)[b];
+            acc0[bt] = block_accum(acc0[bt], s0[j], wq0[j], xq + b, nb, m);
+            acc1[bt] = block_accum(acc1[bt], s1[j], wq1[j], xq + b, nb, m);
           }
         }
       }
@@ -387,7 +468,7 @@ __global__ void __launch_bounds__(256) q4_gemv_kernel(const GemvArgs g) {
         if (bt < g.batch) Epi::store(g, st, bt, p, r0, r1, acc0[bt], acc1[bt]);
     }
   }
-  Epi::template finish<BATCH>(g, st, reinterpret_cast<unsigned long long*>(red + 4));
+  Epi::template finish<BATCH>(g, st, reinterpret_cast<unsigned long long*>(red + 8));
 }
 
 }  // namespace spark

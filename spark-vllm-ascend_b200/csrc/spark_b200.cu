@@ -15,13 +15,19 @@
 #include "attention.cuh"
 #include "misc.cuh"
 #include "q4_gemv.cuh"
+#include "q4_gemv_ring.cuh"
 #include "spark_b200.h"
 
 using namespace spark;
 
+// Device error word: set by kernels whose bounded waits time out (never by a
+// successful run).  Read with spark_read_device_error.
+__device__ int g_spark_error_word;
+
 namespace {
 
 int g_pdl = 1;
+int g_ring = 1;
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
@@ -102,7 +108,7 @@ int gemv_launch_b(const GemvArgs& g, cudaStream_t st) {
   if (grid < sms) grid = duos < sms ? duos : sms;  // spread thin work over all SMs
   if (grid > cap) grid = cap;
   if (grid < 1) grid = 1;
-  const size_t smem = (size_t)BATCH * g.k * sizeof(float) + 128;
+  const size_t smem = (size_t)BATCH * (g.k / 32) * 72 + 160 + (Pro::kNorm ? (size_t)g.k * 4 : 0);
   if (smem > 227 * 1024) return kErrTooLarge;
   if (bpl <= 2) return launch(q4_gemv_kernel<Pro, Epi, BATCH, 2>, dim3(grid), dim3(256), smem, st, g);
   if (bpl <= 5) return launch(q4_gemv_kernel<Pro, Epi, BATCH, 5>, dim3(grid), dim3(256), smem, st, g);
@@ -115,6 +121,82 @@ int check_q4(const uint8_t* qs, const uint16_t* d, int n, int k) {
   if (n <= 0 || k <= 0 || (n & 1) || (k % 32)) return kErrUnsupportedShape;
   if (!aligned(qs, 16) || !aligned(d, 2)) return kErrAlignment;
   return kOk;
+}
+
+int* device_error_ptr() {
+  static int* cached[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (!cached[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_spark_error_word) != cudaSuccess) return nullptr;
+    cached[dev] = static_cast<int*>(p);
+  }
+  return cached[dev];
+}
+
+// The ring kernel copies whole rows, so it needs the fp16 scale rows (K/16 bytes)
+// to be multiples of 16 bytes (K % 256 == 0) and 16-byte aligned planes; other
+// shapes and batch > 1 use the register-direct kernel.
+bool ring_ok(const GemvArgs& g) {
+  return g_ring && g.batch == 1 && g.k % 256 == 0 && aligned(g.qs, 16) && aligned(g.d, 16);
+}
+
+// units per stage: the largest divisor of 24 (even) whose stage fits ~36 KB, and a
+// ring depth that is a multiple of the number of warp groups
+int ring_plan(RingPlan& p, int units, int rows_per_unit, int k, bool norm) {
+  const int row_bytes = k / 2 + k / 16;
+  // staged x (72 B per block) + reduction scratch (40 floats) + linear s for the norm (k floats)
+  const int xs_bytes = (k / 32) * 72 + 160 + (norm ? k * 4 : 0);
+  p.units = units;
+  p.bar_offset = (xs_bytes + 15) / 16 * 16;
+  const int budget = 227 * 1024 - p.bar_offset - 2 * 24 * 8 - 256;
+  static const int kR[] = {24, 12, 8, 6, 4, 2};
+  for (int R : kR) {
+    const int stage = R * rows_per_unit * row_bytes;
+    if (stage > 40 * 1024 && R > 2) continue;
+    const int G = 24 / R;
+    int S = budget / stage;
+    const int cap = G > (8 / G) * G ? G : (8 / G) * G;
+    if (S > cap) S = cap;
+    S = S / G * G;
+    if (S < G) continue;
+    p.R = R;
+    p.stages = S;
+    p.stage_bytes = (stage + 127) / 128 * 128;
+    p.ring_offset = (p.bar_offset + 2 * S * 8 + 127) / 128 * 128;
+    if ((size_t)p.ring_offset + (size_t)S * p.stage_bytes > 227 * 1024) continue;
+    return kOk;
+  }
+  return kErrTooLarge;
+}
+
+template <class Pro, class Epi, int ROWS>
+int ring_launch(GemvArgs g, cudaStream_t st) {
+  RingPlan p;
+  const int units = ROWS == 2 ? g.n / 2 : g.n;
+  if (ring_plan(p, units, ROWS, g.k, Pro::kNorm) != kOk) return kErrTooLarge;
+  const size_t smem = (size_t)p.ring_offset + (size_t)p.stages * p.stage_bytes;
+  int grid = num_sms();
+  if (grid > units) grid = units;
+  g.error = device_error_ptr();
+  // compile-time block counts for the synthetic model's K (2560, 4096, 9728)
+  switch (g.k) {
+    case 2560:
+      return launch(q4_gemv_ring_kernel<Pro, Epi, ROWS, 80>, dim3(grid), dim3(kRingThreads), smem, st, g, p);
+    case 4096:
+      return launch(q4_gemv_ring_kernel<Pro, Epi, ROWS, 128>, dim3(grid), dim3(kRingThreads), smem, st, g, p);
+    case 9728:
+      return launch(q4_gemv_ring_kernel<Pro, Epi, ROWS, 304>, dim3(grid), dim3(kRingThreads), smem, st, g, p);
+    default:
+      return launch(q4_gemv_ring_kernel<Pro, Epi, ROWS, 0>, dim3(grid), dim3(kRingThreads), smem, st, g, p);
+  }
+}
+
+// plain / argmax epilogues: one row per half warp
+template <class Pro, class Epi>
+int ring_launch_plain(const GemvArgs& g, cudaStream_t st) {
+  return ring_launch<Pro, Epi, 1>(g, st);
 }
 
 GemvArgs blank_args() {
@@ -144,6 +226,21 @@ const char* spark_status_string(int status) {
 
 int spark_set_pdl(int enabled) {
   g_pdl = enabled ? 1 : 0;
+  return SPARK_OK;
+}
+
+int spark_set_gemv_ring(int enabled) {
+  g_ring = enabled ? 1 : 0;
+  return SPARK_OK;
+}
+
+int spark_read_device_error(int* value, int reset) {
+  if (!value) return SPARK_ERR_INVALID_ARG;
+  if (cudaMemcpyFromSymbol(value, g_spark_error_word, sizeof(int)) != cudaSuccess) return SPARK_ERR_LAUNCH;
+  if (reset) {
+    const int zero = 0;
+    if (cudaMemcpyToSymbol(g_spark_error_word, &zero, sizeof(int)) != cudaSuccess) return SPARK_ERR_LAUNCH;
+  }
   return SPARK_OK;
 }
 
@@ -187,7 +284,7 @@ int spark_q4_gemv(const uint16_t* x, const uint8_t* qs, const uint16_t* d, uint1
   if (st) return st;
   if (!x || !y) return SPARK_ERR_INVALID_ARG;
   if (batch < 1 || batch > 8) return SPARK_ERR_UNSUPPORTED_SHAPE;
-  if (!aligned(x, 4) || !aligned(y, 4)) return SPARK_ERR_ALIGNMENT;
+  if (!aligned(x, 16) || !aligned(y, 4)) return SPARK_ERR_ALIGNMENT;
   GemvArgs g = blank_args();
   g.qs = qs;
   g.d = d;
@@ -197,6 +294,7 @@ int spark_q4_gemv(const uint16_t* x, const uint8_t* qs, const uint16_t* d, uint1
   g.x = x;
   g.y = y;
   cudaStream_t s = as_stream(stream);
+  if (ring_ok(g)) return ring_launch_plain<ProPlain, EpiPlain>(g, s);
   if (batch == 1) return gemv_launch_b<ProPlain, EpiPlain, 1>(g, s);
   if (batch == 2) return gemv_launch_b<ProPlain, EpiPlain, 2>(g, s);
   if (batch <= 4) return gemv_launch_b<ProPlain, EpiPlain, 4>(g, s);
@@ -206,7 +304,7 @@ int spark_q4_gemv(const uint16_t* x, const uint8_t* qs, const uint16_t* d, uint1
 static int fill_norm(GemvArgs& g, const uint16_t* a, const uint16_t* b, const uint16_t* gamma, float eps,
                      uint16_t* res_out, int k) {
   if (!gamma) return SPARK_ERR_INVALID_ARG;
-  if (!aligned(gamma, 2) || (a && !aligned(a, 4)) || (b && !aligned(b, 4)) || (res_out && !aligned(res_out, 4)))
+  if (!aligned(gamma, 4) || (a && !aligned(a, 4)) || (b && !aligned(b, 4)) || (res_out && !aligned(res_out, 4)))
     return SPARK_ERR_ALIGNMENT;
   if (!(eps >= 0.0f)) return SPARK_ERR_INVALID_ARG;
   g.a = a;
@@ -231,6 +329,7 @@ int spark_rmsnorm_q4_gemv(const uint16_t* a, const uint16_t* b, const uint16_t* 
   g.n = n;
   g.k = k;
   g.y = y;
+  if (ring_ok(g)) return ring_launch_plain<ProNorm, EpiPlain>(g, as_stream(stream));
   return gemv_launch_b<ProNorm, EpiPlain, 1>(g, as_stream(stream));
 }
 
@@ -247,6 +346,7 @@ int spark_rmsnorm_gate_up_silu(const uint16_t* a, const uint16_t* b, const uint1
   g.n = n;
   g.k = k;
   g.y = mid;
+  if (ring_ok(g)) return ring_launch<ProNorm, EpiSiluMul, 2>(g, as_stream(stream));
   return gemv_launch_b<ProNorm, EpiSiluMul, 1>(g, as_stream(stream));
 }
 
@@ -282,6 +382,7 @@ int spark_qkv_rope_kvstore(const uint16_t* a, const uint16_t* b, const uint16_t*
   g.slot_mapping = slot_mapping;
   g.k_cache = k_cache;
   g.v_cache = v_cache;
+  if (ring_ok(g)) return ring_launch<ProNorm, EpiRope, 2>(g, as_stream(stream));
   return gemv_launch_b<ProNorm, EpiRope, 1>(g, as_stream(stream));
 }
 
@@ -300,6 +401,7 @@ int spark_rmsnorm_q4_head_argmax(const uint16_t* a, const uint16_t* b, const uin
   g.k = k;
   g.y = logits;
   g.argmax_key = argmax_key;
+  if (ring_ok(g)) return ring_launch_plain<ProNorm, EpiArgmax>(g, as_stream(stream));
   return gemv_launch_b<ProNorm, EpiArgmax, 1>(g, as_stream(stream));
 }
 

@@ -216,6 +216,18 @@ def set_pdl(enabled: bool) -> None:
     call("spark_set_pdl", 1 if enabled else 0)
 
 
+def set_gemv_ring(enabled: bool) -> None:
+    """Choose the weight-ring GEMV (default) or the register-direct GEMV for K % 512 == 0."""
+    call("spark_set_gemv_ring", 1 if enabled else 0)
+
+
+def read_device_error(reset: bool = True) -> int:
+    """Synchronously read (and optionally clear) the library's device error word."""
+    v = ctypes.c_int(0)
+    call("spark_read_device_error", ctypes.byref(v), 1 if reset else 0)
+    return int(v.value)
+
+
 # ---------------------------------------------------------------- torch.library custom ops
 @torch.library.custom_op("spark_b200::q4_gemv", mutates_args=())
 def _op_q4_gemv(x: torch.Tensor, qs: torch.Tensor, d: torch.Tensor) -> torch.Tensor:

@@ -93,8 +93,19 @@ GEMV_SHAPES = [
 ]
 
 
+@pytest.fixture(params=["ring", "direct"])
+def gemv_path(request, cuda):
+    """Run a GEMV test through both implementations (they must agree bit for bit)."""
+    from spark_b200 import ops
+    ops.set_gemv_ring(request.param == "ring")
+    ops.read_device_error(reset=True)
+    yield request.param
+    assert ops.read_device_error(reset=True) == 0, "a bounded wait timed out"
+    ops.set_gemv_ring(True)
+
+
 @pytest.mark.parametrize("n,k,batch", GEMV_SHAPES)
-def test_q4_gemv_bit_exact(cuda, oracle, n, k, batch):
+def test_q4_gemv_bit_exact(cuda, oracle, gemv_path, n, k, batch):
     torch = _t()
     from spark_b200 import ops
     qs, d = rand_q4(oracle, n, k, seed=n + k)
@@ -132,7 +143,7 @@ def _norm_inputs(oracle, k, seed):
 
 
 @pytest.mark.parametrize("with_b", [True, False])
-def test_rmsnorm_q4_gemv_bit_exact(cuda, oracle, with_b):
+def test_rmsnorm_q4_gemv_bit_exact(cuda, oracle, gemv_path, with_b):
     torch = _t()
     from spark_b200 import ops
     n, k, eps = 2048, 2560, 1e-6
@@ -148,7 +159,7 @@ def test_rmsnorm_q4_gemv_bit_exact(cuda, oracle, with_b):
     assert np.array_equal(u16(y), oracle.q4_gemv(x, qs, d)[0])
 
 
-def test_gate_up_silu_bit_exact(cuda, oracle):
+def test_gate_up_silu_bit_exact(cuda, oracle, gemv_path):
     torch = _t()
     from spark_b200 import ops
     inter, k, eps = 1536, 2560, 1e-6
@@ -166,7 +177,7 @@ def test_gate_up_silu_bit_exact(cuda, oracle):
 
 
 @pytest.mark.parametrize("pos,use_slot_mapping", [(0, False), (777, False), (4095, True)])
-def test_qkv_rope_kvstore_bit_exact(cuda, oracle, pos, use_slot_mapping):
+def test_qkv_rope_kvstore_bit_exact(cuda, oracle, gemv_path, pos, use_slot_mapping):
     torch = _t()
     from spark_b200 import ops
     from spark_b200.config import SparkConfig
@@ -234,7 +245,7 @@ def test_qkv_embedding_input(cuda, oracle):
     assert np.array_equal(u16(q), oracle.rope_neox(qkv[:nq + nkv], u16(cs)[5])[:nq])
 
 
-def test_head_argmax_bit_exact(cuda, oracle):
+def test_head_argmax_bit_exact(cuda, oracle, gemv_path):
     torch = _t()
     from spark_b200 import ops
     n, k, eps = 151936, 2560, 1e-6

@@ -122,34 +122,66 @@ def test_gemv_oracle_vs_dequant_matmul(oracle, n, k, batch):
     assert np.max(np.abs(yf - ref)) < 1e-4 * max(1.0, np.abs(ref).max())
 
 
+def _stage_np(xf):
+    """Independent numpy restatement of the documented activation staging."""
+    X = np.zeros(xf.size, np.int64)
+    sx = np.ones(xf.size // 32, np.float32)
+    C = np.zeros(xf.size // 32, np.int64)
+    for b in range(xf.size // 32):
+        blk = xf[32 * b:32 * b + 32].astype(np.float32)
+        M = np.abs(blk).max()
+        if not (M >= np.float32(2.0 ** -100)) or not np.isfinite(M):
+            continue
+        e = int(np.floor(np.log2(np.float64(M))))
+        S = 14 - e
+        X[32 * b:32 * b + 32] = np.rint(blk.astype(np.float64) * 2.0 ** S).astype(np.int64)
+        sx[b] = np.float32(2.0 ** -S)
+        C[b] = 8 * X[32 * b:32 * b + 32].sum()
+    return X, sx, C
+
+
+def test_stage_x_is_exact_fixed_point(oracle):
+    rng = np.random.default_rng(9)
+    x = f32(bf16(rng.standard_normal(2560).astype(np.float32) * np.exp2(rng.integers(-12, 4, 2560))))
+    X, sx, C = oracle.q4_stage_x(x)
+    eX, esx, eC = _stage_np(x)
+    assert np.array_equal(X.astype(np.int64), eX) and np.array_equal(sx, esx) and np.array_equal(C, eC)
+    assert np.abs(X).max() <= 32640
+    # elements within 2^7 of their block maximum are represented exactly
+    xb, Xb = x.reshape(-1, 32), X.reshape(-1, 32).astype(np.float64) * sx[:, None]
+    big = np.abs(xb) >= np.abs(xb).max(axis=1, keepdims=True) / 128
+    assert np.array_equal(Xb[big], xb[big].astype(np.float64))
+    # all-zero and tiny blocks stage to zero
+    X0, sx0, C0 = oracle.q4_stage_x(np.zeros(64, np.float32))
+    assert not X0.any() and np.all(sx0 == 1.0) and not C0.any()
+
+
 def test_gemv_canonical_order_is_documented(oracle):
-    """Re-derive one row in Python with the documented order and compare bits."""
-    x, qs, d = _q4_setup(2, 1024, seed=3)
+    """Re-derive rows in Python from the documented order and compare bits."""
+    x, qs, d = _q4_setup(3, 1024, seed=3)
     xf = f32(x)[0]
+    X, sx, C = _stage_np(xf)
     nb = 1024 // 32
     dd = d.view(np.float16).astype(np.float32)
-    row = []
-    for r in range(2):
+    rows = []
+    for r in range(3):
         lanes = []
         for lane in range(16):
             acc = np.float32(0)
             for b in range(lane, nb, 16):
-                q = qs[r, b * 16:(b + 1) * 16]
-                a0 = np.float32(0)
-                a1 = np.float32(0)
-                for e in range(16):
-                    a0 = np.float32(np.float64(np.float32((int(q[e]) & 15) - 8)) * np.float64(xf[32 * b + e]) + np.float64(a0))
-                    a1 = np.float32(np.float64(np.float32((int(q[e]) >> 4) - 8)) * np.float64(xf[32 * b + 16 + e]) + np.float64(a1))
-                acc = np.float32(np.float64(dd[r, b]) * np.float64(np.float32(a0 + a1)) + np.float64(acc))
+                q = qs[r, b * 16:(b + 1) * 16].astype(np.int64)
+                P = int(((q & 15) * X[32 * b:32 * b + 16]).sum() + ((q >> 4) * X[32 * b + 16:32 * b + 32]).sum() - C[b])
+                assert abs(P) < 2 ** 24
+                ds = np.float32(dd[r, b] * sx[b])
+                # fma(ds, P, acc): ds * P is exact in float64 (11+24 significant bits < 53)
+                acc = np.float32(np.float64(ds) * np.float64(P) + np.float64(acc))
             lanes.append(acc)
         v = np.array(lanes, np.float32)
         for off in (8, 4, 2, 1):
             v = (v + v[np.arange(16) ^ off]).astype(np.float32)
-        row.append(v[0])
+        rows.append(v[0])
     got = oracle.q4_gemv_f32(xf, qs, d)[0]
-    # fma emulated through float64 is exact for these operand sizes (products of an
-    # integer in [-8, 7] and a bf16 fit in 12 bits), so the bits must agree
-    assert np.array_equal(np.array(row, np.float32).view(np.uint32), got.view(np.uint32))
+    assert np.array_equal(np.array(rows, np.float32).view(np.uint32), got.view(np.uint32))
 
 
 # ----------------------------------------------------------------------------- norm / rope / silu
