@@ -133,7 +133,7 @@ def time_kernels(eng, reps: int = 3) -> dict:
         by_name.setdefault(name, []).append((fn, a))
     out = {}
     stream = torch.cuda.Stream()
-    for name in ("qkv", "attn", "combine", "o_proj", "gate_up", "down", "head"):
+    for name in ("qkv", "attn", "o_proj", "gate_up", "down", "head"):
         seq = by_name[name]
         if name == "head":
             seq = seq * 8
@@ -312,7 +312,7 @@ def run_spark(args):
             "data": "synthetic: seeded N(0,0.02) weights -> Q4_0, 2048 uniform-random prompt ids",
             "config": {"workload": "configs[2]: synthetic 4B Q4_0 batch-1 decode, 2048 prompt, greedy",
                        "layers": layers, "hidden": cfg.hidden_size, "vocab": cfg.vocab_size, "prompt": PROMPT_LEN,
-                       "ctx_range": [PROMPT_LEN, PROMPT_LEN + args.steps - 1], "splits": args.splits,
+                       "ctx_range": [PROMPT_LEN, PROMPT_LEN + args.steps - 1], "splits": eng.splits,
                        "kernels_per_step": eng.kernels_per_step(), "parallelism": f"replicas x{world}",
                        "l2": "inputs larger than L2 (2.26 GB of weights per step)"},
             "e2e": {"value": round(args.steps * world / (e2e_ms / 1e3), 3), "unit": "tokens/s",
@@ -407,7 +407,7 @@ def run_reference(args):
         "dtype": "q4_0 weights x fp32 accumulate, bf16 activations / KV",
         "data": "synthetic: random Q4_0 codes / scales and bf16 KV prefix of the real shapes",
         "config": {"workload": "configs[2]: synthetic 4B Q4_0 batch-1 decode, 2048 prompt, greedy",
-                   "layers": cfg.num_layers, "ctx": PROMPT_LEN, "splits": args.splits, "setup_s": round(setup_s, 1)},
+                   "layers": cfg.num_layers, "ctx": PROMPT_LEN, "splits": eng.splits, "setup_s": round(setup_s, 1)},
         "cpu_baseline": {"value": round(tps, 4), "unit": "tokens/s", "cores": threads, "kind": "port",
                          "sample": f"{args.steps} samples of one layer (or the LM head) of a ctx-{PROMPT_LEN} "
                                    f"decode step; {units} samples = 1 token"},
@@ -421,7 +421,7 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=4096)
     ap.add_argument("--warmup", type=int, default=16)
     ap.add_argument("--impl", choices=["spark", "reference"], default="spark")
-    ap.add_argument("--splits", type=int, default=16)
+    ap.add_argument("--splits", type=int, default=0, help="KV splits per layer (0 = auto: <= 128 tokens each)")
     ap.add_argument("--cpu-tokens", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--prompt", type=int, default=2048, help="prompt length (2048 = the benchmark protocol)")

@@ -109,6 +109,19 @@ int spark_attn_splitkv(const uint16_t* q, const uint16_t* k_cache, const uint16_
                        int head_dim, int block_size, int splits, int max_split_tokens, float scale, float* part_o,
                        float* part_lse, int* error, void* stream);
 
+/* Split-KV attention with the log-sum-exp combine fused in: same inputs and
+ * partial outputs as spark_attn_splitkv (part_o / part_lse are the caller's
+ * workspace), plus counters (int [nkv] on device, all zero before the first call;
+ * the kernel leaves them zero again) and out (bf16 [nq][head_dim]).  The CTA
+ * that finishes last for a kv head merges that head's splits in the same order
+ * as spark_attn_combine, so out is bit-identical to split + combine.
+ * splits <= 256.  Replaces AttentionStage.execute (kernels/attention.py:120-286)
+ * followed by merge_attention (kernels/vector.py:154-192). */
+int spark_attn_decode(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
+                      const int32_t* block_table, const int64_t* pos, const int32_t* seq_len, int nq, int nkv,
+                      int head_dim, int block_size, int splits, int max_split_tokens, float scale, float* part_o,
+                      float* part_lse, int* counters, uint16_t* out, int* error, void* stream);
+
 /* Log-sum-exp combine of split partials -> bf16 [nq][head_dim].
  * Replaces merge_attention (kernels/vector.py:154-192) without the output gate. */
 int spark_attn_combine(const float* part_o, const float* part_lse, int splits, int nq, int head_dim, uint16_t* out,

@@ -34,7 +34,9 @@
  *     The 16 lane sums are combined by an xor butterfly 8,4,2,1 (v[l] += v[l^off]).
  *   RMSNorm: 32 lanes, lane l sums s_i*s_i (product, then add) for i = l mod 32 in
  *     ascending order, xor butterfly 16,8,4,2,1.
- *   Attention scores: a0 over even dims, a1 over odd dims (fma), score = (a0+a1)*scale.
+ *   Attention scores: 8 lanes per token, lane j owns dims 8j..8j+7, 64+8j..64+8j+7;
+ *     a0 / a1 accumulate the even / odd positions of that list (fma), lane value
+ *     a0 + a1, xor butterfly 4,2,1 over the 8 lanes, score = sum * scale.
  *     l: 32 lanes over split-local token index mod 32, ascending adds, butterfly 16..1.
  *     PV: per output dim, fma over tokens in ascending order with bf16-rounded p.
  *   exp: Cody-Waite reduction (ln2 split in a 16-bit head and a tail) + degree-7
@@ -419,6 +421,27 @@ static inline int64_t split_tokens(int64_t len, int splits) {
 
 ORC_API int64_t orc_split_tokens(int64_t len, int splits) { return split_tokens(len, splits); }
 
+/* q . k for one token (dim == 128): 8 lanes, lane j owns dims 8j..8j+7 then
+ * 64+8j..64+8j+7; over that list a0 accumulates the even positions and a1 the odd
+ * ones (fma, ascending); lane value a0 + a1; xor butterfly 4, 2, 1 over the lanes. */
+static float score_dot(const float* qf, const uint16_t* kr, int dim) {
+    float lane[8];
+    int half = dim / 2, per = dim / 16;
+    for (int j = 0; j < 8; j++) {
+        float a0 = 0.0f, a1 = 0.0f;
+        for (int part = 0; part < 2; part++) {
+            int base = part * half + per * j;
+            for (int m = 0; m < per; m += 2) {
+                a0 = fmaf(qf[base + m], bf2f(kr[base + m]), a0);
+                a1 = fmaf(qf[base + m + 1], bf2f(kr[base + m + 1]), a1);
+            }
+        }
+        lane[j] = a0 + a1;
+    }
+    butterfly(lane, 8);
+    return lane[0];
+}
+
 /* q bf16 [nq][dim]; caches bf16 [blocks][nkv][bs][dim]; table int32;
  * part_o fp32 [splits][nq][dim]; part_lse fp32 [splits][nq] */
 ORC_API void orc_attn_split(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const int32_t* table,
@@ -445,12 +468,7 @@ ORC_API void orc_attn_split(const uint16_t* q, const uint16_t* kc, const uint16_
             for (int64_t i = 0; i < n; i++) {
                 int64_t t = t0 + i, blk = table[t / bs], off = t % bs;
                 const uint16_t* kr = kc + ((blk * nkv + hk) * bs + off) * dim;
-                float a0 = 0.0f, a1 = 0.0f;
-                for (int dd = 0; dd < dim; dd += 2) {
-                    a0 = fmaf(qf[dd], bf2f(kr[dd]), a0);
-                    a1 = fmaf(qf[dd + 1], bf2f(kr[dd + 1]), a1);
-                }
-                float sc = (a0 + a1) * scale;
+                float sc = score_dot(qf, kr, dim) * scale;
                 scores[i] = sc;
                 if (sc > m) m = sc;
             }

@@ -11,24 +11,34 @@
 // Token t of the sequence lives in physical block table[t / block_size], row
 // t % block_size.
 //
-// One CTA per (split, kv head); a split covers T = roundup16(ceil(L / S)) tokens.
-// Phase 1: each lane owns one token, streams its K row (16 x 128-bit loads) and
-//   forms the dot products with the G = 4 query heads of the group in fp32
-//   (even dims in .x, odd dims in .y of a packed f32x2 accumulator, ascending).
-// Phase 2: warp g reduces head g: max, p = exp(score - max), l = 32-lane sum
+// One CTA (128 threads) per (split, kv head); a split covers T = roundup16(ceil(L / S))
+// tokens, processed in chunks of 128.
+// Fetch: K and V rows are copied with cp.async into shared memory (K rows padded
+//   to 272 bytes); rows older than the current position are requested before the
+//   programmatic-launch wait, the current token's row (written by the preceding
+//   QKV kernel) after it.
+// Scores: 8 lanes per token; lane j owns dims 8j..8j+7 and 64+8j..64+8j+7, holds
+//   q for two query heads in registers, accumulates the even / odd positions of
+//   its dims in the .x / .y halves of a packed f32x2 FMA, and the 8 lane values
+//   are combined by an xor butterfly (4, 2, 1); score = sum * scale.
+// Softmax: warp g reduces head g: max, p = exp(score - max), l = 32-lane sum
 //   (token i into lane i mod 32, ascending, xor butterfly), P rounded to bf16.
-// Phase 3: thread (g, dim pair) accumulates P.V over the split's tokens in
-//   ascending order from a cp.async-staged V ring in shared memory.
+// P.V: thread (head pair, dim pair) accumulates over the tokens in ascending order.
+// Combine (optional, fused): after writing its partial, each CTA bumps a per-kv-head
+//   arrival counter; the CTA that arrives last merges the splits of its four query
+//   heads in the canonical order and resets the counter for the next call.
 #pragma once
 
 #include "common.cuh"
 
 namespace spark {
 
-constexpr int kAttnThreads = 256;
-constexpr int kAttnChunk = 64;     // tokens per V stage
-constexpr int kAttnStages = 4;     // V ring depth
+constexpr int kAttnThreads = 128;
+constexpr int kAttnChunk = 128;   // tokens per K / V chunk
+constexpr int kKRowBytes = 272;   // padded K row in shared memory (conflict-free 8-lane reads)
+constexpr int kVRowBytes = 256;
 constexpr int kAttnMaxSplitTokens = 2048;
+constexpr int kAttnMaxFusedSplits = 256;
 
 struct AttnArgs {
   const uint16_t* q;          // bf16 [nq][D]
@@ -38,11 +48,13 @@ struct AttnArgs {
   const int64_t* pos64;       // sequence length = pos + 1 (one of pos64 / pos32 / seq_len32)
   const int32_t* pos32;
   const int32_t* seq_len32;
-  int nq, nkv, block_size, splits, t_alloc;
+  int nq, nkv, block_size, splits, t_alloc, kv_slots;
   float scale;
   float* part_o;              // fp32 [splits][nq][D]
   float* part_lse;            // fp32 [splits][nq]
   int* error;                 // set to 1 when the split is longer than t_alloc
+  int* counters;              // fused combine: int [nkv], zero before the first call
+  uint16_t* out;              // fused combine: bf16 [nq][D]; null = partials only
 };
 
 __device__ __forceinline__ int64_t attn_seq_len(const AttnArgs& a) {
@@ -63,137 +75,297 @@ __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// Copy the rows of split-local tokens [c*128, c*128+rows) of one cache into a slot.
+// skip >= 0: leave that token out; only >= 0: copy only that token.
+template <int D>
+__device__ __forceinline__ void attn_issue_rows(const AttnArgs& a, const uint16_t* cache, unsigned char* slot,
+                                                int row_bytes, int64_t tbase, int rows, int hk, int64_t skip,
+                                                int64_t only) {
+  const size_t head_stride = (size_t)a.block_size * D;
+  const size_t block_stride = (size_t)a.nkv * head_stride;
+  constexpr int kPieces = D * 2 / 16;
+  if (only >= 0) {
+    const int r = (int)(only - tbase);
+    if (r < 0 || r >= rows) return;
+    for (int p = threadIdx.x; p < kPieces; p += blockDim.x) {
+      const int64_t blk = a.block_table[only / a.block_size], off = only % a.block_size;
+      cp_async16(slot + (size_t)r * row_bytes + p * 16, cache + blk * block_stride + hk * head_stride + off * D + p * 8);
+    }
+    return;
+  }
+  for (int idx = threadIdx.x; idx < rows * kPieces; idx += blockDim.x) {
+    const int r = idx / kPieces, p = idx - r * kPieces;
+    const int64_t t = tbase + r;
+    if (t == skip) continue;
+    const int64_t blk = a.block_table[t / a.block_size], off = t % a.block_size;
+    cp_async16(slot + (size_t)r * row_bytes + p * 16, cache + blk * block_stride + hk * head_stride + off * D + p * 8);
+  }
+}
+
+// Merge the split partials of G query heads [hq0, hq0+G) into bf16 out, in the
+// canonical order of merge_attention (kernels/vector.py:154-192): M = max lse,
+// w_s = exp(lse_s - M) (0 for empty splits), den = sum_s w_s in ascending s,
+// w_s /= den, out = bf16(sum_s w_s * O_s) in ascending s (product, then add).
+// The weights are computed in parallel, only the two canonical sums are serial;
+// partials are staged through shared memory (buf, buf_bytes) with all loads in
+// flight.  wn: [G][kAttnMaxFusedSplits] floats, mx: [G][2] floats.  128 threads.
+template <int D, int G>
+__device__ __forceinline__ void attn_merge_heads(const float* part_o, const float* part_lse, int splits, int nq,
+                                                 int hq0, uint16_t* out, float* wn, float* mx,
+                                                 unsigned char* buf, size_t buf_bytes) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;  // warp g <-> head g (4 warps)
+  const float ninf = __int_as_float(0xff800000);
+  float* w = wn + warp * kAttnMaxFusedSplits;
+  // lse -> weights (warp g handles head g)
+  float m = ninf;
+  for (int sp = lane; sp < splits; sp += 32) {
+    const float v = __ldcg(part_lse + (size_t)sp * nq + hq0 + warp);
+    w[sp] = v;
+    m = fmaxf(m, v);
+  }
+  m = warp_max(m);
+  __syncwarp();
+  if (m != ninf)
+    for (int sp = lane; sp < splits; sp += 32) w[sp] = (w[sp] == ninf) ? -1.0f : spark_exp(__fsub_rn(w[sp], m));
+  __syncwarp();
+  if (lane == 0) {
+    float den = 0.0f;
+    if (m != ninf)
+      for (int sp = 0; sp < splits; sp++) den = __fadd_rn(den, w[sp] < 0.0f ? 0.0f : w[sp]);
+    mx[warp * 2] = den;
+    mx[warp * 2 + 1] = m;
+  }
+  __syncwarp();
+  const float den = mx[warp * 2];
+  if (m != ninf)
+    for (int sp = lane; sp < splits; sp += 32) w[sp] = w[sp] < 0.0f ? -1.0f : __fdiv_rn(w[sp], den);
+  __syncthreads();
+  // weighted sum; empty splits (w == -1) are skipped
+  const int per_split = G * D * 4;
+  const int chunk = (int)(buf_bytes / per_split) < splits ? (int)(buf_bytes / per_split) : splits;
+  float acc[G * D / 128];
+#pragma unroll
+  for (int i = 0; i < G * D / 128; i++) acc[i] = 0.0f;
+  for (int s0 = 0; s0 < splits; s0 += chunk) {
+    const int ns = min(chunk, splits - s0);
+    __syncthreads();
+    for (int idx = tid; idx < ns * (G * D / 4); idx += 128) {
+      const int sp = idx / (G * D / 4), p = idx - sp * (G * D / 4);
+      cp_async16(buf + (size_t)sp * per_split + p * 16, part_o + ((size_t)(s0 + sp) * nq + hq0) * D + p * 4);
+    }
+    cp_async_commit();
+    cp_async_wait_all();
+    __syncthreads();
+    const float* ob = reinterpret_cast<const float*>(buf);
+#pragma unroll
+    for (int i = 0; i < G * D / 128; i++) {
+      const int e = tid + 128 * i, g = e / D;
+      if (mx[g * 2 + 1] == ninf) continue;
+      const float* wg = wn + g * kAttnMaxFusedSplits + s0;
+      float a = acc[i];
+      for (int sp = 0; sp < ns; sp++) {
+        const float ww = wg[sp];
+        if (ww < 0.0f) continue;
+        a = __fadd_rn(a, __fmul_rn(ww, ob[(size_t)sp * (G * D) + e]));
+      }
+      acc[i] = a;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < G * D / 128; i++) {
+    const int e = tid + 128 * i;
+    out[(size_t)hq0 * D + e] = f2bf(acc[i]);
+  }
+}
 
 template <int D, int G>
-__global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnArgs a) {
-  static_assert(D == 128 && G == 4, "this kernel is specialised for head_dim 128, 4 query heads per kv head");
-  extern __shared__ __align__(16) float smem[];
-  float* qf = smem;                                   // [G][D]
-  float* scores = qf + G * D;                         // [G][t_alloc]
-  float* stat = scores + (size_t)G * a.t_alloc;       // [G][2]: l, m
-  uint16_t* vring = reinterpret_cast<uint16_t*>(stat + 2 * G + 8);  // [stages][chunk][D]
+__global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArgs a) {
+  static_assert(D == 128 && G == 4, "specialised for head_dim 128, 4 query heads per kv head");
+  extern __shared__ __align__(16) unsigned char smem_at[];
+  float* scores = reinterpret_cast<float*>(smem_at);                       // [G][t_alloc]
+  float* stat = scores + (size_t)G * a.t_alloc;                             // [G][2]: l, m
+  float* wn = stat + 2 * G;                                                 // [G][kAttnMaxFusedSplits]
+  int* flag = reinterpret_cast<int*>(wn + G * kAttnMaxFusedSplits);         // [4]
+  unsigned char* kbuf = reinterpret_cast<unsigned char*>(flag + 4);         // [kv_slots][128][272]
+  unsigned char* vbuf = kbuf + (size_t)a.kv_slots * kAttnChunk * kKRowBytes;  // [kv_slots][128][256]
 
   pdl_launch_dependents();
-  pdl_wait();
 
   const int s = blockIdx.x, hk = blockIdx.y, tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5;
+  // Everything read before pdl_wait is stable during this step: the position and
+  // block table are written before the step starts, and cache rows older than the
+  // current position were written by earlier steps.
   const int64_t len = attn_seq_len(a);
+  const int64_t pos = len - 1;
   const int64_t T = attn_split_tokens(len, a.splits);
   const int64_t t0 = (int64_t)s * T;
   const int n = (int)((len - t0) < T ? (len - t0) : T);
-  const size_t head_stride = (size_t)a.block_size * D;
-  const size_t block_stride = (size_t)a.nkv * head_stride;
+  const bool ok = n > 0 && T <= a.t_alloc;
+  const int nch = ok ? (n + kAttnChunk - 1) / kAttnChunk : 0;
+  const int slots = a.kv_slots;
 
-  if (n <= 0 || T > a.t_alloc) {
-    if (T > a.t_alloc && tid == 0 && a.error) atomicExch(a.error, 1);
-    for (int i = tid; i < G * D; i += kAttnThreads) {
-      int g = i / D, dd = i - g * D;
-      a.part_o[((size_t)s * a.nq + hk * G + g) * D + dd] = 0.0f;
-    }
-    if (tid < G) a.part_lse[(size_t)s * a.nq + hk * G + tid] = __int_as_float(0xff800000);
-    return;
-  }
-
-  // q of the group -> fp32
-  for (int i = tid; i < G * D; i += kAttnThreads) qf[i] = bf2f(a.q[(size_t)(hk * G) * D + i]);
-
-  // V ring prefetch of the first stages
-  const int nchunks = (n + kAttnChunk - 1) / kAttnChunk;
-  auto issue_v = [&](int c) {
-    if (c < nchunks) {
-      uint16_t* dst = vring + (size_t)(c % kAttnStages) * kAttnChunk * D;
-#pragma unroll
-      for (int m = 0; m < (kAttnChunk * D * 2 / 16) / kAttnThreads; m++) {
-        int idx = tid + m * kAttnThreads;      // 16-byte piece
-        int j = idx / (D * 2 / 16), piece = idx % (D * 2 / 16);
-        int i = c * kAttnChunk + j;
-        if (i < n) {
-          int64_t t = t0 + i;
-          int64_t blk = a.block_table[t / a.block_size], off = t % a.block_size;
-          const uint16_t* src = a.v_cache + blk * block_stride + hk * head_stride + off * D + piece * 8;
-          cp_async16(dst + (size_t)j * D + piece * 8, src);
-        }
-      }
+  if (ok) {
+    for (int c = 0; c < nch && c < slots; c++) {
+      const int rows = min(kAttnChunk, n - c * kAttnChunk);
+      attn_issue_rows<D>(a, a.k_cache, kbuf + (size_t)c * kAttnChunk * kKRowBytes, kKRowBytes, t0 + c * kAttnChunk, rows,
+                         hk, pos, -1);
+      attn_issue_rows<D>(a, a.v_cache, vbuf + (size_t)c * kAttnChunk * kVRowBytes, kVRowBytes, t0 + c * kAttnChunk, rows,
+                         hk, pos, -1);
     }
     cp_async_commit();
-  };
-#pragma unroll
-  for (int c = 0; c < kAttnStages - 1; c++) issue_v(c);
-  __syncthreads();
+  }
 
-  // phase 1: scores
-  for (int i = tid; i < n; i += kAttnThreads) {
-    int64_t t = t0 + i;
-    int64_t blk = a.block_table[t / a.block_size], off = t % a.block_size;
-    const uint4* kr = reinterpret_cast<const uint4*>(a.k_cache + blk * block_stride + hk * head_stride + off * D);
-    uint4 kv[D / 8];
+  pdl_wait();
+
+  const int hq0 = hk * G;
+  if (!ok) {
+    if (n > 0 && tid == 0 && a.error) atomicExch(a.error, 1);
+    for (int i = tid; i < G * D; i += kAttnThreads) a.part_o[((size_t)s * a.nq + hq0) * D + i] = 0.0f;
+    if (tid < G) a.part_lse[(size_t)s * a.nq + hq0 + tid] = __int_as_float(0xff800000);
+  } else {
+    // the current token's rows, if they fall into an already requested chunk
+    const int cpos = (int)((pos - t0) / kAttnChunk);
+    if (pos >= t0 && pos < t0 + n && cpos < slots) {
+      const int rows = min(kAttnChunk, n - cpos * kAttnChunk);
+      attn_issue_rows<D>(a, a.k_cache, kbuf + (size_t)cpos * kAttnChunk * kKRowBytes, kKRowBytes,
+                         t0 + cpos * kAttnChunk, rows, hk, -1, pos);
+      attn_issue_rows<D>(a, a.v_cache, vbuf + (size_t)cpos * kAttnChunk * kVRowBytes, kVRowBytes,
+                         t0 + cpos * kAttnChunk, rows, hk, -1, pos);
+    }
+    cp_async_commit();
+
+    // q of this lane's dims for its head pair, fp32 in registers
+    const int j = lane & 7, grp = lane >> 3;
+    const int hp = warp >> 1, wsub = warp & 1;
+    float2 qr[2][8];
 #pragma unroll
-    for (int c = 0; c < D / 8; c++) kv[c] = ldg_stream(kr + c);
-    float2 acc[G];
+    for (int hh = 0; hh < 2; hh++) {
+      const uint16_t* qh = a.q + (size_t)(hq0 + 2 * hp + hh) * D;
+      const uint4 q0 = *reinterpret_cast<const uint4*>(qh + 8 * j);
+      const uint4 q1 = *reinterpret_cast<const uint4*>(qh + 64 + 8 * j);
+      const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
-    for (int g = 0; g < G; g++) acc[g] = make_float2(0.0f, 0.0f);
+      for (int m = 0; m < 8; m++) qr[hh][m] = make_float2(bf_lo(w[m]), bf_hi(w[m]));
+    }
+    cp_async_wait_all();
+    __syncthreads();
+
+    // ---- scores
+    for (int c = 0; c < nch; c++) {
+      const int slot = c % slots;
+      if (c >= slots) {
+        // chunk c was not prefetched: fetch it into its slot now (all earlier uses done)
+        __syncthreads();
+        attn_issue_rows<D>(a, a.k_cache, kbuf + (size_t)slot * kAttnChunk * kKRowBytes, kKRowBytes,
+                           t0 + c * kAttnChunk, min(kAttnChunk, n - c * kAttnChunk), hk, -1, -1);
+        cp_async_commit();
+        cp_async_wait_all();
+        __syncthreads();
+      }
+      const int rows = min(kAttnChunk, n - c * kAttnChunk);
+      const unsigned char* kb = kbuf + (size_t)slot * kAttnChunk * kKRowBytes;
+      for (int r0 = 0; r0 < rows; r0 += 8) {
+        const int r = r0 + wsub * 4 + grp;
+        float2 acc0 = make_float2(0.0f, 0.0f), acc1 = make_float2(0.0f, 0.0f);
+        if (r < rows) {
+          const uint4 k0 = *reinterpret_cast<const uint4*>(kb + (size_t)r * kKRowBytes + 16 * j);
+          const uint4 k1 = *reinterpret_cast<const uint4*>(kb + (size_t)r * kKRowBytes + 128 + 16 * j);
+          const uint32_t w[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
 #pragma unroll
-    for (int c = 0; c < D / 8; c++) {
-      const uint32_t w4[4] = {kv[c].x, kv[c].y, kv[c].z, kv[c].w};
+          for (int m = 0; m < 8; m++) {
+            const float2 kk = make_float2(bf_lo(w[m]), bf_hi(w[m]));
+            acc0 = __ffma2_rn(qr[0][m], kk, acc0);
+            acc1 = __ffma2_rn(qr[1][m], kk, acc1);
+          }
+        }
+        float v0 = __fadd_rn(acc0.x, acc0.y), v1 = __fadd_rn(acc1.x, acc1.y);
 #pragma unroll
-      for (int e = 0; e < 4; e++) {
-        const float2 kk = make_float2(bf_lo(w4[e]), bf_hi(w4[e]));
-        const int dd = c * 8 + e * 2;
-#pragma unroll
-        for (int g = 0; g < G; g++) {
-          const float2 qq = *reinterpret_cast<const float2*>(qf + g * D + dd);
-          acc[g] = __ffma2_rn(qq, kk, acc[g]);
+        for (int off = 4; off >= 1; off >>= 1) {
+          v0 = __fadd_rn(v0, __shfl_xor_sync(0xffffffffu, v0, off));
+          v1 = __fadd_rn(v1, __shfl_xor_sync(0xffffffffu, v1, off));
+        }
+        if (j == 0 && r < rows) {
+          const int i = c * kAttnChunk + r;
+          scores[(size_t)(2 * hp) * a.t_alloc + i] = __fmul_rn(v0, a.scale);
+          scores[(size_t)(2 * hp + 1) * a.t_alloc + i] = __fmul_rn(v1, a.scale);
         }
       }
     }
-#pragma unroll
-    for (int g = 0; g < G; g++) scores[(size_t)g * a.t_alloc + i] = __fmul_rn(__fadd_rn(acc[g].x, acc[g].y), a.scale);
-  }
-  __syncthreads();
-
-  // phase 2: softmax statistics, warp g handles head g
-  if (warp < G) {
-    float* sc = scores + (size_t)warp * a.t_alloc;
-    float m = __int_as_float(0xff800000);
-    for (int i = lane; i < n; i += 32) m = fmaxf(m, sc[i]);
-    m = warp_max(m);
-    float l = 0.0f;
-    for (int i = lane; i < n; i += 32) {
-      float p = spark_exp(__fsub_rn(sc[i], m));
-      l = __fadd_rn(l, p);
-      sc[i] = bf2f(f2bf(p));
-    }
-    l = butterfly_sum<32>(l);
-    if (lane == 0) {
-      stat[warp * 2 + 0] = l;
-      stat[warp * 2 + 1] = m;
-    }
-  }
-
-  // phase 3: P.V
-  const int g = tid / (D / 2), dp = tid % (D / 2);
-  const float* pg = scores + (size_t)g * a.t_alloc;
-  float2 o = make_float2(0.0f, 0.0f);
-  for (int c = 0; c < nchunks; c++) {
-    __syncthreads();  // stage (c-1) % stages fully consumed; phase 2 done on first pass
-    issue_v(c + kAttnStages - 1);
-    cp_async_wait<kAttnStages - 1>();
     __syncthreads();
-    const uint16_t* vs = vring + (size_t)(c % kAttnStages) * kAttnChunk * D;
-    const int jn = (n - c * kAttnChunk) < kAttnChunk ? (n - c * kAttnChunk) : kAttnChunk;
-    for (int j = 0; j < jn; j++) {
-      const uint32_t vw = *reinterpret_cast<const uint32_t*>(vs + (size_t)j * D + 2 * dp);
-      const float p = pg[c * kAttnChunk + j];
-      o = __ffma2_rn(make_float2(p, p), make_float2(bf_lo(vw), bf_hi(vw)), o);
+
+    // ---- softmax statistics, warp g handles head g
+    {
+      float* sc = scores + (size_t)warp * a.t_alloc;
+      float m = __int_as_float(0xff800000);
+      for (int i = lane; i < n; i += 32) m = fmaxf(m, sc[i]);
+      m = warp_max(m);
+      float l = 0.0f;
+      for (int i = lane; i < n; i += 32) {
+        const float p = spark_exp(__fsub_rn(sc[i], m));
+        l = __fadd_rn(l, p);
+        sc[i] = bf2f(f2bf(p));
+      }
+      l = butterfly_sum<32>(l);
+      if (lane == 0) {
+        stat[warp * 2 + 0] = l;
+        stat[warp * 2 + 1] = m;
+      }
+    }
+    __syncthreads();
+
+    // ---- P.V: thread (head pair, dim pair)
+    const int php = tid >> 6, dp = tid & 63;
+    const float* p0 = scores + (size_t)(2 * php) * a.t_alloc;
+    const float* p1 = scores + (size_t)(2 * php + 1) * a.t_alloc;
+    float2 o0 = make_float2(0.0f, 0.0f), o1 = make_float2(0.0f, 0.0f);
+    for (int c = 0; c < nch; c++) {
+      const int slot = c % slots;
+      if (c >= slots) {
+        __syncthreads();
+        attn_issue_rows<D>(a, a.v_cache, vbuf + (size_t)slot * kAttnChunk * kVRowBytes, kVRowBytes,
+                           t0 + c * kAttnChunk, min(kAttnChunk, n - c * kAttnChunk), hk, -1, -1);
+        cp_async_commit();
+        cp_async_wait_all();
+        __syncthreads();
+      }
+      const int rows = min(kAttnChunk, n - c * kAttnChunk);
+      const unsigned char* vb = vbuf + (size_t)slot * kAttnChunk * kVRowBytes + 4 * dp;
+      const int ib = c * kAttnChunk;
+#pragma unroll 4
+      for (int r = 0; r < rows; r++) {
+        const uint32_t vw = *reinterpret_cast<const uint32_t*>(vb + (size_t)r * kVRowBytes);
+        const float2 vv = make_float2(bf_lo(vw), bf_hi(vw));
+        const float pa = p0[ib + r], pb = p1[ib + r];
+        o0 = __ffma2_rn(make_float2(pa, pa), vv, o0);
+        o1 = __ffma2_rn(make_float2(pb, pb), vv, o1);
+      }
+    }
+    const int ha = 2 * php, hb = 2 * php + 1;
+    const float la = stat[ha * 2], lb = stat[hb * 2];
+    *reinterpret_cast<float2*>(a.part_o + ((size_t)s * a.nq + hq0 + ha) * D + 2 * dp) =
+        make_float2(__fdiv_rn(o0.x, la), __fdiv_rn(o0.y, la));
+    *reinterpret_cast<float2*>(a.part_o + ((size_t)s * a.nq + hq0 + hb) * D + 2 * dp) =
+        make_float2(__fdiv_rn(o1.x, lb), __fdiv_rn(o1.y, lb));
+    if (dp == 0) {
+      a.part_lse[(size_t)s * a.nq + hq0 + ha] = __fadd_rn(spark_log(la), stat[ha * 2 + 1]);
+      a.part_lse[(size_t)s * a.nq + hq0 + hb] = __fadd_rn(spark_log(lb), stat[hb * 2 + 1]);
     }
   }
-  cp_async_wait<0>();
-  const float l = stat[g * 2 + 0], m = stat[g * 2 + 1];
-  const int hq = hk * G + g;
-  float2 out = make_float2(__fdiv_rn(o.x, l), __fdiv_rn(o.y, l));
-  *reinterpret_cast<float2*>(a.part_o + ((size_t)s * a.nq + hq) * D + 2 * dp) = out;
-  if (dp == 0) a.part_lse[(size_t)s * a.nq + hq] = __fadd_rn(spark_log(l), m);
+
+  if (a.out == nullptr) return;
+  // ---- fused combine: the last split CTA of this kv head merges its four q heads
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) flag[0] = (atomicAdd(&a.counters[hk], 1) == a.splits - 1);
+  __syncthreads();
+  if (!flag[0]) return;
+  __threadfence();
+  attn_merge_heads<D, G>(a.part_o, a.part_lse, a.splits, a.nq, hq0, a.out, wn, stat, kbuf,
+                         (size_t)a.kv_slots * kAttnChunk * (kKRowBytes + kVRowBytes));
+  if (tid == 0) a.counters[hk] = 0;
 }
 
 // ------------------------------------------------------------------ combine
@@ -238,6 +410,18 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(const CombineArgs a) 
     }
     a.out[(size_t)hq * a.dim + dd] = f2bf(acc);
   }
+}
+
+// Standalone combine for groups of 4 query heads (splits <= 256): same helper as the
+// fused path.  grid = nq / 4, 128 threads.
+__global__ void __launch_bounds__(128) attn_combine4_kernel(const CombineArgs a) {
+  extern __shared__ __align__(16) unsigned char smem_c[];
+  float* wn = reinterpret_cast<float*>(smem_c);   // [4][kAttnMaxFusedSplits]
+  float* mx = wn + 4 * kAttnMaxFusedSplits;      // [4][2] (+ pad)
+  unsigned char* buf = reinterpret_cast<unsigned char*>(mx + 8);
+  pdl_launch_dependents();
+  pdl_wait();
+  attn_merge_heads<128, 4>(a.part_o, a.part_lse, a.splits, a.nq, blockIdx.x * 4, a.out, wn, mx, buf, 64 * 1024);
 }
 
 }  // namespace spark

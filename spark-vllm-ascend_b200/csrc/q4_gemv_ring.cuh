@@ -73,9 +73,10 @@ __device__ __forceinline__ void consumer_sync() {
 // (K/2 bytes) and, after all nibble rows, the fp16 scale row (K/16 bytes).  Rows of
 // one side of a stage are mostly consecutive in HBM, so a stage costs a handful of
 // large bulk copies.  Consumer warps form G = 24 / R groups of R/2 warps; group gi
-// consumes stages gi, gi+G, ...; the ring depth S is a multiple of G so that every
-// use of a slot belongs to the same group (each mbarrier phase is then awaited in
-// order by the only warps that consume it).
+// consumes stages gi, gi+G, ...  When a CTA has more stages than ring slots, the
+// ring depth S is a multiple of G so that every use of a slot belongs to the same
+// group (each mbarrier phase is then awaited in order by the only warps that
+// consume it); otherwise every stage has its own slot and is used once.
 struct RingPlan {
   int units;        // total units (pairs or rows)
   int R;            // units per stage (divides 24, even)

@@ -28,6 +28,7 @@ namespace {
 
 int g_pdl = 1;
 int g_ring = 1;
+constexpr int kRingSmemBudget = 227 * 1024;
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
@@ -144,31 +145,41 @@ bool ring_ok(const GemvArgs& g) {
 
 // units per stage: the largest divisor of 24 (even) whose stage fits ~36 KB, and a
 // ring depth that is a multiple of the number of warp groups
-int ring_plan(RingPlan& p, int units, int rows_per_unit, int k, bool norm) {
+int ring_plan_budget(RingPlan& p, int units, int rows_per_unit, int k, bool norm, int total_budget) {
   const int row_bytes = k / 2 + k / 16;
   // staged x (72 B per block) + reduction scratch (40 floats) + linear s for the norm (k floats)
   const int xs_bytes = (k / 32) * 72 + 160 + (norm ? k * 4 : 0);
   p.units = units;
   p.bar_offset = (xs_bytes + 15) / 16 * 16;
-  const int budget = 227 * 1024 - p.bar_offset - 2 * 24 * 8 - 256;
+  const int budget = total_budget - p.bar_offset - 2 * 24 * 8 - 256;
+  const int sms = num_sms();
+  const int max_units_cta = (units + sms - 1) / sms;
   static const int kR[] = {24, 12, 8, 6, 4, 2};
   for (int R : kR) {
     const int stage = R * rows_per_unit * row_bytes;
     if (stage > 40 * 1024 && R > 2) continue;
     const int G = 24 / R;
+    const int max_stages_cta = (max_units_cta + R - 1) / R;
     int S = budget / stage;
     const int cap = G > (8 / G) * G ? G : (8 / G) * G;
     if (S > cap) S = cap;
-    S = S / G * G;
-    if (S < G) continue;
+    // slots are reused only when a CTA has more stages than slots; then every use of
+    // a slot must belong to the same consumer group (S % G == 0)
+    if (max_stages_cta > S) S = S / G * G;
+    else S = max_stages_cta;
+    if (S < 1 || (max_stages_cta > S && S < G)) continue;
     p.R = R;
     p.stages = S;
     p.stage_bytes = (stage + 127) / 128 * 128;
     p.ring_offset = (p.bar_offset + 2 * S * 8 + 127) / 128 * 128;
-    if ((size_t)p.ring_offset + (size_t)S * p.stage_bytes > 227 * 1024) continue;
+    if ((size_t)p.ring_offset + (size_t)S * p.stage_bytes > (size_t)total_budget) continue;
     return kOk;
   }
   return kErrTooLarge;
+}
+
+int ring_plan(RingPlan& p, int units, int rows_per_unit, int k, bool norm) {
+  return ring_plan_budget(p, units, rows_per_unit, k, norm, kRingSmemBudget);
 }
 
 template <class Pro, class Epi, int ROWS>
@@ -405,38 +416,61 @@ int spark_rmsnorm_q4_head_argmax(const uint16_t* a, const uint16_t* b, const uin
   return gemv_launch_b<ProNorm, EpiArgmax, 1>(g, as_stream(stream));
 }
 
-int spark_attn_splitkv(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
+static int attn_launch(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
                        const int32_t* block_table, const int64_t* pos, const int32_t* seq_len, int nq, int nkv,
                        int head_dim, int block_size, int splits, int max_split_tokens, float scale, float* part_o,
-                       float* part_lse, int* error, void* stream) {
+                       float* part_lse, int* error, int* counters, uint16_t* out, void* stream) {
   if (!q || !k_cache || !v_cache || !block_table || !part_o || !part_lse || (!pos && !seq_len))
     return SPARK_ERR_INVALID_ARG;
   if (head_dim != 128 || nkv <= 0 || nq != 4 * nkv || block_size <= 0) return SPARK_ERR_UNSUPPORTED_SHAPE;
   if (splits <= 0 || splits > 4096) return SPARK_ERR_UNSUPPORTED_SHAPE;
+  if (out && (!counters || splits > kAttnMaxFusedSplits)) return SPARK_ERR_UNSUPPORTED_SHAPE;
   if (max_split_tokens <= 0 || max_split_tokens > kAttnMaxSplitTokens) return SPARK_ERR_TOO_LARGE;
-  if (!aligned(k_cache, 16) || !aligned(v_cache, 16) || !aligned(part_o, 8) || !aligned(q, 4))
+  if (!aligned(k_cache, 16) || !aligned(v_cache, 16) || !aligned(part_o, 16) || !aligned(q, 16))
     return SPARK_ERR_ALIGNMENT;
   AttnArgs a;
+  memset(&a, 0, sizeof(a));
   a.q = q;
   a.k_cache = k_cache;
   a.v_cache = v_cache;
   a.block_table = block_table;
   a.pos64 = seq_len ? nullptr : pos;
-  a.pos32 = nullptr;
   a.seq_len32 = seq_len;
   a.nq = nq;
   a.nkv = nkv;
   a.block_size = block_size;
   a.splits = splits;
   a.t_alloc = (max_split_tokens + 15) / 16 * 16;
+  const int nch = (a.t_alloc + kAttnChunk - 1) / kAttnChunk;
+  a.kv_slots = nch < 2 ? nch : 2;
   a.scale = scale;
   a.part_o = part_o;
   a.part_lse = part_lse;
   a.error = error;
-  const int G = 4, D = 128;
-  const size_t smem = (size_t)(G * D + G * a.t_alloc + 2 * G + 8) * sizeof(float) +
-                      (size_t)kAttnStages * kAttnChunk * D * sizeof(uint16_t);
-  return launch(attn_split_kernel<128, 4>, dim3(splits, nkv), dim3(kAttnThreads), smem, as_stream(stream), a);
+  a.counters = counters;
+  a.out = out;
+  const int G = 4;
+  const size_t smem = (size_t)(G * a.t_alloc + 2 * G + G * kAttnMaxFusedSplits + 4) * sizeof(float) +
+                      (size_t)a.kv_slots * kAttnChunk * (kKRowBytes + kVRowBytes);
+  return launch(attn_decode_kernel<128, 4>, dim3(splits, nkv), dim3(kAttnThreads), smem, as_stream(stream), a);
+}
+
+int spark_attn_splitkv(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
+                       const int32_t* block_table, const int64_t* pos, const int32_t* seq_len, int nq, int nkv,
+                       int head_dim, int block_size, int splits, int max_split_tokens, float scale, float* part_o,
+                       float* part_lse, int* error, void* stream) {
+  return attn_launch(q, k_cache, v_cache, block_table, pos, seq_len, nq, nkv, head_dim, block_size, splits,
+                     max_split_tokens, scale, part_o, part_lse, error, nullptr, nullptr, stream);
+}
+
+int spark_attn_decode(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
+                      const int32_t* block_table, const int64_t* pos, const int32_t* seq_len, int nq, int nkv,
+                      int head_dim, int block_size, int splits, int max_split_tokens, float scale, float* part_o,
+                      float* part_lse, int* counters, uint16_t* out, int* error, void* stream) {
+  if (!out || !counters) return SPARK_ERR_INVALID_ARG;
+  if (!aligned(counters, 4) || !aligned(out, 2)) return SPARK_ERR_ALIGNMENT;
+  return attn_launch(q, k_cache, v_cache, block_table, pos, seq_len, nq, nkv, head_dim, block_size, splits,
+                     max_split_tokens, scale, part_o, part_lse, error, counters, out, stream);
 }
 
 int spark_attn_combine(const float* part_o, const float* part_lse, int splits, int nq, int head_dim, uint16_t* out,
@@ -450,6 +484,10 @@ int spark_attn_combine(const float* part_o, const float* part_lse, int splits, i
   c.nq = nq;
   c.dim = head_dim;
   c.out = out;
+  if (head_dim == 128 && nq % 4 == 0 && splits <= kAttnMaxFusedSplits && aligned(part_o, 16)) {
+    const size_t smem = (size_t)(4 * kAttnMaxFusedSplits + 8) * sizeof(float) + 64 * 1024;
+    return launch(attn_combine4_kernel, dim3(nq / 4), dim3(128), smem, as_stream(stream), c);
+  }
   return launch(attn_combine_kernel, dim3(nq), dim3(128), (size_t)splits * sizeof(float), as_stream(stream), c);
 }
 

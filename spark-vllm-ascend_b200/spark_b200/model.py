@@ -8,8 +8,8 @@ programmatic dependent launch and replayed as one CUDA graph):
     qkv      : s = a + b -> res_attn; x = RMSNorm(s) * in_norm; QKV Q4 GEMV; RoPE;
                q -> q_buf, k / v -> paged cache at the step's slot
                (layer 0: a = embedding row of the input token, b = none)
-    attn     : split-KV partials over the sequence
-    combine  : log-sum-exp merge -> attn_out (bf16)
+    attn     : split-KV attention; the last split CTA of each kv head merges the
+               partials (log-sum-exp) -> attn_out (bf16)
     o_proj   : Q4 GEMV attn_out -> oproj
     gate_up  : s = oproj + res_attn -> resmid; x = RMSNorm(s) * post_norm;
                gate/up Q4 GEMV; SiLU(g) * u -> mid
@@ -160,13 +160,15 @@ class DecodeEngine:
     the cache (a random permutation by default, as in the attention parity cases).
     """
 
-    def __init__(self, weights: SyntheticWeights, max_seq_len: int, splits: int = 16, num_blocks: int | None = None,
+    def __init__(self, weights: SyntheticWeights, max_seq_len: int, splits: int = 0, num_blocks: int | None = None,
                  block_table: torch.Tensor | None = None, use_graph: bool = True, max_steps: int | None = None,
                  seed: int = 0):
         cfg = weights.cfg
         self.cfg, self.w = cfg, weights
         dev = weights.device
         self.device = dev
+        if splits <= 0:  # auto: splits of at most 128 tokens (one K/V chunk), at least 16
+            splits = min(256, max(16, -(-max_seq_len // 128)))
         self.splits = splits
         self.max_seq_len = max_seq_len
         bs = cfg.block_size
@@ -192,6 +194,7 @@ class DecodeEngine:
         self.attn_out = e(nq, D)
         self.part_o = e(splits, nq, D, dt=torch.float32)
         self.part_lse = e(splits, nq, dt=torch.float32)
+        self.counters = e(cfg.num_kv_heads, dt=torch.int32)
         self.logits = e(cfg.vocab_size)
         self.key = e(1, dt=torch.int64)
         self.token = e(1, dt=torch.int32)
@@ -225,11 +228,10 @@ class DecodeEngine:
             calls.append((L.spark_qkv_rope_kvstore, "qkv", (
                 a, b, embed, tok, _vp(lw.in_norm), eps, _vp(self.res_attn), _vp(lw.qkv.qs), _vp(lw.qkv.d), h, nq,
                 nkv, D, _vp(w.cos_sin), _vp(self.pos), _vp(self.block_table), None, bs, kc, vc, _vp(self.q))))
-            calls.append((L.spark_attn_splitkv, "attn", (
+            calls.append((L.spark_attn_decode, "attn", (
                 _vp(self.q), kc, vc, _vp(self.block_table), _vp(self.pos), None, nq, nkv, D, bs, self.splits,
-                self.max_split_tokens, scale, _vp(self.part_o), _vp(self.part_lse), _vp(self.error))))
-            calls.append((L.spark_attn_combine, "combine", (
-                _vp(self.part_o), _vp(self.part_lse), self.splits, nq, D, _vp(self.attn_out))))
+                self.max_split_tokens, scale, _vp(self.part_o), _vp(self.part_lse), _vp(self.counters),
+                _vp(self.attn_out), _vp(self.error))))
             calls.append((L.spark_q4_gemv, "o_proj", (
                 _vp(self.attn_out), _vp(lw.o.qs), _vp(lw.o.d), _vp(self.oproj), h, nq * D, 1)))
             calls.append((L.spark_rmsnorm_gate_up_silu, "gate_up", (

@@ -173,6 +173,22 @@ def attn_splitkv_out(q, k_cache, v_cache, block_table, splits, max_split_tokens,
          head_dim, block_size, splits, max_split_tokens, float(scale), _p(part_o), _p(part_lse), _p(error), _stream())
 
 
+def attn_decode_out(q, k_cache, v_cache, block_table, splits, max_split_tokens, scale, part_o, part_lse, counters,
+                    out, pos=None, seq_len=None, error=None):
+    """Split-KV attention with the fused LSE combine (counters: int32 [nkv], zero)."""
+    _cuda(q, "q", BF16)
+    nq, head_dim = q.shape[-2], q.shape[-1]
+    _check(k_cache.dim() == 4 and k_cache.shape == v_cache.shape, "caches must be [blocks, nkv, block_size, D]")
+    nkv, block_size = k_cache.shape[1], k_cache.shape[2]
+    _cuda(counters, "counters", torch.int32)
+    _cuda(out, "out", BF16)
+    _check((pos is None) != (seq_len is None), "give exactly one of pos / seq_len")
+    call("spark_attn_decode", _p(q), _p(k_cache), _p(v_cache), _p(block_table), _p(pos), _p(seq_len), nq, nkv,
+         head_dim, block_size, splits, max_split_tokens, float(scale), _p(part_o), _p(part_lse), _p(counters),
+         _p(out), _p(error), _stream())
+    return out
+
+
 def attn_combine_out(part_o, part_lse, out):
     splits, nq, head_dim = part_o.shape
     _cuda(part_o, "part_o", torch.float32)

@@ -332,6 +332,32 @@ def test_attention_bit_exact(cuda, oracle, L, splits):
     assert np.max(np.abs(oracle.bf16_to_f32(u16(out)) - ref)) < 2e-2
 
 
+@pytest.mark.parametrize("L,splits", [(1, 16), (130, 16), (2048, 48), (6144, 48), (5000, 3), (700, 256)])
+def test_attention_fused_decode_bit_exact(cuda, oracle, L, splits):
+    """Split + fused combine == oracle split + combine, twice in a row (counters self-reset)."""
+    torch = _t()
+    from spark_b200 import ops
+    rng = np.random.default_rng(L + 31 * splits)
+    kc, vc, table = _paged_cache(oracle, rng, L)
+    nq, D = 32, 128
+    scale = float(np.float32(1 / math.sqrt(D)))
+    T = oracle.split_tokens(L, splits)
+    po = torch.empty((splits, nq, D), dtype=torch.float32, device=cuda)
+    pl = torch.empty((splits, nq), dtype=torch.float32, device=cuda)
+    counters = torch.zeros(8, dtype=torch.int32, device=cuda)
+    out = torch.empty((nq, D), dtype=torch.bfloat16, device=cuda)
+    kd, vd, td = dev_bf16(kc, cuda), dev_bf16(vc, cuda), torch.from_numpy(table).to(cuda)
+    for rep in range(2):
+        q = oracle.f32_to_bf16(rng.standard_normal((nq, D)).astype(np.float32))
+        ops.attn_decode_out(dev_bf16(q, cuda), kd, vd, td, splits, T, scale, po, pl, counters, out,
+                            pos=torch.tensor([L - 1], dtype=torch.int64, device=cuda))
+        torch.cuda.synchronize()
+        epo, epl = oracle.attn_split(q, kc, vc, table, L, splits, scale)
+        assert np.array_equal(u16(out), oracle.attn_combine(epo, epl)), rep
+        assert np.array_equal(pl.cpu().numpy().view(np.uint32), epl.view(np.uint32))
+        assert int(counters.abs().sum().item()) == 0
+
+
 def test_attention_seq_len_input_and_overflow_flag(cuda, oracle):
     torch = _t()
     from spark_b200 import ops

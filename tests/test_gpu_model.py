@@ -56,7 +56,7 @@ def test_tiny_model_greedy_64_steps(cuda, oracle):
                                            oracle=oracle)
     assert toks == ref
     assert np.array_equal(lg, ref_lg)
-    assert eng.kernels_per_step() == 6 * cfg.num_layers + 2
+    assert eng.kernels_per_step() == 5 * cfg.num_layers + 2
 
 
 def test_tiny_model_eager_matches_graph(cuda, oracle):
