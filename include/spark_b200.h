@@ -122,6 +122,27 @@ int spark_attn_decode(const uint16_t* q, const uint16_t* k_cache, const uint16_t
                       int head_dim, int block_size, int splits, int max_split_tokens, float scale, float* part_o,
                       float* part_lse, int* counters, uint16_t* out, int* error, void* stream);
 
+/* spark_attn_decode for callers that cannot allocate device memory (a host
+ * framework that owns all GPU memory and lends none to plugins, or a loop that must
+ * not call cudaMalloc after start-up, since it can synchronise the device or fail
+ * under memory pressure).  No counterpart in the reference: this entry point is an
+ * addition of this library.  Same inputs, output and numerics as spark_attn_decode,
+ * but the partials, lse values and arrival counters live in a static device array
+ * inside the library (2,113,792 bytes, held by every GPU that loads the library
+ * until the process exits), so the caller passes no workspace.
+ * Limits: splits <= 64, nq <= 64, nkv <= 64 (else SPARK_ERR_TOO_LARGE); otherwise
+ * as spark_attn_decode (head_dim 128, nq == 4 * nkv, max_split_tokens <= 2048).
+ * The first call on a device looks up the array's device address and zeroes its
+ * counters, a synchronous step: make that first call before any stream capture.
+ * All calls on one device share the array and it keeps the last call's contents;
+ * calls that can overlap on the GPU (e.g. on different streams with no ordering
+ * between them) race and corrupt each other's results, so order them on one stream.
+ * Each device has its own copy.  Allocates nothing. */
+int spark_attn_decode_noalloc(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
+                              const int32_t* block_table, const int64_t* pos, const int32_t* seq_len, int nq,
+                              int nkv, int head_dim, int block_size, int splits, int max_split_tokens, float scale,
+                              uint16_t* out, int* error, void* stream);
+
 /* Log-sum-exp combine of split partials -> bf16 [nq][head_dim].
  * Replaces merge_attention (kernels/vector.py:154-192) without the output gate. */
 int spark_attn_combine(const float* part_o, const float* part_lse, int splits, int nq, int head_dim, uint16_t* out,

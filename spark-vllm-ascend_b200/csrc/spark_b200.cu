@@ -473,6 +473,64 @@ int spark_attn_decode(const uint16_t* q, const uint16_t* k_cache, const uint16_t
                      max_split_tokens, scale, part_o, part_lse, error, counters, out, stream);
 }
 
+// ------------------------------------------------------------------ allocation-free attention
+// Some callers cannot allocate device memory when they decode: a host framework
+// that owns every byte of GPU memory and hands out none to plugins, or a real-time
+// loop that must never call cudaMalloc after start-up (it can synchronise the device
+// and fail under memory pressure).  spark_attn_decode_noalloc gives them the fused
+// split-KV attention without any caller-provided workspace: the partial outputs, the
+// log-sum-exp values and the per-kv-head arrival counters live in the file-scope
+// array below, which every GPU that loads this library keeps until the process exits.
+constexpr int kNoAllocMaxSplits = 64;
+constexpr int kNoAllocMaxQHeads = 64;
+constexpr int kNoAllocMaxKvHeads = 64;
+constexpr size_t kNoAllocPartOFloats = (size_t)kNoAllocMaxSplits * kNoAllocMaxQHeads * 128;
+constexpr size_t kNoAllocLseFloats = (size_t)kNoAllocMaxSplits * kNoAllocMaxQHeads;
+constexpr size_t kNoAllocScratchFloats = kNoAllocPartOFloats + kNoAllocLseFloats + kNoAllocMaxKvHeads;
+// 2,113,792 bytes: partials [64 splits][64 q heads][128] fp32, lse [64][64] fp32, 64 int counters
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
+
+namespace {
+float* g_noalloc_base[64] = {nullptr};
+std::mutex g_noalloc_mu;
+
+// Once per device, with that device current: look up the device address of the
+// scratch array (its name is only a host-side stand-in) and zero the counters.
+int noalloc_scratch(float** base) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return SPARK_ERR_LAUNCH;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_base[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return SPARK_ERR_LAUNCH;
+    float* f = static_cast<float*>(p);
+    if (cudaMemset(f + kNoAllocPartOFloats + kNoAllocLseFloats, 0, kNoAllocMaxKvHeads * sizeof(int)) != cudaSuccess)
+      return SPARK_ERR_LAUNCH;
+    if (cudaDeviceSynchronize() != cudaSuccess) return SPARK_ERR_LAUNCH;
+    g_noalloc_base[dev] = f;
+  }
+  *base = g_noalloc_base[dev];
+  return SPARK_OK;
+}
+}  // namespace
+
+int spark_attn_decode_noalloc(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
+                              const int32_t* block_table, const int64_t* pos, const int32_t* seq_len, int nq,
+                              int nkv, int head_dim, int block_size, int splits, int max_split_tokens, float scale,
+                              uint16_t* out, int* error, void* stream) {
+  if (!out) return SPARK_ERR_INVALID_ARG;
+  if (splits > kNoAllocMaxSplits || nq > kNoAllocMaxQHeads || nkv > kNoAllocMaxKvHeads) return SPARK_ERR_TOO_LARGE;
+  if (splits <= 0 || nq <= 0 || nkv <= 0) return SPARK_ERR_UNSUPPORTED_SHAPE;
+  float* base = nullptr;
+  const int st = noalloc_scratch(&base);
+  if (st != SPARK_OK) return st;
+  float* part_o = base;
+  float* part_lse = base + kNoAllocPartOFloats;
+  int* counters = reinterpret_cast<int*>(base + kNoAllocPartOFloats + kNoAllocLseFloats);
+  return attn_launch(q, k_cache, v_cache, block_table, pos, seq_len, nq, nkv, head_dim, block_size, splits,
+                     max_split_tokens, scale, part_o, part_lse, error, counters, out, stream);
+}
+
 int spark_attn_combine(const float* part_o, const float* part_lse, int splits, int nq, int head_dim, uint16_t* out,
                        void* stream) {
   if (!part_o || !part_lse || !out) return SPARK_ERR_INVALID_ARG;

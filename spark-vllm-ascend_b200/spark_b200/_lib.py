@@ -29,6 +29,7 @@ SIGNATURES: dict[str, list] = {
                                _P],
     "spark_attn_splitkv": [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _F, _P, _P, _P, _P],
     "spark_attn_combine": [_P, _P, _I, _I, _I, _P, _P],
+    "spark_attn_decode_noalloc": [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _F, _P, _P, _P],
     "spark_attn_decode": [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _F, _P, _P, _P, _P, _P, _P],
     "spark_rmsnorm_q4_head_argmax": [_P, _P, _P, _F, _P, _P, _P, _I, _I, _P, _P],
     "spark_decode_finalize": [_P, _P, _P, _P, _P, _P],
