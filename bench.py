@@ -161,6 +161,14 @@ def time_kernels(eng, reps: int = 3) -> dict:
     return out
 
 
+# DRAM bytes (read + write) per launch from one ncu capture of each kernel, divided by
+# the kernel's algorithmic bytes for the captured case; traffic scales with the units
+# processed (weight rows, context tokens), so bench launches get ratio x algorithmic
+# bytes.  Captures: profiles/q4_gemv_ring_gate_up_19456x2560.md,
+# profiles/attn_decode_16splits_ctx6144.md.
+NCU_TRAFFIC_RATIO = {"gate_up": 28_079_360 / 28_051_456, "attn": 25_295_360 / 25_182_208}
+
+
 def kernel_bytes(cfg, ctx: int) -> dict:
     h, i, nq, nkv, D = cfg.hidden_size, cfg.intermediate_size, cfg.num_q_heads, cfg.num_kv_heads, cfg.head_dim
     q4 = lambda n, k: n * k // 32 * 18  # noqa: E731
@@ -321,7 +329,10 @@ def run_spark(args):
             "gpu_launches": eng.kernels_per_step() * args.steps,
             "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": peak,
                          "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
-                         "bytes_per_launch": kb[dom], "us_per_launch": round(kern[dom], 3), "traffic": None},
+                         "bytes_per_launch": kb[dom], "us_per_launch": round(kern[dom], 3),
+                         "traffic": (round(kb[dom] * NCU_TRAFFIC_RATIO[dom]) if dom in NCU_TRAFFIC_RATIO
+                                     else None),
+                         "traffic_source": "ncu dram__bytes_read+write of one capture, scaled by units"},
             "step_roofline": {"bytes_per_step": step_bytes, "achieved_gbs": round(step_bytes / (tpot * 1e-3) / 1e9, 1),
                               "frac": round(step_bytes / (tpot * 1e-3) / 1e9 / peak, 4),
                               "roofline_ms": round(step_bytes / (peak * 1e9) * 1e3, 4)},
