@@ -58,6 +58,10 @@ def lib():
             "orc_silu_mul": (None, [_P, _P, _I64, _P]),
             "orc_slot_mapping": (None, [_I64, _I64, _I64, _I64, _P, _P, _I64, _P]),
             "orc_split_tokens": (_I64, [_I64, _I]),
+            "orc_t16_gemv_parts": (None, [_P, _P, _P, _I64, _I64, _I, _I, _P]),
+            "orc_t16_gemv": (None, [_P, _P, _P, _I64, _I64, _I, _I, _P]),
+            "orc_parts_to_bf16": (None, [_P, _I, _I64, _P]),
+            "orc_attn_split_w": (None, [_P, _P, _P, _P, _I64, _I, _I, _I, _I, _I, _F, _I, _P, _P]),
             "orc_attn_split": (None, [_P, _P, _P, _P, _I64, _I, _I, _I, _I, _I, _F, _P, _P]),
             "orc_attn_combine": (None, [_P, _P, _I, _I, _I, _P]),
             "orc_argmax_bf16": (_I64, [_P, _I64]),
@@ -161,6 +165,28 @@ def q4_gemv_f32(x_f32: np.ndarray, qs: np.ndarray, d: np.ndarray) -> np.ndarray:
     return y
 
 
+def t16_gemv_parts(x_bf16: np.ndarray, qs: np.ndarray, d: np.ndarray, kp: int, ks: int) -> np.ndarray:
+    """Persistent-step GEMV order: fp32 parts [kp, n] (x staged at S = 13 - e)."""
+    xf = bf16_to_f32(np.ascontiguousarray(x_bf16, dtype=np.uint16)).astype(np.float32)
+    n, k = qs.shape[0], qs.shape[1] * 2
+    parts = np.empty((kp, n), np.float32)
+    lib().orc_t16_gemv_parts(_p(np.ascontiguousarray(xf)), _p(np.ascontiguousarray(qs)),
+                             _p(np.ascontiguousarray(d)), n, k, kp, ks, _p(parts))
+    return parts
+
+
+def parts_to_bf16(parts: np.ndarray) -> np.ndarray:
+    parts = np.ascontiguousarray(parts, dtype=np.float32)
+    kp, n = parts.shape
+    y = np.empty(n, np.uint16)
+    lib().orc_parts_to_bf16(_p(parts), kp, n, _p(y))
+    return y
+
+
+def t16_gemv(x_bf16: np.ndarray, qs: np.ndarray, d: np.ndarray, kp: int, ks: int) -> np.ndarray:
+    return parts_to_bf16(t16_gemv_parts(x_bf16, qs, d, kp, ks))
+
+
 # ----------------------------------------------------------------- elementwise
 def add_rmsnorm(a, b, gamma, eps: float, want_res: bool = True):
     a = np.ascontiguousarray(a, dtype=np.uint16)
@@ -212,8 +238,10 @@ def split_tokens(length: int, splits: int) -> int:
     return lib().orc_split_tokens(length, splits)
 
 
-def attn_split(q, kc, vc, table, length: int, splits: int, scale: float):
-    """q bf16 [nq, D]; kc/vc bf16 [blocks, nkv, bs, D]; returns (part_o [S,nq,D], part_lse [S,nq])."""
+def attn_split(q, kc, vc, table, length: int, splits: int, scale: float, chunk_accs: int = 0):
+    """q bf16 [nq, D]; kc/vc bf16 [blocks, nkv, bs, D]; returns (part_o [S,nq,D], part_lse [S,nq]).
+    ``chunk_accs`` > 0 selects the persistent-step PV order (16-token chunks into that
+    many accumulators)."""
     q = np.ascontiguousarray(q, dtype=np.uint16)
     kc = np.ascontiguousarray(kc, dtype=np.uint16)
     vc = np.ascontiguousarray(vc, dtype=np.uint16)
@@ -221,8 +249,8 @@ def attn_split(q, kc, vc, table, length: int, splits: int, scale: float):
     _, nkv, bs, _ = kc.shape
     po = np.empty((splits, nq, dim), np.float32)
     pl = np.empty((splits, nq), np.float32)
-    lib().orc_attn_split(_p(q), _p(kc), _p(vc), _p(np.ascontiguousarray(table, dtype=np.int32)), length, nq, nkv,
-                         dim, bs, splits, scale, _p(po), _p(pl))
+    lib().orc_attn_split_w(_p(q), _p(kc), _p(vc), _p(np.ascontiguousarray(table, dtype=np.int32)), length, nq,
+                           nkv, dim, bs, splits, scale, chunk_accs, _p(po), _p(pl))
     return po, pl
 
 
@@ -256,7 +284,9 @@ class OracleModel:
     ``spark_b200.model.SyntheticWeights.to_numpy()``.
     """
 
-    def __init__(self, cfg, weights: dict, num_blocks: int, splits: int):
+    def __init__(self, cfg, weights: dict, num_blocks: int, splits: int, order: dict | None = None):
+        """``order`` None: per-kernel evaluation order.  Persistent-step order:
+        {"ks": (qkv, o, gate_up, down, head), "kp": (o, down), "chunk_accs": W}."""
         self.cfg = cfg
         self.w = weights
         self.splits = splits
@@ -267,6 +297,11 @@ class OracleModel:
         self.dims = np.array([cfg.hidden_size, cfg.num_q_heads, cfg.num_kv_heads, cfg.head_dim,
                               cfg.intermediate_size, cfg.vocab_size, cfg.num_layers, cfg.block_size,
                               splits, cfg.max_position], dtype=np.int64)
+        if order is None:
+            ext = [0] * 9
+        else:
+            ext = [1, *order["ks"], *order["kp"], order["chunk_accs"]]
+        self.dims = np.concatenate([self.dims, np.array(ext, dtype=np.int64)])
         self._keep = []
         mp = [weights["embed"], weights["final_norm"], weights["head_qs"], weights["head_d"], weights["cos_sin"]]
         self.model_ptrs = (ctypes.c_void_p * 5)(*[_p(a) for a in mp])

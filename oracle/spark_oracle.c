@@ -262,7 +262,7 @@ typedef struct {
 
 static inline float pow2f(int e) { return u2f((uint32_t)(e + 127) << 23); } /* -126 <= e <= 127 */
 
-static void stage_block(const float* x, xq_block* o) {
+static void stage_block_s(const float* x, xq_block* o, int s0) {
     float M = 0.0f;
     for (int j = 0; j < 32; j++) {
         float a = fabsf(x[j]);
@@ -275,7 +275,7 @@ static void stage_block(const float* x, xq_block* o) {
         return;
     }
     int e = (int)((f2u(M) >> 23) & 0xff) - 127; /* M is normal here */
-    int S = 14 - e;
+    int S = s0 - e;
     float sc = pow2f(S);
     int32_t sum = 0;
     for (int j = 0; j < 32; j++) {
@@ -286,6 +286,8 @@ static void stage_block(const float* x, xq_block* o) {
     o->sx = pow2f(-S);
     o->C = 8 * sum;
 }
+
+static void stage_block(const float* x, xq_block* o) { stage_block_s(x, o, 14); }
 
 ORC_API void orc_q4_stage_x(const float* x, int64_t k, int16_t* X, float* sx, int32_t* C) {
     for (int64_t b = 0; b < k / 32; b++) {
@@ -342,6 +344,73 @@ ORC_API void orc_q4_gemv(const uint16_t* x, const uint8_t* qs, const uint16_t* d
     for (int64_t i = 0; i < n * batch; i++) y[i] = f2bf(yf[i]);
     free(xf);
     free(yf);
+}
+
+/* ------------------------------------------------------------------ */
+/* GEMV, persistent-step order ("T16")                                 */
+/* ------------------------------------------------------------------ */
+/* The persistent decode-step kernel evaluates a Q4_0 block's integer dot product
+ * on the tensor cores (16 rows x 32 k per instruction) and splits K differently:
+ *   - x is staged as above but with S = 13 - e (|X_j| <= 16320, so X_j splits into
+ *     two signed bytes, X = 256 h + l); P = sum_j (q_j - 8) X_j is the same exact
+ *     integer however it is evaluated;
+ *   - a row's K/32 blocks are cut into KP equal parts and each part into KS equal
+ *     slices.  Per slice: acc = 0, then for each block in ascending order
+ *     acc = fma(fp32(d) * sx, (float)P, acc).  Part value = ((acc_0 + acc_1) + ...)
+ *     + acc_{KS-1}.  The row's value is ((part_0 + part_1) + ...) + part_{KP-1},
+ *     rounded to bf16 (parts are exchanged between kernels as fp32). */
+static void t16_row_parts(const uint8_t* qs, const uint16_t* d, const xq_block* xb, int64_t nb, int kp, int ks,
+                          float* parts, int64_t pstride) {
+    int64_t bpp = nb / kp, bps = bpp / ks;
+    for (int p = 0; p < kp; p++) {
+        float part = 0.0f;
+        for (int sl = 0; sl < ks; sl++) {
+            float acc = 0.0f;
+            int64_t b0 = (int64_t)p * bpp + (int64_t)sl * bps;
+            for (int64_t b = b0; b < b0 + bps; b++) {
+                const uint8_t* q = qs + b * 16;
+                const xq_block* xx = xb + b;
+                int32_t P = 0;
+                for (int e = 0; e < 16; e++)
+                    P += (int32_t)(q[e] & 15) * xx->X[e] + (int32_t)(q[e] >> 4) * xx->X[e + 16];
+                P -= xx->C;
+                acc = fmaf(h2f(d[b]) * xx->sx, (float)P, acc);
+            }
+            part = sl == 0 ? acc : part + acc;
+        }
+        parts[p * pstride] = part;
+    }
+}
+
+/* parts fp32 [kp][n] of W x for fp32 x [k] (x holds bf16 values) */
+ORC_API void orc_t16_gemv_parts(const float* x, const uint8_t* qs, const uint16_t* d, int64_t n, int64_t k, int kp,
+                                int ks, float* parts) {
+    int64_t nb = k / 32;
+    xq_block* xb = (xq_block*)malloc(sizeof(xq_block) * nb);
+    for (int64_t b = 0; b < nb; b++) stage_block_s(x + b * 32, xb + b, 13);
+#pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < n; r++) t16_row_parts(qs + r * (k / 2), d + r * nb, xb, nb, kp, ks, parts + r, n);
+    free(xb);
+}
+
+/* y bf16 [n] = bf16(((p_0 + p_1) + ...) + p_{kp-1}) */
+ORC_API void orc_parts_to_bf16(const float* parts, int kp, int64_t n, uint16_t* y) {
+    for (int64_t r = 0; r < n; r++) {
+        float v = parts[r];
+        for (int p = 1; p < kp; p++) v = v + parts[(int64_t)p * n + r];
+        y[r] = f2bf(v);
+    }
+}
+
+ORC_API void orc_t16_gemv(const uint16_t* x, const uint8_t* qs, const uint16_t* d, int64_t n, int64_t k, int kp,
+                          int ks, uint16_t* y) {
+    float* xf = (float*)malloc(sizeof(float) * k);
+    float* parts = (float*)malloc(sizeof(float) * n * kp);
+    for (int64_t i = 0; i < k; i++) xf[i] = bf2f(x[i]);
+    orc_t16_gemv_parts(xf, qs, d, n, k, kp, ks, parts);
+    orc_parts_to_bf16(parts, kp, n, y);
+    free(xf);
+    free(parts);
 }
 
 /* ------------------------------------------------------------------ */
@@ -444,14 +513,19 @@ static float score_dot(const float* qf, const uint16_t* kr, int dim) {
 
 /* q bf16 [nq][dim]; caches bf16 [blocks][nkv][bs][dim]; table int32;
  * part_o fp32 [splits][nq][dim]; part_lse fp32 [splits][nq] */
-ORC_API void orc_attn_split(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const int32_t* table,
-                            int64_t len, int nq, int nkv, int dim, int bs, int splits, float scale,
-                            float* part_o, float* part_lse) {
+/* W == 0: PV sums each output dim over the split's tokens in ascending order.
+ * W > 0 (persistent-step order): the split's tokens form 16-token chunks; chunk c
+ * is summed (tokens ascending) into accumulator c mod W, chunks in ascending order;
+ * O = ((O_0 + O_1) + ...) + O_{W-1}, empty accumulators included as 0. */
+ORC_API void orc_attn_split_w(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const int32_t* table,
+                              int64_t len, int nq, int nkv, int dim, int bs, int splits, float scale, int W,
+                              float* part_o, float* part_lse) {
     int group = nq / nkv;
     int64_t T = split_tokens(len, splits);
+    int nacc = W > 0 ? W : 1;
     float* scores = (float*)malloc(sizeof(float) * (T > 0 ? T : 1));
     float* qf = (float*)malloc(sizeof(float) * dim);
-    float* o = (float*)malloc(sizeof(float) * dim);
+    float* o = (float*)malloc(sizeof(float) * dim * nacc);
     for (int s = 0; s < splits; s++) {
         int64_t t0 = (int64_t)s * T, t1 = t0 + T < len ? t0 + T : len;
         int64_t n = t1 - t0;
@@ -481,12 +555,15 @@ ORC_API void orc_attn_split(const uint16_t* q, const uint16_t* kc, const uint16_
             }
             butterfly(lane, 32);
             float l = lane[0];
-            for (int dd = 0; dd < dim; dd++) o[dd] = 0.0f;
+            for (int dd = 0; dd < dim * nacc; dd++) o[dd] = 0.0f;
             for (int64_t i = 0; i < n; i++) {
                 int64_t t = t0 + i, blk = table[t / bs], off = t % bs;
                 const uint16_t* vr = vc + ((blk * nkv + hk) * bs + off) * dim;
-                for (int dd = 0; dd < dim; dd++) o[dd] = fmaf(scores[i], bf2f(vr[dd]), o[dd]);
+                float* oa = o + (W > 0 ? (i / 16) % W : 0) * dim;
+                for (int dd = 0; dd < dim; dd++) oa[dd] = fmaf(scores[i], bf2f(vr[dd]), oa[dd]);
             }
+            for (int w = 1; w < nacc; w++)
+                for (int dd = 0; dd < dim; dd++) o[dd] = o[dd] + o[w * dim + dd];
             for (int dd = 0; dd < dim; dd++) po[dd] = o[dd] / l;
             part_lse[(int64_t)s * nq + hq] = orc_log(l) + m;
         }
@@ -494,6 +571,12 @@ ORC_API void orc_attn_split(const uint16_t* q, const uint16_t* kc, const uint16_
     free(scores);
     free(qf);
     free(o);
+}
+
+ORC_API void orc_attn_split(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const int32_t* table,
+                            int64_t len, int nq, int nkv, int dim, int bs, int splits, float scale,
+                            float* part_o, float* part_lse) {
+    orc_attn_split_w(q, kc, vc, table, len, nq, nkv, dim, bs, splits, scale, 0, part_o, part_lse);
 }
 
 /* out bf16 [nq][dim] = sum_s softmax(lse)_s * part_o[s] */
@@ -552,6 +635,23 @@ ORC_API int64_t orc_argmax_bf16(const uint16_t* logits, int64_t n) {
  *   qkv rows: q heads, then k heads, then v heads; gu rows: gate [I] then up [I].
  * kc / vc: bf16 [layers][blocks][nkv][bs][D]; table int32 shared by all layers. */
 
+/* dims[10] selects the evaluation order: 0 = per-kernel path (lane-16 GEMV,
+ * sequential PV); 1 = persistent-step path (T16 GEMV with dims[11..15] = KS of
+ * qkv, o, gate_up, down, head and dims[16..17] = KP of o and down; attention PV
+ * with dims[18] chunk accumulators). */
+enum { MAT_QKV = 0, MAT_O = 1, MAT_GU = 2, MAT_DOWN = 3, MAT_HEAD = 4 };
+
+static void gemv_v(const int64_t* dims, int mat, const uint16_t* x, const void* qs, const void* d, int64_t n,
+                   int64_t k, uint16_t* y) {
+    if (dims[10] == 0) {
+        orc_q4_gemv(x, (const uint8_t*)qs, (const uint16_t*)d, n, k, 1, y);
+        return;
+    }
+    int ks = (int)dims[11 + mat];
+    int kp = mat == MAT_O ? (int)dims[16] : mat == MAT_DOWN ? (int)dims[17] : 1;
+    orc_t16_gemv(x, (const uint8_t*)qs, (const uint16_t*)d, n, k, kp, ks, y);
+}
+
 /* One decoder layer.  In: a (bf16 [H]) and b (bf16 [H]; ignored for layer 0).
  * Out: a <- down projection, b <- residual after attention (resmid).  kc / vc are
  * this layer's caches [blocks][nkv][bs][D]; the new token is stored at pos. */
@@ -572,21 +672,22 @@ ORC_API void orc_decode_layer(const int64_t* dims, const void* const* lp, const 
     int64_t blk = table[pos / bs], off = pos % bs;
     /* input norm: s = a + b; res = bf16(s) */
     orc_add_rmsnorm(a, has_b ? b : NULL, (const uint16_t*)lp[0], H, eps, res, x);
-    orc_q4_gemv(x, (const uint8_t*)lp[2], (const uint16_t*)lp[3], nqkv, H, 1, qkv);
+    gemv_v(dims, MAT_QKV, x, lp[2], lp[3], nqkv, H, qkv);
     orc_rope_neox(qkv, nq + nkv, D, cos_sin + pos * D);
     for (int hk = 0; hk < nkv; hk++) {
         memcpy(kc + ((blk * nkv + hk) * bs + off) * D, qkv + (int64_t)(nq + hk) * D, 2 * D);
         memcpy(vc + ((blk * nkv + hk) * bs + off) * D, qkv + (int64_t)(nq + nkv + hk) * D, 2 * D);
     }
-    orc_attn_split(qkv, kc, vc, table, pos + 1, nq, nkv, D, bs, splits, scale, po, pl);
+    orc_attn_split_w(qkv, kc, vc, table, pos + 1, nq, nkv, D, bs, splits, scale, dims[10] ? (int)dims[18] : 0, po,
+                     pl);
     orc_attn_combine(po, pl, splits, nq, D, attn);
     /* o_proj -> a */
-    orc_q4_gemv(attn, (const uint8_t*)lp[4], (const uint16_t*)lp[5], H, (int64_t)nq * D, 1, a);
+    gemv_v(dims, MAT_O, attn, lp[4], lp[5], H, (int64_t)nq * D, a);
     /* post-attention norm: s = oproj + res -> resmid (into b) */
     orc_add_rmsnorm(a, res, (const uint16_t*)lp[1], H, eps, b, x);
-    orc_q4_gemv(x, (const uint8_t*)lp[6], (const uint16_t*)lp[7], 2 * (int64_t)I, H, 1, gu);
+    gemv_v(dims, MAT_GU, x, lp[6], lp[7], 2 * (int64_t)I, H, gu);
     orc_silu_mul(gu, gu + I, I, mid);
-    orc_q4_gemv(mid, (const uint8_t*)lp[8], (const uint16_t*)lp[9], H, I, 1, a);
+    gemv_v(dims, MAT_DOWN, mid, lp[8], lp[9], H, I, a);
     free(res); free(x); free(qkv); free(attn); free(gu); free(mid); free(po); free(pl);
 }
 
@@ -598,7 +699,7 @@ ORC_API int64_t orc_decode_head(const int64_t* dims, const void* const* model, c
     uint16_t* x = (uint16_t*)malloc(2 * H);
     orc_add_rmsnorm(a, b, (const uint16_t*)model[1], H, eps, NULL, x);
     uint16_t* lg = logits ? logits : (uint16_t*)malloc(2 * V);
-    orc_q4_gemv(x, (const uint8_t*)model[2], (const uint16_t*)model[3], V, H, 1, lg);
+    gemv_v(dims, MAT_HEAD, x, model[2], model[3], V, H, lg);
     int64_t tok = orc_argmax_bf16(lg, V);
     if (!logits) free(lg);
     free(x);

@@ -122,7 +122,7 @@ def test_gemv_oracle_vs_dequant_matmul(oracle, n, k, batch):
     assert np.max(np.abs(yf - ref)) < 1e-4 * max(1.0, np.abs(ref).max())
 
 
-def _stage_np(xf):
+def _stage_np(xf, s0=14):
     """Independent numpy restatement of the documented activation staging."""
     X = np.zeros(xf.size, np.int64)
     sx = np.ones(xf.size // 32, np.float32)
@@ -133,7 +133,7 @@ def _stage_np(xf):
         if not (M >= np.float32(2.0 ** -100)) or not np.isfinite(M):
             continue
         e = int(np.floor(np.log2(np.float64(M))))
-        S = 14 - e
+        S = s0 - e
         X[32 * b:32 * b + 32] = np.rint(blk.astype(np.float64) * 2.0 ** S).astype(np.int64)
         sx[b] = np.float32(2.0 ** -S)
         C[b] = 8 * X[32 * b:32 * b + 32].sum()
@@ -182,6 +182,54 @@ def test_gemv_canonical_order_is_documented(oracle):
         rows.append(v[0])
     got = oracle.q4_gemv_f32(xf, qs, d)[0]
     assert np.array_equal(np.array(rows, np.float32).view(np.uint32), got.view(np.uint32))
+
+
+@pytest.mark.parametrize("kp,ks", [(1, 1), (1, 4), (2, 2), (4, 1)])
+def test_t16_gemv_order_is_documented(oracle, kp, ks):
+    """Persistent-step order: S = 13 - e staging, KP parts of KS slices, sequential sums."""
+    x, qs, d = _q4_setup(3, 1024, seed=5)
+    xf = f32(x)[0]
+    X, sx, C = _stage_np(xf, s0=13)
+    assert np.abs(X).max() <= 16320
+    # X splits into two signed bytes: X = 256 h + l, h, l in [-128, 127]
+    lo = ((X + 128) & 255) - 128
+    hi = (X - lo) // 256
+    assert np.abs(hi).max() <= 64 and np.array_equal(256 * hi + lo, X)
+    nb = 1024 // 32
+    bpp, bps = nb // kp, nb // kp // ks
+    dd = d.view(np.float16).astype(np.float32)
+    want = np.zeros((kp, 3), np.float32)
+    for r in range(3):
+        for p in range(kp):
+            part = np.float32(0)
+            for sl in range(ks):
+                acc = np.float32(0)
+                for b in range(p * bpp + sl * bps, p * bpp + (sl + 1) * bps):
+                    q = qs[r, b * 16:(b + 1) * 16].astype(np.int64)
+                    P = int(((q & 15) * X[32 * b:32 * b + 16]).sum() + ((q >> 4) * X[32 * b + 16:32 * b + 32]).sum()
+                            - C[b])
+                    ds = np.float32(dd[r, b] * sx[b])
+                    acc = np.float32(np.float64(ds) * np.float64(P) + np.float64(acc))
+                part = acc if sl == 0 else np.float32(part + acc)
+            want[p, r] = part
+    got = oracle.t16_gemv_parts(x[0], qs, d, kp, ks)
+    assert np.array_equal(want.view(np.uint32), got.view(np.uint32))
+    y = oracle.t16_gemv(x[0], qs, d, kp, ks)
+    tot = want[0].copy()
+    for p in range(1, kp):
+        tot = (tot + want[p]).astype(np.float32)
+    assert np.array_equal(y, bf16(tot))
+
+
+@pytest.mark.parametrize("n,k,kp,ks", [(64, 2560, 1, 4), (48, 4096, 2, 4), (32, 9728, 4, 2)])
+def test_t16_gemv_vs_dequant_matmul(oracle, n, k, kp, ks):
+    """The persistent-step order meets the GEMV tolerance (rel 1e-2 / abs 1e-3) against the
+    reference's dequantize-then-matmul."""
+    x, qs, d = _q4_setup(n, k, seed=n + k)
+    w = oracle.q4_dequantize(qs, d)
+    ref = f32(x)[0].astype(np.float64) @ w.astype(np.float64).T
+    y = f32(oracle.t16_gemv(x[0], qs, d, kp, ks))
+    assert np.all(np.abs(y - ref) <= 1e-3 + 1e-2 * np.abs(ref))
 
 
 # ----------------------------------------------------------------------------- norm / rope / silu
@@ -261,6 +309,22 @@ def test_attention_split_combine_vs_float64(oracle, L, splits):
     T = oracle.split_tokens(L, splits)
     empty = [s for s in range(splits) if s * T >= L]
     assert all(np.all(np.isneginf(pl[s])) and np.all(po[s] == 0) for s in empty)
+
+
+@pytest.mark.parametrize("L,splits,W", [(3000, 18, 12), (700, 18, 12), (64, 74, 12), (2049, 5, 3)])
+def test_attention_chunk_accumulators_vs_float64(oracle, L, splits, W):
+    """Persistent-step PV order (16-token chunks into W accumulators) meets abs 2e-2 and
+    agrees with the sequential order to fp32 rounding."""
+    rng = np.random.default_rng(L + W)
+    kc, vc, table = _paged(rng, L)
+    q = bf16(rng.standard_normal((32, 128)).astype(np.float32))
+    scale = float(np.float32(1 / math.sqrt(128)))
+    po, pl = oracle.attn_split(q, kc, vc, table, L, splits, scale, chunk_accs=W)
+    out = f32(oracle.attn_combine(po, pl))
+    assert np.max(np.abs(out - _attn_ref64(q, kc, vc, table, L, scale))) <= 2e-2
+    po0, pl0 = oracle.attn_split(q, kc, vc, table, L, splits, scale)
+    assert np.array_equal(pl, pl0)
+    assert np.allclose(po, po0, rtol=1e-5, atol=1e-6)
 
 
 def test_combine_single_split_identity(oracle):
