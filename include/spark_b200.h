@@ -198,6 +198,103 @@ int spark_set_gemv_ring(int enabled);
  * are then incomplete. */
 int spark_read_device_error(int* value, int reset);
 
+/* ======================================================================
+ * Persistent decode step.
+ *
+ * Replaces the reference's per-layer DecodeLayer launch (integration/model.py:
+ * 118-139; kernels/layer.py:48-109 chains qkv, attention, o, gate_up and down in
+ * one compiled program per layer) with ONE cooperative kernel per decode step
+ * that runs a program of stages over all SMs.  Each SM streams the Q4_0 weights
+ * of its share of every GEMV stage (and the K/V pages of its attention split)
+ * through a shared-memory ring with bulk copies, running ahead of the stage
+ * barriers, so HBM keeps streaming while the stages synchronise.
+ *
+ * Weights use the T16 layout (spark_q4_pack_t16): units of 16 rows x K/kp
+ * columns, 9 * K/kp bytes each, laid out for the integer tensor-core dot
+ * product of a Q4_0 block.  Unit u covers row group u / kp and K part u % kp.
+ * ====================================================================== */
+
+#define SPARK_STAGE_GEMV 0
+#define SPARK_STAGE_ATTN 1
+
+/* GEMV prologue: where x comes from */
+#define SPARK_PRO_BF16 0  /* a: bf16 [k] (or embed row embed[*token] when embed != NULL) */
+#define SPARK_PRO_PARTS 1 /* a: fp32 [a_parts][k]; x = bf16(((a_0 + a_1) + ...)) */
+
+/* GEMV epilogue */
+#define SPARK_EPI_BF16 0     /* out bf16 [n] (kp == 1) */
+#define SPARK_EPI_PARTS 1    /* out fp32 [kp][n], the per-part sums */
+#define SPARK_EPI_ROPE_KV 2  /* qkv: neox RoPE on q/k, q -> q, k/v -> paged cache + kv_new */
+#define SPARK_EPI_SILU_MUL 3 /* gate_up: out bf16 [n/2] = silu(gate) * up */
+#define SPARK_EPI_ARGMAX 4   /* LM head: logits bf16 [n] (out, nullable), atomicMax into key */
+
+/* logical rows of unit position p (0..15) of row group rg */
+#define SPARK_ROWS_PLAIN 0     /* 16 rg + p */
+#define SPARK_ROWS_PAIR_HALF 1 /* qkv heads: pair (i, i + head_dim/2) in positions (p, p + 8) */
+#define SPARK_ROWS_GATE_UP 2   /* gate row 8 rg + p and up row n/2 + 8 rg + p in positions (p, p + 8) */
+
+typedef struct SparkStage {
+  int32_t kind, pro, epi, rowmap;
+  int32_t n, k, kp, ks;         /* GEMV rows, columns, K parts, slices per part (integer order) */
+  int32_t units, rot, wait, norm; /* units = n/16*kp; rot = first CTA; wait = stage to await (-1) */
+  int32_t a_parts, block_size, nq, nkv;
+  int32_t head_dim, splits, max_split_tokens, reserved0;
+  float eps, inv_k, scale, reserved1;
+  const void* w;              /* T16 weight units */
+  const void* a;              /* input (see SPARK_PRO_*) */
+  const void* b;              /* residual added before the norm (nullable) */
+  const void* embed;          /* bf16 [vocab][k]: layer-0 input row *token (nullable) */
+  const int32_t* token;
+  const void* gamma;          /* RMSNorm weight (used when norm != 0) */
+  void* res_out;              /* bf16(a + b) (nullable) */
+  void* out;
+  const void* cos_sin;        /* bf16 [max_pos][head_dim]: cos | sin */
+  const int64_t* pos;         /* position of the token being decoded */
+  const int32_t* block_table; /* int32 logical -> physical KV block */
+  void* k_cache;              /* bf16 [blocks][nkv][block_size][head_dim] (this layer) */
+  void* v_cache;
+  void* q;                    /* bf16 [nq][head_dim] */
+  void* kv_new;               /* bf16 [2][nkv][head_dim]: this token's k and v */
+  unsigned long long* key;    /* argmax key (zero before the stage) */
+  float* part_o;              /* fp32 [splits][nq][head_dim] */
+  float* part_lse;            /* fp32 [splits][nq] */
+  int32_t* head_counters;     /* int32 [nkv], zero; the kernel leaves them zero */
+  void* attn_out;             /* bf16 [nq][head_dim] */
+} SparkStage;
+
+typedef struct SparkStepIO {
+  int32_t* counters;          /* int32 [num_stages + 2], zero before the first launch */
+  int32_t* error;             /* int32 [1] status written on a timed-out wait (nullable) */
+  unsigned long long* key;    /* after the last stage: token = argmax of key (nullable) */
+  int32_t* token_out;
+  int32_t* token_log;         /* token_log[*step] = token (nullable) */
+  int32_t* step;              /* incremented (nullable) */
+  int64_t* pos;               /* incremented (nullable) */
+} SparkStepIO;
+
+/* Bytes of a matrix in the T16 layout: n * k * 9 / 16. */
+int64_t spark_t16_bytes(int n, int k, int kp);
+
+/* Re-lay a Q4_0 matrix (qs / d planes) as T16 units.  rowmap SPARK_ROWS_*; aux =
+ * head_dim for SPARK_ROWS_PAIR_HALF, unused otherwise.  Needs n % 16 == 0,
+ * (k / kp) % 128 == 0.  Replaces the reference's offline packer
+ * (integration/weights.py:42-55, pack into its megakernel tile layout). */
+int spark_q4_pack_t16(const uint8_t* qs, const uint16_t* d, int n, int k, int kp, int rowmap, int aux, uint8_t* out,
+                      void* stream);
+
+/* Shared memory the step kernel keeps for the weight / KV ring (bytes). */
+int spark_step_ring_bytes(void);
+
+/* Number of CTAs (one per SM) the step kernel runs with on the current device. */
+int spark_step_num_ctas(void);
+
+/* Run a stage program as one cooperative launch.  host_stages is validated on the
+ * host; the kernel reads dev_stages (an identical copy in device memory), or, for
+ * a single stage, dev_stages may be NULL and the stage travels in the launch
+ * parameters.  Stage i may only wait on a stage j < i. */
+int spark_step_run(const SparkStage* host_stages, const SparkStage* dev_stages, int num_stages,
+                   const SparkStepIO* io, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

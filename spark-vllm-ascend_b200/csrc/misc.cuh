@@ -159,9 +159,12 @@ __global__ void slot_mapping_kernel(int64_t n, int64_t max_tokens, const int32_t
 }
 
 // ------------------------------------------------------------------ decode bookkeeping
+// The next step's kernels start only after this one has written the new token and
+// position: the attention kernel reads the position before its own PDL wait, so
+// the trigger comes last (after the head kernel completed, which by the chain of
+// waits means the whole previous step completed).
 __global__ void decode_finalize_kernel(unsigned long long* key, int32_t* token_out, int32_t* token_log,
                                        int32_t* step, int64_t* pos) {
-  pdl_launch_dependents();
   pdl_wait();
   if (threadIdx.x == 0 && blockIdx.x == 0) {
     unsigned long long k = *key;
@@ -171,7 +174,10 @@ __global__ void decode_finalize_kernel(unsigned long long* key, int32_t* token_o
     *key = 0ull;
     if (pos) pos[0] += 1;
     if (step) step[0] += 1;
+    __threadfence();
   }
+  __syncthreads();
+  pdl_launch_dependents();
 }
 
 }  // namespace spark

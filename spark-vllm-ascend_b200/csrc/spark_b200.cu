@@ -17,6 +17,7 @@
 #include "q4_gemv.cuh"
 #include "q4_gemv_ring.cuh"
 #include "spark_b200.h"
+#include "step_kernel.cuh"
 
 using namespace spark;
 
@@ -592,6 +593,132 @@ int spark_slot_mapping(int64_t num_tokens, int64_t max_tokens, const int32_t* qu
   if (grid > 4 * num_sms()) grid = 4 * num_sms();
   return launch(slot_mapping_kernel, dim3((unsigned)grid), dim3(256), 0, as_stream(stream), num_tokens, max_tokens,
                 query_start, positions, block_table, block_size, out);
+}
+
+// ------------------------------------------------------------------ persistent decode step
+int64_t spark_t16_bytes(int n, int k, int kp) {
+  if (n <= 0 || k <= 0 || kp <= 0 || k % kp) return -1;
+  return (int64_t)(n / 16) * kp * 9 * (k / kp);
+}
+
+int spark_q4_pack_t16(const uint8_t* qs, const uint16_t* d, int n, int k, int kp, int rowmap, int aux, uint8_t* out,
+                      void* stream) {
+  if (!qs || !d || !out) return SPARK_ERR_INVALID_ARG;
+  if (n <= 0 || k <= 0 || kp <= 0 || n % 16 || k % kp || (k / kp) % 64) return SPARK_ERR_UNSUPPORTED_SHAPE;
+  if (rowmap == SPARK_ROWS_PAIR_HALF) {
+    if (aux <= 0 || aux % 16 || n % aux) return SPARK_ERR_UNSUPPORTED_SHAPE;
+  } else if (rowmap == SPARK_ROWS_GATE_UP) {
+    if ((n / 2) % 8) return SPARK_ERR_UNSUPPORTED_SHAPE;
+  } else if (rowmap != SPARK_ROWS_PLAIN) {
+    return SPARK_ERR_INVALID_ARG;
+  }
+  if ((reinterpret_cast<uintptr_t>(qs) | reinterpret_cast<uintptr_t>(out)) & 15) return SPARK_ERR_ALIGNMENT;
+  if (reinterpret_cast<uintptr_t>(d) & 3) return SPARK_ERR_ALIGNMENT;
+  const int64_t total = (int64_t)(n / 16) * kp * ((k / kp) / 64) * 32;
+  int64_t grid = (total + 255) / 256;
+  if (grid > 16 * num_sms()) grid = 16 * num_sms();
+  return launch(step::t16_pack_kernel, dim3((unsigned)grid), dim3(256), 0, as_stream(stream), qs, d, n, k, kp, rowmap,
+                aux, out);
+}
+
+int spark_step_ring_bytes(void) { return step::kRingBytes; }
+
+int spark_step_num_ctas(void) { return num_sms(); }
+
+static int check_stage(const SparkStage& s, int i, int ncta) {
+  if (s.wait >= i || s.wait < -1) return SPARK_ERR_INVALID_ARG;
+  if (s.kind == SPARK_STAGE_GEMV) {
+    if (!s.w || !s.a && !s.embed) return SPARK_ERR_INVALID_ARG;
+    if (s.n <= 0 || s.n % 16 || s.k <= 0 || s.kp <= 0 || s.k % s.kp || (s.k / s.kp) % 64 || s.ks <= 0 ||
+        ((s.k / s.kp) / 64) % s.ks)
+      return SPARK_ERR_UNSUPPORTED_SHAPE;
+    if (s.units != s.n / 16 * s.kp || s.rot < 0 || s.rot >= ncta) return SPARK_ERR_INVALID_ARG;
+    if (9 * (s.k / s.kp) > step::kRingBytes) return SPARK_ERR_TOO_LARGE;
+    const int nl = (s.units + ncta - 1) / ncta;
+    if (nl * s.ks * 16 * 4 > step::kPartialBytes) return SPARK_ERR_TOO_LARGE;
+    if (72 * (s.k / 32) + (s.norm ? 4 * s.k : 0) > step::kScratchBytes) return SPARK_ERR_TOO_LARGE;
+    if (s.pro == SPARK_PRO_PARTS) {
+      if (s.a_parts <= 0 || !s.a || s.embed) return SPARK_ERR_INVALID_ARG;
+    } else if (s.pro != SPARK_PRO_BF16) {
+      return SPARK_ERR_INVALID_ARG;
+    }
+    if (s.embed && !s.token) return SPARK_ERR_INVALID_ARG;
+    if (s.norm && !s.gamma) return SPARK_ERR_INVALID_ARG;
+    if (reinterpret_cast<uintptr_t>(s.w) & 15) return SPARK_ERR_ALIGNMENT;
+    switch (s.epi) {
+      case SPARK_EPI_BF16:
+        if (s.kp != 1 || !s.out) return SPARK_ERR_INVALID_ARG;
+        break;
+      case SPARK_EPI_PARTS:
+        if (!s.out) return SPARK_ERR_INVALID_ARG;
+        break;
+      case SPARK_EPI_SILU_MUL:
+        if (s.kp != 1 || !s.out || s.rowmap != SPARK_ROWS_GATE_UP) return SPARK_ERR_INVALID_ARG;
+        break;
+      case SPARK_EPI_ARGMAX:
+        if (s.kp != 1 || !s.key) return SPARK_ERR_INVALID_ARG;
+        break;
+      case SPARK_EPI_ROPE_KV:
+        if (s.kp != 1 || s.rowmap != SPARK_ROWS_PAIR_HALF || !s.q || !s.k_cache || !s.v_cache || !s.kv_new ||
+            !s.cos_sin || !s.pos || !s.block_table || s.block_size <= 0 || s.nq <= 0 || s.nkv <= 0)
+          return SPARK_ERR_INVALID_ARG;
+        if (s.n != (s.nq + 2 * s.nkv) * s.head_dim) return SPARK_ERR_UNSUPPORTED_SHAPE;
+        break;
+      default:
+        return SPARK_ERR_INVALID_ARG;
+    }
+    if (s.rowmap == SPARK_ROWS_PAIR_HALF) {
+      if (s.head_dim <= 0 || s.head_dim % 16 || s.n % s.head_dim) return SPARK_ERR_UNSUPPORTED_SHAPE;
+    } else if (s.rowmap != SPARK_ROWS_PLAIN && s.rowmap != SPARK_ROWS_GATE_UP) {
+      return SPARK_ERR_INVALID_ARG;
+    }
+    return SPARK_OK;
+  }
+  if (s.kind != SPARK_STAGE_ATTN) return SPARK_ERR_INVALID_ARG;
+  if (!s.q || !s.k_cache || !s.v_cache || !s.kv_new || !s.pos || !s.block_table || !s.part_o || !s.part_lse ||
+      !s.head_counters || !s.attn_out)
+    return SPARK_ERR_INVALID_ARG;
+  if (s.head_dim != 128 || s.nkv <= 0 || s.nq != 4 * s.nkv || s.block_size <= 0 || s.block_size % step::kRunTokens)
+    return SPARK_ERR_UNSUPPORTED_SHAPE;
+  if (s.splits <= 0 || s.nkv * s.splits > ncta) return SPARK_ERR_UNSUPPORTED_SHAPE;
+  if (s.max_split_tokens <= 0 || s.max_split_tokens > step::kMaxSplitTokens) return SPARK_ERR_TOO_LARGE;
+  if ((reinterpret_cast<uintptr_t>(s.kv_new) | reinterpret_cast<uintptr_t>(s.k_cache) |
+       reinterpret_cast<uintptr_t>(s.v_cache) | reinterpret_cast<uintptr_t>(s.part_o) |
+       reinterpret_cast<uintptr_t>(s.q)) & 15)
+    return SPARK_ERR_ALIGNMENT;
+  return SPARK_OK;
+}
+
+int spark_step_run(const SparkStage* host_stages, const SparkStage* dev_stages, int num_stages, const SparkStepIO* io,
+                   void* stream) {
+  if (!host_stages || !io || !io->counters || num_stages <= 0) return SPARK_ERR_INVALID_ARG;
+  if (num_stages > 1 && !dev_stages) return SPARK_ERR_INVALID_ARG;
+  if (dev_stages && (reinterpret_cast<uintptr_t>(dev_stages) & 15)) return SPARK_ERR_ALIGNMENT;
+  const int ncta = num_sms();
+  for (int i = 0; i < num_stages; i++) {
+    const int st = check_stage(host_stages[i], i, ncta);
+    if (st != SPARK_OK) return st;
+  }
+  step::StepParams P;
+  memset(&P, 0, sizeof(P));
+  P.stages = num_stages > 1 ? dev_stages : nullptr;
+  P.inline_stage = host_stages[0];
+  P.num_stages = num_stages;
+  P.io = *io;
+  if (!P.io.error) P.io.error = device_error_ptr();
+  if (set_smem(reinterpret_cast<const void*>(step::step_kernel), step::kSmemBytes) != kOk) return kErrLaunch;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(ncta);
+  cfg.blockDim = dim3(step::kThreads);
+  cfg.dynamicSmemBytes = step::kSmemBytes;
+  cfg.stream = as_stream(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, step::step_kernel, P);
+  return e == cudaSuccess ? SPARK_OK : SPARK_ERR_LAUNCH;
 }
 
 }  // extern "C"

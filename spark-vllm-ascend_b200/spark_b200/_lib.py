@@ -40,7 +40,35 @@ SIGNATURES: dict[str, list] = {
     "spark_set_pdl": [_I],
     "spark_set_gemv_ring": [_I],
     "spark_read_device_error": [_P, _I],
+    "spark_t16_bytes": [_I, _I, _I],
+    "spark_q4_pack_t16": [_P, _P, _I, _I, _I, _I, _I, _P, _P],
+    "spark_step_ring_bytes": [],
+    "spark_step_num_ctas": [],
+    "spark_step_run": [_P, _P, _I, _P, _P],
 }
+# entry points whose return value is a quantity, not a status
+RESTYPES = {"spark_t16_bytes": _I64}
+
+
+class SparkStage(ctypes.Structure):
+    """Mirror of ``SparkStage`` in include/spark_b200.h (256 bytes)."""
+
+    _fields_ = [(n, ctypes.c_int32) for n in (
+        "kind", "pro", "epi", "rowmap", "n", "k", "kp", "ks", "units", "rot", "wait", "norm", "a_parts",
+        "block_size", "nq", "nkv", "head_dim", "splits", "max_split_tokens", "reserved0")] + [
+        (n, ctypes.c_float) for n in ("eps", "inv_k", "scale", "reserved1")] + [
+        (n, _P) for n in (
+            "w", "a", "b", "embed", "token", "gamma", "res_out", "out", "cos_sin", "pos", "block_table", "k_cache",
+            "v_cache", "q", "kv_new", "key", "part_o", "part_lse", "head_counters", "attn_out")]
+
+
+class SparkStepIO(ctypes.Structure):
+    """Mirror of ``SparkStepIO`` in include/spark_b200.h."""
+
+    _fields_ = [(n, _P) for n in ("counters", "error", "key", "token_out", "token_log", "step", "pos")]
+
+
+assert ctypes.sizeof(SparkStage) == 256
 
 
 class SparkError(RuntimeError):
@@ -66,7 +94,7 @@ def lib():
         L = ctypes.CDLL(str(_LIB_PATH))
         for name, args in SIGNATURES.items():
             fn = getattr(L, name)
-            fn.restype = _I
+            fn.restype = RESTYPES.get(name, _I)
             fn.argtypes = args
         L.spark_status_string.restype = ctypes.c_char_p
         L.spark_status_string.argtypes = [_I]

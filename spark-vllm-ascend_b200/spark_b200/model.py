@@ -162,11 +162,20 @@ class DecodeEngine:
 
     def __init__(self, weights: SyntheticWeights, max_seq_len: int, splits: int = 0, num_blocks: int | None = None,
                  block_table: torch.Tensor | None = None, use_graph: bool = True, max_steps: int | None = None,
-                 seed: int = 0):
+                 seed: int = 0, mode: str = "step"):
+        """``mode`` "step": one persistent kernel per decode step (spark_b200.step);
+        "kernels": the per-stage kernel chain (5 kernels per layer + head + finalize)."""
         cfg = weights.cfg
         self.cfg, self.w = cfg, weights
         dev = weights.device
         self.device = dev
+        if mode not in ("step", "kernels"):
+            raise ValueError(f"unknown mode {mode!r}")
+        self.mode = mode
+        if mode == "step":
+            from . import step as _step
+            self.ncta = _step.num_ctas()
+            splits = splits or _step.attn_splits(cfg, self.ncta)
         if splits <= 0:  # auto: splits of at most 128 tokens (one K/V chunk), at least 16
             splits = min(256, max(16, -(-max_seq_len // 128)))
         self.splits = splits
@@ -205,7 +214,67 @@ class DecodeEngine:
         self.error = e(1, dt=torch.int32)
         self.use_graph = use_graph
         self.graph = None
-        self._calls = self._build_calls()
+        if mode == "step":
+            self._build_program()
+        else:
+            self._calls = self._build_calls()
+
+    # -- the persistent-kernel program of one step
+    def _build_program(self):
+        from . import step as S
+        cfg, w, dev = self.cfg, self.w, self.device
+        h, i, nq, nkv, D, bs = (cfg.hidden_size, cfg.intermediate_size, cfg.num_q_heads, cfg.num_kv_heads,
+                                cfg.head_dim, cfg.block_size)
+        if self.max_split_tokens > S.MAX_SPLIT_TOKENS:
+            raise ValueError(f"{self.splits} splits give {self.max_split_tokens}-token splits (limit "
+                             f"{S.MAX_SPLIT_TOKENS}); max_seq_len too large for the persistent step")
+        order = S.default_order(cfg, self.ncta)
+        self.step_order = order
+        ks_qkv, ks_o, ks_gu, ks_down, ks_head = order["ks"]
+        kp_o, kp_down = order["kp"]
+        # T16 copies of the weights (the gguf planes stay for the per-kernel path)
+        self.t16 = []
+        for lw in w.layers:
+            self.t16.append((S.q4_pack_t16(lw.qkv.qs, lw.qkv.d, 1, S.ROWS_PAIR_HALF, D),
+                             S.q4_pack_t16(lw.o.qs, lw.o.d, kp_o),
+                             S.q4_pack_t16(lw.gate_up.qs, lw.gate_up.d, 1, S.ROWS_GATE_UP),
+                             S.q4_pack_t16(lw.down.qs, lw.down.d, kp_down)))
+        self.t16_head = S.q4_pack_t16(w.head.qs, w.head.d, 1)
+        f32 = torch.float32
+        self.o_parts = torch.zeros((kp_o, h), dtype=f32, device=dev)
+        self.down_parts = torch.zeros((kp_down, h), dtype=f32, device=dev)
+        self.kv_new = torch.zeros((2, nkv, D), dtype=BF16, device=dev)
+        prog = S.StepProgram(dev, self.ncta)
+        eps = cfg.rms_norm_eps
+        prev = -1
+        for li, (lw, (wq, wo, wgu, wd)) in enumerate(zip(w.layers, self.t16)):
+            kc, vc = self.k_cache[li], self.v_cache[li]
+            rope = {"cos_sin": w.cos_sin, "pos": self.pos, "block_table": self.block_table, "k_cache": kc,
+                    "v_cache": vc, "q": self.q, "kv_new": self.kv_new, "block_size": bs, "nq": nq, "nkv": nkv}
+            if li == 0:
+                src = {"embed": w.embed, "token": self.token}
+            else:
+                src = {"a": self.down_parts, "a_parts": kp_down, "b": self.resmid}
+            qkv = prog.gemv(wq, cfg.qkv_rows, h, ks=ks_qkv, gamma=lw.in_norm, eps=eps, res_out=self.res_attn,
+                            epi=S.EPI_ROPE_KV, rowmap=S.ROWS_PAIR_HALF, head_dim=D, rope=rope, wait=prev, **src)
+            att = prog.attention(q=self.q, k_cache=kc, v_cache=vc, kv_new=self.kv_new, block_table=self.block_table,
+                                 pos=self.pos, splits=self.splits, max_split_tokens=self.max_split_tokens,
+                                 scale=cfg.attn_scale, part_o=self.part_o, part_lse=self.part_lse,
+                                 head_counters=self.counters, attn_out=self.attn_out, nq=nq, nkv=nkv, head_dim=D,
+                                 block_size=bs, wait=qkv)
+            o = prog.gemv(wo, h, nq * D, kp=kp_o, ks=ks_o, a=self.attn_out, epi=S.EPI_PARTS, out=self.o_parts,
+                          wait=att)
+            gu = prog.gemv(wgu, 2 * i, h, ks=ks_gu, a=self.o_parts, a_parts=kp_o, b=self.res_attn,
+                           gamma=lw.post_norm, eps=eps, res_out=self.resmid, epi=S.EPI_SILU_MUL,
+                           rowmap=S.ROWS_GATE_UP, out=self.mid, wait=o)
+            prev = prog.gemv(wd, h, i, kp=kp_down, ks=ks_down, a=self.mid, epi=S.EPI_PARTS, out=self.down_parts,
+                             wait=gu)
+        prog.gemv(self.t16_head, cfg.vocab_size, h, ks=ks_head, a=self.down_parts, a_parts=kp_down, b=self.resmid,
+                  gamma=w.final_norm, eps=eps, epi=S.EPI_ARGMAX, out=self.logits, key=self.key, wait=prev)
+        prog.finalize()
+        self.program = prog
+        self._io = prog.io(error=self.error, key=self.key, token_out=self.token, token_log=self.token_log,
+                           step=self.step_idx, pos=self.pos)
 
     # -- the kernel sequence of one step, as prepared ctypes calls (no allocation)
     def _build_calls(self):
@@ -247,10 +316,13 @@ class DecodeEngine:
         return calls
 
     def kernels_per_step(self) -> int:
-        return len(self._calls)
+        return 1 if self.mode == "step" else len(self._calls)
 
     def _enqueue(self):
         stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        if self.mode == "step":
+            self.program.launch(self._io, stream)
+            return
         for fn, name, args in self._calls:
             st = fn(*args, stream)
             if st != 0:
@@ -280,6 +352,13 @@ class DecodeEngine:
         self.step_idx.zero_()
         self.key.zero_()
         self.error.zero_()
+        if self.mode == "step":
+            self.program.reset_counters()
+            self.counters.zero_()
+
+    def oracle_order(self) -> dict | None:
+        """The oracle evaluation order this engine's kernels follow (None: per-kernel order)."""
+        return self.step_order if self.mode == "step" else None
 
     def step(self):
         """Enqueue one decode step on the current stream (graph replay when captured)."""

@@ -1,0 +1,195 @@
+"""Persistent decode step: T16 weight packing and stage programs for ``spark_step_run``.
+
+A decode step of the synthetic model is ONE cooperative kernel launch running a
+program of stages (include/spark_b200.h, ``SparkStage``).  Per layer:
+
+  qkv      GEMV, RMSNorm(a + b) prologue, RoPE + paged KV store epilogue
+  attn     split-KV attention over the paged cache, last split of a head combines
+  o_proj   GEMV, K split in ``kp_o`` parts -> fp32 parts
+  gate_up  GEMV, RMSNorm(sum(o parts) + res) prologue, SiLU * mul epilogue
+  down     GEMV, K split in ``kp_down`` parts -> fp32 parts (next layer's a)
+
+then the LM head (RMSNorm prologue, argmax epilogue).  The last CTA of the launch
+turns the argmax key into the next token and advances the position.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+
+from ._lib import SparkStage, SparkStepIO, call, lib
+
+STAGE_GEMV, STAGE_ATTN = 0, 1
+PRO_BF16, PRO_PARTS = 0, 1
+EPI_BF16, EPI_PARTS, EPI_ROPE_KV, EPI_SILU_MUL, EPI_ARGMAX = range(5)
+ROWS_PLAIN, ROWS_PAIR_HALF, ROWS_GATE_UP = range(3)
+
+PARTIAL_FLOATS = 5 * 1024 // 4  # per-CTA slice-sum buffer of the kernel
+MAX_SPLIT_TOKENS = 2048
+
+
+def _p(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def num_ctas() -> int:
+    return int(lib().spark_step_num_ctas())
+
+
+def ring_bytes() -> int:
+    return int(lib().spark_step_ring_bytes())
+
+
+def t16_bytes(n: int, k: int, kp: int) -> int:
+    return n * k * 9 // 16
+
+
+def q4_pack_t16(qs: torch.Tensor, d: torch.Tensor, kp: int = 1, rowmap: int = ROWS_PLAIN,
+                head_dim: int = 0) -> torch.Tensor:
+    """Re-lay Q4_0 planes (qs uint8 [n, k/2], d fp16-bits [n, k/32]) as T16 units."""
+    n, k = qs.shape[0], qs.shape[1] * 2
+    out = torch.empty(t16_bytes(n, k, kp), dtype=torch.uint8, device=qs.device)
+    call("spark_q4_pack_t16", _p(qs.contiguous()), _p(d.contiguous()), n, k, kp, rowmap, head_dim, _p(out), _stream())
+    return out
+
+
+def pick_ks(n: int, k: int, kp: int, want: int, ncta: int) -> int:
+    """Largest slice count <= want that divides the unit's 64-column tiles and fits the
+    kernel's slice-sum buffer."""
+    tiles = (k // kp) // 64
+    units = n // 16 * kp
+    nl = -(-units // ncta)
+    for ks in range(min(want, tiles), 0, -1):
+        if tiles % ks == 0 and nl * ks * 16 <= PARTIAL_FLOATS:
+            return ks
+    raise ValueError(f"no slice count fits n={n} k={k} kp={kp}")
+
+
+class StepProgram:
+    """An ordered list of stages, its device copy, and the launch state."""
+
+    def __init__(self, device, ncta: int | None = None):
+        self.device = torch.device(device)
+        self.ncta = ncta or num_ctas()
+        self.stages: list[SparkStage] = []
+        self.keep: list = []
+        self._units = 0
+        self.host = None
+        self.dev = None
+        self.counters = None
+
+    # -- stage builders (return the stage index)
+    def gemv(self, w: torch.Tensor, n: int, k: int, *, kp: int = 1, ks: int = 1, a=None, a_parts: int = 0,
+             embed=None, token=None, b=None, gamma=None, eps: float = 0.0, res_out=None, epi: int = EPI_BF16,
+             rowmap: int = ROWS_PLAIN, out=None, wait: int = -1, head_dim: int = 0, key=None, rope=None) -> int:
+        s = SparkStage()
+        s.kind, s.epi, s.rowmap = STAGE_GEMV, epi, rowmap
+        s.pro = PRO_PARTS if a_parts else PRO_BF16
+        s.n, s.k, s.kp, s.ks = n, k, kp, ks
+        s.units = n // 16 * kp
+        s.rot = self._units % self.ncta
+        self._units += s.units
+        s.wait = wait
+        s.norm = 1 if gamma is not None else 0
+        s.a_parts = a_parts
+        s.eps = eps
+        s.inv_k = float(torch.tensor(1.0 / k, dtype=torch.float32))
+        s.head_dim = head_dim
+        s.w, s.a, s.b, s.embed, s.token = _p(w), _p(a), _p(b), _p(embed), _p(token)
+        s.gamma, s.res_out, s.out, s.key = _p(gamma), _p(res_out), _p(out), _p(key)
+        if rope is not None:
+            s.cos_sin, s.pos, s.block_table = _p(rope["cos_sin"]), _p(rope["pos"]), _p(rope["block_table"])
+            s.k_cache, s.v_cache, s.q, s.kv_new = (_p(rope["k_cache"]), _p(rope["v_cache"]), _p(rope["q"]),
+                                                   _p(rope["kv_new"]))
+            s.block_size, s.nq, s.nkv = rope["block_size"], rope["nq"], rope["nkv"]
+        self.keep.extend([w, a, b, embed, token, gamma, res_out, out, key, rope])
+        self.stages.append(s)
+        return len(self.stages) - 1
+
+    def attention(self, *, q, k_cache, v_cache, kv_new, block_table, pos, splits: int, max_split_tokens: int,
+                  scale: float, part_o, part_lse, head_counters, attn_out, nq: int, nkv: int, head_dim: int,
+                  block_size: int, wait: int = -1) -> int:
+        s = SparkStage()
+        s.kind = STAGE_ATTN
+        s.wait = wait
+        s.nq, s.nkv, s.head_dim, s.block_size = nq, nkv, head_dim, block_size
+        s.splits, s.max_split_tokens, s.scale = splits, max_split_tokens, scale
+        s.q, s.k_cache, s.v_cache, s.kv_new = _p(q), _p(k_cache), _p(v_cache), _p(kv_new)
+        s.block_table, s.pos = _p(block_table), _p(pos)
+        s.part_o, s.part_lse, s.head_counters, s.attn_out = _p(part_o), _p(part_lse), _p(head_counters), _p(attn_out)
+        self.keep.extend([q, k_cache, v_cache, kv_new, block_table, pos, part_o, part_lse, head_counters, attn_out])
+        self.stages.append(s)
+        return len(self.stages) - 1
+
+    # -- device copy
+    def finalize(self) -> "StepProgram":
+        n = len(self.stages)
+        self.host = (SparkStage * n)(*self.stages)
+        raw = torch.frombuffer(bytearray(bytes(self.host)), dtype=torch.uint8)
+        self.dev = raw.to(self.device)
+        self.counters = torch.zeros(n + 2, dtype=torch.int32, device=self.device)
+        return self
+
+    def reset_counters(self) -> None:
+        self.counters.zero_()
+
+    def io(self, *, error=None, key=None, token_out=None, token_log=None, step=None, pos=None) -> SparkStepIO:
+        io = SparkStepIO()
+        io.counters, io.error, io.key = _p(self.counters), _p(error), _p(key)
+        io.token_out, io.token_log, io.step, io.pos = _p(token_out), _p(token_log), _p(step), _p(pos)
+        return io
+
+    def launch(self, io: SparkStepIO, stream=None) -> None:
+        if self.host is None:
+            self.finalize()
+        st = stream if stream is not None else _stream()
+        dev = _p(self.dev) if len(self.stages) > 1 else None
+        call("spark_step_run", ctypes.cast(self.host, ctypes.c_void_p), dev, len(self.stages),
+             ctypes.byref(io), st)
+
+
+def t16_gemv(x: torch.Tensor, w: torch.Tensor, n: int, k: int, kp: int = 1, ks: int = 1, parts: bool = False,
+             **kw) -> torch.Tensor:
+    """One T16 GEMV stage as its own launch (tests, kernel timing): bf16 out [n], or the
+    fp32 parts [kp, n] when ``parts``."""
+    dev = x.device
+    if parts:
+        out = torch.empty((kp, n), dtype=torch.float32, device=dev)
+        epi = EPI_PARTS
+    else:
+        out = torch.empty(n, dtype=torch.bfloat16, device=dev)
+        epi = EPI_BF16
+    prog = StepProgram(dev)
+    a_parts = kw.pop("a_parts", 0)
+    prog.gemv(w, n, k, kp=kp, ks=ks, a=x, a_parts=a_parts, epi=epi, out=out, **kw)
+    prog.finalize()
+    prog.launch(prog.io())
+    return out
+
+
+def default_order(cfg, ncta: int) -> dict:
+    """Slice / part counts of the decode program (the oracle's persistent-step order)."""
+    h, i, nq, D, v = cfg.hidden_size, cfg.intermediate_size, cfg.num_q_heads, cfg.head_dim, cfg.vocab_size
+    kp_o = 2 if (nq * D // 2) % 64 == 0 else 1
+    kp_down = 4 if (i // 4) % 64 == 0 else (2 if (i // 2) % 64 == 0 else 1)
+    qkv_n = (nq + 2 * cfg.num_kv_heads) * D
+    return {
+        "ks": (pick_ks(qkv_n, h, 1, 4, ncta), pick_ks(h, nq * D, kp_o, 4, ncta), pick_ks(2 * i, h, 1, 1, ncta),
+               pick_ks(h, i, kp_down, 2, ncta), pick_ks(v, h, 1, 1, ncta)),
+        "kp": (kp_o, kp_down),
+        "chunk_accs": 12,
+    }
+
+
+def attn_splits(cfg, ncta: int) -> int:
+    return max(1, ncta // cfg.num_kv_heads)
+
+
+def max_split_tokens(max_seq_len: int, splits: int) -> int:
+    return (math.ceil(max_seq_len / splits) + 15) // 16 * 16

@@ -18,19 +18,20 @@ def u16(t):
     return t.detach().contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
 
 
-def _run_pair(cfg, prompt_len, new_tokens, splits, max_seq, seed, oracle, use_graph=True):
+def _run_pair(cfg, prompt_len, new_tokens, splits, max_seq, seed, oracle, use_graph=True, mode="step"):
     import torch
     from spark_b200.model import DecodeEngine, SyntheticWeights
     w = SyntheticWeights(cfg, device="cuda", seed=seed)
-    eng = DecodeEngine(w, max_seq_len=max_seq, splits=splits, num_blocks=4 * ((max_seq + 127) // 128),
-                       use_graph=use_graph, seed=seed)
+    eng = DecodeEngine(w, max_seq_len=max_seq, splits=splits if mode == "kernels" else 0,
+                       num_blocks=4 * ((max_seq + 127) // 128), use_graph=use_graph, seed=seed, mode=mode)
+    splits = eng.splits
     rng = np.random.default_rng(seed)
     prompt = rng.integers(0, cfg.vocab_size, prompt_len).astype(np.int32)
     toks = eng.generate(torch.from_numpy(prompt), new_tokens)
     torch.cuda.synchronize()
     assert int(eng.error.item()) == 0
     # oracle: same weights, same block table, same token-by-token feeding
-    om = oracle.OracleModel(cfg, w.to_numpy(), num_blocks=eng.num_blocks, splits=splits)
+    om = oracle.OracleModel(cfg, w.to_numpy(), num_blocks=eng.num_blocks, splits=splits, order=eng.oracle_order())
     table = eng.block_table.cpu().numpy()
     pos = 0
     tok = None
@@ -49,29 +50,32 @@ def _run_pair(cfg, prompt_len, new_tokens, splits, max_seq, seed, oracle, use_gr
     return toks, ref, u16(eng.logits), logits, eng
 
 
-def test_tiny_model_greedy_64_steps(cuda, oracle):
+@pytest.mark.parametrize("mode", ["step", "kernels"])
+def test_tiny_model_greedy_64_steps(cuda, oracle, mode):
     from spark_b200.config import tiny_config
     cfg = tiny_config()
     toks, ref, lg, ref_lg, eng = _run_pair(cfg, prompt_len=24, new_tokens=65, splits=4, max_seq=256, seed=1,
-                                           oracle=oracle)
+                                           oracle=oracle, mode=mode)
     assert toks == ref
     assert np.array_equal(lg, ref_lg)
-    assert eng.kernels_per_step() == 5 * cfg.num_layers + 2
+    assert eng.kernels_per_step() == (1 if mode == "step" else 5 * cfg.num_layers + 2)
 
 
-def test_tiny_model_eager_matches_graph(cuda, oracle):
+@pytest.mark.parametrize("mode", ["step", "kernels"])
+def test_tiny_model_eager_matches_graph(cuda, oracle, mode):
     from spark_b200.config import tiny_config
     cfg = tiny_config(num_layers=3)
     toks, ref, _, _, _ = _run_pair(cfg, prompt_len=5, new_tokens=9, splits=2, max_seq=128, seed=2, oracle=oracle,
-                                   use_graph=False)
+                                   use_graph=False, mode=mode)
     assert toks == ref
 
 
 @pytest.mark.slow
-def test_full_size_model_steps(cuda, oracle):
+@pytest.mark.parametrize("mode", ["step", "kernels"])
+def test_full_size_model_steps(cuda, oracle, mode):
     from spark_b200.config import SparkConfig
     cfg = SparkConfig(max_position=4096)
     toks, ref, lg, ref_lg, _ = _run_pair(cfg, prompt_len=3, new_tokens=3, splits=16, max_seq=512, seed=3,
-                                         oracle=oracle)
+                                         oracle=oracle, mode=mode)
     assert toks == ref
     assert np.array_equal(lg, ref_lg)
