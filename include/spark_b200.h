@@ -235,7 +235,7 @@ int spark_read_device_error(int* value, int reset);
 
 typedef struct SparkStage {
   int32_t kind, pro, epi, rowmap;
-  int32_t n, k, kp, ks;         /* GEMV rows, columns, K parts, slices per part (integer order) */
+  int32_t n, k, kp, ks;         /* GEMV rows, columns, K parts, slices per part (<= 4) */
   int32_t units, rot, wait, norm; /* units = n/16*kp; rot = first CTA; wait = stage to await (-1) */
   int32_t a_parts, block_size, nq, nkv;
   int32_t head_dim, splits, max_split_tokens, reserved0;
@@ -258,18 +258,25 @@ typedef struct SparkStage {
   unsigned long long* key;    /* argmax key (zero before the stage) */
   float* part_o;              /* fp32 [splits][nq][head_dim] */
   float* part_lse;            /* fp32 [splits][nq] */
-  int32_t* head_counters;     /* int32 [nkv], zero; the kernel leaves them zero */
+  int32_t* head_counters;     /* int32 [nkv] of this stage alone, zero when io->counters was zeroed;
+                                 grows by `splits` per launch */
   void* attn_out;             /* bf16 [nq][head_dim] */
 } SparkStage;
 
 typedef struct SparkStepIO {
-  int32_t* counters;          /* int32 [num_stages + 2], zero before the first launch */
+  int32_t* counters;          /* int32 [num_stages + 3], zero before the first launch; the kernel keeps
+                                 the first num_stages + 2 zero between launches and counts launches in
+                                 the last (the attention stages' head counters follow that count) */
   int32_t* error;             /* int32 [1] status written on a timed-out wait (nullable) */
   unsigned long long* key;    /* after the last stage: token = argmax of key (nullable) */
   int32_t* token_out;
   int32_t* token_log;         /* token_log[*step] = token (nullable) */
   int32_t* step;              /* incremented (nullable) */
   int64_t* pos;               /* incremented (nullable) */
+  unsigned long long* trace;  /* optional uint64 [ctas][num_stages][8] globaltimer stamps (ns): consumer
+                                 wait start, work start, work end, producer's first copy of the stage,
+                                 then stage checkpoints (GEMV: tasks start, tasks end; attention:
+                                 scores, softmax, PV, partials written); for profiling, nullable */
 } SparkStepIO;
 
 /* Bytes of a matrix in the T16 layout: n * k * 9 / 16. */

@@ -634,9 +634,13 @@ static int check_stage(const SparkStage& s, int i, int ncta) {
       return SPARK_ERR_UNSUPPORTED_SHAPE;
     if (s.units != s.n / 16 * s.kp || s.rot < 0 || s.rot >= ncta) return SPARK_ERR_INVALID_ARG;
     if (9 * (s.k / s.kp) > step::kRingBytes) return SPARK_ERR_TOO_LARGE;
-    const int nl = (s.units + ncta - 1) / ncta;
-    if (nl * s.ks * 16 * 4 > step::kPartialBytes) return SPARK_ERR_TOO_LARGE;
-    if (72 * (s.k / 32) + (s.norm ? 4 * s.k : 0) > step::kScratchBytes) return SPARK_ERR_TOO_LARGE;
+    if (s.ks > step::kMaxSlices) return SPARK_ERR_UNSUPPORTED_SHAPE;
+    if (72 * (s.k / 32) + (s.norm ? 6 * s.k : 0) > step::kScratchBytes) return SPARK_ERR_TOO_LARGE;
+    if (s.norm && (reinterpret_cast<uintptr_t>(s.gamma) & 15)) return SPARK_ERR_ALIGNMENT;
+    if (s.k > step::kStageGroups * step::kConsumers * 8) return SPARK_ERR_TOO_LARGE;
+    if ((reinterpret_cast<uintptr_t>(s.a) | reinterpret_cast<uintptr_t>(s.b) | reinterpret_cast<uintptr_t>(s.embed) |
+         reinterpret_cast<uintptr_t>(s.gamma) | reinterpret_cast<uintptr_t>(s.res_out)) & 15)
+      return SPARK_ERR_ALIGNMENT;
     if (s.pro == SPARK_PRO_PARTS) {
       if (s.a_parts <= 0 || !s.a || s.embed) return SPARK_ERR_INVALID_ARG;
     } else if (s.pro != SPARK_PRO_BF16) {
@@ -662,7 +666,7 @@ static int check_stage(const SparkStage& s, int i, int ncta) {
         if (s.kp != 1 || s.rowmap != SPARK_ROWS_PAIR_HALF || !s.q || !s.k_cache || !s.v_cache || !s.kv_new ||
             !s.cos_sin || !s.pos || !s.block_table || s.block_size <= 0 || s.nq <= 0 || s.nkv <= 0)
           return SPARK_ERR_INVALID_ARG;
-        if (s.n != (s.nq + 2 * s.nkv) * s.head_dim) return SPARK_ERR_UNSUPPORTED_SHAPE;
+        if (s.n != (s.nq + 2 * s.nkv) * s.head_dim || s.head_dim > 128) return SPARK_ERR_UNSUPPORTED_SHAPE;
         break;
       default:
         return SPARK_ERR_INVALID_ARG;

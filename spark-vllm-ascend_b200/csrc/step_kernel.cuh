@@ -3,7 +3,7 @@
 //
 // A launch runs a program of stages (SparkStage, include/spark_b200.h): GEMV stages
 // over Q4_0 weights in the T16 layout, and split-KV attention stages.  Every CTA has
-// a producer warp and 12 consumer warps:
+// a producer warp and 11 consumer warps:
 //
 //  * the producer (one thread) walks the whole program ahead of the consumers and
 //    streams, with cp.async.bulk, every byte its CTA will read from HBM into a
@@ -33,16 +33,18 @@
 namespace spark {
 namespace step {
 
-constexpr int kWarps = 12;                 // consumer warps
-constexpr int kConsumers = kWarps * 32;    // 384
+constexpr int kWarps = 11;                 // consumer warps (12 warps per CTA keep 168 registers)
+constexpr int kConsumers = kWarps * 32;    // 352
 constexpr int kThreads = kConsumers + 32;  // + the producer warp
-constexpr int kDesc = 32;                  // ring descriptors (units in flight)
+constexpr int kDesc = 16;                  // ring descriptors (units in flight)
+constexpr int kMaxSlices = 4;              // GEMV slices per unit (per-slot slice sums)
+constexpr int kTraceSlots = 8;             // trace stamps per stage
 constexpr int kSmemBytes = 227 * 1024;
 constexpr int kScratchBytes = 32 * 1024;   // x staging | attention scores / reduction
-constexpr int kPartialBytes = 5 * 1024;    // per-slice row sums of a GEMV stage
+constexpr int kPartialBytes = kDesc * kMaxSlices * 16 * 4;  // slice sums per ring slot
 constexpr int kMiscBytes = 2048;
 constexpr int kRingBytes = kSmemBytes - kScratchBytes - kPartialBytes - kMiscBytes;
-constexpr int kMaxSplitTokens = kScratchBytes / 16;  // attention: 16 B per token
+constexpr int kMaxSplitTokens = 1344;  // attention: 24 B of scratch per token (scores + P)
 constexpr int kTileBytes = 576;                      // 16 rows x 64 k: 512 B nibbles + 64 B scales
 constexpr int kRunTokens = 64;                       // K / V tokens per bulk copy (at most)
 constexpr unsigned long long kWaitNs = 2000000000ull;
@@ -83,7 +85,7 @@ __device__ __forceinline__ bool mbar_wait_timed(uint32_t bar, uint32_t parity, v
 
 __device__ __forceinline__ void mma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                          uint32_t b1, int c1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};"
       : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0), "r"(c1), "r"(0), "r"(c1));
@@ -140,6 +142,8 @@ struct Smem {
   float* red;                 // [64] reductions
   unsigned long long* red64;  // [16]
   SparkStage* stage;          // consumers' copy of the current stage
+  long long* misc64;          // [4] per-stage values (position, cache row offset)
+  uint16_t* rope_cs;          // [128] cos | sin row of the position (RoPE stages)
 };
 
 __device__ __forceinline__ Smem carve(unsigned char* base) {
@@ -159,9 +163,11 @@ __device__ __forceinline__ Smem carve(unsigned char* base) {
   s.red = reinterpret_cast<float*>(s.flag + 4);
   s.red64 = reinterpret_cast<unsigned long long*>(s.red + 64);
   s.stage = reinterpret_cast<SparkStage*>(s.red64 + 16);
+  s.misc64 = reinterpret_cast<long long*>(s.stage + 1);
+  s.rope_cs = reinterpret_cast<uint16_t*>(s.misc64 + 4);
   return s;
 }
-// 256 + 256 + 128 + 128 + 128 + 128 + 16 + 16 + 256 + 128 + 256 = 1696 <= kMiscBytes
+// 256 + 256 + 128 + 128 + 128 + 128 + 16 + 16 + 256 + 128 + 256 + 32 + 256 = 1984 <= kMiscBytes
 static_assert(sizeof(SparkStage) == 256, "SparkStage layout");
 
 struct StepParams {
@@ -185,30 +191,33 @@ __device__ __forceinline__ void raise_abort(const StepParams& P, const Smem& s, 
 struct Producer {
   const StepParams& P;
   const Smem& s;
-  uint32_t seq = 0, tail = 0, head = 0;
+  uint32_t seq = 0, tail = 0, head = 0, tail_off = 0;
 
   __device__ Producer(const StepParams& p, const Smem& sm) : P(p), s(sm) {}
 
+  // The ring is a FIFO of byte ranges: outstanding units occupy [tail_off, head)
+  // circularly, tail_off being the start of the oldest unit not yet released.
   __device__ bool issue(const void* src, uint32_t bytes) {
     if (*s.abort_flag) return false;
     uint32_t a = head;
     if (a + bytes > (uint32_t)kRingBytes) a = 0;
     while (tail < seq) {
-      bool must = seq - tail >= (uint32_t)kDesc;
-      for (uint32_t u = tail; !must && u < seq; u++) {
-        const uint32_t b0 = s.prod_start[u % kDesc], b1 = s.prod_end[u % kDesc];
-        must = (a < b1) && (b0 < a + bytes);
+      if (seq - tail < (uint32_t)kDesc) {
+        const uint32_t t = tail_off;
+        const bool ok = t < head ? (a >= head || a + bytes <= t)    // free: [head, R) and [0, t)
+                                 : (t > head && a == head && a + bytes <= t);  // free: [head, t)
+        if (ok) break;
       }
-      if (!must) break;
       if (!mbar_wait_timed(smem_u32(s.empty + tail % kDesc), (tail / kDesc) & 1u, s.abort_flag)) {
         raise_abort(P, s, SPARK_ERR_LAUNCH);
         return false;
       }
       tail++;
+      tail_off = tail < seq ? s.prod_start[tail % kDesc] : head;
     }
     const uint32_t slot = seq % kDesc;
+    if (tail == seq) tail_off = a;
     s.prod_start[slot] = a;
-    s.prod_end[slot] = a + bytes;
     s.desc_off[slot] = a;
     head = a + bytes;
     const uint32_t bar = smem_u32(s.full + slot);
@@ -222,6 +231,7 @@ struct Producer {
     const int ncta = gridDim.x, cta = blockIdx.x;
     for (int i = 0; i < P.num_stages; i++) {
       const SparkStage& st = stage_at(P, i);
+      if (P.io.trace) P.io.trace[((size_t)cta * P.num_stages + i) * kTraceSlots + 3] = gtimer();
       if (st.kind == SPARK_STAGE_GEMV) {
         int u0;
         const int nl = local_units(st, cta, ncta, u0);
@@ -274,31 +284,46 @@ struct Producer {
 // Block b of x becomes X_j = rint(x_j * 2^S), S = 13 - e (e = exponent of the block
 // maximum), split into signed digits X = 256 h + l.  MMA B fragment of block b:
 // entry e in 0..7 (lane & 7): e < 4 -> column 0 (h) with k = 4e.., e >= 4 -> column 1
-// (l) with k = 4(e-4)..; .x holds k 0..15, .y holds k 16..31.  meta = (-8 sum X, sx).
-__device__ __forceinline__ void stage_block13(const float (&v)[32], uint2* xfrag, int2* xmeta, int b) {
+// (l) with k = 4(e-4)..; word 0 holds k 0..15, word 1 holds k 16..31.
+// meta = (-8 sum X, sx).  Four consecutive threads stage one block, 8 elements each.
+constexpr int kStageGroups = 4;  // 8-element groups per consumer thread (k <= 12288)
+
+__device__ __forceinline__ void lds_u32x4(uint32_t addr, uint4& v) {
+  asm("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+}
+__device__ __forceinline__ void lds_u32x2(uint32_t addr, uint2& v) {
+  asm("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+}
+
+__device__ __forceinline__ void unpack8(const uint4 u, float (&v)[8]) {
+  v[0] = bf_lo(u.x); v[1] = bf_hi(u.x); v[2] = bf_lo(u.y); v[3] = bf_hi(u.y);
+  v[4] = bf_lo(u.z); v[5] = bf_hi(u.z); v[6] = bf_lo(u.w); v[7] = bf_hi(u.w);
+}
+
+// stage the 8 elements of group g (block g / 4, elements 8 (g % 4) ..); the 4 lanes of a
+// block are consecutive lanes of one warp and all execute this (valid or not)
+__device__ __forceinline__ void stage_group(const float (&v)[8], bool valid, int g, uint32_t* xfrag32, int2* xmeta) {
   float M = 0.0f;
 #pragma unroll
-  for (int j = 0; j < 32; j++) M = fmaxf(M, fabsf(v[j]));
-  int X[32];
-  float sx = 1.0f;
-  int sum = 0;
-  if (M >= 7.888609052210118e-31f && M != __int_as_float(0x7f800000)) {
-    const int e = (int)((__float_as_uint(M) >> 23) & 0xffu) - 127;
-    const int S = 13 - e;
-    const float sc = __uint_as_float((uint32_t)(S + 127) << 23);
+  for (int j = 0; j < 8; j++) M = fmaxf(M, fabsf(v[j]));
+  M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 1));
+  M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 2));
+  const bool live = M >= 7.888609052210118e-31f && M != __int_as_float(0x7f800000);
+  const int e = (int)((__float_as_uint(M) >> 23) & 0xffu) - 127;
+  const int S = 13 - e;
+  const float sc = live ? __uint_as_float((uint32_t)(S + 127) << 23) : 0.0f;
+  int X[8], sum = 0;
 #pragma unroll
-    for (int j = 0; j < 32; j++) {
-      X[j] = __float2int_rn(__fmul_rn(v[j], sc));
-      sum += X[j];
-    }
-    sx = __uint_as_float((uint32_t)(127 - S) << 23);
-  } else {
-#pragma unroll
-    for (int j = 0; j < 32; j++) X[j] = 0;
+  for (int j = 0; j < 8; j++) {
+    X[j] = live ? __float2int_rn(__fmul_rn(v[j], sc)) : 0;
+    sum += X[j];
   }
-  uint32_t hw[8], lw[8];
+  sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+  sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+  if (!valid) return;
+  const int b = g >> 2, c = g & 3;
 #pragma unroll
-  for (int w = 0; w < 8; w++) {
+  for (int w = 0; w < 2; w++) {
     uint32_t hh = 0, ll = 0;
 #pragma unroll
     for (int t = 0; t < 4; t++) {
@@ -308,113 +333,202 @@ __device__ __forceinline__ void stage_block13(const float (&v)[32], uint2* xfrag
       hh |= (uint32_t)(h & 0xff) << (8 * t);
       ll |= (uint32_t)(l & 0xff) << (8 * t);
     }
-    hw[w] = hh;
-    lw[w] = ll;
+    const int word = 2 * c + w;  // k = 4 word .. 4 word + 3
+    xfrag32[(b * 8 + (word & 3)) * 2 + (word >> 2)] = hh;
+    xfrag32[(b * 8 + 4 + (word & 3)) * 2 + (word >> 2)] = ll;
   }
-#pragma unroll
-  for (int c = 0; c < 4; c++) {
-    xfrag[b * 8 + c] = make_uint2(hw[c], hw[4 + c]);
-    xfrag[b * 8 + 4 + c] = make_uint2(lw[c], lw[4 + c]);
-  }
-  xmeta[b] = make_int2(-8 * sum, __float_as_int(sx));
+  if (c == 0) xmeta[b] = make_int2(-8 * sum, __float_as_int(live ? __uint_as_float((uint32_t)(127 - S) << 23) : 1.0f));
 }
 
-// input element i of the stage's a operand (bf16 value as fp32)
-__device__ __forceinline__ float a_elem(const SparkStage& st, const uint16_t* arow, int i) {
-  if (st.pro == SPARK_PRO_PARTS) {
-    const float* p = static_cast<const float*>(st.a);
-    float v = __ldcg(p + i);
-    for (int q = 1; q < st.a_parts; q++) v = __fadd_rn(v, __ldcg(p + (size_t)q * st.k + i));
-    return bf2f(f2bf(v));
-  }
-  return bf2f(__ldcg(arow + i));
-}
-
-__device__ void stage_x(const SparkStage& st, const Smem& s, int tid) {
-  const int k = st.k, nb = k >> 5;
-  uint2* xfrag = reinterpret_cast<uint2*>(s.scratch);
+__device__ __noinline__ void stage_x(const SparkStage& st, const Smem& s, int tid, unsigned long long* tr) {
+  const int k = st.k, nb = k >> 5, ngrp = k >> 3;
+  uint32_t* xfrag32 = reinterpret_cast<uint32_t*>(s.scratch);
   int2* xmeta = reinterpret_cast<int2*>(s.scratch + 64 * nb);
-  float* slin = reinterpret_cast<float*>(s.scratch + 72 * nb);
+  float* sq = reinterpret_cast<float*>(s.scratch + 72 * nb);
   const uint16_t* arow = static_cast<const uint16_t*>(st.a);
   if (st.embed) arow = static_cast<const uint16_t*>(st.embed) + (size_t)__ldcg(st.token) * k;
-  if (!st.norm) {
-    for (int b = tid; b < nb; b += kConsumers) {
-      float v[32];
-#pragma unroll 8
-      for (int j = 0; j < 32; j++) v[j] = a_elem(st, arow, b * 32 + j);
-      stage_block13(v, xfrag, xmeta, b);
-    }
-    return;
-  }
+  const float* parts = static_cast<const float*>(st.a);
   const uint16_t* bb = static_cast<const uint16_t*>(st.b);
-  uint16_t* res = (blockIdx.x == 0) ? static_cast<uint16_t*>(st.res_out) : nullptr;
-  for (int i = tid; i < k; i += kConsumers) {
-    float v = a_elem(st, arow, i);
-    if (bb) v = __fadd_rn(v, bf2f(__ldcg(bb + i)));
-    slin[i] = v;
-    if (res) res[i] = f2bf(v);
+  const uint16_t* gm = reinterpret_cast<const uint16_t*>(s.scratch + 72 * nb + 4 * k);  // prefetched gamma
+  float v[kStageGroups][8];
+  uint4 gv[kStageGroups];
+  // all loads first: one L2 round trip
+#pragma unroll
+  for (int r = 0; r < kStageGroups; r++) {
+    const int g = tid + r * kConsumers;
+    if (g < ngrp) {
+      if (st.pro == SPARK_PRO_PARTS) {
+        float4 p0 = __ldcg(reinterpret_cast<const float4*>(parts + 8 * g));
+        float4 p1 = __ldcg(reinterpret_cast<const float4*>(parts + 8 * g + 4));
+        for (int q = 1; q < st.a_parts; q++) {
+          const float4 q0 = __ldcg(reinterpret_cast<const float4*>(parts + (size_t)q * k + 8 * g));
+          const float4 q1 = __ldcg(reinterpret_cast<const float4*>(parts + (size_t)q * k + 8 * g + 4));
+          p0 = make_float4(__fadd_rn(p0.x, q0.x), __fadd_rn(p0.y, q0.y), __fadd_rn(p0.z, q0.z), __fadd_rn(p0.w, q0.w));
+          p1 = make_float4(__fadd_rn(p1.x, q1.x), __fadd_rn(p1.y, q1.y), __fadd_rn(p1.z, q1.z), __fadd_rn(p1.w, q1.w));
+        }
+        const float t8[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+#pragma unroll
+        for (int j = 0; j < 8; j++) v[r][j] = bf2f(f2bf(t8[j]));
+      } else {
+        unpack8(__ldcg(reinterpret_cast<const uint4*>(arow + 8 * g)), v[r]);
+      }
+      if (st.norm) {
+        if (bb) {
+          float w8[8];
+          unpack8(__ldcg(reinterpret_cast<const uint4*>(bb + 8 * g)), w8);
+#pragma unroll
+          for (int j = 0; j < 8; j++) v[r][j] = __fadd_rn(v[r][j], w8[j]);
+        }
+        gv[r] = *reinterpret_cast<const uint4*>(gm + 8 * g);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; j++) v[r][j] = 0.0f;
+    }
   }
-  consumer_bar();
-  if (tid < 32) {
-    float acc = 0.0f;
-    for (int i = tid; i < k; i += 32) acc = __fadd_rn(acc, __fmul_rn(slin[i], slin[i]));
-    acc = butterfly_sum<32>(acc);
-    if (tid == 0) s.red[0] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(acc, st.inv_k), st.eps)));
+  if (tr) tr[6] = gtimer();
+  if (st.norm) {
+    uint16_t* res = (blockIdx.x == 0) ? static_cast<uint16_t*>(st.res_out) : nullptr;
+#pragma unroll
+    for (int r = 0; r < kStageGroups; r++) {
+      const int g = tid + r * kConsumers;
+      if (g < ngrp) {
+#pragma unroll
+        for (int j = 0; j < 8; j++) sq[8 * g + j] = __fmul_rn(v[r][j], v[r][j]);
+        if (res) {
+          uint4 o;
+          o.x = (uint32_t)f2bf(v[r][0]) | ((uint32_t)f2bf(v[r][1]) << 16);
+          o.y = (uint32_t)f2bf(v[r][2]) | ((uint32_t)f2bf(v[r][3]) << 16);
+          o.z = (uint32_t)f2bf(v[r][4]) | ((uint32_t)f2bf(v[r][5]) << 16);
+          o.w = (uint32_t)f2bf(v[r][6]) | ((uint32_t)f2bf(v[r][7]) << 16);
+          *reinterpret_cast<uint4*>(res + 8 * g) = o;
+        }
+      }
+    }
+    consumer_bar();
+    if (tid < 32) {  // canonical order: lane l sums s_i^2, i = l mod 32, ascending
+      float acc = 0.0f;
+      int i = tid;
+      for (; i + 15 * 32 < k; i += 16 * 32) {  // 16 loads in flight, then the ordered adds
+        float q16[16];
+#pragma unroll
+        for (int q = 0; q < 16; q++) q16[q] = sq[i + 32 * q];
+#pragma unroll
+        for (int q = 0; q < 16; q++) acc = __fadd_rn(acc, q16[q]);
+      }
+      for (; i < k; i += 32) acc = __fadd_rn(acc, sq[i]);
+      acc = butterfly_sum<32>(acc);
+      if (tid == 0) s.red[0] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(acc, st.inv_k), st.eps)));
+    }
+    consumer_bar();
+    if (tr) tr[7] = gtimer();
+    const float inv = s.red[0];
+#pragma unroll
+    for (int r = 0; r < kStageGroups; r++) {
+      float g8[8];
+      unpack8(gv[r], g8);
+#pragma unroll
+      for (int j = 0; j < 8; j++) v[r][j] = bf2f(f2bf(__fmul_rn(__fmul_rn(v[r][j], inv), g8[j])));
+    }
   }
-  consumer_bar();
-  const float inv = s.red[0];
-  const uint16_t* gm = static_cast<const uint16_t*>(st.gamma);
-  for (int b = tid; b < nb; b += kConsumers) {
-    float v[32];
-#pragma unroll 8
-    for (int j = 0; j < 32; j++) v[j] = bf2f(f2bf(__fmul_rn(__fmul_rn(slin[b * 32 + j], inv), bf2f(gm[b * 32 + j]))));
-    stage_block13(v, xfrag, xmeta, b);
+#pragma unroll
+  for (int r = 0; r < kStageGroups; r++) {
+    const int g = tid + r * kConsumers;
+    if (r * kConsumers < ngrp) stage_group(v[r], g < ngrp, g, xfrag32, xmeta);
   }
 }
 
 // ------------------------------------------------------------------ consumers: GEMV
-// one (unit, slice) task: lanes 4g hold the slice sums of positions g and g + 8
+// one (unit, slice) task: lanes 4g hold the slice sums of positions g and g + 8 as a
+// packed pair.  Tiles are processed 4 at a time (8 blocks: all shared-memory loads,
+// then the 8 MMAs, then the fma chain in block order), then one at a time.
+__device__ __forceinline__ unsigned long long f2pack(float lo, float hi) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2unpack(unsigned long long v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ unsigned long long fmul2(unsigned long long a, unsigned long long b) {
+  unsigned long long d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ unsigned long long ffma2(unsigned long long a, unsigned long long b, unsigned long long c) {
+  unsigned long long d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
+template <int NT>
+__device__ __forceinline__ void gemv_tiles(uint32_t& a_adr, uint32_t& d_adr, uint32_t& b_adr, uint32_t& m_adr,
+                                           unsigned long long& acc) {
+  const uint32_t m = 0x0f0f0f0fu;
+  uint4 A[NT];
+  uint2 Dd[NT], B[2 * NT], Mt[2 * NT];
+#pragma unroll
+  for (int j = 0; j < NT; j++) {
+    lds_u32x4(a_adr + j * kTileBytes, A[j]);
+    lds_u32x2(d_adr + j * kTileBytes, Dd[j]);
+  }
+#pragma unroll
+  for (int j = 0; j < 2 * NT; j++) {
+    lds_u32x2(b_adr + j * 64, B[j]);
+    lds_u32x2(m_adr + j * 8, Mt[j]);
+  }
+  int Dm[2 * NT][4];
+#pragma unroll
+  for (int j = 0; j < NT; j++) {
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      const uint32_t wg = h ? A[j].z : A[j].x, wg8 = h ? A[j].w : A[j].y;
+      mma_u8s8(Dm[2 * j + h], wg & m, wg8 & m, (wg >> 4) & m, (wg8 >> 4) & m, B[2 * j + h].x, B[2 * j + h].y,
+               (int)Mt[2 * j + h].x);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < NT; j++) {
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      const int* d = Dm[2 * j + h];
+      const uint32_t hv = h ? Dd[j].y : Dd[j].x;
+      const float sx = __uint_as_float(Mt[2 * j + h].y);
+      const unsigned long long sc =
+          fmul2(f2pack(h2f((uint16_t)(hv & 0xffffu)), h2f((uint16_t)(hv >> 16))), f2pack(sx, sx));
+      acc = ffma2(sc, f2pack((float)(d[0] * 256 + d[1]), (float)(d[2] * 256 + d[3])), acc);
+    }
+  }
+  a_adr += NT * kTileBytes;
+  d_adr += NT * kTileBytes;
+  b_adr += NT * 128;
+  m_adr += NT * 16;
+}
+
 __device__ __forceinline__ void gemv_task(const SparkStage& st, const Smem& s, uint32_t ubase, int kpi, int sl,
                                           int lane, float& acc0, float& acc1) {
   const int Kp = st.k / st.kp, tiles = Kp >> 6, tps = tiles / st.ks;
-  const uint2* xfrag = reinterpret_cast<const uint2*>(s.scratch);
-  const int2* xmeta = reinterpret_cast<const int2*>(s.scratch + 64 * (st.k >> 5));
-  const int gb0 = kpi * (Kp >> 5);
-  const uint32_t m = 0x0f0f0f0fu;
-  acc0 = 0.0f;
-  acc1 = 0.0f;
-  const int t_end = (sl + 1) * tps;
-#pragma unroll 2
-  for (int t = sl * tps; t < t_end; t++) {
-    const uint32_t tb = ubase + (uint32_t)t * kTileBytes;
-    uint4 w;
-    uint2 dd;
-    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(w.x), "=r"(w.y), "=r"(w.z), "=r"(w.w)
-                 : "r"(tb + lane * 16));
-    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(dd.x), "=r"(dd.y) : "r"(tb + 512 + (lane >> 2) * 8));
-#pragma unroll
-    for (int half = 0; half < 2; half++) {
-      const int gb = gb0 + 2 * t + half;
-      const uint2 bx = xfrag[gb * 8 + (lane & 7)];
-      const int2 meta = xmeta[gb];
-      const uint32_t wg = half ? w.z : w.x, wg8 = half ? w.w : w.y;
-      int d[4];
-      mma_u8s8(d, wg & m, wg8 & m, (wg >> 4) & m, (wg8 >> 4) & m, bx.x, bx.y, meta.x);
-      const int p0 = d[0] * 256 + d[1], p1 = d[2] * 256 + d[3];
-      const uint32_t hv = half ? dd.y : dd.x;
-      const float sx = __int_as_float(meta.y);
-      acc0 = __fmaf_rn(__fmul_rn(h2f((uint16_t)(hv & 0xffffu)), sx), (float)p0, acc0);
-      acc1 = __fmaf_rn(__fmul_rn(h2f((uint16_t)(hv >> 16)), sx), (float)p1, acc1);
-    }
-  }
+  const uint32_t xf = smem_u32(s.scratch), xm = xf + 64 * (st.k >> 5);
+  const int t0 = sl * tps;
+  const int gb = kpi * (Kp >> 5) + 2 * t0;  // first block of the slice
+  // per-lane addresses: A at lane * 16 of each tile, scales at 512 + (lane / 4) * 8,
+  // B fragment entry lane & 7 of each block, block meta
+  uint32_t a_adr = ubase + (uint32_t)t0 * kTileBytes + lane * 16;
+  uint32_t d_adr = ubase + (uint32_t)t0 * kTileBytes + 512 + (lane >> 2) * 8;
+  uint32_t b_adr = xf + (uint32_t)(gb * 8 + (lane & 7)) * 8;
+  uint32_t m_adr = xm + (uint32_t)gb * 8;
+  unsigned long long acc = 0ull;  // (0.0f, 0.0f)
+  int n = tps;
+  for (; n >= 4; n -= 4) gemv_tiles<4>(a_adr, d_adr, b_adr, m_adr, acc);
+  for (; n > 0; n--) gemv_tiles<1>(a_adr, d_adr, b_adr, m_adr, acc);
+  f2unpack(acc, acc0, acc1);
 }
 
 __device__ __forceinline__ uint16_t bf16r(float v) { return f2bf(v); }
 
 // epilogue of one row pair (positions g and g + 8 of unit u)
-__device__ __forceinline__ void gemv_epilogue(const SparkStage& st, int u, int g, float v0, float v1,
-                                              unsigned long long& best) {
+__device__ __forceinline__ void gemv_epilogue(const SparkStage& st, const long long* misc64, const uint16_t* rope_cs,
+                                              int u, int g, float v0, float v1, unsigned long long& best) {
   const int rg = u / st.kp, kpi = u - rg * st.kp;
   const int r0 = t16_row(st.rowmap, rg, g, st.n, st.head_dim);
   const int r1 = t16_row(st.rowmap, rg, g + 8, st.n, st.head_dim);
@@ -451,11 +565,10 @@ __device__ __forceinline__ void gemv_epilogue(const SparkStage& st, int u, int g
     default: {  // SPARK_EPI_ROPE_KV
       const int D = st.head_dim, half = D >> 1;
       const int hd = r0 / D, i = r0 - hd * D;
-      const int64_t pos = __ldcg(st.pos);
+      const int64_t pos = misc64[0];
       float a = bf2f(f2bf(v0)), b = bf2f(f2bf(v1));
       if (hd < st.nq + st.nkv) {
-        const uint16_t* cs = static_cast<const uint16_t*>(st.cos_sin) + (size_t)pos * D;
-        const float c = bf2f(cs[i]), sn = bf2f(cs[i + half]);
+        const float c = bf2f(rope_cs[i]), sn = bf2f(rope_cs[i + half]);
         const float u2 = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, sn));
         const float w2 = __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, sn));
         a = u2;
@@ -469,10 +582,8 @@ __device__ __forceinline__ void gemv_epilogue(const SparkStage& st, int u, int g
       } else {
         const int isv = hd >= st.nq + st.nkv;
         const int hk = hd - st.nq - isv * st.nkv;
-        const int64_t blk = pos / st.block_size, off = pos - blk * st.block_size;
-        const int64_t slot_blk = st.block_table[blk];
         uint16_t* cache = static_cast<uint16_t*>(isv ? st.v_cache : st.k_cache);
-        uint16_t* dst = cache + ((slot_blk * st.nkv + hk) * st.block_size + off) * D;
+        uint16_t* dst = cache + misc64[1] + (int64_t)hk * st.block_size * D;
         dst[i] = ua;
         dst[i + half] = ub;
         uint16_t* kn = static_cast<uint16_t*>(st.kv_new) + ((size_t)isv * st.nkv + hk) * D;
@@ -500,12 +611,19 @@ __device__ __forceinline__ void finish_task(const Smem& s, uint32_t seq, int tas
   }
 }
 
-__device__ bool gemv_stage(const StepParams& P, const SparkStage& st, const Smem& s, uint32_t& seq_base, int tid) {
+__device__ __noinline__ bool gemv_stage(const StepParams& P, const SparkStage& st, const Smem& s, uint32_t& seq_base, int tid) {
   const int ncta = gridDim.x, cta = blockIdx.x, warp = tid >> 5, lane = tid & 31;
   int u0;
   const int nl = local_units(st, cta, ncta, u0);
-  if (nl > 0 || (cta == 0 && st.res_out)) stage_x(st, s, tid);
+  if (nl > 0 || (cta == 0 && st.res_out))
+    stage_x(st, s, tid,
+            (tid == 0 && P.io.trace) ? P.io.trace + ((size_t)cta * P.num_stages + s.flag[2]) * kTraceSlots : nullptr);
   consumer_bar();
+  unsigned long long* tr = (tid == 0 && P.io.trace)
+                               ? P.io.trace + ((size_t)cta * P.num_stages + s.flag[2]) * kTraceSlots
+                               : nullptr;
+  if (tr) tr[4] = gtimer();
+  unsigned long long best = 0ull;
   const int ks = st.ks;
   for (int t = warp; t < nl * ks; t += kWarps) {
     const int j = t / ks, sl = t - j * ks;
@@ -515,26 +633,39 @@ __device__ bool gemv_stage(const StepParams& P, const SparkStage& st, const Smem
       continue;
     }
     const int u = u0 + j * ncta;
+    const uint32_t slot = seq % kDesc;
     float acc0, acc1;
-    gemv_task(st, s, smem_u32(s.ring) + s.desc_off[seq % kDesc], u % st.kp, sl, lane, acc0, acc1);
+    gemv_task(st, s, smem_u32(s.ring) + s.desc_off[slot], u % st.kp, sl, lane, acc0, acc1);
+    float* pr = s.partial + slot * kMaxSlices * 16;
     if ((lane & 3) == 0) {
-      s.partial[(j * ks + sl) * 16 + (lane >> 2)] = acc0;
-      s.partial[(j * ks + sl) * 16 + (lane >> 2) + 8] = acc1;
+      pr[sl * 16 + (lane >> 2)] = acc0;
+      pr[sl * 16 + (lane >> 2) + 8] = acc1;
     }
-    finish_task(s, seq, ks, lane);
-  }
-  consumer_bar();
-  unsigned long long best = 0ull;
-  for (int f = tid; f < nl * 8; f += kConsumers) {
-    const int j = f >> 3, g = f & 7;
-    const float* pr = s.partial + j * ks * 16;
-    float v0 = pr[g], v1 = pr[g + 8];
-    for (int q = 1; q < ks; q++) {
-      v0 = __fadd_rn(v0, pr[q * 16 + g]);
-      v1 = __fadd_rn(v1, pr[q * 16 + g + 8]);
+    // the task that completes the unit sums its slices, runs the epilogue and frees the slot
+    __syncwarp();
+    int last = 0;
+    if (lane == 0) {
+      __threadfence_block();
+      last = atomicAdd(s.done + slot, 1) == ks - 1;
     }
-    gemv_epilogue(st, u0 + j * ncta, g, v0, v1, best);
+    if (__shfl_sync(0xffffffffu, last, 0)) {
+      __threadfence_block();
+      if (lane < 8) {
+        float v0 = pr[lane], v1 = pr[lane + 8];
+        for (int q = 1; q < ks; q++) {
+          v0 = __fadd_rn(v0, pr[q * 16 + lane]);
+          v1 = __fadd_rn(v1, pr[q * 16 + lane + 8]);
+        }
+        gemv_epilogue(st, s.misc64, s.rope_cs, u, lane, v0, v1, best);
+      }
+      __syncwarp();
+      if (lane == 0) {
+        s.done[slot] = 0;
+        mbar_arrive(smem_u32(s.empty + slot));
+      }
+    }
   }
+  if (tr) tr[5] = gtimer();
   if (st.epi == SPARK_EPI_ARGMAX) {
 #pragma unroll
     for (int off = 16; off >= 1; off /= 2) {
@@ -556,17 +687,23 @@ __device__ bool gemv_stage(const StepParams& P, const SparkStage& st, const Smem
 // ------------------------------------------------------------------ consumers: attention
 // Task (kv head g, split j): tokens [t0, t1) of the context pos + 1, T = split_len.
 // Scores: 8 lanes per token (lane jj owns dims 8jj..8jj+7, 64+8jj..64+8jj+7; even /
-// odd positions in two fma chains, butterfly 4,2,1); rec[i] = 4 scores (fp32).  Then
-// max, p = exp(s - m) in place, l per head in the 32-lane order, P = bf16(p) in place.
-// PV: 16-token chunk c is summed by warp c % 12 (lane owns dims 4 lane .. +3 of all 4
-// heads); the 12 warp sums are added in warp order.  The last split of a head to
-// finish combines all splits of its 4 q heads into attn_out.
-__device__ bool attn_stage(const StepParams& P, const SparkStage& st, const Smem& s, uint32_t& seq_base, int tid) {
+// odd positions in two fma chains, butterfly 4,2,1); sc[i] = the 4 heads' scores, each
+// warp keeping the running maximum of its tokens.  Warp h < 4 then computes for head h
+// p_i = exp(s_i - m), lane l summing i = l mod 32 in ascending order (butterfly 16..1
+// gives l), and P_i = bf16(p_i).  PV: 16-token chunk c is summed by warp c % 11 (lane
+// owns dims 4 lane .. +3 of the 4 heads); the 11 warp sums are added in warp order.
+// Each split publishes O / l and lse; once every split of head g has published (the
+// head's counter grows by `splits` each launch), split j combines outputs j, j + S,
+// ... of the head group's 4 x 128 in the oracle's combine order.
+constexpr int kMergeRegs = 32;  // splits combined from registers (more: a loop)
+
+__device__ __noinline__ bool attn_stage(const StepParams& P, const SparkStage& st, const Smem& s, uint32_t& seq_base,
+                                        int tid) {
   const int warp = tid >> 5, lane = tid & 31;
   int g, j;
   if (!attn_task(st, blockIdx.x, g, j)) return true;
   const int D = 128, nq = st.nq, S = st.splits;
-  const int64_t pos = __ldcg(st.pos), len = pos + 1;
+  const int64_t pos = s.misc64[0], len = pos + 1;
   const int T = split_len(len, S);
   if (T > kMaxSplitTokens) {
     if (tid == 0) raise_abort(P, s, SPARK_ERR_TOO_LARGE);
@@ -577,7 +714,11 @@ __device__ bool attn_stage(const StepParams& P, const SparkStage& st, const Smem
   float* part_o = st.part_o;
   float* part_lse = st.part_lse;
   const uint16_t* kv_new = static_cast<const uint16_t*>(st.kv_new);
-  float4* rec = reinterpret_cast<float4*>(s.scratch);
+  unsigned long long* tr = (tid == 0 && P.io.trace)
+                               ? P.io.trace + ((size_t)blockIdx.x * P.num_stages + s.flag[2]) * kTraceSlots
+                               : nullptr;
+  float4* rec = reinterpret_cast<float4*>(s.scratch);                  // [T] scores (fp32 x 4 heads)
+  uint16_t* pbf = reinterpret_cast<uint16_t*>(s.scratch + 16 * T);     // [T][4] bf16 P
   if (n == 0) {
     for (int o = tid; o < 4 * D; o += kConsumers) part_o[((size_t)j * nq + 4 * g) * D + o] = 0.0f;
     if (tid < 4) part_lse[(size_t)j * nq + 4 * g + tid] = __int_as_float(0xff800000);
@@ -586,14 +727,20 @@ __device__ bool attn_stage(const StepParams& P, const SparkStage& st, const Smem
     const int nruns = (int)((t1 - 1) / kRunTokens - w0 + 1);
     const int nch = (n + 15) >> 4;
     const int jj = lane & 7, grp = lane >> 3;
-    // q: 4 heads x 16 dims of this lane
     float qf[4][16];
     {
       const uint16_t* q = static_cast<const uint16_t*>(st.q) + (size_t)4 * g * D;
 #pragma unroll
-      for (int h = 0; h < 4; h++)
+      for (int h = 0; h < 4; h++) {
+        float lo[8], hi[8];
+        unpack8(__ldcg(reinterpret_cast<const uint4*>(q + h * D + 8 * jj)), lo);
+        unpack8(__ldcg(reinterpret_cast<const uint4*>(q + h * D + 64 + 8 * jj)), hi);
 #pragma unroll
-        for (int m = 0; m < 16; m++) qf[h][m] = bf2f(__ldcg(q + h * D + (m < 8 ? 8 * jj + m : 64 + 8 * jj + m - 8)));
+        for (int m = 0; m < 8; m++) {
+          qf[h][m] = lo[m];
+          qf[h][8 + m] = hi[m];
+        }
+      }
     }
     auto run_of = [&](int64_t ts, int64_t& rs, int64_t& re) {
       const int64_t r = ts / kRunTokens - w0;
@@ -601,7 +748,9 @@ __device__ bool attn_stage(const StepParams& P, const SparkStage& st, const Smem
       re = (w0 + r + 1) * kRunTokens < t1 ? (w0 + r + 1) * kRunTokens : t1;
       return (int)r;
     };
-    // ---- scores
+    // ---- scores, with each warp's running maximum
+    float mx[4] = {__int_as_float(0xff800000), __int_as_float(0xff800000), __int_as_float(0xff800000),
+                   __int_as_float(0xff800000)};
     for (int c = warp; c < nch; c += kWarps) {
       const int64_t ts = t0 + 16 * c;
       int64_t rs, re;
@@ -618,8 +767,7 @@ __device__ bool attn_stage(const StepParams& P, const SparkStage& st, const Smem
         const bool valid = i < n;
         uint4 k0 = make_uint4(0, 0, 0, 0), k1 = k0;
         if (valid) {
-          const int64_t t = t0 + i;
-          if (t == pos) {
+          if (t0 + i == pos) {
             const uint16_t* kr = kv_new + (size_t)g * D;
             k0 = __ldcg(reinterpret_cast<const uint4*>(kr + 8 * jj));
             k1 = __ldcg(reinterpret_cast<const uint4*>(kr + 64 + 8 * jj));
@@ -644,35 +792,24 @@ __device__ bool attn_stage(const StepParams& P, const SparkStage& st, const Smem
           v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 2));
           v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 1));
           sc[h] = __fmul_rn(v, st.scale);
+          if (valid) mx[h] = sc[h] > mx[h] ? sc[h] : mx[h];
         }
         if (valid && jj == 0) rec[i] = make_float4(sc[0], sc[1], sc[2], sc[3]);
       }
       finish_task(s, seq, (int)((re - rs + 15) >> 4), lane);
     }
-    consumer_bar();
-    // ---- max (exact in any order)
-    {
-      float m4[4] = {__int_as_float(0xff800000), __int_as_float(0xff800000), __int_as_float(0xff800000),
-                     __int_as_float(0xff800000)};
-      for (int i = tid; i < n; i += kConsumers) {
-        const float4 r4 = rec[i];
-        m4[0] = r4.x > m4[0] ? r4.x : m4[0];
-        m4[1] = r4.y > m4[1] ? r4.y : m4[1];
-        m4[2] = r4.z > m4[2] ? r4.z : m4[2];
-        m4[3] = r4.w > m4[3] ? r4.w : m4[3];
-      }
 #pragma unroll
-      for (int h = 0; h < 4; h++) {
-        float v = m4[h];
+    for (int h = 0; h < 4; h++) {
+      float v = mx[h];
 #pragma unroll
-        for (int off = 16; off >= 1; off /= 2) {
-          const float o = __shfl_xor_sync(0xffffffffu, v, off);
-          v = o > v ? o : v;
-        }
-        if (lane == 0) s.red[warp * 4 + h] = v;
+      for (int off = 16; off >= 1; off /= 2) {
+        const float o = __shfl_xor_sync(0xffffffffu, v, off);
+        v = o > v ? o : v;
       }
+      if (lane == 0) s.red[warp * 4 + h] = v;
     }
     consumer_bar();
+    if (tr) tr[4] = gtimer();
     float mh[4];
 #pragma unroll
     for (int h = 0; h < 4; h++) {
@@ -680,28 +817,21 @@ __device__ bool attn_stage(const StepParams& P, const SparkStage& st, const Smem
       for (int w = 1; w < kWarps; w++) v = s.red[w * 4 + h] > v ? s.red[w * 4 + h] : v;
       mh[h] = v;
     }
-    for (int i = tid; i < n; i += kConsumers) {
-      const float4 r4 = rec[i];
-      rec[i] = make_float4(spark_exp(__fsub_rn(r4.x, mh[0])), spark_exp(__fsub_rn(r4.y, mh[1])),
-                           spark_exp(__fsub_rn(r4.z, mh[2])), spark_exp(__fsub_rn(r4.w, mh[3])));
-    }
-    consumer_bar();
+    // ---- p = exp(s - m), l (32-lane order), P = bf16(p): one warp per head
     if (warp < 4) {
-      const float* pf = reinterpret_cast<const float*>(rec);
+      const int h = warp;
+      const float* sf = reinterpret_cast<const float*>(rec);
       float acc = 0.0f;
-      for (int i = lane; i < n; i += 32) acc = __fadd_rn(acc, pf[4 * i + warp]);
+      for (int i = lane; i < n; i += 32) {
+        const float p = spark_exp(__fsub_rn(sf[4 * i + h], mh[h]));
+        acc = __fadd_rn(acc, p);
+        pbf[4 * i + h] = f2bf(p);
+      }
       acc = butterfly_sum<32>(acc);
-      if (lane == 0) s.red[48 + warp] = acc;
+      if (lane == 0) s.red[48 + h] = acc;
     }
     consumer_bar();
-    for (int i = tid; i < n; i += kConsumers) {
-      const float4 r4 = rec[i];
-      uint2 pb;
-      pb.x = (uint32_t)f2bf(r4.x) | ((uint32_t)f2bf(r4.y) << 16);
-      pb.y = (uint32_t)f2bf(r4.z) | ((uint32_t)f2bf(r4.w) << 16);
-      *reinterpret_cast<uint2*>(rec + i) = pb;
-    }
-    consumer_bar();
+    if (tr) tr[5] = gtimer();
     // ---- PV
     float acc[4][4];
 #pragma unroll
@@ -721,8 +851,8 @@ __device__ bool attn_stage(const StepParams& P, const SparkStage& st, const Smem
       const int cnt = n - 16 * c < 16 ? n - 16 * c : 16;
       for (int tt = 0; tt < cnt; tt++) {
         const int i = 16 * c + tt;
-        const uint2 pb = *reinterpret_cast<const uint2*>(rec + i);
-        const float p4[4] = {bf_lo(pb.x), bf_hi(pb.x), bf_lo(pb.y), bf_hi(pb.y)};
+        const uint2 pv = *reinterpret_cast<const uint2*>(pbf + 4 * i);
+        const float p4[4] = {bf_lo(pv.x), bf_hi(pv.x), bf_lo(pv.y), bf_hi(pv.y)};
         uint2 vv;
         if (t0 + i == pos) {
           vv = __ldcg(reinterpret_cast<const uint2*>(kv_new + ((size_t)st.nkv + g) * D + 4 * lane));
@@ -737,8 +867,8 @@ __device__ bool attn_stage(const StepParams& P, const SparkStage& st, const Smem
       }
       finish_task(s, seq, (int)((re - rs + 15) >> 4), lane);
     }
-    const float lh = s.red[48 + (tid & 3)];  // read before the scratch is reused
     consumer_bar();
+    if (tr) tr[6] = gtimer();
     float* red_o = reinterpret_cast<float*>(s.scratch);
 #pragma unroll
     for (int h = 0; h < 4; h++)
@@ -751,50 +881,83 @@ __device__ bool attn_stage(const StepParams& P, const SparkStage& st, const Smem
       for (int w = 1; w < kWarps; w++) v = __fadd_rn(v, red_o[(w * 4 + h) * D + d]);
       part_o[((size_t)j * nq + 4 * g + h) * D + d] = __fdiv_rn(v, s.red[48 + h]);
     }
-    if (tid < 4) part_lse[(size_t)j * nq + 4 * g + tid] = __fadd_rn(spark_log(lh), mh[tid]);
+    if (tid < 4) part_lse[(size_t)j * nq + 4 * g + tid] = __fadd_rn(spark_log(s.red[48 + tid]), mh[tid]);
     seq_base += 2 * nruns;
   }
-  // ---- the last split of head g combines
+  // ---- publish this split, wait for the head's other splits, combine this split's slice
   consumer_bar();
   if (tid == 0) {
-    __threadfence();
-    s.flag[0] = atomicAdd(st.head_counters + g, 1) == S - 1;
-  }
-  consumer_bar();
-  if (!s.flag[0]) return true;
-  __threadfence();
-  float* wgt = reinterpret_cast<float*>(s.scratch);  // [4][S] weights, then [4] empty flags
-  if (tid < 4) {
-    const int h = tid;
-    float mx = __int_as_float(0xff800000);
-    for (int sp = 0; sp < S; sp++) {
-      const float v = __ldcg(part_lse + (size_t)sp * nq + 4 * g + h);
-      mx = v > mx ? v : mx;
-    }
-    float den = 0.0f;
-    for (int sp = 0; sp < S; sp++) {
-      const float v = __ldcg(part_lse + (size_t)sp * nq + 4 * g + h);
-      const float w = (v == __int_as_float(0xff800000)) ? 0.0f : spark_exp(__fsub_rn(v, mx));
-      wgt[h * S + sp] = w;
-      den = __fadd_rn(den, w);
-    }
-    for (int sp = 0; sp < S; sp++) wgt[h * S + sp] = __fdiv_rn(wgt[h * S + sp], den);
-    s.red[56 + h] = (mx == __int_as_float(0xff800000)) ? 1.0f : 0.0f;
-  }
-  consumer_bar();
-  uint16_t* out = static_cast<uint16_t*>(st.attn_out);
-  for (int o = tid; o < 4 * D; o += kConsumers) {
-    const int h = o >> 7, d = o & 127;
-    float a = 0.0f;
-    if (s.red[56 + h] == 0.0f) {
-      for (int sp = 0; sp < S; sp++) {
-        if (__ldcg(part_lse + (size_t)sp * nq + 4 * g + h) == __int_as_float(0xff800000)) continue;
-        a = __fadd_rn(a, __fmul_rn(wgt[h * S + sp], __ldcg(part_o + ((size_t)sp * nq + 4 * g + h) * D + d)));
+    asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(st.head_counters + g) : "memory");
+    const int target = S * (int)(s.misc64[2] + 1);
+    const unsigned long long tw = gtimer();
+    int ok = 1;
+    for (uint32_t it = 0; ld_acquire(st.head_counters + g) < target; it++) {
+      if (it > 64) __nanosleep(32);
+      if (*s.abort_flag || gtimer() - tw > kWaitNs) {
+        ok = 0;
+        break;
       }
     }
-    out[(size_t)(4 * g + h) * D + d] = f2bf(a);
+    if (!ok) raise_abort(P, s, SPARK_ERR_LAUNCH);
+    if (tr) tr[7] = gtimer();
   }
-  if (tid == 0) st.head_counters[g] = 0;
+  consumer_bar();
+  // combine: lse of the 4 heads x S splits into shared memory (one L2 round trip, with
+  // this thread's part_o values), per-head max and weights w_s / den in parallel, then
+  // outputs j, j + S, ... sum w_s * O_s in split order
+  const float ninf = __int_as_float(0xff800000);
+  float* lse_s = reinterpret_cast<float*>(s.scratch);  // [4][S]
+  float* w_s = lse_s + 4 * S;                          // [4][S]
+  float* den_s = w_s + 4 * S;                          // [4] max, [4] den
+  const int nout = (4 * D - j + S - 1) / S;            // outputs j, j + S, ...
+  const int o = j + tid * S;
+  const int oh = o >> 7, od = o & 127;
+  float ov[kMergeRegs];
+  if (tid < nout && S <= kMergeRegs) {
+    const float* po_h = part_o + (size_t)(4 * g + oh) * D + od;
+#pragma unroll
+    for (int sp = 0; sp < kMergeRegs; sp++) ov[sp] = sp < S ? __ldcg(po_h + (size_t)sp * nq * D) : 0.0f;
+  }
+  for (int i = tid; i < 4 * S; i += kConsumers) {
+    const int h = i / S, sp = i - h * S;
+    lse_s[i] = __ldcg(part_lse + (size_t)sp * nq + 4 * g + h);
+  }
+  consumer_bar();
+  if (tid < 4) {
+    float m = ninf;
+    for (int sp = 0; sp < S; sp++) m = lse_s[tid * S + sp] > m ? lse_s[tid * S + sp] : m;
+    den_s[tid] = m;
+  }
+  consumer_bar();
+  for (int i = tid; i < 4 * S; i += kConsumers) {
+    const float v = lse_s[i], m = den_s[i / S];
+    w_s[i] = v == ninf ? 0.0f : spark_exp(__fsub_rn(v, m));
+  }
+  consumer_bar();
+  if (tid < 4) {
+    float den = 0.0f;
+    for (int sp = 0; sp < S; sp++) den = __fadd_rn(den, w_s[tid * S + sp]);
+    den_s[4 + tid] = den;
+  }
+  consumer_bar();
+  for (int i = tid; i < 4 * S; i += kConsumers) w_s[i] = __fdiv_rn(w_s[i], den_s[4 + i / S]);
+  consumer_bar();
+  if (tid < nout) {
+    const int h = oh, d = od;
+    float a = 0.0f;
+    if (den_s[h] != ninf) {
+      if (S <= kMergeRegs) {
+#pragma unroll
+        for (int sp = 0; sp < kMergeRegs; sp++)
+          if (sp < S && lse_s[h * S + sp] != ninf) a = __fadd_rn(a, __fmul_rn(w_s[h * S + sp], ov[sp]));
+      } else {
+        const float* po_h = part_o + (size_t)(4 * g + h) * D + d;
+        for (int sp = 0; sp < S; sp++)
+          if (lse_s[h * S + sp] != ninf) a = __fadd_rn(a, __fmul_rn(w_s[h * S + sp], __ldcg(po_h + (size_t)sp * nq * D)));
+      }
+    }
+    static_cast<uint16_t*>(st.attn_out)[(size_t)(4 * g + h) * D + d] = f2bf(a);
+  }
   return true;
 }
 
@@ -804,8 +967,8 @@ __device__ __forceinline__ bool wait_stage(const StepParams& P, const Smem& s, i
   const int target = (int)gridDim.x;
   if (ld_acquire(ctr) >= target) return true;
   const unsigned long long t0 = gtimer();
-  for (;;) {
-    __nanosleep(20);
+  for (uint32_t it = 0;; it++) {
+    if (it > 64) __nanosleep(32);
     if (ld_acquire(ctr) >= target) return true;
     if (ld_acquire(P.io.counters + P.num_stages + 1)) return false;
     if (gtimer() - t0 > kWaitNs) return false;
@@ -823,6 +986,8 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepParams P) {
       s.done[i] = 0;
     }
     *s.abort_flag = 0;
+    s.misc64[2] = P.io.counters[P.num_stages + 2];  // launch generation (attention head counters)
+    s.misc64[3] = 0;                                 // no cached launch constants yet
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
@@ -838,6 +1003,38 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepParams P) {
     if (tid < 32)  // 8-byte pieces: the inline stage in the launch parameters is only 8-byte aligned
       reinterpret_cast<unsigned long long*>(s.stage)[tid] =
           reinterpret_cast<const unsigned long long*>(&stage_at(P, i))[tid];
+    unsigned long long* tr = P.io.trace ? P.io.trace + ((size_t)blockIdx.x * P.num_stages + i) * kTraceSlots : nullptr;
+    if (tid == 0 && tr) tr[0] = gtimer();
+    if (tid == 0) s.flag[2] = i;  // stage index for the stage functions' trace stamps
+    {
+      // values that are fixed for the whole launch (position, block table, RoPE table):
+      // fetched before the stage barrier so their latency hides behind it
+      const SparkStage& nx = stage_at(P, i);
+      const bool rope = nx.kind == SPARK_STAGE_GEMV && nx.epi == SPARK_EPI_ROPE_KV;
+      if (nx.kind == SPARK_STAGE_GEMV && nx.norm) {  // RMSNorm weight (a constant) next to the staging area
+        const uint4* src = static_cast<const uint4*>(nx.gamma);
+        uint4* dst = reinterpret_cast<uint4*>(s.scratch + 72 * (nx.k >> 5) + 4 * nx.k);
+        for (int q = tid; q < (nx.k >> 3); q += kConsumers) dst[q] = __ldg(src + q);
+      }
+      // the same position / RoPE row serve every layer: fetch them once per launch
+      const long long key = (long long)reinterpret_cast<uintptr_t>(nx.pos);
+      if ((rope || nx.kind == SPARK_STAGE_ATTN) && s.misc64[3] != key && tid < 32) {
+        const int64_t pos = __ldcg(nx.pos);
+        if (tid == 0) {
+          s.misc64[0] = pos;
+          if (rope) {
+            const int64_t blk = pos / nx.block_size, off = pos - blk * nx.block_size;
+            s.misc64[1] = ((int64_t)nx.block_table[blk] * nx.nkv * nx.block_size + off) * nx.head_dim;
+          }
+        }
+        if (rope) {
+          const uint16_t* cs = static_cast<const uint16_t*>(nx.cos_sin) + (size_t)pos * nx.head_dim;
+          for (int d = tid; d < nx.head_dim; d += 32) s.rope_cs[d] = cs[d];
+        }
+        __syncwarp();
+        if (rope && tid == 0) s.misc64[3] = key;  // cached only once the RoPE row is in place
+      }
+    }
     if (tid == 0) {
       const int w = stage_at(P, i).wait;
       int stop = *s.abort_flag;
@@ -849,6 +1046,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepParams P) {
     }
     consumer_bar();
     if (s.flag[1]) return;  // uniform: every consumer reads the same flag
+    if (tid == 0 && tr) tr[1] = gtimer();
     const SparkStage& st = *s.stage;
     // both stage functions keep every consumer on the same barriers; a stage that
     // fails returns false in all threads (attention: a split longer than the scratch)
@@ -856,10 +1054,9 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepParams P) {
                                                 : attn_stage(P, st, s, seq_base, tid);
     consumer_bar();
     if (!ok) return;
-    if (tid == 0 && !*s.abort_flag) {
-      __threadfence();
-      atomicAdd(P.io.counters + i, 1);
-    }
+    if (tid == 0 && tr) tr[2] = gtimer();
+    if (tid == 0 && !*s.abort_flag)  // release: the CTA's writes (ordered by the barrier) before the count
+      asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(P.io.counters + i) : "memory");
   }
   // ---- the last CTA to finish turns the argmax into a token and resets the counters
   if (tid == 0 && !*s.abort_flag) {
@@ -878,6 +1075,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepParams P) {
       if (io.step) io.step[0] += 1;
       if (io.pos) io.pos[0] += 1;
       for (int i = 0; i <= P.num_stages; i++) P.io.counters[i] = 0;
+      P.io.counters[P.num_stages + 2] += 1;  // next launch's generation
       __threadfence();
     }
   }

@@ -65,7 +65,7 @@ class SparkStage(ctypes.Structure):
 class SparkStepIO(ctypes.Structure):
     """Mirror of ``SparkStepIO`` in include/spark_b200.h."""
 
-    _fields_ = [(n, _P) for n in ("counters", "error", "key", "token_out", "token_log", "step", "pos")]
+    _fields_ = [(n, _P) for n in ("counters", "error", "key", "token_out", "token_log", "step", "pos", "trace")]
 
 
 assert ctypes.sizeof(SparkStage) == 256

@@ -244,6 +244,7 @@ class DecodeEngine:
         self.o_parts = torch.zeros((kp_o, h), dtype=f32, device=dev)
         self.down_parts = torch.zeros((kp_down, h), dtype=f32, device=dev)
         self.kv_new = torch.zeros((2, nkv, D), dtype=BF16, device=dev)
+        self.head_ctr = torch.zeros((cfg.num_layers, nkv), dtype=torch.int32, device=dev)
         prog = S.StepProgram(dev, self.ncta)
         eps = cfg.rms_norm_eps
         prev = -1
@@ -260,7 +261,7 @@ class DecodeEngine:
             att = prog.attention(q=self.q, k_cache=kc, v_cache=vc, kv_new=self.kv_new, block_table=self.block_table,
                                  pos=self.pos, splits=self.splits, max_split_tokens=self.max_split_tokens,
                                  scale=cfg.attn_scale, part_o=self.part_o, part_lse=self.part_lse,
-                                 head_counters=self.counters, attn_out=self.attn_out, nq=nq, nkv=nkv, head_dim=D,
+                                 head_counters=self.head_ctr[li], attn_out=self.attn_out, nq=nq, nkv=nkv, head_dim=D,
                                  block_size=bs, wait=qkv)
             o = prog.gemv(wo, h, nq * D, kp=kp_o, ks=ks_o, a=self.attn_out, epi=S.EPI_PARTS, out=self.o_parts,
                           wait=att)
@@ -352,9 +353,9 @@ class DecodeEngine:
         self.step_idx.zero_()
         self.key.zero_()
         self.error.zero_()
-        if self.mode == "step":
+        if self.mode == "step":  # launch generation and head counters restart together
             self.program.reset_counters()
-            self.counters.zero_()
+            self.head_ctr.zero_()
 
     def oracle_order(self) -> dict | None:
         """The oracle evaluation order this engine's kernels follow (None: per-kernel order)."""

@@ -26,8 +26,9 @@ PRO_BF16, PRO_PARTS = 0, 1
 EPI_BF16, EPI_PARTS, EPI_ROPE_KV, EPI_SILU_MUL, EPI_ARGMAX = range(5)
 ROWS_PLAIN, ROWS_PAIR_HALF, ROWS_GATE_UP = range(3)
 
-PARTIAL_FLOATS = 5 * 1024 // 4  # per-CTA slice-sum buffer of the kernel
-MAX_SPLIT_TOKENS = 2048
+MAX_SLICES = 4  # slices per GEMV unit the kernel supports
+CHUNK_ACCS = 11  # consumer warps of the kernel = attention PV chunk accumulators
+MAX_SPLIT_TOKENS = 1344
 
 
 def _p(t):
@@ -60,13 +61,11 @@ def q4_pack_t16(qs: torch.Tensor, d: torch.Tensor, kp: int = 1, rowmap: int = RO
 
 
 def pick_ks(n: int, k: int, kp: int, want: int, ncta: int) -> int:
-    """Largest slice count <= want that divides the unit's 64-column tiles and fits the
-    kernel's slice-sum buffer."""
+    """Largest slice count <= want (and <= MAX_SLICES) that divides the unit's
+    64-column tiles."""
     tiles = (k // kp) // 64
-    units = n // 16 * kp
-    nl = -(-units // ncta)
-    for ks in range(min(want, tiles), 0, -1):
-        if tiles % ks == 0 and nl * ks * 16 <= PARTIAL_FLOATS:
+    for ks in range(min(want, tiles, MAX_SLICES), 0, -1):
+        if tiles % ks == 0:
             return ks
     raise ValueError(f"no slice count fits n={n} k={k} kp={kp}")
 
@@ -133,17 +132,23 @@ class StepProgram:
         self.host = (SparkStage * n)(*self.stages)
         raw = torch.frombuffer(bytearray(bytes(self.host)), dtype=torch.uint8)
         self.dev = raw.to(self.device)
-        self.counters = torch.zeros(n + 2, dtype=torch.int32, device=self.device)
+        self.counters = torch.zeros(n + 3, dtype=torch.int32, device=self.device)
         return self
 
     def reset_counters(self) -> None:
         self.counters.zero_()
 
-    def io(self, *, error=None, key=None, token_out=None, token_log=None, step=None, pos=None) -> SparkStepIO:
+    def io(self, *, error=None, key=None, token_out=None, token_log=None, step=None, pos=None,
+           trace=None) -> SparkStepIO:
         io = SparkStepIO()
         io.counters, io.error, io.key = _p(self.counters), _p(error), _p(key)
         io.token_out, io.token_log, io.step, io.pos = _p(token_out), _p(token_log), _p(step), _p(pos)
+        io.trace = _p(trace)
         return io
+
+    def trace_buffer(self) -> torch.Tensor:
+        """uint64 [ctas, stages, 8] for ``io(trace=...)``."""
+        return torch.zeros((self.ncta, len(self.stages), 8), dtype=torch.int64, device=self.device)
 
     def launch(self, io: SparkStepIO, stream=None) -> None:
         if self.host is None:
@@ -180,10 +185,10 @@ def default_order(cfg, ncta: int) -> dict:
     kp_down = 4 if (i // 4) % 64 == 0 else (2 if (i // 2) % 64 == 0 else 1)
     qkv_n = (nq + 2 * cfg.num_kv_heads) * D
     return {
-        "ks": (pick_ks(qkv_n, h, 1, 4, ncta), pick_ks(h, nq * D, kp_o, 4, ncta), pick_ks(2 * i, h, 1, 1, ncta),
-               pick_ks(h, i, kp_down, 2, ncta), pick_ks(v, h, 1, 1, ncta)),
+        "ks": (pick_ks(qkv_n, h, 1, 4, ncta), pick_ks(h, nq * D, kp_o, 4, ncta), pick_ks(2 * i, h, 1, 4, ncta),
+               pick_ks(h, i, kp_down, 2, ncta), pick_ks(v, h, 1, 4, ncta)),
         "kp": (kp_o, kp_down),
-        "chunk_accs": 12,
+        "chunk_accs": CHUNK_ACCS,
     }
 
 
