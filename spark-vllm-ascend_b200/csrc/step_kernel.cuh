@@ -300,6 +300,27 @@ __device__ __forceinline__ void unpack8(const uint4 u, float (&v)[8]) {
   v[4] = bf_lo(u.z); v[5] = bf_hi(u.z); v[6] = bf_lo(u.w); v[7] = bf_hi(u.w);
 }
 
+// x -> bf16 (round to nearest even) -> fp32 in one conversion instruction; matches f2bf
+// for every non-NaN input
+__device__ __forceinline__ float bf16_round(float x) {
+  uint16_t h;
+  asm("cvt.rn.bf16.f32 %0, %1;" : "=h"(h) : "f"(x));
+  return __uint_as_float((uint32_t)h << 16);
+}
+
+// two floats -> packed bf16 pair (lo in the low half), round to nearest even
+__device__ __forceinline__ uint32_t bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// low bytes of four ints -> one word (byte t from x_t)
+__device__ __forceinline__ uint32_t pack_bytes(int x0, int x1, int x2, int x3) {
+  return __byte_perm(__byte_perm((uint32_t)x0, (uint32_t)x1, 0x0040), __byte_perm((uint32_t)x2, (uint32_t)x3, 0x0040),
+                     0x5410);
+}
+
 // stage the 8 elements of group g (block g / 4, elements 8 (g % 4) ..); the 4 lanes of a
 // block are consecutive lanes of one warp and all execute this (valid or not)
 __device__ __forceinline__ void stage_group(const float (&v)[8], bool valid, int g, uint32_t* xfrag32, int2* xmeta) {
@@ -324,15 +345,14 @@ __device__ __forceinline__ void stage_group(const float (&v)[8], bool valid, int
   const int b = g >> 2, c = g & 3;
 #pragma unroll
   for (int w = 0; w < 2; w++) {
-    uint32_t hh = 0, ll = 0;
+    int hv[4], lv[4];
 #pragma unroll
-    for (int t = 0; t < 4; t++) {
-      const int x = X[4 * w + t];
-      const int l = ((x + 128) & 255) - 128;
-      const int h = (x - l) >> 8;
-      hh |= (uint32_t)(h & 0xff) << (8 * t);
-      ll |= (uint32_t)(l & 0xff) << (8 * t);
+    for (int t = 0; t < 4; t++) {  // X = 256 h + l, l in [-128, 127]
+      hv[t] = (X[4 * w + t] + 128) >> 8;
+      lv[t] = X[4 * w + t] - 256 * hv[t];
     }
+    const uint32_t hh = pack_bytes(hv[0], hv[1], hv[2], hv[3]);
+    const uint32_t ll = pack_bytes(lv[0], lv[1], lv[2], lv[3]);
     const int word = 2 * c + w;  // k = 4 word .. 4 word + 3
     xfrag32[(b * 8 + (word & 3)) * 2 + (word >> 2)] = hh;
     xfrag32[(b * 8 + 4 + (word & 3)) * 2 + (word >> 2)] = ll;
@@ -340,7 +360,7 @@ __device__ __forceinline__ void stage_group(const float (&v)[8], bool valid, int
   if (c == 0) xmeta[b] = make_int2(-8 * sum, __float_as_int(live ? __uint_as_float((uint32_t)(127 - S) << 23) : 1.0f));
 }
 
-__device__ __noinline__ void stage_x(const SparkStage& st, const Smem& s, int tid, unsigned long long* tr) {
+__device__ __forceinline__ void stage_x(const SparkStage& st, const Smem& s, int tid, unsigned long long* tr) {
   const int k = st.k, nb = k >> 5, ngrp = k >> 3;
   uint32_t* xfrag32 = reinterpret_cast<uint32_t*>(s.scratch);
   int2* xmeta = reinterpret_cast<int2*>(s.scratch + 64 * nb);
@@ -368,7 +388,7 @@ __device__ __noinline__ void stage_x(const SparkStage& st, const Smem& s, int ti
         }
         const float t8[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
 #pragma unroll
-        for (int j = 0; j < 8; j++) v[r][j] = bf2f(f2bf(t8[j]));
+        for (int j = 0; j < 8; j++) v[r][j] = bf16_round(t8[j]);
       } else {
         unpack8(__ldcg(reinterpret_cast<const uint4*>(arow + 8 * g)), v[r]);
       }
@@ -397,10 +417,10 @@ __device__ __noinline__ void stage_x(const SparkStage& st, const Smem& s, int ti
         for (int j = 0; j < 8; j++) sq[8 * g + j] = __fmul_rn(v[r][j], v[r][j]);
         if (res) {
           uint4 o;
-          o.x = (uint32_t)f2bf(v[r][0]) | ((uint32_t)f2bf(v[r][1]) << 16);
-          o.y = (uint32_t)f2bf(v[r][2]) | ((uint32_t)f2bf(v[r][3]) << 16);
-          o.z = (uint32_t)f2bf(v[r][4]) | ((uint32_t)f2bf(v[r][5]) << 16);
-          o.w = (uint32_t)f2bf(v[r][6]) | ((uint32_t)f2bf(v[r][7]) << 16);
+          o.x = bf16x2(v[r][0], v[r][1]);
+          o.y = bf16x2(v[r][2], v[r][3]);
+          o.z = bf16x2(v[r][4], v[r][5]);
+          o.w = bf16x2(v[r][6], v[r][7]);
           *reinterpret_cast<uint4*>(res + 8 * g) = o;
         }
       }
@@ -425,10 +445,11 @@ __device__ __noinline__ void stage_x(const SparkStage& st, const Smem& s, int ti
     const float inv = s.red[0];
 #pragma unroll
     for (int r = 0; r < kStageGroups; r++) {
+      if (r * kConsumers >= ngrp) break;
       float g8[8];
       unpack8(gv[r], g8);
 #pragma unroll
-      for (int j = 0; j < 8; j++) v[r][j] = bf2f(f2bf(__fmul_rn(__fmul_rn(v[r][j], inv), g8[j])));
+      for (int j = 0; j < 8; j++) v[r][j] = bf16_round(__fmul_rn(__fmul_rn(v[r][j], inv), g8[j]));
     }
   }
 #pragma unroll
@@ -611,7 +632,7 @@ __device__ __forceinline__ void finish_task(const Smem& s, uint32_t seq, int tas
   }
 }
 
-__device__ __noinline__ bool gemv_stage(const StepParams& P, const SparkStage& st, const Smem& s, uint32_t& seq_base, int tid) {
+__device__ __forceinline__ bool gemv_stage(const StepParams& P, const SparkStage& st, const Smem& s, uint32_t& seq_base, int tid) {
   const int ncta = gridDim.x, cta = blockIdx.x, warp = tid >> 5, lane = tid & 31;
   int u0;
   const int nl = local_units(st, cta, ncta, u0);
@@ -697,7 +718,7 @@ __device__ __noinline__ bool gemv_stage(const StepParams& P, const SparkStage& s
 // ... of the head group's 4 x 128 in the oracle's combine order.
 constexpr int kMergeRegs = 32;  // splits combined from registers (more: a loop)
 
-__device__ __noinline__ bool attn_stage(const StepParams& P, const SparkStage& st, const Smem& s, uint32_t& seq_base,
+__device__ __forceinline__ bool attn_stage(const StepParams& P, const SparkStage& st, const Smem& s, uint32_t& seq_base,
                                         int tid) {
   const int warp = tid >> 5, lane = tid & 31;
   int g, j;
