@@ -642,7 +642,8 @@ static int check_stage(const SparkStage& s, int i, int ncta) {
          reinterpret_cast<uintptr_t>(s.gamma) | reinterpret_cast<uintptr_t>(s.res_out)) & 15)
       return SPARK_ERR_ALIGNMENT;
     if (s.pro == SPARK_PRO_PARTS) {
-      if (s.a_parts <= 0 || !s.a || s.embed) return SPARK_ERR_INVALID_ARG;
+      if (s.a_parts <= 0 || s.a_parts > step::kMaxParts || !s.a || s.embed) return SPARK_ERR_INVALID_ARG;
+      if (s.k > step::kConsumers * 8) return SPARK_ERR_TOO_LARGE;  // one 8-element group per thread
     } else if (s.pro != SPARK_PRO_BF16) {
       return SPARK_ERR_INVALID_ARG;
     }

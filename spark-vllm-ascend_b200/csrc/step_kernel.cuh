@@ -287,6 +287,7 @@ struct Producer {
 // (l) with k = 4(e-4)..; word 0 holds k 0..15, word 1 holds k 16..31.
 // meta = (-8 sum X, sx).  Four consecutive threads stage one block, 8 elements each.
 constexpr int kStageGroups = 4;  // 8-element groups per consumer thread (k <= 12288)
+constexpr int kMaxParts = 4;
 
 __device__ __forceinline__ void lds_u32x4(uint32_t addr, uint4& v) {
   asm("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
@@ -378,11 +379,20 @@ __device__ __forceinline__ void stage_x(const SparkStage& st, const Smem& s, int
     const int g = tid + r * kConsumers;
     if (g < ngrp) {
       if (st.pro == SPARK_PRO_PARTS) {
+        // parts two at a time (two in flight per round trip), summed in part order
         float4 p0 = __ldcg(reinterpret_cast<const float4*>(parts + 8 * g));
         float4 p1 = __ldcg(reinterpret_cast<const float4*>(parts + 8 * g + 4));
+        float4 n0, n1;
+        if (st.a_parts > 1) {
+          n0 = __ldcg(reinterpret_cast<const float4*>(parts + (size_t)k + 8 * g));
+          n1 = __ldcg(reinterpret_cast<const float4*>(parts + (size_t)k + 8 * g + 4));
+        }
         for (int q = 1; q < st.a_parts; q++) {
-          const float4 q0 = __ldcg(reinterpret_cast<const float4*>(parts + (size_t)q * k + 8 * g));
-          const float4 q1 = __ldcg(reinterpret_cast<const float4*>(parts + (size_t)q * k + 8 * g + 4));
+          const float4 q0 = n0, q1 = n1;
+          if (q + 1 < st.a_parts) {
+            n0 = __ldcg(reinterpret_cast<const float4*>(parts + (size_t)(q + 1) * k + 8 * g));
+            n1 = __ldcg(reinterpret_cast<const float4*>(parts + (size_t)(q + 1) * k + 8 * g + 4));
+          }
           p0 = make_float4(__fadd_rn(p0.x, q0.x), __fadd_rn(p0.y, q0.y), __fadd_rn(p0.z, q0.z), __fadd_rn(p0.w, q0.w));
           p1 = make_float4(__fadd_rn(p1.x, q1.x), __fadd_rn(p1.y, q1.y), __fadd_rn(p1.z, q1.z), __fadd_rn(p1.w, q1.w));
         }
@@ -912,8 +922,7 @@ __device__ __forceinline__ bool attn_stage(const StepParams& P, const SparkStage
     const int target = S * (int)(s.misc64[2] + 1);
     const unsigned long long tw = gtimer();
     int ok = 1;
-    for (uint32_t it = 0; ld_acquire(st.head_counters + g) < target; it++) {
-      if (it > 64) __nanosleep(32);
+    while (ld_acquire(st.head_counters + g) < target) {
       if (*s.abort_flag || gtimer() - tw > kWaitNs) {
         ok = 0;
         break;
@@ -944,24 +953,27 @@ __device__ __forceinline__ bool attn_stage(const StepParams& P, const SparkStage
     lse_s[i] = __ldcg(part_lse + (size_t)sp * nq + 4 * g + h);
   }
   consumer_bar();
-  if (tid < 4) {
+  if (warp < 4) {  // warp h: max, exp, the sequential denominator and w / den of head h
+    const int h = warp;
     float m = ninf;
-    for (int sp = 0; sp < S; sp++) m = lse_s[tid * S + sp] > m ? lse_s[tid * S + sp] : m;
-    den_s[tid] = m;
-  }
-  consumer_bar();
-  for (int i = tid; i < 4 * S; i += kConsumers) {
-    const float v = lse_s[i], m = den_s[i / S];
-    w_s[i] = v == ninf ? 0.0f : spark_exp(__fsub_rn(v, m));
-  }
-  consumer_bar();
-  if (tid < 4) {
+    for (int sp = lane; sp < S; sp += 32) m = lse_s[h * S + sp] > m ? lse_s[h * S + sp] : m;
+#pragma unroll
+    for (int off = 16; off >= 1; off /= 2) {
+      const float o2 = __shfl_xor_sync(0xffffffffu, m, off);
+      m = o2 > m ? o2 : m;
+    }
+    for (int sp = lane; sp < S; sp += 32) {
+      const float v = lse_s[h * S + sp];
+      w_s[h * S + sp] = v == ninf ? 0.0f : spark_exp(__fsub_rn(v, m));
+    }
+    __syncwarp();
     float den = 0.0f;
-    for (int sp = 0; sp < S; sp++) den = __fadd_rn(den, w_s[tid * S + sp]);
-    den_s[4 + tid] = den;
+    if (lane == 0)
+      for (int sp = 0; sp < S; sp++) den = __fadd_rn(den, w_s[h * S + sp]);
+    den = __shfl_sync(0xffffffffu, den, 0);
+    for (int sp = lane; sp < S; sp += 32) w_s[h * S + sp] = __fdiv_rn(w_s[h * S + sp], den);
+    if (lane == 0) den_s[h] = m;
   }
-  consumer_bar();
-  for (int i = tid; i < 4 * S; i += kConsumers) w_s[i] = __fdiv_rn(w_s[i], den_s[4 + i / S]);
   consumer_bar();
   if (tid < nout) {
     const int h = oh, d = od;
@@ -988,8 +1000,7 @@ __device__ __forceinline__ bool wait_stage(const StepParams& P, const Smem& s, i
   const int target = (int)gridDim.x;
   if (ld_acquire(ctr) >= target) return true;
   const unsigned long long t0 = gtimer();
-  for (uint32_t it = 0;; it++) {
-    if (it > 64) __nanosleep(32);
+  for (;;) {  // each poll is one L2 round trip: spin without sleeping
     if (ld_acquire(ctr) >= target) return true;
     if (ld_acquire(P.io.counters + P.num_stages + 1)) return false;
     if (gtimer() - t0 > kWaitNs) return false;
