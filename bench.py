@@ -114,7 +114,7 @@ def build_engine(args, device, seed):
     import torch
     from spark_b200.config import SparkConfig
     from spark_b200.model import DecodeEngine, SyntheticWeights
-    cfg = SparkConfig()
+    cfg = SparkConfig(num_layers=args.layers)
     w = SyntheticWeights(cfg, device=device, seed=seed)
     max_seq = PROMPT_LEN + max(args.steps, args.warmup) + 1
     eng = DecodeEngine(w, max_seq_len=max_seq, splits=args.splits, num_blocks=(max_seq + 127) // 128 + 8,
@@ -163,10 +163,11 @@ def time_kernels(eng, reps: int = 3) -> dict:
 
 # DRAM bytes (read + write) per launch from one ncu capture of each kernel, divided by
 # the kernel's algorithmic bytes for the captured case; traffic scales with the units
-# processed (weight rows, context tokens), so bench launches get ratio x algorithmic
-# bytes.  Captures: profiles/q4_gemv_ring_gate_up_19456x2560.md,
-# profiles/attn_decode_16splits_ctx6144.md.
-NCU_TRAFFIC_RATIO = {"gate_up": 28_079_360 / 28_051_456, "attn": 25_295_360 / 25_182_208}
+# processed (weight rows, context tokens, layers), so bench launches get ratio x
+# algorithmic bytes.  The captures (gate_up ring GEMV, split-KV attention at ctx 6144,
+# an 8-layer persistent step) are summarised under profiles/.
+NCU_TRAFFIC_RATIO = {"gate_up": 28_079_360 / 28_051_456, "attn": 25_295_360 / 25_182_208,
+                     "step": 683_313_152 / 675_087_360}
 
 
 def kernel_bytes(cfg, ctx: int) -> dict:
@@ -373,7 +374,7 @@ def run_reference(args):
     import numpy as np
     import oracle
     from spark_b200.config import SparkConfig
-    cfg = SparkConfig()
+    cfg = SparkConfig(num_layers=args.layers)
     threads = os.cpu_count() or 1
     oracle.set_threads(threads)
     rng = np.random.default_rng(0)
@@ -448,6 +449,8 @@ def main(argv=None):
     ap.add_argument("--cpu-tokens", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--prompt", type=int, default=2048, help="prompt length (2048 = the benchmark protocol)")
+    ap.add_argument("--layers", type=int, default=36,
+                    help="decoder layers (36 = the benchmark model; fewer only for small profiling captures)")
     args = ap.parse_args(argv)
     global PROMPT_LEN
     PROMPT_LEN = args.prompt

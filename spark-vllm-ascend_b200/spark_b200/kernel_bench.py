@@ -142,6 +142,71 @@ def bench_attn(ctx, splits, reps, copies, device, gen, cfg):
             "gbs_split": round(byts / us_split / 1e3, 1), "gbs_split_combine": round(byts / us_both / 1e3, 1)}
 
 
+# ---------------------------------------------------------------- persistent-step stages
+def bench_step_gemv(name, n, k, kind, reps, copies, device, gen, cfg):
+    """One GEMV stage of the persistent decode-step kernel as its own launch (T16
+    weights, the decode program's slice / part counts)."""
+    from . import step as S
+    order = S.default_order(cfg, S.num_ctas())
+    ks_qkv, ks_o, ks_gu, ks_down, ks_head = order["ks"]
+    kp_o, kp_down = order["kp"]
+    spec = {"gemv": (1, ks_head, S.ROWS_PLAIN, S.EPI_BF16), "qkv": (1, ks_qkv, S.ROWS_PAIR_HALF, S.EPI_BF16),
+            "o_proj": (kp_o, ks_o, S.ROWS_PLAIN, S.EPI_PARTS), "gate_up": (1, ks_gu, S.ROWS_GATE_UP, S.EPI_SILU_MUL),
+            "down": (kp_down, ks_down, S.ROWS_PLAIN, S.EPI_PARTS), "head": (1, ks_head, S.ROWS_PLAIN, S.EPI_ARGMAX)}
+    kp, ks, rowmap, epi = spec[name]
+    wb = n * k // 32 * 18
+    copies = max(1, min(copies, math.ceil(400e6 / wb)))
+    x = torch.randn(k, device=device).to(BF16)
+    key = torch.zeros(1, device=device, dtype=torch.int64)
+    out = (torch.empty((kp, n), device=device, dtype=torch.float32) if epi == S.EPI_PARTS else
+           torch.empty(n, device=device, dtype=BF16))
+    progs = []
+    for _ in range(copies):
+        qs, d = _q4(n, k, device, gen)
+        w = S.q4_pack_t16(qs, d, kp, rowmap, cfg.head_dim)
+        del qs, d
+        p = S.StepProgram(device)
+        p.gemv(w, n, k, kp=kp, ks=ks, a=x, epi=epi, rowmap=rowmap, out=out, head_dim=cfg.head_dim,
+               key=key if epi == S.EPI_ARGMAX else None)
+        p.finalize()
+        progs.append((p, p.io(key=key if epi == S.EPI_ARGMAX else None)))
+    us = _time(lambda t: progs[t % copies][0].launch(progs[t % copies][1]), reps)
+    byts = wb + 2 * k + (4 * kp if epi == S.EPI_PARTS else 2) * n
+    return {"us": round(us, 3), "bytes": byts, "gbs": round(byts / us / 1e3, 1), "copies": copies, "kp": kp, "ks": ks}
+
+
+def bench_step_attn(ctx, reps, copies, device, gen, cfg):
+    """The attention stage of the persistent decode-step kernel as its own launch
+    (splits = CTAs / kv heads, distributed combine)."""
+    from . import step as S
+    nq, nkv, D, bs = cfg.num_q_heads, cfg.num_kv_heads, cfg.head_dim, cfg.block_size
+    splits = S.attn_splits(cfg, S.num_ctas())
+    nblk = (ctx + bs - 1) // bs
+    per = 2 * nblk * nkv * bs * D * 2
+    copies = max(1, min(copies, math.ceil(400e6 / per)))
+    q = torch.randn((nq, D), device=device).to(BF16)
+    pos = torch.tensor([ctx - 1], device=device, dtype=torch.int64)
+    progs = []
+    for _ in range(copies):
+        kc = torch.randn((nblk, nkv, bs, D), generator=gen, device=device).to(BF16)
+        vc = torch.randn((nblk, nkv, bs, D), generator=gen, device=device).to(BF16)
+        table = torch.randperm(nblk, device=device, generator=gen).to(torch.int32)
+        kv_new = torch.zeros((2, nkv, D), device=device, dtype=BF16)
+        po = torch.empty((splits, nq, D), device=device, dtype=torch.float32)
+        pl = torch.empty((splits, nq), device=device, dtype=torch.float32)
+        out = torch.empty((nq, D), device=device, dtype=BF16)
+        hc = torch.zeros(nkv, device=device, dtype=torch.int32)
+        p = S.StepProgram(device)
+        p.attention(q=q, k_cache=kc, v_cache=vc, kv_new=kv_new, block_table=table, pos=pos, splits=splits,
+                    max_split_tokens=S.max_split_tokens(ctx, splits), scale=cfg.attn_scale, part_o=po,
+                    part_lse=pl, head_counters=hc, attn_out=out, nq=nq, nkv=nkv, head_dim=D, block_size=bs)
+        p.finalize()
+        progs.append((p, p.io()))
+    us = _time(lambda t: progs[t % copies][0].launch(progs[t % copies][1]), reps)
+    byts = 2 * ctx * nkv * D * 2 + 2 * nq * D * 2
+    return {"us": round(us, 3), "bytes": byts, "gbs": round(byts / us / 1e3, 1), "splits": splits}
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--kernels", default="gemv,qkv,o_proj,gate_up,down,head,attn")
@@ -150,20 +215,24 @@ def main(argv=None):
     ap.add_argument("--ctx", default="2048,4096,6144")
     ap.add_argument("--splits", type=int, default=16)
     ap.add_argument("--direct", action="store_true", help="register-direct GEMV instead of the weight ring")
+    ap.add_argument("--step", action="store_true",
+                    help="stages of the persistent decode-step kernel (one cooperative launch each)")
     args = ap.parse_args(argv)
     device = torch.device("cuda")
     gen = torch.Generator(device=device).manual_seed(0)
     cfg = SparkConfig()
     ops.set_gemv_ring(not args.direct)
-    out = {"path": "direct" if args.direct else "ring"}
+    out = {"path": "step" if args.step else ("direct" if args.direct else "ring")}
     cases = gemv_cases(cfg)
     for name in args.kernels.split(","):
         if name in cases:
             n, k, kind = cases[name]
-            out[name] = bench_gemv(name, n, k, kind, args.reps, args.copies, device, gen, cfg)
+            fn = bench_step_gemv if args.step else bench_gemv
+            out[name] = fn(name, n, k, kind, args.reps, args.copies, device, gen, cfg)
         elif name == "attn":
             for ctx in map(int, args.ctx.split(",")):
-                out[f"attn_{ctx}"] = bench_attn(ctx, args.splits, args.reps, args.copies, device, gen, cfg)
+                out[f"attn_{ctx}"] = (bench_step_attn(ctx, args.reps, args.copies, device, gen, cfg) if args.step else
+                                      bench_attn(ctx, args.splits, args.reps, args.copies, device, gen, cfg))
     out["device_error"] = ops.read_device_error()
     print(json.dumps(out), flush=True)
 
