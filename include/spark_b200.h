@@ -176,6 +176,15 @@ int spark_silu_mul(const uint16_t* g, const uint16_t* u, int64_t n, uint16_t* ou
  * Replaces the rotation in FusedQkvStage.calculate_rotated (kernels/qkv.py:179-189). */
 int spark_rope_neox(uint16_t* x, int nh, int head_dim, const uint16_t* cos_sin, const int64_t* pos, void* stream);
 
+/* Store this step's keys and values into the paged caches: k / v bf16
+ * [tokens][nkv][head_dim] -> k_cache / v_cache bf16 [blocks][nkv][block_size][head_dim]
+ * at slot_mapping[t] (int64; negative = padding, skipped).  head_dim % 8 == 0, 16-byte
+ * aligned tensors.  Replaces the KV write of the reference's attention layer
+ * (the slot scatter of FusedQkvStage.store8, kernels/qkv.py:192-198) for callers that
+ * rotate q / k themselves (the vLLM attention backend). */
+int spark_kv_store(const uint16_t* k, const uint16_t* v, const int64_t* slot_mapping, int64_t tokens, int nkv,
+                   int head_dim, int block_size, uint16_t* k_cache, uint16_t* v_cache, void* stream);
+
 /* Paged-KV slot mapping for one request (single KV group):
  * out[i] = table[pos[i] / block_size] * block_size + pos[i] % block_size for
  * i in [query_start[0], query_start[1]) and i < num_tokens, else -1, for all

@@ -158,6 +158,32 @@ __global__ void slot_mapping_kernel(int64_t n, int64_t max_tokens, const int32_t
   }
 }
 
+// ------------------------------------------------------------------ KV store
+// k / v bf16 [tokens][nkv][D] -> caches [blocks][nkv][bs][D] at slot_mapping[t]
+// (slot = block * bs + offset; negative slots are padding and skipped).  One thread
+// moves 16 bytes.
+__global__ void kv_store_kernel(const uint16_t* __restrict__ k, const uint16_t* __restrict__ v,
+                                const int64_t* __restrict__ slots, int64_t tokens, int nkv, int D, int64_t bs,
+                                uint16_t* __restrict__ k_cache, uint16_t* __restrict__ v_cache) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int per_tok = nkv * D / 8;  // 16-byte pieces per token per tensor
+  const int64_t total = tokens * per_tok * 2;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int side = (int)(i / (tokens * per_tok));
+    const int64_t r = i - side * tokens * per_tok;
+    const int64_t t = r / per_tok;
+    const int piece = (int)(r - t * per_tok);
+    const int64_t slot = slots[t];
+    if (slot < 0) continue;
+    const int h = piece / (D / 8), e = (piece - h * (D / 8)) * 8;
+    const int64_t blk = slot / bs, off = slot - blk * bs;
+    const uint16_t* src = (side ? v : k) + (t * nkv + h) * D + e;
+    uint16_t* dst = (side ? v_cache : k_cache) + ((blk * nkv + h) * bs + off) * D + e;
+    *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+  }
+}
+
 // ------------------------------------------------------------------ decode bookkeeping
 // The next step's kernels start only after this one has written the new token and
 // position: the attention kernel reads the position before its own PDL wait, so

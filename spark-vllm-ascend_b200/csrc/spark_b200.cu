@@ -595,6 +595,21 @@ int spark_slot_mapping(int64_t num_tokens, int64_t max_tokens, const int32_t* qu
                 query_start, positions, block_table, block_size, out);
 }
 
+int spark_kv_store(const uint16_t* k, const uint16_t* v, const int64_t* slot_mapping, int64_t tokens, int nkv,
+                   int head_dim, int block_size, uint16_t* k_cache, uint16_t* v_cache, void* stream) {
+  if (!k || !v || !slot_mapping || !k_cache || !v_cache) return SPARK_ERR_INVALID_ARG;
+  if (tokens < 0 || nkv <= 0 || head_dim <= 0 || head_dim % 8 || block_size <= 0) return SPARK_ERR_UNSUPPORTED_SHAPE;
+  if ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(k_cache) |
+       reinterpret_cast<uintptr_t>(v_cache)) & 15)
+    return SPARK_ERR_ALIGNMENT;
+  if (tokens == 0) return SPARK_OK;
+  const int64_t total = tokens * nkv * head_dim / 8 * 2;
+  int64_t grid = (total + 255) / 256;
+  if (grid > 4 * num_sms()) grid = 4 * num_sms();
+  return launch(kv_store_kernel, dim3((unsigned)grid), dim3(256), 0, as_stream(stream), k, v, slot_mapping, tokens,
+                nkv, head_dim, (int64_t)block_size, k_cache, v_cache);
+}
+
 // ------------------------------------------------------------------ persistent decode step
 int64_t spark_t16_bytes(int n, int k, int kp) {
   if (n <= 0 || k <= 0 || kp <= 0 || k % kp) return -1;

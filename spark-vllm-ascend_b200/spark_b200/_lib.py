@@ -40,6 +40,7 @@ SIGNATURES: dict[str, list] = {
     "spark_set_pdl": [_I],
     "spark_set_gemv_ring": [_I],
     "spark_read_device_error": [_P, _I],
+    "spark_kv_store": [_P, _P, _P, _I64, _I, _I, _I, _P, _P, _P],
     "spark_t16_bytes": [_I, _I, _I],
     "spark_q4_pack_t16": [_P, _P, _I, _I, _I, _I, _I, _P, _P],
     "spark_step_ring_bytes": [],

@@ -228,6 +228,21 @@ def slot_mapping_out(num_tokens, query_start, positions, block_table, block_size
     return out
 
 
+def kv_store_(k: torch.Tensor, v: torch.Tensor, slot_mapping: torch.Tensor, k_cache: torch.Tensor,
+              v_cache: torch.Tensor) -> None:
+    """Scatter k / v [tokens, nkv, D] into the paged caches [blocks, nkv, bs, D] at
+    slot_mapping (int64; negative slots skipped)."""
+    _cuda(k, "k", BF16)
+    _cuda(v, "v", BF16)
+    _cuda(slot_mapping, "slot_mapping", torch.int64)
+    _cuda(k_cache, "k_cache", BF16)
+    _cuda(v_cache, "v_cache", BF16)
+    t, nkv, d = k.shape
+    _check(k_cache.dim() == 4 and k_cache.shape[1] == nkv and k_cache.shape[3] == d, "k_cache shape")
+    call("spark_kv_store", _p(k.contiguous()), _p(v.contiguous()), _p(slot_mapping.contiguous()), t, nkv, d,
+         k_cache.shape[2], _p(k_cache), _p(v_cache), _stream())
+
+
 def set_pdl(enabled: bool) -> None:
     call("spark_set_pdl", 1 if enabled else 0)
 
