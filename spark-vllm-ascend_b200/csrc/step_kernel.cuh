@@ -361,6 +361,13 @@ __device__ __forceinline__ void stage_group(const float (&v)[8], bool valid, int
   if (c == 0) xmeta[b] = make_int2(-8 * sum, __float_as_int(live ? __uint_as_float((uint32_t)(127 - S) << 23) : 1.0f));
 }
 
+// group handled by slot gi of this CTA (out-of-range slots stay out of range)
+__device__ __forceinline__ int stage_grp(int gi, int ngrp, int rot) {
+  if (gi >= ngrp) return gi;
+  const int g = gi + rot;
+  return g >= ngrp ? g - ngrp : g;
+}
+
 __device__ __forceinline__ void stage_x(const SparkStage& st, const Smem& s, int tid, unsigned long long* tr) {
   const int k = st.k, nb = k >> 5, ngrp = k >> 3;
   uint32_t* xfrag32 = reinterpret_cast<uint32_t*>(s.scratch);
@@ -373,10 +380,14 @@ __device__ __forceinline__ void stage_x(const SparkStage& st, const Smem& s, int
   const uint16_t* gm = reinterpret_cast<const uint16_t*>(s.scratch + 72 * nb + 4 * k);  // prefetched gamma
   float v[kStageGroups][8];
   uint4 gv[kStageGroups];
+  // Every CTA reads the whole input vector at the same moment: start each CTA at a
+  // different block (a multiple of 4 groups keeps a block's 4 lanes together) so the
+  // requests spread over the L2 slices instead of queueing on the same lines.
+  const int rot = 4 * (int)((blockIdx.x * 37u) % (unsigned)(ngrp >> 2));
   // all loads first: one L2 round trip
 #pragma unroll
   for (int r = 0; r < kStageGroups; r++) {
-    const int g = tid + r * kConsumers;
+    const int g = stage_grp(tid + r * kConsumers, ngrp, rot);
     if (g < ngrp) {
       if (st.pro == SPARK_PRO_PARTS) {
         // parts two at a time (two in flight per round trip), summed in part order
@@ -421,7 +432,7 @@ __device__ __forceinline__ void stage_x(const SparkStage& st, const Smem& s, int
     uint16_t* res = (blockIdx.x == 0) ? static_cast<uint16_t*>(st.res_out) : nullptr;
 #pragma unroll
     for (int r = 0; r < kStageGroups; r++) {
-      const int g = tid + r * kConsumers;
+      const int g = stage_grp(tid + r * kConsumers, ngrp, rot);
       if (g < ngrp) {
 #pragma unroll
         for (int j = 0; j < 8; j++) sq[8 * g + j] = __fmul_rn(v[r][j], v[r][j]);
@@ -464,7 +475,7 @@ __device__ __forceinline__ void stage_x(const SparkStage& st, const Smem& s, int
   }
 #pragma unroll
   for (int r = 0; r < kStageGroups; r++) {
-    const int g = tid + r * kConsumers;
+    const int g = stage_grp(tid + r * kConsumers, ngrp, rot);
     if (r * kConsumers < ngrp) stage_group(v[r], g < ngrp, g, xfrag32, xmeta);
   }
 }
@@ -536,12 +547,18 @@ __device__ __forceinline__ void gemv_tiles(uint32_t& a_adr, uint32_t& d_adr, uin
   m_adr += NT * 16;
 }
 
-__device__ __forceinline__ void gemv_task(const SparkStage& st, const Smem& s, uint32_t ubase, int kpi, int sl,
-                                          int lane, float& acc0, float& acc1) {
-  const int Kp = st.k / st.kp, tiles = Kp >> 6, tps = tiles / st.ks;
-  const uint32_t xf = smem_u32(s.scratch), xm = xf + 64 * (st.k >> 5);
+// per-stage GEMV constants (computed once per stage, not per task)
+struct GemvDims {
+  int kp, kp_blocks, tps;  // K parts, blocks per part, tiles per slice
+  uint32_t xf, xm;         // staged x fragments / block meta (shared addresses)
+};
+
+__device__ __forceinline__ void gemv_task(const GemvDims& gd, uint32_t ubase, int kpi, int sl, int lane, float& acc0,
+                                          float& acc1) {
+  const int tps = gd.tps;
+  const uint32_t xf = gd.xf, xm = gd.xm;
   const int t0 = sl * tps;
-  const int gb = kpi * (Kp >> 5) + 2 * t0;  // first block of the slice
+  const int gb = kpi * gd.kp_blocks + 2 * t0;  // first block of the slice
   // per-lane addresses: A at lane * 16 of each tile, scales at 512 + (lane / 4) * 8,
   // B fragment entry lane & 7 of each block, block meta
   uint32_t a_adr = ubase + (uint32_t)t0 * kTileBytes + lane * 16;
@@ -656,6 +673,12 @@ __device__ __forceinline__ bool gemv_stage(const StepParams& P, const SparkStage
   if (tr) tr[4] = gtimer();
   unsigned long long best = 0ull;
   const int ks = st.ks;
+  GemvDims gd;
+  gd.kp = st.kp;
+  gd.kp_blocks = (st.k / st.kp) >> 5;
+  gd.tps = (gd.kp_blocks >> 1) / ks;
+  gd.xf = smem_u32(s.scratch);
+  gd.xm = gd.xf + 64 * (st.k >> 5);
   for (int t = warp; t < nl * ks; t += kWarps) {
     const int j = t / ks, sl = t - j * ks;
     const uint32_t seq = seq_base + j;
@@ -666,7 +689,7 @@ __device__ __forceinline__ bool gemv_stage(const StepParams& P, const SparkStage
     const int u = u0 + j * ncta;
     const uint32_t slot = seq % kDesc;
     float acc0, acc1;
-    gemv_task(st, s, smem_u32(s.ring) + s.desc_off[slot], u % st.kp, sl, lane, acc0, acc1);
+    gemv_task(gd, smem_u32(s.ring) + s.desc_off[slot], u % gd.kp, sl, lane, acc0, acc1);
     float* pr = s.partial + slot * kMaxSlices * 16;
     if ((lane & 3) == 0) {
       pr[sl * 16 + (lane >> 2)] = acc0;
@@ -1047,6 +1070,12 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepParams P) {
         const uint4* src = static_cast<const uint4*>(nx.gamma);
         uint4* dst = reinterpret_cast<uint4*>(s.scratch + 72 * (nx.k >> 5) + 4 * nx.k);
         for (int q = tid; q < (nx.k >> 3); q += kConsumers) dst[q] = __ldg(src + q);
+      }
+      if (tid == 32) {  // touch the stage's activation buffers (value unused) to warm their translations
+        const void* bufs[8] = {nx.a, nx.b, nx.out, nx.res_out, nx.q, nx.kv_new, nx.part_o, nx.attn_out};
+#pragma unroll
+        for (int b2 = 0; b2 < 8; b2++)
+          if (bufs[b2]) asm volatile("prefetch.global.L2 [%0];" ::"l"(bufs[b2]));
       }
       // the same position / RoPE row serve every layer: fetch them once per launch
       const long long key = (long long)reinterpret_cast<uintptr_t>(nx.pos);

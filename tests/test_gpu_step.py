@@ -107,7 +107,7 @@ def test_step_run_rejects_bad_stages(cuda):
     qs, d = _q4(64, 512, seed=1)
     w = step.q4_pack_t16(qs, d, 1)
     x = torch.randn(512, device="cuda").to(torch.bfloat16)
-    for kw, status in (({"ks": 5}, 2), ({"ks": 3}, 2)):
+    for kw, status in (({"ks": 5}, 2), ({"ks": 3}, 2), ({"ks": 16}, 2)):
         with pytest.raises(SparkError) as e:
             step.t16_gemv(x, w, 64, 512, 1, **kw)
         assert e.value.status == status
