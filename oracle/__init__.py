@@ -62,7 +62,6 @@ def lib():
             "orc_t16_gemv": (None, [_P, _P, _P, _I64, _I64, _I, _I, _P]),
             "orc_parts_to_bf16": (None, [_P, _I, _I64, _P]),
             "orc_attn_split_w": (None, [_P, _P, _P, _P, _I64, _I, _I, _I, _I, _I, _F, _I, _P, _P]),
-            "orc_attn_split_flash": (None, [_P, _P, _P, _P, _I64, _I, _I, _I, _I, _I, _F, _I, _P, _P]),
             "orc_attn_split": (None, [_P, _P, _P, _P, _I64, _I, _I, _I, _I, _I, _F, _P, _P]),
             "orc_attn_combine": (None, [_P, _P, _I, _I, _I, _P]),
             "orc_argmax_bf16": (_I64, [_P, _I64]),
@@ -252,21 +251,6 @@ def attn_split(q, kc, vc, table, length: int, splits: int, scale: float, chunk_a
     pl = np.empty((splits, nq), np.float32)
     lib().orc_attn_split_w(_p(q), _p(kc), _p(vc), _p(np.ascontiguousarray(table, dtype=np.int32)), length, nq,
                            nkv, dim, bs, splits, scale, chunk_accs, _p(po), _p(pl))
-    return po, pl
-
-
-def attn_split_flash(q, kc, vc, table, length: int, splits: int, scale: float, warps: int):
-    """Persistent-step attention order: online softmax per 16-token chunk, chunk c on
-    warp c mod ``warps``, warps merged in order."""
-    q = np.ascontiguousarray(q, dtype=np.uint16)
-    kc = np.ascontiguousarray(kc, dtype=np.uint16)
-    vc = np.ascontiguousarray(vc, dtype=np.uint16)
-    nq, dim = q.shape
-    _, nkv, bs, _ = kc.shape
-    po = np.empty((splits, nq, dim), np.float32)
-    pl = np.empty((splits, nq), np.float32)
-    lib().orc_attn_split_flash(_p(q), _p(kc), _p(vc), _p(np.ascontiguousarray(table, dtype=np.int32)), length, nq,
-                               nkv, dim, bs, splits, scale, warps, _p(po), _p(pl))
     return po, pl
 
 

@@ -573,91 +573,6 @@ ORC_API void orc_attn_split_w(const uint16_t* q, const uint16_t* kc, const uint1
     free(o);
 }
 
-/* Persistent-step attention order ("flash"): a split's tokens form 16-token chunks;
- * chunk c is processed by warp c mod W, in ascending c, with an online softmax.
- * Per warp and head: m = -inf, l = 0, O = 0; per chunk: s_t = score * scale,
- * mn = max(m, max_t s_t), a = exp(m - mn), p_t = exp(s_t - mn),
- * cs = sum_t p_t (tokens ascending), l = fma(l, a, cs), O = O * a then
- * O = fma(bf16(p_t), V_t, O) for tokens ascending, m = mn.  Merge over warps
- * w = 0..W-1: M = max_w m_w, b_w = exp(m_w - M) (0 when m_w = -inf),
- * L = fma(l_w, b_w, L), O = fma(O_w, b_w, O) (w ascending, from 0); out = O / L,
- * lse = log(L) + M. */
-ORC_API void orc_attn_split_flash(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const int32_t* table,
-                                  int64_t len, int nq, int nkv, int dim, int bs, int splits, float scale, int W,
-                                  float* part_o, float* part_lse) {
-    int group = nq / nkv;
-    int64_t T = split_tokens(len, splits);
-    float* qf = (float*)malloc(sizeof(float) * dim);
-    float* wm = (float*)malloc(sizeof(float) * W);
-    float* wl = (float*)malloc(sizeof(float) * W);
-    float* wo = (float*)malloc(sizeof(float) * W * dim);
-    float sc[16], pe[16];
-    for (int s = 0; s < splits; s++) {
-        int64_t t0 = (int64_t)s * T, t1 = t0 + T < len ? t0 + T : len;
-        int64_t n = t1 - t0;
-        for (int hq = 0; hq < nq; hq++) {
-            int hk = hq / group;
-            float* po = part_o + ((int64_t)s * nq + hq) * dim;
-            if (n <= 0) {
-                for (int dd = 0; dd < dim; dd++) po[dd] = 0.0f;
-                part_lse[(int64_t)s * nq + hq] = -INFINITY;
-                continue;
-            }
-            for (int dd = 0; dd < dim; dd++) qf[dd] = bf2f(q[(int64_t)hq * dim + dd]);
-            for (int w = 0; w < W; w++) {
-                wm[w] = -INFINITY;
-                wl[w] = 0.0f;
-                for (int dd = 0; dd < dim; dd++) wo[w * dim + dd] = 0.0f;
-            }
-            int64_t nch = (n + 15) / 16;
-            for (int64_t c = 0; c < nch; c++) {
-                int w = (int)(c % W);
-                int cnt = (int)(n - 16 * c < 16 ? n - 16 * c : 16);
-                float cm = -INFINITY;
-                for (int i = 0; i < cnt; i++) {
-                    int64_t t = t0 + 16 * c + i, blk = table[t / bs], off = t % bs;
-                    const uint16_t* kr = kc + ((blk * nkv + hk) * bs + off) * dim;
-                    sc[i] = score_dot(qf, kr, dim) * scale;
-                    if (sc[i] > cm) cm = sc[i];
-                }
-                float mn = wm[w] > cm ? wm[w] : cm;
-                float a = orc_exp(wm[w] - mn);
-                float cs = 0.0f;
-                for (int i = 0; i < cnt; i++) {
-                    pe[i] = orc_exp(sc[i] - mn);
-                    cs = cs + pe[i];
-                }
-                wl[w] = fmaf(wl[w], a, cs);
-                float* o = wo + w * dim;
-                for (int dd = 0; dd < dim; dd++) o[dd] = o[dd] * a;
-                for (int i = 0; i < cnt; i++) {
-                    int64_t t = t0 + 16 * c + i, blk = table[t / bs], off = t % bs;
-                    const uint16_t* vr = vc + ((blk * nkv + hk) * bs + off) * dim;
-                    float pb = bf2f(f2bf(pe[i]));
-                    for (int dd = 0; dd < dim; dd++) o[dd] = fmaf(pb, bf2f(vr[dd]), o[dd]);
-                }
-                wm[w] = mn;
-            }
-            float M = -INFINITY;
-            for (int w = 0; w < W; w++)
-                if (wm[w] > M) M = wm[w];
-            float L = 0.0f;
-            for (int dd = 0; dd < dim; dd++) po[dd] = 0.0f;
-            for (int w = 0; w < W; w++) {
-                float b = wm[w] == -INFINITY ? 0.0f : orc_exp(wm[w] - M);
-                L = fmaf(wl[w], b, L);
-                for (int dd = 0; dd < dim; dd++) po[dd] = fmaf(wo[w * dim + dd], b, po[dd]);
-            }
-            for (int dd = 0; dd < dim; dd++) po[dd] = po[dd] / L;
-            part_lse[(int64_t)s * nq + hq] = orc_log(L) + M;
-        }
-    }
-    free(qf);
-    free(wm);
-    free(wl);
-    free(wo);
-}
-
 ORC_API void orc_attn_split(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const int32_t* table,
                             int64_t len, int nq, int nkv, int dim, int bs, int splits, float scale,
                             float* part_o, float* part_lse) {
@@ -722,8 +637,8 @@ ORC_API int64_t orc_argmax_bf16(const uint16_t* logits, int64_t n) {
 
 /* dims[10] selects the evaluation order: 0 = per-kernel path (lane-16 GEMV,
  * sequential PV); 1 = persistent-step path (T16 GEMV with dims[11..15] = KS of
- * qkv, o, gate_up, down, head and dims[16..17] = KP of o and down; attention in the
- * "flash" order over dims[18] warps). */
+ * qkv, o, gate_up, down, head and dims[16..17] = KP of o and down; attention PV
+ * with dims[18] chunk accumulators). */
 enum { MAT_QKV = 0, MAT_O = 1, MAT_GU = 2, MAT_DOWN = 3, MAT_HEAD = 4 };
 
 static void gemv_v(const int64_t* dims, int mat, const uint16_t* x, const void* qs, const void* d, int64_t n,
@@ -763,10 +678,8 @@ ORC_API void orc_decode_layer(const int64_t* dims, const void* const* lp, const 
         memcpy(kc + ((blk * nkv + hk) * bs + off) * D, qkv + (int64_t)(nq + hk) * D, 2 * D);
         memcpy(vc + ((blk * nkv + hk) * bs + off) * D, qkv + (int64_t)(nq + nkv + hk) * D, 2 * D);
     }
-    if (dims[10])
-        orc_attn_split_flash(qkv, kc, vc, table, pos + 1, nq, nkv, D, bs, splits, scale, (int)dims[18], po, pl);
-    else
-        orc_attn_split_w(qkv, kc, vc, table, pos + 1, nq, nkv, D, bs, splits, scale, 0, po, pl);
+    orc_attn_split_w(qkv, kc, vc, table, pos + 1, nq, nkv, D, bs, splits, scale, dims[10] ? (int)dims[18] : 0, po,
+                     pl);
     orc_attn_combine(po, pl, splits, nq, D, attn);
     /* o_proj -> a */
     gemv_v(dims, MAT_O, attn, lp[4], lp[5], H, (int64_t)nq * D, a);

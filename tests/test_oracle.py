@@ -327,84 +327,6 @@ def test_attention_chunk_accumulators_vs_float64(oracle, L, splits, W):
     assert np.allclose(po, po0, rtol=1e-5, atol=1e-6)
 
 
-@pytest.mark.parametrize("L,splits,W", [(3000, 18, 11), (64, 74, 11), (1, 18, 11), (9000, 7, 11), (777, 4, 3)])
-def test_attention_flash_order_vs_float64(oracle, L, splits, W):
-    """Persistent-step attention (online softmax per 16-token chunk, chunks dealt to W
-    warps, warps merged in order) meets abs 2e-2 against float64 eager attention."""
-    rng = np.random.default_rng(L + 7 * W)
-    kc, vc, table = _paged(rng, L)
-    q = bf16(rng.standard_normal((32, 128)).astype(np.float32))
-    scale = float(np.float32(1 / math.sqrt(128)))
-    po, pl = oracle.attn_split_flash(q, kc, vc, table, L, splits, scale, W)
-    out = f32(oracle.attn_combine(po, pl))
-    assert np.max(np.abs(out - _attn_ref64(q, kc, vc, table, L, scale))) <= 2e-2
-    T = oracle.split_tokens(L, splits)
-    assert all(np.all(np.isneginf(pl[sp])) and np.all(po[sp] == 0) for sp in range(splits) if sp * T >= L)
-
-
-def test_attention_flash_order_is_documented(oracle):
-    """Re-derive one split's output in Python from the documented flash order; compare bits."""
-    rng = np.random.default_rng(5)
-    L, splits, W = 100, 2, 3
-    kc, vc, table = _paged(rng, L, nkv=1)
-    q = bf16(rng.standard_normal((4, 128)).astype(np.float32))
-    scale = float(np.float32(1 / math.sqrt(128)))
-    po, pl = oracle.attn_split_flash(q, kc, vc, table, L, splits, scale, W)
-    T = oracle.split_tokens(L, splits)
-    kf, vf, qf = f32(kc), f32(vc), f32(q)
-    f = np.float32
-
-    def fma(a, b, c):
-        return f(np.float64(a) * np.float64(b) + np.float64(c))
-
-    def score(h, t):  # 8-lane order: even / odd positions in two chains, butterfly 4,2,1
-        kr = kf[table[t // 128], 0, t % 128]
-        lanes = []
-        for j in range(8):
-            idx = list(range(8 * j, 8 * j + 8)) + list(range(64 + 8 * j, 64 + 8 * j + 8))
-            a0 = a1 = f(0)
-            for m in range(0, 16, 2):
-                a0 = fma(qf[h, idx[m]], kr[idx[m]], a0)
-                a1 = fma(qf[h, idx[m + 1]], kr[idx[m + 1]], a1)
-            lanes.append(f(a0 + a1))
-        v = np.array(lanes, np.float32)
-        for off in (4, 2, 1):
-            v = (v + v[np.arange(8) ^ off]).astype(np.float32)
-        return f(v[0] * f(scale))
-
-    for sp in range(splits):
-        t0, t1 = sp * T, min(L, (sp + 1) * T)
-        n = t1 - t0
-        for h in range(4):
-            wm, wl, wo = [f(-np.inf)] * W, [f(0)] * W, [np.zeros(128, np.float32) for _ in range(W)]
-            for c in range((n + 15) // 16):
-                w = c % W
-                toks = range(t0 + 16 * c, min(t1, t0 + 16 * c + 16))
-                s_ = [score(h, t) for t in toks]
-                mn = max(wm[w], max(s_))
-                a = f(oracle.exp(f(wm[w] - mn)))
-                p = [f(oracle.exp(f(x - mn))) for x in s_]
-                cs = f(0)
-                for x in p:
-                    cs = f(cs + x)
-                wl[w] = fma(wl[w], a, cs)
-                o = (wo[w] * a).astype(np.float32)
-                for x, t in zip(p, toks):
-                    pb = f32(bf16(np.array([x], np.float32)))[0]
-                    vr = vf[table[t // 128], 0, t % 128]
-                    o = (np.float64(pb) * vr.astype(np.float64) + o.astype(np.float64)).astype(np.float32)
-                wo[w] = o
-                wm[w] = mn
-            M = max(wm)
-            Lsum, O = f(0), np.zeros(128, np.float32)
-            for w in range(W):
-                b = f(0) if wm[w] == -np.inf else f(oracle.exp(f(wm[w] - M)))
-                Lsum = fma(wl[w], b, Lsum)
-                O = (np.float64(b) * wo[w].astype(np.float64) + O.astype(np.float64)).astype(np.float32)
-            assert np.array_equal((O / Lsum).astype(np.float32).view(np.uint32), po[sp, h].view(np.uint32))
-            assert f(oracle.log(Lsum) + M).view(np.uint32) == pl[sp, h].view(np.uint32)
-
-
 def test_combine_single_split_identity(oracle):
     rng = np.random.default_rng(5)
     po = rng.standard_normal((1, 4, 128)).astype(np.float32)
