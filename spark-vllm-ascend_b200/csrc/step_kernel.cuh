@@ -368,15 +368,16 @@ __device__ __forceinline__ int stage_grp(int gi, int ngrp, int rot) {
   return g >= ngrp ? g - ngrp : g;
 }
 
-__device__ __forceinline__ void stage_x(const SparkStage& st, const Smem& s, int tid, unsigned long long* tr) {
-  const int k = st.k, nb = k >> 5, ngrp = k >> 3;
+__device__ __forceinline__ void stage_x(const SparkStage& st, const Smem& s, int tid, unsigned long long* tr, int x0,
+                                        int kx) {
+  const int k = st.k, nb = kx >> 5, ngrp = kx >> 3;
   uint32_t* xfrag32 = reinterpret_cast<uint32_t*>(s.scratch);
   int2* xmeta = reinterpret_cast<int2*>(s.scratch + 64 * nb);
   float* sq = reinterpret_cast<float*>(s.scratch + 72 * nb);
-  const uint16_t* arow = static_cast<const uint16_t*>(st.a);
-  if (st.embed) arow = static_cast<const uint16_t*>(st.embed) + (size_t)__ldcg(st.token) * k;
-  const float* parts = static_cast<const float*>(st.a);
-  const uint16_t* bb = static_cast<const uint16_t*>(st.b);
+  const uint16_t* arow = static_cast<const uint16_t*>(st.a) + x0;
+  if (st.embed) arow = static_cast<const uint16_t*>(st.embed) + (size_t)__ldcg(st.token) * k + x0;
+  const float* parts = static_cast<const float*>(st.a) + x0;
+  const uint16_t* bb = st.b ? static_cast<const uint16_t*>(st.b) + x0 : nullptr;
   const uint16_t* gm = reinterpret_cast<const uint16_t*>(s.scratch + 72 * nb + 4 * k);  // prefetched gamma
   float v[kStageGroups][8];
   uint4 gv[kStageGroups];
@@ -389,23 +390,29 @@ __device__ __forceinline__ void stage_x(const SparkStage& st, const Smem& s, int
   for (int r = 0; r < kStageGroups; r++) {
     const int g = stage_grp(tid + r * kConsumers, ngrp, rot);
     if (g < ngrp) {
+      uint4 bv = make_uint4(0, 0, 0, 0);
+      if (st.norm) {
+        if (bb) bv = __ldcg(reinterpret_cast<const uint4*>(bb + 8 * g));  // with the first loads
+        gv[r] = *reinterpret_cast<const uint4*>(gm + 8 * g);
+      }
       if (st.pro == SPARK_PRO_PARTS) {
-        // parts two at a time (two in flight per round trip), summed in part order
+        // parts in pairs (two in flight per round trip), summed in part order
         float4 p0 = __ldcg(reinterpret_cast<const float4*>(parts + 8 * g));
         float4 p1 = __ldcg(reinterpret_cast<const float4*>(parts + 8 * g + 4));
-        float4 n0, n1;
-        if (st.a_parts > 1) {
-          n0 = __ldcg(reinterpret_cast<const float4*>(parts + (size_t)k + 8 * g));
-          n1 = __ldcg(reinterpret_cast<const float4*>(parts + (size_t)k + 8 * g + 4));
-        }
-        for (int q = 1; q < st.a_parts; q++) {
-          const float4 q0 = n0, q1 = n1;
+        for (int q = 1; q < st.a_parts; q += 2) {
+          const float4 q0 = __ldcg(reinterpret_cast<const float4*>(parts + (size_t)q * k + 8 * g));
+          const float4 q1 = __ldcg(reinterpret_cast<const float4*>(parts + (size_t)q * k + 8 * g + 4));
+          float4 n0 = q0, n1 = q1;
           if (q + 1 < st.a_parts) {
             n0 = __ldcg(reinterpret_cast<const float4*>(parts + (size_t)(q + 1) * k + 8 * g));
             n1 = __ldcg(reinterpret_cast<const float4*>(parts + (size_t)(q + 1) * k + 8 * g + 4));
           }
           p0 = make_float4(__fadd_rn(p0.x, q0.x), __fadd_rn(p0.y, q0.y), __fadd_rn(p0.z, q0.z), __fadd_rn(p0.w, q0.w));
           p1 = make_float4(__fadd_rn(p1.x, q1.x), __fadd_rn(p1.y, q1.y), __fadd_rn(p1.z, q1.z), __fadd_rn(p1.w, q1.w));
+          if (q + 1 < st.a_parts) {
+            p0 = make_float4(__fadd_rn(p0.x, n0.x), __fadd_rn(p0.y, n0.y), __fadd_rn(p0.z, n0.z), __fadd_rn(p0.w, n0.w));
+            p1 = make_float4(__fadd_rn(p1.x, n1.x), __fadd_rn(p1.y, n1.y), __fadd_rn(p1.z, n1.z), __fadd_rn(p1.w, n1.w));
+          }
         }
         const float t8[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
 #pragma unroll
@@ -413,14 +420,11 @@ __device__ __forceinline__ void stage_x(const SparkStage& st, const Smem& s, int
       } else {
         unpack8(__ldcg(reinterpret_cast<const uint4*>(arow + 8 * g)), v[r]);
       }
-      if (st.norm) {
-        if (bb) {
-          float w8[8];
-          unpack8(__ldcg(reinterpret_cast<const uint4*>(bb + 8 * g)), w8);
+      if (st.norm && bb) {
+        float w8[8];
+        unpack8(bv, w8);
 #pragma unroll
-          for (int j = 0; j < 8; j++) v[r][j] = __fadd_rn(v[r][j], w8[j]);
-        }
-        gv[r] = *reinterpret_cast<const uint4*>(gm + 8 * g);
+        for (int j = 0; j < 8; j++) v[r][j] = __fadd_rn(v[r][j], w8[j]);
       }
     } else {
 #pragma unroll
@@ -663,9 +667,12 @@ __device__ __forceinline__ bool gemv_stage(const StepParams& P, const SparkStage
   const int ncta = gridDim.x, cta = blockIdx.x, warp = tid >> 5, lane = tid & 31;
   int u0;
   const int nl = local_units(st, cta, ncta, u0);
+  const bool part_x = !st.norm && st.kp > 1 && ncta % st.kp == 0;
+  const int kx = part_x ? st.k / st.kp : st.k;
   if (nl > 0 || (cta == 0 && st.res_out))
     stage_x(st, s, tid,
-            (tid == 0 && P.io.trace) ? P.io.trace + ((size_t)cta * P.num_stages + s.flag[2]) * kTraceSlots : nullptr);
+            (tid == 0 && P.io.trace) ? P.io.trace + ((size_t)cta * P.num_stages + s.flag[2]) * kTraceSlots : nullptr,
+            part_x ? (u0 % st.kp) * kx : 0, kx);
   consumer_bar();
   unsigned long long* tr = (tid == 0 && P.io.trace)
                                ? P.io.trace + ((size_t)cta * P.num_stages + s.flag[2]) * kTraceSlots
@@ -678,7 +685,7 @@ __device__ __forceinline__ bool gemv_stage(const StepParams& P, const SparkStage
   gd.kp_blocks = (st.k / st.kp) >> 5;
   gd.tps = (gd.kp_blocks >> 1) / ks;
   gd.xf = smem_u32(s.scratch);
-  gd.xm = gd.xf + 64 * (st.k >> 5);
+  gd.xm = gd.xf + 64 * (kx >> 5);
   for (int t = warp; t < nl * ks; t += kWarps) {
     const int j = t / ks, sl = t - j * ks;
     const uint32_t seq = seq_base + j;
@@ -689,7 +696,7 @@ __device__ __forceinline__ bool gemv_stage(const StepParams& P, const SparkStage
     const int u = u0 + j * ncta;
     const uint32_t slot = seq % kDesc;
     float acc0, acc1;
-    gemv_task(gd, smem_u32(s.ring) + s.desc_off[slot], u % gd.kp, sl, lane, acc0, acc1);
+    gemv_task(gd, smem_u32(s.ring) + s.desc_off[slot], part_x ? 0 : u % gd.kp, sl, lane, acc0, acc1);
     float* pr = s.partial + slot * kMaxSlices * 16;
     if ((lane & 3) == 0) {
       pr[sl * 16 + (lane >> 2)] = acc0;

@@ -7,7 +7,9 @@ Runs a synthetic model in persistent-step mode at context C, launches one traced
 kind, the median / max over CTAs of each phase averaged over layers, the barrier gap
 (last CTA done -> first CTA starting the next stage) and how far ahead of the
 consumers the producer started copying the stage's bytes.  GEMV phases: prologue
-(loads, RMSNorm, staging), tasks, tail.  Attention phases: scores, softmax, PV,
+(loads, RMSNorm, staging), tasks, tail.  The prologue is further split into
+loads (input vectors from L2), norm (sum of squares and 1/rms) and digits (fixed-point
+staging of the input plus the CTA barrier).  Attention phases: scores, softmax, PV,
 publish (+ waiting for the head's other splits), combine.
 """
 from __future__ import annotations
@@ -45,6 +47,14 @@ def summarize(t: np.ndarray, kinds: list[str]) -> dict:
             has = c[:, 4] > 0
             ph.update({"prologue": c[has, 4] - c[has, 1], "tasks": c[has, 5] - c[has, 4],
                        "tail": c[has, 2] - c[has, 5]})
+            ld = has & (c[:, 6] > 0)  # staging split: loads | RMSNorm | digits + barrier
+            nm = ld & (c[:, 7] > 0)
+            ph["loads"] = c[ld, 6] - c[ld, 1]
+            if nm.any():
+                ph["norm"] = c[nm, 7] - c[nm, 6]
+                ph["digits"] = c[nm, 4] - c[nm, 7]
+            else:
+                ph["digits"] = c[ld, 4] - c[ld, 6]
         for nm, v in ph.items():
             if v.size:
                 acc = d.setdefault(nm, [0.0, 0.0])
