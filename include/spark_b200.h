@@ -34,6 +34,7 @@ extern "C" {
 #define SPARK_ERR_ALIGNMENT 3
 #define SPARK_ERR_LAUNCH 4
 #define SPARK_ERR_TOO_LARGE 5
+#define SPARK_ERR_CUDA 6 /* a CUDA runtime call (allocation, IPC) failed */
 
 /* Library version (major * 10000 + minor * 100 + patch). */
 int spark_version(void);
@@ -247,8 +248,13 @@ typedef struct SparkStage {
   int32_t n, k, kp, ks;         /* GEMV rows, columns, K parts, slices per part (<= 4) */
   int32_t units, rot, wait, norm; /* units = n/16*kp; rot = first CTA; wait = stage to await (-1) */
   int32_t a_parts, block_size, nq, nkv;
-  int32_t head_dim, splits, max_split_tokens, reserved0;
-  float eps, inv_k, scale, reserved1;
+  int32_t head_dim, splits, max_split_tokens;
+  int32_t xchg;               /* tensor-parallel exchange stage (io->tp_size > 1): SPARK_EPI_PARTS writes
+                                 its part as part tp_rank * kp + kpi of `out` in EVERY rank's exchange
+                                 window, SPARK_EPI_ARGMAX takes the maximum into every rank's key, and
+                                 the stage's completion is counted on every rank; 0: local stage */
+  float eps, inv_k, scale;
+  int32_t row0;               /* SPARK_EPI_ARGMAX: global index of row 0 (vocab shard start), else 0 */
   const void* w;              /* T16 weight units */
   const void* a;              /* input (see SPARK_PRO_*) */
   const void* b;              /* residual added before the norm (nullable) */
@@ -286,6 +292,17 @@ typedef struct SparkStepIO {
                                  wait start, work start, work end, producer's first copy of the stage,
                                  then stage checkpoints (GEMV: tasks start, tasks end; attention:
                                  scores, softmax, PV, partials written); for profiling, nullable */
+  /* Tensor parallelism (one process per GPU, tp_size ranks; tp_size <= 1: single GPU).
+   * Each rank owns an exchange window (device memory holding `counters`, the parts
+   * buffers of the exchange stages and `key`), mapped into every peer's address space;
+   * a peer's copy of a window address is peer_windows[p] + (address - window).
+   * With tp_size > 1 the stage counters are never reset: a stage is complete once its
+   * counter reaches contributors * (launch + 1), contributors = CTAs * tp_size for an
+   * exchange stage, CTAs otherwise (launch = io->counters[num_stages + 2]). */
+  const unsigned long long* peer_windows; /* device uint64 [tp_size]: window base as mapped here */
+  const void* window;                     /* this rank's window base (host-visible value) */
+  unsigned long long window_bytes;
+  int32_t tp_size, tp_rank;
 } SparkStepIO;
 
 /* Bytes of a matrix in the T16 layout: n * k * 9 / 16. */
@@ -303,6 +320,19 @@ int spark_step_ring_bytes(void);
 
 /* Number of CTAs (one per SM) the step kernel runs with on the current device. */
 int spark_step_num_ctas(void);
+
+/* Exchange windows for tensor parallelism (one process per GPU).  A window is plain
+ * device memory from cudaMalloc (zeroed), so that its IPC handle maps the whole
+ * buffer; handles are CUDA IPC handles (SPARK_IPC_HANDLE_BYTES bytes) that the host
+ * side passes between the ranks (torch.distributed), and spark_ipc_open maps a
+ * peer's window with peer access enabled.  No counterpart in the reference, whose
+ * tensor-parallel path is vLLM's own (NCCL all-reduce after row-parallel layers). */
+#define SPARK_IPC_HANDLE_BYTES 64
+int spark_window_alloc(unsigned long long bytes, void** ptr);
+int spark_window_free(void* ptr);
+int spark_ipc_handle(const void* window, void* handle);
+int spark_ipc_open(const void* handle, void** ptr);
+int spark_ipc_close(void* ptr);
 
 /* Run a stage program as one cooperative launch.  host_stages is validated on the
  * host; the kernel reads dev_stages (an identical copy in device memory), or, for

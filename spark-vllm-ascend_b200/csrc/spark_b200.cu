@@ -232,6 +232,7 @@ const char* spark_status_string(int status) {
     case SPARK_ERR_ALIGNMENT: return "pointer alignment violated";
     case SPARK_ERR_LAUNCH: return "CUDA launch failed";
     case SPARK_ERR_TOO_LARGE: return "size exceeds the kernel's limit";
+    case SPARK_ERR_CUDA: return "CUDA runtime call failed (allocation or IPC)";
     default: return "unknown status";
   }
 }
@@ -648,6 +649,7 @@ static int check_stage(const SparkStage& s, int i, int ncta) {
         ((s.k / s.kp) / 64) % s.ks)
       return SPARK_ERR_UNSUPPORTED_SHAPE;
     if (s.units != s.n / 16 * s.kp || s.rot < 0 || s.rot >= ncta) return SPARK_ERR_INVALID_ARG;
+    if (s.row0 < 0 || (s.row0 && s.epi != SPARK_EPI_ARGMAX) || s.xchg < 0 || s.xchg > 1) return SPARK_ERR_INVALID_ARG;
     if (9 * (s.k / s.kp) > step::kRingBytes) return SPARK_ERR_TOO_LARGE;
     if (s.ks > step::kMaxSlices) return SPARK_ERR_UNSUPPORTED_SHAPE;
     if (72 * (s.k / 32) + (s.norm ? 6 * s.k : 0) > step::kScratchBytes) return SPARK_ERR_TOO_LARGE;
@@ -709,9 +711,78 @@ static int check_stage(const SparkStage& s, int i, int ncta) {
   return SPARK_OK;
 }
 
+int spark_window_alloc(unsigned long long bytes, void** ptr) {
+  if (!ptr || bytes == 0) return SPARK_ERR_INVALID_ARG;
+  *ptr = nullptr;
+  if (cudaMalloc(ptr, bytes) != cudaSuccess) return SPARK_ERR_CUDA;
+  if (cudaMemset(*ptr, 0, bytes) != cudaSuccess) {
+    cudaFree(*ptr);
+    *ptr = nullptr;
+    return SPARK_ERR_CUDA;
+  }
+  return SPARK_OK;
+}
+
+int spark_window_free(void* ptr) { return ptr && cudaFree(ptr) != cudaSuccess ? SPARK_ERR_CUDA : SPARK_OK; }
+
+int spark_ipc_handle(const void* window, void* handle) {
+  static_assert(sizeof(cudaIpcMemHandle_t) == SPARK_IPC_HANDLE_BYTES, "IPC handle size");
+  if (!window || !handle) return SPARK_ERR_INVALID_ARG;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, const_cast<void*>(window)) != cudaSuccess) return SPARK_ERR_CUDA;
+  memcpy(handle, &h, sizeof(h));
+  return SPARK_OK;
+}
+
+int spark_ipc_open(const void* handle, void** ptr) {
+  if (!handle || !ptr) return SPARK_ERR_INVALID_ARG;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  *ptr = nullptr;
+  return cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess ? SPARK_OK : SPARK_ERR_CUDA;
+}
+
+int spark_ipc_close(void* ptr) {
+  if (!ptr) return SPARK_ERR_INVALID_ARG;
+  return cudaIpcCloseMemHandle(ptr) == cudaSuccess ? SPARK_OK : SPARK_ERR_CUDA;
+}
+
+static bool in_window(const SparkStepIO& io, const void* p, unsigned long long bytes) {
+  const uintptr_t b = reinterpret_cast<uintptr_t>(io.window), a = reinterpret_cast<uintptr_t>(p);
+  return p && a >= b && a + bytes <= b + io.window_bytes;
+}
+
+// tensor-parallel wiring: exchange stages need the window, and what peers write into
+// (counters, parts, key) must lie inside it
+static int check_tp(const SparkStage* st, int num_stages, const SparkStepIO& io) {
+  bool any = false;
+  for (int i = 0; i < num_stages; i++) any = any || st[i].xchg;
+  if (io.tp_size <= 1) return any ? SPARK_ERR_INVALID_ARG : SPARK_OK;
+  if (io.tp_size > 64 || io.tp_rank < 0 || io.tp_rank >= io.tp_size || !io.peer_windows || !io.window)
+    return SPARK_ERR_INVALID_ARG;
+  if (!in_window(io, io.counters, sizeof(int32_t) * (num_stages + 3))) return SPARK_ERR_INVALID_ARG;
+  for (int i = 0; i < num_stages; i++) {
+    const SparkStage& s = st[i];
+    if (!s.xchg) continue;
+    if (s.kind != SPARK_STAGE_GEMV) return SPARK_ERR_INVALID_ARG;
+    if (s.epi == SPARK_EPI_PARTS) {
+      if (!in_window(io, s.out, 4ull * s.n * s.kp * io.tp_size)) return SPARK_ERR_INVALID_ARG;
+    } else if (s.epi == SPARK_EPI_ARGMAX) {
+      if (!in_window(io, s.key, 8) || (io.key && io.key != s.key)) return SPARK_ERR_INVALID_ARG;
+    } else {
+      return SPARK_ERR_INVALID_ARG;
+    }
+  }
+  return SPARK_OK;
+}
+
 int spark_step_run(const SparkStage* host_stages, const SparkStage* dev_stages, int num_stages, const SparkStepIO* io,
                    void* stream) {
   if (!host_stages || !io || !io->counters || num_stages <= 0) return SPARK_ERR_INVALID_ARG;
+  {
+    const int t = check_tp(host_stages, num_stages, *io);
+    if (t != SPARK_OK) return t;
+  }
   if (num_stages > 1 && !dev_stages) return SPARK_ERR_INVALID_ARG;
   if (dev_stages && (reinterpret_cast<uintptr_t>(dev_stages) & 15)) return SPARK_ERR_ALIGNMENT;
   const int ncta = num_sms();

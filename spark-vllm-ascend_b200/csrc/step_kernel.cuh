@@ -62,6 +62,11 @@ __device__ __forceinline__ int ld_acquire(const int* p) {
   asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
 __device__ __forceinline__ void consumer_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory"); }
 
 __device__ __forceinline__ bool mbar_wait_timed(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
@@ -181,6 +186,25 @@ __device__ __forceinline__ const SparkStage& stage_at(const StepParams& P, int i
   return P.stages ? P.stages[i] : P.inline_stage;
 }
 
+// ------------------------------------------------------------------ tensor parallelism
+// The same exchange-window address as mapped for rank p.
+template <typename T>
+__device__ __forceinline__ T* peer_addr(const SparkStepIO& io, int p, T* local) {
+  const unsigned long long off =
+      (unsigned long long)reinterpret_cast<uintptr_t>(local) - (unsigned long long)reinterpret_cast<uintptr_t>(io.window);
+  return reinterpret_cast<T*>((uintptr_t)(io.peer_windows[p] + off));
+}
+
+// Counter value at which stage `st` is complete in this launch.  Single GPU: counters
+// are zeroed between launches, so CTAs; tensor parallel: never reset, so
+// contributors x (launch + 1), compared wrap-safe.
+__device__ __forceinline__ int stage_target(const SparkStepIO& io, const SparkStage& st, int ncta, long long launch) {
+  if (io.tp_size <= 1) return ncta;
+  const int contrib = st.xchg ? ncta * io.tp_size : ncta;
+  return (int)((unsigned)contrib * (unsigned)(launch + 1));
+}
+__device__ __forceinline__ bool reached(int v, int target) { return (int)((unsigned)v - (unsigned)target) >= 0; }
+
 __device__ __forceinline__ void raise_abort(const StepParams& P, const Smem& s, int code) {
   *s.abort_flag = 1;
   atomicExch(P.io.counters + P.num_stages + 1, 1);
@@ -287,7 +311,7 @@ struct Producer {
 // (l) with k = 4(e-4)..; word 0 holds k 0..15, word 1 holds k 16..31.
 // meta = (-8 sum X, sx).  Four consecutive threads stage one block, 8 elements each.
 constexpr int kStageGroups = 4;  // 8-element groups per consumer thread (k <= 12288)
-constexpr int kMaxParts = 4;
+constexpr int kMaxParts = 8;  // parts summed by a PARTS prologue (K parts x TP ranks)
 
 __device__ __forceinline__ void lds_u32x4(uint32_t addr, uint4& v) {
   asm("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
@@ -579,8 +603,9 @@ __device__ __forceinline__ void gemv_task(const GemvDims& gd, uint32_t ubase, in
 __device__ __forceinline__ uint16_t bf16r(float v) { return f2bf(v); }
 
 // epilogue of one row pair (positions g and g + 8 of unit u)
-__device__ __forceinline__ void gemv_epilogue(const SparkStage& st, const long long* misc64, const uint16_t* rope_cs,
-                                              int u, int g, float v0, float v1, unsigned long long& best) {
+__device__ __forceinline__ void gemv_epilogue(const SparkStage& st, const SparkStepIO& io, const long long* misc64,
+                                              const uint16_t* rope_cs, int u, int g, float v0, float v1,
+                                              unsigned long long& best) {
   const int rg = u / st.kp, kpi = u - rg * st.kp;
   const int r0 = t16_row(st.rowmap, rg, g, st.n, st.head_dim);
   const int r1 = t16_row(st.rowmap, rg, g + 8, st.n, st.head_dim);
@@ -592,9 +617,18 @@ __device__ __forceinline__ void gemv_epilogue(const SparkStage& st, const long l
       break;
     }
     case SPARK_EPI_PARTS: {
-      float* y = static_cast<float*>(st.out) + (size_t)kpi * st.n;
-      y[r0] = v0;
-      y[r1] = v1;
+      if (st.xchg) {  // part tp_rank * kp + kpi, into every rank's window
+        float* y = static_cast<float*>(st.out) + (size_t)(io.tp_rank * st.kp + kpi) * st.n;
+        for (int p = 0; p < io.tp_size; p++) {
+          float* yp = peer_addr(io, p, y);
+          yp[r0] = v0;
+          yp[r1] = v1;
+        }
+      } else {
+        float* y = static_cast<float*>(st.out) + (size_t)kpi * st.n;
+        y[r0] = v0;
+        y[r1] = v1;
+      }
       break;
     }
     case SPARK_EPI_SILU_MUL: {
@@ -609,7 +643,7 @@ __device__ __forceinline__ void gemv_epilogue(const SparkStage& st, const long l
         static_cast<uint16_t*>(st.out)[r0] = b0;
         static_cast<uint16_t*>(st.out)[r1] = b1;
       }
-      const unsigned long long k0 = argmax_key(b0, r0), k1 = argmax_key(b1, r1);
+      const unsigned long long k0 = argmax_key(b0, st.row0 + r0), k1 = argmax_key(b1, st.row0 + r1);
       const unsigned long long k = k0 > k1 ? k0 : k1;
       best = k > best ? k : best;
       break;
@@ -717,7 +751,7 @@ __device__ __forceinline__ bool gemv_stage(const StepParams& P, const SparkStage
           v0 = __fadd_rn(v0, pr[q * 16 + lane]);
           v1 = __fadd_rn(v1, pr[q * 16 + lane + 8]);
         }
-        gemv_epilogue(st, s.misc64, s.rope_cs, u, lane, v0, v1, best);
+        gemv_epilogue(st, P.io, s.misc64, s.rope_cs, u, lane, v0, v1, best);
       }
       __syncwarp();
       if (lane == 0) {
@@ -738,7 +772,13 @@ __device__ __forceinline__ bool gemv_stage(const StepParams& P, const SparkStage
     if (tid == 0) {
       unsigned long long m = 0;
       for (int w = 0; w < kWarps; w++) m = s.red64[w] > m ? s.red64[w] : m;
-      if (m) atomicMax(st.key, m);
+      if (m) {
+        if (st.xchg) {
+          for (int p = 0; p < P.io.tp_size; p++) atomicMax_system(peer_addr(P.io, p, st.key), m);
+        } else {
+          atomicMax(st.key, m);
+        }
+      }
     }
   }
   seq_base += nl;
@@ -1027,11 +1067,15 @@ __device__ __forceinline__ bool attn_stage(const StepParams& P, const SparkStage
 // ------------------------------------------------------------------ the kernel
 __device__ __forceinline__ bool wait_stage(const StepParams& P, const Smem& s, int idx) {
   const int* ctr = P.io.counters + idx;
-  const int target = (int)gridDim.x;
-  if (ld_acquire(ctr) >= target) return true;
+  const SparkStage& w = stage_at(P, idx);
+  const int target = stage_target(P.io, w, (int)gridDim.x, s.misc64[2]);
+  // an exchange stage is counted by other GPUs: acquire at system scope
+  const bool sys = w.xchg != 0;
+  auto poll = [&]() { return reached(sys ? ld_acquire_sys(ctr) : ld_acquire(ctr), target); };
+  if (poll()) return true;
   const unsigned long long t0 = gtimer();
   for (;;) {  // each poll is one L2 round trip: spin without sleeping
-    if (ld_acquire(ctr) >= target) return true;
+    if (poll()) return true;
     if (ld_acquire(P.io.counters + P.num_stages + 1)) return false;
     if (gtimer() - t0 > kWaitNs) return false;
   }
@@ -1123,28 +1167,58 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepParams P) {
     consumer_bar();
     if (!ok) return;
     if (tid == 0 && tr) tr[2] = gtimer();
-    if (tid == 0 && !*s.abort_flag)  // release: the CTA's writes (ordered by the barrier) before the count
-      asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(P.io.counters + i) : "memory");
+    if (tid == 0 && !*s.abort_flag) {  // release: the CTA's writes (ordered by the barrier) before the count
+      if (st.xchg) {  // writes to every rank's window, then a count on every rank
+        asm volatile("fence.acq_rel.sys;" ::: "memory");
+        for (int p = 0; p < P.io.tp_size; p++)
+          asm volatile("red.relaxed.sys.global.add.s32 [%0], 1;" ::"l"(peer_addr(P.io, p, P.io.counters + i))
+                       : "memory");
+      } else {
+        asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(P.io.counters + i) : "memory");
+      }
+    }
   }
   // ---- the last CTA to finish turns the argmax into a token and resets the counters
+  // (tensor parallel: counts launches instead of resetting; the key is complete once
+  // every rank's CTAs have counted the last stage)
   if (tid == 0 && !*s.abort_flag) {
     __threadfence();
-    const int done = atomicAdd(P.io.counters + P.num_stages, 1);
-    if (done == (int)gridDim.x - 1) {
+    const SparkStepIO& io = P.io;
+    const int ncta = (int)gridDim.x;
+    const bool tp = io.tp_size > 1;
+    const int done = atomicAdd(io.counters + P.num_stages, 1);
+    const int last_done = tp ? (int)((unsigned)ncta * (unsigned)(s.misc64[2] + 1) - 1u) : ncta - 1;
+    if (done == last_done) {
       __threadfence();
-      const SparkStepIO& io = P.io;
-      if (io.key) {
-        const unsigned long long k = atomicAdd(io.key, 0ull);
-        const int32_t tok = (int32_t)(0xffffffffu - (uint32_t)(k & 0xffffffffull));
-        if (io.token_out) io.token_out[0] = tok;
-        if (io.token_log) io.token_log[io.step ? io.step[0] : 0] = tok;
-        *io.key = 0ull;
+      bool ok = true;
+      if (tp) {
+        const int li = P.num_stages - 1;
+        const SparkStage& ls = stage_at(P, li);
+        const int target = stage_target(io, ls, ncta, s.misc64[2]);
+        const unsigned long long t0 = gtimer();
+        while (!reached(ls.xchg ? ld_acquire_sys(io.counters + li) : ld_acquire(io.counters + li), target)) {
+          if (gtimer() - t0 > kWaitNs) {
+            ok = false;
+            break;
+          }
+        }
+        if (!ok) raise_abort(P, s, SPARK_ERR_LAUNCH);
       }
-      if (io.step) io.step[0] += 1;
-      if (io.pos) io.pos[0] += 1;
-      for (int i = 0; i <= P.num_stages; i++) P.io.counters[i] = 0;
-      P.io.counters[P.num_stages + 2] += 1;  // next launch's generation
-      __threadfence();
+      if (ok) {
+        if (io.key) {
+          const unsigned long long k = atomicAdd(io.key, 0ull);
+          const int32_t tok = (int32_t)(0xffffffffu - (uint32_t)(k & 0xffffffffull));
+          if (io.token_out) io.token_out[0] = tok;
+          if (io.token_log) io.token_log[io.step ? io.step[0] : 0] = tok;
+          *io.key = 0ull;
+        }
+        if (io.step) io.step[0] += 1;
+        if (io.pos) io.pos[0] += 1;
+        if (!tp)
+          for (int i = 0; i <= P.num_stages; i++) io.counters[i] = 0;
+        io.counters[P.num_stages + 2] += 1;  // next launch's generation
+        __threadfence();
+      }
     }
   }
 }

@@ -46,6 +46,11 @@ SIGNATURES: dict[str, list] = {
     "spark_step_ring_bytes": [],
     "spark_step_num_ctas": [],
     "spark_step_run": [_P, _P, _I, _P, _P],
+    "spark_window_alloc": [ctypes.c_uint64, ctypes.POINTER(_P)],
+    "spark_window_free": [_P],
+    "spark_ipc_handle": [_P, _P],
+    "spark_ipc_open": [_P, ctypes.POINTER(_P)],
+    "spark_ipc_close": [_P],
 }
 # entry points whose return value is a quantity, not a status
 RESTYPES = {"spark_t16_bytes": _I64}
@@ -56,8 +61,8 @@ class SparkStage(ctypes.Structure):
 
     _fields_ = [(n, ctypes.c_int32) for n in (
         "kind", "pro", "epi", "rowmap", "n", "k", "kp", "ks", "units", "rot", "wait", "norm", "a_parts",
-        "block_size", "nq", "nkv", "head_dim", "splits", "max_split_tokens", "reserved0")] + [
-        (n, ctypes.c_float) for n in ("eps", "inv_k", "scale", "reserved1")] + [
+        "block_size", "nq", "nkv", "head_dim", "splits", "max_split_tokens", "xchg")] + [
+        (n, ctypes.c_float) for n in ("eps", "inv_k", "scale")] + [("row0", ctypes.c_int32)] + [
         (n, _P) for n in (
             "w", "a", "b", "embed", "token", "gamma", "res_out", "out", "cos_sin", "pos", "block_table", "k_cache",
             "v_cache", "q", "kv_new", "key", "part_o", "part_lse", "head_counters", "attn_out")]
@@ -66,7 +71,9 @@ class SparkStage(ctypes.Structure):
 class SparkStepIO(ctypes.Structure):
     """Mirror of ``SparkStepIO`` in include/spark_b200.h."""
 
-    _fields_ = [(n, _P) for n in ("counters", "error", "key", "token_out", "token_log", "step", "pos", "trace")]
+    _fields_ = [(n, _P) for n in ("counters", "error", "key", "token_out", "token_log", "step", "pos", "trace",
+                                  "peer_windows", "window")] + [
+        ("window_bytes", ctypes.c_uint64), ("tp_size", ctypes.c_int32), ("tp_rank", ctypes.c_int32)]
 
 
 assert ctypes.sizeof(SparkStage) == 256

@@ -162,9 +162,13 @@ class DecodeEngine:
 
     def __init__(self, weights: SyntheticWeights, max_seq_len: int, splits: int = 0, num_blocks: int | None = None,
                  block_table: torch.Tensor | None = None, use_graph: bool = True, max_steps: int | None = None,
-                 seed: int = 0, mode: str = "step"):
+                 seed: int = 0, mode: str = "step", tp_group=None):
         """``mode`` "step": one persistent kernel per decode step (spark_b200.step);
-        "kernels": the per-stage kernel chain (5 kernels per layer + head + finalize)."""
+        "kernels": the per-stage kernel chain (5 kernels per layer + head + finalize).
+
+        Tensor parallel: ``weights`` is a ``tp.ShardWeights`` (rank r of tp) and every rank
+        constructs its engine at the same time (the exchange windows are connected over
+        torch.distributed, ``tp_group`` or the default group); persistent step only."""
         cfg = weights.cfg
         self.cfg, self.w = cfg, weights
         dev = weights.device
@@ -172,6 +176,12 @@ class DecodeEngine:
         if mode not in ("step", "kernels"):
             raise ValueError(f"unknown mode {mode!r}")
         self.mode = mode
+        self.tp_size = getattr(weights, "tp", 1)
+        self.tp_rank = getattr(weights, "rank", 0)
+        self.tp_group = tp_group
+        self.window = None
+        if self.tp_size > 1 and mode != "step":
+            raise ValueError("tensor parallelism runs on the persistent step (mode='step')")
         if mode == "step":
             from . import step as _step
             self.ncta = _step.num_ctas()
@@ -228,10 +238,11 @@ class DecodeEngine:
         if self.max_split_tokens > S.MAX_SPLIT_TOKENS:
             raise ValueError(f"{self.splits} splits give {self.max_split_tokens}-token splits (limit "
                              f"{S.MAX_SPLIT_TOKENS}); max_seq_len too large for the persistent step")
-        order = S.default_order(cfg, self.ncta)
+        tp = self.tp_size
+        order = S.default_order(cfg, self.ncta, tp)
         self.step_order = order
         ks_qkv, ks_o, ks_gu, ks_down, ks_head = order["ks"]
-        kp_o, kp_down = order["kp"]
+        kp_o, kp_down = order["kp_local"]
         # T16 copies of the weights (the gguf planes stay for the per-kernel path)
         self.t16 = []
         for lw in w.layers:
@@ -241,8 +252,18 @@ class DecodeEngine:
                              S.q4_pack_t16(lw.down.qs, lw.down.d, kp_down)))
         self.t16_head = S.q4_pack_t16(w.head.qs, w.head.d, 1)
         f32 = torch.float32
-        self.o_parts = torch.zeros((kp_o, h), dtype=f32, device=dev)
-        self.down_parts = torch.zeros((kp_down, h), dtype=f32, device=dev)
+        if tp > 1:  # what peers write lives in the exchange window
+            from . import tp as T
+            self.window = T.ExchangeWindow(T.window_fields(cfg, order, T.program_stages(cfg.num_layers), tp), dev,
+                                           self.tp_rank, tp)
+            self.window.exchange(self.tp_group)
+            self.o_parts, self.down_parts = self.window.t["o_parts"], self.window.t["down_parts"]
+            self.key = self.window.t["key"]
+        else:
+            self.o_parts = torch.zeros((kp_o, h), dtype=f32, device=dev)
+            self.down_parts = torch.zeros((kp_down, h), dtype=f32, device=dev)
+        xchg = tp > 1
+        pa_o, pa_down = tp * kp_o, tp * kp_down  # parts the next prologue sums, rank by rank
         self.kv_new = torch.zeros((2, nkv, D), dtype=BF16, device=dev)
         self.head_ctr = torch.zeros((cfg.num_layers, nkv), dtype=torch.int32, device=dev)
         prog = S.StepProgram(dev, self.ncta)
@@ -255,7 +276,7 @@ class DecodeEngine:
             if li == 0:
                 src = {"embed": w.embed, "token": self.token}
             else:
-                src = {"a": self.down_parts, "a_parts": kp_down, "b": self.resmid}
+                src = {"a": self.down_parts, "a_parts": pa_down, "b": self.resmid}
             qkv = prog.gemv(wq, cfg.qkv_rows, h, ks=ks_qkv, gamma=lw.in_norm, eps=eps, res_out=self.res_attn,
                             epi=S.EPI_ROPE_KV, rowmap=S.ROWS_PAIR_HALF, head_dim=D, rope=rope, wait=prev, **src)
             att = prog.attention(q=self.q, k_cache=kc, v_cache=vc, kv_new=self.kv_new, block_table=self.block_table,
@@ -264,18 +285,19 @@ class DecodeEngine:
                                  head_counters=self.head_ctr[li], attn_out=self.attn_out, nq=nq, nkv=nkv, head_dim=D,
                                  block_size=bs, wait=qkv)
             o = prog.gemv(wo, h, nq * D, kp=kp_o, ks=ks_o, a=self.attn_out, epi=S.EPI_PARTS, out=self.o_parts,
-                          wait=att)
-            gu = prog.gemv(wgu, 2 * i, h, ks=ks_gu, a=self.o_parts, a_parts=kp_o, b=self.res_attn,
+                          wait=att, xchg=xchg)
+            gu = prog.gemv(wgu, 2 * i, h, ks=ks_gu, a=self.o_parts, a_parts=pa_o, b=self.res_attn,
                            gamma=lw.post_norm, eps=eps, res_out=self.resmid, epi=S.EPI_SILU_MUL,
                            rowmap=S.ROWS_GATE_UP, out=self.mid, wait=o)
             prev = prog.gemv(wd, h, i, kp=kp_down, ks=ks_down, a=self.mid, epi=S.EPI_PARTS, out=self.down_parts,
-                             wait=gu)
-        prog.gemv(self.t16_head, cfg.vocab_size, h, ks=ks_head, a=self.down_parts, a_parts=kp_down, b=self.resmid,
-                  gamma=w.final_norm, eps=eps, epi=S.EPI_ARGMAX, out=self.logits, key=self.key, wait=prev)
-        prog.finalize()
+                             wait=gu, xchg=xchg)
+        prog.gemv(self.t16_head, cfg.vocab_size, h, ks=ks_head, a=self.down_parts, a_parts=pa_down, b=self.resmid,
+                  gamma=w.final_norm, eps=eps, epi=S.EPI_ARGMAX, out=self.logits, key=self.key, wait=prev,
+                  xchg=xchg, row0=getattr(w, "vocab_start", 0))
+        prog.finalize(self.window.t["counters"] if self.window is not None else None)
         self.program = prog
         self._io = prog.io(error=self.error, key=self.key, token_out=self.token, token_log=self.token_log,
-                           step=self.step_idx, pos=self.pos)
+                           step=self.step_idx, pos=self.pos, window=self.window)
 
     # -- the kernel sequence of one step, as prepared ctypes calls (no allocation)
     def _build_calls(self):
@@ -348,7 +370,15 @@ class DecodeEngine:
         self.graph = g
         return g
 
+    def _tp_barrier(self):
+        import torch.distributed as dist
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.tp_group)
+
     def reset(self, pos: int = 0):
+        """Rewind to position ``pos`` (tensor parallel: collective, every rank calls it)."""
+        if self.tp_size > 1:  # no rank may still be writing into a window being zeroed
+            self._tp_barrier()
         self.pos.fill_(pos)
         self.step_idx.zero_()
         self.key.zero_()
@@ -356,6 +386,17 @@ class DecodeEngine:
         if self.mode == "step":  # launch generation and head counters restart together
             self.program.reset_counters()
             self.head_ctr.zero_()
+        if self.tp_size > 1:
+            self._tp_barrier()
+
+    def close(self):
+        """Release the exchange window (tensor parallel: collective)."""
+        if self.window is not None:
+            self.graph = None
+            self._tp_barrier()
+            self.window.close()
+            self._tp_barrier()
+            self.window = None
 
     def oracle_order(self) -> dict | None:
         """The oracle evaluation order this engine's kernels follow (None: per-kernel order)."""

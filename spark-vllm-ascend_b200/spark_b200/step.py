@@ -27,6 +27,7 @@ EPI_BF16, EPI_PARTS, EPI_ROPE_KV, EPI_SILU_MUL, EPI_ARGMAX = range(5)
 ROWS_PLAIN, ROWS_PAIR_HALF, ROWS_GATE_UP = range(3)
 
 MAX_SLICES = 4  # slices per GEMV unit the kernel supports
+MAX_PARTS = 8  # fp32 parts a PARTS prologue sums (K parts x tensor-parallel ranks)
 CHUNK_ACCS = 11  # consumer warps of the kernel = attention PV chunk accumulators
 MAX_SPLIT_TOKENS = 1344
 
@@ -86,7 +87,11 @@ class StepProgram:
     # -- stage builders (return the stage index)
     def gemv(self, w: torch.Tensor, n: int, k: int, *, kp: int = 1, ks: int = 1, a=None, a_parts: int = 0,
              embed=None, token=None, b=None, gamma=None, eps: float = 0.0, res_out=None, epi: int = EPI_BF16,
-             rowmap: int = ROWS_PLAIN, out=None, wait: int = -1, head_dim: int = 0, key=None, rope=None) -> int:
+             rowmap: int = ROWS_PLAIN, out=None, wait: int = -1, head_dim: int = 0, key=None, rope=None,
+             xchg: bool = False, row0: int = 0) -> int:
+        """``xchg``: tensor-parallel exchange stage (parts / argmax key written to every
+        rank's window, completion counted on every rank); ``row0``: global index of row 0
+        for the argmax (vocab shard start)."""
         s = SparkStage()
         s.kind, s.epi, s.rowmap = STAGE_GEMV, epi, rowmap
         s.pro = PRO_PARTS if a_parts else PRO_BF16
@@ -100,6 +105,7 @@ class StepProgram:
         s.eps = eps
         s.inv_k = float(torch.tensor(1.0 / k, dtype=torch.float32))
         s.head_dim = head_dim
+        s.xchg, s.row0 = int(bool(xchg)), row0
         s.w, s.a, s.b, s.embed, s.token = _p(w), _p(a), _p(b), _p(embed), _p(token)
         s.gamma, s.res_out, s.out, s.key = _p(gamma), _p(res_out), _p(out), _p(key)
         if rope is not None:
@@ -127,23 +133,36 @@ class StepProgram:
         return len(self.stages) - 1
 
     # -- device copy
-    def finalize(self) -> "StepProgram":
+    def finalize(self, counters: torch.Tensor | None = None) -> "StepProgram":
+        """``counters``: int32 [stages + 3] to use (tensor parallel: inside the exchange
+        window), else allocated here."""
         n = len(self.stages)
         self.host = (SparkStage * n)(*self.stages)
         raw = torch.frombuffer(bytearray(bytes(self.host)), dtype=torch.uint8)
         self.dev = raw.to(self.device)
-        self.counters = torch.zeros(n + 3, dtype=torch.int32, device=self.device)
+        if counters is not None:
+            if counters.dtype != torch.int32 or counters.numel() < n + 3:
+                raise ValueError(f"counters must be int32 with at least {n + 3} entries")
+            self.counters = counters
+        else:
+            self.counters = torch.zeros(n + 3, dtype=torch.int32, device=self.device)
         return self
 
     def reset_counters(self) -> None:
         self.counters.zero_()
 
     def io(self, *, error=None, key=None, token_out=None, token_log=None, step=None, pos=None,
-           trace=None) -> SparkStepIO:
+           trace=None, window=None) -> SparkStepIO:
+        """``window``: the rank's connected ``tp.ExchangeWindow`` (tensor parallel)."""
         io = SparkStepIO()
         io.counters, io.error, io.key = _p(self.counters), _p(error), _p(key)
         io.token_out, io.token_log, io.step, io.pos = _p(token_out), _p(token_log), _p(step), _p(pos)
         io.trace = _p(trace)
+        if window is not None:
+            io.peer_windows, io.window = _p(window.peer_table), ctypes.c_void_p(window.ptr)
+            io.window_bytes, io.tp_size, io.tp_rank = window.nbytes, window.size, window.rank
+        else:
+            io.tp_size, io.tp_rank = 1, 0
         return io
 
     def trace_buffer(self) -> torch.Tensor:
@@ -178,16 +197,29 @@ def t16_gemv(x: torch.Tensor, w: torch.Tensor, n: int, k: int, kp: int = 1, ks: 
     return out
 
 
-def default_order(cfg, ncta: int) -> dict:
-    """Slice / part counts of the decode program (the oracle's persistent-step order)."""
+def _pick_kp(k: int, choices, tp: int) -> int:
+    for kp in choices:
+        if tp * kp <= MAX_PARTS and k % kp == 0 and (k // kp) % 64 == 0:
+            return kp
+    raise ValueError(f"no K part count fits k={k} at tp={tp}")
+
+
+def default_order(cfg, ncta: int, tp: int = 1) -> dict:
+    """Slice / part counts of the decode program (the oracle's persistent-step order).
+
+    ``cfg`` is the rank's local config (heads, intermediate size and vocab divided by
+    ``tp``).  "kp_local" are the K parts of o_proj / down on one rank; "kp" the parts of
+    the whole model (tp x kp_local: rank r's parts follow rank r - 1's), which is the
+    order the oracle restates."""
     h, i, nq, D, v = cfg.hidden_size, cfg.intermediate_size, cfg.num_q_heads, cfg.head_dim, cfg.vocab_size
-    kp_o = 2 if (nq * D // 2) % 64 == 0 else 1
-    kp_down = 4 if (i // 4) % 64 == 0 else (2 if (i // 2) % 64 == 0 else 1)
+    kp_o = _pick_kp(nq * D, (2, 1), tp)
+    kp_down = _pick_kp(i, (4, 2, 1), tp)
     qkv_n = (nq + 2 * cfg.num_kv_heads) * D
     return {
         "ks": (pick_ks(qkv_n, h, 1, 4, ncta), pick_ks(h, nq * D, kp_o, 4, ncta), pick_ks(2 * i, h, 1, 4, ncta),
                pick_ks(h, i, kp_down, 2, ncta), pick_ks(v, h, 1, 4, ncta)),
-        "kp": (kp_o, kp_down),
+        "kp": (tp * kp_o, tp * kp_down),
+        "kp_local": (kp_o, kp_down),
         "chunk_accs": CHUNK_ACCS,
     }
 

@@ -1,0 +1,52 @@
+"""Tensor-parallel decode on 2+ GPUs: the ranks' persistent step kernels exchange the
+o_proj / down_proj parts and the argmax key through each other's windows (peer
+stores), and the tokens / logits must be bit-identical to the CPU oracle in the
+order the ranks jointly compute.  Runs tests/tp_worker.py under
+torch.distributed.run with one process per GPU; skipped with fewer than 2 GPUs."""
+from __future__ import annotations
+
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _gpus() -> int:
+    import torch
+    return torch.cuda.device_count() if torch.cuda.is_available() else 0
+
+
+def _run(world: int, *args: str, timeout: int = 600) -> list[dict]:
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", MASTER_ADDR="127.0.0.1")
+    cmd = ["timeout", "-k", "30", str(timeout), sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           f"--nproc-per-node={world}", "--master-addr=127.0.0.1", "--master-port=29533",
+           os.path.join(HERE, "tp_worker.py"), *args]
+    p = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=timeout + 60)
+    lines = [json.loads(l) for l in p.stdout.splitlines() if l.startswith("{")]
+    assert p.returncode == 0, (p.returncode, p.stdout[-3000:], p.stderr[-3000:])
+    return lines
+
+
+@pytest.mark.parametrize("world", [2])
+def test_tp_tiny_64_tokens_match_oracle(cuda, world):
+    if _gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
+    res = _run(world, "--config", "tiny", "--new-tokens", "64")
+    assert len(res) == world and all(r["ok"] for r in res), res
+    r0 = next(r for r in res if r["rank"] == 0)
+    assert r0["oracle_tokens_equal"] and r0["oracle_logits_equal"]
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("world", [2])
+def test_tp_full_size_matches_oracle(cuda, world):
+    if _gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
+    res = _run(world, "--config", "full", "--prompt", "3", "--new-tokens", "3", "--max-seq", "512")
+    assert len(res) == world and all(r["ok"] for r in res), res

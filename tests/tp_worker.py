@@ -1,0 +1,104 @@
+"""One rank of the tensor-parallel decode parity run (launched by test_gpu_tp.py
+through torch.distributed.run, one process per GPU).
+
+Every rank builds the full synthetic weights from the same seed, keeps its shard
+(spark_b200.tp.ShardWeights), decodes greedily with the persistent step kernel and
+its in-kernel exchange, and checks that all ranks produced the same tokens.  Rank 0
+then replays the same prompt through the CPU oracle in the order the ranks jointly
+compute (tp x kp parts, the ranks' attention splits) and requires identical tokens
+and bit-identical logits (the vocab shards gathered from all ranks).
+
+    python -m torch.distributed.run --nproc-per-node 2 tests/tp_worker.py --new-tokens 64
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import sys
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, os.path.join(ROOT, "spark-vllm-ascend_b200"))
+sys.path.insert(0, ROOT)
+
+
+def u16(t):
+    return t.detach().contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--config", choices=["tiny", "full"], default="tiny")
+    ap.add_argument("--layers", type=int, default=0)
+    ap.add_argument("--prompt", type=int, default=24)
+    ap.add_argument("--new-tokens", type=int, default=64)
+    ap.add_argument("--max-seq", type=int, default=256)
+    ap.add_argument("--seed", type=int, default=1)
+    ap.add_argument("--no-oracle", action="store_true")
+    args = ap.parse_args(argv)
+
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", local))
+    from spark_b200 import tp as T
+    from spark_b200.config import SparkConfig, tiny_config
+    from spark_b200.model import DecodeEngine, SyntheticWeights
+
+    kw = {"num_layers": args.layers} if args.layers else {}
+    cfg = tiny_config(**kw) if args.config == "tiny" else SparkConfig(max_position=4096, **kw)
+    full = SyntheticWeights(cfg, device="cuda", seed=args.seed)
+    shard = T.ShardWeights(full, rank, world)
+    host_weights = full.to_numpy() if rank == 0 and not args.no_oracle else None
+    del full
+    eng = DecodeEngine(shard, max_seq_len=args.max_seq, num_blocks=4 * ((args.max_seq + 127) // 128),
+                       seed=args.seed, mode="step")
+    rng = np.random.default_rng(args.seed)
+    prompt = rng.integers(0, cfg.vocab_size, args.prompt).astype(np.int32)
+    toks = eng.generate(torch.from_numpy(prompt), args.new_tokens)
+    torch.cuda.synchronize()
+    err = int(eng.error.item())
+    logits = torch.from_numpy(u16(eng.logits).astype(np.int32)).cuda()
+    all_logits = [torch.empty_like(logits) for _ in range(world)]
+    dist.all_gather(all_logits, logits)
+    all_toks: list = [None] * world
+    dist.all_gather_object(all_toks, toks)
+    res = {"rank": rank, "world": world, "error": err, "splits": eng.splits, "order": eng.oracle_order(),
+           "ranks_agree": all(t == toks for t in all_toks), "tokens": toks[:8]}
+    ok = err == 0 and res["ranks_agree"]
+    if rank == 0 and not args.no_oracle:
+        import oracle
+        om = oracle.OracleModel(cfg, host_weights, num_blocks=eng.num_blocks, splits=eng.splits,
+                                order=eng.oracle_order())
+        table = eng.block_table.cpu().numpy()
+        pos, tok = 0, None
+        for t in prompt:
+            tok = om.step(table, int(t), pos)
+            pos += 1
+        ref, ref_logits = [tok], None
+        for i in range(args.new_tokens - 1):
+            want = i == args.new_tokens - 2
+            r = om.step(table, ref[-1], pos, want_logits=want)
+            if want:
+                r, ref_logits = r
+            ref.append(r)
+            pos += 1
+        got_logits = torch.cat(all_logits).cpu().numpy().astype(np.uint16)
+        res["oracle_tokens_equal"] = ref == toks
+        res["oracle_logits_equal"] = bool(ref_logits is not None and np.array_equal(got_logits, ref_logits))
+        ok = ok and res["oracle_tokens_equal"] and res["oracle_logits_equal"]
+    res["ok"] = ok
+    print(json.dumps(res), flush=True)
+    eng.close()
+    dist.barrier()
+    dist.destroy_process_group()
+    return 0 if ok else 1
+
+
+if __name__ == "__main__":
+    sys.exit(main())
