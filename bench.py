@@ -116,11 +116,15 @@ def build_engine(args, device, seed):
     from spark_b200.model import DecodeEngine, SyntheticWeights
     cfg = SparkConfig(num_layers=args.layers)
     w = SyntheticWeights(cfg, device=device, seed=seed)
+    if args.tp > 1:  # every rank built the same full weights (same seed): keep this rank's shard
+        from spark_b200.tp import ShardWeights
+        w = ShardWeights(w, int(os.environ.get("RANK", "0")), args.tp)
+        torch.cuda.empty_cache()
     max_seq = PROMPT_LEN + max(args.steps, args.warmup) + 1
     eng = DecodeEngine(w, max_seq_len=max_seq, splits=args.splits, num_blocks=(max_seq + 127) // 128 + 8,
                        max_steps=max(max_seq, args.steps + args.warmup + 8), seed=seed, mode=args.mode)
     torch.cuda.synchronize()
-    return cfg, w, eng
+    return w.cfg, w, eng
 
 
 def time_kernels(eng, reps: int = 3) -> dict:
@@ -215,8 +219,14 @@ def run_spark(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    cfg, w, eng = build_engine(args, device, seed=rank)
-    gen = torch.Generator().manual_seed(1234 + rank)
+    tp = args.tp
+    if tp > 1 and (world != tp or args.mode != "step"):
+        raise SystemExit("--tp N runs one tensor-parallel decode over all N ranks (torchrun with N processes) "
+                         "in --mode step")
+    # replicas: a different model and prompt per rank; tensor parallel: one model, one prompt
+    seed = 0 if tp > 1 else rank
+    cfg, w, eng = build_engine(args, device, seed=seed)
+    gen = torch.Generator().manual_seed(1234 + seed)
     prompt = torch.randint(0, cfg.vocab_size, (PROMPT_LEN,), generator=gen, dtype=torch.int32)
     eng.capture()
     first = eng.prefill(prompt)
@@ -296,6 +306,7 @@ def run_spark(args):
     if rank == 0:
         ctx_mid = PROMPT_LEN + args.steps // 2
         tpot = ms / args.steps
+        seqs = 1 if tp > 1 else world  # sequences decoded at once (tensor parallel: one)
         step_bytes = w.q4_bytes() + cfg.hidden_size * 2 + cfg.kv_bytes_per_token() * ctx_mid
         kb = kernel_bytes(cfg, ctx_mid)
         layers = cfg.num_layers
@@ -317,24 +328,26 @@ def run_spark(args):
                        "sample": f"failed: {exc}"}
         result = {
             "metric": METRIC,
-            "value": round(args.steps * world / (ms / 1e3), 3),
+            "value": round(args.steps * seqs / (ms / 1e3), 3),
             "unit": "tokens/s",
             "n_gpus": world,
             "steps": args.steps,
             "warmup": args.warmup,
             "ms_per_step": round(tpot, 5),
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": "strong" if tp > 1 else "weak",
             "vs_baseline": None,
             "dtype": "q4_0 weights x fp32 accumulate, bf16 activations / KV",
             "data": "synthetic: seeded N(0,0.02) weights -> Q4_0, 2048 uniform-random prompt ids",
-            "config": {"workload": "configs[2]: synthetic 4B Q4_0 batch-1 decode, 2048 prompt, greedy",
+            "config": {"workload": (f"configs[3]: synthetic 4B Q4_0 batch-1 decode, tensor parallel over {tp} GPUs, "
+                                    "2048 prompt, greedy") if tp > 1 else
+                       "configs[2]: synthetic 4B Q4_0 batch-1 decode, 2048 prompt, greedy",
                        "layers": layers, "hidden": cfg.hidden_size, "vocab": cfg.vocab_size, "prompt": PROMPT_LEN,
                        "ctx_range": [PROMPT_LEN, PROMPT_LEN + args.steps - 1], "splits": eng.splits,
                        "kernels_per_step": eng.kernels_per_step(), "mode": eng.mode,
-                       "parallelism": f"replicas x{world}",
+                       "parallelism": f"tp{tp}" if tp > 1 else f"replicas x{world}",
                        "l2": "inputs larger than L2 (2.26 GB of weights per step)"},
-            "e2e": {"value": round(args.steps * world / (e2e_ms / 1e3), 3), "unit": "tokens/s",
+            "e2e": {"value": round(args.steps * seqs / (e2e_ms / 1e3), 3), "unit": "tokens/s",
                     "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4, "wall_s": round(wall_e2e, 3),
                     "tokens_match_device_loop": e2e_tokens_match},
             "gpu_launches": eng.kernels_per_step() * args.steps,
@@ -440,6 +453,8 @@ def run_reference(args):
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--tp", type=int, default=1,
+                    help="tensor parallel over all ranks (configs[3]); default 1: independent replicas")
     ap.add_argument("--steps", type=int, default=4096)
     ap.add_argument("--warmup", type=int, default=16)
     ap.add_argument("--impl", choices=["spark", "reference"], default="spark")
