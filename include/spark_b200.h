@@ -310,7 +310,7 @@ int64_t spark_t16_bytes(int n, int k, int kp);
 
 /* Re-lay a Q4_0 matrix (qs / d planes) as T16 units.  rowmap SPARK_ROWS_*; aux =
  * head_dim for SPARK_ROWS_PAIR_HALF, unused otherwise.  Needs n % 16 == 0,
- * (k / kp) % 128 == 0.  Replaces the reference's offline packer
+ * (k / kp) % 64 == 0.  Replaces the reference's offline packer
  * (integration/weights.py:42-55, pack into its megakernel tile layout). */
 int spark_q4_pack_t16(const uint8_t* qs, const uint16_t* d, int n, int k, int kp, int rowmap, int aux, uint8_t* out,
                       void* stream);

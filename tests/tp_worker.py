@@ -40,6 +40,9 @@ def main(argv=None):
     ap.add_argument("--max-seq", type=int, default=256)
     ap.add_argument("--seed", type=int, default=1)
     ap.add_argument("--no-oracle", action="store_true")
+    ap.add_argument("--trace-ctx", type=int, default=0,
+                    help="after the parity run: rewind to this context, time 20 steps, then trace one step "
+                         "(per-stage timeline of rank 0, as spark_b200.step_trace prints it)")
     args = ap.parse_args(argv)
 
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
@@ -94,6 +97,29 @@ def main(argv=None):
         ok = ok and res["oracle_tokens_equal"] and res["oracle_logits_equal"]
     res["ok"] = ok
     print(json.dumps(res), flush=True)
+    if args.trace_ctx:
+        from spark_b200.step_trace import stage_kinds, summarize
+        eng.reset(args.trace_ctx)
+        eng.token.fill_(1)
+        for _ in range(4):
+            eng.step()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(20):
+            eng.step()
+        e1.record()
+        torch.cuda.synchronize()
+        tr = eng.program.trace_buffer()
+        dist.barrier()
+        eng.program.launch(eng.program.io(error=eng.error, key=eng.key, token_out=eng.token,
+                                          token_log=eng.token_log, step=eng.step_idx, pos=eng.pos,
+                                          window=eng.window, trace=tr))
+        torch.cuda.synchronize()
+        t = tr.cpu().numpy().astype(np.int64)
+        if rank == 0:
+            print(json.dumps({"trace_ctx": args.trace_ctx, "ms_per_step": round(e0.elapsed_time(e1) / 20, 4),
+                              "stages": summarize(t, stage_kinds(cfg.num_layers))}), flush=True)
     eng.close()
     dist.barrier()
     dist.destroy_process_group()
