@@ -40,7 +40,7 @@ def summarize(t: np.ndarray, kinds: list[str]) -> dict:
         d["stages"] += 1
         ph = {"work": c[:, 2] - c[:, 1], "producer_lead": c[:, 1] - c[:, 3]}
         if k == "attn":
-            has = c[:, 7] > 0
+            has = (c[:, 7] > 0) & (c[:, 6] > 0)  # splits with tokens (empty splits skip the phases)
             ph.update({"scores": c[has, 4] - c[has, 1], "softmax": c[has, 5] - c[has, 4], "pv": c[has, 6] - c[has, 5],
                        "publish_wait": c[has, 7] - c[has, 6], "combine": c[has, 2] - c[has, 7]})
         else:
