@@ -88,6 +88,12 @@ __device__ __forceinline__ bool mbar_wait_timed(uint32_t bar, uint32_t parity, v
   }
 }
 
+// float(P) without an int-to-float conversion: for |P| < 2^22 the bits of P + kMagic
+// are the fp32 1.5 * 2^23 + P, exactly; subtracting 1.5 * 2^23 leaves P exactly.
+// |P| <= 32 * 8 * 16320 < 2^22 for the staged digits (|X| <= 16320).
+constexpr int kMagic = 0x4B400000;
+constexpr float kMagicF = 12582912.0f;
+
 __device__ __forceinline__ void mma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                          uint32_t b1, int c1) {
   asm(
@@ -382,7 +388,10 @@ __device__ __forceinline__ void stage_group(const float (&v)[8], bool valid, int
     xfrag32[(b * 8 + (word & 3)) * 2 + (word >> 2)] = hh;
     xfrag32[(b * 8 + 4 + (word & 3)) * 2 + (word >> 2)] = ll;
   }
-  if (c == 0) xmeta[b] = make_int2(-8 * sum, __float_as_int(live ? __uint_as_float((uint32_t)(127 - S) << 23) : 1.0f));
+  // meta.x = -8 sum X + kMagic: the MMA's column-1 accumulator input, so that
+  // 256 D0 + D1 = P + kMagic is P as the low mantissa bits of 1.5 * 2^23 (|P| < 2^22)
+  if (c == 0)
+    xmeta[b] = make_int2(-8 * sum + kMagic, __float_as_int(live ? __uint_as_float((uint32_t)(127 - S) << 23) : 1.0f));
 }
 
 // group handled by slot gi of this CTA (out-of-range slots stay out of range)
@@ -525,6 +534,11 @@ __device__ __forceinline__ unsigned long long fmul2(unsigned long long a, unsign
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
+__device__ __forceinline__ unsigned long long fadd2(unsigned long long a, unsigned long long b) {
+  unsigned long long d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
 __device__ __forceinline__ unsigned long long ffma2(unsigned long long a, unsigned long long b, unsigned long long c) {
   unsigned long long d;
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
@@ -566,7 +580,8 @@ __device__ __forceinline__ void gemv_tiles(uint32_t& a_adr, uint32_t& d_adr, uin
       const float sx = __uint_as_float(Mt[2 * j + h].y);
       const unsigned long long sc =
           fmul2(f2pack(h2f((uint16_t)(hv & 0xffffu)), h2f((uint16_t)(hv >> 16))), f2pack(sx, sx));
-      acc = ffma2(sc, f2pack((float)(d[0] * 256 + d[1]), (float)(d[2] * 256 + d[3])), acc);
+      const unsigned long long pm = f2pack(__int_as_float(d[0] * 256 + d[1]), __int_as_float(d[2] * 256 + d[3]));
+      acc = ffma2(sc, fadd2(pm, f2pack(-kMagicF, -kMagicF)), acc);
     }
   }
   a_adr += NT * kTileBytes;

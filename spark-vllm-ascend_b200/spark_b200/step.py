@@ -216,8 +216,10 @@ def default_order(cfg, ncta: int, tp: int = 1) -> dict:
     kp_down = _pick_kp(i, (4, 2, 1), tp)
     qkv_n = (nq + 2 * cfg.num_kv_heads) * D
     return {
-        "ks": (pick_ks(qkv_n, h, 1, 4, ncta), pick_ks(h, nq * D, kp_o, 4, ncta), pick_ks(2 * i, h, 1, 4, ncta),
-               pick_ks(h, i, kp_down, 2, ncta), pick_ks(v, h, 1, 4, ncta)),
+        # 2 slices per unit everywhere: measured on the 36-layer step, 2 beats 4 (per-task
+        # overhead) and 1 (a warp per unit: 11 units in use at once overflow the ring)
+        "ks": (pick_ks(qkv_n, h, 1, 2, ncta), pick_ks(h, nq * D, kp_o, 2, ncta), pick_ks(2 * i, h, 1, 2, ncta),
+               pick_ks(h, i, kp_down, 2, ncta), pick_ks(v, h, 1, 2, ncta)),
         "kp": (tp * kp_o, tp * kp_down),
         "kp_local": (kp_o, kp_down),
         "chunk_accs": CHUNK_ACCS,
