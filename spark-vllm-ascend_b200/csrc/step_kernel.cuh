@@ -666,7 +666,6 @@ __device__ __forceinline__ void gemv_epilogue(const SparkStage& st, const SparkS
     default: {  // SPARK_EPI_ROPE_KV
       const int D = st.head_dim, half = D >> 1;
       const int hd = r0 / D, i = r0 - hd * D;
-      const int64_t pos = misc64[0];
       float a = bf2f(f2bf(v0)), b = bf2f(f2bf(v1));
       if (hd < st.nq + st.nkv) {
         const float c = bf2f(rope_cs[i]), sn = bf2f(rope_cs[i + half]);
