@@ -459,8 +459,8 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=16)
     ap.add_argument("--impl", choices=["spark", "reference"], default="spark")
     ap.add_argument("--splits", type=int, default=0, help="KV splits per layer (0 = auto)")
-    ap.add_argument("--mode", choices=["step", "kernels"], default="kernels",
-                    help="kernels: the per-stage kernel chain (faster today); step: one persistent kernel per token")
+    ap.add_argument("--mode", choices=["step", "kernels"], default="step",
+                    help="step: one persistent kernel per token (the faster engine); kernels: the per-stage kernel chain")
     ap.add_argument("--cpu-tokens", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--prompt", type=int, default=2048, help="prompt length (2048 = the benchmark protocol)")
