@@ -59,6 +59,7 @@ def lib():
             "orc_slot_mapping": (None, [_I64, _I64, _I64, _I64, _P, _P, _I64, _P]),
             "orc_split_tokens": (_I64, [_I64, _I]),
             "orc_t16_gemv_parts": (None, [_P, _P, _P, _I64, _I64, _I, _I, _P]),
+            "orc_q6k_dequantize": (None, [_P, _I64, _P]),
             "orc_t16_gemv": (None, [_P, _P, _P, _I64, _I64, _I, _I, _P]),
             "orc_parts_to_bf16": (None, [_P, _I, _I64, _P]),
             "orc_attn_split_w": (None, [_P, _P, _P, _P, _I64, _I, _I, _I, _I, _I, _F, _I, _P, _P]),
@@ -173,6 +174,14 @@ def t16_gemv_parts(x_bf16: np.ndarray, qs: np.ndarray, d: np.ndarray, kp: int, k
     lib().orc_t16_gemv_parts(_p(np.ascontiguousarray(xf)), _p(np.ascontiguousarray(qs)),
                              _p(np.ascontiguousarray(d)), n, k, kp, ks, _p(parts))
     return parts
+
+
+def q6k_dequantize(blocks: np.ndarray) -> np.ndarray:
+    """Q6_K super-blocks uint8 [..., 210] -> fp32 [n_blocks * 256] (gguf's decode)."""
+    b = np.ascontiguousarray(blocks, dtype=np.uint8).reshape(-1, 210)
+    w = np.empty(b.shape[0] * 256, np.float32)
+    lib().orc_q6k_dequantize(_p(b), b.shape[0], _p(w))
+    return w
 
 
 def parts_to_bf16(parts: np.ndarray) -> np.ndarray:

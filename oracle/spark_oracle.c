@@ -393,6 +393,34 @@ ORC_API void orc_t16_gemv_parts(const float* x, const uint8_t* qs, const uint16_
     free(xb);
 }
 
+/* ------------------------------------------------------------------ */
+/* Q6_K (ggml super-block of 256 weights, 210 bytes; restates gguf 0.19.0 */
+/* quants.Q6_K.dequantize_blocks, the decode the reference's head repack  */
+/* checks itself against, tools/deployment/prepare_head.py:23-26)         */
+/* ------------------------------------------------------------------ */
+/* Bytes 0..127: low nibbles, 128..191: 2-bit high parts, 192..207: int8 scales of the
+ * 16-weight sub-blocks, 208..209: fp16 d.  Weight e (0..255) of the block, half
+ * h = e / 128, l = e % 128: low = ql[64 h + l % 64] >> (4 (l / 64)) & 15, high =
+ * qh[32 h + l % 32] >> (2 (l / 32)) & 3, q = (low | high << 4) - 32;
+ * w = fp32(fp32(d) * sc[e / 16]) * q (two fp32 products). */
+static inline int q6k_code(const uint8_t* blk, int e) {
+    int h = e >> 7, l = e & 127;
+    int lo = (blk[64 * h + (l & 63)] >> (4 * (l >> 6))) & 15;
+    int hi = (blk[128 + 32 * h + (l & 31)] >> (2 * (l >> 5))) & 3;
+    return (lo | (hi << 4)) - 32;
+}
+
+ORC_API void orc_q6k_dequantize(const uint8_t* blocks, int64_t nblocks, float* w) {
+    for (int64_t b = 0; b < nblocks; b++) {
+        const uint8_t* blk = blocks + b * 210;
+        float d = h2f((uint16_t)(blk[208] | (blk[209] << 8)));
+        for (int e = 0; e < 256; e++) {
+            float sc = d * (float)(int8_t)blk[192 + (e >> 4)];
+            w[b * 256 + e] = sc * (float)q6k_code(blk, e);
+        }
+    }
+}
+
 /* y bf16 [n] = bf16(((p_0 + p_1) + ...) + p_{kp-1}) */
 ORC_API void orc_parts_to_bf16(const float* parts, int kp, int64_t n, uint16_t* y) {
     for (int64_t r = 0; r < n; r++) {

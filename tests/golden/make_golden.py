@@ -13,6 +13,13 @@ Fixtures written next to this script:
   and tools/deployment/prepare_model.py:63; ``unpack_q4`` (weights.py:34-40)
   reads the same byte layout.  Cases cover N(0, 0.02) weights, wide dynamic
   range, all-zero blocks, ties between +max and -max, and a negative absmax.
+* ``q6_k_gguf.npz`` -- seeded Q6_K super-blocks (256 weights, 210 bytes: 128 bytes of
+  low nibbles, 64 of 2-bit high parts, 16 int8 sub-block scales, an fp16 scale) and
+  ``gguf.quants.dequantize`` of them, the decode the reference's Q6_K head repack checks
+  itself against (tools/deployment/prepare_head.py:23-26).  gguf 0.19.0 has no Q6_K
+  quantizer, so the blocks are random bytes with chosen scales: N(0, 1e-3) fp16 scales,
+  zero, negative and extreme (+-65504, subnormal) scales, sub-block scales -128 / 127,
+  and a 131072 x 2560 row layout sample (10 blocks per row).
 * ``slot_mapping_kat.npz`` -- the known-answer cases of
   tools/validation/test_slot_mapping.py:13-53 (block sizes {128, 256, 512, 1024},
   reversed tables ``arange(320).flip(0) + 400 i``, token counts {0, 1, 1025,
@@ -67,6 +74,33 @@ def make_q4() -> None:
     np.savez_compressed(HERE / "q4_0_gguf.npz", **out)
 
 
+def q6k_blocks(rng, n: int) -> np.ndarray:
+    """n random Q6_K blocks (uint8 [n, 210]) with fp16 scales ~ N(0, 1e-3)."""
+    b = rng.integers(0, 256, size=(n, 210), dtype=np.uint8)
+    d = (rng.standard_normal(n) * 1e-3).astype(np.float16)
+    b[:, 208:210] = d.view(np.uint8).reshape(n, 2)
+    return b
+
+
+def make_q6k() -> None:
+    from gguf import GGMLQuantizationType as T
+    from gguf import quants
+
+    rng = np.random.default_rng(4321)
+    cases = {"normal": q6k_blocks(rng, 64)}
+    e = q6k_blocks(rng, 8)
+    d = np.array([0.0, -0.0, 65504.0, -65504.0, 6e-8, -3e-5, 1.0, -0.5], np.float16)
+    e[:, 208:210] = d.view(np.uint8).reshape(8, 2)
+    e[0:4, 192:208] = np.array([-128, 127] * 8, np.int8).view(np.uint8)
+    cases["edges"] = e
+    cases["rows"] = q6k_blocks(rng, 40)  # 4 rows of K = 2560 (10 blocks per row)
+    out = {}
+    for name, blocks in cases.items():
+        out[f"{name}.blocks"] = np.ascontiguousarray(blocks)
+        out[f"{name}.deq"] = np.ascontiguousarray(quants.dequantize(blocks, T.Q6_K), dtype=np.float32)
+    np.savez_compressed(HERE / "q6_k_gguf.npz", **out)
+
+
 def make_slots() -> None:
     maximum = 32768
     sizes = [128, 256, 512, 1024]
@@ -85,6 +119,7 @@ def make_slots() -> None:
 
 if __name__ == "__main__":
     make_q4()
+    make_q6k()
     make_slots()
     for p in sorted(HERE.glob("*.npz")):
         print(p.name, p.stat().st_size)

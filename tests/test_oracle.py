@@ -1,7 +1,8 @@
 """CPU tests that pin the oracle (oracle/spark_oracle.c) before it is trusted.
 
 * Q4_0 quantize / dequantize against the committed gguf 0.19.0 golden vectors
-  (tests/golden/q4_0_gguf.npz, made by tests/golden/make_golden.py).
+  (tests/golden/q4_0_gguf.npz, made by tests/golden/make_golden.py); the Q6_K decode
+  against gguf's (tests/golden/q6_k_gguf.npz).
 * Slot mapping against the reference test's known-answer cases
   (tests/golden/slot_mapping_kat.npz, from tools/validation/test_slot_mapping.py).
 * The canonical-order GEMV, attention, combine, norm, RoPE and SiLU against
@@ -47,6 +48,18 @@ def test_q4_dequantize_matches_gguf_golden(oracle):
         qs, d = oracle.q4_split(blocks, w.shape[0], w.shape[1])
         got = oracle.q4_dequantize(qs, d)
         assert np.array_equal(got.view(np.uint32), deq.reshape(got.shape).view(np.uint32)), n
+
+
+# ----------------------------------------------------------------------------- Q6_K golden vectors
+def test_q6k_dequantize_matches_gguf_golden(oracle):
+    """gguf 0.19.0 decode of random / edge-case Q6_K super-blocks, bit for bit."""
+    z = np.load(GOLDEN / "q6_k_gguf.npz")
+    names = sorted({k.split(".")[0] for k in z.files})
+    assert {"normal", "edges", "rows"} <= set(names)
+    for n in names:
+        got = oracle.q6k_dequantize(z[n + ".blocks"])
+        want = z[n + ".deq"].reshape(-1)
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), n
 
 
 def test_q4_split_join_roundtrip(oracle):
