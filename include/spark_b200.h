@@ -226,6 +226,8 @@ int spark_read_device_error(int* value, int reset);
 
 #define SPARK_STAGE_GEMV 0
 #define SPARK_STAGE_ATTN 1
+#define SPARK_STAGE_GEMV_Q6 2  /* GEMV over Q6_K weights in the T6 layout (spark_q6k_pack_t6); rowmap
+                                  SPARK_ROWS_PLAIN, (k / kp) % 256 == 0, otherwise as SPARK_STAGE_GEMV */
 
 /* GEMV prologue: where x comes from */
 #define SPARK_PRO_BF16 0  /* a: bf16 [k] (or embed row embed[*token] when embed != NULL) */
@@ -314,6 +316,18 @@ int64_t spark_t16_bytes(int n, int k, int kp);
  * (integration/weights.py:42-55, pack into its megakernel tile layout). */
 int spark_q4_pack_t16(const uint8_t* qs, const uint16_t* d, int n, int k, int kp, int rowmap, int aux, uint8_t* out,
                       void* stream);
+
+/* Q6_K weights for the persistent step (the reference's Q6_K LM head over the tied
+ * embedding, native/head/head_q6.asc + integration/head.py:6-31, repacked by
+ * tools/deployment/prepare_head.py:11-28).  `blocks` are gguf Q6_K rows, uint8
+ * [n][k / 256 * 210] (super-blocks of 256 weights: 128 B low nibbles, 64 B 2-bit high
+ * parts, 16 int8 sub-block scales, fp16 d).  The T6 layout cuts the matrix into units
+ * of 16 rows x k / kp columns, 105 (k / kp) / 8 bytes each, laid out for the integer
+ * tensor-core dot product of 32 weights (see csrc/step_kernel.cuh); lossless.
+ * spark_q6k_dequantize decodes gguf blocks to fp32 exactly like gguf 0.19.0. */
+int64_t spark_t6_bytes(int n, int k);
+int spark_q6k_pack_t6(const uint8_t* blocks, int n, int k, int kp, uint8_t* out, void* stream);
+int spark_q6k_dequantize(const uint8_t* blocks, int64_t nblocks, float* out, void* stream);
 
 /* Shared memory the step kernel keeps for the weight / KV ring (bytes). */
 int spark_step_ring_bytes(void);

@@ -60,6 +60,7 @@ def lib():
             "orc_split_tokens": (_I64, [_I64, _I]),
             "orc_t16_gemv_parts": (None, [_P, _P, _P, _I64, _I64, _I, _I, _P]),
             "orc_q6k_dequantize": (None, [_P, _I64, _P]),
+            "orc_q6k_gemv_parts": (None, [_P, _P, _I64, _I64, _I, _I, _P]),
             "orc_t16_gemv": (None, [_P, _P, _P, _I64, _I64, _I, _I, _P]),
             "orc_parts_to_bf16": (None, [_P, _I, _I64, _P]),
             "orc_attn_split_w": (None, [_P, _P, _P, _P, _I64, _I, _I, _I, _I, _I, _F, _I, _P, _P]),
@@ -182,6 +183,16 @@ def q6k_dequantize(blocks: np.ndarray) -> np.ndarray:
     w = np.empty(b.shape[0] * 256, np.float32)
     lib().orc_q6k_dequantize(_p(b), b.shape[0], _p(w))
     return w
+
+
+def q6k_gemv_parts(x_bf16: np.ndarray, blocks: np.ndarray, n: int, k: int, kp: int, ks: int) -> np.ndarray:
+    """Persistent-step Q6_K GEMV order: fp32 parts [kp, n] for gguf Q6_K rows
+    (uint8 [n, k / 256 * 210]) and bf16 x [k]."""
+    xf = bf16_to_f32(np.ascontiguousarray(x_bf16, dtype=np.uint16)).astype(np.float32)
+    parts = np.empty((kp, n), np.float32)
+    lib().orc_q6k_gemv_parts(_p(np.ascontiguousarray(xf)), _p(np.ascontiguousarray(blocks, dtype=np.uint8)), n, k,
+                             kp, ks, _p(parts))
+    return parts
 
 
 def parts_to_bf16(parts: np.ndarray) -> np.ndarray:

@@ -421,6 +421,48 @@ ORC_API void orc_q6k_dequantize(const uint8_t* blocks, int64_t nblocks, float* w
     }
 }
 
+/* Q6_K GEMV in the persistent step's order (T6 units).  x staged like the T16 GEMV
+ * (32-element blocks, S = 13 - e, sx = 2^-S, exact X).  Per 16-weight sub-block s:
+ * P = sum q X (exact, |P| < 2^24), scale = (fp32(d) * fp32(sc_s)) * sx, and two chains
+ * per slice: sub-blocks of even index into acc_e, odd into acc_o, each
+ * acc = fma(scale, float(P), acc) in ascending order; slice = acc_e + acc_o; the part
+ * is the slices summed in order (KS equal slices of the part's 32-weight tiles). */
+ORC_API void orc_q6k_gemv_parts(const float* x, const uint8_t* blocks, int64_t n, int64_t k, int kp, int ks,
+                                float* parts) {
+    int64_t nb = k / 32, nsb = k / 256;
+    xq_block* xb = (xq_block*)malloc(sizeof(xq_block) * nb);
+    for (int64_t b = 0; b < nb; b++) stage_block_s(x + b * 32, xb + b, 13);
+#pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < n; r++) {
+        const uint8_t* row = blocks + r * nsb * 210;
+        int64_t tpp = nb / kp, tps = tpp / ks;  /* 32-weight tiles per part / per slice */
+        for (int p = 0; p < kp; p++) {
+            float part = 0.0f;
+            for (int sl = 0; sl < ks; sl++) {
+                float acc[2] = {0.0f, 0.0f};
+                int64_t t0 = (int64_t)p * tpp + (int64_t)sl * tps;
+                for (int64_t t = t0; t < t0 + tps; t++) {
+                    const xq_block* xx = xb + t;
+                    for (int h = 0; h < 2; h++) {
+                        int64_t e0 = 32 * t + 16 * h;  /* first weight of the sub-block */
+                        const uint8_t* blk = row + (e0 / 256) * 210;
+                        int eb = (int)(e0 % 256);
+                        int32_t P = 0;
+                        for (int j = 0; j < 16; j++) P += q6k_code(blk, eb + j) * xx->X[16 * h + j];
+                        float d = h2f((uint16_t)(blk[208] | (blk[209] << 8)));
+                        float sc = (d * (float)(int8_t)blk[192 + (eb >> 4)]) * xx->sx;
+                        acc[h] = fmaf(sc, (float)P, acc[h]);
+                    }
+                }
+                float slice = acc[0] + acc[1];
+                part = sl == 0 ? slice : part + slice;
+            }
+            parts[(int64_t)p * n + r] = part;
+        }
+    }
+    free(xb);
+}
+
 /* y bf16 [n] = bf16(((p_0 + p_1) + ...) + p_{kp-1}) */
 ORC_API void orc_parts_to_bf16(const float* parts, int kp, int64_t n, uint16_t* y) {
     for (int64_t r = 0; r < n; r++) {

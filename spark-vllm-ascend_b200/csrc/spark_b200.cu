@@ -637,20 +637,50 @@ int spark_q4_pack_t16(const uint8_t* qs, const uint16_t* d, int n, int k, int kp
                 aux, out);
 }
 
+int64_t spark_t6_bytes(int n, int k) { return (int64_t)n * k * 105 / 128; }
+
+int spark_q6k_pack_t6(const uint8_t* blocks, int n, int k, int kp, uint8_t* out, void* stream) {
+  if (!blocks || !out) return SPARK_ERR_INVALID_ARG;
+  if (n <= 0 || k <= 0 || kp <= 0 || n % 16 || k % 256 || k % kp || (k / kp) % 256) return SPARK_ERR_UNSUPPORTED_SHAPE;
+  if (reinterpret_cast<uintptr_t>(out) & 15) return SPARK_ERR_ALIGNMENT;
+  const int64_t total = (int64_t)(n / 16) * kp * ((k / kp) / 64) * 32;
+  int64_t grid = (total + 255) / 256;
+  if (grid > 16 * num_sms()) grid = 16 * num_sms();
+  step::t6_pack_kernel<<<(unsigned)grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(blocks, n, k, kp, out);
+  return cudaGetLastError() == cudaSuccess ? SPARK_OK : SPARK_ERR_LAUNCH;
+}
+
+int spark_q6k_dequantize(const uint8_t* blocks, int64_t nblocks, float* out, void* stream) {
+  if (!blocks || !out || nblocks < 0) return SPARK_ERR_INVALID_ARG;
+  if (nblocks == 0) return SPARK_OK;
+  int64_t grid = (nblocks * 256 + 255) / 256;
+  if (grid > 16 * num_sms()) grid = 16 * num_sms();
+  step::q6k_dequant_kernel<<<(unsigned)grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(blocks, nblocks, out);
+  return cudaGetLastError() == cudaSuccess ? SPARK_OK : SPARK_ERR_LAUNCH;
+}
+
 int spark_step_ring_bytes(void) { return step::kRingBytes; }
 
 int spark_step_num_ctas(void) { return num_sms(); }
 
 static int check_stage(const SparkStage& s, int i, int ncta) {
   if (s.wait >= i || s.wait < -1) return SPARK_ERR_INVALID_ARG;
-  if (s.kind == SPARK_STAGE_GEMV) {
+  if (s.kind == SPARK_STAGE_GEMV_Q6) {  // Q6_K weights: plain rows, whole super-blocks per part
+    if (s.k <= 0 || s.kp <= 0 || s.k % s.kp || (s.k / s.kp) % 256 || s.rowmap != SPARK_ROWS_PLAIN)
+      return SPARK_ERR_UNSUPPORTED_SHAPE;
+    if (s.ks <= 0 || ((s.k / s.kp) / 32) % s.ks) return SPARK_ERR_UNSUPPORTED_SHAPE;
+    if (step::t6_unit_bytes(s.k / s.kp) > (uint32_t)step::kRingBytes) return SPARK_ERR_TOO_LARGE;
+    if (72 * (s.k / 32) + 6 * s.k + 8 * (s.k / 32) > step::kScratchBytes) return SPARK_ERR_TOO_LARGE;
+    if (s.epi != SPARK_EPI_BF16 && s.epi != SPARK_EPI_PARTS && s.epi != SPARK_EPI_ARGMAX) return SPARK_ERR_INVALID_ARG;
+  }
+  if (s.kind == SPARK_STAGE_GEMV || s.kind == SPARK_STAGE_GEMV_Q6) {
     if (!s.w || !s.a && !s.embed) return SPARK_ERR_INVALID_ARG;
     if (s.n <= 0 || s.n % 16 || s.k <= 0 || s.kp <= 0 || s.k % s.kp || (s.k / s.kp) % 64 || s.ks <= 0 ||
-        ((s.k / s.kp) / 64) % s.ks)
+        (s.kind == SPARK_STAGE_GEMV && ((s.k / s.kp) / 64) % s.ks))
       return SPARK_ERR_UNSUPPORTED_SHAPE;
     if (s.units != s.n / 16 * s.kp || s.rot < 0 || s.rot >= ncta) return SPARK_ERR_INVALID_ARG;
     if (s.row0 < 0 || (s.row0 && s.epi != SPARK_EPI_ARGMAX) || s.xchg < 0 || s.xchg > 1) return SPARK_ERR_INVALID_ARG;
-    if (9 * (s.k / s.kp) > step::kRingBytes) return SPARK_ERR_TOO_LARGE;
+    if (s.kind == SPARK_STAGE_GEMV && 9 * (s.k / s.kp) > step::kRingBytes) return SPARK_ERR_TOO_LARGE;
     if (s.ks > step::kMaxSlices) return SPARK_ERR_UNSUPPORTED_SHAPE;
     if (72 * (s.k / 32) + (s.norm ? 6 * s.k : 0) > step::kScratchBytes) return SPARK_ERR_TOO_LARGE;
     if (s.norm && (reinterpret_cast<uintptr_t>(s.gamma) & 15)) return SPARK_ERR_ALIGNMENT;
@@ -764,7 +794,7 @@ static int check_tp(const SparkStage* st, int num_stages, const SparkStepIO& io)
   for (int i = 0; i < num_stages; i++) {
     const SparkStage& s = st[i];
     if (!s.xchg) continue;
-    if (s.kind != SPARK_STAGE_GEMV) return SPARK_ERR_INVALID_ARG;
+    if (s.kind != SPARK_STAGE_GEMV && s.kind != SPARK_STAGE_GEMV_Q6) return SPARK_ERR_INVALID_ARG;
     if (s.epi == SPARK_EPI_PARTS) {
       if (!in_window(io, s.out, 4ull * s.n * s.kp * io.tp_size)) return SPARK_ERR_INVALID_ARG;
     } else if (s.epi == SPARK_EPI_ARGMAX) {

@@ -123,6 +123,9 @@ __host__ __device__ __forceinline__ int split_len(int64_t len, int splits) {
   return (int)((t + 15) / 16 * 16);
 }
 
+// bytes of a Q6_K unit in the T6 layout: 16 rows x kp_cols columns (6.5625 bits each)
+__host__ __device__ __forceinline__ uint32_t t6_unit_bytes(int kp_cols) { return (uint32_t)(105 * kp_cols / 8); }
+
 // number of units of a GEMV stage that CTA `cta` owns, and its first unit
 __host__ __device__ __forceinline__ int local_units(const SparkStage& s, int cta, int ncta, int& u0) {
   u0 = (cta - s.rot + ncta) % ncta;
@@ -262,10 +265,10 @@ struct Producer {
     for (int i = 0; i < P.num_stages; i++) {
       const SparkStage& st = stage_at(P, i);
       if (P.io.trace) P.io.trace[((size_t)cta * P.num_stages + i) * kTraceSlots + 3] = gtimer();
-      if (st.kind == SPARK_STAGE_GEMV) {
+      if (st.kind == SPARK_STAGE_GEMV || st.kind == SPARK_STAGE_GEMV_Q6) {
         int u0;
         const int nl = local_units(st, cta, ncta, u0);
-        const uint32_t ub = (uint32_t)(9 * (st.k / st.kp));
+        const uint32_t ub = (uint32_t)(st.kind == SPARK_STAGE_GEMV_Q6 ? t6_unit_bytes(st.k / st.kp) : 9 * (st.k / st.kp));
         for (int j = 0; j < nl; j++) {
           const unsigned char* src = static_cast<const unsigned char*>(st.w) + (size_t)(u0 + j * ncta) * ub;
           if (!issue(src, ub)) return drain();
@@ -354,7 +357,9 @@ __device__ __forceinline__ uint32_t pack_bytes(int x0, int x1, int x2, int x3) {
 
 // stage the 8 elements of group g (block g / 4, elements 8 (g % 4) ..); the 4 lanes of a
 // block are consecutive lanes of one warp and all execute this (valid or not)
-__device__ __forceinline__ void stage_group(const float (&v)[8], bool valid, int g, uint32_t* xfrag32, int2* xmeta) {
+// xmeta2 (nullable, Q6_K stages): (-32 sum of X over elements 0..15, over 16..31)
+__device__ __forceinline__ void stage_group(const float (&v)[8], bool valid, int g, uint32_t* xfrag32, int2* xmeta,
+                                            int2* xmeta2 = nullptr) {
   float M = 0.0f;
 #pragma unroll
   for (int j = 0; j < 8; j++) M = fmaxf(M, fabsf(v[j]));
@@ -370,8 +375,10 @@ __device__ __forceinline__ void stage_group(const float (&v)[8], bool valid, int
     X[j] = live ? __float2int_rn(__fmul_rn(v[j], sc)) : 0;
     sum += X[j];
   }
-  sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-  sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+  sum += __shfl_xor_sync(0xffffffffu, sum, 1);  // lanes 0, 1: X 0..15; lanes 2, 3: X 16..31
+  const int half_other = __shfl_xor_sync(0xffffffffu, sum, 2);
+  if (valid && xmeta2 && (g & 3) == 0) xmeta2[g >> 2] = make_int2(-32 * sum, -32 * half_other);
+  sum += half_other;
   if (!valid) return;
   const int b = g >> 2, c = g & 3;
 #pragma unroll
@@ -406,6 +413,8 @@ __device__ __forceinline__ void stage_x(const SparkStage& st, const Smem& s, int
   const int k = st.k, nb = kx >> 5, ngrp = kx >> 3;
   uint32_t* xfrag32 = reinterpret_cast<uint32_t*>(s.scratch);
   int2* xmeta = reinterpret_cast<int2*>(s.scratch + 64 * nb);
+  // Q6_K stages also need the half-block sums: after the norm area (squares, gamma)
+  int2* xmeta2 = st.kind == SPARK_STAGE_GEMV_Q6 ? reinterpret_cast<int2*>(s.scratch + 72 * nb + 6 * k) : nullptr;
   float* sq = reinterpret_cast<float*>(s.scratch + 72 * nb);
   const uint16_t* arow = static_cast<const uint16_t*>(st.a) + x0;
   if (st.embed) arow = static_cast<const uint16_t*>(st.embed) + (size_t)__ldcg(st.token) * k + x0;
@@ -513,7 +522,7 @@ __device__ __forceinline__ void stage_x(const SparkStage& st, const Smem& s, int
 #pragma unroll
   for (int r = 0; r < kStageGroups; r++) {
     const int g = stage_grp(tid + r * kConsumers, ngrp, rot);
-    if (r * kConsumers < ngrp) stage_group(v[r], g < ngrp, g, xfrag32, xmeta);
+    if (r * kConsumers < ngrp) stage_group(v[r], g < ngrp, g, xfrag32, xmeta, xmeta2);
   }
 }
 
@@ -594,6 +603,7 @@ __device__ __forceinline__ void gemv_tiles(uint32_t& a_adr, uint32_t& d_adr, uin
 struct GemvDims {
   int kp, kp_blocks, tps;  // K parts, blocks per part, tiles per slice
   uint32_t xf, xm;         // staged x fragments / block meta (shared addresses)
+  uint32_t xm2;            // Q6_K: half-block sums (shared address)
 };
 
 __device__ __forceinline__ void gemv_task(const GemvDims& gd, uint32_t ubase, int kpi, int sl, int lane, float& acc0,
@@ -613,6 +623,71 @@ __device__ __forceinline__ void gemv_task(const GemvDims& gd, uint32_t ubase, in
   for (; n >= 4; n -= 4) gemv_tiles<4>(a_adr, d_adr, b_adr, m_adr, acc);
   for (; n > 0; n--) gemv_tiles<1>(a_adr, d_adr, b_adr, m_adr, acc);
   f2unpack(acc, acc0, acc1);
+}
+
+// ------------------------------------------------------------------ Q6_K (T6 units)
+// Unit = 16 rows x Kp columns, 105 Kp / 8 bytes: the fp16 d of each 256-weight super-
+// block for row pairs (g, g + 8) [Kp/256][8][2], the int8 scale of each 16-weight
+// sub-block [Kp/16][8][2], then per 64 weights (two 32-weight tiles, one integer MMA
+// each) 768 B: lane L's nibble words (16 B: per tile N0, N1) and high-bit words (8 B:
+// per tile H).  For lane (g, c) of a tile, with A = q + 32 as u8:
+//   N0 byte i = low(row g, k 4c + i) | low(row g, k 16 + 4c + i) << 4   (a0 | a2)
+//   N1 byte i = the same for row g + 8                                    (a1 | a3)
+//   H  byte i = high(a0_i) | high(a1_i) << 2 | high(a2_i) << 4 | high(a3_i) << 6
+// (low = 4 bits, high = 2 bits).  B columns 0 / 1 carry the h / l digits of k 0..15
+// (sub-block 0), columns 2 / 3 those of k 16..31 (sub-block 1); the accumulator input
+// adds -32 sum X of the sub-block to its l column, so 256 D_h + D_l = sum q X.
+
+// one Q6_K slice: lanes 4g (c = 0) return rows g / g + 8: the even sub-blocks' chain
+// (c = 0) plus the odd sub-blocks' chain (c = 1)
+__device__ __forceinline__ void gemv_task_q6(const GemvDims& gd, uint32_t ubase, int kpi, int t0, int ntiles, int lane,
+                                             float& acc0, float& acc1) {
+  const int g = lane >> 2, c = lane & 3, n = lane >> 2;
+  const int kp_cols = gd.kp_blocks * 32;
+  const uint32_t d_pl = ubase, sc_pl = ubase + kp_cols / 8, grp = ubase + kp_cols / 8 + kp_cols;
+  // B: the T16 staging's digit entry of this lane, masked to the lane's column block
+  const uint32_t m0 = n < 2 ? 0xffffffffu : 0u, m1 = (n == 2 || n == 3) ? 0xffffffffu : 0u;
+  const uint32_t m = 0x0f0f0f0fu;
+  unsigned long long acc = 0ull;
+  int sb_cur = -1;
+  unsigned long long dpair = 0ull;
+  for (int t = t0; t < t0 + ntiles; t++) {
+    const int gb = kpi * gd.kp_blocks + t;  // x block of the tile
+    uint2 nib;
+    uint32_t H;
+    lds_u32x2(grp + (uint32_t)(t >> 1) * 768u + lane * 16 + (t & 1) * 8, nib);
+    asm("ld.shared.u32 %0, [%1];" : "=r"(H) : "r"(grp + (uint32_t)(t >> 1) * 768u + 512 + lane * 8 + (t & 1) * 4));
+    uint2 B;
+    lds_u32x2(gd.xf + (uint32_t)(gb * 8 + (lane & 7)) * 8, B);
+    uint2 mt, m2;
+    lds_u32x2(gd.xm + (uint32_t)gb * 8, mt);
+    lds_u32x2(gd.xm2 + (uint32_t)gb * 8, m2);
+    const uint32_t a0 = (nib.x & m) | ((H << 4) & 0x30303030u);
+    const uint32_t a2 = ((nib.x >> 4) & m) | (H & 0x30303030u);
+    const uint32_t a1 = (nib.y & m) | ((H << 2) & 0x30303030u);
+    const uint32_t a3 = ((nib.y >> 4) & m) | ((H >> 2) & 0x30303030u);
+    const int corr = c == 0 ? (int)m2.x : (c == 1 ? (int)m2.y : 0);
+    int d[4];
+    mma_u8s8(d, a0, a1, a2, a3, B.x & m0, B.y & m1, corr);
+    const int sb = t >> 3;  // super-block of the tile (8 tiles of 32)
+    if (sb != sb_cur) {
+      uint32_t dv;
+      asm("ld.shared.u32 %0, [%1];" : "=r"(dv) : "r"(d_pl + (uint32_t)sb * 32 + g * 4));
+      dpair = f2pack(h2f((uint16_t)(dv & 0xffffu)), h2f((uint16_t)(dv >> 16)));
+      sb_cur = sb;
+    }
+    uint16_t scv;
+    asm("ld.shared.u16 %0, [%1];" : "=h"(scv) : "r"(sc_pl + (uint32_t)(2 * t + (c & 1)) * 16 + g * 2));
+    const float sx = __uint_as_float(mt.y);
+    const unsigned long long scp =
+        fmul2(fmul2(dpair, f2pack((float)(int8_t)(scv & 0xff), (float)(int8_t)(scv >> 8))), f2pack(sx, sx));
+    acc = ffma2(scp, f2pack((float)(d[0] * 256 + d[1]), (float)(d[2] * 256 + d[3])), acc);
+  }
+  float e0, e1;
+  f2unpack(acc, e0, e1);
+  // chain of the odd sub-blocks (lane c = 1) onto the even one (lane c = 0)
+  acc0 = __fadd_rn(e0, __shfl_xor_sync(0xffffffffu, e0, 1));
+  acc1 = __fadd_rn(e1, __shfl_xor_sync(0xffffffffu, e1, 1));
 }
 
 __device__ __forceinline__ uint16_t bf16r(float v) { return f2bf(v); }
@@ -734,6 +809,7 @@ __device__ __forceinline__ bool gemv_stage(const StepParams& P, const SparkStage
   gd.tps = (gd.kp_blocks >> 1) / ks;
   gd.xf = smem_u32(s.scratch);
   gd.xm = gd.xf + 64 * (kx >> 5);
+  gd.xm2 = gd.xf + 72 * (kx >> 5) + 6 * st.k;  // Q6_K half-block sums (stage_x)
   for (int t = warp; t < nl * ks; t += kWarps) {
     const int j = t / ks, sl = t - j * ks;
     const uint32_t seq = seq_base + j;
@@ -744,7 +820,12 @@ __device__ __forceinline__ bool gemv_stage(const StepParams& P, const SparkStage
     const int u = u0 + j * ncta;
     const uint32_t slot = seq % kDesc;
     float acc0, acc1;
-    gemv_task(gd, smem_u32(s.ring) + s.desc_off[slot], part_x ? 0 : u % gd.kp, sl, lane, acc0, acc1);
+    if (st.kind == SPARK_STAGE_GEMV_Q6) {
+      const int tq = gd.kp_blocks / ks;  // 32-weight tiles per slice
+      gemv_task_q6(gd, smem_u32(s.ring) + s.desc_off[slot], part_x ? 0 : u % gd.kp, sl * tq, tq, lane, acc0, acc1);
+    } else {
+      gemv_task(gd, smem_u32(s.ring) + s.desc_off[slot], part_x ? 0 : u % gd.kp, sl, lane, acc0, acc1);
+    }
     float* pr = s.partial + slot * kMaxSlices * 16;
     if ((lane & 3) == 0) {
       pr[sl * 16 + (lane >> 2)] = acc0;
@@ -1130,8 +1211,9 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepParams P) {
       // values that are fixed for the whole launch (position, block table, RoPE table):
       // fetched before the stage barrier so their latency hides behind it
       const SparkStage& nx = stage_at(P, i);
-      const bool rope = nx.kind == SPARK_STAGE_GEMV && nx.epi == SPARK_EPI_ROPE_KV;
-      if (nx.kind == SPARK_STAGE_GEMV && nx.norm) {  // RMSNorm weight (a constant) next to the staging area
+      const bool gemv = nx.kind == SPARK_STAGE_GEMV || nx.kind == SPARK_STAGE_GEMV_Q6;
+      const bool rope = gemv && nx.epi == SPARK_EPI_ROPE_KV;
+      if (gemv && nx.norm) {  // RMSNorm weight (a constant) next to the staging area
         const uint4* src = static_cast<const uint4*>(nx.gamma);
         uint4* dst = reinterpret_cast<uint4*>(s.scratch + 72 * (nx.k >> 5) + 4 * nx.k);
         for (int q = tid; q < (nx.k >> 3); q += kConsumers) dst[q] = __ldg(src + q);
@@ -1176,7 +1258,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepParams P) {
     const SparkStage& st = *s.stage;
     // both stage functions keep every consumer on the same barriers; a stage that
     // fails returns false in all threads (attention: a split longer than the scratch)
-    const bool ok = st.kind == SPARK_STAGE_GEMV ? gemv_stage(P, st, s, seq_base, tid)
+    const bool ok = st.kind != SPARK_STAGE_ATTN ? gemv_stage(P, st, s, seq_base, tid)
                                                 : attn_stage(P, st, s, seq_base, tid);
     consumer_bar();
     if (!ok) return;
@@ -1268,6 +1350,87 @@ __global__ void t16_pack_kernel(const uint8_t* __restrict__ qs, const uint16_t* 
       dv.y = (uint32_t)d[(size_t)ra * nb + b0 + 1] | ((uint32_t)d[(size_t)rb * nb + b0 + 1] << 16);
       *reinterpret_cast<uint2*>(tile + 512 + 8 * g) = dv;
     }
+  }
+}
+
+// ------------------------------------------------------------------ T6 packing (Q6_K)
+__device__ __forceinline__ int q6k_code_dev(const uint8_t* blk, int e) {  // q + 32 of weight e
+  const int h = e >> 7, l = e & 127;
+  const int lo = (blk[64 * h + (l & 63)] >> (4 * (l >> 6))) & 15;
+  const int hi = (blk[128 + 32 * h + (l & 31)] >> (2 * (l >> 5))) & 3;
+  return lo | (hi << 4);
+}
+
+// blocks: gguf Q6_K rows [n][k / 256 * 210]; one thread per (unit, 64-weight group, lane)
+__global__ void t6_pack_kernel(const uint8_t* __restrict__ blocks, int n, int k, int kp, uint8_t* __restrict__ out) {
+  const int Kp = k / kp, groups = Kp >> 6;
+  const size_t row_bytes = (size_t)(k >> 8) * 210;
+  const size_t total = (size_t)(n >> 4) * kp * groups * 32;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int L = (int)(i & 31);
+    const size_t gi = i >> 5;
+    const int G = (int)(gi % groups);
+    const int u = (int)(gi / groups);
+    const int rg = u / kp, kpi = u - rg * kp;
+    const int g = L >> 2, c = L & 3;
+    const int ra = 16 * rg + g, rb = ra + 8;
+    const uint8_t* rowa = blocks + (size_t)ra * row_bytes;
+    const uint8_t* rowb = blocks + (size_t)rb * row_bytes;
+    uint8_t* unit = out + (size_t)u * t6_unit_bytes(Kp);
+    uint8_t* grp = unit + Kp / 8 + Kp + (size_t)G * 768;
+    uint32_t nibw[4], hw[2];
+#pragma unroll
+    for (int j = 0; j < 2; j++) {  // the two 32-weight tiles of the group
+      uint32_t n0 = 0, n1 = 0, h = 0;
+#pragma unroll
+      for (int b = 0; b < 4; b++) {
+        const int e0 = kpi * Kp + 64 * G + 32 * j + 4 * c + b;  // k = 4c + b (sub-block 0)
+        const int e2 = e0 + 16;                                  // k = 16 + 4c + b (sub-block 1)
+        const int qa0 = q6k_code_dev(rowa + (size_t)(e0 >> 8) * 210, e0 & 255);
+        const int qa2 = q6k_code_dev(rowa + (size_t)(e2 >> 8) * 210, e2 & 255);
+        const int qb0 = q6k_code_dev(rowb + (size_t)(e0 >> 8) * 210, e0 & 255);
+        const int qb2 = q6k_code_dev(rowb + (size_t)(e2 >> 8) * 210, e2 & 255);
+        n0 |= (uint32_t)((qa0 & 15) | ((qa2 & 15) << 4)) << (8 * b);
+        n1 |= (uint32_t)((qb0 & 15) | ((qb2 & 15) << 4)) << (8 * b);
+        h |= (uint32_t)((qa0 >> 4) | ((qb0 >> 4) << 2) | ((qa2 >> 4) << 4) | ((qb2 >> 4) << 6)) << (8 * b);
+      }
+      nibw[2 * j] = n0;
+      nibw[2 * j + 1] = n1;
+      hw[j] = h;
+    }
+    *reinterpret_cast<uint4*>(grp + 16 * L) = make_uint4(nibw[0], nibw[1], nibw[2], nibw[3]);
+    *reinterpret_cast<uint2*>(grp + 512 + 8 * L) = make_uint2(hw[0], hw[1]);
+    if (c == 0) {  // the group's 4 sub-block scales and (every 4 groups) the super-block d of rows ra, rb
+      const int e = kpi * Kp + 64 * G;
+      const uint8_t* ba = rowa + (size_t)(e >> 8) * 210;
+      const uint8_t* bb = rowb + (size_t)(e >> 8) * 210;
+#pragma unroll
+      for (int sbk = 0; sbk < 4; sbk++) {
+        const int s16 = ((e & 255) >> 4) + sbk;  // sub-block within the super-block
+        uint8_t* sc = unit + Kp / 8 + (size_t)(4 * G + sbk) * 16 + 2 * g;
+        sc[0] = ba[192 + s16];
+        sc[1] = bb[192 + s16];
+      }
+      if ((G & 3) == 0) {
+        uint8_t* dp = unit + (size_t)(G >> 2) * 32 + 4 * g;
+        dp[0] = ba[208];
+        dp[1] = ba[209];
+        dp[2] = bb[208];
+        dp[3] = bb[209];
+      }
+    }
+  }
+}
+
+// gguf Q6_K blocks -> fp32 weights, the decode of orc_q6k_dequantize (validation)
+__global__ void q6k_dequant_kernel(const uint8_t* __restrict__ blocks, int64_t nblocks, float* __restrict__ w) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nblocks * 256;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const uint8_t* blk = blocks + (i >> 8) * 210;
+    const int e = (int)(i & 255);
+    const float d = h2f((uint16_t)(blk[208] | (blk[209] << 8)));
+    const float sc = __fmul_rn(d, (float)(int8_t)blk[192 + (e >> 4)]);
+    w[i] = __fmul_rn(sc, (float)(q6k_code_dev(blk, e) - 32));
   }
 }
 

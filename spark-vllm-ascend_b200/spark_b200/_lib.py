@@ -46,6 +46,9 @@ SIGNATURES: dict[str, list] = {
     "spark_step_ring_bytes": [],
     "spark_step_num_ctas": [],
     "spark_step_run": [_P, _P, _I, _P, _P],
+    "spark_t6_bytes": [_I, _I],
+    "spark_q6k_pack_t6": [_P, _I, _I, _I, _P, _P],
+    "spark_q6k_dequantize": [_P, _I64, _P, _P],
     "spark_window_alloc": [ctypes.c_uint64, ctypes.POINTER(_P)],
     "spark_window_free": [_P],
     "spark_ipc_handle": [_P, _P],
@@ -53,7 +56,7 @@ SIGNATURES: dict[str, list] = {
     "spark_ipc_close": [_P],
 }
 # entry points whose return value is a quantity, not a status
-RESTYPES = {"spark_t16_bytes": _I64}
+RESTYPES = {"spark_t16_bytes": _I64, "spark_t6_bytes": _I64}
 
 
 class SparkStage(ctypes.Structure):

@@ -360,3 +360,15 @@ def _op_silu_mul(gu: torch.Tensor) -> torch.Tensor:
 @_op_silu_mul.register_fake
 def _(gu):
     return gu.new_empty((*gu.shape[:-1], gu.shape[-1] // 2))
+
+
+def q6k_dequantize(blocks: torch.Tensor) -> torch.Tensor:
+    """gguf Q6_K super-blocks (uint8 [..., 210] on the device) -> fp32 weights, the decode
+    of gguf 0.19.0 (``spark_q6k_dequantize``)."""
+    b = blocks.contiguous()
+    if b.dtype != torch.uint8 or b.numel() % 210:
+        raise ValueError("Q6_K blocks are uint8 rows of 210-byte super-blocks")
+    nb = b.numel() // 210
+    out = torch.empty(nb * 256, dtype=torch.float32, device=b.device)
+    call("spark_q6k_dequantize", _p(b), nb, _p(out), _stream())
+    return out

@@ -21,7 +21,7 @@ import torch
 
 from ._lib import SparkStage, SparkStepIO, call, lib
 
-STAGE_GEMV, STAGE_ATTN = 0, 1
+STAGE_GEMV, STAGE_ATTN, STAGE_GEMV_Q6 = 0, 1, 2
 PRO_BF16, PRO_PARTS = 0, 1
 EPI_BF16, EPI_PARTS, EPI_ROPE_KV, EPI_SILU_MUL, EPI_ARGMAX = range(5)
 ROWS_PLAIN, ROWS_PAIR_HALF, ROWS_GATE_UP = range(3)
@@ -61,6 +61,19 @@ def q4_pack_t16(qs: torch.Tensor, d: torch.Tensor, kp: int = 1, rowmap: int = RO
     return out
 
 
+def t6_bytes(n: int, k: int) -> int:
+    return n * k * 105 // 128
+
+
+def q6k_pack_t6(blocks: torch.Tensor, n: int, k: int, kp: int = 1) -> torch.Tensor:
+    """Re-lay gguf Q6_K rows (uint8 [n, k / 256 * 210], on the device) as T6 units."""
+    if blocks.dtype != torch.uint8 or blocks.numel() != n * (k // 256) * 210:
+        raise ValueError("blocks must be uint8 gguf Q6_K rows [n, k / 256 * 210]")
+    out = torch.empty(t6_bytes(n, k), dtype=torch.uint8, device=blocks.device)
+    call("spark_q6k_pack_t6", _p(blocks.contiguous()), n, k, kp, _p(out), _stream())
+    return out
+
+
 def pick_ks(n: int, k: int, kp: int, want: int, ncta: int) -> int:
     """Largest slice count <= want (and <= MAX_SLICES) that divides the unit's
     64-column tiles."""
@@ -88,12 +101,13 @@ class StepProgram:
     def gemv(self, w: torch.Tensor, n: int, k: int, *, kp: int = 1, ks: int = 1, a=None, a_parts: int = 0,
              embed=None, token=None, b=None, gamma=None, eps: float = 0.0, res_out=None, epi: int = EPI_BF16,
              rowmap: int = ROWS_PLAIN, out=None, wait: int = -1, head_dim: int = 0, key=None, rope=None,
-             xchg: bool = False, row0: int = 0) -> int:
+             xchg: bool = False, row0: int = 0, q6: bool = False) -> int:
         """``xchg``: tensor-parallel exchange stage (parts / argmax key written to every
         rank's window, completion counted on every rank); ``row0``: global index of row 0
-        for the argmax (vocab shard start)."""
+        for the argmax (vocab shard start); ``q6``: ``w`` holds Q6_K weights in the T6 layout
+        (``q6k_pack_t6``); slices then count 32-weight tiles."""
         s = SparkStage()
-        s.kind, s.epi, s.rowmap = STAGE_GEMV, epi, rowmap
+        s.kind, s.epi, s.rowmap = (STAGE_GEMV_Q6 if q6 else STAGE_GEMV), epi, rowmap
         s.pro = PRO_PARTS if a_parts else PRO_BF16
         s.n, s.k, s.kp, s.ks = n, k, kp, ks
         s.units = n // 16 * kp

@@ -62,6 +62,19 @@ def test_q6k_dequantize_matches_gguf_golden(oracle):
         assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), n
 
 
+def test_q6k_gemv_order_within_tolerance(oracle):
+    """The Q6_K GEMV order against a float64 dequantize-then-matmul of gguf's decode."""
+    z = np.load(GOLDEN / "q6_k_gguf.npz")
+    blocks = z["rows.blocks"].reshape(4, 10 * 210)  # 4 rows of K = 2560
+    rng = np.random.default_rng(0)
+    for amp in (1e-3, 1.0, 1e3):
+        x = bf16((rng.standard_normal(2560) * amp).astype(np.float32))
+        for kp, ks in ((1, 1), (1, 2), (2, 5)):
+            y = f32(oracle.parts_to_bf16(oracle.q6k_gemv_parts(x, blocks, 4, 2560, kp, ks)))
+            ref = oracle.q6k_dequantize(blocks).reshape(4, 2560).astype(np.float64) @ f32(x).astype(np.float64)
+            assert np.all(np.abs(y - ref) <= 1e-3 * amp + 1e-2 * np.abs(ref)), (amp, kp, ks)
+
+
 def test_q4_split_join_roundtrip(oracle):
     z = np.load(GOLDEN / "q4_0_gguf.npz")
     blocks = z["normal.blocks"]
