@@ -827,7 +827,10 @@ int spark_step_run(const SparkStage* host_stages, const SparkStage* dev_stages, 
   P.num_stages = num_stages;
   P.io = *io;
   if (!P.io.error) P.io.error = device_error_ptr();
-  if (set_smem(reinterpret_cast<const void*>(step::step_kernel), step::kSmemBytes) != kOk) return kErrLaunch;
+  bool q6 = false;  // Q6_K stages run in the kernel instantiation that has their code
+  for (int i = 0; i < num_stages; i++) q6 = q6 || host_stages[i].kind == SPARK_STAGE_GEMV_Q6;
+  void (*kernel)(const step::StepParams) = q6 ? step::step_kernel<true> : step::step_kernel<false>;
+  if (set_smem(reinterpret_cast<const void*>(kernel), step::kSmemBytes) != kOk) return kErrLaunch;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(ncta);
   cfg.blockDim = dim3(step::kThreads);
@@ -838,7 +841,7 @@ int spark_step_run(const SparkStage* host_stages, const SparkStage* dev_stages, 
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, step::step_kernel, P);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, P);
   return e == cudaSuccess ? SPARK_OK : SPARK_ERR_LAUNCH;
 }
 

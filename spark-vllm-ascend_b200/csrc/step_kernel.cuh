@@ -408,13 +408,14 @@ __device__ __forceinline__ int stage_grp(int gi, int ngrp, int rot) {
   return g >= ngrp ? g - ngrp : g;
 }
 
+template <bool Q6>
 __device__ __forceinline__ void stage_x(const SparkStage& st, const Smem& s, int tid, unsigned long long* tr, int x0,
                                         int kx) {
   const int k = st.k, nb = kx >> 5, ngrp = kx >> 3;
   uint32_t* xfrag32 = reinterpret_cast<uint32_t*>(s.scratch);
   int2* xmeta = reinterpret_cast<int2*>(s.scratch + 64 * nb);
   // Q6_K stages also need the half-block sums: after the norm area (squares, gamma)
-  int2* xmeta2 = st.kind == SPARK_STAGE_GEMV_Q6 ? reinterpret_cast<int2*>(s.scratch + 72 * nb + 6 * k) : nullptr;
+  int2* xmeta2 = (Q6 && st.kind == SPARK_STAGE_GEMV_Q6) ? reinterpret_cast<int2*>(s.scratch + 72 * nb + 6 * k) : nullptr;
   float* sq = reinterpret_cast<float*>(s.scratch + 72 * nb);
   const uint16_t* arow = static_cast<const uint16_t*>(st.a) + x0;
   if (st.embed) arow = static_cast<const uint16_t*>(st.embed) + (size_t)__ldcg(st.token) * k + x0;
@@ -786,6 +787,9 @@ __device__ __forceinline__ void finish_task(const Smem& s, uint32_t seq, int tas
   }
 }
 
+// Q6: the kernel instantiation that also runs SPARK_STAGE_GEMV_Q6 stages (programs
+// without them use the Q4-only instantiation, whose registers the Q6 code does not touch)
+template <bool Q6>
 __device__ __forceinline__ bool gemv_stage(const StepParams& P, const SparkStage& st, const Smem& s, uint32_t& seq_base, int tid) {
   const int ncta = gridDim.x, cta = blockIdx.x, warp = tid >> 5, lane = tid & 31;
   int u0;
@@ -793,7 +797,7 @@ __device__ __forceinline__ bool gemv_stage(const StepParams& P, const SparkStage
   const bool part_x = !st.norm && st.kp > 1 && ncta % st.kp == 0;
   const int kx = part_x ? st.k / st.kp : st.k;
   if (nl > 0 || (cta == 0 && st.res_out))
-    stage_x(st, s, tid,
+    stage_x<Q6>(st, s, tid,
             (tid == 0 && P.io.trace) ? P.io.trace + ((size_t)cta * P.num_stages + s.flag[2]) * kTraceSlots : nullptr,
             part_x ? (u0 % st.kp) * kx : 0, kx);
   consumer_bar();
@@ -820,7 +824,7 @@ __device__ __forceinline__ bool gemv_stage(const StepParams& P, const SparkStage
     const int u = u0 + j * ncta;
     const uint32_t slot = seq % kDesc;
     float acc0, acc1;
-    if (st.kind == SPARK_STAGE_GEMV_Q6) {
+    if (Q6 && st.kind == SPARK_STAGE_GEMV_Q6) {
       const int tq = gd.kp_blocks / ks;  // 32-weight tiles per slice
       gemv_task_q6(gd, smem_u32(s.ring) + s.desc_off[slot], part_x ? 0 : u % gd.kp, sl * tq, tq, lane, acc0, acc1);
     } else {
@@ -1176,6 +1180,7 @@ __device__ __forceinline__ bool wait_stage(const StepParams& P, const Smem& s, i
   }
 }
 
+template <bool Q6>
 __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepParams P) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const Smem s = carve(smem_raw);
@@ -1258,7 +1263,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepParams P) {
     const SparkStage& st = *s.stage;
     // both stage functions keep every consumer on the same barriers; a stage that
     // fails returns false in all threads (attention: a split longer than the scratch)
-    const bool ok = st.kind != SPARK_STAGE_ATTN ? gemv_stage(P, st, s, seq_base, tid)
+    const bool ok = st.kind != SPARK_STAGE_ATTN ? gemv_stage<Q6>(P, st, s, seq_base, tid)
                                                 : attn_stage(P, st, s, seq_base, tid);
     consumer_bar();
     if (!ok) return;
