@@ -639,51 +639,64 @@ __device__ __forceinline__ void gemv_task(const GemvDims& gd, uint32_t ubase, in
 // (sub-block 0), columns 2 / 3 those of k 16..31 (sub-block 1); the accumulator input
 // adds -32 sum X of the sub-block to its l column, so 256 D_h + D_l = sum q X.
 
+// NT consecutive 32-weight tiles starting at tile t (all in one 256-weight super-block):
+// all shared-memory loads, then the NT integer MMAs, then the scale / fma chain in tile
+// order (the same order as one tile at a time)
+template <int NT>
+__device__ __forceinline__ void q6_tiles(uint32_t grp, uint32_t sc_pl, uint32_t d_pl, const GemvDims& gd, int kpi,
+                                         int t, int lane, uint32_t m0, uint32_t m1, unsigned long long& acc) {
+  const int g = lane >> 2, c = lane & 3;
+  const uint32_t m = 0x0f0f0f0fu;
+  uint2 nib[NT], B[NT], mt[NT], m2[NT];
+  uint32_t H[NT];
+  uint16_t scv[NT];
+#pragma unroll
+  for (int j = 0; j < NT; j++) {
+    const int tt = t + j, gb = kpi * gd.kp_blocks + tt;
+    lds_u32x2(grp + (uint32_t)(tt >> 1) * 768u + lane * 16 + (tt & 1) * 8, nib[j]);
+    asm("ld.shared.u32 %0, [%1];" : "=r"(H[j]) : "r"(grp + (uint32_t)(tt >> 1) * 768u + 512 + lane * 8 + (tt & 1) * 4));
+    lds_u32x2(gd.xf + (uint32_t)(gb * 8 + (lane & 7)) * 8, B[j]);
+    lds_u32x2(gd.xm + (uint32_t)gb * 8, mt[j]);
+    lds_u32x2(gd.xm2 + (uint32_t)gb * 8, m2[j]);
+    asm("ld.shared.u16 %0, [%1];" : "=h"(scv[j]) : "r"(sc_pl + (uint32_t)(2 * tt + (c & 1)) * 16 + g * 2));
+  }
+  uint32_t dv;
+  asm("ld.shared.u32 %0, [%1];" : "=r"(dv) : "r"(d_pl + (uint32_t)(t >> 3) * 32 + g * 4));
+  int D[NT][4];
+#pragma unroll
+  for (int j = 0; j < NT; j++) {
+    const uint32_t a0 = (nib[j].x & m) | ((H[j] << 4) & 0x30303030u);
+    const uint32_t a2 = ((nib[j].x >> 4) & m) | (H[j] & 0x30303030u);
+    const uint32_t a1 = (nib[j].y & m) | ((H[j] << 2) & 0x30303030u);
+    const uint32_t a3 = ((nib[j].y >> 4) & m) | ((H[j] >> 2) & 0x30303030u);
+    const int corr = c == 0 ? (int)m2[j].x : (c == 1 ? (int)m2[j].y : 0);
+    mma_u8s8(D[j], a0, a1, a2, a3, B[j].x & m0, B[j].y & m1, corr);
+  }
+  const unsigned long long dpair = f2pack(h2f((uint16_t)(dv & 0xffffu)), h2f((uint16_t)(dv >> 16)));
+#pragma unroll
+  for (int j = 0; j < NT; j++) {
+    const float sx = __uint_as_float(mt[j].y);
+    const unsigned long long scp =
+        fmul2(fmul2(dpair, f2pack((float)(int8_t)(scv[j] & 0xff), (float)(int8_t)(scv[j] >> 8))), f2pack(sx, sx));
+    acc = ffma2(scp, f2pack((float)(D[j][0] * 256 + D[j][1]), (float)(D[j][2] * 256 + D[j][3])), acc);
+  }
+}
+
 // one Q6_K slice: lanes 4g (c = 0) return rows g / g + 8: the even sub-blocks' chain
 // (c = 0) plus the odd sub-blocks' chain (c = 1)
 __device__ __forceinline__ void gemv_task_q6(const GemvDims& gd, uint32_t ubase, int kpi, int t0, int ntiles, int lane,
                                              float& acc0, float& acc1) {
-  const int g = lane >> 2, c = lane & 3, n = lane >> 2;
+  const int n = lane >> 2;
   const int kp_cols = gd.kp_blocks * 32;
   const uint32_t d_pl = ubase, sc_pl = ubase + kp_cols / 8, grp = ubase + kp_cols / 8 + kp_cols;
   // B: the T16 staging's digit entry of this lane, masked to the lane's column block
   const uint32_t m0 = n < 2 ? 0xffffffffu : 0u, m1 = (n == 2 || n == 3) ? 0xffffffffu : 0u;
-  const uint32_t m = 0x0f0f0f0fu;
   unsigned long long acc = 0ull;
-  int sb_cur = -1;
-  unsigned long long dpair = 0ull;
-  for (int t = t0; t < t0 + ntiles; t++) {
-    const int gb = kpi * gd.kp_blocks + t;  // x block of the tile
-    uint2 nib;
-    uint32_t H;
-    lds_u32x2(grp + (uint32_t)(t >> 1) * 768u + lane * 16 + (t & 1) * 8, nib);
-    asm("ld.shared.u32 %0, [%1];" : "=r"(H) : "r"(grp + (uint32_t)(t >> 1) * 768u + 512 + lane * 8 + (t & 1) * 4));
-    uint2 B;
-    lds_u32x2(gd.xf + (uint32_t)(gb * 8 + (lane & 7)) * 8, B);
-    uint2 mt, m2;
-    lds_u32x2(gd.xm + (uint32_t)gb * 8, mt);
-    lds_u32x2(gd.xm2 + (uint32_t)gb * 8, m2);
-    const uint32_t a0 = (nib.x & m) | ((H << 4) & 0x30303030u);
-    const uint32_t a2 = ((nib.x >> 4) & m) | (H & 0x30303030u);
-    const uint32_t a1 = (nib.y & m) | ((H << 2) & 0x30303030u);
-    const uint32_t a3 = ((nib.y >> 4) & m) | ((H >> 2) & 0x30303030u);
-    const int corr = c == 0 ? (int)m2.x : (c == 1 ? (int)m2.y : 0);
-    int d[4];
-    mma_u8s8(d, a0, a1, a2, a3, B.x & m0, B.y & m1, corr);
-    const int sb = t >> 3;  // super-block of the tile (8 tiles of 32)
-    if (sb != sb_cur) {
-      uint32_t dv;
-      asm("ld.shared.u32 %0, [%1];" : "=r"(dv) : "r"(d_pl + (uint32_t)sb * 32 + g * 4));
-      dpair = f2pack(h2f((uint16_t)(dv & 0xffffu)), h2f((uint16_t)(dv >> 16)));
-      sb_cur = sb;
-    }
-    uint16_t scv;
-    asm("ld.shared.u16 %0, [%1];" : "=h"(scv) : "r"(sc_pl + (uint32_t)(2 * t + (c & 1)) * 16 + g * 2));
-    const float sx = __uint_as_float(mt.y);
-    const unsigned long long scp =
-        fmul2(fmul2(dpair, f2pack((float)(int8_t)(scv & 0xff), (float)(int8_t)(scv >> 8))), f2pack(sx, sx));
-    acc = ffma2(scp, f2pack((float)(d[0] * 256 + d[1]), (float)(d[2] * 256 + d[3])), acc);
-  }
+  int t = t0;
+  const int te = t0 + ntiles;
+  for (; t < te && (t & 3); t++) q6_tiles<1>(grp, sc_pl, d_pl, gd, kpi, t, lane, m0, m1, acc);
+  for (; t + 4 <= te; t += 4) q6_tiles<4>(grp, sc_pl, d_pl, gd, kpi, t, lane, m0, m1, acc);
+  for (; t < te; t++) q6_tiles<1>(grp, sc_pl, d_pl, gd, kpi, t, lane, m0, m1, acc);
   float e0, e1;
   f2unpack(acc, e0, e1);
   // chain of the odd sub-blocks (lane c = 1) onto the even one (lane c = 0)

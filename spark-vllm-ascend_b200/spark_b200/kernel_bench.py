@@ -175,6 +175,31 @@ def bench_step_gemv(name, n, k, kind, reps, copies, device, gen, cfg):
     return {"us": round(us, 3), "bytes": byts, "gbs": round(byts / us / 1e3, 1), "copies": copies, "kp": kp, "ks": ks}
 
 
+def bench_step_q6_head(reps, copies, device, gen, n=131072, k=2560, ks=2):
+    """The Q6_K LM head of the Spark checkpoint (tied embedding, 131072 x 2560) as a
+    persistent-step GEMV stage with the argmax epilogue (T6 units)."""
+    from . import step as S
+    wb = S.t6_bytes(n, k)
+    copies = max(1, min(copies, math.ceil(400e6 / wb)))
+    x = torch.randn(k, device=device).to(BF16)
+    key = torch.zeros(1, device=device, dtype=torch.int64)
+    out = torch.empty(n, device=device, dtype=BF16)
+    progs = []
+    for _ in range(copies):
+        blk = torch.randint(0, 256, (n * (k // 256), 210), device=device, dtype=torch.uint8, generator=gen)
+        d = (torch.randn(n * (k // 256), device=device, generator=gen) * 2e-5).to(torch.float16)
+        blk[:, 208:210] = d.view(torch.uint8).view(-1, 2)
+        w = S.q6k_pack_t6(blk, n, k)
+        del blk
+        p = S.StepProgram(device)
+        p.gemv(w, n, k, ks=ks, a=x, epi=S.EPI_ARGMAX, out=out, key=key, q6=True)
+        p.finalize()
+        progs.append((p, p.io(key=key)))
+    us = _time(lambda t: progs[t % copies][0].launch(progs[t % copies][1]), reps)
+    byts = wb + 2 * k + 2 * n
+    return {"us": round(us, 3), "bytes": byts, "gbs": round(byts / us / 1e3, 1), "copies": copies, "ks": ks}
+
+
 def bench_step_attn(ctx, reps, copies, device, gen, cfg):
     """The attention stage of the persistent decode-step kernel as its own launch
     (splits = CTAs / kv heads, distributed combine)."""
@@ -229,6 +254,8 @@ def main(argv=None):
             n, k, kind = cases[name]
             fn = bench_step_gemv if args.step else bench_gemv
             out[name] = fn(name, n, k, kind, args.reps, args.copies, device, gen, cfg)
+        elif name == "head_q6" and args.step:
+            out[name] = bench_step_q6_head(args.reps, args.copies, device, gen)
         elif name == "attn":
             for ctx in map(int, args.ctx.split(",")):
                 out[f"attn_{ctx}"] = (bench_step_attn(ctx, args.reps, args.copies, device, gen, cfg) if args.step else

@@ -1,5 +1,6 @@
 """GPU parity of the vLLM plugin classes (the drop-in boundary): the spark_q4_0 linear
-method and the attention backend's decode / prefill paths, against the oracle."""
+method, the attention backend's decode / prefill paths and the Q6_K LM head method,
+against the oracle."""
 from __future__ import annotations
 
 import math
@@ -122,3 +123,35 @@ def test_attention_backend_prefill_causal(cuda, oracle):
             p = np.exp(s - s.max())
             ref = p @ V / p.sum()
             assert np.max(np.abs(got[i, h] - ref)) <= 2e-2
+
+
+def test_q6_head_method_decode_matches_oracle(cuda, oracle):
+    """The Q6_K LM head over a tied bf16 embedding (reference integration/head.py): one
+    decode token runs the Q6_K GEMV bit-exactly in the oracle's order; other shapes take
+    vLLM's bf16 path; a weight that is not the decode of the codes is refused."""
+    import torch
+    from spark_b200.plugin.head import install_q6_head
+    rng = np.random.default_rng(6)
+    vocab, hidden = 4096, 2560
+    blocks = rng.integers(0, 256, size=(vocab * hidden // 256, 210), dtype=np.uint8)
+    blocks[:, 208:210] = (rng.standard_normal(blocks.shape[0]) * 2e-5).astype(np.float16).view(np.uint8).reshape(-1, 2)
+    weight = oracle.q6k_dequantize(blocks).reshape(vocab, hidden)
+    head = torch.nn.Module()
+    head.weight = torch.nn.Parameter(torch.from_numpy(weight).cuda().to(torch.bfloat16), requires_grad=False)
+    tblocks = torch.from_numpy(blocks.reshape(vocab, -1)).cuda()
+    bad = torch.nn.Module()
+    bad.weight = torch.nn.Parameter(head.weight.detach().clone(), requires_grad=False)
+    bad.weight.data[3, 7] += 1.0
+    with pytest.raises(ValueError):
+        install_q6_head(bad, tblocks)
+    method = install_q6_head(head, tblocks)
+    x = torch.randn((1, hidden), device="cuda").to(torch.bfloat16)
+    for _ in range(2):  # the stage counters are left ready for the next call
+        y = method.apply(head, x)
+        assert y.shape == (1, vocab)
+        want = oracle.parts_to_bf16(oracle.q6k_gemv_parts(u16(x), blocks.reshape(vocab, -1), vocab, hidden, 1, 4))
+        assert np.array_equal(u16(y).reshape(-1), want)
+    x2 = torch.randn((3, hidden), device="cuda").to(torch.bfloat16)
+    y2 = method.apply(head, x2).float()
+    ref = x2.float() @ head.weight.float().t()
+    assert torch.allclose(y2, ref, rtol=2e-2, atol=2e-2)
