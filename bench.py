@@ -171,7 +171,7 @@ def time_kernels(eng, reps: int = 3) -> dict:
 # algorithmic bytes.  The captures (gate_up ring GEMV, split-KV attention at ctx 6144,
 # an 8-layer persistent step) are summarised under profiles/.
 NCU_TRAFFIC_RATIO = {"gate_up": 28_079_360 / 28_051_456, "attn": 25_295_360 / 25_182_208,
-                     "step": 683_313_152 / 675_087_360}
+                     "step": 680_050_944 / 675_087_360}
 
 
 def kernel_bytes(cfg, ctx: int) -> dict:
