@@ -732,7 +732,7 @@ static int check_stage(const SparkStage& s, int i, int ncta) {
     return SPARK_ERR_INVALID_ARG;
   if (s.head_dim != 128 || s.nkv <= 0 || s.nq != 4 * s.nkv || s.block_size <= 0 || s.block_size % step::kRunTokens)
     return SPARK_ERR_UNSUPPORTED_SHAPE;
-  if (s.splits <= 0 || s.nkv * s.splits > ncta) return SPARK_ERR_UNSUPPORTED_SHAPE;
+  if (s.splits <= 0 || s.splits > 4096) return SPARK_ERR_UNSUPPORTED_SHAPE;  // (kv head, split) tasks round-robin
   if (s.max_split_tokens <= 0 || s.max_split_tokens > step::kMaxSplitTokens) return SPARK_ERR_TOO_LARGE;
   if ((reinterpret_cast<uintptr_t>(s.kv_new) | reinterpret_cast<uintptr_t>(s.k_cache) |
        reinterpret_cast<uintptr_t>(s.v_cache) | reinterpret_cast<uintptr_t>(s.part_o) |
@@ -827,9 +827,17 @@ int spark_step_run(const SparkStage* host_stages, const SparkStage* dev_stages, 
   P.num_stages = num_stages;
   P.io = *io;
   if (!P.io.error) P.io.error = device_error_ptr();
-  bool q6 = false;  // Q6_K stages run in the kernel instantiation that has their code
-  for (int i = 0; i < num_stages; i++) q6 = q6 || host_stages[i].kind == SPARK_STAGE_GEMV_Q6;
-  void (*kernel)(const step::StepParams) = q6 ? step::step_kernel<true> : step::step_kernel<false>;
+  // Q6_K stages, and attention stages with more (kv head, split) tasks than CTAs, run in
+  // the kernel instantiations that have their code
+  bool q6 = false, multi = false;
+  for (int i = 0; i < num_stages; i++) {
+    const SparkStage& h = host_stages[i];
+    q6 = q6 || h.kind == SPARK_STAGE_GEMV_Q6;
+    multi = multi || (h.kind == SPARK_STAGE_ATTN && (int64_t)h.nkv * h.splits > ncta);
+  }
+  void (*kernel)(const step::StepParams) =
+      q6 ? (multi ? step::step_kernel<true, true> : step::step_kernel<true, false>)
+         : (multi ? step::step_kernel<false, true> : step::step_kernel<false, false>);
   if (set_smem(reinterpret_cast<const void*>(kernel), step::kSmemBytes) != kOk) return kErrLaunch;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(ncta);

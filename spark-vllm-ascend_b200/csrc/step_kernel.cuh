@@ -132,14 +132,6 @@ __host__ __device__ __forceinline__ int local_units(const SparkStage& s, int cta
   return u0 < s.units ? (s.units - u0 + ncta - 1) / ncta : 0;
 }
 
-// attention task of CTA `cta`: kv head g and split j, or false
-__host__ __device__ __forceinline__ bool attn_task(const SparkStage& s, int cta, int& g, int& j) {
-  if (cta >= s.nkv * s.splits) return false;
-  g = cta / s.splits;
-  j = cta - g * s.splits;
-  return true;
-}
-
 // ------------------------------------------------------------------ shared memory
 struct Smem {
   unsigned char* ring;
@@ -260,6 +252,8 @@ struct Producer {
     return true;
   }
 
+  // Multi: attention tasks may outnumber the CTAs (several per CTA)
+  template <bool Multi>
   __device__ void run() {
     const int ncta = gridDim.x, cta = blockIdx.x;
     for (int i = 0; i < P.num_stages; i++) {
@@ -274,24 +268,35 @@ struct Producer {
           if (!issue(src, ub)) return drain();
         }
       } else {
-        int g, j;
-        if (!attn_task(st, cta, g, j)) continue;
+        // this CTA's tasks (kv head g, split j) in the consumers' order: K then V runs each
+        const int S = st.splits, ntask = st.nkv * S;
         const int64_t len = st.pos[0] + 1;
-        const int T = split_len(len, st.splits);
+        const int T = split_len(len, S);
         if (T > kMaxSplitTokens) return drain();
-        const int64_t t0 = (int64_t)j * T, t1 = t0 + T < len ? t0 + T : len;
-        if (t1 <= t0) continue;
-        const int64_t w0 = t0 / kRunTokens, nruns = (t1 - 1) / kRunTokens - w0 + 1;
-        const int D = st.head_dim, bs = st.block_size, nkv = st.nkv;
-        for (int side = 0; side < 2; side++) {
-          const uint16_t* cache = static_cast<const uint16_t*>(side ? st.v_cache : st.k_cache);
-          for (int64_t r = 0; r < nruns; r++) {
-            const int64_t rs = (w0 + r) * kRunTokens > t0 ? (w0 + r) * kRunTokens : t0;
-            const int64_t re = (w0 + r + 1) * kRunTokens < t1 ? (w0 + r + 1) * kRunTokens : t1;
-            const int64_t page = st.block_table[rs / bs];
-            const uint16_t* src = cache + ((page * nkv + g) * bs + (rs % bs)) * D;
-            if (!issue(src, (uint32_t)((re - rs) * D * 2))) return drain();
+        // K then V runs of task t; false: aborted
+        auto task = [&](int t) -> bool {
+          const int g = t / S, j = t - g * S;
+          const int64_t t0 = (int64_t)j * T, t1 = t0 + T < len ? t0 + T : len;
+          if (t1 <= t0) return true;
+          const int64_t w0 = t0 / kRunTokens, nruns = (t1 - 1) / kRunTokens - w0 + 1;
+          const int D = st.head_dim, bs = st.block_size, nkv = st.nkv;
+          for (int side = 0; side < 2; side++) {
+            const uint16_t* cache = static_cast<const uint16_t*>(side ? st.v_cache : st.k_cache);
+            for (int64_t r = 0; r < nruns; r++) {
+              const int64_t rs = (w0 + r) * kRunTokens > t0 ? (w0 + r) * kRunTokens : t0;
+              const int64_t re = (w0 + r + 1) * kRunTokens < t1 ? (w0 + r + 1) * kRunTokens : t1;
+              const int64_t page = st.block_table[rs / bs];
+              const uint16_t* src = cache + ((page * nkv + g) * bs + (rs % bs)) * D;
+              if (!issue(src, (uint32_t)((re - rs) * D * 2))) return false;
+            }
           }
+          return true;
+        };
+        if constexpr (Multi) {
+          for (int t = cta; t < ntask; t += ncta)
+            if (!task(t)) return drain();
+        } else if (cta < ntask && !task(cta)) {
+          return drain();
         }
       }
     }
@@ -910,11 +915,10 @@ __device__ __forceinline__ bool gemv_stage(const StepParams& P, const SparkStage
 // ... of the head group's 4 x 128 in the oracle's combine order.
 constexpr int kMergeRegs = 32;  // splits combined from registers (more: a loop)
 
-__device__ __forceinline__ bool attn_stage(const StepParams& P, const SparkStage& st, const Smem& s, uint32_t& seq_base,
-                                        int tid) {
+// One task (kv head g, split j): scores, softmax, P.V and the split's partials.
+__device__ __forceinline__ bool attn_split(const StepParams& P, const SparkStage& st, const Smem& s, uint32_t& seq_base,
+                                           int tid, int g, int j) {
   const int warp = tid >> 5, lane = tid & 31;
-  int g, j;
-  if (!attn_task(st, blockIdx.x, g, j)) return true;
   const int D = 128, nq = st.nq, S = st.splits;
   const int64_t pos = s.misc64[0], len = pos + 1;
   const int T = split_len(len, S);
@@ -1097,10 +1101,20 @@ __device__ __forceinline__ bool attn_stage(const StepParams& P, const SparkStage
     if (tid < 4) part_lse[(size_t)j * nq + 4 * g + tid] = __fadd_rn(spark_log(s.red[48 + tid]), mh[tid]);
     seq_base += 2 * nruns;
   }
-  // ---- publish this split, wait for the head's other splits, combine this split's slice
-  consumer_bar();
+  return true;
+}
+
+// The combine share of task (g, j), once every split of kv head g has published.
+__device__ __forceinline__ void attn_combine(const StepParams& P, const SparkStage& st, const Smem& s, int tid, int g,
+                                             int j) {
+  const int warp = tid >> 5, lane = tid & 31;
+  const int D = 128, nq = st.nq, S = st.splits;
+  float* part_o = st.part_o;
+  float* part_lse = st.part_lse;
+  unsigned long long* tr = (tid == 0 && P.io.trace)
+                               ? P.io.trace + ((size_t)blockIdx.x * P.num_stages + s.flag[2]) * kTraceSlots
+                               : nullptr;
   if (tid == 0) {
-    asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(st.head_counters + g) : "memory");
     const int target = S * (int)(s.misc64[2] + 1);
     const unsigned long long tw = gtimer();
     int ok = 1;
@@ -1173,6 +1187,39 @@ __device__ __forceinline__ bool attn_stage(const StepParams& P, const SparkStage
     }
     static_cast<uint16_t*>(st.attn_out)[(size_t)(4 * g + h) * D + d] = f2bf(a);
   }
+}
+
+// Tasks (kv head g, split j) = t / S, t % S go round-robin to the CTAs (t = cta, cta +
+// CTAs, ...): each CTA runs its tasks' splits, publishing each on the head's counter,
+// then combines its tasks' shares (every task is published before any CTA waits, so
+// several tasks per CTA -- contexts longer than CTAs / kv heads splits hold -- cannot
+// deadlock).  !Multi: at most one task per CTA, in a form with no loop state (the
+// usual program; a loop here costs the GEMV stages registers in the same kernel).
+template <bool Multi>
+__device__ __forceinline__ bool attn_stage(const StepParams& P, const SparkStage& st, const Smem& s, uint32_t& seq_base,
+                                        int tid) {
+  const int S = st.splits, ntask = st.nkv * S;
+  if constexpr (!Multi) {
+    if ((int)blockIdx.x >= ntask) return true;
+    const int g = blockIdx.x / S, j = blockIdx.x - g * S;
+    if (!attn_split(P, st, s, seq_base, tid, g, j)) return false;
+    consumer_bar();
+    if (tid == 0) asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(st.head_counters + g) : "memory");
+    attn_combine(P, st, s, tid, g, j);
+  } else {
+#pragma unroll 1
+    for (int t = blockIdx.x; t < ntask; t += gridDim.x) {
+      if (!attn_split(P, st, s, seq_base, tid, t / S, t - (t / S) * S)) return false;
+      consumer_bar();  // the split's partials (all threads) before its count
+      if (tid == 0)
+        asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(st.head_counters + t / S) : "memory");
+    }
+#pragma unroll 1
+    for (int t = blockIdx.x; t < ntask; t += gridDim.x) {
+      attn_combine(P, st, s, tid, t / S, t - (t / S) * S);
+      if (t + (int)gridDim.x < ntask) consumer_bar();  // its shared memory before the next task's
+    }
+  }
   return true;
 }
 
@@ -1193,7 +1240,10 @@ __device__ __forceinline__ bool wait_stage(const StepParams& P, const Smem& s, i
   }
 }
 
-template <bool Q6>
+// Q6: the program has Q6_K GEMV stages; Multi: an attention stage has more tasks than
+// CTAs.  Each is its own instantiation so the usual program (Q4_0, one attention task
+// per CTA) carries neither's registers.
+template <bool Q6, bool Multi>
 __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepParams P) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const Smem s = carve(smem_raw);
@@ -1213,7 +1263,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepParams P) {
   if (tid >= kConsumers) {
     if (tid == kConsumers) {
       Producer pr(P, s);
-      pr.run();
+      pr.run<Multi>();
     }
     return;
   }
@@ -1277,7 +1327,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepParams P) {
     // both stage functions keep every consumer on the same barriers; a stage that
     // fails returns false in all threads (attention: a split longer than the scratch)
     const bool ok = st.kind != SPARK_STAGE_ATTN ? gemv_stage<Q6>(P, st, s, seq_base, tid)
-                                                : attn_stage(P, st, s, seq_base, tid);
+                                                : attn_stage<Multi>(P, st, s, seq_base, tid);
     consumer_bar();
     if (!ok) return;
     if (tid == 0 && tr) tr[2] = gtimer();

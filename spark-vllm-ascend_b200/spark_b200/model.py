@@ -185,7 +185,7 @@ class DecodeEngine:
         if mode == "step":
             from . import step as _step
             self.ncta = _step.num_ctas()
-            splits = splits or _step.attn_splits(cfg, self.ncta)
+            splits = splits or _step.attn_splits(cfg, self.ncta, max_seq_len)
         if splits <= 0:  # auto: splits of at most 128 tokens (one K/V chunk), at least 16
             splits = min(256, max(16, -(-max_seq_len // 128)))
         self.splits = splits

@@ -240,8 +240,16 @@ def default_order(cfg, ncta: int, tp: int = 1) -> dict:
     }
 
 
-def attn_splits(cfg, ncta: int) -> int:
-    return max(1, ncta // cfg.num_kv_heads)
+def attn_splits(cfg, ncta: int, max_seq_len: int = 0) -> int:
+    """Splits per kv head: one (kv head, split) task per CTA, or more when the context
+    needs them (a split holds at most MAX_SPLIT_TOKENS tokens; CTAs then run several
+    tasks in turn).  The count fills whole rounds of tasks over the CTAs (8 kv heads on
+    148 CTAs: 18 splits = 144 tasks, then 37 = 296 = two per CTA, ...), so no CTA runs
+    a round more than the others with fewer tokens per task."""
+    nkv = cfg.num_kv_heads
+    need = max(1, -(-max_seq_len // MAX_SPLIT_TOKENS))
+    rounds = max(1, -(-need * nkv // ncta))
+    return max(need, rounds * ncta // nkv)
 
 
 def max_split_tokens(max_seq_len: int, splits: int) -> int:

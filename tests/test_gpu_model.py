@@ -79,3 +79,38 @@ def test_full_size_model_steps(cuda, oracle, mode):
                                          oracle=oracle, mode=mode)
     assert toks == ref
     assert np.array_equal(lg, ref_lg)
+
+
+def test_long_context_decode_matches_oracle(cuda, oracle):
+    """Context 32000+ on the persistent step: 37 splits per kv head (296 (kv head, split)
+    tasks on 148 CTAs, two in turn on each); a random KV cache, two decode steps,
+    identical tokens and logits to the oracle.  Two layers keep the caches small."""
+    import torch
+    from spark_b200.config import SparkConfig
+    from spark_b200.model import DecodeEngine, SyntheticWeights
+    cfg = SparkConfig(num_layers=2)
+    w = SyntheticWeights(cfg, device="cuda", seed=5)
+    max_seq = 32768
+    eng = DecodeEngine(w, max_seq_len=max_seq, num_blocks=max_seq // 128 + 4, seed=5, mode="step")
+    assert eng.splits * cfg.num_kv_heads > eng.ncta
+    g = torch.Generator(device="cuda").manual_seed(5)
+    eng.k_cache.copy_(torch.randn(eng.k_cache.shape, generator=g, device="cuda").to(torch.bfloat16))
+    eng.v_cache.copy_(torch.randn(eng.v_cache.shape, generator=g, device="cuda").to(torch.bfloat16))
+    pos0 = 32000
+    om = oracle.OracleModel(cfg, w.to_numpy(), num_blocks=eng.num_blocks, splits=eng.splits,
+                            order=eng.oracle_order())
+    om.kc[...] = u16(eng.k_cache).reshape(om.kc.shape)
+    om.vc[...] = u16(eng.v_cache).reshape(om.vc.shape)
+    eng.reset(pos0)
+    eng.set_token(123)
+    table = eng.block_table.cpu().numpy()
+    tok = 123
+    for i in range(2):
+        eng.step()
+        torch.cuda.synchronize()
+        want, want_lg = om.step(table, tok, pos0 + i, want_logits=True)
+        assert int(eng.error.item()) == 0
+        assert int(eng.token.item()) == want
+        assert np.array_equal(u16(eng.logits), want_lg)
+        tok = want
+

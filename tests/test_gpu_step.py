@@ -243,8 +243,9 @@ def test_t16_rope_kvstore_epilogue(cuda, oracle):
     assert np.array_equal(kc1, kc0) and np.array_equal(vc1, vc0)
 
 
+# (splits x 8 kv heads > 148 CTAs: several (kv head, split) tasks per CTA)
 @pytest.mark.parametrize("L,splits", [(1, 18), (17, 18), (300, 18), (2048, 18), (3000, 18), (6144, 18),
-                                      (9000, 7), (129, 2)])
+                                      (9000, 7), (129, 2), (6144, 37), (20000, 40), (32768, 25)])
 def test_attention_stage_bitexact(cuda, oracle, L, splits):
     import torch
     from spark_b200 import step
