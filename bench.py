@@ -112,9 +112,14 @@ def dist_setup():
 
 def build_engine(args, device, seed):
     import torch
-    from spark_b200.config import SparkConfig
+    from spark_b200.config import SparkConfig, spark_x26_config
     from spark_b200.model import DecodeEngine, SyntheticWeights
-    cfg = SparkConfig(num_layers=args.layers)
+    if args.model == "spark-x26":
+        if args.tp > 1 or args.mode != "step":
+            raise SystemExit("--model spark-x26 runs on one GPU per replica in --mode step")
+        cfg = spark_x26_config(num_layers=args.layers)
+    else:
+        cfg = SparkConfig(num_layers=args.layers)
     w = SyntheticWeights(cfg, device=device, seed=seed)
     if args.tp > 1:  # every rank built the same full weights (same seed): keep this rank's shard
         from spark_b200.tp import ShardWeights
@@ -193,8 +198,11 @@ def cpu_baseline(eng, w, cfg, n_tokens: int, threads: int) -> dict:
     import numpy as np
     import oracle
     oracle.set_threads(threads)
-    om = oracle.OracleModel(cfg, w.to_numpy(), num_blocks=eng.num_blocks, splits=eng.splits,
-                            order=eng.oracle_order())
+    if cfg.spark_features:
+        om = oracle.SparkOracleModel(cfg, w.to_numpy(), eng.num_blocks, eng.splits, eng.oracle_order())
+    else:
+        om = oracle.OracleModel(cfg, w.to_numpy(), num_blocks=eng.num_blocks, splits=eng.splits,
+                                order=eng.oracle_order())
     om.kc[...] = eng.k_cache.view(__import__("torch").int16).cpu().numpy().view(np.uint16)
     om.vc[...] = eng.v_cache.view(__import__("torch").int16).cpu().numpy().view(np.uint16)
     table = eng.block_table.cpu().numpy()
@@ -205,7 +213,7 @@ def cpu_baseline(eng, w, cfg, n_tokens: int, threads: int) -> dict:
         tok = om.step(table, tok, PROMPT_LEN + s)
     dt = time.perf_counter() - t0
     return {"value": round(n_tokens / dt, 4), "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": f"{n_tokens} decode tokens of the full 36-layer model at ctx {PROMPT_LEN} "
+            "sample": f"{n_tokens} decode tokens of the full {cfg.num_layers}-layer model at ctx {PROMPT_LEN} "
                       f"(C oracle, OpenMP {threads} threads, {dt:.1f} s)"}
 
 
@@ -307,7 +315,7 @@ def run_spark(args):
         ctx_mid = PROMPT_LEN + args.steps // 2
         tpot = ms / args.steps
         seqs = 1 if tp > 1 else world  # sequences decoded at once (tensor parallel: one)
-        step_bytes = w.q4_bytes() + cfg.hidden_size * 2 + cfg.kv_bytes_per_token() * ctx_mid
+        step_bytes = w.q4_bytes() + cfg.hidden_size * 2 + cfg.kv_bytes_at(ctx_mid)
         kb = kernel_bytes(cfg, ctx_mid)
         layers = cfg.num_layers
         if step_mode:
@@ -341,12 +349,15 @@ def run_spark(args):
             "data": "synthetic: seeded N(0,0.02) weights -> Q4_0, 2048 uniform-random prompt ids",
             "config": {"workload": (f"configs[3]: synthetic 4B Q4_0 batch-1 decode, tensor parallel over {tp} GPUs, "
                                     "2048 prompt, greedy") if tp > 1 else
-                       "configs[2]: synthetic 4B Q4_0 batch-1 decode, 2048 prompt, greedy",
+                       ("Spark-X2.6-4B architecture (gate, GELU, sliding 513 / partial RoPE, head_dim 256, tied "
+                        "Q6_K head), synthetic weights, batch-1 decode, greedy" if cfg.spark_features else
+                        "configs[2]: synthetic 4B Q4_0 batch-1 decode, 2048 prompt, greedy"),
+                       "model": cfg.name,
                        "layers": layers, "hidden": cfg.hidden_size, "vocab": cfg.vocab_size, "prompt": PROMPT_LEN,
                        "ctx_range": [PROMPT_LEN, PROMPT_LEN + args.steps - 1], "splits": eng.splits,
                        "kernels_per_step": eng.kernels_per_step(), "mode": eng.mode,
                        "parallelism": f"tp{tp}" if tp > 1 else f"replicas x{world}",
-                       "l2": "inputs larger than L2 (2.26 GB of weights per step)"},
+                       "l2": f"inputs larger than L2 ({w.q4_bytes() / 1e9:.2f} GB of weights per step)"},
             "e2e": {"value": round(args.steps * seqs / (e2e_ms / 1e3), 3), "unit": "tokens/s",
                     "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4, "wall_s": round(wall_e2e, 3),
                     "tokens_match_device_loop": e2e_tokens_match},
@@ -464,6 +475,9 @@ def main(argv=None):
     ap.add_argument("--cpu-tokens", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--prompt", type=int, default=2048, help="prompt length (2048 = the benchmark protocol)")
+    ap.add_argument("--model", choices=["synthetic-4b", "spark-x26"], default="synthetic-4b",
+                    help="synthetic-4b: the benchmark model (configs[2]); spark-x26: the reference's served "
+                         "architecture with synthetic weights")
     ap.add_argument("--layers", type=int, default=36,
                     help="decoder layers (36 = the benchmark model; fewer only for small profiling captures)")
     args = ap.parse_args(argv)

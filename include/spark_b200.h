@@ -225,7 +225,8 @@ int spark_read_device_error(int* value, int reset);
  * ====================================================================== */
 
 #define SPARK_STAGE_GEMV 0
-#define SPARK_STAGE_ATTN 1
+#define SPARK_STAGE_ATTN 1  /* head_dim 128; 256 with the Spark layer features (a program using any of
+                               them takes head_dim 256 attention only) */
 #define SPARK_STAGE_GEMV_Q6 2  /* GEMV over Q6_K weights in the T6 layout (spark_q6k_pack_t6); rowmap
                                   SPARK_ROWS_PLAIN, (k / kp) % 256 == 0, otherwise as SPARK_STAGE_GEMV */
 
@@ -239,10 +240,15 @@ int spark_read_device_error(int* value, int reset);
 #define SPARK_EPI_ROPE_KV 2  /* qkv: neox RoPE on q/k, q -> q, k/v -> paged cache + kv_new */
 #define SPARK_EPI_SILU_MUL 3 /* gate_up: out bf16 [n/2] = silu(gate) * up */
 #define SPARK_EPI_ARGMAX 4   /* LM head: logits bf16 [n] (out, nullable), atomicMax into key */
+#define SPARK_EPI_GELU_MUL 5 /* gate_up (Spark MLP): out bf16 [n/2] = bf16(gelu(bf16 gate) * up), gelu from
+                                `table` (see SparkStage.table) */
 
 /* logical rows of unit position p (0..15) of row group rg */
 #define SPARK_ROWS_PLAIN 0     /* 16 rg + p */
-#define SPARK_ROWS_PAIR_HALF 1 /* qkv heads: pair (i, i + head_dim/2) in positions (p, p + 8) */
+#define SPARK_ROWS_PAIR_HALF 1 /* qkv heads: per head, rotary pairs (i, i + r/2) in positions (p, p + 8)
+                                  (r = rotary_dim, or head_dim when 0), then the head's dims r.. in
+                                  plain runs of 16; rows past the last whole head (the gate rows)
+                                  plain */
 #define SPARK_ROWS_GATE_UP 2   /* gate row 8 rg + p and up row n/2 + 8 rg + p in positions (p, p + 8) */
 
 typedef struct SparkStage {
@@ -278,6 +284,17 @@ typedef struct SparkStage {
   int32_t* head_counters;     /* int32 [nkv] of this stage alone, zero when io->counters was zeroed;
                                  grows by `splits` per launch */
   void* attn_out;             /* bf16 [nq][head_dim] */
+  /* Spark layer features (zero / NULL: off) */
+  int32_t rotary_dim;         /* SPARK_EPI_ROPE_KV: dims rotated per head (partial RoPE, pairs (i, i + r/2)),
+                                 cos_sin rows of r entries; 0: head_dim */
+  int32_t window;             /* SPARK_STAGE_ATTN: attend to the last `window` positions only (sliding) */
+  const void* table;          /* SPARK_EPI_GELU_MUL: bf16 [4096] gelu of the bf16 inputs 0x3b00 + i (i < 2048)
+                                 and 0xbb00 + i - 2048 (|x| in [2^-9, 128)); outside that range gelu is
+                                 x / 2 (|x| < 2^-9), x (x >= 128), -0 (x <= -128) */
+  void* gate;                 /* bf16 [nq] headwise output gate: SPARK_EPI_ROPE_KV computes it from its
+                                 gate rows (rows (nq + 2 nkv) head_dim + h, h < nq, padded to 16 rows):
+                                 bf16(1 / (1 + exp(-bf16(logit)))); SPARK_STAGE_ATTN multiplies head h's
+                                 combined output by it: bf16(bf16(o) * gate[h]) */
 } SparkStage;
 
 typedef struct SparkStepIO {

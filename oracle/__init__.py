@@ -66,6 +66,11 @@ def lib():
             "orc_attn_split_w": (None, [_P, _P, _P, _P, _I64, _I, _I, _I, _I, _I, _F, _I, _P, _P]),
             "orc_attn_split": (None, [_P, _P, _P, _P, _I64, _I, _I, _I, _I, _I, _F, _P, _P]),
             "orc_attn_combine": (None, [_P, _P, _I, _I, _I, _P]),
+            "orc_attn_split_x": (None, [_P, _P, _P, _P, _I64, _I, _I, _I, _I, _I, _F, _I, _I, _P, _P]),
+            "orc_attn_combine_g": (None, [_P, _P, _I, _I, _I, _P, _P]),
+            "orc_rope_partial": (None, [_P, _I, _I, _I, _P]),
+            "orc_gelu_mul": (None, [_P, _P, _I64, _P, _P]),
+            "orc_sigmoid_bf16": (None, [_P, _I64, _P]),
             "orc_argmax_bf16": (_I64, [_P, _I64]),
             "orc_decode_step": (_I64, [_P, _P, _P, _P, _P, _I64, _P, _I64, _I64, _F, _F, _P]),
             "orc_decode_layer": (None, [_P, _P, _P, _P, _P, _P, _I64, _F, _F, _P, _P, _I]),
@@ -258,10 +263,11 @@ def split_tokens(length: int, splits: int) -> int:
     return lib().orc_split_tokens(length, splits)
 
 
-def attn_split(q, kc, vc, table, length: int, splits: int, scale: float, chunk_accs: int = 0):
+def attn_split(q, kc, vc, table, length: int, splits: int, scale: float, chunk_accs: int = 0, window: int = 0):
     """q bf16 [nq, D]; kc/vc bf16 [blocks, nkv, bs, D]; returns (part_o [S,nq,D], part_lse [S,nq]).
-    ``chunk_accs`` > 0 selects the persistent-step PV order (16-token chunks into that
-    many accumulators)."""
+    ``chunk_accs`` > 0 selects the persistent-step order (scores over D / 16 lanes per
+    token, PV in 16-token chunks into that many accumulators); ``window`` > 0: only the
+    last ``window`` positions (Spark sliding layers)."""
     q = np.ascontiguousarray(q, dtype=np.uint16)
     kc = np.ascontiguousarray(kc, dtype=np.uint16)
     vc = np.ascontiguousarray(vc, dtype=np.uint16)
@@ -269,17 +275,52 @@ def attn_split(q, kc, vc, table, length: int, splits: int, scale: float, chunk_a
     _, nkv, bs, _ = kc.shape
     po = np.empty((splits, nq, dim), np.float32)
     pl = np.empty((splits, nq), np.float32)
-    lib().orc_attn_split_w(_p(q), _p(kc), _p(vc), _p(np.ascontiguousarray(table, dtype=np.int32)), length, nq,
-                           nkv, dim, bs, splits, scale, chunk_accs, _p(po), _p(pl))
+    lib().orc_attn_split_x(_p(q), _p(kc), _p(vc), _p(np.ascontiguousarray(table, dtype=np.int32)), length, nq,
+                           nkv, dim, bs, splits, scale, chunk_accs, window, _p(po), _p(pl))
     return po, pl
 
 
-def attn_combine(part_o, part_lse) -> np.ndarray:
+def attn_combine(part_o, part_lse, gate=None) -> np.ndarray:
+    """``gate`` bf16 [nq] (Spark headwise output gate) or None."""
     po = np.ascontiguousarray(part_o, dtype=np.float32)
     pl = np.ascontiguousarray(part_lse, dtype=np.float32)
     splits, nq, dim = po.shape
     out = np.empty((nq, dim), np.uint16)
-    lib().orc_attn_combine(_p(po), _p(pl), splits, nq, dim, _p(out))
+    g = None if gate is None else np.ascontiguousarray(gate, dtype=np.uint16)
+    lib().orc_attn_combine_g(_p(po), _p(pl), splits, nq, dim, _p(g), _p(out))
+    return out
+
+
+def rope_partial(x_bf16: np.ndarray, rot: int, cs_row: np.ndarray) -> np.ndarray:
+    """x bf16 [nh, D]; pairs (i, i + rot/2) rotated with a cos | sin row of rot entries."""
+    x = np.ascontiguousarray(x_bf16, dtype=np.uint16).copy()
+    nh, dim = x.shape
+    lib().orc_rope_partial(_p(x), nh, dim, rot, _p(np.ascontiguousarray(cs_row, dtype=np.uint16)))
+    return x
+
+
+def gelu_table() -> np.ndarray:
+    """The reference's GELU table (integration/model.py:12-16): torch's exact-erf gelu of
+    every bf16 input, kept for |x| in [2^-9, 128) -- inputs 0x3b00 + i, then 0xbb00 + i."""
+    import torch
+    bits = torch.arange(65536, dtype=torch.int32).to(torch.int16).view(torch.bfloat16)
+    full = torch.nn.functional.gelu(bits, approximate="none")
+    t = torch.cat((full[0x3B00:0x4300], full[0xBB00:0xC300])).contiguous()
+    return t.view(torch.int16).numpy().view(np.uint16).copy()
+
+
+def gelu_mul(g, u, table) -> np.ndarray:
+    g = np.ascontiguousarray(g, dtype=np.uint16)
+    u = np.ascontiguousarray(u, dtype=np.uint16)
+    out = np.empty_like(g)
+    lib().orc_gelu_mul(_p(g), _p(u), g.size, _p(np.ascontiguousarray(table, dtype=np.uint16)), _p(out))
+    return out
+
+
+def sigmoid_bf16(x) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.uint16)
+    out = np.empty_like(x)
+    lib().orc_sigmoid_bf16(_p(x), x.size, _p(out))
     return out
 
 
@@ -353,3 +394,70 @@ class OracleModel:
                                     self.num_blocks, _p(table), token, pos, cfg.rms_norm_eps,
                                     cfg.attn_scale, _p(logits))
         return (int(tok), logits) if want_logits else int(tok)
+
+
+class SparkOracleModel:
+    """Host decoder of the Spark architecture in the persistent-step order.
+
+    The same steps as ``orc_decode_layer`` / ``orc_decode_step`` (add + RMSNorm, T16
+    GEMVs, RoPE, paged KV store, split attention and combine, MLP, head), with the Spark
+    layer features of the reference (plugin/spark2_5.py:140-241): the gate rows after the
+    qkv heads give bf16 sigmoid gates that multiply the combined attention heads
+    (vector.py:81); full layers rotate ``rotary_dim`` dims with their theta, sliding
+    layers the whole head with theirs and attend to the last ``sliding_window`` positions
+    (attention.py:124-127); GELU * mul through the reference's table (linear.py:540-577);
+    the LM head is the tied Q6_K embedding when ``weights`` has ``head_q6``.
+    ``order``: the engine's persistent-step order ({"ks", "kp", "chunk_accs"})."""
+
+    def __init__(self, cfg, weights: dict, num_blocks: int, splits: int, order: dict):
+        self.cfg, self.w, self.splits, self.order = cfg, weights, splits, order
+        L, nkv, bs, D = cfg.num_layers, cfg.num_kv_heads, cfg.block_size, cfg.head_dim
+        self.kc = np.zeros((L, num_blocks, nkv, bs, D), np.uint16)
+        self.vc = np.zeros_like(self.kc)
+        self.gelu = gelu_table() if cfg.hidden_act == "gelu" else None
+
+    def layer(self, li: int, a: np.ndarray, b: np.ndarray | None, table: np.ndarray, pos: int):
+        """One decoder layer: returns (down projection, residual after attention)."""
+        cfg, w, o = self.cfg, self.w, self.order
+        p = f"layers.{li}."
+        ks_qkv, ks_o, ks_gu, ks_down, _ = o["ks"]
+        kp_o, kp_down = o["kp"]
+        nq, nkv, D, bs, eps = cfg.num_q_heads, cfg.num_kv_heads, cfg.head_dim, cfg.block_size, cfg.rms_norm_eps
+        nh = nq + 2 * nkv
+        res, x = add_rmsnorm(a, b, w[p + "in_norm"], eps)
+        y = t16_gemv(x, w[p + "qkv_qs"], w[p + "qkv_d"], 1, ks_qkv)
+        qkv = y[:nh * D].reshape(nh, D)
+        _, r = cfg.layer_rope(li)
+        cs = w["cos_sin_sliding"] if cfg.is_sliding(li) else w["cos_sin"]
+        rot = rope_partial(qkv[:nq + nkv], r, cs[pos])
+        blk, off = int(table[pos // bs]), pos % bs
+        self.kc[li, blk, :, off] = rot[nq:]
+        self.vc[li, blk, :, off] = qkv[nq + nkv:]
+        gate = sigmoid_bf16(y[nh * D:nh * D + nq]) if cfg.attn_gate else None
+        po, pl = attn_split(rot[:nq], self.kc[li], self.vc[li], table, pos + 1, self.splits, cfg.attn_scale,
+                            chunk_accs=o["chunk_accs"], window=cfg.layer_window(li))
+        attn = attn_combine(po, pl, gate).reshape(-1)
+        oproj = t16_gemv(attn, w[p + "o_qs"], w[p + "o_d"], kp_o, ks_o)
+        resmid, x2 = add_rmsnorm(oproj, res, w[p + "post_norm"], eps)
+        gu = t16_gemv(x2, w[p + "gu_qs"], w[p + "gu_d"], 1, ks_gu)
+        i = cfg.intermediate_size
+        mid = gelu_mul(gu[:i], gu[i:], self.gelu) if self.gelu is not None else silu_mul(gu[:i], gu[i:])
+        return t16_gemv(mid, w[p + "down_qs"], w[p + "down_d"], kp_down, ks_down), resmid
+
+    def head(self, a: np.ndarray, b: np.ndarray):
+        cfg, w = self.cfg, self.w
+        _, x = add_rmsnorm(a, b, w["final_norm"], cfg.rms_norm_eps, want_res=False)
+        ks = self.order["ks"][4]
+        if "head_q6" in w:
+            logits = parts_to_bf16(q6k_gemv_parts(x, w["head_q6"], cfg.vocab_size, cfg.hidden_size, 1, ks))
+        else:
+            logits = t16_gemv(x, w["head_qs"], w["head_d"], 1, ks)
+        return argmax_bf16(logits), logits
+
+    def step(self, table: np.ndarray, token: int, pos: int, want_logits: bool = False):
+        table = np.ascontiguousarray(table, dtype=np.int32)
+        a, b = self.w["embed"][token].copy(), None
+        for li in range(self.cfg.num_layers):
+            a, b = self.layer(li, a, b, table, pos)
+        tok, logits = self.head(a, b)
+        return (tok, logits) if want_logits else tok

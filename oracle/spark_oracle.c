@@ -528,6 +528,46 @@ ORC_API void orc_rope_neox(uint16_t* x, int nh, int dim, const uint16_t* cs_row)
     }
 }
 
+/* Partial RoPE (Spark full-attention layers): pairs (i, i + rot/2), i < rot/2, rotated
+ * as in orc_rope_neox with a cos_sin row of rot entries; dims rot.. unchanged. */
+ORC_API void orc_rope_partial(uint16_t* x, int nh, int dim, int rot, const uint16_t* cs_row) {
+    int half = rot / 2;
+    for (int hh = 0; hh < nh; hh++) {
+        uint16_t* v = x + (int64_t)hh * dim;
+        for (int i = 0; i < half; i++) {
+            float a = bf2f(v[i]), bb = bf2f(v[i + half]);
+            float c = bf2f(cs_row[i]), s = bf2f(cs_row[i + half]);
+            float u = (a * c) - (bb * s);
+            float w = (bb * c) + (a * s);
+            v[i] = f2bf(u);
+            v[i + half] = f2bf(w);
+        }
+    }
+}
+
+/* GELU of a bf16 value as the reference's table lookup (kernels/linear.py:540-577,
+ * table built in integration/model.py:12-16): table [4096] = gelu of the inputs
+ * 0x3b00 + i and 0xbb00 + i (|x| in [2^-9, 128)); |x| < 2^-9: bf16(x / 2); x >= 128: x;
+ * x <= -128: -0; NaN and -inf: 0x7fff. */
+static uint16_t gelu_bf16(uint16_t x, const uint16_t* table) {
+    uint32_t ab = x & 0x7fffu;
+    if (ab > 0x7f80u || x == 0xff80u) return 0x7fff;
+    if (x >= 0xc300u) return 0x8000;
+    if (ab >= 0x4300u) return x;
+    if (ab < 0x3b00u) return f2bf(0.5f * bf2f(x));
+    return table[(ab - 0x3b00u) | ((uint32_t)(x >> 4) & 0x800u)];
+}
+
+/* Spark MLP activation: out = bf16(gelu(g) * u), gelu bf16 from the table */
+ORC_API void orc_gelu_mul(const uint16_t* g, const uint16_t* u, int64_t n, const uint16_t* table, uint16_t* out) {
+    for (int64_t i = 0; i < n; i++) out[i] = f2bf(bf2f(gelu_bf16(g[i], table)) * bf2f(u[i]));
+}
+
+/* Spark headwise output gate: g = bf16(1 / (1 + exp(-x))) of the bf16 gate logits */
+ORC_API void orc_sigmoid_bf16(const uint16_t* x, int64_t n, uint16_t* out) {
+    for (int64_t i = 0; i < n; i++) out[i] = f2bf(1.0f / (1.0f + orc_exp(-bf2f(x[i]))));
+}
+
 ORC_API void orc_silu_mul(const uint16_t* g, const uint16_t* u, int64_t n, uint16_t* out) {
     for (int64_t i = 0; i < n; i++) {
         float gf = bf2f(g[i]);
@@ -560,13 +600,14 @@ static inline int64_t split_tokens(int64_t len, int splits) {
 
 ORC_API int64_t orc_split_tokens(int64_t len, int splits) { return split_tokens(len, splits); }
 
-/* q . k for one token (dim == 128): 8 lanes, lane j owns dims 8j..8j+7 then
- * 64+8j..64+8j+7; over that list a0 accumulates the even positions and a1 the odd
- * ones (fma, ascending); lane value a0 + a1; xor butterfly 4, 2, 1 over the lanes. */
-static float score_dot(const float* qf, const uint16_t* kr, int dim) {
-    float lane[8];
-    int half = dim / 2, per = dim / 16;
-    for (int j = 0; j < 8; j++) {
+/* q . k for one token: `lanes` lanes, lane j owns dims per*j..per*j+per-1 of each half
+ * (per = dim / 2 / lanes; dim 128 with 8 lanes: 8j..8j+7 then 64+8j..64+8j+7); over that
+ * list a0 accumulates the even positions and a1 the odd ones (fma, ascending); lane
+ * value a0 + a1; xor butterfly over the lanes (4, 2, 1 for 8 lanes). */
+static float score_dot_l(const float* qf, const uint16_t* kr, int dim, int lanes) {
+    float lane[16];
+    int half = dim / 2, per = half / lanes;
+    for (int j = 0; j < lanes; j++) {
         float a0 = 0.0f, a1 = 0.0f;
         for (int part = 0; part < 2; part++) {
             int base = part * half + per * j;
@@ -577,7 +618,7 @@ static float score_dot(const float* qf, const uint16_t* kr, int dim) {
         }
         lane[j] = a0 + a1;
     }
-    butterfly(lane, 8);
+    butterfly(lane, lanes);
     return lane[0];
 }
 
@@ -587,17 +628,26 @@ static float score_dot(const float* qf, const uint16_t* kr, int dim) {
  * W > 0 (persistent-step order): the split's tokens form 16-token chunks; chunk c
  * is summed (tokens ascending) into accumulator c mod W, chunks in ascending order;
  * O = ((O_0 + O_1) + ...) + O_{W-1}, empty accumulators included as 0. */
-ORC_API void orc_attn_split_w(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const int32_t* table,
+/* window > 0 (Spark sliding layers): only the last `window` positions, [lo, len) with
+ * lo = len - window (the reference masks below max(0, len - 513), attention.py:124-127,
+ * so its 512-window layers take window 513); the splits cover [lo & ~15, len) and the
+ * positions before lo score -inf (p = 0: they add zeros in every sum).  The
+ * persistent-step order (W > 0) scores with dim / 16 lanes per token; the per-kernel
+ * order (W == 0) with 8. */
+ORC_API void orc_attn_split_x(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const int32_t* table,
                               int64_t len, int nq, int nkv, int dim, int bs, int splits, float scale, int W,
-                              float* part_o, float* part_lse) {
+                              int window, float* part_o, float* part_lse) {
     int group = nq / nkv;
-    int64_t T = split_tokens(len, splits);
+    int lanes = W > 0 ? dim / 16 : 8;
+    int64_t lo = window > 0 && len > window ? len - window : 0;
+    int64_t start = lo & ~(int64_t)15;
+    int64_t T = split_tokens(len - start, splits);
     int nacc = W > 0 ? W : 1;
     float* scores = (float*)malloc(sizeof(float) * (T > 0 ? T : 1));
     float* qf = (float*)malloc(sizeof(float) * dim);
     float* o = (float*)malloc(sizeof(float) * dim * nacc);
     for (int s = 0; s < splits; s++) {
-        int64_t t0 = (int64_t)s * T, t1 = t0 + T < len ? t0 + T : len;
+        int64_t t0 = start + (int64_t)s * T, t1 = t0 + T < len ? t0 + T : len;
         int64_t n = t1 - t0;
         for (int hq = 0; hq < nq; hq++) {
             int hk = hq / group;
@@ -612,7 +662,11 @@ ORC_API void orc_attn_split_w(const uint16_t* q, const uint16_t* kc, const uint1
             for (int64_t i = 0; i < n; i++) {
                 int64_t t = t0 + i, blk = table[t / bs], off = t % bs;
                 const uint16_t* kr = kc + ((blk * nkv + hk) * bs + off) * dim;
-                float sc = score_dot(qf, kr, dim) * scale;
+                if (t < lo) {
+                    scores[i] = -INFINITY;
+                    continue;
+                }
+                float sc = score_dot_l(qf, kr, dim, lanes) * scale;
                 scores[i] = sc;
                 if (sc > m) m = sc;
             }
@@ -643,15 +697,22 @@ ORC_API void orc_attn_split_w(const uint16_t* q, const uint16_t* kc, const uint1
     free(o);
 }
 
+ORC_API void orc_attn_split_w(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const int32_t* table,
+                              int64_t len, int nq, int nkv, int dim, int bs, int splits, float scale, int W,
+                              float* part_o, float* part_lse) {
+    orc_attn_split_x(q, kc, vc, table, len, nq, nkv, dim, bs, splits, scale, W, 0, part_o, part_lse);
+}
+
 ORC_API void orc_attn_split(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const int32_t* table,
                             int64_t len, int nq, int nkv, int dim, int bs, int splits, float scale,
                             float* part_o, float* part_lse) {
     orc_attn_split_w(q, kc, vc, table, len, nq, nkv, dim, bs, splits, scale, 0, part_o, part_lse);
 }
 
-/* out bf16 [nq][dim] = sum_s softmax(lse)_s * part_o[s] */
-ORC_API void orc_attn_combine(const float* part_o, const float* part_lse, int splits, int nq, int dim,
-                              uint16_t* out) {
+/* out bf16 [nq][dim] = sum_s softmax(lse)_s * part_o[s]; gate (bf16 [nq], nullable):
+ * then out = bf16(out * gate[head]) (the Spark headwise output gate, vector.py:81) */
+ORC_API void orc_attn_combine_g(const float* part_o, const float* part_lse, int splits, int nq, int dim,
+                                const uint16_t* gate, uint16_t* out) {
     float* w = (float*)malloc(sizeof(float) * splits);
     for (int hq = 0; hq < nq; hq++) {
         float mx = -INFINITY;
@@ -676,10 +737,17 @@ ORC_API void orc_attn_combine(const float* part_o, const float* part_lse, int sp
                 if (part_lse[(int64_t)s * nq + hq] == -INFINITY) continue; /* empty split */
                 acc = acc + w[s] * part_o[((int64_t)s * nq + hq) * dim + dd];
             }
-            out[(int64_t)hq * dim + dd] = f2bf(acc);
+            uint16_t o = f2bf(acc);
+            if (gate) o = f2bf(bf2f(o) * bf2f(gate[hq]));
+            out[(int64_t)hq * dim + dd] = o;
         }
     }
     free(w);
+}
+
+ORC_API void orc_attn_combine(const float* part_o, const float* part_lse, int splits, int nq, int dim,
+                              uint16_t* out) {
+    orc_attn_combine_g(part_o, part_lse, splits, nq, dim, NULL, out);
 }
 
 /* ------------------------------------------------------------------ */

@@ -621,8 +621,9 @@ int spark_q4_pack_t16(const uint8_t* qs, const uint16_t* d, int n, int k, int kp
                       void* stream) {
   if (!qs || !d || !out) return SPARK_ERR_INVALID_ARG;
   if (n <= 0 || k <= 0 || kp <= 0 || n % 16 || k % kp || (k / kp) % 64) return SPARK_ERR_UNSUPPORTED_SHAPE;
-  if (rowmap == SPARK_ROWS_PAIR_HALF) {
-    if (aux <= 0 || aux % 16 || n % aux) return SPARK_ERR_UNSUPPORTED_SHAPE;
+  if (rowmap == SPARK_ROWS_PAIR_HALF) {  // aux = head_dim | rotary_dim << 16
+    const int hd = aux & 0xffff, rot = (aux >> 16) & 0xffff;
+    if (aux < 0 || hd <= 0 || hd % 16 || (n % hd) % 16 || rot % 16 || rot > hd) return SPARK_ERR_UNSUPPORTED_SHAPE;
   } else if (rowmap == SPARK_ROWS_GATE_UP) {
     if ((n / 2) % 8) return SPARK_ERR_UNSUPPORTED_SHAPE;
   } else if (rowmap != SPARK_ROWS_PLAIN) {
@@ -707,6 +708,10 @@ static int check_stage(const SparkStage& s, int i, int ncta) {
       case SPARK_EPI_SILU_MUL:
         if (s.kp != 1 || !s.out || s.rowmap != SPARK_ROWS_GATE_UP) return SPARK_ERR_INVALID_ARG;
         break;
+      case SPARK_EPI_GELU_MUL:
+        if (s.kp != 1 || !s.out || !s.table || s.rowmap != SPARK_ROWS_GATE_UP) return SPARK_ERR_INVALID_ARG;
+        if (reinterpret_cast<uintptr_t>(s.table) & 1) return SPARK_ERR_ALIGNMENT;
+        break;
       case SPARK_EPI_ARGMAX:
         if (s.kp != 1 || !s.key) return SPARK_ERR_INVALID_ARG;
         break;
@@ -714,13 +719,20 @@ static int check_stage(const SparkStage& s, int i, int ncta) {
         if (s.kp != 1 || s.rowmap != SPARK_ROWS_PAIR_HALF || !s.q || !s.k_cache || !s.v_cache || !s.kv_new ||
             !s.cos_sin || !s.pos || !s.block_table || s.block_size <= 0 || s.nq <= 0 || s.nkv <= 0)
           return SPARK_ERR_INVALID_ARG;
-        if (s.n != (s.nq + 2 * s.nkv) * s.head_dim || s.head_dim > 128) return SPARK_ERR_UNSUPPORTED_SHAPE;
+        if (s.head_dim > 256 || s.head_dim % 16) return SPARK_ERR_UNSUPPORTED_SHAPE;
+        if (s.rotary_dim < 0 || s.rotary_dim > s.head_dim || s.rotary_dim % 16) return SPARK_ERR_UNSUPPORTED_SHAPE;
+        {  // gate rows (Spark): the heads' gate logits after the q / k / v heads, 16-row padded
+          const int gate_rows = s.gate ? (s.nq + 15) / 16 * 16 : 0;
+          if (gate_rows >= s.head_dim || s.n != (s.nq + 2 * s.nkv) * s.head_dim + gate_rows)
+            return SPARK_ERR_UNSUPPORTED_SHAPE;
+        }
+        if (reinterpret_cast<uintptr_t>(s.gate) & 1) return SPARK_ERR_ALIGNMENT;
         break;
       default:
         return SPARK_ERR_INVALID_ARG;
     }
     if (s.rowmap == SPARK_ROWS_PAIR_HALF) {
-      if (s.head_dim <= 0 || s.head_dim % 16 || s.n % s.head_dim) return SPARK_ERR_UNSUPPORTED_SHAPE;
+      if (s.head_dim <= 0 || s.head_dim % 16 || (s.n % s.head_dim) % 16) return SPARK_ERR_UNSUPPORTED_SHAPE;
     } else if (s.rowmap != SPARK_ROWS_PLAIN && s.rowmap != SPARK_ROWS_GATE_UP) {
       return SPARK_ERR_INVALID_ARG;
     }
@@ -730,8 +742,11 @@ static int check_stage(const SparkStage& s, int i, int ncta) {
   if (!s.q || !s.k_cache || !s.v_cache || !s.kv_new || !s.pos || !s.block_table || !s.part_o || !s.part_lse ||
       !s.head_counters || !s.attn_out)
     return SPARK_ERR_INVALID_ARG;
-  if (s.head_dim != 128 || s.nkv <= 0 || s.nq != 4 * s.nkv || s.block_size <= 0 || s.block_size % step::kRunTokens)
+  if ((s.head_dim != 128 && s.head_dim != 256) || s.nkv <= 0 || s.nq != 4 * s.nkv || s.block_size <= 0 ||
+      s.block_size % step::kRunTokens)
     return SPARK_ERR_UNSUPPORTED_SHAPE;
+  if (s.window < 0) return SPARK_ERR_INVALID_ARG;
+  if (reinterpret_cast<uintptr_t>(s.gate) & 1) return SPARK_ERR_ALIGNMENT;
   if (s.splits <= 0 || s.splits > 4096) return SPARK_ERR_UNSUPPORTED_SHAPE;  // (kv head, split) tasks round-robin
   if (s.max_split_tokens <= 0 || s.max_split_tokens > step::kMaxSplitTokens) return SPARK_ERR_TOO_LARGE;
   if ((reinterpret_cast<uintptr_t>(s.kv_new) | reinterpret_cast<uintptr_t>(s.k_cache) |
@@ -829,15 +844,28 @@ int spark_step_run(const SparkStage* host_stages, const SparkStage* dev_stages, 
   if (!P.io.error) P.io.error = device_error_ptr();
   // Q6_K stages, and attention stages with more (kv head, split) tasks than CTAs, run in
   // the kernel instantiations that have their code
-  bool q6 = false, multi = false;
+  bool q6 = false, multi = false, spark = false;
   for (int i = 0; i < num_stages; i++) {
     const SparkStage& h = host_stages[i];
     q6 = q6 || h.kind == SPARK_STAGE_GEMV_Q6;
     multi = multi || (h.kind == SPARK_STAGE_ATTN && (int64_t)h.nkv * h.splits > ncta);
+    if (h.kind == SPARK_STAGE_ATTN)
+      spark = spark || h.head_dim != 128 || h.window > 0 || h.gate;
+    else
+      spark = spark || h.epi == SPARK_EPI_GELU_MUL ||
+              (h.epi == SPARK_EPI_ROPE_KV && (h.gate || (h.rotary_dim && h.rotary_dim != h.head_dim)));
   }
-  void (*kernel)(const step::StepParams) =
-      q6 ? (multi ? step::step_kernel<true, true> : step::step_kernel<true, false>)
-         : (multi ? step::step_kernel<false, true> : step::step_kernel<false, false>);
+  // the Spark instantiation's attention is head_dim 256, the others' 128
+  for (int i = 0; i < num_stages; i++)
+    if (host_stages[i].kind == SPARK_STAGE_ATTN && host_stages[i].head_dim != (spark ? 256 : 128))
+      return SPARK_ERR_UNSUPPORTED_SHAPE;
+  using Kernel = void (*)(const step::StepParams);
+  static const Kernel kernels[8] = {
+      step::step_kernel<false, false, false>, step::step_kernel<false, false, true>,
+      step::step_kernel<false, true, false>,  step::step_kernel<false, true, true>,
+      step::step_kernel<true, false, false>,  step::step_kernel<true, false, true>,
+      step::step_kernel<true, true, false>,   step::step_kernel<true, true, true>};
+  const Kernel kernel = kernels[4 * q6 + 2 * multi + spark];
   if (set_smem(reinterpret_cast<const void*>(kernel), step::kSmemBytes) != kOk) return kErrLaunch;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(ncta);

@@ -118,6 +118,20 @@ __host__ __device__ __forceinline__ int t16_row(int rowmap, int rg, int p, int n
   return 16 * rg + p;
 }
 
+// t16_row with the Spark qkv layout: aux = head_dim | rotary_dim << 16 for
+// SPARK_ROWS_PAIR_HALF (rotary_dim 0: head_dim): per head, the rotary pairs (i, i + r/2)
+// (r/16 units), then dims r.. in plain runs of 16; rows past the last whole head (the
+// gate rows) plain.  Equal to t16_row when rotary_dim is 0 and n is whole heads.
+__host__ __device__ __forceinline__ int t16_row_x(int rowmap, int rg, int p, int n, int aux) {
+  if (rowmap != SPARK_ROWS_PAIR_HALF) return t16_row(rowmap, rg, p, n, aux);
+  const int head_dim = aux & 0xffff, r = (aux >> 16) ? (aux >> 16) : head_dim;
+  const int per = head_dim >> 4, hd = rg / per, s = rg - hd * per;
+  if ((hd + 1) * head_dim > n) return hd * head_dim + 16 * s + p;
+  const int npair = r >> 4;
+  if (s < npair) return hd * head_dim + (p < 8 ? 8 * s + p : (r >> 1) + 8 * s + (p - 8));
+  return hd * head_dim + r + 16 * (s - npair) + p;
+}
+
 __host__ __device__ __forceinline__ int split_len(int64_t len, int splits) {
   const int64_t t = (len + splits - 1) / splits;
   return (int)((t + 15) / 16 * 16);
@@ -149,7 +163,7 @@ struct Smem {
   unsigned long long* red64;  // [16]
   SparkStage* stage;          // consumers' copy of the current stage
   long long* misc64;          // [4] per-stage values (position, cache row offset)
-  uint16_t* rope_cs;          // [128] cos | sin row of the position (RoPE stages)
+  uint16_t* rope_cs;          // [256] cos | sin row of the position (RoPE stages)
 };
 
 __device__ __forceinline__ Smem carve(unsigned char* base) {
@@ -173,8 +187,10 @@ __device__ __forceinline__ Smem carve(unsigned char* base) {
   s.rope_cs = reinterpret_cast<uint16_t*>(s.misc64 + 4);
   return s;
 }
-// 256 + 256 + 128 + 128 + 128 + 128 + 16 + 16 + 256 + 128 + 256 + 32 + 256 = 1984 <= kMiscBytes
-static_assert(sizeof(SparkStage) == 256, "SparkStage layout");
+// full 128 + empty 128 + desc_off / done / prod_start / prod_end 4 x 64 + abort / flag 32 +
+// red 256 + red64 128 + stage 280 + misc64 32 + rope_cs 512 = 1752 <= kMiscBytes
+static_assert(sizeof(SparkStage) == 280, "SparkStage layout");
+constexpr int kStageWords = (int)sizeof(SparkStage) / 8;
 
 struct StepParams {
   SparkStage inline_stage;   // the program when it has one stage (8-byte aligned)
@@ -252,8 +268,9 @@ struct Producer {
     return true;
   }
 
-  // Multi: attention tasks may outnumber the CTAs (several per CTA)
-  template <bool Multi>
+  // Multi: attention tasks may outnumber the CTAs (several per CTA); Spark: sliding
+  // window attention stages
+  template <bool Multi, bool Spark>
   __device__ void run() {
     const int ncta = gridDim.x, cta = blockIdx.x;
     for (int i = 0; i < P.num_stages; i++) {
@@ -271,12 +288,14 @@ struct Producer {
         // this CTA's tasks (kv head g, split j) in the consumers' order: K then V runs each
         const int S = st.splits, ntask = st.nkv * S;
         const int64_t len = st.pos[0] + 1;
-        const int T = split_len(len, S);
+        // (Spark sliding window: splits from the window start rounded down to 16)
+        const int64_t start = (Spark && st.window > 0 && len > st.window ? len - st.window : 0) & ~(int64_t)15;
+        const int T = split_len(len - start, S);
         if (T > kMaxSplitTokens) return drain();
         // K then V runs of task t; false: aborted
         auto task = [&](int t) -> bool {
           const int g = t / S, j = t - g * S;
-          const int64_t t0 = (int64_t)j * T, t1 = t0 + T < len ? t0 + T : len;
+          const int64_t t0 = start + (int64_t)j * T, t1 = t0 + T < len ? t0 + T : len;
           if (t1 <= t0) return true;
           const int64_t w0 = t0 / kRunTokens, nruns = (t1 - 1) / kRunTokens - w0 + 1;
           const int D = st.head_dim, bs = st.block_size, nkv = st.nkv;
@@ -711,13 +730,32 @@ __device__ __forceinline__ void gemv_task_q6(const GemvDims& gd, uint32_t ubase,
 
 __device__ __forceinline__ uint16_t bf16r(float v) { return f2bf(v); }
 
-// epilogue of one row pair (positions g and g + 8 of unit u)
+// GELU of a bf16 value by the table (SparkStage.table) and its closed-form ranges
+__device__ __forceinline__ uint16_t gelu_bf16(uint16_t x, const uint16_t* table) {
+  const uint32_t ab = x & 0x7fffu;
+  if (ab > 0x7f80u || x == 0xff80u) return 0x7fff;  // NaN, gelu(-inf)
+  if (x >= 0xc300u) return 0x8000;                   // x <= -128: -0
+  if (ab >= 0x4300u) return x;                       // x >= 128: x
+  if (ab < 0x3b00u) return f2bf(__fmul_rn(0.5f, bf2f(x)));
+  return __ldg(table + ((ab - 0x3b00u) | ((uint32_t)(x >> 4) & 0x800u)));
+}
+
+// epilogue of one row pair (positions g and g + 8 of unit u); Spark: the qkv stage's
+// partial RoPE and gate rows, the GELU * mul epilogue
+template <bool Spark>
 __device__ __forceinline__ void gemv_epilogue(const SparkStage& st, const SparkStepIO& io, const long long* misc64,
                                               const uint16_t* rope_cs, int u, int g, float v0, float v1,
                                               unsigned long long& best) {
   const int rg = u / st.kp, kpi = u - rg * st.kp;
-  const int r0 = t16_row(st.rowmap, rg, g, st.n, st.head_dim);
-  const int r1 = t16_row(st.rowmap, rg, g + 8, st.n, st.head_dim);
+  int r0, r1;
+  if constexpr (Spark) {
+    const int aux = st.head_dim | (st.rotary_dim << 16);
+    r0 = t16_row_x(st.rowmap, rg, g, st.n, aux);
+    r1 = t16_row_x(st.rowmap, rg, g + 8, st.n, aux);
+  } else {
+    r0 = t16_row(st.rowmap, rg, g, st.n, st.head_dim);
+    r1 = t16_row(st.rowmap, rg, g + 8, st.n, st.head_dim);
+  }
   switch (st.epi) {
     case SPARK_EPI_BF16: {
       uint16_t* y = static_cast<uint16_t*>(st.out);
@@ -746,6 +784,13 @@ __device__ __forceinline__ void gemv_epilogue(const SparkStage& st, const SparkS
       static_cast<uint16_t*>(st.out)[r0] = f2bf(__fmul_rn(act, uf));
       break;
     }
+    case SPARK_EPI_GELU_MUL: {
+      if constexpr (Spark) {
+        const float act = bf2f(gelu_bf16(f2bf(v0), static_cast<const uint16_t*>(st.table)));
+        static_cast<uint16_t*>(st.out)[r0] = f2bf(__fmul_rn(act, bf2f(f2bf(v1))));
+      }
+      break;
+    }
     case SPARK_EPI_ARGMAX: {
       const uint16_t b0 = f2bf(v0), b1 = f2bf(v1);
       if (st.out) {
@@ -758,10 +803,29 @@ __device__ __forceinline__ void gemv_epilogue(const SparkStage& st, const SparkS
       break;
     }
     default: {  // SPARK_EPI_ROPE_KV
-      const int D = st.head_dim, half = D >> 1;
+      const int D = st.head_dim;
+      int half = D >> 1;
       const int hd = r0 / D, i = r0 - hd * D;
       float a = bf2f(f2bf(v0)), b = bf2f(f2bf(v1));
-      if (hd < st.nq + st.nkv) {
+      bool rot = hd < st.nq + st.nkv;
+      if constexpr (Spark) {
+        const int nh = st.nq + 2 * st.nkv;
+        if (hd >= nh) {  // gate rows: g = bf16(sigmoid(bf16(logit))) of head r - nh D
+          const int h0 = r0 - nh * D, h1 = r1 - nh * D;
+          uint16_t* gt = static_cast<uint16_t*>(st.gate);
+          if (h0 < st.nq) gt[h0] = f2bf(__fdiv_rn(1.0f, __fadd_rn(1.0f, spark_exp(-a))));
+          if (h1 < st.nq) gt[h1] = f2bf(__fdiv_rn(1.0f, __fadd_rn(1.0f, spark_exp(-b))));
+          break;
+        }
+        const int r = st.rotary_dim ? st.rotary_dim : D;
+        if (i < (r >> 1)) {
+          half = r >> 1;
+        } else {  // the head's dims past the rotary part: plain rows i and i + 8
+          half = 8;
+          rot = false;
+        }
+      }
+      if (rot) {
         const float c = bf2f(rope_cs[i]), sn = bf2f(rope_cs[i + half]);
         const float u2 = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, sn));
         const float w2 = __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, sn));
@@ -807,7 +871,7 @@ __device__ __forceinline__ void finish_task(const Smem& s, uint32_t seq, int tas
 
 // Q6: the kernel instantiation that also runs SPARK_STAGE_GEMV_Q6 stages (programs
 // without them use the Q4-only instantiation, whose registers the Q6 code does not touch)
-template <bool Q6>
+template <bool Q6, bool Spark>
 __device__ __forceinline__ bool gemv_stage(const StepParams& P, const SparkStage& st, const Smem& s, uint32_t& seq_base, int tid) {
   const int ncta = gridDim.x, cta = blockIdx.x, warp = tid >> 5, lane = tid & 31;
   int u0;
@@ -868,7 +932,7 @@ __device__ __forceinline__ bool gemv_stage(const StepParams& P, const SparkStage
           v0 = __fadd_rn(v0, pr[q * 16 + lane]);
           v1 = __fadd_rn(v1, pr[q * 16 + lane + 8]);
         }
-        gemv_epilogue(st, P.io, s.misc64, s.rope_cs, u, lane, v0, v1, best);
+        gemv_epilogue<Spark>(st, P.io, s.misc64, s.rope_cs, u, lane, v0, v1, best);
       }
       __syncwarp();
       if (lane == 0) {
@@ -903,30 +967,37 @@ __device__ __forceinline__ bool gemv_stage(const StepParams& P, const SparkStage
 }
 
 // ------------------------------------------------------------------ consumers: attention
-// Task (kv head g, split j): tokens [t0, t1) of the context pos + 1, T = split_len.
-// Scores: 8 lanes per token (lane jj owns dims 8jj..8jj+7, 64+8jj..64+8jj+7; even /
-// odd positions in two fma chains, butterfly 4,2,1); sc[i] = the 4 heads' scores, each
-// warp keeping the running maximum of its tokens.  Warp h < 4 then computes for head h
-// p_i = exp(s_i - m), lane l summing i = l mod 32 in ascending order (butterfly 16..1
-// gives l), and P_i = bf16(p_i).  PV: 16-token chunk c is summed by warp c % 11 (lane
-// owns dims 4 lane .. +3 of the 4 heads); the 11 warp sums are added in warp order.
-// Each split publishes O / l and lse; once every split of head g has published (the
-// head's counter grows by `splits` each launch), split j combines outputs j, j + S,
-// ... of the head group's 4 x 128 in the oracle's combine order.
+// Task (kv head g, split j): tokens [t0, t1) of the context pos + 1 (Spark sliding
+// window: of its last `window` positions), T = split_len.  Head dim D = 128 (256 in the
+// Spark instantiation).  Scores: D / 16 lanes per token (lane jj owns dims 8jj..8jj+7,
+// D/2+8jj..D/2+8jj+7; even / odd positions in two fma chains, xor butterfly over the
+// token's lanes); sc[i] = the 4 heads' scores, each warp keeping the running maximum of
+// its tokens.  Warp h < 4 then computes for head h p_i = exp(s_i - m), lane l summing
+// i = l mod 32 in ascending order (butterfly 16..1 gives l), and P_i = bf16(p_i).  PV:
+// 16-token chunk c is summed by warp c % 11 (lane owns dims D/32 lane .. +D/32-1 of the
+// 4 heads); the 11 warp sums are added in warp order.  Each split publishes O / l and
+// lse; once every split of head g has published (the head's counter grows by `splits`
+// each launch), split j combines outputs j, j + S, ... of the head group's 4 x D in the
+// oracle's combine order (Spark: then times the head's output gate).
 constexpr int kMergeRegs = 32;  // splits combined from registers (more: a loop)
 
 // One task (kv head g, split j): scores, softmax, P.V and the split's partials.
+template <int D, bool Spark>
 __device__ __forceinline__ bool attn_split(const StepParams& P, const SparkStage& st, const Smem& s, uint32_t& seq_base,
                                            int tid, int g, int j) {
   const int warp = tid >> 5, lane = tid & 31;
-  const int D = 128, nq = st.nq, S = st.splits;
+  const int nq = st.nq, S = st.splits;
   const int64_t pos = s.misc64[0], len = pos + 1;
-  const int T = split_len(len, S);
+  // Spark sliding window: positions [lo, len); the splits start at lo rounded down to 16
+  // (16-token chunks then stay inside the 64-token runs), positions before lo score -inf
+  const int64_t lo = Spark && st.window > 0 && len > st.window ? len - st.window : 0;
+  const int64_t start = lo & ~(int64_t)15;
+  const int T = split_len(len - start, S);
   if (T > kMaxSplitTokens) {
     if (tid == 0) raise_abort(P, s, SPARK_ERR_TOO_LARGE);
     return false;
   }
-  const int64_t t0 = (int64_t)j * T, t1 = t0 + T < len ? t0 + T : len;
+  const int64_t t0 = start + (int64_t)j * T, t1 = t0 + T < len ? t0 + T : len;
   const int n = t1 > t0 ? (int)(t1 - t0) : 0;
   float* part_o = st.part_o;
   float* part_lse = st.part_lse;
@@ -943,7 +1014,8 @@ __device__ __forceinline__ bool attn_split(const StepParams& P, const SparkStage
     const int64_t w0 = t0 / kRunTokens;
     const int nruns = (int)((t1 - 1) / kRunTokens - w0 + 1);
     const int nch = (n + 15) >> 4;
-    const int jj = lane & 7, grp = lane >> 3;
+    constexpr int LPT = D / 16, TPI = 32 / LPT;  // lanes per token, tokens per warp step
+    const int jj = lane & (LPT - 1), grp = lane / LPT;
     float qf[4][16];
     {
       const uint16_t* q = static_cast<const uint16_t*>(st.q) + (size_t)4 * g * D;
@@ -951,7 +1023,7 @@ __device__ __forceinline__ bool attn_split(const StepParams& P, const SparkStage
       for (int h = 0; h < 4; h++) {
         float lo[8], hi[8];
         unpack8(__ldcg(reinterpret_cast<const uint4*>(q + h * D + 8 * jj)), lo);
-        unpack8(__ldcg(reinterpret_cast<const uint4*>(q + h * D + 64 + 8 * jj)), hi);
+        unpack8(__ldcg(reinterpret_cast<const uint4*>(q + h * D + D / 2 + 8 * jj)), hi);
 #pragma unroll
         for (int m = 0; m < 8; m++) {
           qf[h][m] = lo[m];
@@ -977,21 +1049,21 @@ __device__ __forceinline__ bool attn_split(const StepParams& P, const SparkStage
         raise_abort(P, s, SPARK_ERR_LAUNCH);
         continue;
       }
-      const unsigned char* rowbase = s.ring + s.desc_off[seq % kDesc] + (ts - rs) * 256;
+      const unsigned char* rowbase = s.ring + s.desc_off[seq % kDesc] + (ts - rs) * (2 * D);
 #pragma unroll 1
-      for (int step4 = 0; step4 < 4; step4++) {
-        const int i = 16 * c + 4 * step4 + grp;
-        const bool valid = i < n;
+      for (int step4 = 0; step4 < 16 / TPI; step4++) {
+        const int i = 16 * c + TPI * step4 + grp;
+        const bool valid = i < n && (!Spark || t0 + i >= lo);
         uint4 k0 = make_uint4(0, 0, 0, 0), k1 = k0;
         if (valid) {
           if (t0 + i == pos) {
             const uint16_t* kr = kv_new + (size_t)g * D;
             k0 = __ldcg(reinterpret_cast<const uint4*>(kr + 8 * jj));
-            k1 = __ldcg(reinterpret_cast<const uint4*>(kr + 64 + 8 * jj));
+            k1 = __ldcg(reinterpret_cast<const uint4*>(kr + D / 2 + 8 * jj));
           } else {
-            const unsigned char* kr = rowbase + (4 * step4 + grp) * 256;
+            const unsigned char* kr = rowbase + (TPI * step4 + grp) * (2 * D);
             k0 = *reinterpret_cast<const uint4*>(kr + 16 * jj);
-            k1 = *reinterpret_cast<const uint4*>(kr + 128 + 16 * jj);
+            k1 = *reinterpret_cast<const uint4*>(kr + D + 16 * jj);
           }
         }
         const uint32_t kw[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
@@ -1005,13 +1077,19 @@ __device__ __forceinline__ bool attn_split(const StepParams& P, const SparkStage
             a1 = __fmaf_rn(qf[h][2 * m + 1], bf_hi(kw[m]), a1);
           }
           float v = __fadd_rn(a0, a1);
+          if constexpr (LPT == 16) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 8));
           v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 4));
           v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 2));
           v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 1));
           sc[h] = __fmul_rn(v, st.scale);
           if (valid) mx[h] = sc[h] > mx[h] ? sc[h] : mx[h];
         }
-        if (valid && jj == 0) rec[i] = make_float4(sc[0], sc[1], sc[2], sc[3]);
+        if constexpr (Spark) {
+          const float ni = __int_as_float(0xff800000);
+          if (jj == 0 && i < n) rec[i] = valid ? make_float4(sc[0], sc[1], sc[2], sc[3]) : make_float4(ni, ni, ni, ni);
+        } else {
+          if (valid && jj == 0) rec[i] = make_float4(sc[0], sc[1], sc[2], sc[3]);
+        }
       }
       finish_task(s, seq, (int)((re - rs + 15) >> 4), lane);
     }
@@ -1050,11 +1128,12 @@ __device__ __forceinline__ bool attn_split(const StepParams& P, const SparkStage
     consumer_bar();
     if (tr) tr[5] = gtimer();
     // ---- PV
-    float acc[4][4];
+    constexpr int DL = D / 32;  // dims per lane
+    float acc[4][DL];
 #pragma unroll
     for (int h = 0; h < 4; h++)
 #pragma unroll
-      for (int d = 0; d < 4; d++) acc[h][d] = 0.0f;
+      for (int d = 0; d < DL; d++) acc[h][d] = 0.0f;
     for (int c = warp; c < nch; c += kWarps) {
       const int64_t ts = t0 + 16 * c;
       int64_t rs, re;
@@ -1064,39 +1143,75 @@ __device__ __forceinline__ bool attn_split(const StepParams& P, const SparkStage
         raise_abort(P, s, SPARK_ERR_LAUNCH);
         continue;
       }
-      const unsigned char* rowbase = s.ring + s.desc_off[seq % kDesc] + (ts - rs) * 256;
+      const unsigned char* rowbase = s.ring + s.desc_off[seq % kDesc] + (ts - rs) * (2 * D);
       const int cnt = n - 16 * c < 16 ? n - 16 * c : 16;
       for (int tt = 0; tt < cnt; tt++) {
         const int i = 16 * c + tt;
         const uint2 pv = *reinterpret_cast<const uint2*>(pbf + 4 * i);
         const float p4[4] = {bf_lo(pv.x), bf_hi(pv.x), bf_lo(pv.y), bf_hi(pv.y)};
-        uint2 vv;
-        if (t0 + i == pos) {
-          vv = __ldcg(reinterpret_cast<const uint2*>(kv_new + ((size_t)st.nkv + g) * D + 4 * lane));
+        float v4[DL];
+        if constexpr (D == 128) {
+          uint2 vv;
+          if (t0 + i == pos) {
+            vv = __ldcg(reinterpret_cast<const uint2*>(kv_new + ((size_t)st.nkv + g) * D + 4 * lane));
+          } else {
+            vv = *reinterpret_cast<const uint2*>(rowbase + tt * 256 + 8 * lane);
+          }
+          v4[0] = bf_lo(vv.x);
+          v4[1] = bf_hi(vv.x);
+          v4[2] = bf_lo(vv.y);
+          v4[3] = bf_hi(vv.y);
         } else {
-          vv = *reinterpret_cast<const uint2*>(rowbase + tt * 256 + 8 * lane);
+          uint4 vv;
+          if (t0 + i == pos) {
+            vv = __ldcg(reinterpret_cast<const uint4*>(kv_new + ((size_t)st.nkv + g) * D + 8 * lane));
+          } else {
+            vv = *reinterpret_cast<const uint4*>(rowbase + tt * (2 * D) + 16 * lane);
+          }
+          unpack8(vv, v4);
         }
-        const float v4[4] = {bf_lo(vv.x), bf_hi(vv.x), bf_lo(vv.y), bf_hi(vv.y)};
 #pragma unroll
         for (int h = 0; h < 4; h++)
 #pragma unroll
-          for (int d = 0; d < 4; d++) acc[h][d] = __fmaf_rn(p4[h], v4[d], acc[h][d]);
+          for (int d = 0; d < DL; d++) acc[h][d] = __fmaf_rn(p4[h], v4[d], acc[h][d]);
       }
       finish_task(s, seq, (int)((re - rs + 15) >> 4), lane);
     }
     consumer_bar();
     if (tr) tr[6] = gtimer();
     float* red_o = reinterpret_cast<float*>(s.scratch);
+    if constexpr (D == 128) {
 #pragma unroll
-    for (int h = 0; h < 4; h++)
-      *reinterpret_cast<float4*>(red_o + (warp * 4 + h) * D + 4 * lane) =
-          make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
-    consumer_bar();
-    for (int o = tid; o < 4 * D; o += kConsumers) {
-      const int h = o >> 7, d = o & 127;
-      float v = red_o[h * D + d];
-      for (int w = 1; w < kWarps; w++) v = __fadd_rn(v, red_o[(w * 4 + h) * D + d]);
-      part_o[((size_t)j * nq + 4 * g + h) * D + d] = __fdiv_rn(v, s.red[48 + h]);
+      for (int h = 0; h < 4; h++)
+        *reinterpret_cast<float4*>(red_o + (warp * 4 + h) * D + 4 * lane) =
+            make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
+      consumer_bar();
+      for (int o = tid; o < 4 * D; o += kConsumers) {
+        const int h = o >> 7, d = o & 127;
+        float v = red_o[h * D + d];
+        for (int w = 1; w < kWarps; w++) v = __fadd_rn(v, red_o[(w * 4 + h) * D + d]);
+        part_o[((size_t)j * nq + 4 * g + h) * D + d] = __fdiv_rn(v, s.red[48 + h]);
+      }
+    } else {  // the warp sums of dims 0..127, then 128..255 (the scratch holds one half)
+#pragma unroll 1
+      for (int ph = 0; ph < 2; ph++) {
+        if ((lane >> 4) == ph) {
+#pragma unroll
+          for (int h = 0; h < 4; h++) {
+            float* dst = red_o + (warp * 4 + h) * 128 + 8 * (lane & 15);
+            *reinterpret_cast<float4*>(dst) = make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
+            *reinterpret_cast<float4*>(dst + 4) = make_float4(acc[h][4], acc[h][5], acc[h][6], acc[h][7]);
+          }
+        }
+        consumer_bar();
+        for (int o = tid; o < 4 * 128; o += kConsumers) {
+          const int h = o >> 7, d = o & 127;
+          float v = red_o[h * 128 + d];
+          for (int w = 1; w < kWarps; w++) v = __fadd_rn(v, red_o[(w * 4 + h) * 128 + d]);
+          part_o[((size_t)j * nq + 4 * g + h) * D + 128 * ph + d] = __fdiv_rn(v, s.red[48 + h]);
+        }
+        if (ph == 0) consumer_bar();  // the first half's reads before the second half's writes
+      }
     }
     if (tid < 4) part_lse[(size_t)j * nq + 4 * g + tid] = __fadd_rn(spark_log(s.red[48 + tid]), mh[tid]);
     seq_base += 2 * nruns;
@@ -1105,10 +1220,11 @@ __device__ __forceinline__ bool attn_split(const StepParams& P, const SparkStage
 }
 
 // The combine share of task (g, j), once every split of kv head g has published.
+template <int D, bool Spark>
 __device__ __forceinline__ void attn_combine(const StepParams& P, const SparkStage& st, const Smem& s, int tid, int g,
                                              int j) {
   const int warp = tid >> 5, lane = tid & 31;
-  const int D = 128, nq = st.nq, S = st.splits;
+  const int nq = st.nq, S = st.splits;
   float* part_o = st.part_o;
   float* part_lse = st.part_lse;
   unsigned long long* tr = (tid == 0 && P.io.trace)
@@ -1137,7 +1253,7 @@ __device__ __forceinline__ void attn_combine(const StepParams& P, const SparkSta
   float* den_s = w_s + 4 * S;                          // [4] max, [4] den
   const int nout = (4 * D - j + S - 1) / S;            // outputs j, j + S, ...
   const int o = j + tid * S;
-  const int oh = o >> 7, od = o & 127;
+  const int oh = o / D, od = o - oh * D;
   float ov[kMergeRegs];
   if (tid < nout && S <= kMergeRegs) {
     const float* po_h = part_o + (size_t)(4 * g + oh) * D + od;
@@ -1185,7 +1301,12 @@ __device__ __forceinline__ void attn_combine(const StepParams& P, const SparkSta
           if (lse_s[h * S + sp] != ninf) a = __fadd_rn(a, __fmul_rn(w_s[h * S + sp], __ldcg(po_h + (size_t)sp * nq * D)));
       }
     }
-    static_cast<uint16_t*>(st.attn_out)[(size_t)(4 * g + h) * D + d] = f2bf(a);
+    uint16_t ob = f2bf(a);
+    if constexpr (Spark) {
+      if (st.gate)  // headwise output gate (written by the qkv stage)
+        ob = f2bf(__fmul_rn(bf2f(ob), bf2f(__ldcg(static_cast<const unsigned short*>(st.gate) + 4 * g + h))));
+    }
+    static_cast<uint16_t*>(st.attn_out)[(size_t)(4 * g + h) * D + d] = ob;
   }
 }
 
@@ -1195,32 +1316,44 @@ __device__ __forceinline__ void attn_combine(const StepParams& P, const SparkSta
 // several tasks per CTA -- contexts longer than CTAs / kv heads splits hold -- cannot
 // deadlock).  !Multi: at most one task per CTA, in a form with no loop state (the
 // usual program; a loop here costs the GEMV stages registers in the same kernel).
-template <bool Multi>
-__device__ __forceinline__ bool attn_stage(const StepParams& P, const SparkStage& st, const Smem& s, uint32_t& seq_base,
-                                        int tid) {
+template <int D, bool Multi, bool Spark>
+__device__ __forceinline__ bool attn_stage_d(const StepParams& P, const SparkStage& st, const Smem& s,
+                                          uint32_t& seq_base, int tid) {
   const int S = st.splits, ntask = st.nkv * S;
   if constexpr (!Multi) {
     if ((int)blockIdx.x >= ntask) return true;
     const int g = blockIdx.x / S, j = blockIdx.x - g * S;
-    if (!attn_split(P, st, s, seq_base, tid, g, j)) return false;
+    if (!attn_split<D, Spark>(P, st, s, seq_base, tid, g, j)) return false;
     consumer_bar();
     if (tid == 0) asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(st.head_counters + g) : "memory");
-    attn_combine(P, st, s, tid, g, j);
+    attn_combine<D, Spark>(P, st, s, tid, g, j);
   } else {
 #pragma unroll 1
     for (int t = blockIdx.x; t < ntask; t += gridDim.x) {
-      if (!attn_split(P, st, s, seq_base, tid, t / S, t - (t / S) * S)) return false;
+      if (!attn_split<D, Spark>(P, st, s, seq_base, tid, t / S, t - (t / S) * S)) return false;
       consumer_bar();  // the split's partials (all threads) before its count
       if (tid == 0)
         asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(st.head_counters + t / S) : "memory");
     }
 #pragma unroll 1
     for (int t = blockIdx.x; t < ntask; t += gridDim.x) {
-      attn_combine(P, st, s, tid, t / S, t - (t / S) * S);
+      attn_combine<D, Spark>(P, st, s, tid, t / S, t - (t / S) * S);
       if (t + (int)gridDim.x < ntask) consumer_bar();  // its shared memory before the next task's
     }
   }
   return true;
+}
+
+// head_dim 256 in the Spark instantiation, 128 in the others (the host checks; one
+// attention body per kernel keeps its registers)
+template <bool Multi, bool Spark>
+__device__ __forceinline__ bool attn_stage(const StepParams& P, const SparkStage& st, const Smem& s, uint32_t& seq_base,
+                                        int tid) {
+  if constexpr (Spark) {
+    return attn_stage_d<256, Multi, true>(P, st, s, seq_base, tid);
+  } else {
+    return attn_stage_d<128, Multi, false>(P, st, s, seq_base, tid);
+  }
 }
 
 // ------------------------------------------------------------------ the kernel
@@ -1241,9 +1374,10 @@ __device__ __forceinline__ bool wait_stage(const StepParams& P, const Smem& s, i
 }
 
 // Q6: the program has Q6_K GEMV stages; Multi: an attention stage has more tasks than
-// CTAs.  Each is its own instantiation so the usual program (Q4_0, one attention task
-// per CTA) carries neither's registers.
-template <bool Q6, bool Multi>
+// CTAs; Spark: the program uses a Spark layer feature (head_dim 256, sliding window,
+// output gate, partial RoPE, GELU * mul).  Each is its own instantiation so the usual
+// program (Q4_0, one attention task per CTA) carries none of their registers.
+template <bool Q6, bool Multi, bool Spark>
 __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepParams P) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const Smem s = carve(smem_raw);
@@ -1263,13 +1397,13 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepParams P) {
   if (tid >= kConsumers) {
     if (tid == kConsumers) {
       Producer pr(P, s);
-      pr.run<Multi>();
+      pr.template run<Multi, Spark>();
     }
     return;
   }
   uint32_t seq_base = 0;
   for (int i = 0; i < P.num_stages; i++) {
-    if (tid < 32)  // 8-byte pieces: the inline stage in the launch parameters is only 8-byte aligned
+    if (tid < kStageWords)  // 8-byte pieces: the inline stage in the launch parameters is only 8-byte aligned
       reinterpret_cast<unsigned long long*>(s.stage)[tid] =
           reinterpret_cast<const unsigned long long*>(&stage_at(P, i))[tid];
     unsigned long long* tr = P.io.trace ? P.io.trace + ((size_t)blockIdx.x * P.num_stages + i) * kTraceSlots : nullptr;
@@ -1293,7 +1427,10 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepParams P) {
           if (bufs[b2]) asm volatile("prefetch.global.L2 [%0];" ::"l"(bufs[b2]));
       }
       // the same position / RoPE row serve every layer: fetch them once per launch
-      const long long key = (long long)reinterpret_cast<uintptr_t>(nx.pos);
+      // (Spark: sliding and full layers rotate with different tables, so the table is part
+      // of the key and a layer of the other type fetches its own row)
+      const long long key = (long long)reinterpret_cast<uintptr_t>(nx.pos) ^
+                            (Spark && rope ? (long long)reinterpret_cast<uintptr_t>(nx.cos_sin) : 0ll);
       if ((rope || nx.kind == SPARK_STAGE_ATTN) && s.misc64[3] != key && tid < 32) {
         const int64_t pos = __ldcg(nx.pos);
         if (tid == 0) {
@@ -1303,9 +1440,10 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepParams P) {
             s.misc64[1] = ((int64_t)nx.block_table[blk] * nx.nkv * nx.block_size + off) * nx.head_dim;
           }
         }
-        if (rope) {
-          const uint16_t* cs = static_cast<const uint16_t*>(nx.cos_sin) + (size_t)pos * nx.head_dim;
-          for (int d = tid; d < nx.head_dim; d += 32) s.rope_cs[d] = cs[d];
+        if (rope) {  // a row of r = rotary dims (Spark partial RoPE) or head_dim entries
+          const int r = Spark && nx.rotary_dim ? nx.rotary_dim : nx.head_dim;
+          const uint16_t* cs = static_cast<const uint16_t*>(nx.cos_sin) + (size_t)pos * r;
+          for (int d = tid; d < r; d += 32) s.rope_cs[d] = cs[d];
         }
         __syncwarp();
         if (rope && tid == 0) s.misc64[3] = key;  // cached only once the RoPE row is in place
@@ -1326,8 +1464,8 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepParams P) {
     const SparkStage& st = *s.stage;
     // both stage functions keep every consumer on the same barriers; a stage that
     // fails returns false in all threads (attention: a split longer than the scratch)
-    const bool ok = st.kind != SPARK_STAGE_ATTN ? gemv_stage<Q6>(P, st, s, seq_base, tid)
-                                                : attn_stage<Multi>(P, st, s, seq_base, tid);
+    const bool ok = st.kind != SPARK_STAGE_ATTN ? gemv_stage<Q6, Spark>(P, st, s, seq_base, tid)
+                                                : attn_stage<Multi, Spark>(P, st, s, seq_base, tid);
     consumer_bar();
     if (!ok) return;
     if (tid == 0 && tr) tr[2] = gtimer();
@@ -1400,7 +1538,7 @@ __global__ void t16_pack_kernel(const uint8_t* __restrict__ qs, const uint16_t* 
     const int u = (int)(tt / tiles);
     const int rg = u / kp, kpi = u - rg * kp;
     const int g = L >> 2, c = L & 3;
-    const int ra = t16_row(rowmap, rg, g, n, aux), rb = t16_row(rowmap, rg, g + 8, n, aux);
+    const int ra = t16_row_x(rowmap, rg, g, n, aux), rb = t16_row_x(rowmap, rg, g + 8, n, aux);
     const int b0 = kpi * (Kp >> 5) + 2 * t;
     const uint8_t* qa = qs + (size_t)ra * (k >> 1) + (size_t)b0 * 16 + 4 * c;
     const uint8_t* qb = qs + (size_t)rb * (k >> 1) + (size_t)b0 * 16 + 4 * c;

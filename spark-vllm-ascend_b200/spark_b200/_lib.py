@@ -60,7 +60,7 @@ RESTYPES = {"spark_t16_bytes": _I64, "spark_t6_bytes": _I64}
 
 
 class SparkStage(ctypes.Structure):
-    """Mirror of ``SparkStage`` in include/spark_b200.h (256 bytes)."""
+    """Mirror of ``SparkStage`` in include/spark_b200.h (280 bytes)."""
 
     _fields_ = [(n, ctypes.c_int32) for n in (
         "kind", "pro", "epi", "rowmap", "n", "k", "kp", "ks", "units", "rot", "wait", "norm", "a_parts",
@@ -68,7 +68,8 @@ class SparkStage(ctypes.Structure):
         (n, ctypes.c_float) for n in ("eps", "inv_k", "scale")] + [("row0", ctypes.c_int32)] + [
         (n, _P) for n in (
             "w", "a", "b", "embed", "token", "gamma", "res_out", "out", "cos_sin", "pos", "block_table", "k_cache",
-            "v_cache", "q", "kv_new", "key", "part_o", "part_lse", "head_counters", "attn_out")]
+            "v_cache", "q", "kv_new", "key", "part_o", "part_lse", "head_counters", "attn_out")] + [
+        ("rotary_dim", ctypes.c_int32), ("window", ctypes.c_int32), ("table", _P), ("gate", _P)]
 
 
 class SparkStepIO(ctypes.Structure):
@@ -79,7 +80,7 @@ class SparkStepIO(ctypes.Structure):
         ("window_bytes", ctypes.c_uint64), ("tp_size", ctypes.c_int32), ("tp_rank", ctypes.c_int32)]
 
 
-assert ctypes.sizeof(SparkStage) == 256
+assert ctypes.sizeof(SparkStage) == 280
 
 
 class SparkError(RuntimeError):

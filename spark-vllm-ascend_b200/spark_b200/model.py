@@ -39,15 +39,18 @@ BF16 = torch.bfloat16
 
 
 # ---------------------------------------------------------------------------- RoPE table
-def rope_cos_sin(cfg: SparkConfig, max_position: int | None = None) -> torch.Tensor:
-    """bf16 [max_pos, head_dim]: cos(pos * inv_freq) | sin(pos * inv_freq), neox layout.
+def rope_cos_sin(cfg: SparkConfig, max_position: int | None = None, theta: float | None = None,
+                 rotary_dim: int | None = None) -> torch.Tensor:
+    """bf16 [max_pos, r]: cos(pos * inv_freq) | sin(pos * inv_freq), neox layout over the
+    r rotated dims (r = head_dim, or a Spark layer type's rotary_dim, with its theta).
 
     Same construction as vLLM's RotaryEmbedding._compute_cos_sin_cache (fp32 on the
     CPU, then cast to the model dtype), which the reference feeds to its kernel as
     ``cs`` (integration/model.py:71)."""
     max_pos = max_position or cfg.max_position
-    d = cfg.head_dim
-    inv_freq = 1.0 / (cfg.rope_theta ** (torch.arange(0, d, 2, dtype=torch.float32) / d))
+    d = rotary_dim or cfg.head_dim
+    th = theta or cfg.rope_theta
+    inv_freq = 1.0 / (th ** (torch.arange(0, d, 2, dtype=torch.float32) / d))
     t = torch.arange(max_pos, dtype=torch.float32)
     freqs = torch.einsum("i,j->ij", t, inv_freq)
     return torch.cat((freqs.cos(), freqs.sin()), dim=-1).to(BF16).contiguous()
@@ -87,6 +90,11 @@ class SyntheticWeights:
     Linear weights are N(0, init_std) in fp32, quantized to Q4_0 on the device by
     ``spark_q4_quantize`` (bit-identical to gguf's quantizer).  Embeddings are bf16
     N(0, init_std).  RMSNorm weights are bf16(1 + N(0, init_std)).
+
+    Spark architecture (``cfg.spark_features``): the qkv rows end with the gate rows;
+    with ``tied_q6k_head`` the token embedding is random gguf Q6_K rows (``head_q6``,
+    d ~ N(0, init_std / 32)) whose decode is the bf16 embedding and whose codes are the
+    LM head; ``cos_sin`` serves the full layers and ``cos_sin_sliding`` the sliding ones.
     """
 
     def __init__(self, cfg: SparkConfig, device="cuda", seed: int = 0):
@@ -112,7 +120,19 @@ class SyntheticWeights:
         def norm(n):
             return (1.0 + std * torch.randn((n,), generator=gen, device=self.device)).to(BF16)
 
-        self.embed = (torch.randn((cfg.vocab_size, h), generator=gen, device=self.device) * std).to(BF16)
+        self.head_q6 = None
+        if cfg.tied_q6k_head:
+            if h % 256 or cfg.vocab_size % 16:
+                raise ValueError("a Q6_K head needs hidden % 256 == 0 and vocab % 16 == 0")
+            nb = cfg.vocab_size * (h // 256)
+            blocks = torch.randint(0, 256, (nb, 210), generator=gen, device=self.device, dtype=torch.int32)
+            blocks = blocks.to(torch.uint8)
+            d = (torch.randn(nb, generator=gen, device=self.device) * (std / 32)).to(torch.float16)
+            blocks[:, 208:210] = d.view(torch.uint8).view(nb, 2)
+            self.head_q6 = blocks.view(cfg.vocab_size, -1).contiguous()
+            self.embed = ops.q6k_dequantize(self.head_q6).view(cfg.vocab_size, h).to(BF16)
+        else:
+            self.embed = (torch.randn((cfg.vocab_size, h), generator=gen, device=self.device) * std).to(BF16)
         self.layers: list[LayerWeights] = []
         for _ in range(cfg.num_layers):
             self.layers.append(LayerWeights(
@@ -120,12 +140,19 @@ class SyntheticWeights:
                 qkv=q4(cfg.qkv_rows, h), o=q4(h, cfg.num_q_heads * cfg.head_dim),
                 gate_up=q4(2 * i, h), down=q4(h, i)))
         self.final_norm = norm(h)
-        self.head = q4(cfg.vocab_size, h)
-        self.cos_sin = rope_cos_sin(cfg).to(self.device)
+        self.head = None if cfg.tied_q6k_head else q4(cfg.vocab_size, h)
+        self.cos_sin = rope_cos_sin(cfg, theta=cfg.rope_theta, rotary_dim=cfg.rotary_dim or None).to(self.device)
+        self.cos_sin_sliding = None
+        if any(cfg.is_sliding(li) for li in range(cfg.num_layers)):
+            self.cos_sin_sliding = rope_cos_sin(cfg, theta=cfg.rope_theta_sliding or cfg.rope_theta).to(self.device)
+
+    def layer_cos_sin(self, li: int) -> torch.Tensor:
+        return self.cos_sin_sliding if self.cfg.is_sliding(li) else self.cos_sin
 
     def q4_bytes(self) -> int:
-        return sum(l.qkv.nbytes() + l.o.nbytes() + l.gate_up.nbytes() + l.down.nbytes() for l in self.layers) + \
-            self.head.nbytes()
+        """Weight bytes a decode step streams (Q4_0 layers + the LM head)."""
+        head = self.head.nbytes() if self.head is not None else self.head_q6.numel()
+        return sum(l.qkv.nbytes() + l.o.nbytes() + l.gate_up.nbytes() + l.down.nbytes() for l in self.layers) + head
 
     def to_numpy(self) -> dict:
         """Host copies (uint16 bit patterns for bf16 / fp16) for the CPU checker."""
@@ -135,8 +162,13 @@ class SyntheticWeights:
         def u8(t):
             return t.detach().contiguous().cpu().numpy()
 
-        out = {"embed": u16(self.embed), "final_norm": u16(self.final_norm), "head_qs": u8(self.head.qs),
-               "head_d": u16(self.head.d), "cos_sin": u16(self.cos_sin)}
+        out = {"embed": u16(self.embed), "final_norm": u16(self.final_norm), "cos_sin": u16(self.cos_sin)}
+        if self.head is not None:
+            out["head_qs"], out["head_d"] = u8(self.head.qs), u16(self.head.d)
+        if self.head_q6 is not None:
+            out["head_q6"] = u8(self.head_q6)
+        if self.cos_sin_sliding is not None:
+            out["cos_sin_sliding"] = u16(self.cos_sin_sliding)
         for li, l in enumerate(self.layers):
             p = f"layers.{li}."
             out[p + "in_norm"] = u16(l.in_norm)
@@ -182,6 +214,8 @@ class DecodeEngine:
         self.window = None
         if self.tp_size > 1 and mode != "step":
             raise ValueError("tensor parallelism runs on the persistent step (mode='step')")
+        if cfg.spark_features and (mode != "step" or self.tp_size > 1):
+            raise ValueError("the Spark layer features run on the single-GPU persistent step (mode='step')")
         if mode == "step":
             from . import step as _step
             self.ncta = _step.num_ctas()
@@ -245,12 +279,19 @@ class DecodeEngine:
         kp_o, kp_down = order["kp_local"]
         # T16 copies of the weights (the gguf planes stay for the per-kernel path)
         self.t16 = []
-        for lw in w.layers:
-            self.t16.append((S.q4_pack_t16(lw.qkv.qs, lw.qkv.d, 1, S.ROWS_PAIR_HALF, D),
+        rots = [cfg.layer_rope(li)[1] % D for li in range(cfg.num_layers)]  # 0: the whole head
+        for lw, rot in zip(w.layers, rots):
+            self.t16.append((S.q4_pack_t16(lw.qkv.qs, lw.qkv.d, 1, S.ROWS_PAIR_HALF, D, rot),
                              S.q4_pack_t16(lw.o.qs, lw.o.d, kp_o),
                              S.q4_pack_t16(lw.gate_up.qs, lw.gate_up.d, 1, S.ROWS_GATE_UP),
                              S.q4_pack_t16(lw.down.qs, lw.down.d, kp_down)))
-        self.t16_head = S.q4_pack_t16(w.head.qs, w.head.d, 1)
+        q6_head = getattr(w, "head_q6", None) is not None
+        if q6_head:  # the tied Q6_K embedding as LM head
+            self.t16_head = S.q6k_pack_t6(w.head_q6, cfg.vocab_size, h)
+        else:
+            self.t16_head = S.q4_pack_t16(w.head.qs, w.head.d, 1)
+        self.gate = torch.zeros(nq, dtype=BF16, device=dev) if cfg.attn_gate else None
+        self.gelu = S.gelu_table(dev) if cfg.hidden_act == "gelu" else None
         f32 = torch.float32
         if tp > 1:  # what peers write lives in the exchange window
             from . import tp as T
@@ -271,29 +312,32 @@ class DecodeEngine:
         prev = -1
         for li, (lw, (wq, wo, wgu, wd)) in enumerate(zip(w.layers, self.t16)):
             kc, vc = self.k_cache[li], self.v_cache[li]
-            rope = {"cos_sin": w.cos_sin, "pos": self.pos, "block_table": self.block_table, "k_cache": kc,
+            cs = w.layer_cos_sin(li) if hasattr(w, "layer_cos_sin") else w.cos_sin
+            rope = {"cos_sin": cs, "pos": self.pos, "block_table": self.block_table, "k_cache": kc,
                     "v_cache": vc, "q": self.q, "kv_new": self.kv_new, "block_size": bs, "nq": nq, "nkv": nkv}
             if li == 0:
                 src = {"embed": w.embed, "token": self.token}
             else:
                 src = {"a": self.down_parts, "a_parts": pa_down, "b": self.resmid}
             qkv = prog.gemv(wq, cfg.qkv_rows, h, ks=ks_qkv, gamma=lw.in_norm, eps=eps, res_out=self.res_attn,
-                            epi=S.EPI_ROPE_KV, rowmap=S.ROWS_PAIR_HALF, head_dim=D, rope=rope, wait=prev, **src)
+                            epi=S.EPI_ROPE_KV, rowmap=S.ROWS_PAIR_HALF, head_dim=D, rope=rope, wait=prev,
+                            rotary_dim=rots[li], gate=self.gate, **src)
             att = prog.attention(q=self.q, k_cache=kc, v_cache=vc, kv_new=self.kv_new, block_table=self.block_table,
                                  pos=self.pos, splits=self.splits, max_split_tokens=self.max_split_tokens,
                                  scale=cfg.attn_scale, part_o=self.part_o, part_lse=self.part_lse,
                                  head_counters=self.head_ctr[li], attn_out=self.attn_out, nq=nq, nkv=nkv, head_dim=D,
-                                 block_size=bs, wait=qkv)
+                                 block_size=bs, wait=qkv, window=cfg.layer_window(li), gate=self.gate)
             o = prog.gemv(wo, h, nq * D, kp=kp_o, ks=ks_o, a=self.attn_out, epi=S.EPI_PARTS, out=self.o_parts,
                           wait=att, xchg=xchg)
             gu = prog.gemv(wgu, 2 * i, h, ks=ks_gu, a=self.o_parts, a_parts=pa_o, b=self.res_attn,
-                           gamma=lw.post_norm, eps=eps, res_out=self.resmid, epi=S.EPI_SILU_MUL,
-                           rowmap=S.ROWS_GATE_UP, out=self.mid, wait=o)
+                           gamma=lw.post_norm, eps=eps, res_out=self.resmid,
+                           epi=S.EPI_GELU_MUL if self.gelu is not None else S.EPI_SILU_MUL,
+                           rowmap=S.ROWS_GATE_UP, out=self.mid, wait=o, table=self.gelu)
             prev = prog.gemv(wd, h, i, kp=kp_down, ks=ks_down, a=self.mid, epi=S.EPI_PARTS, out=self.down_parts,
                              wait=gu, xchg=xchg)
         prog.gemv(self.t16_head, cfg.vocab_size, h, ks=ks_head, a=self.down_parts, a_parts=pa_down, b=self.resmid,
                   gamma=w.final_norm, eps=eps, epi=S.EPI_ARGMAX, out=self.logits, key=self.key, wait=prev,
-                  xchg=xchg, row0=getattr(w, "vocab_start", 0))
+                  xchg=xchg, row0=getattr(w, "vocab_start", 0), q6=q6_head)
         prog.finalize(self.window.t["counters"] if self.window is not None else None)
         self.program = prog
         self._io = prog.io(error=self.error, key=self.key, token_out=self.token, token_log=self.token_log,

@@ -23,7 +23,7 @@ from ._lib import SparkStage, SparkStepIO, call, lib
 
 STAGE_GEMV, STAGE_ATTN, STAGE_GEMV_Q6 = 0, 1, 2
 PRO_BF16, PRO_PARTS = 0, 1
-EPI_BF16, EPI_PARTS, EPI_ROPE_KV, EPI_SILU_MUL, EPI_ARGMAX = range(5)
+EPI_BF16, EPI_PARTS, EPI_ROPE_KV, EPI_SILU_MUL, EPI_ARGMAX, EPI_GELU_MUL = range(6)
 ROWS_PLAIN, ROWS_PAIR_HALF, ROWS_GATE_UP = range(3)
 
 MAX_SLICES = 4  # slices per GEMV unit the kernel supports
@@ -53,12 +53,25 @@ def t16_bytes(n: int, k: int, kp: int) -> int:
 
 
 def q4_pack_t16(qs: torch.Tensor, d: torch.Tensor, kp: int = 1, rowmap: int = ROWS_PLAIN,
-                head_dim: int = 0) -> torch.Tensor:
-    """Re-lay Q4_0 planes (qs uint8 [n, k/2], d fp16-bits [n, k/32]) as T16 units."""
+                head_dim: int = 0, rotary_dim: int = 0) -> torch.Tensor:
+    """Re-lay Q4_0 planes (qs uint8 [n, k/2], d fp16-bits [n, k/32]) as T16 units.
+    ``ROWS_PAIR_HALF``: ``rotary_dim`` (Spark partial RoPE, 0 = head_dim) and rows past
+    the last whole head (the Spark gate rows) as the qkv epilogue expects them."""
     n, k = qs.shape[0], qs.shape[1] * 2
     out = torch.empty(t16_bytes(n, k, kp), dtype=torch.uint8, device=qs.device)
-    call("spark_q4_pack_t16", _p(qs.contiguous()), _p(d.contiguous()), n, k, kp, rowmap, head_dim, _p(out), _stream())
+    aux = head_dim | (rotary_dim << 16) if rowmap == ROWS_PAIR_HALF else head_dim
+    call("spark_q4_pack_t16", _p(qs.contiguous()), _p(d.contiguous()), n, k, kp, rowmap, aux, _p(out), _stream())
     return out
+
+
+def gelu_table(device) -> torch.Tensor:
+    """The table of ``EPI_GELU_MUL``, bf16 [4096]: torch's exact-erf gelu of the bf16
+    inputs 0x3b00 + i and 0xbb00 + i (|x| in [2^-9, 128)), built as the reference builds
+    its activation table (integration/model.py:12-16); the kernel covers the rest of the
+    range in closed form."""
+    bits = torch.arange(65536, dtype=torch.int32).to(torch.int16).view(torch.bfloat16)
+    full = torch.nn.functional.gelu(bits, approximate="none")
+    return torch.cat((full[0x3B00:0x4300], full[0xBB00:0xC300])).contiguous().to(device)
 
 
 def t6_bytes(n: int, k: int) -> int:
@@ -101,11 +114,15 @@ class StepProgram:
     def gemv(self, w: torch.Tensor, n: int, k: int, *, kp: int = 1, ks: int = 1, a=None, a_parts: int = 0,
              embed=None, token=None, b=None, gamma=None, eps: float = 0.0, res_out=None, epi: int = EPI_BF16,
              rowmap: int = ROWS_PLAIN, out=None, wait: int = -1, head_dim: int = 0, key=None, rope=None,
-             xchg: bool = False, row0: int = 0, q6: bool = False) -> int:
+             xchg: bool = False, row0: int = 0, q6: bool = False, rotary_dim: int = 0, gate=None,
+             table=None) -> int:
         """``xchg``: tensor-parallel exchange stage (parts / argmax key written to every
         rank's window, completion counted on every rank); ``row0``: global index of row 0
         for the argmax (vocab shard start); ``q6``: ``w`` holds Q6_K weights in the T6 layout
-        (``q6k_pack_t6``); slices then count 32-weight tiles."""
+        (``q6k_pack_t6``); slices then count 32-weight tiles.  Spark layer features:
+        ``rotary_dim`` (partial RoPE) and ``gate`` (bf16 [nq], computed from the gate rows
+        after the heads) for ``EPI_ROPE_KV``; ``table`` (``gelu_table()``) for
+        ``EPI_GELU_MUL``."""
         s = SparkStage()
         s.kind, s.epi, s.rowmap = (STAGE_GEMV_Q6 if q6 else STAGE_GEMV), epi, rowmap
         s.pro = PRO_PARTS if a_parts else PRO_BF16
@@ -120,6 +137,7 @@ class StepProgram:
         s.inv_k = float(torch.tensor(1.0 / k, dtype=torch.float32))
         s.head_dim = head_dim
         s.xchg, s.row0 = int(bool(xchg)), row0
+        s.rotary_dim, s.gate, s.table = rotary_dim, _p(gate), _p(table)
         s.w, s.a, s.b, s.embed, s.token = _p(w), _p(a), _p(b), _p(embed), _p(token)
         s.gamma, s.res_out, s.out, s.key = _p(gamma), _p(res_out), _p(out), _p(key)
         if rope is not None:
@@ -127,13 +145,15 @@ class StepProgram:
             s.k_cache, s.v_cache, s.q, s.kv_new = (_p(rope["k_cache"]), _p(rope["v_cache"]), _p(rope["q"]),
                                                    _p(rope["kv_new"]))
             s.block_size, s.nq, s.nkv = rope["block_size"], rope["nq"], rope["nkv"]
-        self.keep.extend([w, a, b, embed, token, gamma, res_out, out, key, rope])
+        self.keep.extend([w, a, b, embed, token, gamma, res_out, out, key, rope, gate, table])
         self.stages.append(s)
         return len(self.stages) - 1
 
     def attention(self, *, q, k_cache, v_cache, kv_new, block_table, pos, splits: int, max_split_tokens: int,
                   scale: float, part_o, part_lse, head_counters, attn_out, nq: int, nkv: int, head_dim: int,
-                  block_size: int, wait: int = -1) -> int:
+                  block_size: int, wait: int = -1, window: int = 0, gate=None) -> int:
+        """Spark layer features: ``window`` > 0 attends to the last ``window`` positions
+        (sliding layers); ``gate`` bf16 [nq] multiplies each head's output; head_dim 256."""
         s = SparkStage()
         s.kind = STAGE_ATTN
         s.wait = wait
@@ -142,7 +162,9 @@ class StepProgram:
         s.q, s.k_cache, s.v_cache, s.kv_new = _p(q), _p(k_cache), _p(v_cache), _p(kv_new)
         s.block_table, s.pos = _p(block_table), _p(pos)
         s.part_o, s.part_lse, s.head_counters, s.attn_out = _p(part_o), _p(part_lse), _p(head_counters), _p(attn_out)
-        self.keep.extend([q, k_cache, v_cache, kv_new, block_table, pos, part_o, part_lse, head_counters, attn_out])
+        s.window, s.gate = window, _p(gate)
+        self.keep.extend([q, k_cache, v_cache, kv_new, block_table, pos, part_o, part_lse, head_counters, attn_out,
+                          gate])
         self.stages.append(s)
         return len(self.stages) - 1
 
