@@ -335,7 +335,8 @@ def run_spark(args):
                 cpu = {"value": None, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
                        "sample": f"failed: {exc}"}
         result = {
-            "metric": METRIC,
+            "metric": METRIC if not cfg.spark_features else
+                      "batch-1 decode tokens/s (Spark-X2.6-4B architecture, synthetic weights, ctx 2048->2048+K)",
             "value": round(args.steps * seqs / (ms / 1e3), 3),
             "unit": "tokens/s",
             "n_gpus": world,
@@ -346,7 +347,8 @@ def run_spark(args):
             "scaling": "strong" if tp > 1 else "weak",
             "vs_baseline": None,
             "dtype": "q4_0 weights x fp32 accumulate, bf16 activations / KV",
-            "data": "synthetic: seeded N(0,0.02) weights -> Q4_0, 2048 uniform-random prompt ids",
+            "data": "synthetic: seeded N(0,0.02) weights -> Q4_0" +
+                    (", random Q6_K tied embedding" if cfg.tied_q6k_head else "") + ", 2048 uniform-random prompt ids",
             "config": {"workload": (f"configs[3]: synthetic 4B Q4_0 batch-1 decode, tensor parallel over {tp} GPUs, "
                                     "2048 prompt, greedy") if tp > 1 else
                        ("Spark-X2.6-4B architecture (gate, GELU, sliding 513 / partial RoPE, head_dim 256, tied "
@@ -365,7 +367,8 @@ def run_spark(args):
             "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": peak,
                          "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "bytes_per_launch": kb[dom], "us_per_launch": round(kern[dom], 3),
-                         "traffic": (round(kb[dom] * NCU_TRAFFIC_RATIO[dom]) if dom in NCU_TRAFFIC_RATIO
+                         "traffic": (round(kb[dom] * NCU_TRAFFIC_RATIO[dom])
+                                     if dom in NCU_TRAFFIC_RATIO and not cfg.spark_features
                                      else None),
                          "traffic_source": "ncu dram__bytes_read+write of one capture, scaled by units"},
             "step_roofline": {"bytes_per_step": step_bytes, "achieved_gbs": round(step_bytes / (tpot * 1e-3) / 1e9, 1),

@@ -1255,7 +1255,7 @@ __device__ __forceinline__ void attn_combine(const StepParams& P, const SparkSta
   const int o = j + tid * S;
   const int oh = o / D, od = o - oh * D;
   float ov[kMergeRegs];
-  if (tid < nout && S <= kMergeRegs) {
+  if (tid < nout && (S <= kMergeRegs || Spark)) {  // (Spark: the first kMergeRegs splits)
     const float* po_h = part_o + (size_t)(4 * g + oh) * D + od;
 #pragma unroll
     for (int sp = 0; sp < kMergeRegs; sp++) ov[sp] = sp < S ? __ldcg(po_h + (size_t)sp * nq * D) : 0.0f;
@@ -1295,6 +1295,20 @@ __device__ __forceinline__ void attn_combine(const StepParams& P, const SparkSta
 #pragma unroll
         for (int sp = 0; sp < kMergeRegs; sp++)
           if (sp < S && lse_s[h * S + sp] != ninf) a = __fadd_rn(a, __fmul_rn(w_s[h * S + sp], ov[sp]));
+      } else if constexpr (Spark) {  // splits 0..31 from the registers, then batches of 16 loads
+#pragma unroll
+        for (int sp = 0; sp < kMergeRegs; sp++)
+          if (lse_s[h * S + sp] != ninf) a = __fadd_rn(a, __fmul_rn(w_s[h * S + sp], ov[sp]));
+        const float* po_h = part_o + (size_t)(4 * g + h) * D + d;
+#pragma unroll 1
+        for (int s0 = kMergeRegs; s0 < S; s0 += 16) {
+          float c[16];
+#pragma unroll
+          for (int b = 0; b < 16; b++) c[b] = s0 + b < S ? __ldcg(po_h + (size_t)(s0 + b) * nq * D) : 0.0f;
+#pragma unroll
+          for (int b = 0; b < 16; b++)
+            if (s0 + b < S && lse_s[h * S + s0 + b] != ninf) a = __fadd_rn(a, __fmul_rn(w_s[h * S + s0 + b], c[b]));
+        }
       } else {
         const float* po_h = part_o + (size_t)(4 * g + h) * D + d;
         for (int sp = 0; sp < S; sp++)

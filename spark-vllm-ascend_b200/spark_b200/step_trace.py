@@ -1,6 +1,6 @@
 """Per-stage timeline of one persistent decode step (the kernel's optional trace).
 
-    python -m spark_b200.step_trace [--layers N] [--ctx C]
+    python -m spark_b200.step_trace [--layers N] [--ctx C] [--model synthetic-4b|spark-x26]
 
 Runs a synthetic model in persistent-step mode at context C, launches one traced step
 (``SparkStepIO.trace``: globaltimer stamps per CTA and stage) and prints, per stage
@@ -79,8 +79,13 @@ def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--layers", type=int, default=36)
     ap.add_argument("--ctx", type=int, default=2048)
+    ap.add_argument("--model", choices=["synthetic-4b", "spark-x26"], default="synthetic-4b")
     args = ap.parse_args(argv)
-    cfg = SparkConfig(num_layers=args.layers)
+    if args.model == "spark-x26":
+        from .config import spark_x26_config
+        cfg = spark_x26_config(num_layers=args.layers)
+    else:
+        cfg = SparkConfig(num_layers=args.layers)
     w = SyntheticWeights(cfg, device="cuda", seed=0)
     eng = DecodeEngine(w, max_seq_len=args.ctx + 64, num_blocks=(args.ctx + 64) // 128 + 8, use_graph=False)
     prog = eng.program
