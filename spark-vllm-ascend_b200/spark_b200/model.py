@@ -134,10 +134,15 @@ class SyntheticWeights:
         else:
             self.embed = (torch.randn((cfg.vocab_size, h), generator=gen, device=self.device) * std).to(BF16)
         self.layers: list[LayerWeights] = []
+        pad0 = cfg.qkv_rows - cfg.gate_rows + cfg.num_q_heads  # gate rows past the q heads: zero
         for _ in range(cfg.num_layers):
+            qkv = q4(cfg.qkv_rows, h)
+            if cfg.attn_gate:
+                qkv.qs[pad0:].zero_()
+                qkv.d[pad0:].zero_()
             self.layers.append(LayerWeights(
                 in_norm=norm(h), post_norm=norm(h),
-                qkv=q4(cfg.qkv_rows, h), o=q4(h, cfg.num_q_heads * cfg.head_dim),
+                qkv=qkv, o=q4(h, cfg.num_q_heads * cfg.head_dim),
                 gate_up=q4(2 * i, h), down=q4(h, i)))
         self.final_norm = norm(h)
         self.head = None if cfg.tied_q6k_head else q4(cfg.vocab_size, h)
