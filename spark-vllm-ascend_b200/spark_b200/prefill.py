@@ -1,0 +1,159 @@
+"""Batched prompt prefill for ``DecodeEngine``: all prompt tokens of a chunk at once.
+
+The reference keeps vLLM's standard PyTorch path for prefill and runs its megakernel
+for decode only (integration/model.py:50-62: query length > 1 falls back to the torch
+layer).  This is the same split on B200: each layer's Q4_0 weights are dequantized to
+bf16 by ``spark_q4_dequantize_bf16`` (the reference's ``dequantize(...).bfloat16()``,
+weights.py:28-31) and multiplied by the chunk's activations with bf16 tensor-core GEMMs
+(fp32 accumulation), attention is causal scaled-dot-product attention over the paged
+cache (the chunk's own K / V are written into it first), and the element-wise steps
+follow the decode engine's semantics (bf16 residual, fp32 RMSNorm, bf16-rounded inputs
+to the fp32 RoPE, SiLU / GELU of the bf16 gate, the Spark output gate and sliding
+window).  Results agree with token-by-token decode within bf16 rounding, not bit for
+bit (the GEMM summation order is cuBLAS's).  The bf16 weights are made once per engine
+(2 bytes per weight of HBM, kept for later prompts).  After ``prefill`` the engine holds
+the prompt's K / V, ``pos`` = prompt length and ``token`` = the first generated token.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+from . import ops
+
+BF16 = torch.bfloat16
+
+
+def _rmsnorm(s: torch.Tensor, gamma: torch.Tensor, eps: float) -> torch.Tensor:
+    """s fp32 [n, h] -> bf16(s / rms(s) * gamma)."""
+    inv = torch.rsqrt(s.pow(2).mean(-1, keepdim=True) + eps)
+    return (s * inv * gamma.float()).to(BF16)
+
+
+def _rope(x: torch.Tensor, cs: torch.Tensor, rot: int) -> torch.Tensor:
+    """x bf16 [n, heads, D]; cs bf16 [n, rot] (cos | sin); neox pairs (i, i + rot/2)."""
+    h = rot // 2
+    a, b = x[..., :h].float(), x[..., h:rot].float()
+    c, s = cs[:, None, :h].float(), cs[:, None, h:rot].float()
+    out = x.clone()
+    out[..., :h] = (a * c - b * s).to(BF16)
+    out[..., h:rot] = (b * c + a * s).to(BF16)
+    return out
+
+
+def _sdpa(q, K, V, scale, causal, mask=None):
+    """q [nq, n, D], K / V [nq, m, D] bf16 -> [nq, n, D]: a fused backend (flash, cuDNN,
+    memory-efficient) when one takes the shapes, else the math path."""
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+    args = (q.unsqueeze(0).contiguous(), K.unsqueeze(0).contiguous(), V.unsqueeze(0).contiguous())
+    kw = dict(is_causal=causal, scale=scale) if mask is None else dict(attn_mask=mask, scale=scale)
+    try:
+        with sdpa_kernel([SDPBackend.FLASH_ATTENTION, SDPBackend.CUDNN_ATTENTION, SDPBackend.EFFICIENT_ATTENTION]):
+            return F.scaled_dot_product_attention(*args, **kw)[0]
+    except RuntimeError:
+        return F.scaled_dot_product_attention(*args, **kw)[0]
+
+
+def _bf16_weights(eng) -> list:
+    """Per layer the bf16 dequantization of qkv / o / gate_up / down (made once per
+    engine: 2 bytes per weight of HBM, 4.5 GB for the 4B models)."""
+    if getattr(eng, "_prefill_w", None) is None:
+        deq = ops.q4_dequantize
+        eng._prefill_w = [(deq(l.qkv.qs, l.qkv.d), deq(l.o.qs, l.o.d), deq(l.gate_up.qs, l.gate_up.d),
+                           deq(l.down.qs, l.down.d)) for l in eng.w.layers]
+    return eng._prefill_w
+
+
+def _gather(cache: torch.Tensor, table: torch.Tensor, n: int, bs: int) -> torch.Tensor:
+    """Positions [0, n) of one layer's paged cache [blocks, nkv, bs, D] -> [nkv, n, D]."""
+    pos = torch.arange(n, device=cache.device)
+    return cache[table[pos // bs].long(), :, pos % bs].transpose(0, 1)
+
+
+@torch.no_grad()
+def prefill(eng, prompt: torch.Tensor, chunk: int = 2048) -> torch.Tensor:
+    """Fill ``eng``'s KV cache with ``prompt`` (int32 [P]) from position 0 and set the
+    first generated token; returns it (int32 [1])."""
+    cfg, w = eng.cfg, eng.w
+    dev = eng.device
+    prompt = torch.as_tensor(prompt, dtype=torch.int64).to(dev)
+    P = prompt.numel()
+    if P == 0 or P > eng.max_seq_len:
+        raise ValueError(f"prompt of {P} tokens (max_seq_len {eng.max_seq_len})")
+    h, i, nq, nkv, D, bs = (cfg.hidden_size, cfg.intermediate_size, cfg.num_q_heads, cfg.num_kv_heads,
+                            cfg.head_dim, cfg.block_size)
+    nh, eps, scale = nq + 2 * nkv, cfg.rms_norm_eps, cfg.attn_scale
+    table = eng.block_table
+    wb = _bf16_weights(eng)
+    heads = torch.arange(nkv, device=dev)
+    eng.reset(0)
+    a_last = b_last = None
+    for p0 in range(0, P, chunk):
+        p1 = min(P, p0 + chunk)
+        n = p1 - p0
+        pos = torch.arange(p0, p1, device=dev)
+        a = w.embed[prompt[p0:p1]]  # bf16 [n, h]
+        b = None
+        for li, (lw, (w_qkv, w_o, w_gu, w_down)) in enumerate(zip(w.layers, wb)):
+            s = a.float() + b.float() if b is not None else a.float()
+            res = s.to(BF16)
+            x = _rmsnorm(s, lw.in_norm, eps)  # (the fp32 sum, as the decode prologue)
+            y = x @ w_qkv.t()
+            q = y[:, :nq * D].reshape(n, nq, D)
+            k = y[:, nq * D:(nq + nkv) * D].reshape(n, nkv, D)
+            v = y[:, (nq + nkv) * D:nh * D].reshape(n, nkv, D)
+            _, rot = cfg.layer_rope(li)
+            cs = (w.layer_cos_sin(li) if hasattr(w, "layer_cos_sin") else w.cos_sin)[pos]
+            q, k = _rope(q, cs, rot), _rope(k, cs, rot)
+            # cache rows ((block * nkv + head) * bs + offset) of the chunk's positions
+            rows = ((table[pos // bs].long()[:, None] * nkv + heads[None, :]) * bs + (pos % bs)[:, None]).reshape(-1)
+            eng.k_cache[li].view(-1, D).index_copy_(0, rows, k.reshape(-1, D))
+            eng.v_cache[li].view(-1, D).index_copy_(0, rows, v.reshape(-1, D))
+            win = cfg.layer_window(li)
+            if p0 == 0:  # the first chunk attends to itself only
+                K, V = k.transpose(0, 1), v.transpose(0, 1)  # [nkv, n, D]
+            else:
+                K = _gather(eng.k_cache[li], table, p1, bs)  # [nkv, p1, D]
+                V = _gather(eng.v_cache[li], table, p1, bs)
+            K, V = K.repeat_interleave(nq // nkv, 0), V.repeat_interleave(nq // nkv, 0)
+            if p0 == 0 and (win == 0 or win >= n):  # plain causal: no mask
+                o = _sdpa(q.transpose(0, 1), K, V, scale, True)
+            else:
+                kp = torch.arange(p1, device=dev)
+                mask = kp[None, :] <= pos[:, None]
+                if win:
+                    mask &= kp[None, :] > pos[:, None] - win
+                o = _sdpa(q.transpose(0, 1), K, V, scale, False, mask)
+            o = o.transpose(0, 1).to(BF16)  # [n, nq, D]
+            if cfg.attn_gate:
+                g = torch.sigmoid(y[:, nh * D:nh * D + nq].float()).to(BF16)
+                o = (o.float() * g.float()[:, :, None]).to(BF16)
+            oproj = o.reshape(n, nq * D) @ w_o.t()
+            s2 = oproj.float() + res.float()
+            resmid = s2.to(BF16)
+            x2 = _rmsnorm(s2, lw.post_norm, eps)
+            gu = x2 @ w_gu.t()
+            gate, up = gu[:, :i], gu[:, i:]
+            act = F.gelu(gate, approximate="none") if cfg.hidden_act == "gelu" else F.silu(gate.float()).to(BF16)
+            mid = (act.float() * up.float()).to(BF16)
+            a = mid @ w_down.t()
+            b = resmid
+        a_last, b_last = a[-1:], b[-1:]
+    # LM head of the last position, greedy
+    x = _rmsnorm(a_last.float() + b_last.float(), w.final_norm, eps)
+    logits = torch.empty(cfg.vocab_size, dtype=BF16, device=dev)
+    rows = 16384
+    for r0 in range(0, cfg.vocab_size, rows):
+        r1 = min(cfg.vocab_size, r0 + rows)
+        if getattr(w, "head_q6", None) is not None:
+            wt = ops.q6k_dequantize(w.head_q6[r0:r1].contiguous()).view(r1 - r0, h).to(BF16)
+        else:
+            wt = ops.q4_dequantize(w.head.qs[r0:r1].contiguous(), w.head.d[r0:r1].contiguous())
+        logits[r0:r1] = (x @ wt.t())[0]
+    eng.logits.copy_(logits)
+    tok = torch.argmax(logits.float()).to(torch.int32).reshape(1)
+    eng.token.copy_(tok)
+    eng.pos.fill_(P)
+    eng.step_idx.zero_()
+    eng.key.zero_()
+    return tok.clone()
