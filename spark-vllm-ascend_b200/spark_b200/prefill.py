@@ -157,3 +157,45 @@ def prefill(eng, prompt: torch.Tensor, chunk: int = 2048) -> torch.Tensor:
     eng.step_idx.zero_()
     eng.key.zero_()
     return tok.clone()
+
+
+def main(argv=None):
+    """Time the batched prefill of a random prompt (CUDA events, best of 3 after a warm
+    call); ``--profile`` adds torch's CUDA kernel table of one prefill."""
+    import argparse
+    import json
+
+    from .config import SparkConfig, spark_x26_config
+    from .model import DecodeEngine, SyntheticWeights
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--model", choices=["synthetic-4b", "spark-x26"], default="synthetic-4b")
+    ap.add_argument("--tokens", type=int, default=2048)
+    ap.add_argument("--profile", action="store_true")
+    args = ap.parse_args(argv)
+    cfg = spark_x26_config() if args.model == "spark-x26" else SparkConfig()
+    w = SyntheticWeights(cfg, device="cuda", seed=0)
+    eng = DecodeEngine(w, max_seq_len=args.tokens + 64, num_blocks=(args.tokens + 64) // 128 + 8, use_graph=False)
+    prompt = torch.randint(0, cfg.vocab_size, (args.tokens,), generator=torch.Generator().manual_seed(0),
+                           dtype=torch.int32)
+    eng.prefill_batched(prompt)
+    torch.cuda.synchronize()
+    best = None
+    for _ in range(3):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        eng.prefill_batched(prompt)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        best = ms if best is None else min(best, ms)
+    print(json.dumps({"model": cfg.name, "tokens": args.tokens, "ttft_ms": round(best, 3)}))
+    if args.profile:
+        from torch.profiler import ProfilerActivity, profile
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            eng.prefill_batched(prompt)
+            torch.cuda.synchronize()
+        print(prof.key_averages().table(sort_by="cuda_time_total", row_limit=12, max_name_column_width=70))
+
+
+if __name__ == "__main__":
+    main()
