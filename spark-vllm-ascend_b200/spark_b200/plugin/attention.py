@@ -12,6 +12,12 @@ metadata to the sm_100a kernels:
   the slot mapping, then split-KV attention with the fused log-sum-exp combine per
   request (``spark_attn_decode``); uniform single-token decode batches are CUDA-graph
   capturable;
+* head_size 256 and sliding-window layers (the reference's Spark model,
+  plugin/spark2_5.py:140-241): decode runs the persistent step kernel's attention stage
+  as a one-stage program (``spark_step_run``, its Spark instantiation: 16 lanes per
+  token, the window's positions only).  A sliding window of W attends to W + 1
+  positions, the current one included, as the reference's kernel does (it masks below
+  len - 513 for its 512-window layers, kernels/attention.py:124-127);
 * prefill (query length > 1) is not on the decode hot path: causal attention in torch
   over the request's gathered pages, on the GPU.
 """
@@ -21,6 +27,8 @@ import math
 from dataclasses import dataclass
 from typing import ClassVar
 
+import ctypes
+
 import torch
 from vllm.v1.attention.backend import (AttentionBackend, AttentionCGSupport, AttentionImpl, AttentionMetadataBuilder,
                                        AttentionType, CommonAttentionMetadata)
@@ -29,6 +37,7 @@ from .. import ops
 
 BLOCK_SIZE = 128
 HEAD_SIZE = 128
+HEAD_SIZES = (128, 256)  # 256: the persistent kernel's attention stage (the Spark model)
 
 
 def choose_splits(max_model_len: int) -> int:
@@ -84,10 +93,14 @@ class SparkAttentionImpl(AttentionImpl[SparkAttentionMetadata]):
                  alibi_slopes: list[float] | None = None, sliding_window: int | None = None,
                  kv_cache_dtype: str = "auto", logits_soft_cap: float | None = None,
                  attn_type: str = AttentionType.DECODER, kv_sharing_target_layer_name: str | None = None) -> None:
-        if head_size != HEAD_SIZE:
-            raise ValueError(f"SparkAttentionBackend supports head_size {HEAD_SIZE}, got {head_size}")
-        if alibi_slopes is not None or sliding_window is not None or logits_soft_cap:
-            raise NotImplementedError("SparkAttentionBackend: alibi / sliding window / soft cap are not supported")
+        if head_size not in HEAD_SIZES:
+            raise ValueError(f"SparkAttentionBackend supports head_size {HEAD_SIZES}, got {head_size}")
+        if alibi_slopes is not None or logits_soft_cap:
+            raise NotImplementedError("SparkAttentionBackend: alibi / soft cap are not supported")
+        if sliding_window is not None and head_size != 256:
+            raise NotImplementedError("SparkAttentionBackend: sliding windows with head_size 256 only")
+        if head_size == 256 and num_heads != 4 * (num_kv_heads or num_heads):
+            raise NotImplementedError("SparkAttentionBackend: head_size 256 needs 4 query heads per kv head")
         if attn_type != AttentionType.DECODER:
             raise NotImplementedError("SparkAttentionBackend: decoder self-attention only")
         if kv_cache_dtype not in ("auto", "bfloat16"):
@@ -98,7 +111,10 @@ class SparkAttentionImpl(AttentionImpl[SparkAttentionMetadata]):
         self.scale = float(scale)
         self.kv_cache_dtype = kv_cache_dtype
         self.kv_sharing_target_layer_name = kv_sharing_target_layer_name
+        # positions attended by a sliding layer (the reference's 512-window layers: 513)
+        self.window = sliding_window + 1 if sliding_window is not None else 0
         self._ws: dict = {}
+        self._step = None
 
     def _workspace(self, splits: int, device) -> tuple:
         key = (splits, device)
@@ -125,6 +141,8 @@ class SparkAttentionImpl(AttentionImpl[SparkAttentionMetadata]):
         if self.kv_sharing_target_layer_name is None and key is not None:
             ops.kv_store_(key[:t].view(t, nkv, d), value[:t].view(t, nkv, d), md.slot_mapping[:t], k_cache, v_cache)
         out = output[:t].view(t, nq, d)
+        if md.is_decode and (d != HEAD_SIZE or self.window):
+            return self._decode_step(q, key, value, k_cache, v_cache, md, out, output)
         if md.is_decode:
             part_o, part_lse, counters, err = self._workspace(md.splits, query.device)
             for r in range(md.num_reqs):  # one query token per request
@@ -133,6 +151,53 @@ class SparkAttentionImpl(AttentionImpl[SparkAttentionMetadata]):
                                     error=err)
             return output
         return self._prefill(q, k_cache, v_cache, md, out, output)
+
+    def _step_state(self, md, device):
+        """Persistent buffers of the one-stage step-kernel program (fixed pointers, so a
+        captured decode graph replays them): partials, head counters, launch counters,
+        this step's k / v per request, positions, the error word."""
+        from .. import step as S
+        if self._step is None:
+            nq, nkv, d = self.num_heads, self.num_kv_heads, self.head_size
+            ncta = S.num_ctas()
+            max_len = md.splits * md.max_split_tokens  # the builder's bound on the model length
+            need = max(1, -(-max_len // S.MAX_SPLIT_TOKENS))
+            splits = max(need, max(1, -(-need * nkv // ncta)) * ncta // nkv)
+            z = lambda *sh, dt=torch.float32: torch.zeros(sh, dtype=dt, device=device)  # noqa: E731
+            self._step = {"splits": splits, "T": S.max_split_tokens(max_len, splits), "part_o": z(splits, nq, d),
+                          "part_lse": z(splits, nq), "head_ctr": z(nkv, dt=torch.int32),
+                          "counters": z(4, dt=torch.int32), "error": z(1, dt=torch.int32), "kv_new": {}, "pos": {}}
+        return self._step
+
+    def _decode_step(self, q, key, value, k_cache, v_cache, md, out, output):
+        from .. import step as S
+        from .._lib import SparkStage, call
+        st_ = self._step_state(md, q.device)
+        nq, nkv, d, R = self.num_heads, self.num_kv_heads, self.head_size, md.num_reqs
+        kvn = st_["kv_new"].get(R)
+        if kvn is None:
+            kvn = st_["kv_new"][R] = torch.zeros((R, 2, nkv, d), dtype=torch.bfloat16, device=q.device)
+            st_["pos"][R] = torch.zeros(R, dtype=torch.int64, device=q.device)
+        pos = st_["pos"][R]
+        kvn[:, 0].copy_(key[:R].view(R, nkv, d))
+        kvn[:, 1].copy_(value[:R].view(R, nkv, d))
+        pos.copy_(md.seq_lens[:R])
+        pos.sub_(1)
+        io = S.SparkStepIO()
+        io.counters, io.error, io.tp_size = ctypes.c_void_p(st_["counters"].data_ptr()), \
+            ctypes.c_void_p(st_["error"].data_ptr()), 1
+        for r in range(R):  # one query token per request
+            stg = SparkStage()
+            stg.kind, stg.wait = S.STAGE_ATTN, -1
+            stg.nq, stg.nkv, stg.head_dim, stg.block_size = nq, nkv, d, k_cache.shape[2]
+            stg.splits, stg.max_split_tokens, stg.scale, stg.window = st_["splits"], st_["T"], self.scale, self.window
+            for name, tns in (("q", q[r]), ("k_cache", k_cache), ("v_cache", v_cache), ("kv_new", kvn[r]),
+                              ("block_table", md.block_table[r]), ("pos", pos[r:r + 1]),
+                              ("part_o", st_["part_o"]), ("part_lse", st_["part_lse"]),
+                              ("head_counters", st_["head_ctr"]), ("attn_out", out[r])):
+                setattr(stg, name, ctypes.c_void_p(tns.data_ptr()))
+            call("spark_step_run", ctypes.byref(stg), None, 1, ctypes.byref(io), S._stream())
+        return output
 
     def _prefill(self, q, k_cache, v_cache, md, out, output):
         qsl = md.query_start_loc_cpu.tolist()
@@ -152,7 +217,11 @@ class SparkAttentionImpl(AttentionImpl[SparkAttentionMetadata]):
             qr = q[q0:q1].transpose(0, 1)  # [nq, lq, d]
             lq = q1 - q0
             # query i sits at absolute position n - lq + i and sees keys 0 .. n - lq + i
-            mask = torch.arange(n, device=q.device)[None, :] <= (n - lq + torch.arange(lq, device=q.device))[:, None]
+            qpos = (n - lq + torch.arange(lq, device=q.device))[:, None]
+            kpos = torch.arange(n, device=q.device)[None, :]
+            mask = kpos <= qpos
+            if self.window:  # (sliding layers: the last `window` positions)
+                mask &= kpos > qpos - self.window
             o = torch.nn.functional.scaled_dot_product_attention(qr.float(), kr.float(), vr.float(), attn_mask=mask,
                                                                  scale=self.scale)
             out[q0:q1] = o.transpose(0, 1).to(out.dtype)
@@ -187,4 +256,4 @@ class SparkAttentionBackend(AttentionBackend):
 
     @classmethod
     def get_supported_head_sizes(cls) -> list[int]:
-        return [HEAD_SIZE]
+        return list(HEAD_SIZES)

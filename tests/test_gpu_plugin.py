@@ -90,6 +90,42 @@ def test_attention_backend_decode_matches_oracle(cuda, oracle):
         assert np.array_equal(u16(out[r]).reshape(nq, D), oracle.attn_combine(po, pl))
 
 
+def test_attention_backend_spark_head256_window(cuda, oracle):
+    """The Spark model's attention through the vLLM backend: head_size 256, 16 q / 4 kv
+    heads, a sliding layer (window 512 -> the reference's 513 positions) and a full one;
+    decode bit-exact against the oracle's persistent-step order, twice in a row."""
+    import torch
+    from spark_b200 import step
+    nq, nkv, D, bs = 16, 4, 256, 128
+    seq_lens = [300, 2049]
+    for window in (None, 512):
+        kv, table, _, MD = _backend_setup(seq_lens, nq=nq, nkv=nkv, D=D, seed=7)
+        from spark_b200.plugin.attention import SparkAttentionImpl
+        impl = SparkAttentionImpl(nq, D, 1 / 16, nkv, sliding_window=window)
+        t = len(seq_lens)
+        q = torch.randn((t, nq * D), device="cuda").to(torch.bfloat16)
+        k = torch.randn((t, nkv * D), device="cuda").to(torch.bfloat16)
+        v = torch.randn((t, nkv * D), device="cuda").to(torch.bfloat16)
+        slots = torch.tensor([int(table[r, (n - 1) // bs]) * bs + (n - 1) % bs for r, n in enumerate(seq_lens)],
+                             device="cuda", dtype=torch.int64)
+        md = MD(num_actual_tokens=t, num_reqs=t, max_query_len=1, max_seq_len=max(seq_lens),
+                query_start_loc=torch.arange(t + 1, device="cuda", dtype=torch.int32),
+                query_start_loc_cpu=torch.arange(t + 1, dtype=torch.int32),
+                seq_lens=torch.tensor(seq_lens, device="cuda", dtype=torch.int32), block_table=table,
+                slot_mapping=slots, splits=24, max_split_tokens=96)
+        out = torch.empty((t, nq * D), device="cuda", dtype=torch.bfloat16)
+        for rep in range(2):  # a second call (next launch generation) gives the same
+            impl.forward(None, q, k, v, kv, md, out)
+            torch.cuda.synchronize()
+            kc, vc = u16(kv[0]), u16(kv[1])
+            for r, n in enumerate(seq_lens):
+                S = impl._step["splits"]
+                po, pl = oracle.attn_split(u16(q[r]).reshape(nq, D), kc, vc, table[r].cpu().numpy(), n, S,
+                                           impl.scale, chunk_accs=step.CHUNK_ACCS, window=impl.window)
+                assert np.array_equal(u16(out[r]).reshape(nq, D), oracle.attn_combine(po, pl)), (window, r, rep)
+        assert int(impl._step["error"].item()) == 0
+
+
 def test_attention_backend_prefill_causal(cuda, oracle):
     import torch
     nq, nkv, D, bs = 32, 8, 128, 128

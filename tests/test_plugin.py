@@ -73,7 +73,7 @@ def test_attention_backend_layout_and_metadata():
     from vllm.v1.attention.backend import AttentionCGSupport, CommonAttentionMetadata
     B = SparkAttentionBackend
     assert B.get_kv_cache_shape(10, 128, 8, 128) == (2, 10, 8, 128, 128)
-    assert B.get_supported_kernel_block_sizes() == [128] and B.get_supported_head_sizes() == [128]
+    assert B.get_supported_kernel_block_sizes() == [128] and B.get_supported_head_sizes() == [128, 256]
     assert B.get_impl_cls() is SparkAttentionImpl and B.get_builder_cls() is SparkAttentionMetadataBuilder
     assert B.get_kv_cache_block_dim(128, 8, 128) == 1
     assert SparkAttentionMetadataBuilder._cudagraph_support == AttentionCGSupport.UNIFORM_SINGLE_TOKEN_DECODE
@@ -91,5 +91,8 @@ def test_attention_backend_layout_and_metadata():
     assert impl.num_kv_heads == 8
     with pytest.raises(ValueError):
         SparkAttentionImpl(32, 64, 0.125, 8)
-    with pytest.raises(NotImplementedError):
+    with pytest.raises(NotImplementedError):  # windows: the head_size-256 (Spark) path only
         SparkAttentionImpl(32, 128, 0.1, 8, sliding_window=512)
+    assert SparkAttentionImpl(16, 256, 0.0625, 4, sliding_window=512).window == 513
+    with pytest.raises(NotImplementedError):  # head_size 256 takes 4 query heads per kv head
+        SparkAttentionImpl(16, 256, 0.0625, 8)
