@@ -262,16 +262,27 @@ def default_order(cfg, ncta: int, tp: int = 1) -> dict:
     }
 
 
-def attn_splits(cfg, ncta: int, max_seq_len: int = 0) -> int:
-    """Splits per kv head: one (kv head, split) task per CTA, or more when the context
-    needs them (a split holds at most MAX_SPLIT_TOKENS tokens; CTAs then run several
-    tasks in turn).  The count fills whole rounds of tasks over the CTAs (8 kv heads on
-    148 CTAs: 18 splits = 144 tasks, then 37 = 296 = two per CTA, ...), so no CTA runs
-    a round more than the others with fewer tokens per task."""
-    nkv = cfg.num_kv_heads
+SHORT_SPLITS = 18  # splits per kv head when the context allows (measured best, see splits_for)
+
+
+def splits_for(nkv: int, ncta: int, max_seq_len: int = 0) -> int:
+    """Splits per kv head.  A context that fits SHORT_SPLITS splits of MAX_SPLIT_TOKENS
+    takes min(CTAs / kv heads, SHORT_SPLITS): each (kv head, split) task has a fixed cost
+    (q load, barriers, softmax warps, publish, combine share) that outweighs a shorter
+    K / V stream -- measured at ctx 2048: 8 kv heads x 128 dims best at 18 (9, 12 worse),
+    4 x 256 at 18-24 (27, 32, 37 worse).  Longer contexts take the fewest splits that hold
+    them, rounded up to whole rounds of tasks over the CTAs (8 kv heads: 37 = 296 tasks =
+    two per CTA, ...) so no CTA runs a round more than the others."""
     need = max(1, -(-max_seq_len // MAX_SPLIT_TOKENS))
+    if need <= SHORT_SPLITS:
+        return max(need, min(max(1, ncta // nkv), SHORT_SPLITS))
     rounds = max(1, -(-need * nkv // ncta))
     return max(need, rounds * ncta // nkv)
+
+
+def attn_splits(cfg, ncta: int, max_seq_len: int = 0) -> int:
+    """Splits per kv head of ``cfg`` (the rank's local config under tensor parallelism)."""
+    return splits_for(cfg.num_kv_heads, ncta, max_seq_len)
 
 
 def max_split_tokens(max_seq_len: int, splits: int) -> int:
