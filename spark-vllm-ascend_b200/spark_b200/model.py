@@ -219,8 +219,8 @@ class DecodeEngine:
         self.window = None
         if self.tp_size > 1 and mode != "step":
             raise ValueError("tensor parallelism runs on the persistent step (mode='step')")
-        if cfg.spark_features and (mode != "step" or self.tp_size > 1):
-            raise ValueError("the Spark layer features run on the single-GPU persistent step (mode='step')")
+        if cfg.spark_features and mode != "step":
+            raise ValueError("the Spark layer features run on the persistent step (mode='step')")
         if mode == "step":
             from . import step as _step
             self.ncta = _step.num_ctas()

@@ -161,7 +161,7 @@ class SparkAttentionImpl(AttentionImpl[SparkAttentionMetadata]):
             nq, nkv, d = self.num_heads, self.num_kv_heads, self.head_size
             ncta = S.num_ctas()
             max_len = md.splits * md.max_split_tokens  # the builder's bound on the model length
-            splits = S.splits_for(nkv, ncta, max_len)
+            splits = S.splits_for(nkv, ncta, max_len, d)
             z = lambda *sh, dt=torch.float32: torch.zeros(sh, dtype=dt, device=device)  # noqa: E731
             self._step = {"splits": splits, "T": S.max_split_tokens(max_len, splits), "part_o": z(splits, nq, d),
                           "part_lse": z(splits, nq), "head_ctr": z(nkv, dt=torch.int32),

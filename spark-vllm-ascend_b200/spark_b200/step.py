@@ -262,27 +262,30 @@ def default_order(cfg, ncta: int, tp: int = 1) -> dict:
     }
 
 
-SHORT_SPLITS = 18  # splits per kv head when the context allows (measured best, see splits_for)
+SHORT_SPLITS_256 = 18  # head_dim 256: splits per kv head when the context allows (see splits_for)
 
 
-def splits_for(nkv: int, ncta: int, max_seq_len: int = 0) -> int:
-    """Splits per kv head.  A context that fits SHORT_SPLITS splits of MAX_SPLIT_TOKENS
-    takes min(CTAs / kv heads, SHORT_SPLITS): each (kv head, split) task has a fixed cost
-    (q load, barriers, softmax warps, publish, combine share) that outweighs a shorter
-    K / V stream -- measured at ctx 2048: 8 kv heads x 128 dims best at 18 (9, 12 worse),
-    4 x 256 at 18-24 (27, 32, 37 worse).  Longer contexts take the fewest splits that hold
-    them, rounded up to whole rounds of tasks over the CTAs (8 kv heads: 37 = 296 tasks =
-    two per CTA, ...) so no CTA runs a round more than the others."""
+def splits_for(nkv: int, ncta: int, max_seq_len: int = 0, head_dim: int = 128) -> int:
+    """Splits per kv head.  A context that fits: head_dim 128 takes one (kv head, split)
+    task per CTA (CTAs / kv heads), head_dim 256 at most SHORT_SPLITS_256 -- its tasks'
+    fixed cost (q load, barriers, softmax warps, publish, combine share) outweighs the
+    idle CTAs.  Measured at ctx 2048: 8 kv heads x 128 dims best at 18 (12, 9 worse),
+    4 x 128 (tensor parallel over 2) at 37 (18: 376 vs 416 tok/s), 4 x 256 at 18-24 (27,
+    32, 37 worse).  Longer contexts take the fewest splits that hold them, rounded up to
+    whole rounds of tasks over the CTAs (8 kv heads: 37 = 296 tasks = two per CTA, ...)
+    so no CTA runs a round more than the others."""
     need = max(1, -(-max_seq_len // MAX_SPLIT_TOKENS))
-    if need <= SHORT_SPLITS:
-        return max(need, min(max(1, ncta // nkv), SHORT_SPLITS))
+    one_round = max(1, ncta // nkv)
+    short = one_round if head_dim <= 128 else min(one_round, SHORT_SPLITS_256)
+    if need <= short:
+        return short
     rounds = max(1, -(-need * nkv // ncta))
     return max(need, rounds * ncta // nkv)
 
 
 def attn_splits(cfg, ncta: int, max_seq_len: int = 0) -> int:
     """Splits per kv head of ``cfg`` (the rank's local config under tensor parallelism)."""
-    return splits_for(cfg.num_kv_heads, ncta, max_seq_len)
+    return splits_for(cfg.num_kv_heads, ncta, max_seq_len, cfg.head_dim)
 
 
 def max_split_tokens(max_seq_len: int, splits: int) -> int:

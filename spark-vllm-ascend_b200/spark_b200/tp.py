@@ -141,12 +141,26 @@ def local_config(cfg: SparkConfig, tp: int) -> SparkConfig:
 
 
 def qkv_rows(cfg: SparkConfig, rank: int, tp: int) -> torch.Tensor:
-    """Rows of the fused qkv weight rank r owns: its q heads, then k heads, then v heads."""
+    """Rows of the fused qkv weight rank r owns: its q heads, then k heads, then v heads,
+    then (Spark output gate) its q heads' gate rows (the caller pads those to 16)."""
     D, nq, nkv = cfg.head_dim, cfg.num_q_heads, cfg.num_kv_heads
     ql, kl = nq // tp, nkv // tp
     heads = [*range(rank * ql, (rank + 1) * ql), *(nq + h for h in range(rank * kl, (rank + 1) * kl)),
              *(nq + nkv + h for h in range(rank * kl, (rank + 1) * kl))]
-    return torch.cat([torch.arange(h * D, (h + 1) * D) for h in heads])
+    rows = [torch.arange(h * D, (h + 1) * D) for h in heads]
+    if cfg.attn_gate:
+        g0 = (nq + 2 * nkv) * D
+        rows.append(torch.arange(g0 + rank * ql, g0 + (rank + 1) * ql))
+    return torch.cat(rows)
+
+
+def _pad_rows(lin: Q4Linear, rows: int) -> Q4Linear:
+    """Zero Q4_0 rows appended up to ``rows`` (the local gate rows' 16-row padding)."""
+    n = rows - lin.n
+    if n <= 0:
+        return lin
+    return Q4Linear(torch.cat([lin.qs, torch.zeros((n, lin.qs.shape[1]), dtype=lin.qs.dtype, device=lin.qs.device)]),
+                    torch.cat([lin.d, torch.zeros((n, lin.d.shape[1]), dtype=lin.d.dtype, device=lin.d.device)]))
 
 
 def gate_up_rows(cfg: SparkConfig, rank: int, tp: int) -> torch.Tensor:
@@ -182,16 +196,25 @@ class ShardWeights:
         il = i // tp
         self.vocab_start = rank * (cfg.vocab_size // tp)
         qr, gr = qkv_rows(cfg, rank, tp), gate_up_rows(cfg, rank, tp)
-        self.layers = [LayerWeights(in_norm=l.in_norm, post_norm=l.post_norm, qkv=rows_of(l.qkv, qr),
+        self.layers = [LayerWeights(in_norm=l.in_norm, post_norm=l.post_norm,
+                                    qkv=_pad_rows(rows_of(l.qkv, qr), self.cfg.qkv_rows),
                                     o=cols_of(l.o, rank * ko, (rank + 1) * ko), gate_up=rows_of(l.gate_up, gr),
                                     down=cols_of(l.down, rank * il, (rank + 1) * il)) for l in full.layers]
         self.embed, self.final_norm, self.cos_sin = full.embed, full.final_norm, full.cos_sin
+        self.cos_sin_sliding = getattr(full, "cos_sin_sliding", None)
         vl = cfg.vocab_size // tp
-        self.head = rows_of(full.head, torch.arange(self.vocab_start, self.vocab_start + vl))
+        if getattr(full, "head_q6", None) is not None:  # the tied Q6_K head: this rank's vocab rows
+            self.head, self.head_q6 = None, full.head_q6[self.vocab_start:self.vocab_start + vl].contiguous()
+        else:
+            self.head_q6 = None
+            self.head = rows_of(full.head, torch.arange(self.vocab_start, self.vocab_start + vl))
+
+    def layer_cos_sin(self, li: int) -> torch.Tensor:
+        return self.cos_sin_sliding if self.cfg.is_sliding(li) else self.cos_sin
 
     def q4_bytes(self) -> int:
-        return sum(l.qkv.nbytes() + l.o.nbytes() + l.gate_up.nbytes() + l.down.nbytes() for l in self.layers) + \
-            self.head.nbytes()
+        head = self.head.nbytes() if self.head is not None else self.head_q6.numel()
+        return sum(l.qkv.nbytes() + l.o.nbytes() + l.gate_up.nbytes() + l.down.nbytes() for l in self.layers) + head
 
 
 def window_fields(cfg_local: SparkConfig, order: dict, num_stages: int, tp: int) -> list:

@@ -43,6 +43,18 @@ def test_tp_tiny_64_tokens_match_oracle(cuda, world):
     assert r0["oracle_tokens_equal"] and r0["oracle_logits_equal"]
 
 
+@pytest.mark.parametrize("world", [2])
+def test_tp_spark_tiny_matches_oracle(cuda, world):
+    """The Spark architecture over 2 ranks (gate rows and the Q6_K head sharded with the
+    heads / vocab; a prompt past the sliding window): identical tokens and logits."""
+    if _gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
+    res = _run(world, "--config", "spark-tiny", "--prompt", "70", "--new-tokens", "16")
+    assert len(res) == world and all(r["ok"] for r in res), res
+    r0 = next(r for r in res if r["rank"] == 0)
+    assert r0["oracle_tokens_equal"] and r0["oracle_logits_equal"]
+
+
 @pytest.mark.slow
 @pytest.mark.parametrize("world", [2])
 def test_tp_full_size_matches_oracle(cuda, world):

@@ -33,7 +33,7 @@ def u16(t):
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("--config", choices=["tiny", "full"], default="tiny")
+    ap.add_argument("--config", choices=["tiny", "full", "spark-tiny"], default="tiny")
     ap.add_argument("--layers", type=int, default=0)
     ap.add_argument("--prompt", type=int, default=24)
     ap.add_argument("--new-tokens", type=int, default=64)
@@ -50,11 +50,16 @@ def main(argv=None):
     torch.cuda.set_device(local)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", local))
     from spark_b200 import tp as T
-    from spark_b200.config import SparkConfig, tiny_config
+    from spark_b200.config import SparkConfig, spark_x26_config, tiny_config
     from spark_b200.model import DecodeEngine, SyntheticWeights
 
     kw = {"num_layers": args.layers} if args.layers else {}
-    cfg = tiny_config(**kw) if args.config == "tiny" else SparkConfig(max_position=4096, **kw)
+    if args.config == "spark-tiny":  # the Spark architecture (gate, GELU, sliding window, Q6_K head)
+        cfg = spark_x26_config(num_layers=args.layers or 4, hidden_size=512, num_q_heads=8, num_kv_heads=2,
+                               intermediate_size=1024, vocab_size=4096, sliding_window=33, max_position=4096,
+                               name="spark-tiny")
+    else:
+        cfg = tiny_config(**kw) if args.config == "tiny" else SparkConfig(max_position=4096, **kw)
     full = SyntheticWeights(cfg, device="cuda", seed=args.seed)
     shard = T.ShardWeights(full, rank, world)
     host_weights = full.to_numpy() if rank == 0 and not args.no_oracle else None
@@ -76,8 +81,11 @@ def main(argv=None):
     ok = err == 0 and res["ranks_agree"]
     if rank == 0 and not args.no_oracle:
         import oracle
-        om = oracle.OracleModel(cfg, host_weights, num_blocks=eng.num_blocks, splits=eng.splits,
-                                order=eng.oracle_order())
+        if cfg.spark_features:
+            om = oracle.SparkOracleModel(cfg, host_weights, eng.num_blocks, eng.splits, eng.oracle_order())
+        else:
+            om = oracle.OracleModel(cfg, host_weights, num_blocks=eng.num_blocks, splits=eng.splits,
+                                    order=eng.oracle_order())
         table = eng.block_table.cpu().numpy()
         pos, tok = 0, None
         for t in prompt:
