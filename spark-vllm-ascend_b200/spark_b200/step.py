@@ -270,7 +270,7 @@ def splits_for(nkv: int, ncta: int, max_seq_len: int = 0, head_dim: int = 128) -
     task per CTA (CTAs / kv heads), head_dim 256 at most SHORT_SPLITS_256 -- its tasks'
     fixed cost (q load, barriers, softmax warps, publish, combine share) outweighs the
     idle CTAs.  Measured at ctx 2048: 8 kv heads x 128 dims best at 18 (12, 9 worse),
-    4 x 128 (tensor parallel over 2) at 37 (18: 376 vs 416 tok/s), 4 x 256 at 18-24 (27,
+    4 x 128 (tensor parallel over 2) the same at 18 and 37, 4 x 256 best at 18-24 (27,
     32, 37 worse).  Longer contexts take the fewest splits that hold them, rounded up to
     whole rounds of tasks over the CTAs (8 kv heads: 37 = 296 tasks = two per CTA, ...)
     so no CTA runs a round more than the others."""
