@@ -38,15 +38,18 @@ Q4_0, Q6_K, F32, F16, BF16_T = 2, 14, 0, 1, 30
 
 def verify(path, sha256: str | None = None) -> dict:
     """Size and sha256 of ``path`` against ``DOWNLOAD_VERIFIED.json`` beside it (when
-    present) and against ``sha256`` (when given); raises ValueError on a mismatch."""
+    present) and against ``sha256`` (when given); raises ValueError on a mismatch.  With
+    neither, the file is not hashed (``sha256`` None in the result)."""
     p = Path(path)
     size = p.stat().st_size
+    rec = p.with_name("DOWNLOAD_VERIFIED.json")
+    if sha256 is None and not rec.exists():  # nothing to check against: skip the hash
+        return {"size": size, "sha256": None}
     h = hashlib.sha256()
     with open(p, "rb") as f:
         for chunk in iter(lambda: f.read(1 << 24), b""):
             h.update(chunk)
     digest = h.hexdigest()
-    rec = p.with_name("DOWNLOAD_VERIFIED.json")
     if rec.exists():
         v = json.loads(rec.read_text())
         if int(v.get("size", size)) != size:

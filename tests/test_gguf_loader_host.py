@@ -69,6 +69,7 @@ def test_verify_download_record(tmp_path):
     data = p.read_bytes()
     sha = hashlib.sha256(data).hexdigest()
     assert gguf_loader.verify(p, sha)["size"] == len(data)
+    assert gguf_loader.verify(p)["sha256"] is None  # no record, no expected digest: not hashed
     rec = tmp_path / "DOWNLOAD_VERIFIED.json"
     rec.write_text(json.dumps({"size": len(data), "sha256": sha}))
     assert gguf_loader.verify(p)["sha256"] == sha
