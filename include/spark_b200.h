@@ -177,6 +177,17 @@ int spark_silu_mul(const uint16_t* g, const uint16_t* u, int64_t n, uint16_t* ou
  * Replaces the rotation in FusedQkvStage.calculate_rotated (kernels/qkv.py:179-189). */
 int spark_rope_neox(uint16_t* x, int nh, int head_dim, const uint16_t* cos_sin, const int64_t* pos, void* stream);
 
+/* Prefill helpers over `rows` tokens at once.  The reference prefills with vLLM's torch
+ * layers (integration/model.py:50-62); these replace the torch element-wise steps of the
+ * batched prefill (spark_b200/prefill.py).  add + RMSNorm per row (hidden <= 12288,
+ * res_out nullable): res_out = bf16(a + b), y = bf16((a+b) * rsqrt(mean((a+b)^2) + eps)
+ * * gamma).  RoPE in place on `nh` heads of each row (row r at x + r * row_stride,
+ * position pos0 + r; pairs (i, i + rotary_dim / 2), cos_sin rows of rotary_dim). */
+int spark_add_rmsnorm_rows(const uint16_t* a, const uint16_t* b, const uint16_t* gamma, float eps, int rows,
+                           int hidden, uint16_t* res_out, uint16_t* y, void* stream);
+int spark_rope_neox_rows(uint16_t* x, int64_t row_stride, int rows, int nh, int head_dim, int rotary_dim,
+                         const uint16_t* cos_sin, int64_t pos0, void* stream);
+
 /* Store this step's keys and values into the paged caches: k / v bf16
  * [tokens][nkv][head_dim] -> k_cache / v_cache bf16 [blocks][nkv][block_size][head_dim]
  * at slot_mapping[t] (int64; negative = padding, skipped).  head_dim % 8 == 0, 16-byte

@@ -141,6 +141,54 @@ __global__ void rope_neox_kernel(uint16_t* x, int nh, int dim, const uint16_t* _
   }
 }
 
+// ------------------------------------------------------------------ prefill rows
+// add + RMSNorm of n rows (one CTA of 256 threads per row): res_out = bf16(a + b),
+// y = bf16((a + b) * rsqrt(mean((a + b)^2) + eps) * gamma).  Prefill only: the sum of
+// squares is a block tree, not the decode path's canonical lane order.
+__global__ void __launch_bounds__(256) add_rmsnorm_rows_kernel(const uint16_t* __restrict__ a,
+                                                               const uint16_t* __restrict__ b,
+                                                               const uint16_t* __restrict__ gamma, float eps,
+                                                               float inv_h, int h, uint16_t* res_out, uint16_t* y) {
+  extern __shared__ float s_row[];  // [h] then [8] warp partials
+  const size_t off = (size_t)blockIdx.x * h;
+  float part = 0.0f;
+  for (int i = threadIdx.x; i < h; i += blockDim.x) {
+    const float s = b ? __fadd_rn(bf2f(a[off + i]), bf2f(b[off + i])) : bf2f(a[off + i]);
+    s_row[i] = s;
+    if (res_out) res_out[off + i] = f2bf(s);
+    part = __fmaf_rn(s, s, part);
+  }
+  part = butterfly_sum<32>(part);
+  float* red = s_row + h;
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = part;
+  __syncthreads();
+  float tot = 0.0f;
+  for (int w = 0; w < (int)(blockDim.x >> 5); w++) tot += red[w];
+  const float inv = rsqrtf(__fadd_rn(__fmul_rn(tot, inv_h), eps));
+  for (int i = threadIdx.x; i < h; i += blockDim.x)
+    y[off + i] = f2bf(__fmul_rn(__fmul_rn(s_row[i], inv), bf2f(gamma[i])));
+}
+
+// In-place neox RoPE of n rows of `nh` heads (row r at x + r * row_stride, position
+// pos0 + r), pairs (i, i + rot/2) with cos_sin rows of rot entries (the decode kernels'
+// arithmetic: separate products, then the rounded difference / sum).
+__global__ void rope_rows_kernel(uint16_t* x, int64_t row_stride, int n, int nh, int dim, int rot,
+                                 const uint16_t* __restrict__ cos_sin, int64_t pos0) {
+  const int half = rot >> 1;
+  const int64_t total = (int64_t)n * nh * half;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = idx / (nh * half);
+    const int rem = (int)(idx - r * nh * half), h = rem / half, i = rem - h * half;
+    uint16_t* v = x + r * row_stride + (int64_t)h * dim;
+    const uint16_t* cs = cos_sin + (pos0 + r) * rot;
+    const float a = bf2f(v[i]), b = bf2f(v[i + half]);
+    const float c = bf2f(cs[i]), s = bf2f(cs[i + half]);
+    v[i] = f2bf(__fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s)));
+    v[i + half] = f2bf(__fadd_rn(__fmul_rn(b, c), __fmul_rn(a, s)));
+  }
+}
+
 // ------------------------------------------------------------------ slot mapping (integration/slot_mapping.py:8-22)
 __global__ void slot_mapping_kernel(int64_t n, int64_t max_tokens, const int32_t* __restrict__ query_start,
                                     const int64_t* __restrict__ positions, const int32_t* __restrict__ table,

@@ -7,6 +7,7 @@
 // launch and prologue with the tail of the previous kernel.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdint>
 #include <cstring>
 #include <mutex>
@@ -575,6 +576,26 @@ int spark_silu_mul(const uint16_t* g, const uint16_t* u, int64_t n, uint16_t* ou
   int64_t grid = (n + 255) / 256;
   if (grid > 4 * num_sms()) grid = 4 * num_sms();
   return launch(silu_mul_kernel, dim3((unsigned)grid), dim3(256), 0, as_stream(stream), g, u, n, out);
+}
+
+int spark_add_rmsnorm_rows(const uint16_t* a, const uint16_t* b, const uint16_t* gamma, float eps, int rows,
+                           int hidden, uint16_t* res_out, uint16_t* y, void* stream) {
+  if (!a || !gamma || !y) return SPARK_ERR_INVALID_ARG;
+  if (rows <= 0 || hidden <= 0 || hidden > 12288) return SPARK_ERR_UNSUPPORTED_SHAPE;
+  return launch(add_rmsnorm_rows_kernel, dim3((unsigned)rows), dim3(256), (size_t)(hidden + 8) * sizeof(float),
+                as_stream(stream), a, b, gamma, eps, (float)(1.0 / (double)hidden), hidden, res_out, y);
+}
+
+int spark_rope_neox_rows(uint16_t* x, int64_t row_stride, int rows, int nh, int head_dim, int rotary_dim,
+                         const uint16_t* cos_sin, int64_t pos0, void* stream) {
+  if (!x || !cos_sin) return SPARK_ERR_INVALID_ARG;
+  if (rows <= 0 || nh <= 0 || head_dim <= 0 || rotary_dim <= 0 || rotary_dim > head_dim || rotary_dim % 2 ||
+      pos0 < 0 || row_stride < (int64_t)nh * head_dim)
+    return SPARK_ERR_UNSUPPORTED_SHAPE;
+  const int64_t total = (int64_t)rows * nh * (rotary_dim / 2);
+  const int64_t grid = std::min<int64_t>((total + 255) / 256, 16LL * num_sms());
+  return launch(rope_rows_kernel, dim3((unsigned)grid), dim3(256), 0, as_stream(stream), x, row_stride, rows, nh,
+                head_dim, rotary_dim, cos_sin, pos0);
 }
 
 int spark_rope_neox(uint16_t* x, int nh, int head_dim, const uint16_t* cos_sin, const int64_t* pos, void* stream) {

@@ -221,6 +221,28 @@ def rope_neox_(x, cos_sin, pos):
     return x
 
 
+def add_rmsnorm_rows(a: torch.Tensor, b: torch.Tensor | None, gamma: torch.Tensor, eps: float):
+    """Prefill rows: a / b bf16 [n, h] -> (bf16(a + b), bf16 RMSNorm(a + b) * gamma)."""
+    _cuda(a, "a", BF16)
+    _cuda(gamma, "gamma", BF16)
+    n, h = a.shape
+    a = a.contiguous()
+    b = None if b is None else b.contiguous()
+    res, y = torch.empty_like(a), torch.empty_like(a)
+    call("spark_add_rmsnorm_rows", _p(a), _p(b), _p(gamma), float(eps), n, h, _p(res), _p(y), _stream())
+    return res, y
+
+
+def rope_rows_(x: torch.Tensor, nh: int, head_dim: int, rotary_dim: int, cos_sin: torch.Tensor, pos0: int):
+    """In-place RoPE of the first ``nh`` heads of each row of x (bf16 [n, >= nh * head_dim],
+    rows contiguous), row r at position pos0 + r."""
+    _cuda(x, "x", BF16)
+    _check(x.dim() == 2 and x.stride(1) == 1, "x must be [rows, cols] with contiguous rows")
+    call("spark_rope_neox_rows", _p(x), x.stride(0), x.shape[0], nh, head_dim, rotary_dim, _p(cos_sin), pos0,
+         _stream())
+    return x
+
+
 def slot_mapping_out(num_tokens, query_start, positions, block_table, block_size, out):
     _cuda(out, "out", torch.int64)
     call("spark_slot_mapping", num_tokens, out.numel(), _p(query_start), _p(positions), _p(block_table), block_size,

@@ -9,7 +9,8 @@ weights.py:28-31) and multiplied by the chunk's activations with bf16 tensor-cor
 cache (the chunk's own K / V are written into it first), and the element-wise steps
 follow the decode engine's semantics (bf16 residual, fp32 RMSNorm, bf16-rounded inputs
 to the fp32 RoPE, SiLU / GELU of the bf16 gate, the Spark output gate and sliding
-window).  Results agree with token-by-token decode within bf16 rounding, not bit for
+window); add + RMSNorm and RoPE run as row-batched kernels (``spark_add_rmsnorm_rows``,
+``spark_rope_neox_rows``).  Results agree with token-by-token decode within bf16 rounding, not bit for
 bit (the GEMM summation order is cuBLAS's).  The bf16 weights are made once per engine
 (2 bytes per weight of HBM, kept for later prompts).  After ``prefill`` the engine holds
 the prompt's K / V, ``pos`` = prompt length and ``token`` = the first generated token.
@@ -22,23 +23,6 @@ import torch.nn.functional as F
 from . import ops
 
 BF16 = torch.bfloat16
-
-
-def _rmsnorm(s: torch.Tensor, gamma: torch.Tensor, eps: float) -> torch.Tensor:
-    """s fp32 [n, h] -> bf16(s / rms(s) * gamma)."""
-    inv = torch.rsqrt(s.pow(2).mean(-1, keepdim=True) + eps)
-    return (s * inv * gamma.float()).to(BF16)
-
-
-def _rope(x: torch.Tensor, cs: torch.Tensor, rot: int) -> torch.Tensor:
-    """x bf16 [n, heads, D]; cs bf16 [n, rot] (cos | sin); neox pairs (i, i + rot/2)."""
-    h = rot // 2
-    a, b = x[..., :h].float(), x[..., h:rot].float()
-    c, s = cs[:, None, :h].float(), cs[:, None, h:rot].float()
-    out = x.clone()
-    out[..., :h] = (a * c - b * s).to(BF16)
-    out[..., h:rot] = (b * c + a * s).to(BF16)
-    return out
 
 
 def _sdpa(q, K, V, scale, causal, mask=None):
@@ -95,16 +79,14 @@ def prefill(eng, prompt: torch.Tensor, chunk: int = 2048) -> torch.Tensor:
         a = w.embed[prompt[p0:p1]]  # bf16 [n, h]
         b = None
         for li, (lw, (w_qkv, w_o, w_gu, w_down)) in enumerate(zip(w.layers, wb)):
-            s = a.float() + b.float() if b is not None else a.float()
-            res = s.to(BF16)
-            x = _rmsnorm(s, lw.in_norm, eps)  # (the fp32 sum, as the decode prologue)
+            res, x = ops.add_rmsnorm_rows(a, b, lw.in_norm, eps)  # (norm of the fp32 sum a + b)
             y = x @ w_qkv.t()
+            _, rot = cfg.layer_rope(li)
+            cs = w.layer_cos_sin(li) if hasattr(w, "layer_cos_sin") else w.cos_sin
+            ops.rope_rows_(y, nq + nkv, D, rot, cs, p0)  # q and k heads, in place
             q = y[:, :nq * D].reshape(n, nq, D)
             k = y[:, nq * D:(nq + nkv) * D].reshape(n, nkv, D)
             v = y[:, (nq + nkv) * D:nh * D].reshape(n, nkv, D)
-            _, rot = cfg.layer_rope(li)
-            cs = (w.layer_cos_sin(li) if hasattr(w, "layer_cos_sin") else w.cos_sin)[pos]
-            q, k = _rope(q, cs, rot), _rope(k, cs, rot)
             # cache rows ((block * nkv + head) * bs + offset) of the chunk's positions
             rows = ((table[pos // bs].long()[:, None] * nkv + heads[None, :]) * bs + (pos % bs)[:, None]).reshape(-1)
             eng.k_cache[li].view(-1, D).index_copy_(0, rows, k.reshape(-1, D))
@@ -129,9 +111,7 @@ def prefill(eng, prompt: torch.Tensor, chunk: int = 2048) -> torch.Tensor:
                 g = torch.sigmoid(y[:, nh * D:nh * D + nq].float()).to(BF16)
                 o = (o.float() * g.float()[:, :, None]).to(BF16)
             oproj = o.reshape(n, nq * D) @ w_o.t()
-            s2 = oproj.float() + res.float()
-            resmid = s2.to(BF16)
-            x2 = _rmsnorm(s2, lw.post_norm, eps)
+            resmid, x2 = ops.add_rmsnorm_rows(oproj, res, lw.post_norm, eps)
             gu = x2 @ w_gu.t()
             gate, up = gu[:, :i], gu[:, i:]
             act = F.gelu(gate, approximate="none") if cfg.hidden_act == "gelu" else F.silu(gate.float()).to(BF16)
@@ -140,7 +120,7 @@ def prefill(eng, prompt: torch.Tensor, chunk: int = 2048) -> torch.Tensor:
             b = resmid
         a_last, b_last = a[-1:], b[-1:]
     # LM head of the last position, greedy
-    x = _rmsnorm(a_last.float() + b_last.float(), w.final_norm, eps)
+    _, x = ops.add_rmsnorm_rows(a_last, b_last, w.final_norm, eps)
     logits = torch.empty(cfg.vocab_size, dtype=BF16, device=dev)
     rows = 16384
     for r0 in range(0, cfg.vocab_size, rows):

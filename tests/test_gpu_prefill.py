@@ -47,3 +47,35 @@ def test_batched_prefill_matches_decode(cuda, which):
         eng.step()
     torch.cuda.synchronize()
     assert int(eng.error.item()) == 0 and int(eng.pos.item()) == P + 4
+
+
+def test_prefill_row_kernels(cuda, oracle):
+    """spark_add_rmsnorm_rows against float64 (bf16 rounding), spark_rope_neox_rows bit for
+    bit against the oracle's RoPE (the same products and rounding), partial rotary on a
+    strided row view of a qkv output."""
+    import numpy as np
+    import torch
+    from spark_b200 import ops
+    g = torch.Generator(device="cuda").manual_seed(5)
+    n, h = 37, 2560
+    a = torch.randn((n, h), generator=g, device="cuda").to(torch.bfloat16)
+    b = torch.randn((n, h), generator=g, device="cuda").to(torch.bfloat16)
+    gamma = (1 + 0.1 * torch.randn(h, generator=g, device="cuda")).to(torch.bfloat16)
+    res, y = ops.add_rmsnorm_rows(a, b, gamma, 1e-6)
+    s = a.double() + b.double()
+    want = s * torch.rsqrt((s * s).mean(-1, keepdim=True) + 1e-6) * gamma.double()
+    assert torch.equal(res, (a.float() + b.float()).to(torch.bfloat16))
+    assert (y.double() - want).abs().max().item() <= 0.01 * want.abs().max().item()
+    nh, D, rot, cols = 6, 256, 64, 6 * 256 + 16
+    x = torch.randn((n, cols), generator=g, device="cuda").to(torch.bfloat16)
+    cs = (torch.rand((n + 100, rot), generator=g, device="cuda") * 2 - 1).to(torch.bfloat16)
+    x0 = x.clone()
+    ops.rope_rows_(x, nh, D, rot, cs, 50)
+    torch.cuda.synchronize()
+    xs = x0.view(torch.int16).cpu().numpy().view(np.uint16)
+    css = cs.view(torch.int16).cpu().numpy().view(np.uint16)
+    got = x.view(torch.int16).cpu().numpy().view(np.uint16)
+    for r in range(n):
+        want_r = oracle.rope_partial(xs[r, :nh * D].reshape(nh, D), rot, css[50 + r])
+        assert np.array_equal(got[r, :nh * D].reshape(nh, D), want_r), r
+        assert np.array_equal(got[r, nh * D:], xs[r, nh * D:])  # the columns past the heads untouched
