@@ -187,6 +187,11 @@ int spark_add_rmsnorm_rows(const uint16_t* a, const uint16_t* b, const uint16_t*
                            int hidden, uint16_t* res_out, uint16_t* y, void* stream);
 int spark_rope_neox_rows(uint16_t* x, int64_t row_stride, int rows, int nh, int head_dim, int rotary_dim,
                          const uint16_t* cos_sin, int64_t pos0, void* stream);
+/* Activation * mul per row of a fused gate / up output gu bf16 [rows][2 inter]:
+ * out bf16 [rows][inter] = bf16(act(gate) * up) with the decode epilogues' arithmetic:
+ * bf16 SiLU (gelu_table NULL) or the GELU table of SPARK_EPI_GELU_MUL. */
+int spark_act_mul_rows(const uint16_t* gu, int rows, int inter, const uint16_t* gelu_table, uint16_t* out,
+                       void* stream);
 
 /* Store this step's keys and values into the paged caches: k / v bf16
  * [tokens][nkv][head_dim] -> k_cache / v_cache bf16 [blocks][nkv][block_size][head_dim]

@@ -189,6 +189,36 @@ __global__ void rope_rows_kernel(uint16_t* x, int64_t row_stride, int n, int nh,
   }
 }
 
+// Activation * mul of n rows of a fused gate / up output gu [n][2 I] (gate columns
+// [0, I), up [I, 2 I)): out [n][I] = bf16(act(bf16 gate) * bf16 up), act = the decode
+// epilogues' bf16(silu) (table == nullptr) or the GELU table lookup (SparkStage.table).
+__global__ void act_mul_rows_kernel(const uint16_t* __restrict__ gu, int64_t n, int inter,
+                                    const uint16_t* __restrict__ table, uint16_t* __restrict__ out) {
+  const int64_t total = n * inter;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = idx / inter;
+    const int i = (int)(idx - r * inter);
+    const uint16_t gb = gu[r * 2 * inter + i];
+    const float uf = bf2f(gu[r * 2 * inter + inter + i]);
+    float act;
+    if (table) {
+      const uint32_t ab = gb & 0x7fffu;
+      uint16_t o;
+      if (ab > 0x7f80u || gb == 0xff80u) o = 0x7fff;
+      else if (gb >= 0xc300u) o = 0x8000;
+      else if (ab >= 0x4300u) o = gb;
+      else if (ab < 0x3b00u) o = f2bf(__fmul_rn(0.5f, bf2f(gb)));
+      else o = table[(ab - 0x3b00u) | ((uint32_t)(gb >> 4) & 0x800u)];
+      act = bf2f(o);
+    } else {
+      const float gf = bf2f(gb);
+      act = bf2f(f2bf(__fdiv_rn(gf, __fadd_rn(1.0f, spark_exp(-gf)))));
+    }
+    out[idx] = f2bf(__fmul_rn(act, uf));
+  }
+}
+
 // ------------------------------------------------------------------ slot mapping (integration/slot_mapping.py:8-22)
 __global__ void slot_mapping_kernel(int64_t n, int64_t max_tokens, const int32_t* __restrict__ query_start,
                                     const int64_t* __restrict__ positions, const int32_t* __restrict__ table,

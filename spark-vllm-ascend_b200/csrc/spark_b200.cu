@@ -598,6 +598,16 @@ int spark_rope_neox_rows(uint16_t* x, int64_t row_stride, int rows, int nh, int 
                 head_dim, rotary_dim, cos_sin, pos0);
 }
 
+int spark_act_mul_rows(const uint16_t* gu, int rows, int inter, const uint16_t* gelu_table, uint16_t* out,
+                       void* stream) {
+  if (!gu || !out) return SPARK_ERR_INVALID_ARG;
+  if (rows <= 0 || inter <= 0) return SPARK_ERR_UNSUPPORTED_SHAPE;
+  const int64_t total = (int64_t)rows * inter;
+  const int64_t grid = std::min<int64_t>((total + 255) / 256, 16LL * num_sms());
+  return launch(act_mul_rows_kernel, dim3((unsigned)grid), dim3(256), 0, as_stream(stream), gu, (int64_t)rows,
+                inter, gelu_table, out);
+}
+
 int spark_rope_neox(uint16_t* x, int nh, int head_dim, const uint16_t* cos_sin, const int64_t* pos, void* stream) {
   if (!x || !cos_sin || !pos) return SPARK_ERR_INVALID_ARG;
   if (nh <= 0 || head_dim <= 0 || (head_dim & 1)) return SPARK_ERR_UNSUPPORTED_SHAPE;

@@ -38,6 +38,7 @@ SIGNATURES: dict[str, list] = {
     "spark_rope_neox": [_P, _I, _I, _P, _P, _P],
     "spark_add_rmsnorm_rows": [_P, _P, _P, _F, _I, _I, _P, _P, _P],
     "spark_rope_neox_rows": [_P, _I64, _I, _I, _I, _I, _P, _I64, _P],
+    "spark_act_mul_rows": [_P, _I, _I, _P, _P, _P],
     "spark_slot_mapping": [_I64, _I64, _P, _P, _P, _I64, _P, _P],
     "spark_set_pdl": [_I],
     "spark_set_gemv_ring": [_I],

@@ -243,6 +243,17 @@ def rope_rows_(x: torch.Tensor, nh: int, head_dim: int, rotary_dim: int, cos_sin
     return x
 
 
+def act_mul_rows(gu: torch.Tensor, gelu_table: torch.Tensor | None = None) -> torch.Tensor:
+    """gu bf16 [n, 2 I] (gate | up) -> bf16 [n, I] = act(gate) * up (SiLU, or GELU by the
+    table of ``step.gelu_table``), the decode epilogues' arithmetic."""
+    _cuda(gu, "gu", BF16)
+    n, i2 = gu.shape
+    gu = gu.contiguous()
+    out = torch.empty((n, i2 // 2), dtype=BF16, device=gu.device)
+    call("spark_act_mul_rows", _p(gu), n, i2 // 2, _p(gelu_table), _p(out), _stream())
+    return out
+
+
 def slot_mapping_out(num_tokens, query_start, positions, block_table, block_size, out):
     _cuda(out, "out", torch.int64)
     call("spark_slot_mapping", num_tokens, out.numel(), _p(query_start), _p(positions), _p(block_table), block_size,

@@ -9,8 +9,9 @@ weights.py:28-31) and multiplied by the chunk's activations with bf16 tensor-cor
 cache (the chunk's own K / V are written into it first), and the element-wise steps
 follow the decode engine's semantics (bf16 residual, fp32 RMSNorm, bf16-rounded inputs
 to the fp32 RoPE, SiLU / GELU of the bf16 gate, the Spark output gate and sliding
-window); add + RMSNorm and RoPE run as row-batched kernels (``spark_add_rmsnorm_rows``,
-``spark_rope_neox_rows``).  Results agree with token-by-token decode within bf16 rounding, not bit for
+window); add + RMSNorm, RoPE and the activation * mul run as row-batched kernels
+(``spark_add_rmsnorm_rows``, ``spark_rope_neox_rows``, ``spark_act_mul_rows``, the last
+with the decode epilogues' SiLU / GELU-table arithmetic).  Results agree with token-by-token decode within bf16 rounding, not bit for
 bit (the GEMM summation order is cuBLAS's).  The bf16 weights are made once per engine
 (2 bytes per weight of HBM, kept for later prompts).  After ``prefill`` the engine holds
 the prompt's K / V, ``pos`` = prompt length and ``token`` = the first generated token.
@@ -113,9 +114,7 @@ def prefill(eng, prompt: torch.Tensor, chunk: int = 2048) -> torch.Tensor:
             oproj = o.reshape(n, nq * D) @ w_o.t()
             resmid, x2 = ops.add_rmsnorm_rows(oproj, res, lw.post_norm, eps)
             gu = x2 @ w_gu.t()
-            gate, up = gu[:, :i], gu[:, i:]
-            act = F.gelu(gate, approximate="none") if cfg.hidden_act == "gelu" else F.silu(gate.float()).to(BF16)
-            mid = (act.float() * up.float()).to(BF16)
+            mid = ops.act_mul_rows(gu, getattr(eng, "gelu", None) if cfg.hidden_act == "gelu" else None)
             a = mid @ w_down.t()
             b = resmid
         a_last, b_last = a[-1:], b[-1:]

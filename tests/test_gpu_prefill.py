@@ -79,3 +79,22 @@ def test_prefill_row_kernels(cuda, oracle):
         want_r = oracle.rope_partial(xs[r, :nh * D].reshape(nh, D), rot, css[50 + r])
         assert np.array_equal(got[r, :nh * D].reshape(nh, D), want_r), r
         assert np.array_equal(got[r, nh * D:], xs[r, nh * D:])  # the columns past the heads untouched
+
+
+def test_act_mul_rows_matches_decode_arithmetic(cuda, oracle):
+    """spark_act_mul_rows: bit for bit the oracle's SiLU * mul and GELU-table * mul (the
+    decode epilogues' arithmetic), over gate values spanning every range of the table."""
+    import numpy as np
+    import torch
+    from spark_b200 import ops, step
+    g = torch.Generator(device="cuda").manual_seed(6)
+    n, i = 19, 1024
+    gu = (torch.randn((n, 2 * i), generator=g, device="cuda") *
+          torch.exp2(torch.randint(-14, 9, (n, 2 * i), generator=g, device="cuda").float())).to(torch.bfloat16)
+    u = gu.view(torch.int16).cpu().numpy().view(np.uint16)
+    silu = ops.act_mul_rows(gu).view(torch.int16).cpu().numpy().view(np.uint16)
+    gelu = ops.act_mul_rows(gu, step.gelu_table("cuda")).view(torch.int16).cpu().numpy().view(np.uint16)
+    table = oracle.gelu_table()
+    for r in range(n):
+        assert np.array_equal(silu[r], oracle.silu_mul(u[r, :i], u[r, i:])), r
+        assert np.array_equal(gelu[r], oracle.gelu_mul(u[r, :i], u[r, i:], table)), r
