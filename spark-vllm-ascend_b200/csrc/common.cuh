@@ -75,6 +75,19 @@ __device__ __forceinline__ float spark_exp(float x) {
                    __uint_as_float((uint32_t)(n2 + 127) << 23));
 }
 
+// GELU of a bf16 value as the reference's activation table (kernels/linear.py:540-577,
+// table built in integration/model.py:12-16): table [4096] = gelu of the bf16 inputs
+// 0x3b00 + i and 0xbb00 + i (|x| in [2^-9, 128)); |x| < 2^-9: bf16(x / 2); x >= 128: x;
+// x <= -128: -0; NaN and -inf: 0x7fff.
+__device__ __forceinline__ uint16_t spark_gelu_bf16(uint16_t x, const uint16_t* table) {
+  const uint32_t ab = x & 0x7fffu;
+  if (ab > 0x7f80u || x == 0xff80u) return 0x7fff;
+  if (x >= 0xc300u) return 0x8000;
+  if (ab >= 0x4300u) return x;
+  if (ab < 0x3b00u) return f2bf(__fmul_rn(0.5f, bf2f(x)));
+  return __ldg(table + ((ab - 0x3b00u) | ((uint32_t)(x >> 4) & 0x800u)));
+}
+
 __device__ __forceinline__ float spark_log(float x) {
   if (x != x || x < 0.0f) return __int_as_float(0x7fc00000);
   if (x == 0.0f) return __int_as_float(0xff800000);

@@ -203,14 +203,7 @@ __global__ void act_mul_rows_kernel(const uint16_t* __restrict__ gu, int64_t n, 
     const float uf = bf2f(gu[r * 2 * inter + inter + i]);
     float act;
     if (table) {
-      const uint32_t ab = gb & 0x7fffu;
-      uint16_t o;
-      if (ab > 0x7f80u || gb == 0xff80u) o = 0x7fff;
-      else if (gb >= 0xc300u) o = 0x8000;
-      else if (ab >= 0x4300u) o = gb;
-      else if (ab < 0x3b00u) o = f2bf(__fmul_rn(0.5f, bf2f(gb)));
-      else o = table[(ab - 0x3b00u) | ((uint32_t)(gb >> 4) & 0x800u)];
-      act = bf2f(o);
+      act = bf2f(spark_gelu_bf16(gb, table));
     } else {
       const float gf = bf2f(gb);
       act = bf2f(f2bf(__fdiv_rn(gf, __fadd_rn(1.0f, spark_exp(-gf)))));

@@ -730,16 +730,6 @@ __device__ __forceinline__ void gemv_task_q6(const GemvDims& gd, uint32_t ubase,
 
 __device__ __forceinline__ uint16_t bf16r(float v) { return f2bf(v); }
 
-// GELU of a bf16 value by the table (SparkStage.table) and its closed-form ranges
-__device__ __forceinline__ uint16_t gelu_bf16(uint16_t x, const uint16_t* table) {
-  const uint32_t ab = x & 0x7fffu;
-  if (ab > 0x7f80u || x == 0xff80u) return 0x7fff;  // NaN, gelu(-inf)
-  if (x >= 0xc300u) return 0x8000;                   // x <= -128: -0
-  if (ab >= 0x4300u) return x;                       // x >= 128: x
-  if (ab < 0x3b00u) return f2bf(__fmul_rn(0.5f, bf2f(x)));
-  return __ldg(table + ((ab - 0x3b00u) | ((uint32_t)(x >> 4) & 0x800u)));
-}
-
 // epilogue of one row pair (positions g and g + 8 of unit u); Spark: the qkv stage's
 // partial RoPE and gate rows, the GELU * mul epilogue
 template <bool Spark>
@@ -786,7 +776,7 @@ __device__ __forceinline__ void gemv_epilogue(const SparkStage& st, const SparkS
     }
     case SPARK_EPI_GELU_MUL: {
       if constexpr (Spark) {
-        const float act = bf2f(gelu_bf16(f2bf(v0), static_cast<const uint16_t*>(st.table)));
+        const float act = bf2f(spark_gelu_bf16(f2bf(v0), static_cast<const uint16_t*>(st.table)));
         static_cast<uint16_t*>(st.out)[r0] = f2bf(__fmul_rn(act, bf2f(f2bf(v1))));
       }
       break;
