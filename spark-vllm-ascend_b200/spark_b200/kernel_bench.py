@@ -205,7 +205,7 @@ def bench_step_attn(ctx, reps, copies, device, gen, cfg):
     (splits = CTAs / kv heads, distributed combine)."""
     from . import step as S
     nq, nkv, D, bs = cfg.num_q_heads, cfg.num_kv_heads, cfg.head_dim, cfg.block_size
-    splits = S.attn_splits(cfg, S.num_ctas())
+    splits = S.attn_splits(cfg, S.num_ctas(), ctx)
     nblk = (ctx + bs - 1) // bs
     per = 2 * nblk * nkv * bs * D * 2
     copies = max(1, min(copies, math.ceil(400e6 / per)))
