@@ -430,7 +430,9 @@ def run_reference(args):
         return oracle.f32_to_bf16((base + scale * rng.standard_normal(n)).astype(np.float32))
 
     t_setup = time.perf_counter()
-    w = {"embed": bfv(V * h, 0.02).reshape(V, h), "final_norm": bfv(h, 0.02, 1.0)}
+    # the embedding keeps its real shape, but a sample reads one row: only that row is drawn
+    w = {"embed": np.zeros((V, h), np.uint16), "final_norm": bfv(h, 0.02, 1.0)}
+    w["embed"][1] = bfv(h, 0.02)
     w["head_qs"], w["head_d"] = q4(V, h)
     w["cos_sin"] = np.zeros((cfg.max_position, cfg.head_dim), np.uint16)
     for li in range(cfg.num_layers):
@@ -440,7 +442,10 @@ def run_reference(args):
                             ("gu", (2 * i, h)), ("down", (h, i))):
             w[p_ + key + "_qs"], w[p_ + key + "_d"] = q4(n, k)
     nblk = (PROMPT_LEN + 1 + 127) // 128
-    om = oracle.OracleModel(cfg, w, num_blocks=nblk, splits=args.splits)
+    from spark_b200 import step as S  # (host-side split rule only; no GPU code runs)
+    # --splits 0: the persistent step's own choice on a B200 (148 CTAs, one per SM)
+    splits = args.splits or S.splits_for(cfg.num_kv_heads, 148, PROMPT_LEN + 1, cfg.head_dim)
+    om = oracle.OracleModel(cfg, w, num_blocks=nblk, splits=splits)
     om.kc[...] = rng.integers(0, 65536, size=om.kc.shape, dtype=np.uint16) & 0xBFFF  # finite bf16
     om.vc[...] = rng.integers(0, 65536, size=om.vc.shape, dtype=np.uint16) & 0xBFFF
     table = np.arange(nblk, dtype=np.int32)
@@ -470,7 +475,7 @@ def run_reference(args):
         "dtype": "q4_0 weights x fp32 accumulate, bf16 activations / KV",
         "data": "synthetic: random Q4_0 codes / scales and bf16 KV prefix of the real shapes",
         "config": {"workload": "configs[2]: synthetic 4B Q4_0 batch-1 decode, 2048 prompt, greedy",
-                   "layers": cfg.num_layers, "ctx": PROMPT_LEN, "splits": eng.splits, "setup_s": round(setup_s, 1)},
+                   "layers": cfg.num_layers, "ctx": PROMPT_LEN, "splits": splits, "setup_s": round(setup_s, 1)},
         "cpu_baseline": {"value": round(tps, 4), "unit": "tokens/s", "cores": threads, "kind": "port",
                          "sample": f"{args.steps} samples of one layer (or the LM head) of a ctx-{PROMPT_LEN} "
                                    f"decode step; {units} samples = 1 token"},

@@ -348,6 +348,8 @@ class OracleModel:
     def __init__(self, cfg, weights: dict, num_blocks: int, splits: int, order: dict | None = None):
         """``order`` None: per-kernel evaluation order.  Persistent-step order:
         {"ks": (qkv, o, gate_up, down, head), "kp": (o, down), "chunk_accs": W}."""
+        if splits <= 0:
+            raise ValueError(f"splits must be positive, got {splits}")
         self.cfg = cfg
         self.w = weights
         self.splits = splits
