@@ -33,3 +33,24 @@ def test_gguf_round_trip_and_decode(cuda, oracle, tmp_path):
                      eng.logits.clone()))
     assert toks[0][0] == toks[1][0]
     assert torch.equal(toks[0][1], toks[1][1])
+
+
+def test_gguf_separate_qkv_untied_head(cuda, oracle, tmp_path):
+    """The llama-style layout the loader also reads: separate attn_q / attn_k / attn_v,
+    a float token_embd and a Q4_0 output head (the synthetic 4B architecture, small)."""
+    import torch
+    from gguf_fixture import write_spark_gguf
+    from spark_b200.config import tiny_config
+    from spark_b200.gguf_loader import load_gguf
+    from spark_b200.model import DecodeEngine, SyntheticWeights
+    cfg = tiny_config(num_layers=2)
+    src = SyntheticWeights(cfg, device="cuda", seed=10)
+    ref = src.to_numpy()
+    path = write_spark_gguf(tmp_path / "llama.gguf", cfg, ref, oracle, fused_qkv=False)
+    got = load_gguf(path, cfg).to_numpy()
+    assert sorted(got) == sorted(ref)
+    for k in ref:
+        assert np.array_equal(got[k], ref[k]), k
+    toks = [DecodeEngine(w, max_seq_len=128, num_blocks=4, seed=10).generate(
+        torch.arange(9, dtype=torch.int32) * 53 % cfg.vocab_size, 6) for w in (src, load_gguf(path, cfg))]
+    assert toks[0] == toks[1]
