@@ -674,11 +674,32 @@ __device__ __forceinline__ void q6_tiles(uint32_t grp, uint32_t sc_pl, uint32_t 
   uint2 nib[NT], B[NT], mt[NT], m2[NT];
   uint32_t H[NT];
   uint16_t scv[NT];
+  if constexpr (NT % 2 == 0) {
+    // t even: tiles (t + 2p, t + 2p + 1) share one 768-B group, whose 16 nibble bytes and
+    // 8 high-bit bytes of this lane are one load each
+#pragma unroll
+    for (int p = 0; p < NT / 2; p++) {
+      const uint32_t pb = grp + (uint32_t)((t >> 1) + p) * 768u;
+      uint4 nn;
+      uint2 hh;
+      lds_u32x4(pb + lane * 16, nn);
+      lds_u32x2(pb + 512 + lane * 8, hh);
+      nib[2 * p] = make_uint2(nn.x, nn.y);
+      nib[2 * p + 1] = make_uint2(nn.z, nn.w);
+      H[2 * p] = hh.x;
+      H[2 * p + 1] = hh.y;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < NT; j++) {
+      const int tt = t + j;
+      lds_u32x2(grp + (uint32_t)(tt >> 1) * 768u + lane * 16 + (tt & 1) * 8, nib[j]);
+      asm("ld.shared.u32 %0, [%1];" : "=r"(H[j]) : "r"(grp + (uint32_t)(tt >> 1) * 768u + 512 + lane * 8 + (tt & 1) * 4));
+    }
+  }
 #pragma unroll
   for (int j = 0; j < NT; j++) {
     const int tt = t + j, gb = kpi * gd.kp_blocks + tt;
-    lds_u32x2(grp + (uint32_t)(tt >> 1) * 768u + lane * 16 + (tt & 1) * 8, nib[j]);
-    asm("ld.shared.u32 %0, [%1];" : "=r"(H[j]) : "r"(grp + (uint32_t)(tt >> 1) * 768u + 512 + lane * 8 + (tt & 1) * 4));
     lds_u32x2(gd.xf + (uint32_t)(gb * 8 + (lane & 7)) * 8, B[j]);
     lds_u32x2(gd.xm + (uint32_t)gb * 8, mt[j]);
     lds_u32x2(gd.xm2 + (uint32_t)gb * 8, m2[j]);
