@@ -57,6 +57,15 @@ int spark_q4_split_gguf(const uint8_t* blocks, int64_t rows, int64_t k, uint8_t*
 int spark_q4_dequantize_bf16(const uint8_t* qs, const uint16_t* d, int64_t rows, int64_t k, uint16_t* w,
                              void* stream);
 
+/* Prefill GEMM on the tensor cores: y[t][n] = bf16(sum_k W[n][k] * x[t][k]) for t < T
+ * tokens, W the Q4_0 planes [n][k] dequantized to bf16 in shared memory (the same
+ * rounding as spark_q4_dequantize_bf16), fp32 accumulation (tcgen05.mma).  Replaces the
+ * prefill's dequantize -> bf16 matmul (integration/weights.py:28-31 and vLLM's torch
+ * linear layers, integration/model.py:50-62) without the bf16 weight copy.  k % 64 == 0;
+ * x [T][k] bf16 16-B aligned; *error is set nonzero if a wait inside the kernel timed out. */
+int spark_q4_gemm_tc(const uint16_t* x, const uint8_t* qs, const uint16_t* d, uint16_t* y, int t, int n, int k,
+                     int* error, void* stream);
+
 /* y[b][n] = bf16(sum_k W[n][k] * x[b][k]) for b < batch (1..8); fp32 accumulation
  * in the fixed order documented in q4_gemv.cuh.  n even, k % 32 == 0.
  * Replaces GemvStage.calculate (kernels/linear.py:17-200) as used by

@@ -16,6 +16,7 @@
 #include "attention.cuh"
 #include "misc.cuh"
 #include "q4_gemv.cuh"
+#include "q4_gemm_tc.cuh"
 #include "q4_gemv_ring.cuh"
 #include "spark_b200.h"
 #include "step_kernel.cuh"
@@ -289,6 +290,18 @@ int spark_q4_dequantize_bf16(const uint8_t* qs, const uint16_t* d, int64_t rows,
   int64_t grid = (nblocks + 255) / 256;
   if (grid > 65535 * 16) grid = 65535 * 16;
   q4_dequant_bf16_kernel<<<(unsigned)grid, 256, 0, as_stream(stream)>>>(qs, d, nblocks, w);
+  return cudaGetLastError() == cudaSuccess ? SPARK_OK : SPARK_ERR_LAUNCH;
+}
+
+int spark_q4_gemm_tc(const uint16_t* x, const uint8_t* qs, const uint16_t* d, uint16_t* y, int t, int n, int k,
+                     int* error, void* stream) {
+  if (!x || !qs || !d || !y || !error) return SPARK_ERR_INVALID_ARG;
+  if (t <= 0 || n <= 0 || k <= 0 || k % tc::kBK || t > 65535 * tc::kBN) return SPARK_ERR_UNSUPPORTED_SHAPE;
+  if (!aligned(x, 16) || !aligned(qs, 16) || !aligned(d, 2) || !aligned(y, 2) || !aligned(error, 4))
+    return SPARK_ERR_ALIGNMENT;
+  if (set_smem(reinterpret_cast<const void*>(&tc::q4_gemm_tc_kernel), tc::kSmemBytes)) return SPARK_ERR_LAUNCH;
+  const dim3 grid((unsigned)((n + tc::kBM - 1) / tc::kBM), (unsigned)((t + tc::kBN - 1) / tc::kBN));
+  tc::q4_gemm_tc_kernel<<<grid, 128, tc::kSmemBytes, as_stream(stream)>>>(x, qs, d, y, t, n, k, error);
   return cudaGetLastError() == cudaSuccess ? SPARK_OK : SPARK_ERR_LAUNCH;
 }
 

@@ -82,6 +82,21 @@ def q4_dequantize(qs: torch.Tensor, d: torch.Tensor) -> torch.Tensor:
     return w
 
 
+def q4_gemm(x: torch.Tensor, qs: torch.Tensor, d: torch.Tensor, error: torch.Tensor | None = None) -> torch.Tensor:
+    """Prefill GEMM on the tensor cores: x bf16 [T, K] times the Q4_0 weight [N, K]
+    (dequantized in shared memory) -> bf16 [T, N].  K % 64 == 0.  ``error`` (int32 [1],
+    optional) receives a nonzero value if a wait inside the kernel timed out."""
+    n, k = _q4(qs, d)
+    _cuda(x, "x", BF16)
+    x2 = x.reshape(-1, k)
+    _check(x2.is_contiguous(), "x must be contiguous")
+    t = x2.shape[0]
+    y = torch.empty((t, n), dtype=BF16, device=x.device)
+    err = error if error is not None else torch.zeros(1, dtype=torch.int32, device=x.device)
+    call("spark_q4_gemm_tc", _p(x2), _p(qs), _p(d), _p(y), t, n, k, _p(err), _stream())
+    return y
+
+
 # ---------------------------------------------------------------- GEMV family
 def q4_gemv_out(x: torch.Tensor, qs: torch.Tensor, d: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
     n, k = _q4(qs, d)

@@ -1,0 +1,60 @@
+"""GPU parity of the tensor-core Q4_0 prefill GEMM (``spark_q4_gemm_tc``, tcgen05.mma with
+the weight tile dequantized in shared memory) against the same product in fp32 over the
+bf16 dequantization (``spark_q4_dequantize_bf16``, the reference's
+``dequantize(...).bfloat16()`` weights, integration/weights.py:28-31) and against the
+cuBLAS bf16 matmul the prefill used before.  Both accumulate in fp32 over identical bf16
+operands, so they differ only by summation order: tolerance rel 1e-2 + abs 1e-3 of the
+row scale, and at least 99 % of outputs bit-identical to cuBLAS's.
+"""
+from __future__ import annotations
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [  # (tokens, rows, K)
+    (1, 128, 64),
+    (77, 200, 2560),
+    (128, 256, 4096),
+    (300, 6144, 2560),
+    (129, 2560, 9728),
+]
+
+
+def _planes(n, k, seed):
+    import torch
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    qs = torch.randint(0, 256, (n, k // 2), generator=g, device="cuda", dtype=torch.int32).to(torch.uint8)
+    d = (torch.rand((n, k // 32), generator=g, device="cuda") * 0.01 + 1e-4).to(torch.float16)
+    return qs, d
+
+
+@pytest.mark.parametrize("t,n,k", SHAPES)
+def test_q4_gemm_tc_matches_fp32_and_cublas(cuda, t, n, k):
+    import torch
+    from spark_b200 import ops
+    qs, d = _planes(n, k, seed=t * 7 + n)
+    g = torch.Generator(device="cuda").manual_seed(n + k)
+    x = torch.randn((t, k), generator=g, device="cuda").to(torch.bfloat16)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    y = ops.q4_gemm(x, qs, d, err)
+    w = ops.q4_dequantize(qs, d)
+    ref = x.float() @ w.float().t()
+    blas = x @ w.t()
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert y.shape == (t, n) and y.dtype == torch.bfloat16
+    scale = ref.abs().amax(dim=1, keepdim=True).clamp_min(1e-6)
+    diff = (y.float() - ref).abs()
+    assert bool((diff <= 1e-2 * ref.abs() + 1e-3 * scale).all()), float((diff / scale).max())
+    same = (y.view(torch.int16) == blas.view(torch.int16)).float().mean().item()
+    assert same >= 0.99, same
+
+
+def test_q4_gemm_tc_rejects_bad_shapes(cuda):
+    import torch
+    from spark_b200 import ops
+    qs, d = _planes(128, 96, seed=1)  # K = 96: not a multiple of 64
+    x = torch.zeros((4, 96), dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(Exception):
+        ops.q4_gemm(x, qs, d)
