@@ -70,17 +70,35 @@ __device__ __forceinline__ bool bar_wait(uint32_t bar, uint32_t parity) {
 }
 
 // 8 weights of one Q4_0 block as 4 bf16 pairs: the nibbles at `shift` of the 8 bytes
-// held by (w0, w1)
+// held by (w0, w1).  q - 8 as fp32 from the bits of 2^23 + q minus 2^23 + 8 (exact);
+// fp32(d) * (q - 8) is exact in fp32 (11 + 4 significant bits), and cvt.rn.bf16x2 rounds
+// the pair to nearest-even (NaN -> 0x7fff), the same bits as f2bf.
 __device__ __forceinline__ uint4 deq8(uint32_t w0, uint32_t w1, int shift, float s) {
   uint32_t o[4];
 #pragma unroll
   for (int i = 0; i < 4; i++) {
     const uint32_t wd = i < 2 ? w0 : w1;
     const int b = (2 * i) & 3;
-    const int q0 = (int)((wd >> (8 * b + shift)) & 15u), q1 = (int)((wd >> (8 * (b + 1) + shift)) & 15u);
-    o[i] = (uint32_t)f2bf(__fmul_rn(s, (float)(q0 - 8))) | ((uint32_t)f2bf(__fmul_rn(s, (float)(q1 - 8))) << 16);
+    const float m0 = __uint_as_float(0x4B000000u | ((wd >> (8 * b + shift)) & 15u)) - 8388616.0f;
+    const float m1 = __uint_as_float(0x4B000000u | ((wd >> (8 * (b + 1) + shift)) & 15u)) - 8388616.0f;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(o[i]) : "f"(__fmul_rn(s, m1)), "f"(__fmul_rn(s, m0)));
   }
   return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// global loads of one K step for this thread: its weight row's two Q4_0 blocks and its
+// token row's 64 activations (zeros past the last row / token)
+__device__ __forceinline__ void load_step(const uint8_t* qrow, const uint16_t* drow, const uint16_t* xrow, bool nv,
+                                          bool tv, int kb, uint4 (&q)[2], uint16_t (&dd)[2], uint4 (&xv)[8]) {
+#pragma unroll
+  for (int blk = 0; blk < 2; blk++) {
+    const int bi = kb * 2 + blk;
+    dd[blk] = nv ? __ldg(drow + bi) : (uint16_t)0;
+    q[blk] = nv ? __ldg(reinterpret_cast<const uint4*>(qrow + (size_t)bi * 16)) : make_uint4(0, 0, 0, 0);
+  }
+#pragma unroll
+  for (int c = 0; c < 8; c++)
+    xv[c] = tv ? __ldg(reinterpret_cast<const uint4*>(xrow + (size_t)kb * kBK + c * 8)) : make_uint4(0, 0, 0, 0);
 }
 
 __device__ __forceinline__ void sts128(uint32_t addr, uint4 v) {
@@ -120,9 +138,20 @@ __global__ void __launch_bounds__(128) q4_gemm_tc_kernel(const uint16_t* __restr
   const uint8_t* qrow = qs + (size_t)(n < N ? n : 0) * (K / 2);
   const uint16_t* drow = d + (size_t)(n < N ? n : 0) * kblocks;
   const uint16_t* xrow = x + (size_t)(t < T ? t : 0) * K;
+  const bool nv = n < N, tv = t < T;
+  // software pipeline: step kb + 1's global loads are in flight while step kb is
+  // dequantized into shared memory and multiplied
+  uint4 q[2], xv[8];
+  uint16_t dd[2];
+  load_step(qrow, drow, xrow, nv, tv, 0, q, dd, xv);
   bool ok = true;
   for (int kb = 0; kb < nk; kb++) {
     const int s = kb & 1;
+    uint4 qc[2] = {q[0], q[1]}, xc[8];
+    const uint16_t dc[2] = {dd[0], dd[1]};
+#pragma unroll
+    for (int c = 0; c < 8; c++) xc[c] = xv[c];
+    if (kb + 1 < nk) load_step(qrow, drow, xrow, nv, tv, kb + 1, q, dd, xv);
     if (kb >= kStages) {  // the MMAs of step kb - 2 read this stage
       const bool mine = bar_wait(bars + 8 * s, ((kb - kStages) >> 1) & 1);
       if (__syncthreads_or(!mine)) {
@@ -131,27 +160,16 @@ __global__ void __launch_bounds__(128) q4_gemm_tc_kernel(const uint16_t* __restr
       }
     }
     const uint32_t a_tile = base + s * 2 * kTileBytes, b_tile = a_tile + kTileBytes;
-    if (n < N) {
 #pragma unroll
-      for (int blk = 0; blk < 2; blk++) {
-        const int bi = kb * 2 + blk;
-        const float sc = h2f(__ldg(drow + bi));
-        const uint4 q = __ldg(reinterpret_cast<const uint4*>(qrow + (size_t)bi * 16));
-        sts128(a_tile + sw128(tid, 4 * blk + 0), deq8(q.x, q.y, 0, sc));
-        sts128(a_tile + sw128(tid, 4 * blk + 1), deq8(q.z, q.w, 0, sc));
-        sts128(a_tile + sw128(tid, 4 * blk + 2), deq8(q.x, q.y, 4, sc));
-        sts128(a_tile + sw128(tid, 4 * blk + 3), deq8(q.z, q.w, 4, sc));
-      }
-    } else {
-#pragma unroll
-      for (int c = 0; c < 8; c++) sts128(a_tile + sw128(tid, c), make_uint4(0, 0, 0, 0));
+    for (int blk = 0; blk < 2; blk++) {  // rows past N hold zero codes and scales: zero weights
+      const float sc = h2f(dc[blk]);
+      sts128(a_tile + sw128(tid, 4 * blk + 0), deq8(qc[blk].x, qc[blk].y, 0, sc));
+      sts128(a_tile + sw128(tid, 4 * blk + 1), deq8(qc[blk].z, qc[blk].w, 0, sc));
+      sts128(a_tile + sw128(tid, 4 * blk + 2), deq8(qc[blk].x, qc[blk].y, 4, sc));
+      sts128(a_tile + sw128(tid, 4 * blk + 3), deq8(qc[blk].z, qc[blk].w, 4, sc));
     }
 #pragma unroll
-    for (int c = 0; c < 8; c++) {
-      const uint4 v = t < T ? __ldg(reinterpret_cast<const uint4*>(xrow + (size_t)kb * kBK + c * 8))
-                            : make_uint4(0, 0, 0, 0);
-      sts128(b_tile + sw128(tid, c), v);
-    }
+    for (int c = 0; c < 8; c++) sts128(b_tile + sw128(tid, c), xc[c]);
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncthreads();
     if (tid == 0) {

@@ -51,6 +51,25 @@ def test_q4_gemm_tc_matches_fp32_and_cublas(cuda, t, n, k):
     assert same >= 0.99, same
 
 
+@pytest.mark.parametrize("n,k", [(200, 256), (384, 2560)])
+def test_q4_gemm_tc_identity_is_bit_exact_dequant(cuda, n, k):
+    """x = the identity: every output is one product W[n][t] * 1, so y must equal the
+    transposed bf16 dequantization exactly (scales of either sign, q = 0..15).  Compared
+    as values: a -0.0 weight (negative scale, q = 8) sums with the +0.0 products of the
+    other columns to +0.0, so only the sign of zero may differ."""
+    import torch
+    from spark_b200 import ops
+    qs, d = _planes(n, k, seed=n)
+    d = torch.where(torch.arange(d.numel(), device="cuda").reshape(d.shape) % 3 == 0, -d, d)
+    x = torch.eye(k, dtype=torch.bfloat16, device="cuda")
+    y = ops.q4_gemm(x, qs, d)
+    w = ops.q4_dequantize(qs, d)
+    torch.cuda.synchronize()
+    assert torch.equal(y.float(), w.t().float())
+    nz = w.t() != 0
+    assert torch.equal(y.view(torch.int16)[nz], w.t().contiguous().view(torch.int16)[nz])
+
+
 def test_q4_gemm_tc_rejects_bad_shapes(cuda):
     import torch
     from spark_b200 import ops
