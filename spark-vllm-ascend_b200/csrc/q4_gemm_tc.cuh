@@ -9,9 +9,10 @@
 // operands, fp32 accumulators in tensor memory).
 //
 // Tile: M = 128 weight rows (TMEM lanes), N = 128 tokens (TMEM columns), K = 64 per
-// stage (one 128-byte swizzle atom of bf16), 2 stages.  Both operands are K-major with
-// the 128-byte swizzle: row r of a tile at (r / 8) * 1024 + (r % 8) * 128, its 16-byte
-// chunk c at chunk position c ^ (r % 8).  Every wait is bounded by %globaltimer; a wait
+// stage (one 128-byte swizzle atom of bf16), 2 stages; 256 threads, two per tile row
+// (one per 32-wide half of a K step).  Both operands are K-major with the 128-byte
+// swizzle: row r of a tile at (r / 8) * 1024 + (r % 8) * 128, its 16-byte chunk c at
+// chunk position c ^ (r % 8).  Every wait is bounded by %globaltimer; a wait
 // that runs out sets *error and the CTA frees its tensor memory and returns.
 #pragma once
 
@@ -26,6 +27,7 @@ constexpr int kBM = 128;                  // weight rows per tile (MMA M)
 constexpr int kBN = 128;                  // tokens per tile (MMA N)
 constexpr int kBK = 64;                   // K per stage
 constexpr int kStages = 2;
+constexpr int kThreads = 256;            // two threads per tile row: one per half of a K step
 constexpr int kTileBytes = kBM * kBK * 2;  // 16 KB; the token tile is the same size (kBN == kBM)
 constexpr int kSmemBytes = kStages * 2 * kTileBytes + 1024 + 64;  // tiles, 1024-B alignment slack, barriers
 constexpr unsigned long long kWaitNs = 500ull * 1000 * 1000;      // 0.5 s per wait
@@ -86,19 +88,18 @@ __device__ __forceinline__ uint4 deq8(uint32_t w0, uint32_t w1, int shift, float
   return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
-// global loads of one K step for this thread: its weight row's two Q4_0 blocks and its
-// token row's 64 activations (zeros past the last row / token)
+// global loads of half a K step for this thread (half h = 0 / 1: k 32h .. 32h + 31 of
+// the step): its weight row's Q4_0 block and its token row's 32 activations (zeros past
+// the last row / token)
 __device__ __forceinline__ void load_step(const uint8_t* qrow, const uint16_t* drow, const uint16_t* xrow, bool nv,
-                                          bool tv, int kb, uint4 (&q)[2], uint16_t (&dd)[2], uint4 (&xv)[8]) {
+                                          bool tv, int kb, int h, uint4& q, uint16_t& dd, uint4 (&xv)[4]) {
+  const int bi = kb * 2 + h;
+  dd = nv ? __ldg(drow + bi) : (uint16_t)0;
+  q = nv ? __ldg(reinterpret_cast<const uint4*>(qrow + (size_t)bi * 16)) : make_uint4(0, 0, 0, 0);
 #pragma unroll
-  for (int blk = 0; blk < 2; blk++) {
-    const int bi = kb * 2 + blk;
-    dd[blk] = nv ? __ldg(drow + bi) : (uint16_t)0;
-    q[blk] = nv ? __ldg(reinterpret_cast<const uint4*>(qrow + (size_t)bi * 16)) : make_uint4(0, 0, 0, 0);
-  }
-#pragma unroll
-  for (int c = 0; c < 8; c++)
-    xv[c] = tv ? __ldg(reinterpret_cast<const uint4*>(xrow + (size_t)kb * kBK + c * 8)) : make_uint4(0, 0, 0, 0);
+  for (int c = 0; c < 4; c++)
+    xv[c] = tv ? __ldg(reinterpret_cast<const uint4*>(xrow + (size_t)kb * kBK + (4 * h + c) * 8))
+               : make_uint4(0, 0, 0, 0);
 }
 
 __device__ __forceinline__ void sts128(uint32_t addr, uint4 v) {
@@ -106,7 +107,7 @@ __device__ __forceinline__ void sts128(uint32_t addr, uint4 v) {
                : "memory");
 }
 
-__global__ void __launch_bounds__(128) q4_gemm_tc_kernel(const uint16_t* __restrict__ x,
+__global__ void __launch_bounds__(kThreads) q4_gemm_tc_kernel(const uint16_t* __restrict__ x,
                                                          const uint8_t* __restrict__ qs,
                                                          const uint16_t* __restrict__ d, uint16_t* __restrict__ y,
                                                          int T, int N, int K, int* __restrict__ error) {
@@ -134,42 +135,42 @@ __global__ void __launch_bounds__(128) q4_gemm_tc_kernel(const uint16_t* __restr
   uint32_t tmem;
   asm volatile("ld.shared.u32 %0, [%1];" : "=r"(tmem) : "r"(tslot) : "memory");
 
-  const int n = n0 + tid, t = t0 + tid;  // this thread stages weight row n and token row t
+  const int r = tid & (kBM - 1), h = tid >> 7;  // tile row r, half h of each K step
+  const int n = n0 + r, t = t0 + r;              // this thread stages weight row n and token row t
   const uint8_t* qrow = qs + (size_t)(n < N ? n : 0) * (K / 2);
   const uint16_t* drow = d + (size_t)(n < N ? n : 0) * kblocks;
   const uint16_t* xrow = x + (size_t)(t < T ? t : 0) * K;
   const bool nv = n < N, tv = t < T;
-  // software pipeline: step kb + 1's global loads are in flight while step kb is
-  // dequantized into shared memory and multiplied
-  uint4 q[2], xv[8];
-  uint16_t dd[2];
-  load_step(qrow, drow, xrow, nv, tv, 0, q, dd, xv);
-  bool ok = true;
-  for (int kb = 0; kb < nk; kb++) {
+  // software pipeline: two register sets alternate, so step kb + 2's global loads are
+  // in flight while steps kb and kb + 1 are dequantized into shared memory and multiplied
+  uint4 qa, xa[4], qb, xb[4];
+  uint16_t da, db;
+  load_step(qrow, drow, xrow, nv, tv, 0, h, qa, da, xa);
+  if (nk > 1) load_step(qrow, drow, xrow, nv, tv, 1, h, qb, db, xb);
+  // one K step from register set (q, dd, xv), which is then refilled with step kb + 2;
+  // false (in every thread) if the wait for the stage's previous MMAs ran out
+  auto step = [&](int kb, uint4& q, uint16_t& dd, uint4 (&xv)[4]) -> bool {
     const int s = kb & 1;
-    uint4 qc[2] = {q[0], q[1]}, xc[8];
-    const uint16_t dc[2] = {dd[0], dd[1]};
+    const uint4 qc = q;
+    const uint16_t dc = dd;
+    uint4 xc[4];
 #pragma unroll
-    for (int c = 0; c < 8; c++) xc[c] = xv[c];
-    if (kb + 1 < nk) load_step(qrow, drow, xrow, nv, tv, kb + 1, q, dd, xv);
+    for (int c = 0; c < 4; c++) xc[c] = xv[c];
+    if (kb + 2 < nk) load_step(qrow, drow, xrow, nv, tv, kb + 2, h, q, dd, xv);
     if (kb >= kStages) {  // the MMAs of step kb - 2 read this stage
       const bool mine = bar_wait(bars + 8 * s, ((kb - kStages) >> 1) & 1);
-      if (__syncthreads_or(!mine)) {
-        ok = false;
-        break;
-      }
+      if (__syncthreads_or(!mine)) return false;
     }
     const uint32_t a_tile = base + s * 2 * kTileBytes, b_tile = a_tile + kTileBytes;
-#pragma unroll
-    for (int blk = 0; blk < 2; blk++) {  // rows past N hold zero codes and scales: zero weights
-      const float sc = h2f(dc[blk]);
-      sts128(a_tile + sw128(tid, 4 * blk + 0), deq8(qc[blk].x, qc[blk].y, 0, sc));
-      sts128(a_tile + sw128(tid, 4 * blk + 1), deq8(qc[blk].z, qc[blk].w, 0, sc));
-      sts128(a_tile + sw128(tid, 4 * blk + 2), deq8(qc[blk].x, qc[blk].y, 4, sc));
-      sts128(a_tile + sw128(tid, 4 * blk + 3), deq8(qc[blk].z, qc[blk].w, 4, sc));
+    {  // rows past N hold zero codes and scales: zero weights
+      const float sc = h2f(dc);
+      sts128(a_tile + sw128(r, 4 * h + 0), deq8(qc.x, qc.y, 0, sc));
+      sts128(a_tile + sw128(r, 4 * h + 1), deq8(qc.z, qc.w, 0, sc));
+      sts128(a_tile + sw128(r, 4 * h + 2), deq8(qc.x, qc.y, 4, sc));
+      sts128(a_tile + sw128(r, 4 * h + 3), deq8(qc.z, qc.w, 4, sc));
     }
 #pragma unroll
-    for (int c = 0; c < 8; c++) sts128(b_tile + sw128(tid, c), xc[c]);
+    for (int c = 0; c < 4; c++) sts128(b_tile + sw128(r, 4 * h + c), xc[c]);
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncthreads();
     if (tid == 0) {
@@ -186,6 +187,12 @@ __global__ void __launch_bounds__(128) q4_gemm_tc_kernel(const uint16_t* __restr
       asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bars + 8 * s)
                    : "memory");
     }
+    return true;
+  };
+  bool ok = true;
+  for (int kb = 0; kb < nk && ok; kb += 2) {
+    ok = step(kb, qa, da, xa);
+    if (ok && kb + 1 < nk) ok = step(kb + 1, qb, db, xb);
   }
   if (ok) {  // the last commit tracks every MMA this CTA issued
     const bool mine = bar_wait(bars + 8 * ((nk - 1) & 1), ((nk - 1) >> 1) & 1);
@@ -193,15 +200,17 @@ __global__ void __launch_bounds__(128) q4_gemm_tc_kernel(const uint16_t* __restr
   }
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   if (ok) {
-    const int row = n0 + warp * 32 + lane;  // TMEM lane = weight row; columns = tokens
+    // TMEM lane = weight row (warp w reaches lanes 32 (w % 4) ..), columns = tokens:
+    // warps 0-3 read columns [0, 64), warps 4-7 [64, 128)
+    const int row = n0 + (warp & 3) * 32 + lane, cb = (warp >> 2) * (kBN / 2);
 #pragma unroll 1
-    for (int c0 = 0; c0 < kBN; c0 += 16) {
+    for (int c0 = cb; c0 < cb + kBN / 2; c0 += 16) {
       uint32_t v[16];
       asm volatile(
           "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
           : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
             "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
-          : "r"(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0));
+          : "r"(tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)c0));
       asm volatile("tcgen05.wait::ld.sync.aligned;"
                    : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]),
                      "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]), "+r"(v[14]),

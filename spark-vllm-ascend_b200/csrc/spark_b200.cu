@@ -301,7 +301,7 @@ int spark_q4_gemm_tc(const uint16_t* x, const uint8_t* qs, const uint16_t* d, ui
     return SPARK_ERR_ALIGNMENT;
   if (set_smem(reinterpret_cast<const void*>(&tc::q4_gemm_tc_kernel), tc::kSmemBytes)) return SPARK_ERR_LAUNCH;
   const dim3 grid((unsigned)((n + tc::kBM - 1) / tc::kBM), (unsigned)((t + tc::kBN - 1) / tc::kBN));
-  tc::q4_gemm_tc_kernel<<<grid, 128, tc::kSmemBytes, as_stream(stream)>>>(x, qs, d, y, t, n, k, error);
+  tc::q4_gemm_tc_kernel<<<grid, tc::kThreads, tc::kSmemBytes, as_stream(stream)>>>(x, qs, d, y, t, n, k, error);
   return cudaGetLastError() == cudaSuccess ? SPARK_OK : SPARK_ERR_LAUNCH;
 }
 
