@@ -110,6 +110,21 @@ def dist_setup():
     return world, rank, local
 
 
+def _workload_config(args, cfg, world: int, splits: int) -> dict:
+    """The workload keys both arms report (the same dict for the same command line)."""
+    tp = args.tp
+    if tp > 1:
+        workload = f"configs[3]: synthetic 4B Q4_0 batch-1 decode, tensor parallel over {tp} GPUs, 2048 prompt, greedy"
+    elif cfg.spark_features:
+        workload = ("Spark-X2.6-4B architecture (gate, GELU, sliding 513 / partial RoPE, head_dim 256, tied "
+                    "Q6_K head), synthetic weights, batch-1 decode, greedy")
+    else:
+        workload = "configs[2]: synthetic 4B Q4_0 batch-1 decode, 2048 prompt, greedy"
+    return {"workload": workload, "model": cfg.name, "layers": cfg.num_layers, "hidden": cfg.hidden_size,
+            "vocab": cfg.vocab_size, "prompt": PROMPT_LEN, "ctx_range": [PROMPT_LEN, PROMPT_LEN + args.steps - 1],
+            "splits": splits, "parallelism": f"tp{tp}" if tp > 1 else f"replicas x{world}"}
+
+
 def build_engine(args, device, seed):
     import torch
     from spark_b200.config import SparkConfig, spark_x26_config
@@ -360,16 +375,8 @@ def run_spark(args):
             "dtype": "q4_0 weights x fp32 accumulate, bf16 activations / KV",
             "data": "synthetic: seeded N(0,0.02) weights -> Q4_0" +
                     (", random Q6_K tied embedding" if cfg.tied_q6k_head else "") + ", 2048 uniform-random prompt ids",
-            "config": {"workload": (f"configs[3]: synthetic 4B Q4_0 batch-1 decode, tensor parallel over {tp} GPUs, "
-                                    "2048 prompt, greedy") if tp > 1 else
-                       ("Spark-X2.6-4B architecture (gate, GELU, sliding 513 / partial RoPE, head_dim 256, tied "
-                        "Q6_K head), synthetic weights, batch-1 decode, greedy" if cfg.spark_features else
-                        "configs[2]: synthetic 4B Q4_0 batch-1 decode, 2048 prompt, greedy"),
-                       "model": cfg.name,
-                       "layers": layers, "hidden": cfg.hidden_size, "vocab": cfg.vocab_size, "prompt": PROMPT_LEN,
-                       "ctx_range": [PROMPT_LEN, PROMPT_LEN + args.steps - 1], "splits": eng.splits,
+            "config": {**_workload_config(args, cfg, world, eng.splits),
                        "kernels_per_step": eng.kernels_per_step(), "mode": eng.mode,
-                       "parallelism": f"tp{tp}" if tp > 1 else f"replicas x{world}",
                        "l2": f"inputs larger than L2 ({w.q4_bytes() / 1e9:.2f} GB of weights per step)"},
             "e2e": {"value": round(args.steps * seqs / (e2e_ms / 1e3), 3), "unit": "tokens/s",
                     "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4, "wall_s": round(wall_e2e, 3),
@@ -474,11 +481,10 @@ def run_reference(args):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "q4_0 weights x fp32 accumulate, bf16 activations / KV",
         "data": "synthetic: random Q4_0 codes / scales and bf16 KV prefix of the real shapes",
-        "config": {"workload": "configs[2]: synthetic 4B Q4_0 batch-1 decode, 2048 prompt, greedy",
-                   "layers": cfg.num_layers, "ctx": PROMPT_LEN, "splits": splits, "setup_s": round(setup_s, 1)},
+        "config": _workload_config(args, cfg, world, splits),
         "cpu_baseline": {"value": round(tps, 4), "unit": "tokens/s", "cores": threads, "kind": "port",
                          "sample": f"{args.steps} samples of one layer (or the LM head) of a ctx-{PROMPT_LEN} "
-                                   f"decode step; {units} samples = 1 token"},
+                                   f"decode step; {units} samples = 1 token (setup {setup_s:.1f} s)"},
         "e2e": {"value": round(tps, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 

@@ -62,9 +62,14 @@ int spark_q4_dequantize_bf16(const uint8_t* qs, const uint16_t* d, int64_t rows,
  * rounding as spark_q4_dequantize_bf16), fp32 accumulation (tcgen05.mma).  Replaces the
  * prefill's dequantize -> bf16 matmul (integration/weights.py:28-31 and vLLM's torch
  * linear layers, integration/model.py:50-62) without the bf16 weight copy.  k % 64 == 0;
- * x [T][k] bf16 16-B aligned; *error is set nonzero if a wait inside the kernel timed out. */
+ * x [T][k] bf16 16-B aligned.  Each wait on the tensor cores is bounded by wait_ns
+ * (< 0: the default 0.5 s; 0: give up at the first look, for testing the error path).
+ * *error (caller-owned, required) becomes 1 when a wait ran out (y is then not
+ * written); the CTA still waits, with a fixed 2 s bound, for the MMAs it issued before it
+ * frees its tensor memory.  2 means that drain ran out too and the CTA kept its tensor
+ * memory: the CUDA context must then be treated as unusable. */
 int spark_q4_gemm_tc(const uint16_t* x, const uint8_t* qs, const uint16_t* d, uint16_t* y, int t, int n, int k,
-                     int* error, void* stream);
+                     int* error, int64_t wait_ns, void* stream);
 
 /* y[b][n] = bf16(sum_k W[n][k] * x[b][k]) for b < batch (1..8); fp32 accumulation
  * in the fixed order documented in q4_gemv.cuh.  n even, k % 32 == 0.
@@ -126,7 +131,7 @@ int spark_attn_splitkv(const uint16_t* q, const uint16_t* k_cache, const uint16_
  * that finishes last for a kv head merges that head's splits in the same order
  * as spark_attn_combine, so out is bit-identical to split + combine.
  * splits <= 256.  Replaces AttentionStage.execute (kernels/attention.py:120-286)
- * followed by merge_attention (kernels/vector.py:154-192). */
+ * followed by merge_attention (kernels/vector.py:46-83). */
 int spark_attn_decode(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
                       const int32_t* block_table, const int64_t* pos, const int32_t* seq_len, int nq, int nkv,
                       int head_dim, int block_size, int splits, int max_split_tokens, float scale, float* part_o,
@@ -154,7 +159,7 @@ int spark_attn_decode_noalloc(const uint16_t* q, const uint16_t* k_cache, const 
                               uint16_t* out, int* error, void* stream);
 
 /* Log-sum-exp combine of split partials -> bf16 [nq][head_dim].
- * Replaces merge_attention (kernels/vector.py:154-192) without the output gate. */
+ * Replaces merge_attention (kernels/vector.py:46-83) without the output gate. */
 int spark_attn_combine(const float* part_o, const float* part_lse, int splits, int nq, int head_dim, uint16_t* out,
                        void* stream);
 

@@ -18,7 +18,7 @@
  *   RoPE (neox) .............. kernels/qkv.py:179-189 (bf16 inputs, separate fp32 products, bf16 out)
  *   split-KV attention ....... kernels/attention.py:59-117 (fp32 scores, max, exp, fp32 sum,
  *                              bf16 P for PV, out = acc / l, lse = log(l) + m)
- *   LSE combine .............. kernels/vector.py:154-192 (softmax over lse, weights divided
+ *   LSE combine .............. kernels/vector.py:46-83 (softmax over lse, weights divided
  *                              first, acc += w * O without fusion, bf16 round)
  *   slot mapping ............. integration/slot_mapping.py:8-22 and
  *                              tools/validation/test_slot_mapping.py:26-28

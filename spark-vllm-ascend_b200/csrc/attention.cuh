@@ -3,7 +3,7 @@
 // Reference: kernels/attention.py:59-117 (softmax / accumulate / finish of one
 // (part, kv-head) task: fp32 scores scaled after the dot product, running max,
 // exp, fp32 sum, P rounded to bf16 for P.V, out = acc / l, lse = log l + m) and
-// kernels/vector.py:154-192 (merge_attention: softmax over the split lse values,
+// kernels/vector.py:46-83 (merge_attention: softmax over the split lse values,
 // weights divided by their sum first, acc += w * O, bf16 round).
 //
 // KV cache layout (per layer): bf16 [num_blocks][num_kv_heads][block_size][head_dim]
@@ -105,7 +105,7 @@ __device__ __forceinline__ void attn_issue_rows(const AttnArgs& a, const uint16_
 }
 
 // Merge the split partials of G query heads [hq0, hq0+G) into bf16 out, in the
-// canonical order of merge_attention (kernels/vector.py:154-192): M = max lse,
+// canonical order of merge_attention (kernels/vector.py:46-83): M = max lse,
 // w_s = exp(lse_s - M) (0 for empty splits), den = sum_s w_s in ascending s,
 // w_s /= den, out = bf16(sum_s w_s * O_s) in ascending s (product, then add).
 // The weights are computed in parallel, only the two canonical sums are serial;

@@ -12,8 +12,18 @@
 // stage (one 128-byte swizzle atom of bf16), 2 stages; 256 threads, two per tile row
 // (one per 32-wide half of a K step).  Both operands are K-major with the 128-byte
 // swizzle: row r of a tile at (r / 8) * 1024 + (r % 8) * 128, its 16-byte chunk c at
-// chunk position c ^ (r % 8).  Every wait is bounded by %globaltimer; a wait
-// that runs out sets *error and the CTA frees its tensor memory and returns.
+// chunk position c ^ (r % 8).
+//
+// Waits on the MMA completion barriers are bounded by %globaltimer (limit_ns, a kernel
+// argument).  A wait that runs out sets *error = 1; the CTA then waits, with its own
+// bound of kDrainNs, for the commit of the last step whose MMAs it issued (a commit
+// tracks every earlier MMA of the issuing thread), so no MMA still reads the shared
+// tiles or writes the accumulator columns when the CTA frees them.  If that drain also
+// runs out, the CTA sets *error = 2 and exits WITHOUT freeing its tensor memory: the
+// context must then be treated as unusable.  tcgen05.alloc itself has no bound: it
+// blocks until 128 columns are free, so the kernel assumes no other tensor-memory user
+// on the SM at the same time (shared memory admits at most 3 of its own CTAs per SM,
+// 384 of the 512 columns).
 #pragma once
 
 #include <cstdint>
@@ -30,7 +40,8 @@ constexpr int kStages = 2;
 constexpr int kThreads = 256;            // two threads per tile row: one per half of a K step
 constexpr int kTileBytes = kBM * kBK * 2;  // 16 KB; the token tile is the same size (kBN == kBM)
 constexpr int kSmemBytes = kStages * 2 * kTileBytes + 1024 + 64;  // tiles, 1024-B alignment slack, barriers
-constexpr unsigned long long kWaitNs = 500ull * 1000 * 1000;      // 0.5 s per wait
+constexpr unsigned long long kWaitNs = 500ull * 1000 * 1000;      // default limit of a wait: 0.5 s
+constexpr unsigned long long kDrainNs = 2000ull * 1000 * 1000;    // drain of issued MMAs after a timeout
 
 static_assert(kBN == kBM, "token and weight tiles share one size");
 
@@ -57,17 +68,18 @@ __device__ __forceinline__ unsigned long long now_ns() {
   return t;
 }
 
-__device__ __forceinline__ bool bar_wait(uint32_t bar, uint32_t parity) {
+// non-blocking test of the phase, so a limit of 0 ns gives up after one look
+__device__ __forceinline__ bool bar_wait(uint32_t bar, uint32_t parity, unsigned long long limit_ns) {
   const unsigned long long t0 = now_ns();
   for (;;) {
     uint32_t done;
     asm volatile(
-        "{.reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p;}"
+        "{.reg .pred p; mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p;}"
         : "=r"(done)
         : "r"(bar), "r"(parity)
         : "memory");
     if (done) return true;
-    if (now_ns() - t0 > kWaitNs) return false;
+    if (now_ns() - t0 >= limit_ns) return false;
   }
 }
 
@@ -110,7 +122,8 @@ __device__ __forceinline__ void sts128(uint32_t addr, uint4 v) {
 __global__ void __launch_bounds__(kThreads) q4_gemm_tc_kernel(const uint16_t* __restrict__ x,
                                                          const uint8_t* __restrict__ qs,
                                                          const uint16_t* __restrict__ d, uint16_t* __restrict__ y,
-                                                         int T, int N, int K, int* __restrict__ error) {
+                                                         int T, int N, int K, int* __restrict__ error,
+                                                         unsigned long long limit_ns) {
   extern __shared__ unsigned char smem_raw[];
   const uint32_t raw = (uint32_t)__cvta_generic_to_shared(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -158,7 +171,7 @@ __global__ void __launch_bounds__(kThreads) q4_gemm_tc_kernel(const uint16_t* __
     for (int c = 0; c < 4; c++) xc[c] = xv[c];
     if (kb + 2 < nk) load_step(qrow, drow, xrow, nv, tv, kb + 2, h, q, dd, xv);
     if (kb >= kStages) {  // the MMAs of step kb - 2 read this stage
-      const bool mine = bar_wait(bars + 8 * s, ((kb - kStages) >> 1) & 1);
+      const bool mine = bar_wait(bars + 8 * s, ((kb - kStages) >> 1) & 1, limit_ns);
       if (__syncthreads_or(!mine)) return false;
     }
     const uint32_t a_tile = base + s * 2 * kTileBytes, b_tile = a_tile + kTileBytes;
@@ -190,13 +203,32 @@ __global__ void __launch_bounds__(kThreads) q4_gemm_tc_kernel(const uint16_t* __
     return true;
   };
   bool ok = true;
+  int issued = 0;  // steps whose MMAs and commit were issued
   for (int kb = 0; kb < nk && ok; kb += 2) {
     ok = step(kb, qa, da, xa);
-    if (ok && kb + 1 < nk) ok = step(kb + 1, qb, db, xb);
+    issued += ok;
+    if (ok && kb + 1 < nk) {
+      ok = step(kb + 1, qb, db, xb);
+      issued += ok;
+    }
   }
   if (ok) {  // the last commit tracks every MMA this CTA issued
-    const bool mine = bar_wait(bars + 8 * ((nk - 1) & 1), ((nk - 1) >> 1) & 1);
+    const bool mine = bar_wait(bars + 8 * ((nk - 1) & 1), ((nk - 1) >> 1) & 1, limit_ns);
     ok = !__syncthreads_or(!mine);
+  }
+  if (!ok) {
+    // a wait ran out: report it, then wait (own bound) until every issued MMA has
+    // completed before the shared tiles and the accumulator columns are given up
+    if (tid == 0) atomicExch(error, 1);
+    bool drained = true;
+    if (issued > 0) {
+      const int last = issued - 1;
+      drained = !__syncthreads_or(!bar_wait(bars + 8 * (last & 1), (last >> 1) & 1, kDrainNs));
+    }
+    if (!drained) {  // MMAs still outstanding after kDrainNs: keep the columns, poison
+      if (tid == 0) atomicExch(error, 2);
+      return;
+    }
   }
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   if (ok) {
@@ -225,8 +257,6 @@ __global__ void __launch_bounds__(kThreads) q4_gemm_tc_kernel(const uint16_t* __
         }
       }
     }
-  } else if (tid == 0) {
-    atomicExch(error, 1);
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();

@@ -4,7 +4,7 @@
 // NativeLinear.execute_o/execute_down (linear.py:339-370), NativeUp.execute
 // (linear.py:585-611) and FusedQkvStage.execute_fused (qkv.py:201-236).
 //
-// Weight layout in HBM (lossless split of gguf Q4_0 blocks, see DESIGN.md):
+// Weight layout in HBM (lossless split of gguf Q4_0 blocks):
 //   qs : uint8  [N][K/2]   the 16 nibble bytes of each 32-weight block, gguf order
 //                          (byte j: low nibble = element j, high nibble = element j+16)
 //   d  : fp16   [N][K/32]  the block scale

@@ -294,14 +294,15 @@ int spark_q4_dequantize_bf16(const uint8_t* qs, const uint16_t* d, int64_t rows,
 }
 
 int spark_q4_gemm_tc(const uint16_t* x, const uint8_t* qs, const uint16_t* d, uint16_t* y, int t, int n, int k,
-                     int* error, void* stream) {
+                     int* error, int64_t wait_ns, void* stream) {
   if (!x || !qs || !d || !y || !error) return SPARK_ERR_INVALID_ARG;
   if (t <= 0 || n <= 0 || k <= 0 || k % tc::kBK || t > 65535 * tc::kBN) return SPARK_ERR_UNSUPPORTED_SHAPE;
   if (!aligned(x, 16) || !aligned(qs, 16) || !aligned(d, 2) || !aligned(y, 2) || !aligned(error, 4))
     return SPARK_ERR_ALIGNMENT;
   if (set_smem(reinterpret_cast<const void*>(&tc::q4_gemm_tc_kernel), tc::kSmemBytes)) return SPARK_ERR_LAUNCH;
   const dim3 grid((unsigned)((n + tc::kBM - 1) / tc::kBM), (unsigned)((t + tc::kBN - 1) / tc::kBN));
-  tc::q4_gemm_tc_kernel<<<grid, tc::kThreads, tc::kSmemBytes, as_stream(stream)>>>(x, qs, d, y, t, n, k, error);
+  const unsigned long long limit = wait_ns < 0 ? tc::kWaitNs : (unsigned long long)wait_ns;
+  tc::q4_gemm_tc_kernel<<<grid, tc::kThreads, tc::kSmemBytes, as_stream(stream)>>>(x, qs, d, y, t, n, k, error, limit);
   return cudaGetLastError() == cudaSuccess ? SPARK_OK : SPARK_ERR_LAUNCH;
 }
 

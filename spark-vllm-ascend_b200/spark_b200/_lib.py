@@ -22,7 +22,7 @@ SIGNATURES: dict[str, list] = {
     "spark_q4_quantize": [_P, _I64, _I64, _P, _P, _P],
     "spark_q4_split_gguf": [_P, _I64, _I64, _P, _P, _P],
     "spark_q4_dequantize_bf16": [_P, _P, _I64, _I64, _P, _P],
-    "spark_q4_gemm_tc": [_P, _P, _P, _P, _I, _I, _I, _P, _P],
+    "spark_q4_gemm_tc": [_P, _P, _P, _P, _I, _I, _I, _P, _I64, _P],
     "spark_q4_gemv": [_P, _P, _P, _P, _I, _I, _I, _P],
     "spark_rmsnorm_q4_gemv": [_P, _P, _P, _F, _P, _P, _P, _P, _I, _I, _P],
     "spark_rmsnorm_gate_up_silu": [_P, _P, _P, _F, _P, _P, _P, _P, _I, _I, _P],

@@ -82,18 +82,22 @@ def q4_dequantize(qs: torch.Tensor, d: torch.Tensor) -> torch.Tensor:
     return w
 
 
-def q4_gemm(x: torch.Tensor, qs: torch.Tensor, d: torch.Tensor, error: torch.Tensor | None = None) -> torch.Tensor:
+def q4_gemm(x: torch.Tensor, qs: torch.Tensor, d: torch.Tensor, error: torch.Tensor,
+            wait_ns: int = -1) -> torch.Tensor:
     """Prefill GEMM on the tensor cores: x bf16 [T, K] times the Q4_0 weight [N, K]
     (dequantized in shared memory) -> bf16 [T, N].  K % 64 == 0.  ``error`` (int32 [1],
-    optional) receives a nonzero value if a wait inside the kernel timed out."""
+    required, on the device) becomes nonzero if a wait inside the kernel ran out, and y
+    is then not valid: the caller owns the status word and must read it.  ``wait_ns``
+    bounds each wait (-1: the kernel's 0.5 s; 0: give up at once, for tests)."""
     n, k = _q4(qs, d)
     _cuda(x, "x", BF16)
+    _cuda(error, "error", torch.int32)
+    _check(error.numel() >= 1, "error must hold one int32")
     x2 = x.reshape(-1, k)
     _check(x2.is_contiguous(), "x must be contiguous")
     t = x2.shape[0]
     y = torch.empty((t, n), dtype=BF16, device=x.device)
-    err = error if error is not None else torch.zeros(1, dtype=torch.int32, device=x.device)
-    call("spark_q4_gemm_tc", _p(x2), _p(qs), _p(d), _p(y), t, n, k, _p(err), _stream())
+    call("spark_q4_gemm_tc", _p(x2), _p(qs), _p(d), _p(y), t, n, k, _p(error), int(wait_ns), _stream())
     return y
 
 

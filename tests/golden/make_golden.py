@@ -27,6 +27,15 @@ Fixtures written next to this script:
   the expected slots computed by that test's own CPU formula (:26-28):
   ``table[pos // size] * size + pos % size``, -1 padding up to ``maximum``.
   Stored sparsely: only the first ``count`` entries (the rest are -1).
+* ``ref_pack_q4.npz`` -- outputs of the reference's own host repack functions, imported
+  from its source tree (``spark_vllm_ascend.integration.weights``: ``unpack_q4``,
+  weights.py:34-40, and ``pack``, weights.py:42-54; pure numpy / torch): gguf Q4_0 block
+  bytes, ``unpack_q4``'s signed codes and fp16 scales, and ``pack(q, s, m)`` for m = 8 and
+  m = 4 (the tile heights the reference uses for qkv / o / gate_up and down,
+  weights.py:62, 77).  ``pack`` asserts BF16-exact scales (weights.py:52), so the packed
+  case uses blocks whose fp16 scales are bf16 values; the unpack case also covers the
+  seeded N(0, 0.02) weights quantized by gguf.  Needs the reference tree (path in
+  ``SPARK_REFERENCE_SRC``, default the mounted checkout); skipped when it is absent.
 """
 from __future__ import annotations
 
@@ -117,9 +126,61 @@ def make_slots() -> None:
     np.savez_compressed(HERE / "slot_mapping_kat.npz", **out)
 
 
+class _GgufTensor:
+    """The attributes of a gguf ReaderTensor that ``unpack_q4`` reads."""
+
+    def __init__(self, blocks: np.ndarray, n: int, k: int):
+        self.name = "synthetic.weight"
+        self.tensor_type = 2  # GGMLQuantizationType.Q4_0
+        self.shape = np.array([k, n], dtype=np.uint64)  # gguf order: innermost first
+        self.data = blocks.reshape(n, k // 32 * 18)
+
+
+def ref_pack_blocks(rng, n: int, k: int) -> np.ndarray:
+    """Q4_0 blocks [n, k/32, 18] with random nibbles and fp16 scales that are bf16 values
+    (the reference's pack requires BF16-exact scales)."""
+    d32 = (rng.standard_normal((n, k // 32)) * 2e-3).astype(np.float32)
+    d_bf = (d32.view(np.uint32) & 0xFFFF0000).view(np.float32)  # truncate to bf16
+    d16 = d_bf.astype(np.float16)
+    assert np.array_equal(d16.astype(np.float32), d_bf)
+    b = np.empty((n, k // 32, 18), np.uint8)
+    b[:, :, :2] = d16.view(np.uint8).reshape(n, k // 32, 2)
+    b[:, :, 2:] = rng.integers(0, 256, size=(n, k // 32, 16), dtype=np.uint8)
+    return b
+
+
+def make_ref_pack() -> bool:
+    import os
+    import sys
+    src = os.environ.get("SPARK_REFERENCE_SRC", "/root/reference/src")
+    if not Path(src, "spark_vllm_ascend", "integration", "weights.py").exists():
+        print("reference tree not found: ref_pack_q4.npz not regenerated")
+        return False
+    sys.path.insert(0, src)
+    from gguf import GGMLQuantizationType as T
+    from gguf import quants
+    from spark_vllm_ascend.integration.weights import pack, unpack_q4
+
+    rng = np.random.default_rng(2468)
+    out = {}
+    n, k = 64, 512
+    w = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
+    blocks = np.ascontiguousarray(quants.quantize(w, T.Q4_0), dtype=np.uint8).reshape(n, k // 32, 18)
+    q, s = unpack_q4(_GgufTensor(blocks, n, k))
+    out.update({"gguf.blocks": blocks, "gguf.q": q, "gguf.s": s})
+    n, k = 32, 256
+    blocks = ref_pack_blocks(rng, n, k)
+    q, s = unpack_q4(_GgufTensor(blocks, n, k))
+    out.update({"bf16.blocks": blocks, "bf16.q": q, "bf16.s": s,
+                "bf16.pack8": pack(q, s, 8), "bf16.pack4": pack(q, s, 4)})
+    np.savez_compressed(HERE / "ref_pack_q4.npz", **out)
+    return True
+
+
 if __name__ == "__main__":
     make_q4()
     make_q6k()
     make_slots()
+    make_ref_pack()
     for p in sorted(HERE.glob("*.npz")):
         print(p.name, p.stat().st_size)

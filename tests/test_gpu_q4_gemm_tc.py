@@ -62,9 +62,11 @@ def test_q4_gemm_tc_identity_is_bit_exact_dequant(cuda, n, k):
     qs, d = _planes(n, k, seed=n)
     d = torch.where(torch.arange(d.numel(), device="cuda").reshape(d.shape) % 3 == 0, -d, d)
     x = torch.eye(k, dtype=torch.bfloat16, device="cuda")
-    y = ops.q4_gemm(x, qs, d)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    y = ops.q4_gemm(x, qs, d, err)
     w = ops.q4_dequantize(qs, d)
     torch.cuda.synchronize()
+    assert int(err.item()) == 0
     assert torch.equal(y.float(), w.t().float())
     nz = w.t() != 0
     assert torch.equal(y.view(torch.int16)[nz], w.t().contiguous().view(torch.int16)[nz])
@@ -75,5 +77,32 @@ def test_q4_gemm_tc_rejects_bad_shapes(cuda):
     from spark_b200 import ops
     qs, d = _planes(128, 96, seed=1)  # K = 96: not a multiple of 64
     x = torch.zeros((4, 96), dtype=torch.bfloat16, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
     with pytest.raises(Exception):
-        ops.q4_gemm(x, qs, d)
+        ops.q4_gemm(x, qs, d, err)
+
+
+def test_q4_gemm_tc_wait_timeout_reports_and_recovers(cuda):
+    """A wait limit of 0 ns makes the first unfinished MMA wait give up: the kernel must
+    return (no hang), report 1 in the caller's status word (not 2: the issued MMAs drained
+    and the tensor memory was freed), and the next call with the default limit must
+    match the dequantize + fp32 product again on the same context."""
+    import torch
+    from spark_b200 import ops
+    t, n, k = 256, 512, 4096  # 64 K steps per CTA: waits on in-flight MMAs are certain
+    qs, d = _planes(n, k, seed=5)
+    g = torch.Generator(device="cuda").manual_seed(11)
+    x = torch.randn((t, k), generator=g, device="cuda").to(torch.bfloat16)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ops.q4_gemm(x, qs, d, err, wait_ns=0)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 1
+    err.zero_()
+    y = ops.q4_gemm(x, qs, d, err)
+    w = ops.q4_dequantize(qs, d)
+    ref = x.float() @ w.float().t()
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    scale = ref.abs().amax(dim=1, keepdim=True).clamp_min(1e-6)
+    diff = (y.float() - ref).abs()
+    assert bool((diff <= 1e-2 * ref.abs() + 1e-3 * scale).all()), float((diff / scale).max())
