@@ -14,8 +14,11 @@ the roofline of the dominant kernel (Q4 gate_up GEMV) against the measured HBM
 peak, the whole-step roofline (weights + KV bytes / TPOT), clocks sampled during the
 timed region, and the CPU baseline (the C oracle on the host cores).
 
-Multi-GPU (torchrun): every rank decodes its own replica (no collective on the data
-path; "scaling": "weak"); timing is the max over ranks.
+Multi-GPU (torchrun): by default all N ranks decode ONE sequence tensor-parallel
+(qkv / gate_up / LM head row-sharded, o_proj / down K-sharded, the
+partial sums exchanged inside the step kernel over peer memory; "scaling": "strong");
+``--tp 1`` runs independent replicas instead ("scaling": "weak").  Timing is the max over
+ranks.
 """
 from __future__ import annotations
 
@@ -492,8 +495,9 @@ def run_reference(args):
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--tp", type=int, default=1,
-                    help="tensor parallel over all ranks (configs[3]); default 1: independent replicas")
+    ap.add_argument("--tp", type=int, default=0,
+                    help="tensor parallel degree: 0 (default) = all ranks decode one sequence together "
+                         "(configs[3] under torchrun, one GPU alone); 1 = independent replicas")
     ap.add_argument("--steps", type=int, default=4096)
     ap.add_argument("--warmup", type=int, default=16)
     ap.add_argument("--impl", choices=["spark", "reference"], default="spark")
@@ -509,6 +513,8 @@ def main(argv=None):
     ap.add_argument("--layers", type=int, default=36,
                     help="decoder layers (36 = the benchmark model; fewer only for small profiling captures)")
     args = ap.parse_args(argv)
+    if args.tp == 0:  # the multi-GPU bench measures tensor parallelism, not replicas
+        args.tp = int(os.environ.get("WORLD_SIZE", "1"))
     global PROMPT_LEN
     PROMPT_LEN = args.prompt
     if args.warmup < 3:

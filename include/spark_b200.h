@@ -263,6 +263,13 @@ int spark_read_device_error(int* value, int reset);
 /* GEMV prologue: where x comes from */
 #define SPARK_PRO_BF16 0  /* a: bf16 [k] (or embed row embed[*token] when embed != NULL) */
 #define SPARK_PRO_PARTS 1 /* a: fp32 [a_parts][k]; x = bf16(((a_0 + a_1) + ...)) */
+#define SPARK_PRO_ATTN 2  /* o_proj fused behind the attention stage just before it (wait = -1, no norm,
+                             kp = that stage's nkv, k = nq * head_dim, splits = its splits, nkv * splits
+                             <= CTAs): CTA c takes K part g = c / splits (kv head g) of the row groups
+                             c % splits + splits * m, its input being head g's combined attention output,
+                             which the attention stage combines in every CTA of the head and leaves staged
+                             in shared memory (attn_out is then not written, and no stage may wait on the
+                             attention stage); a is unused */
 
 /* GEMV epilogue */
 #define SPARK_EPI_BF16 0     /* out bf16 [n] (kp == 1) */

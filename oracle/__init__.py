@@ -265,9 +265,10 @@ def split_tokens(length: int, splits: int) -> int:
 
 def attn_split(q, kc, vc, table, length: int, splits: int, scale: float, chunk_accs: int = 0, window: int = 0):
     """q bf16 [nq, D]; kc/vc bf16 [blocks, nkv, bs, D]; returns (part_o [S,nq,D], part_lse [S,nq]).
-    ``chunk_accs`` > 0 selects the persistent-step order (scores over D / 16 lanes per
-    token, PV in 16-token chunks into that many accumulators); ``window`` > 0: only the
-    last ``window`` positions (Spark sliding layers)."""
+    ``chunk_accs`` > 0 selects the persistent-step order with that many consumer warps
+    (scores over D / 16 lanes per token; each split cut into that many token ranges, each
+    with its own softmax, merged by their maxima); ``window`` > 0: only the last
+    ``window`` positions (Spark sliding layers)."""
     q = np.ascontiguousarray(q, dtype=np.uint16)
     kc = np.ascontiguousarray(kc, dtype=np.uint16)
     vc = np.ascontiguousarray(vc, dtype=np.uint16)

@@ -355,17 +355,20 @@ ORC_API void orc_q4_gemv(const uint16_t* x, const uint8_t* qs, const uint16_t* d
  *     two signed bytes, X = 256 h + l); P = sum_j (q_j - 8) X_j is the same exact
  *     integer however it is evaluated;
  *   - a row's K/32 blocks are cut into KP equal parts and each part into KS equal
- *     slices.  Per slice: acc = 0, then for each block in ascending order
- *     acc = fma(fp32(d) * sx, (float)P, acc).  Part value = ((acc_0 + acc_1) + ...)
- *     + acc_{KS-1}.  The row's value is ((part_0 + part_1) + ...) + part_{KP-1},
- *     rounded to bf16 (parts are exchanged between kernels as fp32). */
+ *     slices.  A slice runs four chains (the kernel's four lanes per row pair, each
+ *     scaling one block of every group of four): chain c = blocks b0 + c, b0 + 4 + c,
+ *     ... of the slice (b0 its first block) in ascending order, each from acc = 0 with
+ *     acc = fma(fp32(d) * sx, (float)P, acc).  Slice value = (chain_0 + chain_1) +
+ *     (chain_2 + chain_3).  Part value = ((slice_0 + slice_1) + ...) + slice_{KS-1}.
+ *     The row's value is ((part_0 + part_1) + ...) + part_{KP-1}, rounded to bf16
+ *     (parts are exchanged between kernels as fp32). */
 static void t16_row_parts(const uint8_t* qs, const uint16_t* d, const xq_block* xb, int64_t nb, int kp, int ks,
                           float* parts, int64_t pstride) {
     int64_t bpp = nb / kp, bps = bpp / ks;
     for (int p = 0; p < kp; p++) {
         float part = 0.0f;
         for (int sl = 0; sl < ks; sl++) {
-            float acc = 0.0f;
+            float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
             int64_t b0 = (int64_t)p * bpp + (int64_t)sl * bps;
             for (int64_t b = b0; b < b0 + bps; b++) {
                 const uint8_t* q = qs + b * 16;
@@ -374,9 +377,11 @@ static void t16_row_parts(const uint8_t* qs, const uint16_t* d, const xq_block* 
                 for (int e = 0; e < 16; e++)
                     P += (int32_t)(q[e] & 15) * xx->X[e] + (int32_t)(q[e] >> 4) * xx->X[e + 16];
                 P -= xx->C;
-                acc = fmaf(h2f(d[b]) * xx->sx, (float)P, acc);
+                float* a = acc + ((b - b0) & 3);
+                *a = fmaf(h2f(d[b]) * xx->sx, (float)P, *a);
             }
-            part = sl == 0 ? acc : part + acc;
+            float sv = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+            part = sl == 0 ? sv : part + sv;
         }
         parts[p * pstride] = part;
     }
@@ -624,16 +629,57 @@ static float score_dot_l(const float* qf, const uint16_t* kr, int dim, int lanes
 
 /* q bf16 [nq][dim]; caches bf16 [blocks][nkv][bs][dim]; table int32;
  * part_o fp32 [splits][nq][dim]; part_lse fp32 [splits][nq] */
-/* W == 0: PV sums each output dim over the split's tokens in ascending order.
- * W > 0 (persistent-step order): the split's tokens form 16-token chunks; chunk c
- * is summed (tokens ascending) into accumulator c mod W, chunks in ascending order;
- * O = ((O_0 + O_1) + ...) + O_{W-1}, empty accumulators included as 0. */
+/* W == 0 (per-kernel order): scores over 8 lanes per token; m = max; p = exp(s - m),
+ * l over 32 lanes (token i -> lane i mod 32, butterfly), P = bf16(p); PV sums each output
+ * dim over the split's tokens in ascending order; part = O / l, lse = log(l) + m.
+ * W > 0 (persistent-step order, W = consumer warps): the split's n tokens are cut into W
+ * contiguous ranges of C = roundup(ceil(n / W), tpi) tokens (tpi = 512 / dim, the tokens
+ * one warp scores per step; range w = [w C, min((w + 1) C, n)), empty past n).  Range w
+ * runs a softmax of its own: scores over dim / 16 lanes per token, m_w = its maximum,
+ * p = exp(s - m_w) (0 when m_w = -inf), l_w over 32 lanes (token a + i -> lane i mod 32,
+ * butterfly), P = bf16(p), O_w = sum over its tokens of P V (ascending).  The ranges merge
+ * in order: M = max m_w, f_w = exp(m_w - M) (0 for m_w = -inf), L = (L + f_w l_w),
+ * O = (O + f_w O_w) over w ascending; part = O / L, lse = log(L) + M (a split without a
+ * scored position: part 0, lse -inf). */
 /* window > 0 (Spark sliding layers): only the last `window` positions, [lo, len) with
  * lo = len - window (the reference masks below max(0, len - 513), attention.py:124-127,
  * so its 512-window layers take window 513); the splits cover [lo & ~15, len) and the
  * positions before lo score -inf (p = 0: they add zeros in every sum).  The
  * persistent-step order (W > 0) scores with dim / 16 lanes per token; the per-kernel
  * order (W == 0) with 8. */
+static void attn_range(const float* qf, const uint16_t* kc, const uint16_t* vc, const int32_t* table, int64_t t0,
+                       int64_t a, int64_t b, int64_t lo, int nkv, int hk, int dim, int bs, int lanes, float scale,
+                       float* scores, float* o, float* m_out, float* l_out) {
+    float m = -INFINITY;
+    for (int64_t i = a; i < b; i++) {
+        int64_t t = t0 + i, blk = table[t / bs], off = t % bs;
+        const uint16_t* kr = kc + ((blk * nkv + hk) * bs + off) * dim;
+        if (t < lo) {
+            scores[i] = -INFINITY;
+            continue;
+        }
+        float sc = score_dot_l(qf, kr, dim, lanes) * scale;
+        scores[i] = sc;
+        if (sc > m) m = sc;
+    }
+    float lane[32];
+    for (int l = 0; l < 32; l++) lane[l] = 0.0f;
+    for (int64_t i = a; i < b; i++) {
+        float p = m == -INFINITY ? 0.0f : orc_exp(scores[i] - m);
+        lane[(i - a) % 32] = lane[(i - a) % 32] + p;
+        scores[i] = bf2f(f2bf(p));
+    }
+    butterfly(lane, 32);
+    for (int dd = 0; dd < dim; dd++) o[dd] = 0.0f;
+    for (int64_t i = a; i < b; i++) {
+        int64_t t = t0 + i, blk = table[t / bs], off = t % bs;
+        const uint16_t* vr = vc + ((blk * nkv + hk) * bs + off) * dim;
+        for (int dd = 0; dd < dim; dd++) o[dd] = fmaf(scores[i], bf2f(vr[dd]), o[dd]);
+    }
+    *m_out = m;
+    *l_out = lane[0];
+}
+
 ORC_API void orc_attn_split_x(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const int32_t* table,
                               int64_t len, int nq, int nkv, int dim, int bs, int splits, float scale, int W,
                               int window, float* part_o, float* part_lse) {
@@ -642,59 +688,67 @@ ORC_API void orc_attn_split_x(const uint16_t* q, const uint16_t* kc, const uint1
     int64_t lo = window > 0 && len > window ? len - window : 0;
     int64_t start = lo & ~(int64_t)15;
     int64_t T = split_tokens(len - start, splits);
-    int nacc = W > 0 ? W : 1;
+    int nw = W > 0 ? W : 1;
     float* scores = (float*)malloc(sizeof(float) * (T > 0 ? T : 1));
     float* qf = (float*)malloc(sizeof(float) * dim);
-    float* o = (float*)malloc(sizeof(float) * dim * nacc);
+    float* ow = (float*)malloc(sizeof(float) * dim * nw);
+    float* mw = (float*)malloc(sizeof(float) * nw);
+    float* lw = (float*)malloc(sizeof(float) * nw);
     for (int s = 0; s < splits; s++) {
         int64_t t0 = start + (int64_t)s * T, t1 = t0 + T < len ? t0 + T : len;
         int64_t n = t1 - t0;
         for (int hq = 0; hq < nq; hq++) {
             int hk = hq / group;
             float* po = part_o + ((int64_t)s * nq + hq) * dim;
+            float* pl = part_lse + (int64_t)s * nq + hq;
             if (n <= 0) {
                 for (int dd = 0; dd < dim; dd++) po[dd] = 0.0f;
-                part_lse[(int64_t)s * nq + hq] = -INFINITY;
+                *pl = -INFINITY;
                 continue;
             }
             for (int dd = 0; dd < dim; dd++) qf[dd] = bf2f(q[(int64_t)hq * dim + dd]);
-            float m = -INFINITY;
-            for (int64_t i = 0; i < n; i++) {
-                int64_t t = t0 + i, blk = table[t / bs], off = t % bs;
-                const uint16_t* kr = kc + ((blk * nkv + hk) * bs + off) * dim;
-                if (t < lo) {
-                    scores[i] = -INFINITY;
+            if (W <= 0) {
+                attn_range(qf, kc, vc, table, t0, 0, n, lo, nkv, hk, dim, bs, lanes, scale, scores, ow, mw, lw);
+                for (int dd = 0; dd < dim; dd++) po[dd] = ow[dd] / lw[0];
+                *pl = orc_log(lw[0]) + mw[0];
+                continue;
+            }
+            int64_t tpi = 512 / dim, C = (n + W - 1) / W;
+            C = (C + tpi - 1) / tpi * tpi;
+            float M = -INFINITY;
+            for (int w = 0; w < W; w++) {
+                int64_t a = (int64_t)w * C, b = a + C < n ? a + C : n;
+                if (a >= n) {
+                    mw[w] = -INFINITY;
+                    lw[w] = 0.0f;
+                    for (int dd = 0; dd < dim; dd++) ow[(int64_t)w * dim + dd] = 0.0f;
                     continue;
                 }
-                float sc = score_dot_l(qf, kr, dim, lanes) * scale;
-                scores[i] = sc;
-                if (sc > m) m = sc;
+                attn_range(qf, kc, vc, table, t0, a, b, lo, nkv, hk, dim, bs, lanes, scale, scores,
+                           ow + (int64_t)w * dim, mw + w, lw + w);
+                if (mw[w] > M) M = mw[w];
             }
-            float lane[32];
-            for (int l = 0; l < 32; l++) lane[l] = 0.0f;
-            for (int64_t i = 0; i < n; i++) {
-                float p = orc_exp(scores[i] - m);
-                lane[i % 32] = lane[i % 32] + p;
-                scores[i] = bf2f(f2bf(p));
+            if (M == -INFINITY) {
+                for (int dd = 0; dd < dim; dd++) po[dd] = 0.0f;
+                *pl = -INFINITY;
+                continue;
             }
-            butterfly(lane, 32);
-            float l = lane[0];
-            for (int dd = 0; dd < dim * nacc; dd++) o[dd] = 0.0f;
-            for (int64_t i = 0; i < n; i++) {
-                int64_t t = t0 + i, blk = table[t / bs], off = t % bs;
-                const uint16_t* vr = vc + ((blk * nkv + hk) * bs + off) * dim;
-                float* oa = o + (W > 0 ? (i / 16) % W : 0) * dim;
-                for (int dd = 0; dd < dim; dd++) oa[dd] = fmaf(scores[i], bf2f(vr[dd]), oa[dd]);
+            float L = 0.0f;
+            for (int dd = 0; dd < dim; dd++) po[dd] = 0.0f;
+            for (int w = 0; w < W; w++) {
+                float f = mw[w] == -INFINITY ? 0.0f : orc_exp(mw[w] - M);
+                L = L + f * lw[w];
+                for (int dd = 0; dd < dim; dd++) po[dd] = po[dd] + f * ow[(int64_t)w * dim + dd];
             }
-            for (int w = 1; w < nacc; w++)
-                for (int dd = 0; dd < dim; dd++) o[dd] = o[dd] + o[w * dim + dd];
-            for (int dd = 0; dd < dim; dd++) po[dd] = o[dd] / l;
-            part_lse[(int64_t)s * nq + hq] = orc_log(l) + m;
+            for (int dd = 0; dd < dim; dd++) po[dd] = po[dd] / L;
+            *pl = orc_log(L) + M;
         }
     }
     free(scores);
     free(qf);
-    free(o);
+    free(ow);
+    free(mw);
+    free(lw);
 }
 
 ORC_API void orc_attn_split_w(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const int32_t* table,

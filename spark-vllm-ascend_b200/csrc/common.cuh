@@ -75,6 +75,29 @@ __device__ __forceinline__ float spark_exp(float x) {
                    __uint_as_float((uint32_t)(n2 + 127) << 23));
 }
 
+// spark_exp for x <= 0 (or -inf) without branches: the same reduction and polynomial,
+// and the scaling by 2^n always as two exact steps (p 2^(n/2)) 2^(n - n/2), which rounds
+// once, where spark_exp rounds once in p 2^n: bit-identical to spark_exp on x <= 0.
+// Arguments below -104 give 0 (spark_exp's cut); NaN is not expected.
+__device__ __forceinline__ float spark_exp_neg(float x) {
+  const float n = rintf(__fmul_rn(x, kLog2e));
+  float r = __fmaf_rn(-n, kLn2Hi, x);
+  r = __fmaf_rn(-n, kLn2Lo, r);
+  float p = 1.98412698e-04f;
+  p = __fmaf_rn(p, r, 1.38888889e-03f);
+  p = __fmaf_rn(p, r, 8.33333377e-03f);
+  p = __fmaf_rn(p, r, 4.16666679e-02f);
+  p = __fmaf_rn(p, r, 1.66666672e-01f);
+  p = __fmaf_rn(p, r, 0.5f);
+  p = __fmaf_rn(p, r, 1.0f);
+  p = __fmaf_rn(p, r, 1.0f);
+  const int ni = x < -104.0f ? 0 : (int)n;  // (the result is discarded below -104)
+  const int n1 = ni / 2, n2 = ni - n1;
+  const float v = __fmul_rn(__fmul_rn(p, __uint_as_float((uint32_t)(n1 + 127) << 23)),
+                            __uint_as_float((uint32_t)(n2 + 127) << 23));
+  return x < -104.0f ? 0.0f : v;
+}
+
 // GELU of a bf16 value as the reference's activation table (kernels/linear.py:540-577,
 // table built in integration/model.py:12-16): table [4096] = gelu of the bf16 inputs
 // 0x3b00 + i and 0xbb00 + i (|x| in [2^-9, 128)); |x| < 2^-9: bf16(x / 2); x >= 128: x;

@@ -720,7 +720,7 @@ static int check_stage(const SparkStage& s, int i, int ncta) {
     if (s.epi != SPARK_EPI_BF16 && s.epi != SPARK_EPI_PARTS && s.epi != SPARK_EPI_ARGMAX) return SPARK_ERR_INVALID_ARG;
   }
   if (s.kind == SPARK_STAGE_GEMV || s.kind == SPARK_STAGE_GEMV_Q6) {
-    if (!s.w || !s.a && !s.embed) return SPARK_ERR_INVALID_ARG;
+    if (!s.w || (!s.a && !s.embed && s.pro != SPARK_PRO_ATTN)) return SPARK_ERR_INVALID_ARG;
     if (s.n <= 0 || s.n % 16 || s.k <= 0 || s.kp <= 0 || s.k % s.kp || (s.k / s.kp) % 64 || s.ks <= 0 ||
         (s.kind == SPARK_STAGE_GEMV && ((s.k / s.kp) / 64) % s.ks))
       return SPARK_ERR_UNSUPPORTED_SHAPE;
@@ -737,6 +737,9 @@ static int check_stage(const SparkStage& s, int i, int ncta) {
     if (s.pro == SPARK_PRO_PARTS) {
       if (s.a_parts <= 0 || s.a_parts > step::kMaxParts || !s.a || s.embed) return SPARK_ERR_INVALID_ARG;
       if (s.k > step::kConsumers * 8) return SPARK_ERR_TOO_LARGE;  // one 8-element group per thread
+    } else if (s.pro == SPARK_PRO_ATTN) {
+      if (s.kind != SPARK_STAGE_GEMV || s.norm || s.embed || s.wait != -1) return SPARK_ERR_INVALID_ARG;
+      if (s.splits <= 0 || (int64_t)s.kp * s.splits > ncta) return SPARK_ERR_INVALID_ARG;
     } else if (s.pro != SPARK_PRO_BF16) {
       return SPARK_ERR_INVALID_ARG;
     }
@@ -792,7 +795,8 @@ static int check_stage(const SparkStage& s, int i, int ncta) {
     return SPARK_ERR_UNSUPPORTED_SHAPE;
   if (s.window < 0) return SPARK_ERR_INVALID_ARG;
   if (reinterpret_cast<uintptr_t>(s.gate) & 1) return SPARK_ERR_ALIGNMENT;
-  if (s.splits <= 0 || s.splits > 4096) return SPARK_ERR_UNSUPPORTED_SHAPE;  // (kv head, split) tasks round-robin
+  // (kv head, split) tasks round-robin; the combine keeps 2 x 4 x splits floats in the scratch
+  if (s.splits <= 0 || s.splits > step::kMaxCombineSplits) return SPARK_ERR_UNSUPPORTED_SHAPE;
   if (s.max_split_tokens <= 0 || s.max_split_tokens > step::kMaxSplitTokens) return SPARK_ERR_TOO_LARGE;
   if ((reinterpret_cast<uintptr_t>(s.kv_new) | reinterpret_cast<uintptr_t>(s.k_cache) |
        reinterpret_cast<uintptr_t>(s.v_cache) | reinterpret_cast<uintptr_t>(s.part_o) |
@@ -879,6 +883,18 @@ int spark_step_run(const SparkStage* host_stages, const SparkStage* dev_stages, 
   for (int i = 0; i < num_stages; i++) {
     const int st = check_stage(host_stages[i], i, ncta);
     if (st != SPARK_OK) return st;
+  }
+  for (int i = 0; i < num_stages; i++) {  // an o_proj fused behind attention: wiring of the pair
+    const SparkStage& o = host_stages[i];
+    if (o.kind == SPARK_STAGE_ATTN) continue;
+    if (o.pro != SPARK_PRO_ATTN) continue;
+    if (i == 0) return SPARK_ERR_INVALID_ARG;
+    const SparkStage& a = host_stages[i - 1];
+    if (a.kind != SPARK_STAGE_ATTN || o.kp != a.nkv || o.k != a.nq * a.head_dim || o.splits != a.splits ||
+        o.epi != SPARK_EPI_PARTS)
+      return SPARK_ERR_INVALID_ARG;
+    for (int j = i; j < num_stages; j++)
+      if (host_stages[j].wait == i - 1) return SPARK_ERR_INVALID_ARG;  // nothing waits on the fused attention
   }
   step::StepParams P;
   memset(&P, 0, sizeof(P));

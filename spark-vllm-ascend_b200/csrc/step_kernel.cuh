@@ -38,9 +38,9 @@ constexpr int kConsumers = kWarps * 32;    // 352
 constexpr int kThreads = kConsumers + 32;  // + the producer warp
 constexpr int kDesc = 16;                  // ring descriptors (units in flight)
 constexpr int kMaxSlices = 4;              // GEMV slices per unit (per-slot slice sums)
-constexpr int kTraceSlots = 8;             // trace stamps per stage
+constexpr int kTraceSlots = 24;            // trace stamps per stage
 constexpr int kSmemBytes = 227 * 1024;
-constexpr int kScratchBytes = 32 * 1024;   // x staging | attention scores / reduction
+constexpr int kScratchBytes = 40 * 1024;   // x staging | attention scores / reduction / combine
 constexpr int kPartialBytes = kDesc * kMaxSlices * 16 * 4;  // slice sums per ring slot
 constexpr int kMiscBytes = 2048;
 constexpr int kRingBytes = kSmemBytes - kScratchBytes - kPartialBytes - kMiscBytes;
@@ -56,6 +56,10 @@ __device__ __forceinline__ unsigned long long gtimer() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
+}
+// cycle checkpoint (clock64) for the optional trace: slot k of the stage's stamps
+__device__ __forceinline__ void cstamp(unsigned long long* tr, int k) {
+  if (tr) tr[k] = (unsigned long long)clock64();
 }
 __device__ __forceinline__ int ld_acquire(const int* p) {
   int v;
@@ -140,9 +144,20 @@ __host__ __device__ __forceinline__ int split_len(int64_t len, int splits) {
 // bytes of a Q6_K unit in the T6 layout: 16 rows x kp_cols columns (6.5625 bits each)
 __host__ __device__ __forceinline__ uint32_t t6_unit_bytes(int kp_cols) { return (uint32_t)(105 * kp_cols / 8); }
 
-// number of units of a GEMV stage that CTA `cta` owns, and its first unit
-__host__ __device__ __forceinline__ int local_units(const SparkStage& s, int cta, int ncta, int& u0) {
+// number of units of a GEMV stage that CTA `cta` owns, its first unit and the stride
+// between its units.  SPARK_PRO_ATTN (o_proj fused behind attention, kp = kv heads):
+// CTA c < kp * splits holds kv head c / splits's combined output, so it takes K part
+// c / splits of the row groups c % splits, c % splits + splits, ...; other stages rotate
+// their units over all CTAs (first unit `rot` on CTA 0).
+__host__ __device__ __forceinline__ int local_units(const SparkStage& s, int cta, int ncta, int& u0, int& ustride) {
+  if (s.pro == SPARK_PRO_ATTN) {
+    const int grp = cta / s.splits, jj = cta - grp * s.splits, rgs = s.n >> 4;
+    u0 = jj * s.kp + grp;
+    ustride = s.splits * s.kp;
+    return grp < s.kp && jj < rgs ? (rgs - jj + s.splits - 1) / s.splits : 0;
+  }
   u0 = (cta - s.rot + ncta) % ncta;
+  ustride = ncta;
   return u0 < s.units ? (s.units - u0 + ncta - 1) / ncta : 0;
 }
 
@@ -154,6 +169,7 @@ struct Smem {
   unsigned long long* full;   // [kDesc] mbarriers
   unsigned long long* empty;  // [kDesc]
   uint32_t* desc_off;         // [kDesc]
+  uint32_t* desc_seq;         // [kDesc] sequence number of the copy last issued into the slot
   int* done;                  // [kDesc] finished tasks of the unit in the slot
   uint32_t* prod_start;       // [kDesc] producer bookkeeping
   uint32_t* prod_end;         // [kDesc]
@@ -175,7 +191,8 @@ __device__ __forceinline__ Smem carve(unsigned char* base) {
   s.full = reinterpret_cast<unsigned long long*>(m);
   s.empty = s.full + kDesc;
   s.desc_off = reinterpret_cast<uint32_t*>(s.empty + kDesc);
-  s.done = reinterpret_cast<int*>(s.desc_off + kDesc);
+  s.desc_seq = s.desc_off + kDesc;
+  s.done = reinterpret_cast<int*>(s.desc_seq + kDesc);
   s.prod_start = reinterpret_cast<uint32_t*>(s.done + kDesc);
   s.prod_end = s.prod_start + kDesc;
   s.abort_flag = reinterpret_cast<volatile int*>(s.prod_end + kDesc);
@@ -187,8 +204,8 @@ __device__ __forceinline__ Smem carve(unsigned char* base) {
   s.rope_cs = reinterpret_cast<uint16_t*>(s.misc64 + 4);
   return s;
 }
-// full 128 + empty 128 + desc_off / done / prod_start / prod_end 4 x 64 + abort / flag 32 +
-// red 256 + red64 128 + stage 280 + misc64 32 + rope_cs 512 = 1752 <= kMiscBytes
+// full 128 + empty 128 + desc_off / desc_seq / done / prod_start / prod_end 5 x 64 + abort / flag 32 +
+// red 256 + red64 128 + stage 280 + misc64 32 + rope_cs 512 = 1816 <= kMiscBytes
 static_assert(sizeof(SparkStage) == 280, "SparkStage layout");
 constexpr int kStageWords = (int)sizeof(SparkStage) / 8;
 
@@ -260,6 +277,7 @@ struct Producer {
     if (tail == seq) tail_off = a;
     s.prod_start[slot] = a;
     s.desc_off[slot] = a;
+    *reinterpret_cast<volatile uint32_t*>(s.desc_seq + slot) = seq;  // (ordered before the arrive below)
     head = a + bytes;
     const uint32_t bar = smem_u32(s.full + slot);
     mbar_expect_tx(bar, bytes);
@@ -277,11 +295,11 @@ struct Producer {
       const SparkStage& st = stage_at(P, i);
       if (P.io.trace) P.io.trace[((size_t)cta * P.num_stages + i) * kTraceSlots + 3] = gtimer();
       if (st.kind == SPARK_STAGE_GEMV || st.kind == SPARK_STAGE_GEMV_Q6) {
-        int u0;
-        const int nl = local_units(st, cta, ncta, u0);
+        int u0, ustride;
+        const int nl = local_units(st, cta, ncta, u0, ustride);
         const uint32_t ub = (uint32_t)(st.kind == SPARK_STAGE_GEMV_Q6 ? t6_unit_bytes(st.k / st.kp) : 9 * (st.k / st.kp));
         for (int j = 0; j < nl; j++) {
-          const unsigned char* src = static_cast<const unsigned char*>(st.w) + (size_t)(u0 + j * ncta) * ub;
+          const unsigned char* src = static_cast<const unsigned char*>(st.w) + (size_t)(u0 + j * ustride) * ub;
           if (!issue(src, ub)) return drain();
         }
       } else {
@@ -318,6 +336,7 @@ struct Producer {
           return drain();
         }
       }
+      if (P.io.trace) P.io.trace[((size_t)cta * P.num_stages + i) * kTraceSlots + 10] = gtimer();
     }
     drain();
   }
@@ -345,6 +364,7 @@ struct Producer {
 // meta = (-8 sum X, sx).  Four consecutive threads stage one block, 8 elements each.
 constexpr int kStageGroups = 4;  // 8-element groups per consumer thread (k <= 12288)
 constexpr int kMaxParts = 8;  // parts summed by a PARTS prologue (K parts x TP ranks)
+constexpr int kPartsBatch = 4;  // parts loaded per L2 round trip
 
 __device__ __forceinline__ void lds_u32x4(uint32_t addr, uint4& v) {
   asm("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
@@ -453,6 +473,60 @@ __device__ __forceinline__ void stage_x(const SparkStage& st, const Smem& s, int
   // requests spread over the L2 slices instead of queueing on the same lines.
   const int rot = 4 * (int)((blockIdx.x * 37u) % (unsigned)(ngrp >> 2));
   // all loads first: one L2 round trip
+  if (st.pro == SPARK_PRO_PARTS) {
+    // every part in flight at once, then summed in part order.  A PARTS input has at most
+    // one 8-element group per thread (k <= kConsumers * 8, the host checks): slot 0.
+    const int g = stage_grp(tid, ngrp, rot);
+#pragma unroll
+    for (int r = 1; r < kStageGroups; r++)
+#pragma unroll
+      for (int j = 0; j < 8; j++) v[r][j] = 0.0f;
+    if (g < ngrp) {
+      uint4 bv = make_uint4(0, 0, 0, 0);
+      if (st.norm) {
+        if (bb) bv = __ldcg(reinterpret_cast<const uint4*>(bb + 8 * g));
+        gv[0] = *reinterpret_cast<const uint4*>(gm + 8 * g);
+      }
+      float4 p0 = make_float4(0.f, 0.f, 0.f, 0.f), p1 = p0;
+#pragma unroll
+      for (int q4 = 0; q4 < kMaxParts; q4 += kPartsBatch) {  // kPartsBatch parts per round trip
+        if (q4 < st.a_parts) {
+          float4 q0[kPartsBatch], q1[kPartsBatch];
+#pragma unroll
+          for (int q = 0; q < kPartsBatch; q++) {
+            if (q4 + q < st.a_parts) {
+              q0[q] = __ldcg(reinterpret_cast<const float4*>(parts + (size_t)(q4 + q) * k + 8 * g));
+              q1[q] = __ldcg(reinterpret_cast<const float4*>(parts + (size_t)(q4 + q) * k + 8 * g + 4));
+            }
+          }
+#pragma unroll
+          for (int q = 0; q < kPartsBatch; q++) {
+            if (q4 + q == 0) {
+              p0 = q0[0];
+              p1 = q1[0];
+            } else if (q4 + q < st.a_parts) {
+              p0 = make_float4(__fadd_rn(p0.x, q0[q].x), __fadd_rn(p0.y, q0[q].y), __fadd_rn(p0.z, q0[q].z),
+                               __fadd_rn(p0.w, q0[q].w));
+              p1 = make_float4(__fadd_rn(p1.x, q1[q].x), __fadd_rn(p1.y, q1[q].y), __fadd_rn(p1.z, q1[q].z),
+                               __fadd_rn(p1.w, q1[q].w));
+            }
+          }
+        }
+      }
+      const float t8[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+#pragma unroll
+      for (int j = 0; j < 8; j++) v[0][j] = bf16_round(t8[j]);
+      if (st.norm && bb) {
+        float w8[8];
+        unpack8(bv, w8);
+#pragma unroll
+        for (int j = 0; j < 8; j++) v[0][j] = __fadd_rn(v[0][j], w8[j]);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; j++) v[0][j] = 0.0f;
+    }
+  } else {
 #pragma unroll
   for (int r = 0; r < kStageGroups; r++) {
     const int g = stage_grp(tid + r * kConsumers, ngrp, rot);
@@ -462,31 +536,7 @@ __device__ __forceinline__ void stage_x(const SparkStage& st, const Smem& s, int
         if (bb) bv = __ldcg(reinterpret_cast<const uint4*>(bb + 8 * g));  // with the first loads
         gv[r] = *reinterpret_cast<const uint4*>(gm + 8 * g);
       }
-      if (st.pro == SPARK_PRO_PARTS) {
-        // parts in pairs (two in flight per round trip), summed in part order
-        float4 p0 = __ldcg(reinterpret_cast<const float4*>(parts + 8 * g));
-        float4 p1 = __ldcg(reinterpret_cast<const float4*>(parts + 8 * g + 4));
-        for (int q = 1; q < st.a_parts; q += 2) {
-          const float4 q0 = __ldcg(reinterpret_cast<const float4*>(parts + (size_t)q * k + 8 * g));
-          const float4 q1 = __ldcg(reinterpret_cast<const float4*>(parts + (size_t)q * k + 8 * g + 4));
-          float4 n0 = q0, n1 = q1;
-          if (q + 1 < st.a_parts) {
-            n0 = __ldcg(reinterpret_cast<const float4*>(parts + (size_t)(q + 1) * k + 8 * g));
-            n1 = __ldcg(reinterpret_cast<const float4*>(parts + (size_t)(q + 1) * k + 8 * g + 4));
-          }
-          p0 = make_float4(__fadd_rn(p0.x, q0.x), __fadd_rn(p0.y, q0.y), __fadd_rn(p0.z, q0.z), __fadd_rn(p0.w, q0.w));
-          p1 = make_float4(__fadd_rn(p1.x, q1.x), __fadd_rn(p1.y, q1.y), __fadd_rn(p1.z, q1.z), __fadd_rn(p1.w, q1.w));
-          if (q + 1 < st.a_parts) {
-            p0 = make_float4(__fadd_rn(p0.x, n0.x), __fadd_rn(p0.y, n0.y), __fadd_rn(p0.z, n0.z), __fadd_rn(p0.w, n0.w));
-            p1 = make_float4(__fadd_rn(p1.x, n1.x), __fadd_rn(p1.y, n1.y), __fadd_rn(p1.z, n1.z), __fadd_rn(p1.w, n1.w));
-          }
-        }
-        const float t8[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
-#pragma unroll
-        for (int j = 0; j < 8; j++) v[r][j] = bf16_round(t8[j]);
-      } else {
-        unpack8(__ldcg(reinterpret_cast<const uint4*>(arow + 8 * g)), v[r]);
-      }
+      unpack8(__ldcg(reinterpret_cast<const uint4*>(arow + 8 * g)), v[r]);
       if (st.norm && bb) {
         float w8[8];
         unpack8(bv, w8);
@@ -497,6 +547,7 @@ __device__ __forceinline__ void stage_x(const SparkStage& st, const Smem& s, int
 #pragma unroll
       for (int j = 0; j < 8; j++) v[r][j] = 0.0f;
     }
+  }
   }
   if (tr) tr[6] = gtimer();
   if (st.norm) {
@@ -579,49 +630,100 @@ __device__ __forceinline__ unsigned long long ffma2(unsigned long long a, unsign
   return d;
 }
 
-template <int NT>
-__device__ __forceinline__ void gemv_tiles(uint32_t& a_adr, uint32_t& d_adr, uint32_t& b_adr, uint32_t& m_adr,
-                                           unsigned long long& acc) {
+// Integer MMA with the accumulator as input and output (D = A B + D).
+__device__ __forceinline__ void mma_u8s8_acc(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                             uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// A group = 4 consecutive Q4_0 blocks of a 16-row unit (2 tiles).  Its 4 MMAs run as one
+// accumulator chain: MMA j multiplies block j's nibbles by B columns 2j / 2j + 1 = block
+// j's h / l digits (every other column zero: lane L supplies column L / 4 = the entry of
+// block L / 8, masked to MMA L / 8), so at the end lane (g, c) holds block c's two digit
+// sums for rows g and g + 8 -- every lane has a block to scale, not one lane in four.
+// The accumulator input carries each block's -8 sum X + kMagic in its l column (the
+// meta of block c, loaded by lane c), so 256 D_h + D_l = P + kMagic as before.  Per
+// lane: acc = fma(fp32(d) * sx, P, acc) for its block, i.e. chain c of the slice takes
+// blocks c, c + 4, c + 8, ... in ascending order.
+struct GemvLane {
+  uint32_t bmask[4];  // ~0 for MMA L / 8, else 0
+};
+
+// NG groups: all shared-memory loads, then the 4 chain steps of every group (the groups'
+// chains interleaved), then the fma chain in group order
+template <int NG>
+__device__ __forceinline__ void gemv_groups(uint32_t& a_adr, uint32_t& d_adr, uint32_t& b_adr, uint32_t& m_adr,
+                                            const GemvLane& gl, unsigned long long& acc) {
   const uint32_t m = 0x0f0f0f0fu;
-  uint4 A[NT];
-  uint2 Dd[NT], B[2 * NT], Mt[2 * NT];
+  uint4 A[NG][2];
+  uint2 B[NG], Mt[NG];
+  uint32_t Ds[NG];
 #pragma unroll
-  for (int j = 0; j < NT; j++) {
-    lds_u32x4(a_adr + j * kTileBytes, A[j]);
-    lds_u32x2(d_adr + j * kTileBytes, Dd[j]);
+  for (int i = 0; i < NG; i++) {
+    lds_u32x4(a_adr + i * 2 * kTileBytes, A[i][0]);
+    lds_u32x4(a_adr + i * 2 * kTileBytes + kTileBytes, A[i][1]);
+    lds_u32x2(b_adr + i * 256, B[i]);
+    lds_u32x2(m_adr + i * 32, Mt[i]);
+    asm("ld.shared.u32 %0, [%1];" : "=r"(Ds[i]) : "r"(d_adr + i * 2 * kTileBytes));
+  }
+  int D[NG][4];
+#pragma unroll
+  for (int i = 0; i < NG; i++) {
+    D[i][0] = 0;
+    D[i][1] = (int)Mt[i].x;
+    D[i][2] = 0;
+    D[i][3] = (int)Mt[i].x;
   }
 #pragma unroll
-  for (int j = 0; j < 2 * NT; j++) {
-    lds_u32x2(b_adr + j * 64, B[j]);
-    lds_u32x2(m_adr + j * 8, Mt[j]);
-  }
-  int Dm[2 * NT][4];
+  for (int j = 0; j < 4; j++) {
 #pragma unroll
-  for (int j = 0; j < NT; j++) {
-#pragma unroll
-    for (int h = 0; h < 2; h++) {
-      const uint32_t wg = h ? A[j].z : A[j].x, wg8 = h ? A[j].w : A[j].y;
-      mma_u8s8(Dm[2 * j + h], wg & m, wg8 & m, (wg >> 4) & m, (wg8 >> 4) & m, B[2 * j + h].x, B[2 * j + h].y,
-               (int)Mt[2 * j + h].x);
+    for (int i = 0; i < NG; i++) {
+      const uint4& a = A[i][j >> 1];
+      const uint32_t w0 = (j & 1) ? a.z : a.x, w1 = (j & 1) ? a.w : a.y;
+      mma_u8s8_acc(D[i], w0 & m, w1 & m, (w0 >> 4) & m, (w1 >> 4) & m, B[i].x & gl.bmask[j], B[i].y & gl.bmask[j]);
     }
   }
 #pragma unroll
-  for (int j = 0; j < NT; j++) {
-#pragma unroll
-    for (int h = 0; h < 2; h++) {
-      const int* d = Dm[2 * j + h];
-      const uint32_t hv = h ? Dd[j].y : Dd[j].x;
-      const float sx = __uint_as_float(Mt[2 * j + h].y);
-      const unsigned long long sc =
-          fmul2(f2pack(h2f((uint16_t)(hv & 0xffffu)), h2f((uint16_t)(hv >> 16))), f2pack(sx, sx));
-      const unsigned long long pm = f2pack(__int_as_float(d[0] * 256 + d[1]), __int_as_float(d[2] * 256 + d[3]));
-      acc = ffma2(sc, fadd2(pm, f2pack(-kMagicF, -kMagicF)), acc);
-    }
+  for (int i = 0; i < NG; i++) {
+    const float sx = __uint_as_float(Mt[i].y);
+    const unsigned long long sc =
+        fmul2(f2pack(h2f((uint16_t)(Ds[i] & 0xffffu)), h2f((uint16_t)(Ds[i] >> 16))), f2pack(sx, sx));
+    const unsigned long long pm =
+        f2pack(__int_as_float(D[i][0] * 256 + D[i][1]), __int_as_float(D[i][2] * 256 + D[i][3]));
+    acc = ffma2(sc, fadd2(pm, f2pack(-kMagicF, -kMagicF)), acc);
   }
-  a_adr += NT * kTileBytes;
-  d_adr += NT * kTileBytes;
-  b_adr += NT * 128;
-  m_adr += NT * 16;
+  a_adr += NG * 2 * kTileBytes;
+  d_adr += NG * 2 * kTileBytes;
+  b_adr += NG * 256;
+  m_adr += NG * 32;
+}
+
+// the last tile of a slice with an odd tile count: blocks 0 / 1 of a group, two MMAs,
+// lanes c = 0 / 1 extend their chains (lanes 2 / 3 have no block here)
+__device__ __forceinline__ void gemv_half_group(uint32_t a_adr, uint32_t d_adr, uint32_t b_adr, uint32_t m_adr,
+                                                const GemvLane& gl, int c, unsigned long long& acc) {
+  const uint32_t m = 0x0f0f0f0fu;
+  uint4 A;
+  uint2 B, Mt = make_uint2(0u, 0u);
+  uint32_t Ds = 0u;
+  lds_u32x4(a_adr, A);
+  lds_u32x2(b_adr, B);
+  if (c < 2) {
+    lds_u32x2(m_adr, Mt);
+    asm("ld.shared.u32 %0, [%1];" : "=r"(Ds) : "r"(d_adr));
+  }
+  int D[4] = {0, (int)Mt.x, 0, (int)Mt.x};
+  mma_u8s8_acc(D, A.x & m, A.y & m, (A.x >> 4) & m, (A.y >> 4) & m, B.x & gl.bmask[0], B.y & gl.bmask[0]);
+  mma_u8s8_acc(D, A.z & m, A.w & m, (A.z >> 4) & m, (A.w >> 4) & m, B.x & gl.bmask[1], B.y & gl.bmask[1]);
+  if (c < 2) {
+    const float sx = __uint_as_float(Mt.y);
+    const unsigned long long sc =
+        fmul2(f2pack(h2f((uint16_t)(Ds & 0xffffu)), h2f((uint16_t)(Ds >> 16))), f2pack(sx, sx));
+    const unsigned long long pm = f2pack(__int_as_float(D[0] * 256 + D[1]), __int_as_float(D[2] * 256 + D[3]));
+    acc = ffma2(sc, fadd2(pm, f2pack(-kMagicF, -kMagicF)), acc);
+  }
 }
 
 // per-stage GEMV constants (computed once per stage, not per task)
@@ -631,23 +733,41 @@ struct GemvDims {
   uint32_t xm2;            // Q6_K: half-block sums (shared address)
 };
 
+// One (unit, slice) task.  Returns the slice value of rows g / g + 8 in every lane of
+// group g: ((chain 0 + chain 1) + (chain 2 + chain 3)).
 __device__ __forceinline__ void gemv_task(const GemvDims& gd, uint32_t ubase, int kpi, int sl, int lane, float& acc0,
                                           float& acc1) {
-  const int tps = gd.tps;
-  const uint32_t xf = gd.xf, xm = gd.xm;
+  const int tps = gd.tps, g = lane >> 2, c = lane & 3;
   const int t0 = sl * tps;
   const int gb = kpi * gd.kp_blocks + 2 * t0;  // first block of the slice
-  // per-lane addresses: A at lane * 16 of each tile, scales at 512 + (lane / 4) * 8,
-  // B fragment entry lane & 7 of each block, block meta
+  // per-lane addresses: A at lane * 16 of each tile; the scales of block c of the group
+  // (rows g, g + 8) in tile c / 2 at 512 + 8 g + 4 (c % 2); digit entry lane of the group's
+  // 4 blocks (256 B); the meta of block c
   uint32_t a_adr = ubase + (uint32_t)t0 * kTileBytes + lane * 16;
-  uint32_t d_adr = ubase + (uint32_t)t0 * kTileBytes + 512 + (lane >> 2) * 8;
-  uint32_t b_adr = xf + (uint32_t)(gb * 8 + (lane & 7)) * 8;
-  uint32_t m_adr = xm + (uint32_t)gb * 8;
+  uint32_t d_adr = ubase + (uint32_t)(t0 + (c >> 1)) * kTileBytes + 512 + g * 8 + (c & 1) * 4;
+  uint32_t b_adr = gd.xf + (uint32_t)(gb * 8 + lane) * 8;
+  uint32_t m_adr = gd.xm + (uint32_t)(gb + c) * 8;
+  GemvLane gl;
+#pragma unroll
+  for (int j = 0; j < 4; j++) gl.bmask[j] = (lane >> 3) == j ? 0xffffffffu : 0u;
   unsigned long long acc = 0ull;  // (0.0f, 0.0f)
   int n = tps;
-  for (; n >= 4; n -= 4) gemv_tiles<4>(a_adr, d_adr, b_adr, m_adr, acc);
-  for (; n > 0; n--) gemv_tiles<1>(a_adr, d_adr, b_adr, m_adr, acc);
-  f2unpack(acc, acc0, acc1);
+  for (; n >= 8; n -= 8) gemv_groups<4>(a_adr, d_adr, b_adr, m_adr, gl, acc);
+  if (n >= 4) {
+    gemv_groups<2>(a_adr, d_adr, b_adr, m_adr, gl, acc);
+    n -= 4;
+  }
+  if (n >= 2) {
+    gemv_groups<1>(a_adr, d_adr, b_adr, m_adr, gl, acc);
+    n -= 2;
+  }
+  if (n) gemv_half_group(a_adr, d_adr, b_adr, m_adr, gl, c, acc);
+  float e0, e1;
+  f2unpack(acc, e0, e1);
+  e0 = __fadd_rn(e0, __shfl_xor_sync(0xffffffffu, e0, 1));
+  e1 = __fadd_rn(e1, __shfl_xor_sync(0xffffffffu, e1, 1));
+  acc0 = __fadd_rn(e0, __shfl_xor_sync(0xffffffffu, e0, 2));
+  acc1 = __fadd_rn(e1, __shfl_xor_sync(0xffffffffu, e1, 2));
 }
 
 // ------------------------------------------------------------------ Q6_K (T6 units)
@@ -864,32 +984,42 @@ __device__ __forceinline__ void gemv_epilogue(const SparkStage& st, const SparkS
   }
 }
 
+// Wait until ring sequence `seq` has landed.  A parity wait alone cannot tell a slot two
+// phases behind (its previous copy, seq - kDesc, still in flight) from a completed one, and
+// warps move through the ring out of step with each other (attention ranges, GEMV tasks),
+// so the wait first sees the slot's issue tag equal `seq`: the producer issues seq only
+// after seq - kDesc was released, hence landed, and cannot issue seq + kDesc before this
+// warp releases seq.  Both waits are bounded like every other.
 __device__ __forceinline__ bool wait_unit(const Smem& s, uint32_t seq) {
+  const volatile uint32_t* tag = s.desc_seq + seq % kDesc;
+  if (*tag != seq) {
+    unsigned long long t0 = 0;
+    for (uint32_t i = 0; *tag != seq; i++) {
+      if ((i & 255) == 255) {
+        if (*s.abort_flag) return false;
+        const unsigned long long t = gtimer();
+        if (t0 == 0) t0 = t;
+        else if (t - t0 > kWaitNs) return false;
+      }
+    }
+  }
   return mbar_wait_timed(smem_u32(s.full + seq % kDesc), (seq / kDesc) & 1u, s.abort_flag);
 }
 
-// the task that completes a unit releases its ring bytes
-__device__ __forceinline__ void finish_task(const Smem& s, uint32_t seq, int tasks, int lane) {
-  __syncwarp();
-  if (lane == 0) {
-    const uint32_t slot = seq % kDesc;
-    if (atomicAdd(s.done + slot, 1) == tasks - 1) {
-      s.done[slot] = 0;
-      mbar_arrive(smem_u32(s.empty + slot));
-    }
-  }
-}
 
 // Q6: the kernel instantiation that also runs SPARK_STAGE_GEMV_Q6 stages (programs
 // without them use the Q4-only instantiation, whose registers the Q6 code does not touch)
 template <bool Q6, bool Spark>
 __device__ __forceinline__ bool gemv_stage(const StepParams& P, const SparkStage& st, const Smem& s, uint32_t& seq_base, int tid) {
   const int ncta = gridDim.x, cta = blockIdx.x, warp = tid >> 5, lane = tid & 31;
-  int u0;
-  const int nl = local_units(st, cta, ncta, u0);
-  const bool part_x = !st.norm && st.kp > 1 && ncta % st.kp == 0;
+  int u0, ustride;
+  const int nl = local_units(st, cta, ncta, u0, ustride);
+  // the CTA's K part alone is staged when all its units share it (SPARK_PRO_ATTN: staged
+  // already, by the attention stage before)
+  const bool pro_attn = st.pro == SPARK_PRO_ATTN;
+  const bool part_x = pro_attn || (!st.norm && st.kp > 1 && ncta % st.kp == 0);
   const int kx = part_x ? st.k / st.kp : st.k;
-  if (nl > 0 || (cta == 0 && st.res_out))
+  if (!pro_attn && (nl > 0 || (cta == 0 && st.res_out)))
     stage_x<Q6>(st, s, tid,
             (tid == 0 && P.io.trace) ? P.io.trace + ((size_t)cta * P.num_stages + s.flag[2]) * kTraceSlots : nullptr,
             part_x ? (u0 % st.kp) * kx : 0, kx);
@@ -907,14 +1037,25 @@ __device__ __forceinline__ bool gemv_stage(const StepParams& P, const SparkStage
   gd.xf = smem_u32(s.scratch);
   gd.xm = gd.xf + 64 * (kx >> 5);
   gd.xm2 = gd.xf + 72 * (kx >> 5) + 6 * st.k;  // Q6_K half-block sums (stage_x)
+  unsigned long long wsum = 0;  // trace: warp 0's time waiting for ring data (ns)
+  long long csum = 0;           // trace: warp 0's SM cycles inside its GEMV tasks
+  long long psum = 0;           // trace: ... after them (slice sums, epilogue, slot release)
+  const long long cloop = tr ? clock64() : 0ll;
+  int ntask = 0;
   for (int t = warp; t < nl * ks; t += kWarps) {
     const int j = t / ks, sl = t - j * ks;
     const uint32_t seq = seq_base + j;
+    const unsigned long long w0 = tr ? gtimer() : 0ull;
     if (!wait_unit(s, seq)) {  // abort: skip the work, keep the barriers
       raise_abort(P, s, SPARK_ERR_LAUNCH);
       continue;
     }
-    const int u = u0 + j * ncta;
+    if (tr) {
+      wsum += gtimer() - w0;
+      ntask++;
+    }
+    const long long c0 = tr ? clock64() : 0ll;
+    const int u = u0 + j * ustride;
     const uint32_t slot = seq % kDesc;
     float acc0, acc1;
     if (Q6 && st.kind == SPARK_STAGE_GEMV_Q6) {
@@ -923,36 +1064,60 @@ __device__ __forceinline__ bool gemv_stage(const StepParams& P, const SparkStage
     } else {
       gemv_task(gd, smem_u32(s.ring) + s.desc_off[slot], part_x ? 0 : u % gd.kp, sl, lane, acc0, acc1);
     }
-    float* pr = s.partial + slot * kMaxSlices * 16;
-    if ((lane & 3) == 0) {
-      pr[sl * 16 + (lane >> 2)] = acc0;
-      pr[sl * 16 + (lane >> 2) + 8] = acc1;
-    }
-    // the task that completes the unit sums its slices, runs the epilogue and frees the slot
-    __syncwarp();
-    int last = 0;
-    if (lane == 0) {
-      __threadfence_block();
-      last = atomicAdd(s.done + slot, 1) == ks - 1;
-    }
-    if (__shfl_sync(0xffffffffu, last, 0)) {
-      __threadfence_block();
-      if (lane < 8) {
-        float v0 = pr[lane], v1 = pr[lane + 8];
-        for (int q = 1; q < ks; q++) {
-          v0 = __fadd_rn(v0, pr[q * 16 + lane]);
-          v1 = __fadd_rn(v1, pr[q * 16 + lane + 8]);
-        }
-        gemv_epilogue<Spark>(st, P.io, s.misc64, s.rope_cs, u, lane, v0, v1, best);
-      }
+    const long long c1 = tr ? clock64() : 0ll;
+    if (tr) csum += c1 - c0;
+    if (ks == 1) {  // the unit is this task: lane g takes rows g / g + 8 from lane 4 g
+      const float v0 = __shfl_sync(0xffffffffu, acc0, 4 * (lane & 7));
+      const float v1 = __shfl_sync(0xffffffffu, acc1, 4 * (lane & 7));
+      if (lane < 8) gemv_epilogue<Spark>(st, P.io, s.misc64, s.rope_cs, u, lane, v0, v1, best);
       __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(s.empty + slot));
+    } else {
+      float* pr = s.partial + slot * kMaxSlices * 16;
+      if ((lane & 3) == 0) {
+        pr[sl * 16 + (lane >> 2)] = acc0;
+        pr[sl * 16 + (lane >> 2) + 8] = acc1;
+      }
+      // the task that completes the unit sums its slices, runs the epilogue and frees the
+      // slot: the warp's slice sums (ordered by the warp barrier) are released, and the
+      // other slices' acquired, by lane 0's acquire-release count
+      __syncwarp();
+      int last = 0;
       if (lane == 0) {
-        s.done[slot] = 0;
-        mbar_arrive(smem_u32(s.empty + slot));
+        int old;
+        asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], 1;" : "=r"(old) : "r"(smem_u32(s.done + slot))
+                     : "memory");
+        last = old == ks - 1;
+      }
+      last = __shfl_sync(0xffffffffu, last, 0);
+      __syncwarp();
+      if (last) {
+        if (lane < 8) {
+          float v0 = pr[lane], v1 = pr[lane + 8];
+          for (int q = 1; q < ks; q++) {
+            v0 = __fadd_rn(v0, pr[q * 16 + lane]);
+            v1 = __fadd_rn(v1, pr[q * 16 + lane + 8]);
+          }
+          gemv_epilogue<Spark>(st, P.io, s.misc64, s.rope_cs, u, lane, v0, v1, best);
+        }
+        __syncwarp();
+        if (lane == 0) {
+          s.done[slot] = 0;
+          mbar_arrive(smem_u32(s.empty + slot));
+        }
       }
     }
+    if (tr) psum += clock64() - c1;
   }
-  if (tr) tr[5] = gtimer();
+  if (tr) {
+    tr[5] = gtimer();
+    tr[12] = (unsigned long long)psum;
+    tr[13] = (unsigned long long)(clock64() - cloop);
+    tr[8] = (unsigned long long)csum;
+    tr[9] = wsum;
+    tr[11] = (unsigned long long)ntask * (unsigned long long)(Q6 && st.kind == SPARK_STAGE_GEMV_Q6 ? gd.kp_blocks / ks
+                                                                                                  : gd.tps);
+  }
   if (st.epi == SPARK_EPI_ARGMAX) {
 #pragma unroll
     for (int off = 16; off >= 1; off /= 2) {
@@ -980,27 +1145,66 @@ __device__ __forceinline__ bool gemv_stage(const StepParams& P, const SparkStage
 // ------------------------------------------------------------------ consumers: attention
 // Task (kv head g, split j): tokens [t0, t1) of the context pos + 1 (Spark sliding
 // window: of its last `window` positions), T = split_len.  Head dim D = 128 (256 in the
-// Spark instantiation).  Scores: D / 16 lanes per token (lane jj owns dims 8jj..8jj+7,
-// D/2+8jj..D/2+8jj+7; even / odd positions in two fma chains, xor butterfly over the
-// token's lanes); sc[i] = the 4 heads' scores, each warp keeping the running maximum of
-// its tokens.  Warp h < 4 then computes for head h p_i = exp(s_i - m), lane l summing
-// i = l mod 32 in ascending order (butterfly 16..1 gives l), and P_i = bf16(p_i).  PV:
-// 16-token chunk c is summed by warp c % 11 (lane owns dims D/32 lane .. +D/32-1 of the
-// 4 heads); the 11 warp sums are added in warp order.  Each split publishes O / l and
-// lse; once every split of head g has published (the head's counter grows by `splits`
-// each launch), split j combines outputs j, j + S, ... of the head group's 4 x D in the
-// oracle's combine order (Spark: then times the head's output gate).
-constexpr int kMergeRegs = 32;  // splits combined from registers (more: a loop)
+// Spark instantiation).  The split's n tokens are cut into kWarps contiguous ranges of
+// C = roundup(ceil(n / kWarps), TPI) tokens (TPI = 512 / D tokens per warp step); warp w
+// runs a softmax of its own over range w: scores with D / 16 lanes per token (lane jj owns
+// dims 8jj..8jj+7 and D/2+8jj..; even / odd positions in two fma chains, xor butterfly
+// over the token's lanes), m_w = the range's maximum, p = exp(s - m_w) with lane i mod 32
+// of the range summing l_w (butterfly), P = bf16(p), O_w = sum over the range of P V
+// (lane owns D / 32 dims of the 4 heads, tokens ascending).  The CTA merges the ranges in
+// warp order: M = max m_w, f_w = exp(m_w - M), L = L + f_w l_w, O = O + f_w O_w; the
+// split's partial is O / L with lse = log(L) + M.  No CTA barrier separates a warp's
+// scores, softmax and P V.
+//
+// The combine of a kv head's S partials (the oracle's combine order: M = max lse,
+// w_s = exp(lse_s - M) / sum, out = bf16(sum w_s O_s); Spark: times the head's gate) is
+// done by every CTA of the head when the next stage is a SPARK_PRO_ATTN o_proj (its
+// input then stays in shared memory), else by the split that completes the head last
+// (no CTA waits for another).
+// combine: a head group's partials pass through the scratch in rounds of whole splits
+constexpr int kCombineBytes = 36 * 1024;          // partials of one round
+constexpr int kCombineLseOff = kCombineBytes;     // lse [4][S], weights [4][S], maxima [4]
+constexpr int kMaxCombineSplits = (kScratchBytes - kCombineLseOff - 16) / 32;
+constexpr int kXinOff = 32 * 1024;                // combined output (bf16) before the o_proj staging
 
-// One task (kv head g, split j): scores, softmax, P.V and the split's partials.
+__host__ __device__ __forceinline__ int warp_range(int n, int tpi) {
+  const int c = (n + kWarps - 1) / kWarps;
+  return (c + tpi - 1) / tpi * tpi;
+}
+
+// Ring runs seq0 + r0 .. seq0 + r1 (K or V runs of the split [t0, t1) starting at run w0)
+// are done for this warp: lane 0 counts each, and the last of the warps whose range
+// touches a run (range w = [w C, w C + C) of the split) frees its ring bytes.  A run is
+// only freed after it has landed (the run of the decoded token alone is never read from
+// the ring, so the range may not have waited on it).
+__device__ __forceinline__ void release_runs(const Smem& s, uint32_t seq0, int r0, int r1, int64_t t0, int64_t t1,
+                                             int64_t w0, int C, int lane) {
+  if (lane == 0) {
+    for (int r = r0; r <= r1; r++) {
+      if (!wait_unit(s, seq0 + r)) break;  // (abort: the producer no longer issues)
+      const int64_t rs = ((w0 + r) * kRunTokens > t0 ? (w0 + r) * kRunTokens : t0) - t0;
+      const int64_t re = ((w0 + r + 1) * kRunTokens < t1 ? (w0 + r + 1) * kRunTokens : t1) - t0;
+      const int nw = (int)((re - 1) / C - rs / C + 1);
+      const uint32_t slot = (seq0 + r) % kDesc;
+      if (atomicAdd(s.done + slot, 1) == nw - 1) {
+        s.done[slot] = 0;
+        mbar_arrive(smem_u32(s.empty + slot));
+      }
+    }
+  }
+  __syncwarp();
+}
+
+// One task (kv head g, split j): the ranges' softmax and P V, their merge, the split's
+// partials.  false: the split is longer than the scratch holds (launch aborted).
 template <int D, bool Spark>
 __device__ __forceinline__ bool attn_split(const StepParams& P, const SparkStage& st, const Smem& s, uint32_t& seq_base,
                                            int tid, int g, int j) {
   const int warp = tid >> 5, lane = tid & 31;
   const int nq = st.nq, S = st.splits;
   const int64_t pos = s.misc64[0], len = pos + 1;
-  // Spark sliding window: positions [lo, len); the splits start at lo rounded down to 16
-  // (16-token chunks then stay inside the 64-token runs), positions before lo score -inf
+  // Spark sliding window: positions [lo, len); the splits start at lo rounded down to 16,
+  // positions before lo score -inf
   const int64_t lo = Spark && st.window > 0 && len > st.window ? len - st.window : 0;
   const int64_t start = lo & ~(int64_t)15;
   const int T = split_len(len - start, S);
@@ -1016,266 +1220,332 @@ __device__ __forceinline__ bool attn_split(const StepParams& P, const SparkStage
   unsigned long long* tr = (tid == 0 && P.io.trace)
                                ? P.io.trace + ((size_t)blockIdx.x * P.num_stages + s.flag[2]) * kTraceSlots
                                : nullptr;
-  float4* rec = reinterpret_cast<float4*>(s.scratch);                  // [T] scores (fp32 x 4 heads)
-  uint16_t* pbf = reinterpret_cast<uint16_t*>(s.scratch + 16 * T);     // [T][4] bf16 P
+  const float ninf = __int_as_float(0xff800000);
   if (n == 0) {
     for (int o = tid; o < 4 * D; o += kConsumers) part_o[((size_t)j * nq + 4 * g) * D + o] = 0.0f;
-    if (tid < 4) part_lse[(size_t)j * nq + 4 * g + tid] = __int_as_float(0xff800000);
-  } else {
-    const int64_t w0 = t0 / kRunTokens;
-    const int nruns = (int)((t1 - 1) / kRunTokens - w0 + 1);
-    const int nch = (n + 15) >> 4;
-    constexpr int LPT = D / 16, TPI = 32 / LPT;  // lanes per token, tokens per warp step
-    const int jj = lane & (LPT - 1), grp = lane / LPT;
+    if (tid < 4) part_lse[(size_t)j * nq + 4 * g + tid] = ninf;
+    return true;
+  }
+  const int64_t w0 = t0 / kRunTokens;
+  const int nruns = (int)((t1 - 1) / kRunTokens - w0 + 1);
+  constexpr int LPT = D / 16, TPI = 32 / LPT, DL = D / 32;
+  const int jj = lane & (LPT - 1), grp = lane / LPT;
+  const int C = warp_range(n, TPI);
+  const int a = warp * C, b = a + C < n ? a + C : n;  // this warp's range (empty when a >= n)
+  float4* rec = reinterpret_cast<float4*>(s.scratch);             // [T] scores of the 4 heads
+  uint2* pbf = reinterpret_cast<uint2*>(s.scratch + 16 * T);      // [T] bf16 P of the 4 heads
+  float mx[4] = {ninf, ninf, ninf, ninf}, l[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  float acc[4][DL];
+#pragma unroll
+  for (int h = 0; h < 4; h++)
+#pragma unroll
+    for (int d = 0; d < DL; d++) acc[h][d] = 0.0f;
+  bool ok = true;
+  cstamp(tr, 12);
+  if (a < b) {
     float qf[4][16];
     {
       const uint16_t* q = static_cast<const uint16_t*>(st.q) + (size_t)4 * g * D;
 #pragma unroll
       for (int h = 0; h < 4; h++) {
-        float lo[8], hi[8];
-        unpack8(__ldcg(reinterpret_cast<const uint4*>(q + h * D + 8 * jj)), lo);
-        unpack8(__ldcg(reinterpret_cast<const uint4*>(q + h * D + D / 2 + 8 * jj)), hi);
+        float lo8[8], hi8[8];
+        unpack8(__ldcg(reinterpret_cast<const uint4*>(q + h * D + 8 * jj)), lo8);
+        unpack8(__ldcg(reinterpret_cast<const uint4*>(q + h * D + D / 2 + 8 * jj)), hi8);
 #pragma unroll
         for (int m = 0; m < 8; m++) {
-          qf[h][m] = lo[m];
-          qf[h][8 + m] = hi[m];
+          qf[h][m] = lo8[m];
+          qf[h][8 + m] = hi8[m];
         }
       }
     }
-    auto run_of = [&](int64_t ts, int64_t& rs, int64_t& re) {
-      const int64_t r = ts / kRunTokens - w0;
-      rs = (w0 + r) * kRunTokens > t0 ? (w0 + r) * kRunTokens : t0;
-      re = (w0 + r + 1) * kRunTokens < t1 ? (w0 + r + 1) * kRunTokens : t1;
-      return (int)r;
-    };
-    // ---- scores, with each warp's running maximum
-    float mx[4] = {__int_as_float(0xff800000), __int_as_float(0xff800000), __int_as_float(0xff800000),
-                   __int_as_float(0xff800000)};
-    for (int c = warp; c < nch; c += kWarps) {
-      const int64_t ts = t0 + 16 * c;
-      int64_t rs, re;
-      const int r = run_of(ts, rs, re);
-      const uint32_t seq = seq_base + r;
-      if (!wait_unit(s, seq)) {  // abort: skip the work, keep the barriers
-        raise_abort(P, s, SPARK_ERR_LAUNCH);
-        continue;
-      }
-      const unsigned char* rowbase = s.ring + s.desc_off[seq % kDesc] + (ts - rs) * (2 * D);
-#pragma unroll 1
-      for (int step4 = 0; step4 < 16 / TPI; step4++) {
-        const int i = 16 * c + TPI * step4 + grp;
-        const bool valid = i < n && (!Spark || t0 + i >= lo);
-        uint4 k0 = make_uint4(0, 0, 0, 0), k1 = k0;
-        if (valid) {
-          if (t0 + i == pos) {
-            const uint16_t* kr = kv_new + (size_t)g * D;
-            k0 = __ldcg(reinterpret_cast<const uint4*>(kr + 8 * jj));
-            k1 = __ldcg(reinterpret_cast<const uint4*>(kr + D / 2 + 8 * jj));
-          } else {
-            const unsigned char* kr = rowbase + (TPI * step4 + grp) * (2 * D);
-            k0 = *reinterpret_cast<const uint4*>(kr + 16 * jj);
-            k1 = *reinterpret_cast<const uint4*>(kr + D + 16 * jj);
-          }
+    // The token being decoded (pos, the last token of the last split) is peeled off both
+    // loops: its K / V come from kv_new (this launch's qkv stage wrote them; the ring's copy
+    // of its run predates that), so the loops themselves read shared memory only.
+    const bool has_pos = pos >= t0 + a && pos < t0 + b;  // then pos = t0 + b - 1
+    const int bl = has_pos ? b - 1 : b;                  // ring tokens of the range: [a, bl)
+    // ---- scores (a TPI-token step never crosses a 64-token run: t0 and a are multiples of TPI)
+    int waited = -1;
+    const unsigned char* rowbase = nullptr;
+    int64_t rs = 0;
+    auto dot4 = [&](const uint4& k0, const uint4& k1, float (&sc)[4]) {
+      const uint32_t kw[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
+#pragma unroll
+      for (int h = 0; h < 4; h++) {
+        float a0 = 0.0f, a1 = 0.0f;
+#pragma unroll
+        for (int m = 0; m < 8; m++) {
+          a0 = __fmaf_rn(qf[h][2 * m], bf_lo(kw[m]), a0);
+          a1 = __fmaf_rn(qf[h][2 * m + 1], bf_hi(kw[m]), a1);
         }
-        const uint32_t kw[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
-        float sc[4];
+        float v = __fadd_rn(a0, a1);
+        if constexpr (LPT == 16) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 8));
+        v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 4));
+        v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 2));
+        v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 1));
+        sc[h] = __fmul_rn(v, st.scale);
+      }
+    };
+    for (int i0 = a; i0 < bl; i0 += TPI) {
+      const int r = (int)((t0 + i0) / kRunTokens - w0);
+      if (r != waited) {
+        if (!wait_unit(s, seq_base + r)) {
+          ok = false;
+          break;
+        }
+        waited = r;
+        rs = (w0 + r) * kRunTokens > t0 ? (w0 + r) * kRunTokens : t0;
+        rowbase = s.ring + s.desc_off[(seq_base + r) % kDesc];
+      }
+      const int i = i0 + grp;
+      const bool in = i < bl;
+      const bool valid = in && (!Spark || t0 + i >= lo);
+      uint4 k0 = make_uint4(0, 0, 0, 0), k1 = k0;
+      if (in) {
+        const unsigned char* kr = rowbase + (t0 + i - rs) * (2 * D);
+        k0 = *reinterpret_cast<const uint4*>(kr + 16 * jj);
+        k1 = *reinterpret_cast<const uint4*>(kr + D + 16 * jj);
+      }
+      float sc[4];
+      dot4(k0, k1, sc);
+#pragma unroll
+      for (int h = 0; h < 4; h++)
+        if (valid) mx[h] = sc[h] > mx[h] ? sc[h] : mx[h];
+      if (jj == 0 && in) rec[i] = valid ? make_float4(sc[0], sc[1], sc[2], sc[3]) : make_float4(ninf, ninf, ninf, ninf);
+    }
+    if (ok && has_pos) {  // every lane group scores the decoded token; group 0 stores it
+      const uint16_t* kr = kv_new + (size_t)g * D;
+      const uint4 k0 = __ldcg(reinterpret_cast<const uint4*>(kr + 8 * jj));
+      const uint4 k1 = __ldcg(reinterpret_cast<const uint4*>(kr + D / 2 + 8 * jj));
+      float sc[4];
+      dot4(k0, k1, sc);
+#pragma unroll
+      for (int h = 0; h < 4; h++) mx[h] = sc[h] > mx[h] ? sc[h] : mx[h];
+      if (lane == 0) rec[b - 1] = make_float4(sc[0], sc[1], sc[2], sc[3]);
+    }
+    cstamp(tr, 13);
+    const int r0 = (int)((t0 + a) / kRunTokens - w0), r1 = (int)((t0 + b - 1) / kRunTokens - w0);
+    if (ok) release_runs(s, seq_base, r0, r1, t0, t1, w0, C, lane);  // K runs
+    if (ok) {
+      // ---- the range's maximum, p = exp(s - m_w), l_w (lane i mod 32 of the range), P = bf16(p)
+#pragma unroll
+      for (int h = 0; h < 4; h++)
+#pragma unroll
+        for (int off = LPT; off < 32; off <<= 1) {
+          const float o = __shfl_xor_sync(0xffffffffu, mx[h], off);
+          mx[h] = o > mx[h] ? o : mx[h];
+        }
+      __syncwarp();
+      for (int i = a + lane; i < b; i += 32) {
+        const float4 s4 = rec[i];
+        const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
+        float pv[4];
 #pragma unroll
         for (int h = 0; h < 4; h++) {
-          float a0 = 0.0f, a1 = 0.0f;
-#pragma unroll
-          for (int m = 0; m < 8; m++) {
-            a0 = __fmaf_rn(qf[h][2 * m], bf_lo(kw[m]), a0);
-            a1 = __fmaf_rn(qf[h][2 * m + 1], bf_hi(kw[m]), a1);
-          }
-          float v = __fadd_rn(a0, a1);
-          if constexpr (LPT == 16) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 8));
-          v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 4));
-          v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 2));
-          v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 1));
-          sc[h] = __fmul_rn(v, st.scale);
-          if (valid) mx[h] = sc[h] > mx[h] ? sc[h] : mx[h];
+          pv[h] = mx[h] == ninf ? 0.0f : spark_exp_neg(__fsub_rn(sv[h], mx[h]));
+          l[h] = __fadd_rn(l[h], pv[h]);
         }
-        if constexpr (Spark) {
-          const float ni = __int_as_float(0xff800000);
-          if (jj == 0 && i < n) rec[i] = valid ? make_float4(sc[0], sc[1], sc[2], sc[3]) : make_float4(ni, ni, ni, ni);
-        } else {
-          if (valid && jj == 0) rec[i] = make_float4(sc[0], sc[1], sc[2], sc[3]);
-        }
+        pbf[i] = make_uint2(bf16x2(pv[0], pv[1]), bf16x2(pv[2], pv[3]));
       }
-      finish_task(s, seq, (int)((re - rs + 15) >> 4), lane);
-    }
 #pragma unroll
-    for (int h = 0; h < 4; h++) {
-      float v = mx[h];
+      for (int h = 0; h < 4; h++) l[h] = butterfly_sum<32>(l[h]);
+      __syncwarp();
+      cstamp(tr, 14);
+      // ---- P V over the range, tokens ascending: run by run, four tokens per batch (all
+      // shared-memory loads first), then the decoded token from kv_new
+      const uint32_t pbf_u = smem_u32(pbf);
+      auto pv_token = [&](uint2 pw, const float (&v4)[DL]) {
+        const float p4[4] = {bf_lo(pw.x), bf_hi(pw.x), bf_lo(pw.y), bf_hi(pw.y)};
 #pragma unroll
-      for (int off = 16; off >= 1; off /= 2) {
-        const float o = __shfl_xor_sync(0xffffffffu, v, off);
-        v = o > v ? o : v;
-      }
-      if (lane == 0) s.red[warp * 4 + h] = v;
-    }
-    consumer_bar();
-    if (tr) tr[4] = gtimer();
-    float mh[4];
+        for (int h = 0; h < 4; h++)
 #pragma unroll
-    for (int h = 0; h < 4; h++) {
-      float v = s.red[h];
-      for (int w = 1; w < kWarps; w++) v = s.red[w * 4 + h] > v ? s.red[w * 4 + h] : v;
-      mh[h] = v;
-    }
-    // ---- p = exp(s - m), l (32-lane order), P = bf16(p): one warp per head
-    if (warp < 4) {
-      const int h = warp;
-      const float* sf = reinterpret_cast<const float*>(rec);
-      float acc = 0.0f;
-      for (int i = lane; i < n; i += 32) {
-        const float p = spark_exp(__fsub_rn(sf[4 * i + h], mh[h]));
-        acc = __fadd_rn(acc, p);
-        pbf[4 * i + h] = f2bf(p);
-      }
-      acc = butterfly_sum<32>(acc);
-      if (lane == 0) s.red[48 + h] = acc;
-    }
-    consumer_bar();
-    if (tr) tr[5] = gtimer();
-    // ---- PV
-    constexpr int DL = D / 32;  // dims per lane
-    float acc[4][DL];
-#pragma unroll
-    for (int h = 0; h < 4; h++)
-#pragma unroll
-      for (int d = 0; d < DL; d++) acc[h][d] = 0.0f;
-    for (int c = warp; c < nch; c += kWarps) {
-      const int64_t ts = t0 + 16 * c;
-      int64_t rs, re;
-      const int r = run_of(ts, rs, re);
-      const uint32_t seq = seq_base + nruns + r;
-      if (!wait_unit(s, seq)) {  // abort: skip the work, keep the barriers
-        raise_abort(P, s, SPARK_ERR_LAUNCH);
-        continue;
-      }
-      const unsigned char* rowbase = s.ring + s.desc_off[seq % kDesc] + (ts - rs) * (2 * D);
-      const int cnt = n - 16 * c < 16 ? n - 16 * c : 16;
-      for (int tt = 0; tt < cnt; tt++) {
-        const int i = 16 * c + tt;
-        const uint2 pv = *reinterpret_cast<const uint2*>(pbf + 4 * i);
-        const float p4[4] = {bf_lo(pv.x), bf_hi(pv.x), bf_lo(pv.y), bf_hi(pv.y)};
-        float v4[DL];
+          for (int d = 0; d < DL; d++) acc[h][d] = __fmaf_rn(p4[h], v4[d], acc[h][d]);
+      };
+      auto v_load = [&](uint32_t adr, float (&v4)[DL]) {
         if constexpr (D == 128) {
           uint2 vv;
-          if (t0 + i == pos) {
-            vv = __ldcg(reinterpret_cast<const uint2*>(kv_new + ((size_t)st.nkv + g) * D + 4 * lane));
-          } else {
-            vv = *reinterpret_cast<const uint2*>(rowbase + tt * 256 + 8 * lane);
-          }
+          lds_u32x2(adr, vv);
           v4[0] = bf_lo(vv.x);
           v4[1] = bf_hi(vv.x);
           v4[2] = bf_lo(vv.y);
           v4[3] = bf_hi(vv.y);
         } else {
           uint4 vv;
-          if (t0 + i == pos) {
-            vv = __ldcg(reinterpret_cast<const uint4*>(kv_new + ((size_t)st.nkv + g) * D + 8 * lane));
-          } else {
-            vv = *reinterpret_cast<const uint4*>(rowbase + tt * (2 * D) + 16 * lane);
-          }
+          lds_u32x4(adr, vv);
           unpack8(vv, v4);
         }
+      };
+      int i = a;
+      while (ok && i < bl) {
+        const int r = (int)((t0 + i) / kRunTokens - w0);
+        if (!wait_unit(s, seq_base + nruns + r)) {
+          ok = false;
+          break;
+        }
+        const int64_t rs2 = (w0 + r) * kRunTokens > t0 ? (w0 + r) * kRunTokens : t0;
+        const int64_t re2 = (w0 + r + 1) * kRunTokens - t0;
+        const int seg = re2 < (int64_t)bl ? (int)re2 : bl;  // this run's tokens of the range: [i, seg)
+        uint32_t vadr = smem_u32(s.ring) + s.desc_off[(seq_base + nruns + r) % kDesc] +
+                        (uint32_t)(t0 + i - rs2) * (2 * D) + lane * (2 * DL);
+        uint32_t padr = pbf_u + (uint32_t)i * 8;
+        for (; i + 4 <= seg; i += 4) {
+          uint2 pw[4];
+          float v4[4][DL];
 #pragma unroll
-        for (int h = 0; h < 4; h++)
+          for (int q = 0; q < 4; q++) {
+            lds_u32x2(padr + q * 8, pw[q]);
+            v_load(vadr + q * (2 * D), v4[q]);
+          }
 #pragma unroll
-          for (int d = 0; d < DL; d++) acc[h][d] = __fmaf_rn(p4[h], v4[d], acc[h][d]);
+          for (int q = 0; q < 4; q++) pv_token(pw[q], v4[q]);
+          vadr += 4 * (2 * D);
+          padr += 32;
+        }
+        for (; i < seg; i++) {
+          uint2 pw;
+          float v4[DL];
+          lds_u32x2(padr, pw);
+          v_load(vadr, v4);
+          pv_token(pw, v4);
+          vadr += 2 * D;
+          padr += 8;
+        }
       }
-      finish_task(s, seq, (int)((re - rs + 15) >> 4), lane);
+      if (ok && has_pos) {
+        const uint2 pw = pbf[b - 1];
+        float v4[DL];
+        if constexpr (D == 128) {
+          const uint2 vv = __ldcg(reinterpret_cast<const uint2*>(kv_new + ((size_t)st.nkv + g) * D + 4 * lane));
+          v4[0] = bf_lo(vv.x);
+          v4[1] = bf_hi(vv.x);
+          v4[2] = bf_lo(vv.y);
+          v4[3] = bf_hi(vv.y);
+        } else {
+          const uint4 vv = __ldcg(reinterpret_cast<const uint4*>(kv_new + ((size_t)st.nkv + g) * D + 8 * lane));
+          unpack8(vv, v4);
+        }
+        pv_token(pw, v4);
+      }
+      if (ok) release_runs(s, seq_base + nruns, r0, r1, t0, t1, w0, C, lane);  // V runs
+      cstamp(tr, 15);
+    }
+  }
+  if (!ok) raise_abort(P, s, SPARK_ERR_LAUNCH);  // (skip the work, keep the barriers)
+  consumer_bar();  // every warp is done with the scores and P
+  cstamp(tr, 16);
+  if (tr) tr[4] = gtimer();
+  // ---- merge the ranges: O_w [kWarps][4][128] (one 128-dim half at a time), m_w, l_w
+  float* ow = reinterpret_cast<float*>(s.scratch);
+  float* mlw = ow + kWarps * 4 * 128;  // m [kWarps][4], l [kWarps][4]
+  float* fac = mlw + 2 * kWarps * 4;   // f [4][kWarps], L [4], M [4]
+  if (lane == 0) {
+#pragma unroll
+    for (int h = 0; h < 4; h++) {
+      mlw[warp * 4 + h] = mx[h];
+      mlw[kWarps * 4 + warp * 4 + h] = l[h];
+    }
+  }
+#pragma unroll 1
+  for (int ph = 0; ph < D / 128; ph++) {
+    if (D == 128 || (lane >> 4) == ph) {
+#pragma unroll
+      for (int h = 0; h < 4; h++) {
+        float* dst = ow + (warp * 4 + h) * 128 + DL * (D == 128 ? lane : (lane & 15));
+#pragma unroll
+        for (int d = 0; d < DL; d += 4)
+          *reinterpret_cast<float4*>(dst + d) = make_float4(acc[h][d], acc[h][d + 1], acc[h][d + 2], acc[h][d + 3]);
+      }
     }
     consumer_bar();
-    if (tr) tr[6] = gtimer();
-    float* red_o = reinterpret_cast<float*>(s.scratch);
-    if constexpr (D == 128) {
+    if (ph == 0 && warp < 4) {  // warp h: M, the range factors (lane w), L in range order
+      const int h = warp;
+      const float mw = lane < kWarps ? mlw[lane * 4 + h] : ninf;
+      const float lw = lane < kWarps ? mlw[kWarps * 4 + lane * 4 + h] : 0.0f;
+      float M = mw;
 #pragma unroll
-      for (int h = 0; h < 4; h++)
-        *reinterpret_cast<float4*>(red_o + (warp * 4 + h) * D + 4 * lane) =
-            make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
-      consumer_bar();
-      for (int o = tid; o < 4 * D; o += kConsumers) {
-        const int h = o >> 7, d = o & 127;
-        float v = red_o[h * D + d];
-        for (int w = 1; w < kWarps; w++) v = __fadd_rn(v, red_o[(w * 4 + h) * D + d]);
-        part_o[((size_t)j * nq + 4 * g + h) * D + d] = __fdiv_rn(v, s.red[48 + h]);
+      for (int off = 16; off >= 1; off /= 2) {
+        const float o = __shfl_xor_sync(0xffffffffu, M, off);
+        M = o > M ? o : M;
       }
-    } else {  // the warp sums of dims 0..127, then 128..255 (the scratch holds one half)
-#pragma unroll 1
-      for (int ph = 0; ph < 2; ph++) {
-        if ((lane >> 4) == ph) {
+      const float f = (mw == ninf || M == ninf) ? 0.0f : spark_exp_neg(__fsub_rn(mw, M));
+      if (lane < kWarps) fac[h * kWarps + lane] = f;
+      const float fl = __fmul_rn(f, lw);
+      float fls[kWarps];
 #pragma unroll
-          for (int h = 0; h < 4; h++) {
-            float* dst = red_o + (warp * 4 + h) * 128 + 8 * (lane & 15);
-            *reinterpret_cast<float4*>(dst) = make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
-            *reinterpret_cast<float4*>(dst + 4) = make_float4(acc[h][4], acc[h][5], acc[h][6], acc[h][7]);
-          }
-        }
-        consumer_bar();
-        for (int o = tid; o < 4 * 128; o += kConsumers) {
-          const int h = o >> 7, d = o & 127;
-          float v = red_o[h * 128 + d];
-          for (int w = 1; w < kWarps; w++) v = __fadd_rn(v, red_o[(w * 4 + h) * 128 + d]);
-          part_o[((size_t)j * nq + 4 * g + h) * D + 128 * ph + d] = __fdiv_rn(v, s.red[48 + h]);
-        }
-        if (ph == 0) consumer_bar();  // the first half's reads before the second half's writes
+      for (int w = 0; w < kWarps; w++) fls[w] = __shfl_sync(0xffffffffu, fl, w);
+      float L = 0.0f;
+#pragma unroll
+      for (int w = 0; w < kWarps; w++) L = __fadd_rn(L, fls[w]);
+      if (lane == 0) {
+        fac[4 * kWarps + h] = L;
+        fac[4 * kWarps + 4 + h] = M;
       }
     }
-    if (tid < 4) part_lse[(size_t)j * nq + 4 * g + tid] = __fadd_rn(spark_log(s.red[48 + tid]), mh[tid]);
-    seq_base += 2 * nruns;
+    if (ph == 0) consumer_bar();
+    if (ph == 0) cstamp(tr, 17);
+    for (int o = tid; o < 4 * 128; o += kConsumers) {
+      const int h = o >> 7, d = o & 127;
+      float v = 0.0f;
+      if (fac[4 * kWarps + 4 + h] != ninf) {
+        float O = 0.0f;
+        for (int w = 0; w < kWarps; w++) O = __fadd_rn(O, __fmul_rn(fac[h * kWarps + w], ow[(w * 4 + h) * 128 + d]));
+        v = __fdiv_rn(O, fac[4 * kWarps + h]);
+      }
+      part_o[((size_t)j * nq + 4 * g + h) * D + 128 * ph + d] = v;
+    }
+    if (ph + 1 < D / 128) consumer_bar();  // the first half's reads before the second half's writes
   }
+  if (tid < 4) {
+    const float M = fac[4 * kWarps + 4 + tid];
+    part_lse[(size_t)j * nq + 4 * g + tid] = M == ninf ? ninf : __fadd_rn(spark_log(fac[4 * kWarps + tid]), M);
+  }
+  if (tr) tr[5] = gtimer();
+  seq_base += 2 * nruns;
   return true;
 }
 
-// The combine share of task (g, j), once every split of kv head g has published.
-template <int D, bool Spark>
-__device__ __forceinline__ void attn_combine(const StepParams& P, const SparkStage& st, const Smem& s, int tid, int g,
-                                             int j) {
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// All 4 x D combined outputs of kv head g from its S published partials (the oracle's
+// combine order).  The partials come into the scratch with 16-byte asynchronous copies,
+// kCombineBytes / (16 D) splits per round, while the lse values load; each thread then
+// accumulates its outputs over the splits in ascending order.  ToSmem: the outputs become
+// the staged (fixed-point digit) input of the following SPARK_PRO_ATTN o_proj stage; else
+// they go to attn_out.
+template <int D, bool Spark, bool ToSmem>
+__device__ __forceinline__ void attn_combine_all(const SparkStage& st, const Smem& s, int tid, int g,
+                                                 unsigned long long* tr) {
   const int warp = tid >> 5, lane = tid & 31;
+  cstamp(tr, 18);
   const int nq = st.nq, S = st.splits;
-  float* part_o = st.part_o;
-  float* part_lse = st.part_lse;
-  unsigned long long* tr = (tid == 0 && P.io.trace)
-                               ? P.io.trace + ((size_t)blockIdx.x * P.num_stages + s.flag[2]) * kTraceSlots
-                               : nullptr;
-  if (tid == 0) {
-    const int target = S * (int)(s.misc64[2] + 1);
-    const unsigned long long tw = gtimer();
-    int ok = 1;
-    while (ld_acquire(st.head_counters + g) < target) {
-      if (*s.abort_flag || gtimer() - tw > kWaitNs) {
-        ok = 0;
-        break;
-      }
-    }
-    if (!ok) raise_abort(P, s, SPARK_ERR_LAUNCH);
-    if (tr) tr[7] = gtimer();
-  }
-  consumer_bar();
-  // combine: lse of the 4 heads x S splits into shared memory (one L2 round trip, with
-  // this thread's part_o values), per-head max and weights w_s / den in parallel, then
-  // outputs j, j + S, ... sum w_s * O_s in split order
+  constexpr int NO = (4 * D + kConsumers - 1) / kConsumers;  // outputs per thread
+  constexpr int PER = kCombineBytes / (16 * D);              // splits per round
+  constexpr int CH = D;                                      // 16-byte chunks per split (4 D floats)
   const float ninf = __int_as_float(0xff800000);
-  float* lse_s = reinterpret_cast<float*>(s.scratch);  // [4][S]
-  float* w_s = lse_s + 4 * S;                          // [4][S]
-  float* den_s = w_s + 4 * S;                          // [4] max, [4] den
-  const int nout = (4 * D - j + S - 1) / S;            // outputs j, j + S, ...
-  const int o = j + tid * S;
-  const int oh = o / D, od = o - oh * D;
-  float ov[kMergeRegs];
-  if (tid < nout && (S <= kMergeRegs || Spark)) {  // (Spark: the first kMergeRegs splits)
-    const float* po_h = part_o + (size_t)(4 * g + oh) * D + od;
-#pragma unroll
-    for (int sp = 0; sp < kMergeRegs; sp++) ov[sp] = sp < S ? __ldcg(po_h + (size_t)sp * nq * D) : 0.0f;
-  }
+  const float* part_o = st.part_o;
+  const float* part_lse = st.part_lse;
+  const float* pc = reinterpret_cast<const float*>(s.scratch);             // [PER][4 D]
+  float* lse_s = reinterpret_cast<float*>(s.scratch + kCombineLseOff);      // [4][S]
+  float* w_s = lse_s + 4 * S;                                               // [4][S]
+  float* mx_s = w_s + 4 * S;                                                // [4]
+  const uint32_t pc_u = smem_u32(s.scratch);
+  auto fetch = [&](int s0) {  // splits s0 .. s0 + PER - 1 into the round buffer
+    const int ns = S - s0 < PER ? S - s0 : PER;
+    for (int c = tid; c < ns * CH; c += kConsumers) {
+      const int sp = c / CH, q = c - sp * CH;
+      cp_async16(pc_u + (uint32_t)(sp * CH + q) * 16, part_o + ((size_t)(s0 + sp) * nq + 4 * g) * D + 4 * q);
+    }
+  };
+  fetch(0);
   for (int i = tid; i < 4 * S; i += kConsumers) {
     const int h = i / S, sp = i - h * S;
     lse_s[i] = __ldcg(part_lse + (size_t)sp * nq + 4 * g + h);
   }
+  cp_async_wait_all();
   consumer_bar();
+  cstamp(tr, 19);
   if (warp < 4) {  // warp h: max, exp, the sequential denominator and w / den of head h
     const int h = warp;
     float m = ninf;
@@ -1287,83 +1557,149 @@ __device__ __forceinline__ void attn_combine(const StepParams& P, const SparkSta
     }
     for (int sp = lane; sp < S; sp += 32) {
       const float v = lse_s[h * S + sp];
-      w_s[h * S + sp] = v == ninf ? 0.0f : spark_exp(__fsub_rn(v, m));
+      w_s[h * S + sp] = v == ninf ? 0.0f : spark_exp_neg(__fsub_rn(v, m));
     }
     __syncwarp();
+    // den = sum of w_s in split order: batches of 8 loads ahead of the ordered adds
     float den = 0.0f;
-    if (lane == 0)
-      for (int sp = 0; sp < S; sp++) den = __fadd_rn(den, w_s[h * S + sp]);
-    den = __shfl_sync(0xffffffffu, den, 0);
+    for (int s0 = 0; s0 < S; s0 += 8) {
+      float w8[8];
+#pragma unroll
+      for (int q = 0; q < 8; q++) w8[q] = s0 + q < S ? w_s[h * S + s0 + q] : 0.0f;
+#pragma unroll
+      for (int q = 0; q < 8; q++)
+        if (s0 + q < S) den = __fadd_rn(den, w8[q]);
+    }
+    __syncwarp();
     for (int sp = lane; sp < S; sp += 32) w_s[h * S + sp] = __fdiv_rn(w_s[h * S + sp], den);
-    if (lane == 0) den_s[h] = m;
+    if (lane == 0) mx_s[h] = m;
   }
   consumer_bar();
-  if (tid < nout) {
-    const int h = oh, d = od;
-    float a = 0.0f;
-    if (den_s[h] != ninf) {
-      if (S <= kMergeRegs) {
+  cstamp(tr, 20);
+  float a[NO];
 #pragma unroll
-        for (int sp = 0; sp < kMergeRegs; sp++)
-          if (sp < S && lse_s[h * S + sp] != ninf) a = __fadd_rn(a, __fmul_rn(w_s[h * S + sp], ov[sp]));
-      } else if constexpr (Spark) {  // splits 0..31 from the registers, then batches of 16 loads
-#pragma unroll
-        for (int sp = 0; sp < kMergeRegs; sp++)
-          if (lse_s[h * S + sp] != ninf) a = __fadd_rn(a, __fmul_rn(w_s[h * S + sp], ov[sp]));
-        const float* po_h = part_o + (size_t)(4 * g + h) * D + d;
+  for (int k = 0; k < NO; k++) a[k] = 0.0f;
 #pragma unroll 1
-        for (int s0 = kMergeRegs; s0 < S; s0 += 16) {
-          float c[16];
+  for (int s0 = 0; s0 < S; s0 += PER) {
+    if (s0 > 0) {  // the next round's partials (the previous round's reads are done)
+      consumer_bar();
+      fetch(s0);
+      cp_async_wait_all();
+      consumer_bar();
+    }
+    const int ns = S - s0 < PER ? S - s0 : PER;
 #pragma unroll
-          for (int b = 0; b < 16; b++) c[b] = s0 + b < S ? __ldcg(po_h + (size_t)(s0 + b) * nq * D) : 0.0f;
+    for (int k = 0; k < NO; k++) {
+      const int o = tid + k * kConsumers;
+      if (o < 4 * D) {
+        const int h = o / D;
+        for (int b0 = 0; b0 < ns; b0 += 6) {  // 6 splits' loads ahead of their ordered adds
+          float wv[6], pv[6];
+          bool live[6];
 #pragma unroll
-          for (int b = 0; b < 16; b++)
-            if (s0 + b < S && lse_s[h * S + s0 + b] != ninf) a = __fadd_rn(a, __fmul_rn(w_s[h * S + s0 + b], c[b]));
+          for (int q = 0; q < 6; q++) {
+            const int sp = b0 + q;
+            live[q] = sp < ns && lse_s[h * S + s0 + sp] != ninf;
+            wv[q] = sp < ns ? w_s[h * S + s0 + sp] : 0.0f;
+            pv[q] = sp < ns ? pc[sp * 4 * D + o] : 0.0f;
+          }
+#pragma unroll
+          for (int q = 0; q < 6; q++)
+            if (live[q]) a[k] = __fadd_rn(a[k], __fmul_rn(wv[q], pv[q]));
         }
-      } else {
-        const float* po_h = part_o + (size_t)(4 * g + h) * D + d;
-        for (int sp = 0; sp < S; sp++)
-          if (lse_s[h * S + sp] != ninf) a = __fadd_rn(a, __fmul_rn(w_s[h * S + sp], __ldcg(po_h + (size_t)sp * nq * D)));
       }
     }
-    uint16_t ob = f2bf(a);
-    if constexpr (Spark) {
-      if (st.gate)  // headwise output gate (written by the qkv stage)
-        ob = f2bf(__fmul_rn(bf2f(ob), bf2f(__ldcg(static_cast<const unsigned short*>(st.gate) + 4 * g + h))));
-    }
-    static_cast<uint16_t*>(st.attn_out)[(size_t)(4 * g + h) * D + d] = ob;
   }
+  cstamp(tr, 21);
+  if constexpr (ToSmem) consumer_bar();  // the last round's reads before xin overwrites the round buffer
+  uint16_t* xin = reinterpret_cast<uint16_t*>(s.scratch + kXinOff);  // [4 D]
+#pragma unroll
+  for (int k = 0; k < NO; k++) {
+    const int o = tid + k * kConsumers;
+    if (o < 4 * D) {
+      const int h = o / D;
+      uint16_t ob = f2bf(mx_s[h] != ninf ? a[k] : 0.0f);
+      if constexpr (Spark) {
+        if (st.gate)  // headwise output gate (written by the qkv stage)
+          ob = f2bf(__fmul_rn(bf2f(ob), bf2f(__ldcg(static_cast<const unsigned short*>(st.gate) + 4 * g + h))));
+      }
+      if constexpr (ToSmem) {
+        xin[o] = ob;
+      } else {
+        static_cast<uint16_t*>(st.attn_out)[(size_t)4 * g * D + o] = ob;
+      }
+    }
+  }
+  if constexpr (ToSmem) {  // stage the 4 D values as the o_proj K part's fixed-point digits
+    consumer_bar();
+    constexpr int NG = 4 * D / 8;  // 8-element groups: threads 0 .. NG - 1 (whole warps)
+    if (tid < NG) {
+      float v[8];
+      unpack8(*reinterpret_cast<const uint4*>(xin + 8 * tid), v);
+      stage_group(v, true, tid, reinterpret_cast<uint32_t*>(s.scratch),
+                  reinterpret_cast<int2*>(s.scratch + 64 * (4 * D / 32)));
+    }
+  }
+  cstamp(tr, 22);
+}
+
+// Waits (bounded) until all S splits of kv head g have published in this launch.
+__device__ __forceinline__ bool attn_wait_head(const StepParams& P, const SparkStage& st, const Smem& s, int g) {
+  const int target = st.splits * (int)(s.misc64[2] + 1);
+  const unsigned long long tw = gtimer();
+  while (ld_acquire(st.head_counters + g) < target)
+    if (*s.abort_flag || gtimer() - tw > kWaitNs) return false;
+  return true;
 }
 
 // Tasks (kv head g, split j) = t / S, t % S go round-robin to the CTAs (t = cta, cta +
-// CTAs, ...): each CTA runs its tasks' splits, publishing each on the head's counter,
-// then combines its tasks' shares (every task is published before any CTA waits, so
-// several tasks per CTA -- contexts longer than CTAs / kv heads splits hold -- cannot
-// deadlock).  !Multi: at most one task per CTA, in a form with no loop state (the
-// usual program; a loop here costs the GEMV stages registers in the same kernel).
+// CTAs, ...).  Fused (the next stage is a SPARK_PRO_ATTN o_proj; one task per CTA): each
+// CTA publishes its split, waits for the head's other splits and combines the whole head
+// into shared memory.  Otherwise each split counts itself on the head's counter with an
+// acquire-release add and the one that completes the head combines it into attn_out,
+// so no CTA waits for another (several tasks per CTA cannot deadlock).  !Multi: at most
+// one task per CTA, in a form with no loop state (the usual program; a loop here costs
+// the GEMV stages registers in the same kernel).
 template <int D, bool Multi, bool Spark>
 __device__ __forceinline__ bool attn_stage_d(const StepParams& P, const SparkStage& st, const Smem& s,
-                                          uint32_t& seq_base, int tid) {
+                                          uint32_t& seq_base, int tid, bool fused) {
   const int S = st.splits, ntask = st.nkv * S;
+  unsigned long long* tr = (tid == 0 && P.io.trace)
+                               ? P.io.trace + ((size_t)blockIdx.x * P.num_stages + s.flag[2]) * kTraceSlots
+                               : nullptr;
+  auto finish = [&](int g) {
+    consumer_bar();  // the split's partials (all threads) before its count
+    if (fused) {
+      if (tid == 0) {
+        asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(st.head_counters + g) : "memory");
+        if (!attn_wait_head(P, st, s, g)) raise_abort(P, s, SPARK_ERR_LAUNCH);
+        if (tr) tr[6] = gtimer();
+      }
+      consumer_bar();
+      attn_combine_all<D, Spark, true>(st, s, tid, g, tr);
+    } else {
+      if (tid == 0) {
+        int old;
+        asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(old) : "l"(st.head_counters + g) : "memory");
+        s.flag[3] = old == st.splits * (int)(s.misc64[2] + 1) - 1;
+        if (tr) tr[6] = gtimer();
+      }
+      consumer_bar();
+      if (s.flag[3]) attn_combine_all<D, Spark, false>(st, s, tid, g, tr);
+    }
+    if (tr) tr[7] = gtimer();
+  };
   if constexpr (!Multi) {
     if ((int)blockIdx.x >= ntask) return true;
     const int g = blockIdx.x / S, j = blockIdx.x - g * S;
     if (!attn_split<D, Spark>(P, st, s, seq_base, tid, g, j)) return false;
-    consumer_bar();
-    if (tid == 0) asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(st.head_counters + g) : "memory");
-    attn_combine<D, Spark>(P, st, s, tid, g, j);
+    finish(g);
   } else {
 #pragma unroll 1
     for (int t = blockIdx.x; t < ntask; t += gridDim.x) {
       if (!attn_split<D, Spark>(P, st, s, seq_base, tid, t / S, t - (t / S) * S)) return false;
-      consumer_bar();  // the split's partials (all threads) before its count
-      if (tid == 0)
-        asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(st.head_counters + t / S) : "memory");
-    }
-#pragma unroll 1
-    for (int t = blockIdx.x; t < ntask; t += gridDim.x) {
-      attn_combine<D, Spark>(P, st, s, tid, t / S, t - (t / S) * S);
-      if (t + (int)gridDim.x < ntask) consumer_bar();  // its shared memory before the next task's
+      finish(t / S);
+      if (t + (int)gridDim.x < ntask) consumer_bar();  // this task's shared memory before the next task's
     }
   }
   return true;
@@ -1373,11 +1709,11 @@ __device__ __forceinline__ bool attn_stage_d(const StepParams& P, const SparkSta
 // attention body per kernel keeps its registers)
 template <bool Multi, bool Spark>
 __device__ __forceinline__ bool attn_stage(const StepParams& P, const SparkStage& st, const Smem& s, uint32_t& seq_base,
-                                        int tid) {
+                                        int tid, bool fused) {
   if constexpr (Spark) {
-    return attn_stage_d<256, Multi, true>(P, st, s, seq_base, tid);
+    return attn_stage_d<256, Multi, true>(P, st, s, seq_base, tid, fused);
   } else {
-    return attn_stage_d<128, Multi, false>(P, st, s, seq_base, tid);
+    return attn_stage_d<128, Multi, false>(P, st, s, seq_base, tid, fused);
   }
 }
 
@@ -1412,6 +1748,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepParams P) {
       mbar_init(smem_u32(s.full + i), 1);
       mbar_init(smem_u32(s.empty + i), 1);
       s.done[i] = 0;
+      s.desc_seq[i] = 0xffffffffu;  // no copy issued yet
     }
     *s.abort_flag = 0;
     s.misc64[2] = P.io.counters[P.num_stages + 2];  // launch generation (attention head counters)
@@ -1487,14 +1824,17 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepParams P) {
     if (s.flag[1]) return;  // uniform: every consumer reads the same flag
     if (tid == 0 && tr) tr[1] = gtimer();
     const SparkStage& st = *s.stage;
+    // an attention stage followed by a SPARK_PRO_ATTN o_proj combines into shared memory
+    // and is waited on by no stage (the host checks): it is not counted
+    const bool fused = st.kind == SPARK_STAGE_ATTN && i + 1 < P.num_stages && stage_at(P, i + 1).pro == SPARK_PRO_ATTN;
     // both stage functions keep every consumer on the same barriers; a stage that
     // fails returns false in all threads (attention: a split longer than the scratch)
     const bool ok = st.kind != SPARK_STAGE_ATTN ? gemv_stage<Q6, Spark>(P, st, s, seq_base, tid)
-                                                : attn_stage<Multi, Spark>(P, st, s, seq_base, tid);
+                                                : attn_stage<Multi, Spark>(P, st, s, seq_base, tid, fused);
     consumer_bar();
     if (!ok) return;
     if (tid == 0 && tr) tr[2] = gtimer();
-    if (tid == 0 && !*s.abort_flag) {  // release: the CTA's writes (ordered by the barrier) before the count
+    if (tid == 0 && !*s.abort_flag && !fused) {  // release: the CTA's writes (ordered by the barrier) before the count
       if (st.xchg) {  // writes to every rank's window, then a count on every rank
         asm volatile("fence.acq_rel.sys;" ::: "memory");
         for (int p = 0; p < P.io.tp_size; p++)

@@ -278,7 +278,8 @@ class DecodeEngine:
             raise ValueError(f"{self.splits} splits give {self.max_split_tokens}-token splits (limit "
                              f"{S.MAX_SPLIT_TOKENS}); max_seq_len too large for the persistent step")
         tp = self.tp_size
-        order = S.default_order(cfg, self.ncta, tp)
+        order = S.default_order(cfg, self.ncta, tp, self.splits)
+        fused = order["fused_o"]
         self.step_order = order
         ks_qkv, ks_o, ks_gu, ks_down, ks_head = order["ks"]
         kp_o, kp_down = order["kp_local"]
@@ -332,8 +333,12 @@ class DecodeEngine:
                                  scale=cfg.attn_scale, part_o=self.part_o, part_lse=self.part_lse,
                                  head_counters=self.head_ctr[li], attn_out=self.attn_out, nq=nq, nkv=nkv, head_dim=D,
                                  block_size=bs, wait=qkv, window=cfg.layer_window(li), gate=self.gate)
-            o = prog.gemv(wo, h, nq * D, kp=kp_o, ks=ks_o, a=self.attn_out, epi=S.EPI_PARTS, out=self.o_parts,
-                          wait=att, xchg=xchg)
+            if fused:  # o_proj behind the attention, K part = kv head, input in shared memory
+                o = prog.gemv(wo, h, nq * D, kp=kp_o, ks=ks_o, epi=S.EPI_PARTS, out=self.o_parts, wait=-1,
+                              xchg=xchg, attn_splits=self.splits)
+            else:
+                o = prog.gemv(wo, h, nq * D, kp=kp_o, ks=ks_o, a=self.attn_out, epi=S.EPI_PARTS, out=self.o_parts,
+                              wait=att, xchg=xchg)
             gu = prog.gemv(wgu, 2 * i, h, ks=ks_gu, a=self.o_parts, a_parts=pa_o, b=self.res_attn,
                            gamma=lw.post_norm, eps=eps, res_out=self.resmid,
                            epi=S.EPI_GELU_MUL if self.gelu is not None else S.EPI_SILU_MUL,

@@ -22,7 +22,7 @@ import torch
 from ._lib import SparkStage, SparkStepIO, call, lib
 
 STAGE_GEMV, STAGE_ATTN, STAGE_GEMV_Q6 = 0, 1, 2
-PRO_BF16, PRO_PARTS = 0, 1
+PRO_BF16, PRO_PARTS, PRO_ATTN = 0, 1, 2
 EPI_BF16, EPI_PARTS, EPI_ROPE_KV, EPI_SILU_MUL, EPI_ARGMAX, EPI_GELU_MUL = range(6)
 ROWS_PLAIN, ROWS_PAIR_HALF, ROWS_GATE_UP = range(3)
 
@@ -30,6 +30,8 @@ MAX_SLICES = 4  # slices per GEMV unit the kernel supports
 MAX_PARTS = 8  # fp32 parts a PARTS prologue sums (K parts x tensor-parallel ranks)
 CHUNK_ACCS = 11  # consumer warps of the kernel = attention PV chunk accumulators
 MAX_SPLIT_TOKENS = 1344
+MAX_SPLITS = 127  # splits per kv head the attention stage's combine holds (kMaxCombineSplits)
+TRACE_SLOTS = 24  # trace stamps per CTA and stage (kTraceSlots of the kernel)
 
 
 def _p(t):
@@ -115,17 +117,20 @@ class StepProgram:
              embed=None, token=None, b=None, gamma=None, eps: float = 0.0, res_out=None, epi: int = EPI_BF16,
              rowmap: int = ROWS_PLAIN, out=None, wait: int = -1, head_dim: int = 0, key=None, rope=None,
              xchg: bool = False, row0: int = 0, q6: bool = False, rotary_dim: int = 0, gate=None,
-             table=None) -> int:
+             table=None, attn_splits: int = 0) -> int:
         """``xchg``: tensor-parallel exchange stage (parts / argmax key written to every
         rank's window, completion counted on every rank); ``row0``: global index of row 0
         for the argmax (vocab shard start); ``q6``: ``w`` holds Q6_K weights in the T6 layout
         (``q6k_pack_t6``); slices then count 32-weight tiles.  Spark layer features:
         ``rotary_dim`` (partial RoPE) and ``gate`` (bf16 [nq], computed from the gate rows
         after the heads) for ``EPI_ROPE_KV``; ``table`` (``gelu_table()``) for
-        ``EPI_GELU_MUL``."""
+        ``EPI_GELU_MUL``.  ``attn_splits`` > 0: an o_proj fused behind the attention stage
+        added just before (``PRO_ATTN``: kp = its kv heads, input staged by it in shared
+        memory, units assigned by head group; ``wait`` must be -1)."""
         s = SparkStage()
         s.kind, s.epi, s.rowmap = (STAGE_GEMV_Q6 if q6 else STAGE_GEMV), epi, rowmap
-        s.pro = PRO_PARTS if a_parts else PRO_BF16
+        s.pro = PRO_ATTN if attn_splits else (PRO_PARTS if a_parts else PRO_BF16)
+        s.splits = attn_splits
         s.n, s.k, s.kp, s.ks = n, k, kp, ks
         s.units = n // 16 * kp
         s.rot = self._units % self.ncta
@@ -202,8 +207,8 @@ class StepProgram:
         return io
 
     def trace_buffer(self) -> torch.Tensor:
-        """uint64 [ctas, stages, 8] for ``io(trace=...)``."""
-        return torch.zeros((self.ncta, len(self.stages), 8), dtype=torch.int64, device=self.device)
+        """uint64 [ctas, stages, TRACE_SLOTS] for ``io(trace=...)``."""
+        return torch.zeros((self.ncta, len(self.stages), TRACE_SLOTS), dtype=torch.int64, device=self.device)
 
     def launch(self, io: SparkStepIO, stream=None) -> None:
         if self.host is None:
@@ -240,25 +245,35 @@ def _pick_kp(k: int, choices, tp: int) -> int:
     raise ValueError(f"no K part count fits k={k} at tp={tp}")
 
 
-def default_order(cfg, ncta: int, tp: int = 1) -> dict:
+def fuse_o_proj(cfg, ncta: int, splits: int) -> bool:
+    """o_proj runs fused behind the attention stage (``PRO_ATTN``) when every (kv head,
+    split) task has a CTA of its own and the heads are 128-dim (the 4B architecture)."""
+    return splits > 0 and cfg.num_kv_heads * splits <= ncta and cfg.head_dim == 128 and not cfg.spark_features
+
+
+def default_order(cfg, ncta: int, tp: int = 1, splits: int = 0) -> dict:
     """Slice / part counts of the decode program (the oracle's persistent-step order).
 
     ``cfg`` is the rank's local config (heads, intermediate size and vocab divided by
-    ``tp``).  "kp_local" are the K parts of o_proj / down on one rank; "kp" the parts of
-    the whole model (tp x kp_local: rank r's parts follow rank r - 1's), which is the
-    order the oracle restates."""
+    ``tp``); ``splits`` its attention splits per kv head (0: unknown, no fusion).
+    "kp_local" are the K parts of o_proj / down on one rank; "kp" the parts of the whole
+    model (tp x kp_local: rank r's parts follow rank r - 1's), which is the order the
+    oracle restates.  A fused o_proj (``fuse_o_proj``) is cut into one K part per kv head,
+    one slice per unit."""
     h, i, nq, D, v = cfg.hidden_size, cfg.intermediate_size, cfg.num_q_heads, cfg.head_dim, cfg.vocab_size
-    kp_o = _pick_kp(nq * D, (2, 1), tp)
+    fused = fuse_o_proj(cfg, ncta, splits)
+    kp_o = cfg.num_kv_heads if fused else _pick_kp(nq * D, (2, 1), tp)
     kp_down = _pick_kp(i, (4, 2, 1), tp)
     qkv_n = (nq + 2 * cfg.num_kv_heads) * D
     return {
-        # 2 slices per unit everywhere: measured on the 36-layer step, 2 beats 4 (per-task
+        # 2 slices per unit elsewhere: measured on the 36-layer step, 2 beats 4 (per-task
         # overhead) and 1 (a warp per unit: 11 units in use at once overflow the ring)
-        "ks": (pick_ks(qkv_n, h, 1, 2, ncta), pick_ks(h, nq * D, kp_o, 2, ncta), pick_ks(2 * i, h, 1, 2, ncta),
-               pick_ks(h, i, kp_down, 2, ncta), pick_ks(v, h, 1, 2, ncta)),
+        "ks": (pick_ks(qkv_n, h, 1, 2, ncta), 1 if fused else pick_ks(h, nq * D, kp_o, 2, ncta),
+               pick_ks(2 * i, h, 1, 2, ncta), pick_ks(h, i, kp_down, 2, ncta), pick_ks(v, h, 1, 2, ncta)),
         "kp": (tp * kp_o, tp * kp_down),
         "kp_local": (kp_o, kp_down),
         "chunk_accs": CHUNK_ACCS,
+        "fused_o": fused,
     }
 
 
@@ -275,12 +290,15 @@ def splits_for(nkv: int, ncta: int, max_seq_len: int = 0, head_dim: int = 128) -
     whole rounds of tasks over the CTAs (8 kv heads: 37 = 296 tasks = two per CTA, ...)
     so no CTA runs a round more than the others."""
     need = max(1, -(-max_seq_len // MAX_SPLIT_TOKENS))
-    one_round = max(1, ncta // nkv)
+    one_round = max(1, min(ncta // nkv, MAX_SPLITS))
     short = one_round if head_dim <= 128 else min(one_round, SHORT_SPLITS_256)
     if need <= short:
         return short
     rounds = max(1, -(-need * nkv // ncta))
-    return max(need, rounds * ncta // nkv)
+    splits = max(need, rounds * ncta // nkv)
+    if splits > MAX_SPLITS:
+        raise ValueError(f"max_seq_len {max_seq_len} needs {splits} splits per kv head (limit {MAX_SPLITS})")
+    return splits
 
 
 def attn_splits(cfg, ncta: int, max_seq_len: int = 0) -> int:

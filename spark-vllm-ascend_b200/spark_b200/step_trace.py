@@ -9,8 +9,9 @@ kind, the median / max over CTAs of each phase averaged over layers, the barrier
 consumers the producer started copying the stage's bytes.  GEMV phases: prologue
 (loads, RMSNorm, staging), tasks, tail.  The prologue is further split into
 loads (input vectors from L2), norm (sum of squares and 1/rms) and digits (fixed-point
-staging of the input plus the CTA barrier).  Attention phases: scores, softmax, PV,
-publish (+ waiting for the head's other splits), combine.
+staging of the input plus the CTA barrier).  Attention phases: ranges (each warp's
+scores, softmax and P V over its token range), merge (the CTA's merge of the ranges),
+publish (fused with o_proj: + waiting for the head's other splits), combine.
 """
 from __future__ import annotations
 
@@ -38,15 +39,47 @@ def summarize(t: np.ndarray, kinds: list[str]) -> dict:
         c = c[act]
         d = out.setdefault(k, {"stages": 0})
         d["stages"] += 1
-        ph = {"work": c[:, 2] - c[:, 1], "producer_lead": c[:, 1] - c[:, 3]}
+        ph = {"work": c[:, 2] - c[:, 1], "producer_lead": c[:, 1] - c[:, 3],
+              # the producer's last copy of the stage issued this long before the stage began
+              # (negative: issued after it began -- the stage waited for HBM / ring space)
+              "producer_last_lead": c[:, 1] - c[:, 10]}
         if k == "attn":
-            has = (c[:, 7] > 0) & (c[:, 6] > 0)  # splits with tokens (empty splits skip the phases)
-            ph.update({"scores": c[has, 4] - c[has, 1], "softmax": c[has, 5] - c[has, 4], "pv": c[has, 6] - c[has, 5],
-                       "publish_wait": c[has, 7] - c[has, 6], "combine": c[has, 2] - c[has, 7]})
+            has = (c[:, 5] > 0) & (c[:, 7] > 0)  # splits with tokens (empty splits skip the phases)
+            # ranges: the warps' scores / softmax / P V; merge: the CTA's merge of its ranges and
+            # the split's partials; publish: counting the split (fused: and waiting for the
+            # head's other splits); combine: the head's combine (fused: every CTA; else the
+            # split that completed the head)
+            ph.update({"ranges": c[has, 4] - c[has, 1], "merge": c[has, 5] - c[has, 4],
+                       "publish": c[has, 6] - c[has, 5], "combine": c[has, 7] - c[has, 6],
+                       "tail": c[has, 2] - c[has, 7]})
+            # SM-cycle checkpoints of thread 0 (clock64): q + scores, exp, P V, CTA barrier,
+            # merge factors, merge outputs; combine: loads, weights, accumulation, staging
+            raw = d.setdefault("raw", {})
+            names = ["cyc_q_scores", "cyc_exp", "cyc_pv", "cyc_bar", "cyc_fac", "cyc_merge_out"]
+            for q, nm in enumerate(names):
+                ok = has & (c[:, 13 + q] > 0) & (c[:, 12 + q] > 0)
+                if ok.any():
+                    raw.setdefault(nm, []).append(float(np.median(c[ok, 13 + q] - c[ok, 12 + q])))
+            for q, nm in enumerate(["cyc_c_loads", "cyc_c_weights", "cyc_c_acc", "cyc_c_stage"]):
+                ok = has & (c[:, 19 + q] > 0) & (c[:, 18 + q] > 0) & (c[:, 19 + q] >= c[:, 18 + q])
+                if ok.any():
+                    raw.setdefault(nm, []).append(float(np.median(c[ok, 19 + q] - c[ok, 18 + q])))
         else:
             has = c[:, 4] > 0
             ph.update({"prologue": c[has, 4] - c[has, 1], "tasks": c[has, 5] - c[has, 4],
                        "tail": c[has, 2] - c[has, 5]})
+            fd = has & (c[:, 11] > 0)  # warp 0: time waiting for ring data; SM cycles per tile in its tasks
+            ph["data_wait"] = c[fd, 9]
+            raw = d.setdefault("raw", {})
+            v = c[fd, 8] / c[fd, 11]
+            if v.size:
+                raw.setdefault("cycles_per_tile_warp0", []).append(float(np.median(v)))
+                raw.setdefault("tiles_warp0", []).append(float(np.median(c[fd, 11])))
+                # warp 0's SM cycles: in its GEMV tasks, after them (slice sums, epilogue,
+                # slot release), and the whole task loop
+                raw.setdefault("cyc_tasks", []).append(float(np.median(c[fd, 8])))
+                raw.setdefault("cyc_post", []).append(float(np.median(c[fd, 12])))
+                raw.setdefault("cyc_loop", []).append(float(np.median(c[fd, 13])))
             ld = has & (c[:, 6] > 0)  # staging split: loads | RMSNorm | digits + barrier
             nm = ld & (c[:, 7] > 0)
             ph["loads"] = c[ld, 6] - c[ld, 1]
@@ -69,8 +102,10 @@ def summarize(t: np.ndarray, kinds: list[str]) -> dict:
     res = {}
     for k, d in out.items():
         n = d.pop("stages")
+        raw = d.pop("raw", {})
         res[k] = {nm: {"median_us": round(v[0] / n / 1e3, 2), "max_us": round(v[1] / n / 1e3, 2)}
                   for nm, v in d.items()}
+        res[k].update({nm: round(float(np.mean(v)), 1) for nm, v in raw.items()})  # medians over CTAs, mean over layers
         res[k]["stages"] = n
     return res
 

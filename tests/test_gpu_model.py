@@ -114,3 +114,44 @@ def test_long_context_decode_matches_oracle(cuda, oracle):
         assert np.array_equal(u16(eng.logits), want_lg)
         tok = want
 
+
+
+@pytest.mark.slow
+def test_full_model_2048_prompt_greedy_64_tokens(cuda, oracle):
+    """The north-star parity criterion on the benchmark model itself:
+    the 36-layer synthetic 4B Q4_0 model, a seeded 2048-token prompt through the batched
+    GPU prefill, then 64 greedy decode steps of the persistent step kernel.  The CPU oracle
+    decodes from the same KV cache (the prefill's output) and must produce identical
+    tokens and, after the last step, bit-identical logits."""
+    import torch
+    from spark_b200.config import SparkConfig
+    from spark_b200.model import DecodeEngine, SyntheticWeights
+    cfg = SparkConfig()
+    w = SyntheticWeights(cfg, device="cuda", seed=21)
+    P, N = 2048, 64
+    max_seq = P + N + 1
+    eng = DecodeEngine(w, max_seq_len=max_seq, num_blocks=(max_seq + 127) // 128 + 4, seed=21, mode="step")
+    prompt = np.random.default_rng(21).integers(0, cfg.vocab_size, P).astype(np.int32)
+    first = int(eng.prefill_batched(torch.from_numpy(prompt)).item())
+    torch.cuda.synchronize()
+    om = oracle.OracleModel(cfg, w.to_numpy(), num_blocks=eng.num_blocks, splits=eng.splits,
+                            order=eng.oracle_order())
+    om.kc[...] = u16(eng.k_cache).reshape(om.kc.shape)
+    om.vc[...] = u16(eng.v_cache).reshape(om.vc.shape)
+    table = eng.block_table.cpu().numpy()
+    eng.step_idx.zero_()
+    for _ in range(N):
+        eng.step()
+    torch.cuda.synchronize()
+    assert int(eng.error.item()) == 0
+    gpu = eng.token_log[:N].cpu().tolist()
+    gpu_lg = u16(eng.logits)
+    tok, ref, ref_lg = first, [], None
+    for i in range(N):
+        r = om.step(table, tok, P + i, want_logits=i == N - 1)
+        if i == N - 1:
+            r, ref_lg = r
+        ref.append(int(r))
+        tok = int(r)
+    assert gpu == ref
+    assert np.array_equal(gpu_lg, ref_lg)

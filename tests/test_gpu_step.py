@@ -78,7 +78,9 @@ def test_pack_t16_matches_numpy(cuda, n, k, kp, rowmap, hd):
 
 
 @pytest.mark.parametrize("n,k,kp,ks", [(64, 256, 1, 1), (48, 512, 1, 2), (160, 2560, 1, 4), (2560, 4096, 2, 4),
-                                       (2560, 9728, 4, 2), (4096, 2560, 1, 1), (9728, 2560, 1, 4)])
+                                       (2560, 9728, 4, 2), (4096, 2560, 1, 1), (9728, 2560, 1, 4),
+                                       # tiles per slice 1, 3, 5, 16: the odd last tile and every group batch
+                                       (32, 192, 1, 3), (32, 384, 1, 2), (32, 640, 1, 2), (16, 1024, 1, 1)])
 def test_t16_gemv_bitexact(cuda, oracle, n, k, kp, ks):
     import torch
     from spark_b200 import step

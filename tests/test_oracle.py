@@ -212,7 +212,8 @@ def test_gemv_canonical_order_is_documented(oracle):
 
 @pytest.mark.parametrize("kp,ks", [(1, 1), (1, 4), (2, 2), (4, 1)])
 def test_t16_gemv_order_is_documented(oracle, kp, ks):
-    """Persistent-step order: S = 13 - e staging, KP parts of KS slices, sequential sums."""
+    """Persistent-step order: S = 13 - e staging, KP parts of KS slices, each slice four
+    block chains (blocks b0 + c, b0 + c + 4, ...) summed as (c0 + c1) + (c2 + c3)."""
     x, qs, d = _q4_setup(3, 1024, seed=5)
     xf = f32(x)[0]
     X, sx, C = _stage_np(xf, s0=13)
@@ -229,13 +230,16 @@ def test_t16_gemv_order_is_documented(oracle, kp, ks):
         for p in range(kp):
             part = np.float32(0)
             for sl in range(ks):
-                acc = np.float32(0)
-                for b in range(p * bpp + sl * bps, p * bpp + (sl + 1) * bps):
+                chains = [np.float32(0)] * 4
+                b0 = p * bpp + sl * bps
+                for b in range(b0, b0 + bps):
                     q = qs[r, b * 16:(b + 1) * 16].astype(np.int64)
                     P = int(((q & 15) * X[32 * b:32 * b + 16]).sum() + ((q >> 4) * X[32 * b + 16:32 * b + 32]).sum()
                             - C[b])
                     ds = np.float32(dd[r, b] * sx[b])
-                    acc = np.float32(np.float64(ds) * np.float64(P) + np.float64(acc))
+                    c = (b - b0) & 3
+                    chains[c] = np.float32(np.float64(ds) * np.float64(P) + np.float64(chains[c]))
+                acc = np.float32(np.float32(chains[0] + chains[1]) + np.float32(chains[2] + chains[3]))
                 part = acc if sl == 0 else np.float32(part + acc)
             want[p, r] = part
     got = oracle.t16_gemv_parts(x[0], qs, d, kp, ks)
@@ -337,10 +341,11 @@ def test_attention_split_combine_vs_float64(oracle, L, splits):
     assert all(np.all(np.isneginf(pl[s])) and np.all(po[s] == 0) for s in empty)
 
 
-@pytest.mark.parametrize("L,splits,W", [(3000, 18, 12), (700, 18, 12), (64, 74, 12), (2049, 5, 3)])
-def test_attention_chunk_accumulators_vs_float64(oracle, L, splits, W):
-    """Persistent-step PV order (16-token chunks into W accumulators) meets abs 2e-2 and
-    agrees with the sequential order to fp32 rounding."""
+@pytest.mark.parametrize("L,splits,W", [(3000, 18, 11), (700, 18, 11), (64, 74, 11), (2049, 5, 3), (2049, 2, 11)])
+def test_attention_warp_ranges_vs_float64(oracle, L, splits, W):
+    """Persistent-step order (each split cut into W token ranges with their own softmax,
+    merged by their maxima) meets abs 2e-2 and agrees with the one-range order to within
+    the bf16 rounding of P (each range rounds p relative to its own maximum)."""
     rng = np.random.default_rng(L + W)
     kc, vc, table = _paged(rng, L)
     q = bf16(rng.standard_normal((32, 128)).astype(np.float32))
@@ -349,8 +354,88 @@ def test_attention_chunk_accumulators_vs_float64(oracle, L, splits, W):
     out = f32(oracle.attn_combine(po, pl))
     assert np.max(np.abs(out - _attn_ref64(q, kc, vc, table, L, scale))) <= 2e-2
     po0, pl0 = oracle.attn_split(q, kc, vc, table, L, splits, scale)
-    assert np.array_equal(pl, pl0)
-    assert np.allclose(po, po0, rtol=1e-5, atol=1e-6)
+    assert np.array_equal(np.isneginf(pl), np.isneginf(pl0))
+    fin = np.isfinite(pl0)
+    assert np.allclose(pl[fin], pl0[fin], rtol=0, atol=1e-5)
+    assert np.allclose(po, po0, rtol=1e-2, atol=4e-3)
+
+
+def test_attention_warp_ranges_order_is_documented(oracle):
+    """numpy restatement of the persistent-step order, compared bit for bit: ranges of
+    C = roundup(ceil(n / W), 512 / D) tokens, per-range max / exp / 32-lane sum / bf16 P /
+    ascending P V, then the merge in range order."""
+    rng = np.random.default_rng(17)
+    L, splits, W, D = 300, 2, 11, 128
+    kc, vc, table = _paged(rng, L)
+    q = bf16(rng.standard_normal((32, D)).astype(np.float32))
+    scale = float(np.float32(1 / math.sqrt(D)))
+    po, pl = oracle.attn_split(q, kc, vc, table, L, splits, scale, chunk_accs=W)
+    T = oracle.split_tokens(L, splits)
+    bs = kc.shape[2]
+    lanes = D // 16
+    ninf = np.float32(-np.inf)
+    for s in range(splits):
+        t0, t1 = s * T, min((s + 1) * T, L)
+        n = t1 - t0
+        C = -(-(-(-n // W)) // (512 // D)) * (512 // D)
+        for hq in (0, 5, 31):
+            hk = hq // 4
+            qf = f32(q[hq])
+            ms, ls, os = [], [], []
+            for w in range(W):
+                a, b = w * C, min(w * C + C, n)
+                if a >= n:
+                    ms.append(ninf), ls.append(np.float32(0)), os.append(np.zeros(D, np.float32))
+                    continue
+                sc = []
+                for i in range(a, b):
+                    t = t0 + i
+                    k = f32(kc[table[t // bs], hk, t % bs])
+                    per = D // 2 // lanes
+                    lane = []
+                    for j in range(lanes):
+                        a0 = a1 = np.float32(0)
+                        for part in range(2):
+                            base = part * D // 2 + per * j
+                            for m in range(0, per, 2):
+                                a0 = np.float32(np.float64(qf[base + m]) * np.float64(k[base + m]) + np.float64(a0))
+                                a1 = np.float32(np.float64(qf[base + m + 1]) * np.float64(k[base + m + 1])
+                                                + np.float64(a1))
+                        lane.append(np.float32(a0 + a1))
+                    v = np.array(lane, np.float32)
+                    off = lanes // 2
+                    while off:
+                        v = (v + v[np.arange(lanes) ^ off]).astype(np.float32)
+                        off //= 2
+                    sc.append(np.float32(v[0] * np.float32(scale)))
+                m = max(sc)
+                lane = np.zeros(32, np.float32)
+                P = []
+                for i, x in enumerate(sc):
+                    pv = np.float32(oracle.exp(float(np.float32(x - m))))
+                    lane[i % 32] = np.float32(lane[i % 32] + pv)
+                    P.append(f32(bf16(np.array([pv], np.float32)))[0])
+                off = 16
+                while off:
+                    lane = (lane + lane[np.arange(32) ^ off]).astype(np.float32)
+                    off //= 2
+                o = np.zeros(D, np.float32)
+                for i in range(a, b):
+                    t = t0 + i
+                    v = f32(vc[table[t // bs], hk, t % bs])
+                    o = (np.float64(P[i - a]) * v.astype(np.float64) + o.astype(np.float64)).astype(np.float32)
+                ms.append(np.float32(m)), ls.append(lane[0]), os.append(o)
+            M = max(ms)
+            Lsum = np.float32(0)
+            O = np.zeros(D, np.float32)
+            for w in range(W):
+                f = np.float32(0) if ms[w] == ninf else np.float32(oracle.exp(float(np.float32(ms[w] - M))))
+                Lsum = np.float32(Lsum + np.float32(f * ls[w]))
+                O = (O + (f * os[w]).astype(np.float32)).astype(np.float32)
+            want_o = (O / Lsum).astype(np.float32)
+            want_l = np.float32(np.float32(oracle.log(float(Lsum))) + M)
+            assert np.array_equal(po[s, hq].view(np.uint32), want_o.view(np.uint32)), (s, hq)
+            assert np.float32(pl[s, hq]).view(np.uint32) == want_l.view(np.uint32), (s, hq)
 
 
 def test_combine_single_split_identity(oracle):
