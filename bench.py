@@ -378,7 +378,7 @@ def run_spark(args):
             "dtype": "q4_0 weights x fp32 accumulate, bf16 activations / KV",
             "data": "synthetic: seeded N(0,0.02) weights -> Q4_0" +
                     (", random Q6_K tied embedding" if cfg.tied_q6k_head else "") + ", 2048 uniform-random prompt ids",
-            "config": {**_workload_config(args, cfg, world, eng.splits),
+            "config": {**_workload_config(args, getattr(w, "full_cfg", cfg), world, eng.splits),
                        "kernels_per_step": eng.kernels_per_step(), "mode": eng.mode,
                        "l2": f"inputs larger than L2 ({w.q4_bytes() / 1e9:.2f} GB of weights per step)"},
             "e2e": {"value": round(args.steps * seqs / (e2e_ms / 1e3), 3), "unit": "tokens/s",

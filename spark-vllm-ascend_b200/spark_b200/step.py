@@ -277,21 +277,21 @@ def default_order(cfg, ncta: int, tp: int = 1, splits: int = 0) -> dict:
     }
 
 
-SHORT_SPLITS_256 = 18  # head_dim 256: splits per kv head when the context allows (see splits_for)
+SHORT_SPLITS = 18  # splits per kv head when the context allows (see splits_for)
 
 
 def splits_for(nkv: int, ncta: int, max_seq_len: int = 0, head_dim: int = 128) -> int:
-    """Splits per kv head.  A context that fits: head_dim 128 takes one (kv head, split)
-    task per CTA (CTAs / kv heads), head_dim 256 at most SHORT_SPLITS_256 -- its tasks'
-    fixed cost (q load, barriers, softmax warps, publish, combine share) outweighs the
-    idle CTAs.  Measured at ctx 2048: 8 kv heads x 128 dims best at 18 (12, 9 worse),
-    4 x 128 (tensor parallel over 2) the same at 18 and 37, 4 x 256 best at 18-24 (27,
-    32, 37 worse).  Longer contexts take the fewest splits that hold them, rounded up to
-    whole rounds of tasks over the CTAs (8 kv heads: 37 = 296 tasks = two per CTA, ...)
-    so no CTA runs a round more than the others."""
+    """Splits per kv head.  A context that fits takes SHORT_SPLITS (fewer when the CTAs
+    cannot give every (kv head, split) task its own CTA): an attention task is bound by its
+    latency chain, not by its K / V bytes, so more, shorter splits only add per-task cost
+    (q load, merge, combine over more partials).  Measured at ctx 2048: 8 kv heads x 128
+    dims best at 18 (12, 9 worse), 4 x 128 (tensor parallel over 2) the same at 18 and 37,
+    4 x 256 best at 18-24 (27, 32, 37 worse).  Longer contexts take the fewest splits that
+    hold them, rounded up to whole rounds of tasks over the CTAs (8 kv heads: 37 = 296
+    tasks = two per CTA, ...) so no CTA runs a round more than the others."""
     need = max(1, -(-max_seq_len // MAX_SPLIT_TOKENS))
     one_round = max(1, min(ncta // nkv, MAX_SPLITS))
-    short = one_round if head_dim <= 128 else min(one_round, SHORT_SPLITS_256)
+    short = min(one_round, SHORT_SPLITS)
     if need <= short:
         return short
     rounds = max(1, -(-need * nkv // ncta))

@@ -43,6 +43,19 @@ def test_tp_tiny_64_tokens_match_oracle(cuda, world):
     assert r0["oracle_tokens_equal"] and r0["oracle_logits_equal"]
 
 
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_kv8_64_tokens_match_oracle(cuda, world):
+    """The 4B model's head layout (32 q / 8 kv heads) at a small size over 2, 4 and 8 ranks
+    (BASELINE configs[3]'s degrees): 64 greedy tokens and the final logits identical to the
+    oracle in the ranks' joint order."""
+    if _gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
+    res = _run(world, "--config", "kv8", "--new-tokens", "64", "--prompt", "40")
+    assert len(res) == world and all(r["ok"] for r in res), res
+    r0 = next(r for r in res if r["rank"] == 0)
+    assert r0["oracle_tokens_equal"] and r0["oracle_logits_equal"]
+
+
 @pytest.mark.parametrize("world", [2])
 def test_tp_spark_tiny_matches_oracle(cuda, world):
     """The Spark architecture over 2 ranks (gate rows and the Q6_K head sharded with the
@@ -56,7 +69,7 @@ def test_tp_spark_tiny_matches_oracle(cuda, world):
 
 
 @pytest.mark.slow
-@pytest.mark.parametrize("world", [2])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_tp_full_size_matches_oracle(cuda, world):
     if _gpus() < world:
         pytest.skip(f"needs {world} GPUs")

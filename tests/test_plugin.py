@@ -96,3 +96,15 @@ def test_attention_backend_layout_and_metadata():
     assert SparkAttentionImpl(16, 256, 0.0625, 4, sliding_window=512).window == 513
     with pytest.raises(NotImplementedError):  # head_size 256 takes 4 query heads per kv head
         SparkAttentionImpl(16, 256, 0.0625, 8)
+
+
+def test_layer_run_op_registered_with_fake():
+    """torch.ops.spark_b200.layer_run exists with the reference's signature and a fake
+    implementation (no GPU, no library call: meta tensors)."""
+    import torch
+    from spark_b200 import layer_op  # noqa: F401  (registers the op)
+    op = torch.ops.spark_b200.layer_run
+    x = torch.empty((1, 2560), dtype=torch.bfloat16, device="meta")
+    pos = torch.empty((1,), dtype=torch.int64, device="meta")
+    y, r = op(x, x, pos, "model.layers.0.self_attn")
+    assert y.shape == (1, 2560) and r.shape == (1, 2560) and y.dtype == torch.bfloat16

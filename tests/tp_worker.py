@@ -33,7 +33,7 @@ def u16(t):
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("--config", choices=["tiny", "full", "spark-tiny"], default="tiny")
+    ap.add_argument("--config", choices=["tiny", "full", "spark-tiny", "kv8"], default="tiny")
     ap.add_argument("--layers", type=int, default=0)
     ap.add_argument("--prompt", type=int, default=24)
     ap.add_argument("--new-tokens", type=int, default=64)
@@ -58,6 +58,10 @@ def main(argv=None):
         cfg = spark_x26_config(num_layers=args.layers or 4, hidden_size=512, num_q_heads=8, num_kv_heads=2,
                                intermediate_size=1024, vocab_size=4096, sliding_window=33, max_position=4096,
                                name="spark-tiny")
+    elif args.config == "kv8":  # the 4B model's head layout (32 q / 8 kv heads of 128) at a small size:
+        # shards over 2, 4 and 8 ranks (intermediate 1024 / 8 = 128 rows, vocab 4096 / 8 per rank)
+        cfg = tiny_config(hidden_size=512, num_q_heads=32, num_kv_heads=8, intermediate_size=1024,
+                          vocab_size=4096, name="spark-kv8", **kw)
     else:
         cfg = tiny_config(**kw) if args.config == "tiny" else SparkConfig(max_position=4096, **kw)
     full = SyntheticWeights(cfg, device="cuda", seed=args.seed)
