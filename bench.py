@@ -194,7 +194,7 @@ def time_kernels(eng, reps: int = 3) -> dict:
 # algorithmic bytes.  The captures (gate_up ring GEMV, split-KV attention at ctx 6144,
 # an 8-layer persistent step) are summarised under profiles/.
 NCU_TRAFFIC_RATIO = {"gate_up": 28_079_360 / 28_051_456, "attn": 25_295_360 / 25_182_208,
-                     "step": 680_050_944 / 675_087_360}
+                     "step": 680_838_144 / 675_120_128}
 
 
 def kernel_bytes(cfg, ctx: int) -> dict:
@@ -283,13 +283,16 @@ def run_spark(args):
         torch.cuda.synchronize()
 
     rewind()
-    if world > 1:
-        torch.distributed.barrier()
-    torch.cuda.synchronize()
+    # the clock sampler starts (and settles) BEFORE the ranks line up: under tensor
+    # parallelism a rank that entered its timed loop while rank 0 still slept would spin
+    # in its first exchange, inside its own timed region
     sampler = ClockSampler(device.index if device.index is not None else 0) if rank == 0 else None
     if sampler:
         sampler.start()
         time.sleep(0.4)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.nvtx.range_push("timed")
     e0.record()

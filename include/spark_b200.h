@@ -261,8 +261,14 @@ int spark_read_device_error(int* value, int reset);
                                   SPARK_ROWS_PLAIN, (k / kp) % 256 == 0, otherwise as SPARK_STAGE_GEMV */
 
 /* GEMV prologue: where x comes from */
+#define SPARK_XCHG_TAGGED 2
 #define SPARK_PRO_BF16 0  /* a: bf16 [k] (or embed row embed[*token] when embed != NULL) */
 #define SPARK_PRO_PARTS 1 /* a: fp32 [a_parts][k]; x = bf16(((a_0 + a_1) + ...)) */
+#define SPARK_PRO_PARTS_TAGGED 3 /* a: uint64 [a_parts][k] tagged parts written by a SPARK_XCHG_TAGGED stage:
+                                   word = fp32 bits | tag << 32, tag = launch + 1 (launch =
+                                   io->counters[num_stages + 2]); the prologue waits (bounded) for each
+                                   word's tag, then x = bf16(((a_0 + a_1) + ...)).  `wait` orders the
+                                   stage's other inputs (residual) and names no tagged stage */
 #define SPARK_PRO_ATTN 2  /* o_proj fused behind the attention stage just before it (wait = -1, no norm,
                              kp = that stage's nkv, k = nq * head_dim, splits = its splits, nkv * splits
                              <= CTAs): CTA c takes K part g = c / splits (kv head g) of the row groups
@@ -297,7 +303,10 @@ typedef struct SparkStage {
   int32_t xchg;               /* tensor-parallel exchange stage (io->tp_size > 1): SPARK_EPI_PARTS writes
                                  its part as part tp_rank * kp + kpi of `out` in EVERY rank's exchange
                                  window, SPARK_EPI_ARGMAX takes the maximum into every rank's key, and
-                                 the stage's completion is counted on every rank; 0: local stage */
+                                 the stage's completion is counted on every rank; 0: local stage;
+                                 SPARK_XCHG_TAGGED (EPI_PARTS only): the parts go to every rank as tagged
+                                 64-bit words (see SPARK_PRO_PARTS_TAGGED) and the stage is not counted:
+                                 its readers wait on the words themselves, no stage may wait on it */
   float eps, inv_k, scale;
   int32_t row0;               /* SPARK_EPI_ARGMAX: global index of row 0 (vocab shard start), else 0 */
   const void* w;              /* T16 weight units */

@@ -725,7 +725,10 @@ static int check_stage(const SparkStage& s, int i, int ncta) {
         (s.kind == SPARK_STAGE_GEMV && ((s.k / s.kp) / 64) % s.ks))
       return SPARK_ERR_UNSUPPORTED_SHAPE;
     if (s.units != s.n / 16 * s.kp || s.rot < 0 || s.rot >= ncta) return SPARK_ERR_INVALID_ARG;
-    if (s.row0 < 0 || (s.row0 && s.epi != SPARK_EPI_ARGMAX) || s.xchg < 0 || s.xchg > 1) return SPARK_ERR_INVALID_ARG;
+    if (s.row0 < 0 || (s.row0 && s.epi != SPARK_EPI_ARGMAX) || s.xchg < 0 || s.xchg > SPARK_XCHG_TAGGED)
+      return SPARK_ERR_INVALID_ARG;
+    if (s.xchg == SPARK_XCHG_TAGGED && s.epi != SPARK_EPI_PARTS) return SPARK_ERR_INVALID_ARG;
+    if (s.pro == SPARK_PRO_PARTS_TAGGED && (reinterpret_cast<uintptr_t>(s.a) & 15)) return SPARK_ERR_ALIGNMENT;
     if (s.kind == SPARK_STAGE_GEMV && 9 * (s.k / s.kp) > step::kRingBytes) return SPARK_ERR_TOO_LARGE;
     if (s.ks > step::kMaxSlices) return SPARK_ERR_UNSUPPORTED_SHAPE;
     if (72 * (s.k / 32) + (s.norm ? 6 * s.k : 0) > step::kScratchBytes) return SPARK_ERR_TOO_LARGE;
@@ -734,7 +737,7 @@ static int check_stage(const SparkStage& s, int i, int ncta) {
     if ((reinterpret_cast<uintptr_t>(s.a) | reinterpret_cast<uintptr_t>(s.b) | reinterpret_cast<uintptr_t>(s.embed) |
          reinterpret_cast<uintptr_t>(s.gamma) | reinterpret_cast<uintptr_t>(s.res_out)) & 15)
       return SPARK_ERR_ALIGNMENT;
-    if (s.pro == SPARK_PRO_PARTS) {
+    if (s.pro == SPARK_PRO_PARTS || s.pro == SPARK_PRO_PARTS_TAGGED) {
       if (s.a_parts <= 0 || s.a_parts > step::kMaxParts || !s.a || s.embed) return SPARK_ERR_INVALID_ARG;
       if (s.k > step::kConsumers * 8) return SPARK_ERR_TOO_LARGE;  // one 8-element group per thread
     } else if (s.pro == SPARK_PRO_ATTN) {
@@ -860,7 +863,8 @@ static int check_tp(const SparkStage* st, int num_stages, const SparkStepIO& io)
     if (!s.xchg) continue;
     if (s.kind != SPARK_STAGE_GEMV && s.kind != SPARK_STAGE_GEMV_Q6) return SPARK_ERR_INVALID_ARG;
     if (s.epi == SPARK_EPI_PARTS) {
-      if (!in_window(io, s.out, 4ull * s.n * s.kp * io.tp_size)) return SPARK_ERR_INVALID_ARG;
+      const unsigned long long word = s.xchg == SPARK_XCHG_TAGGED ? 8ull : 4ull;
+      if (!in_window(io, s.out, word * s.n * s.kp * io.tp_size)) return SPARK_ERR_INVALID_ARG;
     } else if (s.epi == SPARK_EPI_ARGMAX) {
       if (!in_window(io, s.key, 8) || (io.key && io.key != s.key)) return SPARK_ERR_INVALID_ARG;
     } else {
@@ -884,6 +888,10 @@ int spark_step_run(const SparkStage* host_stages, const SparkStage* dev_stages, 
     const int st = check_stage(host_stages[i], i, ncta);
     if (st != SPARK_OK) return st;
   }
+  for (int i = 0; i < num_stages; i++)  // a tagged exchange stage is not counted: nothing may wait on it
+    if (host_stages[i].xchg == SPARK_XCHG_TAGGED)
+      for (int j = i + 1; j < num_stages; j++)
+        if (host_stages[j].wait == i) return SPARK_ERR_INVALID_ARG;
   for (int i = 0; i < num_stages; i++) {  // an o_proj fused behind attention: wiring of the pair
     const SparkStage& o = host_stages[i];
     if (o.kind == SPARK_STAGE_ATTN) continue;
@@ -921,12 +929,18 @@ int spark_step_run(const SparkStage* host_stages, const SparkStage* dev_stages, 
     if (host_stages[i].kind == SPARK_STAGE_ATTN && host_stages[i].head_dim != (spark ? 256 : 128))
       return SPARK_ERR_UNSUPPORTED_SHAPE;
   using Kernel = void (*)(const step::StepParams);
-  static const Kernel kernels[8] = {
-      step::step_kernel<false, false, false>, step::step_kernel<false, false, true>,
-      step::step_kernel<false, true, false>,  step::step_kernel<false, true, true>,
-      step::step_kernel<true, false, false>,  step::step_kernel<true, false, true>,
-      step::step_kernel<true, true, false>,   step::step_kernel<true, true, true>};
-  const Kernel kernel = kernels[4 * q6 + 2 * multi + spark];
+  // tensor-parallel programs (tagged exchange reads) run in their own instantiations
+  static const Kernel kernels[16] = {
+      step::step_kernel<false, false, false, false>, step::step_kernel<false, false, true, false>,
+      step::step_kernel<false, true, false, false>,  step::step_kernel<false, true, true, false>,
+      step::step_kernel<true, false, false, false>,  step::step_kernel<true, false, true, false>,
+      step::step_kernel<true, true, false, false>,   step::step_kernel<true, true, true, false>,
+      step::step_kernel<false, false, false, true>,  step::step_kernel<false, false, true, true>,
+      step::step_kernel<false, true, false, true>,   step::step_kernel<false, true, true, true>,
+      step::step_kernel<true, false, false, true>,   step::step_kernel<true, false, true, true>,
+      step::step_kernel<true, true, false, true>,    step::step_kernel<true, true, true, true>};
+  const bool tp = io->tp_size > 1;
+  const Kernel kernel = kernels[8 * tp + 4 * q6 + 2 * multi + spark];
   if (set_smem(reinterpret_cast<const void*>(kernel), step::kSmemBytes) != kOk) return kErrLaunch;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(ncta);

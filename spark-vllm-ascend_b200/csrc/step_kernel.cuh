@@ -365,6 +365,7 @@ struct Producer {
 constexpr int kStageGroups = 4;  // 8-element groups per consumer thread (k <= 12288)
 constexpr int kMaxParts = 8;  // parts summed by a PARTS prologue (K parts x TP ranks)
 constexpr int kPartsBatch = 4;  // parts loaded per L2 round trip
+constexpr int kTaggedBatch = 2;  // tagged exchange parts read per round trip
 
 __device__ __forceinline__ void lds_u32x4(uint32_t addr, uint4& v) {
   asm("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
@@ -452,8 +453,68 @@ __device__ __forceinline__ int stage_grp(int gi, int ngrp, int rot) {
   return g >= ngrp ? g - ngrp : g;
 }
 
-template <bool Q6>
-__device__ __forceinline__ void stage_x(const SparkStage& st, const Smem& s, int tid, unsigned long long* tr, int x0,
+// Sum, in part order, the 8 elements of group g of a_parts tagged parts (uint64 words:
+// fp32 bits | tag << 32, part q at tp + q k) once every word carries this launch's tag:
+// each batch of parts is re-read until it does (bounded like every wait).  Only the
+// tensor-parallel kernel instantiations carry it, so its registers stay out of the  false: the wait ran out or the launch
+// aborted.
+__device__ __forceinline__ bool tagged_parts_sum(const unsigned long long* tp, int a_parts, int k, int g, uint32_t tag,
+                                              volatile int* abort_flag, float4& p0, float4& p1) {
+  bool first = true, ok = true;
+  for (int q2 = 0; q2 < a_parts; q2 += kTaggedBatch) {
+    unsigned long long wv[kTaggedBatch][8];
+    unsigned long long t0 = 0;
+    for (uint32_t it = 0;; it++) {
+      bool ready = true;
+#pragma unroll
+      for (int q = 0; q < kTaggedBatch; q++) {
+        if (q2 + q < a_parts) {
+          const unsigned long long* src = tp + (size_t)(q2 + q) * k + 8 * g;
+#pragma unroll
+          for (int j = 0; j < 8; j += 2)
+            asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];"
+                         : "=l"(wv[q][j]), "=l"(wv[q][j + 1])
+                         : "l"(src + j)
+                         : "memory");
+#pragma unroll
+          for (int j = 0; j < 8; j++) ready = ready && (uint32_t)(wv[q][j] >> 32) == tag;
+        }
+      }
+      if (ready) break;
+      if ((it & 15) == 15) {
+        const unsigned long long t = gtimer();
+        if (t0 == 0) t0 = t;
+        if (*abort_flag || t - t0 > kWaitNs) {
+          ok = false;
+          break;
+        }
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < kTaggedBatch; q++) {
+      if (q2 + q < a_parts) {
+        const float4 a0 = make_float4(__uint_as_float((uint32_t)wv[q][0]), __uint_as_float((uint32_t)wv[q][1]),
+                                      __uint_as_float((uint32_t)wv[q][2]), __uint_as_float((uint32_t)wv[q][3]));
+        const float4 a1 = make_float4(__uint_as_float((uint32_t)wv[q][4]), __uint_as_float((uint32_t)wv[q][5]),
+                                      __uint_as_float((uint32_t)wv[q][6]), __uint_as_float((uint32_t)wv[q][7]));
+        if (first) {
+          p0 = a0;
+          p1 = a1;
+          first = false;
+        } else {
+          p0 = make_float4(__fadd_rn(p0.x, a0.x), __fadd_rn(p0.y, a0.y), __fadd_rn(p0.z, a0.z), __fadd_rn(p0.w, a0.w));
+          p1 = make_float4(__fadd_rn(p1.x, a1.x), __fadd_rn(p1.y, a1.y), __fadd_rn(p1.z, a1.z), __fadd_rn(p1.w, a1.w));
+        }
+      }
+    }
+    if (!ok) break;
+  }
+  return ok;
+}
+
+template <bool Q6, bool TP>
+__device__ __forceinline__ void stage_x(const StepParams& P, const SparkStage& st, const Smem& s, int tid,
+                                        unsigned long long* tr, int x0,
                                         int kx) {
   const int k = st.k, nb = kx >> 5, ngrp = kx >> 3;
   uint32_t* xfrag32 = reinterpret_cast<uint32_t*>(s.scratch);
@@ -473,8 +534,8 @@ __device__ __forceinline__ void stage_x(const SparkStage& st, const Smem& s, int
   // requests spread over the L2 slices instead of queueing on the same lines.
   const int rot = 4 * (int)((blockIdx.x * 37u) % (unsigned)(ngrp >> 2));
   // all loads first: one L2 round trip
-  if (st.pro == SPARK_PRO_PARTS) {
-    // every part in flight at once, then summed in part order.  A PARTS input has at most
+  if (st.pro == SPARK_PRO_PARTS || st.pro == SPARK_PRO_PARTS_TAGGED) {
+    // parts in flight in batches, then summed in part order.  A PARTS input has at most
     // one 8-element group per thread (k <= kConsumers * 8, the host checks): slot 0.
     const int g = stage_grp(tid, ngrp, rot);
 #pragma unroll
@@ -488,6 +549,11 @@ __device__ __forceinline__ void stage_x(const SparkStage& st, const Smem& s, int
         gv[0] = *reinterpret_cast<const uint4*>(gm + 8 * g);
       }
       float4 p0 = make_float4(0.f, 0.f, 0.f, 0.f), p1 = p0;
+      if (TP && st.pro == SPARK_PRO_PARTS_TAGGED) {
+        if (!tagged_parts_sum(static_cast<const unsigned long long*>(st.a) + x0, st.a_parts, k, g,
+                              (uint32_t)(s.misc64[2] + 1), s.abort_flag, p0, p1))
+          raise_abort(P, s, SPARK_ERR_LAUNCH);
+      } else
 #pragma unroll
       for (int q4 = 0; q4 < kMaxParts; q4 += kPartsBatch) {  // kPartsBatch parts per round trip
         if (q4 < st.a_parts) {
@@ -895,7 +961,17 @@ __device__ __forceinline__ void gemv_epilogue(const SparkStage& st, const SparkS
       break;
     }
     case SPARK_EPI_PARTS: {
-      if (st.xchg) {  // part tp_rank * kp + kpi, into every rank's window
+      if (st.xchg == SPARK_XCHG_TAGGED) {  // tagged words (value | tag << 32), into every rank's window
+        const unsigned long long tag = (unsigned long long)(uint32_t)(misc64[2] + 1) << 32;
+        unsigned long long* y = static_cast<unsigned long long*>(st.out) + (size_t)(io.tp_rank * st.kp + kpi) * st.n;
+        for (int p = 0; p < io.tp_size; p++) {
+          unsigned long long* yp = peer_addr(io, p, y);
+          asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(yp + r0), "l"(tag | __float_as_uint(v0))
+                       : "memory");
+          asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(yp + r1), "l"(tag | __float_as_uint(v1))
+                       : "memory");
+        }
+      } else if (st.xchg) {  // part tp_rank * kp + kpi, into every rank's window
         float* y = static_cast<float*>(st.out) + (size_t)(io.tp_rank * st.kp + kpi) * st.n;
         for (int p = 0; p < io.tp_size; p++) {
           float* yp = peer_addr(io, p, y);
@@ -1009,7 +1085,7 @@ __device__ __forceinline__ bool wait_unit(const Smem& s, uint32_t seq) {
 
 // Q6: the kernel instantiation that also runs SPARK_STAGE_GEMV_Q6 stages (programs
 // without them use the Q4-only instantiation, whose registers the Q6 code does not touch)
-template <bool Q6, bool Spark>
+template <bool Q6, bool Spark, bool TP>
 __device__ __forceinline__ bool gemv_stage(const StepParams& P, const SparkStage& st, const Smem& s, uint32_t& seq_base, int tid) {
   const int ncta = gridDim.x, cta = blockIdx.x, warp = tid >> 5, lane = tid & 31;
   int u0, ustride;
@@ -1020,7 +1096,7 @@ __device__ __forceinline__ bool gemv_stage(const StepParams& P, const SparkStage
   const bool part_x = pro_attn || (!st.norm && st.kp > 1 && ncta % st.kp == 0);
   const int kx = part_x ? st.k / st.kp : st.k;
   if (!pro_attn && (nl > 0 || (cta == 0 && st.res_out)))
-    stage_x<Q6>(st, s, tid,
+    stage_x<Q6, TP>(P, st, s, tid,
             (tid == 0 && P.io.trace) ? P.io.trace + ((size_t)cta * P.num_stages + s.flag[2]) * kTraceSlots : nullptr,
             part_x ? (u0 % st.kp) * kx : 0, kx);
   consumer_bar();
@@ -1738,7 +1814,7 @@ __device__ __forceinline__ bool wait_stage(const StepParams& P, const Smem& s, i
 // CTAs; Spark: the program uses a Spark layer feature (head_dim 256, sliding window,
 // output gate, partial RoPE, GELU * mul).  Each is its own instantiation so the usual
 // program (Q4_0, one attention task per CTA) carries none of their registers.
-template <bool Q6, bool Multi, bool Spark>
+template <bool Q6, bool Multi, bool Spark, bool TP>
 __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepParams P) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const Smem s = carve(smem_raw);
@@ -1829,12 +1905,15 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepParams P) {
     const bool fused = st.kind == SPARK_STAGE_ATTN && i + 1 < P.num_stages && stage_at(P, i + 1).pro == SPARK_PRO_ATTN;
     // both stage functions keep every consumer on the same barriers; a stage that
     // fails returns false in all threads (attention: a split longer than the scratch)
-    const bool ok = st.kind != SPARK_STAGE_ATTN ? gemv_stage<Q6, Spark>(P, st, s, seq_base, tid)
+    const bool ok = st.kind != SPARK_STAGE_ATTN ? gemv_stage<Q6, Spark, TP>(P, st, s, seq_base, tid)
                                                 : attn_stage<Multi, Spark>(P, st, s, seq_base, tid, fused);
     consumer_bar();
     if (!ok) return;
     if (tid == 0 && tr) tr[2] = gtimer();
-    if (tid == 0 && !*s.abort_flag && !fused) {  // release: the CTA's writes (ordered by the barrier) before the count
+    // a tagged exchange stage is not counted (its readers wait on its words); a fused
+    // attention stage neither
+    if (tid == 0 && !*s.abort_flag && !fused && st.xchg != SPARK_XCHG_TAGGED) {  // release: the CTA's writes
+                                                                                 // (ordered by the barrier) first
       if (st.xchg) {  // writes to every rank's window, then a count on every rank
         asm volatile("fence.acq_rel.sys;" ::: "memory");
         for (int p = 0; p < P.io.tp_size; p++)

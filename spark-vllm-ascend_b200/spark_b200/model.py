@@ -199,13 +199,20 @@ class DecodeEngine:
 
     def __init__(self, weights: SyntheticWeights, max_seq_len: int, splits: int = 0, num_blocks: int | None = None,
                  block_table: torch.Tensor | None = None, use_graph: bool = True, max_steps: int | None = None,
-                 seed: int = 0, mode: str = "step", tp_group=None):
+                 seed: int = 0, mode: str = "step", tp_group=None, tp_exchange: str = "counted"):
         """``mode`` "step": one persistent kernel per decode step (spark_b200.step);
         "kernels": the per-stage kernel chain (5 kernels per layer + head + finalize).
 
         Tensor parallel: ``weights`` is a ``tp.ShardWeights`` (rank r of tp) and every rank
         constructs its engine at the same time (the exchange windows are connected over
-        torch.distributed, ``tp_group`` or the default group); persistent step only."""
+        torch.distributed, ``tp_group`` or the default group); persistent step only.
+        ``tp_exchange``: "counted" (parts stored to every rank, then a system-scope fence
+        and a count on every rank's stage counter; the default, measured faster) or
+        "tagged" (parts as 64-bit words carrying the launch number, read once the tags
+        match, no fence or counter)."""
+        if tp_exchange not in ("counted", "tagged"):
+            raise ValueError(f"unknown tp_exchange {tp_exchange!r}")
+        self.tp_exchange = tp_exchange
         cfg = weights.cfg
         self.cfg, self.w = cfg, weights
         dev = weights.device
@@ -301,15 +308,23 @@ class DecodeEngine:
         f32 = torch.float32
         if tp > 1:  # what peers write lives in the exchange window
             from . import tp as T
-            self.window = T.ExchangeWindow(T.window_fields(cfg, order, T.program_stages(cfg.num_layers), tp), dev,
-                                           self.tp_rank, tp)
+            tagged_x = self.tp_exchange == "tagged"
+            self.window = T.ExchangeWindow(T.window_fields(cfg, order, T.program_stages(cfg.num_layers), tp,
+                                                           tagged_x), dev, self.tp_rank, tp)
             self.window.exchange(self.tp_group)
-            self.o_parts, self.down_parts = self.window.t["o_parts"], self.window.t["down_parts"]
             self.key = self.window.t["key"]
+            if not tagged_x:
+                self.o_parts, self.down_parts = self.window.t["o_parts"], self.window.t["down_parts"]
         else:
             self.o_parts = torch.zeros((kp_o, h), dtype=f32, device=dev)
             self.down_parts = torch.zeros((kp_down, h), dtype=f32, device=dev)
-        xchg = tp > 1
+        # tensor parallel: o_proj / down parts go to every rank's window, counted (fence +
+        # remote counts) or as tagged words (per-layer buffers; readers wait on the tags);
+        # the LM head's argmax key is always a counted exchange
+        tagged = tp > 1 and self.tp_exchange == "tagged"
+        xchg = S.XCHG_TAGGED if tagged else (S.XCHG_COUNTED if tp > 1 else S.XCHG_LOCAL)
+        o_out = (lambda li: self.window.t["o_tag"][li]) if tagged else (lambda li: self.o_parts)
+        down_out = (lambda li: self.window.t["down_tag"][li]) if tagged else (lambda li: self.down_parts)
         pa_o, pa_down = tp * kp_o, tp * kp_down  # parts the next prologue sums, rank by rank
         self.kv_new = torch.zeros((2, nkv, D), dtype=BF16, device=dev)
         self.head_ctr = torch.zeros((cfg.num_layers, nkv), dtype=torch.int32, device=dev)
@@ -324,7 +339,7 @@ class DecodeEngine:
             if li == 0:
                 src = {"embed": w.embed, "token": self.token}
             else:
-                src = {"a": self.down_parts, "a_parts": pa_down, "b": self.resmid}
+                src = {"a": down_out(li - 1), "a_parts": pa_down, "b": self.resmid, "tagged": tagged}
             qkv = prog.gemv(wq, cfg.qkv_rows, h, ks=ks_qkv, gamma=lw.in_norm, eps=eps, res_out=self.res_attn,
                             epi=S.EPI_ROPE_KV, rowmap=S.ROWS_PAIR_HALF, head_dim=D, rope=rope, wait=prev,
                             rotary_dim=rots[li], gate=self.gate, **src)
@@ -334,20 +349,24 @@ class DecodeEngine:
                                  head_counters=self.head_ctr[li], attn_out=self.attn_out, nq=nq, nkv=nkv, head_dim=D,
                                  block_size=bs, wait=qkv, window=cfg.layer_window(li), gate=self.gate)
             if fused:  # o_proj behind the attention, K part = kv head, input in shared memory
-                o = prog.gemv(wo, h, nq * D, kp=kp_o, ks=ks_o, epi=S.EPI_PARTS, out=self.o_parts, wait=-1,
+                o = prog.gemv(wo, h, nq * D, kp=kp_o, ks=ks_o, epi=S.EPI_PARTS, out=o_out(li), wait=-1,
                               xchg=xchg, attn_splits=self.splits)
             else:
-                o = prog.gemv(wo, h, nq * D, kp=kp_o, ks=ks_o, a=self.attn_out, epi=S.EPI_PARTS, out=self.o_parts,
+                o = prog.gemv(wo, h, nq * D, kp=kp_o, ks=ks_o, a=self.attn_out, epi=S.EPI_PARTS, out=o_out(li),
                               wait=att, xchg=xchg)
-            gu = prog.gemv(wgu, 2 * i, h, ks=ks_gu, a=self.o_parts, a_parts=pa_o, b=self.res_attn,
+            # gate_up: with tagged parts its wait only orders the residual (written by qkv)
+            gu = prog.gemv(wgu, 2 * i, h, ks=ks_gu, a=o_out(li), a_parts=pa_o, b=self.res_attn,
                            gamma=lw.post_norm, eps=eps, res_out=self.resmid,
                            epi=S.EPI_GELU_MUL if self.gelu is not None else S.EPI_SILU_MUL,
-                           rowmap=S.ROWS_GATE_UP, out=self.mid, wait=o, table=self.gelu)
-            prev = prog.gemv(wd, h, i, kp=kp_down, ks=ks_down, a=self.mid, epi=S.EPI_PARTS, out=self.down_parts,
+                           rowmap=S.ROWS_GATE_UP, out=self.mid, wait=(qkv if tagged else o), table=self.gelu,
+                           tagged=tagged)
+            down = prog.gemv(wd, h, i, kp=kp_down, ks=ks_down, a=self.mid, epi=S.EPI_PARTS, out=down_out(li),
                              wait=gu, xchg=xchg)
-        prog.gemv(self.t16_head, cfg.vocab_size, h, ks=ks_head, a=self.down_parts, a_parts=pa_down, b=self.resmid,
-                  gamma=w.final_norm, eps=eps, epi=S.EPI_ARGMAX, out=self.logits, key=self.key, wait=prev,
-                  xchg=xchg, row0=getattr(w, "vocab_start", 0), q6=q6_head)
+            prev = gu if tagged else down  # what the next reader of the down parts waits on
+        prog.gemv(self.t16_head, cfg.vocab_size, h, ks=ks_head, a=down_out(cfg.num_layers - 1), a_parts=pa_down,
+                  b=self.resmid, gamma=w.final_norm, eps=eps, epi=S.EPI_ARGMAX, out=self.logits, key=self.key,
+                  wait=prev, xchg=S.XCHG_COUNTED if tp > 1 else S.XCHG_LOCAL, row0=getattr(w, "vocab_start", 0),
+                  q6=q6_head, tagged=tagged)
         prog.finalize(self.window.t["counters"] if self.window is not None else None)
         self.program = prog
         self._io = prog.io(error=self.error, key=self.key, token_out=self.token, token_log=self.token_log,
@@ -440,6 +459,9 @@ class DecodeEngine:
         if self.mode == "step":  # launch generation and head counters restart together
             self.program.reset_counters()
             self.head_ctr.zero_()
+            if self.window is not None and "o_tag" in self.window.t:  # tags restart with the launch count
+                self.window.t["o_tag"].zero_()
+                self.window.t["down_tag"].zero_()
         if self.tp_size > 1:
             self._tp_barrier()
 

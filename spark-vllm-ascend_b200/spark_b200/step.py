@@ -22,7 +22,8 @@ import torch
 from ._lib import SparkStage, SparkStepIO, call, lib
 
 STAGE_GEMV, STAGE_ATTN, STAGE_GEMV_Q6 = 0, 1, 2
-PRO_BF16, PRO_PARTS, PRO_ATTN = 0, 1, 2
+PRO_BF16, PRO_PARTS, PRO_ATTN, PRO_PARTS_TAGGED = 0, 1, 2, 3
+XCHG_LOCAL, XCHG_COUNTED, XCHG_TAGGED = 0, 1, 2
 EPI_BF16, EPI_PARTS, EPI_ROPE_KV, EPI_SILU_MUL, EPI_ARGMAX, EPI_GELU_MUL = range(6)
 ROWS_PLAIN, ROWS_PAIR_HALF, ROWS_GATE_UP = range(3)
 
@@ -116,10 +117,12 @@ class StepProgram:
     def gemv(self, w: torch.Tensor, n: int, k: int, *, kp: int = 1, ks: int = 1, a=None, a_parts: int = 0,
              embed=None, token=None, b=None, gamma=None, eps: float = 0.0, res_out=None, epi: int = EPI_BF16,
              rowmap: int = ROWS_PLAIN, out=None, wait: int = -1, head_dim: int = 0, key=None, rope=None,
-             xchg: bool = False, row0: int = 0, q6: bool = False, rotary_dim: int = 0, gate=None,
-             table=None, attn_splits: int = 0) -> int:
-        """``xchg``: tensor-parallel exchange stage (parts / argmax key written to every
-        rank's window, completion counted on every rank); ``row0``: global index of row 0
+             xchg: int = 0, row0: int = 0, q6: bool = False, rotary_dim: int = 0, gate=None,
+             table=None, attn_splits: int = 0, tagged: bool = False) -> int:
+        """``xchg``: tensor-parallel exchange stage: XCHG_COUNTED (parts / argmax key
+        written to every rank's window, completion counted on every rank) or XCHG_TAGGED
+        (parts as tagged 64-bit words, not counted); ``tagged``: ``a`` holds tagged parts
+        (``PRO_PARTS_TAGGED``, read once their tags are this launch's); ``row0``: global index of row 0
         for the argmax (vocab shard start); ``q6``: ``w`` holds Q6_K weights in the T6 layout
         (``q6k_pack_t6``); slices then count 32-weight tiles.  Spark layer features:
         ``rotary_dim`` (partial RoPE) and ``gate`` (bf16 [nq], computed from the gate rows
@@ -129,7 +132,7 @@ class StepProgram:
         memory, units assigned by head group; ``wait`` must be -1)."""
         s = SparkStage()
         s.kind, s.epi, s.rowmap = (STAGE_GEMV_Q6 if q6 else STAGE_GEMV), epi, rowmap
-        s.pro = PRO_ATTN if attn_splits else (PRO_PARTS if a_parts else PRO_BF16)
+        s.pro = PRO_ATTN if attn_splits else ((PRO_PARTS_TAGGED if tagged else PRO_PARTS) if a_parts else PRO_BF16)
         s.splits = attn_splits
         s.n, s.k, s.kp, s.ks = n, k, kp, ks
         s.units = n // 16 * kp
@@ -141,7 +144,7 @@ class StepProgram:
         s.eps = eps
         s.inv_k = float(torch.tensor(1.0 / k, dtype=torch.float32))
         s.head_dim = head_dim
-        s.xchg, s.row0 = int(bool(xchg)), row0
+        s.xchg, s.row0 = int(xchg), row0
         s.rotary_dim, s.gate, s.table = rotary_dim, _p(gate), _p(table)
         s.w, s.a, s.b, s.embed, s.token = _p(w), _p(a), _p(b), _p(embed), _p(token)
         s.gamma, s.res_out, s.out, s.key = _p(gamma), _p(res_out), _p(out), _p(key)

@@ -217,11 +217,18 @@ class ShardWeights:
         return sum(l.qkv.nbytes() + l.o.nbytes() + l.gate_up.nbytes() + l.down.nbytes() for l in self.layers) + head
 
 
-def window_fields(cfg_local: SparkConfig, order: dict, num_stages: int, tp: int) -> list:
-    h = cfg_local.hidden_size
+def window_fields(cfg_local: SparkConfig, order: dict, num_stages: int, tp: int, tagged: bool = False) -> list:
+    """What the peers write into a rank's window: the stage counters, the argmax key and
+    the o_proj / down parts of every rank -- counted exchange: fp32 [tp * kp][h], one
+    buffer for all layers; tagged exchange: int64 [layers][tp * kp][h] words (fp32 bits |
+    launch tag << 32), one buffer per layer so a word is written once per launch and its
+    tag names the launch."""
+    h, L = cfg_local.hidden_size, cfg_local.num_layers
     kp_o, kp_down = order["kp_local"]
-    return [("counters", (num_stages + 3,), torch.int32), ("key", (1,), torch.int64),
-            ("o_parts", (tp * kp_o, h), torch.float32), ("down_parts", (tp * kp_down, h), torch.float32)]
+    fields = [("counters", (num_stages + 3,), torch.int32), ("key", (1,), torch.int64)]
+    if tagged:
+        return fields + [("o_tag", (L, tp * kp_o, h), torch.int64), ("down_tag", (L, tp * kp_down, h), torch.int64)]
+    return fields + [("o_parts", (tp * kp_o, h), torch.float32), ("down_parts", (tp * kp_down, h), torch.float32)]
 
 
 def program_stages(num_layers: int) -> int:

@@ -56,6 +56,18 @@ def test_tp_kv8_64_tokens_match_oracle(cuda, world):
     assert r0["oracle_tokens_equal"] and r0["oracle_logits_equal"]
 
 
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_tagged_exchange_matches_oracle(cuda, world):
+    """The tagged exchange (o_proj / down parts as 64-bit words carrying the launch number,
+    read once the tags match; no fence, no counter): the same tokens and logits."""
+    if _gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
+    res = _run(world, "--config", "kv8", "--new-tokens", "32", "--prompt", "20", "--exchange", "tagged")
+    assert len(res) == world and all(r["ok"] for r in res), res
+    r0 = next(r for r in res if r["rank"] == 0)
+    assert r0["oracle_tokens_equal"] and r0["oracle_logits_equal"]
+
+
 @pytest.mark.parametrize("world", [2])
 def test_tp_spark_tiny_matches_oracle(cuda, world):
     """The Spark architecture over 2 ranks (gate rows and the Q6_K head sharded with the

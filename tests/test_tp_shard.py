@@ -121,11 +121,17 @@ def test_window_layout_aligned():
     from spark_b200.config import SparkConfig
     from spark_b200 import step
     cfg = T.local_config(SparkConfig(), 2)
-    order = step.default_order(cfg, 148, 2)
+    order = step.default_order(cfg, 148, 2, step.attn_splits(cfg, 148, 4096))
     fields = T.window_fields(cfg, order, T.program_stages(cfg.num_layers), 2)
     off, total = T.window_layout(fields)
     assert all(v % 256 == 0 for v in off.values())
     assert off["counters"] == 0 and total >= off["down_parts"] + 4 * 2 * order["kp_local"][1] * cfg.hidden_size
+    # tagged exchange: per-layer words (8 bytes) of o_proj and down, every rank's parts
+    off, total = T.window_layout(T.window_fields(cfg, order, T.program_stages(cfg.num_layers), 2, tagged=True))
+    L, h = cfg.num_layers, cfg.hidden_size
+    assert all(v % 256 == 0 for v in off.values()) and off["counters"] == 0
+    assert off["down_tag"] >= off["o_tag"] + 8 * L * 2 * order["kp_local"][0] * h
+    assert total >= off["down_tag"] + 8 * L * 2 * order["kp_local"][1] * h
 
 
 def _gather_worker(rank, world, port, q):

@@ -40,6 +40,8 @@ def main(argv=None):
     ap.add_argument("--max-seq", type=int, default=256)
     ap.add_argument("--seed", type=int, default=1)
     ap.add_argument("--no-oracle", action="store_true")
+    ap.add_argument("--exchange", choices=["counted", "tagged"], default="counted",
+                    help="how o_proj / down parts cross the ranks (DecodeEngine tp_exchange)")
     ap.add_argument("--trace-ctx", type=int, default=0,
                     help="after the parity run: rewind to this context, time 20 steps, then trace one step "
                          "(per-stage timeline of rank 0, as spark_b200.step_trace prints it)")
@@ -69,7 +71,7 @@ def main(argv=None):
     host_weights = full.to_numpy() if rank == 0 and not args.no_oracle else None
     del full
     eng = DecodeEngine(shard, max_seq_len=args.max_seq, num_blocks=4 * ((args.max_seq + 127) // 128),
-                       seed=args.seed, mode="step")
+                       seed=args.seed, mode="step", tp_exchange=args.exchange)
     rng = np.random.default_rng(args.seed)
     prompt = rng.integers(0, cfg.vocab_size, args.prompt).astype(np.int32)
     toks = eng.generate(torch.from_numpy(prompt), args.new_tokens)
