@@ -412,6 +412,125 @@ def run_spark(args):
     return result
 
 
+def run_spark_batch(args):
+    """configs[4]'s small-batch decode: B sequences (``--batch``) of the synthetic 4B model
+    through one persistent launch per step (``spark_b200.batch``), one GPU.  Each sequence
+    gets its own prompt of ``--prompt`` random ids (batched prefill, timed as the TTFT of
+    the B prompts), then the K timed steps advance every sequence by one token; ``value``
+    = B x K tokens / time.  e2e: the B tokens go host -> device and back every step."""
+    import torch
+    world, rank, local = dist_setup()
+    if world > 1:
+        raise SystemExit("--batch runs on one GPU")
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    from spark_b200.batch import BatchDecodeEngine
+    from spark_b200.config import SparkConfig
+    from spark_b200.model import SyntheticWeights
+    B = args.batch
+    cfg = SparkConfig(num_layers=args.layers)
+    w = SyntheticWeights(cfg, device=device, seed=0)
+    max_seq = PROMPT_LEN + max(args.steps, args.warmup) + 1
+    eng = BatchDecodeEngine(w, B, max_seq_len=max_seq, splits=args.splits, seed=0,
+                            max_steps=max(max_seq, args.steps + args.warmup + 8))
+    gen = torch.Generator().manual_seed(1234)
+    prompts = [torch.randint(0, cfg.vocab_size, (PROMPT_LEN,), generator=gen, dtype=torch.int32) for _ in range(B)]
+    eng.capture()
+    eng.prefill(prompts[:1] * B)  # (warm: cuBLAS handles, the bf16 weights)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    first = eng.prefill(prompts)
+    e1.record()
+    torch.cuda.synchronize()
+    ttft = e0.elapsed_time(e1)
+    eng._prefill_w = None  # the bf16 prefill weights (4.5 GB) are not needed to decode
+    torch.cuda.empty_cache()
+    saved = first.clone()
+    eng.step_idx.zero_()
+    for _ in range(args.warmup):
+        eng.step()
+    torch.cuda.synchronize()
+
+    def rewind():
+        eng.pos.fill_(PROMPT_LEN)
+        eng.step_idx.zero_()
+        eng.key.zero_()
+        eng.token.copy_(saved)
+        torch.cuda.synchronize()
+
+    rewind()
+    sampler = ClockSampler(device.index if device.index is not None else 0)
+    sampler.start()
+    time.sleep(0.4)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("timed")
+    e0.record()
+    for _ in range(args.steps):
+        eng.graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_pop()
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1)
+    assert int(eng.error.item()) == 0, "batch step reported an error"
+    tokens_timed = eng.token_log[:args.steps].cpu()
+    rewind()
+    tok_host = torch.empty(B, dtype=torch.int32, pin_memory=True)
+    out_host = torch.empty(B, dtype=torch.int32, pin_memory=True)
+    tok_host.copy_(saved.cpu())
+    torch.cuda.synchronize()
+    x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    x0.record()
+    for _ in range(args.steps):
+        eng.token.copy_(tok_host, non_blocking=True)
+        eng.graph.replay()
+        out_host.copy_(eng.token, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        tok_host.copy_(out_host)
+    x1.record()
+    torch.cuda.synchronize()
+    e2e_ms = x0.elapsed_time(x1)
+    e2e_match = bool(torch.equal(eng.token_log[:args.steps].cpu(), tokens_timed))
+    peak, peak_kind = _peaks()
+    ctx_mid = PROMPT_LEN + args.steps // 2
+    tpot = ms / args.steps
+    step_bytes = w.q4_bytes() + B * (cfg.hidden_size * 2 + cfg.kv_bytes_at(ctx_mid))
+    achieved = step_bytes / (tpot * 1e-3) / 1e9
+    return {
+        "metric": f"batch-{B} decode tokens/s (synthetic 4B Q4_0, ctx {PROMPT_LEN}->{PROMPT_LEN}+K)",
+        "value": round(args.steps * B / (ms / 1e3), 3),
+        "unit": "tokens/s",
+        "n_gpus": 1,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(tpot, 5),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "q4_0 weights x fp32 accumulate, bf16 activations / KV",
+        "data": f"synthetic: seeded N(0,0.02) weights -> Q4_0, {B} prompts of {PROMPT_LEN} uniform-random ids",
+        "config": {"workload": f"configs[4]: synthetic 4B Q4_0, batch {B}, context {PROMPT_LEN}, greedy",
+                   "model": cfg.name, "layers": cfg.num_layers, "hidden": cfg.hidden_size, "vocab": cfg.vocab_size,
+                   "batch": B, "prompt": PROMPT_LEN, "ctx_range": [PROMPT_LEN, PROMPT_LEN + args.steps - 1],
+                   "splits": eng.splits, "parallelism": "none (one GPU, B sequences per launch)",
+                   "kernels_per_step": 1, "mode": "step",
+                   "l2": f"inputs larger than L2 ({step_bytes / 1e9:.2f} GB per step)"},
+        "e2e": {"value": round(args.steps * B / (e2e_ms / 1e3), 3), "unit": "tokens/s",
+                "h2d_bytes_per_step": 4 * B, "d2h_bytes_per_step": 4 * B, "tokens_match_device_loop": e2e_match},
+        "prefill": {"tokens": PROMPT_LEN * B, "ttft_ms": round(ttft, 3),
+                    "method": "batched per sequence: dequantized bf16 GEMMs + causal SDPA"},
+        "gpu_launches": args.steps,
+        "roofline": {"bound": "hbm", "kernel": "step", "achieved": round(achieved, 1), "peak": peak,
+                     "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                     "bytes_per_launch": step_bytes, "us_per_launch": round(tpot * 1e3, 3), "traffic": None,
+                     "traffic_source": "no ncu capture of the batch kernels yet"},
+        "clocks": clocks,
+        "cpu_baseline": None,
+    }
+
+
 def run_reference(args):
     """The reference's CPU implementation of the path, timed on the host cores.
 
@@ -515,6 +634,8 @@ def main(argv=None):
                          "architecture with synthetic weights")
     ap.add_argument("--layers", type=int, default=36,
                     help="decoder layers (36 = the benchmark model; fewer only for small profiling captures)")
+    ap.add_argument("--batch", type=int, default=1, choices=[1, 2, 4, 8],
+                    help="sequences decoded together on one GPU (configs[4]; 1 = the batch-1 benchmark)")
     args = ap.parse_args(argv)
     if args.tp == 0:  # the multi-GPU bench measures tensor parallelism, not replicas
         args.tp = int(os.environ.get("WORLD_SIZE", "1"))
@@ -522,7 +643,10 @@ def main(argv=None):
     PROMPT_LEN = args.prompt
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
-    res = run_reference(args) if args.impl == "reference" else run_spark(args)
+    if args.impl == "reference":
+        res = run_reference(args)
+    else:
+        res = run_spark_batch(args) if args.batch > 1 else run_spark(args)
     if res is not None:
         print(json.dumps(res), flush=True)
 

@@ -341,6 +341,18 @@ typedef struct SparkStage {
                                  gate rows (rows (nq + 2 nkv) head_dim + h, h < nq, padded to 16 rows):
                                  bf16(1 / (1 + exp(-bf16(logit)))); SPARK_STAGE_ATTN multiplies head h's
                                  combined output by it: bf16(bf16(o) * gate[h]) */
+  /* Small-batch decode: B sequences through one launch (the weights stream once, each
+   * integer MMA of a Q4_0 block multiplies the B sequences' digit columns together). */
+  int32_t batch;              /* B: 0 or 1 = one sequence; 2, 4 or 8, the same in every stage of a program.
+                                 Every per-sequence buffer then holds B copies of its one-sequence layout,
+                                 sequence-major: a, b, res_out, out (SPARK_EPI_PARTS: [B][kp][n]), q,
+                                 kv_new, part_o, part_lse, head_counters and attn_out hold sequence s at
+                                 s times their one-sequence size; token, pos and key hold B entries.
+                                 Each sequence's result is bit-identical to decoding it alone with the
+                                 same program.  Not combined with tensor parallelism, Q6_K stages, the
+                                 Spark features or SPARK_PRO_ATTN; ks <= 2 */
+  int32_t bt_stride;          /* batch > 1: block_table is int32 [B][bt_stride] (sequence s's logical ->
+                                 physical blocks at s * bt_stride) */
 } SparkStage;
 
 typedef struct SparkStepIO {
@@ -348,11 +360,11 @@ typedef struct SparkStepIO {
                                  the first num_stages + 2 zero between launches and counts launches in
                                  the last (the attention stages' head counters follow that count) */
   int32_t* error;             /* int32 [1] status written on a timed-out wait (nullable) */
-  unsigned long long* key;    /* after the last stage: token = argmax of key (nullable) */
-  int32_t* token_out;
-  int32_t* token_log;         /* token_log[*step] = token (nullable) */
+  unsigned long long* key;    /* [B] after the last stage: token = argmax of key (nullable) */
+  int32_t* token_out;         /* [B] (B = the last stage's batch) */
+  int32_t* token_log;         /* token_log[*step * B + s] = sequence s's token (nullable) */
   int32_t* step;              /* incremented (nullable) */
-  int64_t* pos;               /* incremented (nullable) */
+  int64_t* pos;               /* [B], each incremented (nullable) */
   unsigned long long* trace;  /* optional uint64 [ctas][num_stages][8] globaltimer stamps (ns): consumer
                                  wait start, work start, work end, producer's first copy of the stage,
                                  then stage checkpoints (GEMV: tasks start, tasks end; attention:
@@ -392,8 +404,11 @@ int64_t spark_t6_bytes(int n, int k);
 int spark_q6k_pack_t6(const uint8_t* blocks, int n, int k, int kp, uint8_t* out, void* stream);
 int spark_q6k_dequantize(const uint8_t* blocks, int64_t nblocks, float* out, void* stream);
 
-/* Shared memory the step kernel keeps for the weight / KV ring (bytes). */
+/* Shared memory the step kernel keeps for the weight / KV ring (bytes), one sequence. */
 int spark_step_ring_bytes(void);
+
+/* The same for a program of batch B (1, 2, 4 or 8); 0 for another B. */
+int spark_step_ring_bytes_batch(int batch);
 
 /* Number of CTAs (one per SM) the step kernel runs with on the current device. */
 int spark_step_num_ctas(void);

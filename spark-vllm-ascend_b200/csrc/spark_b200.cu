@@ -707,10 +707,54 @@ int spark_q6k_dequantize(const uint8_t* blocks, int64_t nblocks, float* out, voi
 
 int spark_step_ring_bytes(void) { return step::kRingBytes; }
 
+int spark_step_ring_bytes_batch(int batch) {
+  switch (batch) {
+    case 1: return step::Layout<1>::ring;
+    case 2: return step::Layout<2>::ring;
+    case 4: return step::Layout<4>::ring;
+    case 8: return step::Layout<8>::ring;
+    default: return 0;
+  }
+}
+
+static int batch_scratch(int nb) {
+  return nb == 2 ? step::Layout<2>::scratch : nb == 4 ? step::Layout<4>::scratch : step::Layout<8>::scratch;
+}
+
+// a stage of a batch program (batch 2, 4 or 8): the subset of the stage forms the batch
+// kernels carry, and the shared-memory sizes of NB staged inputs
+static int check_batch_stage(const SparkStage& s, int ncta) {
+  const int nb = s.batch;
+  if (nb != 2 && nb != 4 && nb != 8) return SPARK_ERR_UNSUPPORTED_SHAPE;
+  if (s.xchg || s.gate || s.window || s.table) return SPARK_ERR_UNSUPPORTED_SHAPE;
+  if (s.kind == SPARK_STAGE_ATTN) {
+    if (s.head_dim != 128 || s.bt_stride <= 0) return SPARK_ERR_UNSUPPORTED_SHAPE;
+    return SPARK_OK;
+  }
+  if (s.kind != SPARK_STAGE_GEMV) return SPARK_ERR_UNSUPPORTED_SHAPE;
+  if (s.pro != SPARK_PRO_BF16 && (s.pro != SPARK_PRO_PARTS || !s.norm)) return SPARK_ERR_UNSUPPORTED_SHAPE;
+  if (s.epi == SPARK_EPI_GELU_MUL || s.ks > 2) return SPARK_ERR_UNSUPPORTED_SHAPE;
+  if (s.epi == SPARK_EPI_ROPE_KV &&
+      (s.head_dim != 128 || (s.rotary_dim && s.rotary_dim != 128) || s.bt_stride <= 0))
+    return SPARK_ERR_UNSUPPORTED_SHAPE;
+  const int ring = spark_step_ring_bytes_batch(nb), scratch = batch_scratch(nb);
+  if (9 * (s.k / s.kp) > ring) return SPARK_ERR_TOO_LARGE;
+  if (s.norm) {  // fp32 pre-norm vectors + gamma; items per thread
+    if ((int64_t)4 * s.k * nb + 2 * s.k > scratch) return SPARK_ERR_TOO_LARGE;
+    if ((int64_t)nb * (s.k / 8) > (int64_t)step::kBatchItems * step::kConsumers) return SPARK_ERR_TOO_LARGE;
+  } else {
+    const bool part_x = s.kp > 1 && ncta % s.kp == 0;
+    const int kx = part_x ? s.k / s.kp : s.k;
+    if ((int64_t)72 * (kx / 32) * nb > scratch) return SPARK_ERR_TOO_LARGE;
+  }
+  return SPARK_OK;
+}
+
 int spark_step_num_ctas(void) { return num_sms(); }
 
 static int check_stage(const SparkStage& s, int i, int ncta) {
   if (s.wait >= i || s.wait < -1) return SPARK_ERR_INVALID_ARG;
+  if (s.batch < 0 || s.bt_stride < 0) return SPARK_ERR_INVALID_ARG;
   if (s.kind == SPARK_STAGE_GEMV_Q6) {  // Q6_K weights: plain rows, whole super-blocks per part
     if (s.k <= 0 || s.kp <= 0 || s.k % s.kp || (s.k / s.kp) % 256 || s.rowmap != SPARK_ROWS_PLAIN)
       return SPARK_ERR_UNSUPPORTED_SHAPE;
@@ -729,17 +773,19 @@ static int check_stage(const SparkStage& s, int i, int ncta) {
       return SPARK_ERR_INVALID_ARG;
     if (s.xchg == SPARK_XCHG_TAGGED && s.epi != SPARK_EPI_PARTS) return SPARK_ERR_INVALID_ARG;
     if (s.pro == SPARK_PRO_PARTS_TAGGED && (reinterpret_cast<uintptr_t>(s.a) & 15)) return SPARK_ERR_ALIGNMENT;
-    if (s.kind == SPARK_STAGE_GEMV && 9 * (s.k / s.kp) > step::kRingBytes) return SPARK_ERR_TOO_LARGE;
+    if (s.batch <= 1) {  // (batch programs: check_batch_stage)
+      if (s.kind == SPARK_STAGE_GEMV && 9 * (s.k / s.kp) > step::kRingBytes) return SPARK_ERR_TOO_LARGE;
+      if (72 * (s.k / 32) + (s.norm ? 6 * s.k : 0) > step::kScratchBytes) return SPARK_ERR_TOO_LARGE;
+    }
     if (s.ks > step::kMaxSlices) return SPARK_ERR_UNSUPPORTED_SHAPE;
-    if (72 * (s.k / 32) + (s.norm ? 6 * s.k : 0) > step::kScratchBytes) return SPARK_ERR_TOO_LARGE;
     if (s.norm && (reinterpret_cast<uintptr_t>(s.gamma) & 15)) return SPARK_ERR_ALIGNMENT;
-    if (s.k > step::kStageGroups * step::kConsumers * 8) return SPARK_ERR_TOO_LARGE;
+    if (s.batch <= 1 && s.k > step::kStageGroups * step::kConsumers * 8) return SPARK_ERR_TOO_LARGE;
     if ((reinterpret_cast<uintptr_t>(s.a) | reinterpret_cast<uintptr_t>(s.b) | reinterpret_cast<uintptr_t>(s.embed) |
          reinterpret_cast<uintptr_t>(s.gamma) | reinterpret_cast<uintptr_t>(s.res_out)) & 15)
       return SPARK_ERR_ALIGNMENT;
     if (s.pro == SPARK_PRO_PARTS || s.pro == SPARK_PRO_PARTS_TAGGED) {
       if (s.a_parts <= 0 || s.a_parts > step::kMaxParts || !s.a || s.embed) return SPARK_ERR_INVALID_ARG;
-      if (s.k > step::kConsumers * 8) return SPARK_ERR_TOO_LARGE;  // one 8-element group per thread
+      if (s.batch <= 1 && s.k > step::kConsumers * 8) return SPARK_ERR_TOO_LARGE;  // one 8-element group per thread
     } else if (s.pro == SPARK_PRO_ATTN) {
       if (s.kind != SPARK_STAGE_GEMV || s.norm || s.embed || s.wait != -1) return SPARK_ERR_INVALID_ARG;
       if (s.splits <= 0 || (int64_t)s.kp * s.splits > ncta) return SPARK_ERR_INVALID_ARG;
@@ -888,6 +934,16 @@ int spark_step_run(const SparkStage* host_stages, const SparkStage* dev_stages, 
     const int st = check_stage(host_stages[i], i, ncta);
     if (st != SPARK_OK) return st;
   }
+  // batch: one B for the whole program, not tensor parallel, the batch kernels' stage forms
+  const int nb = host_stages[0].batch > 1 ? host_stages[0].batch : 1;
+  for (int i = 0; i < num_stages; i++) {
+    if ((host_stages[i].batch > 1 ? host_stages[i].batch : 1) != nb) return SPARK_ERR_INVALID_ARG;
+    if (nb > 1) {
+      if (io->tp_size > 1 || host_stages[i].pro == SPARK_PRO_ATTN) return SPARK_ERR_UNSUPPORTED_SHAPE;
+      const int st = check_batch_stage(host_stages[i], ncta);
+      if (st != SPARK_OK) return st;
+    }
+  }
   for (int i = 0; i < num_stages; i++)  // a tagged exchange stage is not counted: nothing may wait on it
     if (host_stages[i].xchg == SPARK_XCHG_TAGGED)
       for (int j = i + 1; j < num_stages; j++)
@@ -939,8 +995,13 @@ int spark_step_run(const SparkStage* host_stages, const SparkStage* dev_stages, 
       step::step_kernel<false, true, false, true>,   step::step_kernel<false, true, true, true>,
       step::step_kernel<true, false, false, true>,   step::step_kernel<true, false, true, true>,
       step::step_kernel<true, true, false, true>,    step::step_kernel<true, true, true, true>};
+  // batch programs: one instantiation per B (any number of attention tasks)
+  static const Kernel batch_kernels[3] = {step::step_kernel<false, true, false, false, 2>,
+                                          step::step_kernel<false, true, false, false, 4>,
+                                          step::step_kernel<false, true, false, false, 8>};
   const bool tp = io->tp_size > 1;
-  const Kernel kernel = kernels[8 * tp + 4 * q6 + 2 * multi + spark];
+  const Kernel kernel =
+      nb > 1 ? batch_kernels[nb == 2 ? 0 : (nb == 4 ? 1 : 2)] : kernels[8 * tp + 4 * q6 + 2 * multi + spark];
   if (set_smem(reinterpret_cast<const void*>(kernel), step::kSmemBytes) != kOk) return kErrLaunch;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(ncta);

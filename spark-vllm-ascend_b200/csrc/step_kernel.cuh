@@ -51,6 +51,22 @@ constexpr unsigned long long kWaitNs = 2000000000ull;
 
 static_assert(kRingBytes % 16 == 0, "ring alignment");
 
+// Shared-memory budget of a batch-NB program (NB = 1: the constants above).  A batch
+// stage stages NB input vectors: NB x 72 B per 32-element block of digits / meta, and for
+// an RMSNorm prologue the NB pre-norm vectors in fp32 (4 k NB bytes, reused by the digits)
+// plus gamma; its slice sums are NB x 16 per slice (ks <= 2); the per-sequence launch
+// constants (position, cache row, RoPE row) sit in the misc area.
+template <int NB>
+struct Layout {
+  static constexpr int scratch = NB == 1 ? kScratchBytes : (NB == 2 ? 40 * 1024 : (NB == 4 ? 48 * 1024 : 88 * 1024));
+  static constexpr int slices = NB == 1 ? kMaxSlices : 2;
+  static constexpr int partial = kDesc * slices * 16 * 4 * NB;
+  static constexpr int misc = NB == 1 ? kMiscBytes : 4608;
+  static constexpr int ring = kSmemBytes - scratch - partial - misc;
+  static_assert(ring % 16 == 0 && ring >= 96 * 1024, "ring");
+};
+static_assert(Layout<1>::ring == kRingBytes, "one-sequence layout");
+
 // ------------------------------------------------------------------ small helpers
 __device__ __forceinline__ unsigned long long gtimer() {
   unsigned long long t;
@@ -179,15 +195,19 @@ struct Smem {
   unsigned long long* red64;  // [16]
   SparkStage* stage;          // consumers' copy of the current stage
   long long* misc64;          // [4] per-stage values (position, cache row offset)
-  uint16_t* rope_cs;          // [256] cos | sin row of the position (RoPE stages)
+  uint16_t* rope_cs;          // [256] cos | sin row of the position (RoPE stages); batch: [NB][128]
+  long long* bpos;            // batch: [NB] positions
+  long long* bkvoff;          // batch: [NB] paged-cache element offsets of the decoded tokens
 };
 
+template <int NB>
 __device__ __forceinline__ Smem carve(unsigned char* base) {
+  using L = Layout<NB>;
   Smem s;
   s.ring = base;
-  s.scratch = base + kRingBytes;
-  s.partial = reinterpret_cast<float*>(base + kRingBytes + kScratchBytes);
-  unsigned char* m = base + kRingBytes + kScratchBytes + kPartialBytes;
+  s.scratch = base + L::ring;
+  s.partial = reinterpret_cast<float*>(base + L::ring + L::scratch);
+  unsigned char* m = base + L::ring + L::scratch + L::partial;
   s.full = reinterpret_cast<unsigned long long*>(m);
   s.empty = s.full + kDesc;
   s.desc_off = reinterpret_cast<uint32_t*>(s.empty + kDesc);
@@ -199,14 +219,17 @@ __device__ __forceinline__ Smem carve(unsigned char* base) {
   s.flag = reinterpret_cast<int*>(s.prod_end + kDesc) + 4;
   s.red = reinterpret_cast<float*>(s.flag + 4);
   s.red64 = reinterpret_cast<unsigned long long*>(s.red + 64);
-  s.stage = reinterpret_cast<SparkStage*>(s.red64 + 16);
+  s.stage = reinterpret_cast<SparkStage*>(s.red64 + 16 * NB);
   s.misc64 = reinterpret_cast<long long*>(s.stage + 1);
   s.rope_cs = reinterpret_cast<uint16_t*>(s.misc64 + 4);
+  s.bpos = reinterpret_cast<long long*>(s.rope_cs + (NB == 1 ? 256 : 128 * NB));
+  s.bkvoff = s.bpos + NB;
   return s;
 }
 // full 128 + empty 128 + desc_off / desc_seq / done / prod_start / prod_end 5 x 64 + abort / flag 32 +
-// red 256 + red64 128 + stage 280 + misc64 32 + rope_cs 512 = 1816 <= kMiscBytes
-static_assert(sizeof(SparkStage) == 280, "SparkStage layout");
+// red 256 + red64 128 NB + stage 288 + misc64 32 + rope_cs 512 (batch: 256 NB) + bpos / bkvoff 16 NB:
+// 1824 (NB = 1) <= kMiscBytes, 4480 (NB = 8) <= Layout<8>::misc
+static_assert(sizeof(SparkStage) == 288, "SparkStage layout");
 constexpr int kStageWords = (int)sizeof(SparkStage) / 8;
 
 struct StepParams {
@@ -246,6 +269,8 @@ __device__ __forceinline__ void raise_abort(const StepParams& P, const Smem& s, 
 }
 
 // ------------------------------------------------------------------ producer
+// NB: the program's batch (ring size; attention tasks of NB sequences)
+template <int NB>
 struct Producer {
   const StepParams& P;
   const Smem& s;
@@ -258,7 +283,7 @@ struct Producer {
   __device__ bool issue(const void* src, uint32_t bytes) {
     if (*s.abort_flag) return false;
     uint32_t a = head;
-    if (a + bytes > (uint32_t)kRingBytes) a = 0;
+    if (a + bytes > (uint32_t)Layout<NB>::ring) a = 0;
     while (tail < seq) {
       if (seq - tail < (uint32_t)kDesc) {
         const uint32_t t = tail_off;
@@ -303,26 +328,29 @@ struct Producer {
           if (!issue(src, ub)) return drain();
         }
       } else {
-        // this CTA's tasks (kv head g, split j) in the consumers' order: K then V runs each
-        const int S = st.splits, ntask = st.nkv * S;
-        const int64_t len = st.pos[0] + 1;
-        // (Spark sliding window: splits from the window start rounded down to 16)
-        const int64_t start = (Spark && st.window > 0 && len > st.window ? len - st.window : 0) & ~(int64_t)15;
-        const int T = split_len(len - start, S);
-        if (T > kMaxSplitTokens) return drain();
+        // this CTA's tasks (sequence b, kv head g, split j) in the consumers' order: K then V
+        // runs each
+        const int S = st.splits, ntask = NB * st.nkv * S;
         // K then V runs of task t; false: aborted
         auto task = [&](int t) -> bool {
-          const int g = t / S, j = t - g * S;
+          const int b = NB == 1 ? 0 : t / (st.nkv * S), tb = t - b * st.nkv * S;
+          const int g = tb / S, j = tb - g * S;
+          const int64_t len = st.pos[b] + 1;
+          // (Spark sliding window: splits from the window start rounded down to 16)
+          const int64_t start = (Spark && st.window > 0 && len > st.window ? len - st.window : 0) & ~(int64_t)15;
+          const int T = split_len(len - start, S);
+          if (T > kMaxSplitTokens) return false;
           const int64_t t0 = start + (int64_t)j * T, t1 = t0 + T < len ? t0 + T : len;
           if (t1 <= t0) return true;
           const int64_t w0 = t0 / kRunTokens, nruns = (t1 - 1) / kRunTokens - w0 + 1;
           const int D = st.head_dim, bs = st.block_size, nkv = st.nkv;
+          const int32_t* table = st.block_table + (NB == 1 ? 0 : (size_t)b * st.bt_stride);
           for (int side = 0; side < 2; side++) {
             const uint16_t* cache = static_cast<const uint16_t*>(side ? st.v_cache : st.k_cache);
             for (int64_t r = 0; r < nruns; r++) {
               const int64_t rs = (w0 + r) * kRunTokens > t0 ? (w0 + r) * kRunTokens : t0;
               const int64_t re = (w0 + r + 1) * kRunTokens < t1 ? (w0 + r + 1) * kRunTokens : t1;
-              const int64_t page = st.block_table[rs / bs];
+              const int64_t page = table[rs / bs];
               const uint16_t* src = cache + ((page * nkv + g) * bs + (rs % bs)) * D;
               if (!issue(src, (uint32_t)((re - rs) * D * 2))) return false;
             }
@@ -403,8 +431,10 @@ __device__ __forceinline__ uint32_t pack_bytes(int x0, int x1, int x2, int x3) {
 // stage the 8 elements of group g (block g / 4, elements 8 (g % 4) ..); the 4 lanes of a
 // block are consecutive lanes of one warp and all execute this (valid or not)
 // xmeta2 (nullable, Q6_K stages): (-32 sum of X over elements 0..15, over 16..31)
+// bs: records between consecutive blocks (a batch of NB sequences interleaves its
+// sequences' records: block b of sequence q at record b NB + q)
 __device__ __forceinline__ void stage_group(const float (&v)[8], bool valid, int g, uint32_t* xfrag32, int2* xmeta,
-                                            int2* xmeta2 = nullptr) {
+                                            int2* xmeta2 = nullptr, int bs = 1) {
   float M = 0.0f;
 #pragma unroll
   for (int j = 0; j < 8; j++) M = fmaxf(M, fabsf(v[j]));
@@ -437,13 +467,14 @@ __device__ __forceinline__ void stage_group(const float (&v)[8], bool valid, int
     const uint32_t hh = pack_bytes(hv[0], hv[1], hv[2], hv[3]);
     const uint32_t ll = pack_bytes(lv[0], lv[1], lv[2], lv[3]);
     const int word = 2 * c + w;  // k = 4 word .. 4 word + 3
-    xfrag32[(b * 8 + (word & 3)) * 2 + (word >> 2)] = hh;
-    xfrag32[(b * 8 + 4 + (word & 3)) * 2 + (word >> 2)] = ll;
+    xfrag32[(b * bs * 8 + (word & 3)) * 2 + (word >> 2)] = hh;
+    xfrag32[(b * bs * 8 + 4 + (word & 3)) * 2 + (word >> 2)] = ll;
   }
   // meta.x = -8 sum X + kMagic: the MMA's column-1 accumulator input, so that
   // 256 D0 + D1 = P + kMagic is P as the low mantissa bits of 1.5 * 2^23 (|P| < 2^22)
   if (c == 0)
-    xmeta[b] = make_int2(-8 * sum + kMagic, __float_as_int(live ? __uint_as_float((uint32_t)(127 - S) << 23) : 1.0f));
+    xmeta[b * bs] =
+        make_int2(-8 * sum + kMagic, __float_as_int(live ? __uint_as_float((uint32_t)(127 - S) << 23) : 1.0f));
 }
 
 // group handled by slot gi of this CTA (out-of-range slots stay out of range)
@@ -668,6 +699,208 @@ __device__ __forceinline__ void stage_x(const StepParams& P, const SparkStage& s
   }
 }
 
+
+// ------------------------------------------------------------------ batch x staging
+// A batch-NB stage stages the NB sequences' input vectors with the arithmetic of stage_x,
+// sequence by sequence the same (the RMSNorm's canonical order included), so each
+// sequence's digits equal those of its one-sequence launch.  Work items are (sequence q,
+// 8-element group g), item q ngrp + g, spread over the consumer threads from a rotated
+// start as in stage_x.  Block b of sequence q lands at record b NB + q (stage_group's
+// block stride), so the 4 blocks x NB sequences of a block group are one contiguous run.
+// Norm stages keep the pre-norm values in fp32 in the scratch ([NB][k], the digits reuse
+// it afterwards); warp q sums sequence q's squares.
+constexpr int kBatchItems = 8;  // items per thread (NB k / 8 <= 8 x 352: k <= 2816 at NB = 8)
+
+// the pre-norm values of item (q, g): the bf16 input (or the embedding row of token[q]),
+// plus the residual b of a norm stage
+__device__ __forceinline__ void batch_load_bf16(const SparkStage& st, int q, int g, int x0, float (&v)[8]) {
+  const int k = st.k;
+  const uint16_t* arow = st.embed ? static_cast<const uint16_t*>(st.embed) + (size_t)__ldcg(st.token + q) * k
+                                  : static_cast<const uint16_t*>(st.a) + (size_t)q * k;
+  unpack8(__ldcg(reinterpret_cast<const uint4*>(arow + x0 + 8 * g)), v);
+  if (st.norm && st.b) {
+    float w8[8];
+    unpack8(__ldcg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(st.b) + (size_t)q * k + x0 + 8 * g)),
+            w8);
+#pragma unroll
+    for (int j = 0; j < 8; j++) v[j] = __fadd_rn(v[j], w8[j]);
+  }
+}
+
+// ... of a SPARK_PRO_PARTS norm stage: bf16 of the part sum (part order), plus b
+__device__ __forceinline__ void batch_load_parts(const SparkStage& st, int q, int g, float (&v)[8]) {
+  const int k = st.k;
+  const float* parts = static_cast<const float*>(st.a) + (size_t)q * st.a_parts * k + 8 * g;
+  uint4 bv = make_uint4(0u, 0u, 0u, 0u);
+  if (st.b) bv = __ldcg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(st.b) + (size_t)q * k + 8 * g));
+  float4 p0 = __ldcg(reinterpret_cast<const float4*>(parts));
+  float4 p1 = __ldcg(reinterpret_cast<const float4*>(parts + 4));
+#pragma unroll 1
+  for (int q4 = 1; q4 < st.a_parts; q4 += kPartsBatch) {
+    float4 a0[kPartsBatch], a1[kPartsBatch];
+#pragma unroll
+    for (int i = 0; i < kPartsBatch; i++) {
+      if (q4 + i < st.a_parts) {
+        a0[i] = __ldcg(reinterpret_cast<const float4*>(parts + (size_t)(q4 + i) * k));
+        a1[i] = __ldcg(reinterpret_cast<const float4*>(parts + (size_t)(q4 + i) * k + 4));
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kPartsBatch; i++) {
+      if (q4 + i < st.a_parts) {
+        p0 = make_float4(__fadd_rn(p0.x, a0[i].x), __fadd_rn(p0.y, a0[i].y), __fadd_rn(p0.z, a0[i].z),
+                         __fadd_rn(p0.w, a0[i].w));
+        p1 = make_float4(__fadd_rn(p1.x, a1[i].x), __fadd_rn(p1.y, a1[i].y), __fadd_rn(p1.z, a1[i].z),
+                         __fadd_rn(p1.w, a1[i].w));
+      }
+    }
+  }
+  const float t8[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+#pragma unroll
+  for (int j = 0; j < 8; j++) v[j] = bf16_round(t8[j]);
+  if (st.b) {
+    float w8[8];
+    unpack8(bv, w8);
+#pragma unroll
+    for (int j = 0; j < 8; j++) v[j] = __fadd_rn(v[j], w8[j]);
+  }
+}
+
+// Norm stages: the pre-norm values of the thread's items, IR items' loads per L2 round
+// trip, into the fp32 buffer (and the residual output, CTA 0)
+template <int IR, bool Parts>
+__device__ __forceinline__ void batch_prenorm(const SparkStage& st, int tid, int nitem, int ngrp, int rot, float* vbuf,
+                                              uint16_t* res) {
+  const int k = st.k;
+#pragma unroll 1
+  for (int r0 = 0; r0 * kConsumers < nitem; r0 += IR) {
+    float v[IR][8];
+#pragma unroll
+    for (int r = 0; r < IR; r++) {
+      const int it = stage_grp(tid + (r0 + r) * kConsumers, nitem, rot);
+      if (it < nitem) {
+        const int q = it / ngrp;
+        if constexpr (Parts)
+          batch_load_parts(st, q, it - q * ngrp, v[r]);
+        else
+          batch_load_bf16(st, q, it - q * ngrp, 0, v[r]);
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < IR; r++) {
+      const int it = stage_grp(tid + (r0 + r) * kConsumers, nitem, rot);
+      if (it < nitem) {
+        const int q = it / ngrp, g = it - q * ngrp;
+        float4* dst = reinterpret_cast<float4*>(vbuf + (size_t)q * k + 8 * g);
+        dst[0] = make_float4(v[r][0], v[r][1], v[r][2], v[r][3]);
+        dst[1] = make_float4(v[r][4], v[r][5], v[r][6], v[r][7]);
+        if (res) {
+          uint4 o;
+          o.x = bf16x2(v[r][0], v[r][1]);
+          o.y = bf16x2(v[r][2], v[r][3]);
+          o.z = bf16x2(v[r][4], v[r][5]);
+          o.w = bf16x2(v[r][6], v[r][7]);
+          *reinterpret_cast<uint4*>(res + (size_t)q * k + 8 * g) = o;
+        }
+      }
+    }
+  }
+}
+
+template <int NB>
+__device__ __forceinline__ void stage_x_batch(const SparkStage& st, const Smem& s, int tid, unsigned long long* tr,
+                                              int x0, int kx) {
+  const int k = st.k, nb = kx >> 5, ngrp = kx >> 3, nitem = NB * ngrp;
+  uint32_t* xfrag32 = reinterpret_cast<uint32_t*>(s.scratch);
+  int2* xmeta = reinterpret_cast<int2*>(s.scratch + 64 * nb * NB);
+  const int rot = 4 * (int)((blockIdx.x * 37u) % (unsigned)(nitem >> 2));
+  if (!st.norm) {  // load and stage, kBatchItems / 2 items per L2 round trip
+#pragma unroll 1
+    for (int r0 = 0; r0 * kConsumers < nitem; r0 += kBatchItems / 2) {
+      float v[kBatchItems / 2][8];
+#pragma unroll
+      for (int r = 0; r < kBatchItems / 2; r++) {
+        const int it = stage_grp(tid + (r0 + r) * kConsumers, nitem, rot);
+        if (it < nitem) {
+          const int q = it / ngrp;
+          batch_load_bf16(st, q, it - q * ngrp, x0, v[r]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; j++) v[r][j] = 0.0f;
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < kBatchItems / 2; r++) {
+        if ((r0 + r) * kConsumers < nitem) {
+          const int it = stage_grp(tid + (r0 + r) * kConsumers, nitem, rot);
+          const int q = it < nitem ? it / ngrp : 0;
+          stage_group(v[r], it < nitem, it - q * ngrp, xfrag32 + 16 * q, xmeta + q, nullptr, NB);
+        }
+      }
+    }
+    if (tr) tr[6] = tr[7] = gtimer();
+    return;
+  }
+  float* vbuf = reinterpret_cast<float*>(s.scratch);  // [NB][k] (norm stages stage the whole k)
+  const uint16_t* gm = reinterpret_cast<const uint16_t*>(s.scratch + 4 * k * NB);  // prefetched gamma
+  uint16_t* res = (blockIdx.x == 0) ? static_cast<uint16_t*>(st.res_out) : nullptr;
+  if (st.pro == SPARK_PRO_PARTS)
+    batch_prenorm<1, true>(st, tid, nitem, ngrp, rot, vbuf, res);
+  else
+    batch_prenorm<4, false>(st, tid, nitem, ngrp, rot, vbuf, res);
+  if (tr) tr[6] = gtimer();
+  consumer_bar();
+  if (tid < 32 * NB) {  // warp q: sequence q's canonical sum (lane l: s_i^2, i = l mod 32, ascending)
+    const float* sv = vbuf + (size_t)(tid >> 5) * k;
+    float acc = 0.0f;
+    int i = tid & 31;
+    for (; i + 15 * 32 < k; i += 16 * 32) {
+      float q16[16];
+#pragma unroll
+      for (int q = 0; q < 16; q++) q16[q] = sv[i + 32 * q];
+#pragma unroll
+      for (int q = 0; q < 16; q++) acc = __fadd_rn(acc, __fmul_rn(q16[q], q16[q]));
+    }
+    for (; i < k; i += 32) acc = __fadd_rn(acc, __fmul_rn(sv[i], sv[i]));
+    acc = butterfly_sum<32>(acc);
+    if ((tid & 31) == 0) s.red[tid >> 5] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(acc, st.inv_k), st.eps)));
+  }
+  consumer_bar();
+  if (tr) tr[7] = gtimer();
+  // normalized values as packed bf16 (the scratch is rewritten by the digits below)
+  uint4 yq[kBatchItems];
+#pragma unroll
+  for (int r = 0; r < kBatchItems; r++) {
+    const int it = stage_grp(tid + r * kConsumers, nitem, rot);
+    if (r * kConsumers < nitem && it < nitem) {
+      const int q = it / ngrp, g = it - q * ngrp;
+      const float inv = s.red[q];
+      const float4 a0 = *reinterpret_cast<const float4*>(vbuf + (size_t)q * k + 8 * g);
+      const float4 a1 = *reinterpret_cast<const float4*>(vbuf + (size_t)q * k + 8 * g + 4);
+      float g8[8];
+      unpack8(*reinterpret_cast<const uint4*>(gm + 8 * g), g8);
+      const float t8[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      float y[8];
+#pragma unroll
+      for (int j = 0; j < 8; j++) y[j] = __fmul_rn(__fmul_rn(t8[j], inv), g8[j]);
+      yq[r] = make_uint4(bf16x2(y[0], y[1]), bf16x2(y[2], y[3]), bf16x2(y[4], y[5]), bf16x2(y[6], y[7]));
+    } else {
+      yq[r] = make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+  consumer_bar();
+#pragma unroll
+  for (int r = 0; r < kBatchItems; r++) {
+    if (r * kConsumers < nitem) {
+      const int it = stage_grp(tid + r * kConsumers, nitem, rot);
+      const int q = it < nitem ? it / ngrp : 0;
+      float y[8];
+      unpack8(yq[r], y);
+      stage_group(y, it < nitem, it - q * ngrp, xfrag32 + 16 * q, xmeta + q, nullptr, NB);
+    }
+  }
+}
+
 // ------------------------------------------------------------------ consumers: GEMV
 // one (unit, slice) task: lanes 4g hold the slice sums of positions g and g + 8 as a
 // packed pair.  Tiles are processed 4 at a time (8 blocks: all shared-memory loads,
@@ -836,6 +1069,130 @@ __device__ __forceinline__ void gemv_task(const GemvDims& gd, uint32_t ubase, in
   acc1 = __fadd_rn(e1, __shfl_xor_sync(0xffffffffu, e1, 2));
 }
 
+// ------------------------------------------------------------------ batch GEMV
+// One (unit, slice) task for NB sequences.  A 4-block group's integer MMAs multiply the
+// NB sequences' digit columns together, the weight fragments loaded once:
+//   NB <= 4: NB accumulator sets of CL = 4 / NB blocks; the MMA of block a CL + jc of set a
+//            uses B columns 2 NB jc .. 2 NB jc + 2 NB - 1 = the h / l digits of the NB
+//            sequences (one 256-B run of staged records, masked to the MMA as in the
+//            one-sequence chain), so lane (g, c) ends with block a CL + c / NB of sequence
+//            c % NB;
+//   NB = 8:  two MMAs per block (sequences 0..3, 4..7), lane (g, c) ends with the block of
+//            sequences c and c + 4.
+// Either way a lane extends, per sequence, the chains c' = 0..3 of the one-sequence order
+// (chain c' = blocks c', c' + 4, ... ascending, acc = fma(fp32(d) sx, P, acc)), and the
+// slice value is ((chain 0 + chain 1) + (chain 2 + chain 3)) as there: each sequence's
+// result is bit-identical to its one-sequence launch.  The MMA count per group is 4 for
+// NB <= 4 and 8 for NB = 8 (the tensor instruction has the columns to spare).
+template <int NB>
+struct BatchShape {
+  static constexpr int CL = NB >= 4 ? 1 : 4 / NB;   // blocks per accumulator set (NB <= 4)
+  static constexpr int NA = NB == 8 ? 8 : NB;       // accumulator pairs per lane
+  static constexpr int NV = NB == 8 ? 2 : 1;        // sequences per lane
+};
+
+// the group of NBLK (4, or 2 for the last tile of an odd tile count) blocks at the
+// addresses, accumulated into acc; advances the addresses by one whole group
+template <int NB, int NBLK>
+__device__ __forceinline__ void gemv_group_b(uint32_t& a_adr, uint32_t& s_adr, uint32_t& b_adr, uint32_t& m_adr,
+                                             int lane, unsigned long long (&acc)[BatchShape<NB>::NA]) {
+  constexpr int CL = BatchShape<NB>::CL;
+  constexpr int NSET = NB == 8 ? 2 * NBLK : (NBLK + CL - 1) / CL;
+  const uint32_t m = 0x0f0f0f0fu;
+  const int c = lane & 3;
+  uint4 A[NBLK / 2];
+  uint2 SC[NBLK / 2];
+  uint2 B[NSET], Mt[NSET];
+#pragma unroll
+  for (int t = 0; t < NBLK / 2; t++) {
+    lds_u32x4(a_adr + t * kTileBytes, A[t]);
+    lds_u32x2(s_adr + t * kTileBytes, SC[t]);
+  }
+#pragma unroll
+  for (int a = 0; a < NSET; a++) {
+    lds_u32x2(b_adr + a * 256, B[a]);
+    lds_u32x2(m_adr + a * 32, Mt[a]);
+  }
+  int D[NSET][4];
+#pragma unroll
+  for (int a = 0; a < NSET; a++) {
+    D[a][0] = 0;
+    D[a][1] = (int)Mt[a].x;
+    D[a][2] = 0;
+    D[a][3] = (int)Mt[a].x;
+  }
+#pragma unroll
+  for (int a = 0; a < NSET; a++) {
+#pragma unroll
+    for (int jc = 0; jc < (NB == 8 ? 1 : CL); jc++) {
+      const int j = NB == 8 ? a >> 1 : a * CL + jc;  // block of the group
+      if (j < NBLK) {
+        const uint4& w = A[j >> 1];
+        const uint32_t w0 = (j & 1) ? w.z : w.x, w1 = (j & 1) ? w.w : w.y;
+        const uint32_t bm = (NB >= 4 || (lane / (32 / CL)) == jc) ? 0xffffffffu : 0u;
+        mma_u8s8_acc(D[a], w0 & m, w1 & m, (w0 >> 4) & m, (w1 >> 4) & m, B[a].x & bm, B[a].y & bm);
+      }
+    }
+  }
+#pragma unroll
+  for (int a = 0; a < NSET; a++) {
+    const int blk = NB == 8 ? a >> 1 : a * CL + c / NB;  // this lane's block in set a
+    const uint2 sw = (NBLK == 4 && (blk >> 1)) ? SC[NBLK / 2 - 1] : SC[0];
+    const uint32_t ds = (blk & 1) ? sw.y : sw.x;
+    const float sx = __uint_as_float(Mt[a].y);
+    const unsigned long long sc =
+        fmul2(f2pack(h2f((uint16_t)(ds & 0xffffu)), h2f((uint16_t)(ds >> 16))), f2pack(sx, sx));
+    const unsigned long long pm = f2pack(__int_as_float(D[a][0] * 256 + D[a][1]), __int_as_float(D[a][2] * 256 + D[a][3]));
+    acc[a] = ffma2(sc, fadd2(pm, f2pack(-kMagicF, -kMagicF)), acc[a]);
+  }
+  a_adr += 2 * kTileBytes;
+  s_adr += 2 * kTileBytes;
+  b_adr += NB * 256;
+  m_adr += NB * 32;
+}
+
+// lane (g, c): rows g / g + 8 of sequence c % NB (NB = 8: of sequences c and c + 4); for
+// NB = 2 lanes c and c ^ 2 hold the same values
+template <int NB>
+__device__ __forceinline__ void gemv_task_b(const GemvDims& gd, uint32_t ubase, int kpi, int sl, int lane,
+                                            float (&v0)[BatchShape<NB>::NV], float (&v1)[BatchShape<NB>::NV]) {
+  constexpr int NA = BatchShape<NB>::NA;
+  const int tps = gd.tps, g = lane >> 2, c = lane & 3;
+  const int t0 = sl * tps;
+  const int gb = kpi * gd.kp_blocks + 2 * t0;  // first block of the slice
+  uint32_t a_adr = ubase + (uint32_t)t0 * kTileBytes + lane * 16;
+  uint32_t s_adr = ubase + (uint32_t)t0 * kTileBytes + 512 + g * 8;
+  uint32_t b_adr = gd.xf + (uint32_t)(gb * NB * 8 + lane) * 8;
+  uint32_t m_adr = gd.xm + (uint32_t)(gb * NB + c) * 8;
+  unsigned long long acc[NA];
+#pragma unroll
+  for (int a = 0; a < NA; a++) acc[a] = 0ull;
+  int n = tps;
+#pragma unroll(NB == 8 ? 1 : 2)
+  for (; n >= 2; n -= 2) gemv_group_b<NB, 4>(a_adr, s_adr, b_adr, m_adr, lane, acc);
+  if (n) gemv_group_b<NB, 2>(a_adr, s_adr, b_adr, m_adr, lane, acc);
+  float e[NA][2];
+#pragma unroll
+  for (int a = 0; a < NA; a++) f2unpack(acc[a], e[a][0], e[a][1]);
+  if constexpr (NB == 2) {  // set a: chains 2a + c / 2; partner c ^ 2 holds chain 2a + 1 - c / 2
+#pragma unroll
+    for (int a = 0; a < 2; a++)
+#pragma unroll
+      for (int r = 0; r < 2; r++) e[a][r] = __fadd_rn(e[a][r], __shfl_xor_sync(0xffffffffu, e[a][r], 2));
+    v0[0] = __fadd_rn(e[0][0], e[1][0]);
+    v1[0] = __fadd_rn(e[0][1], e[1][1]);
+  } else if constexpr (NB == 4) {  // set a = chain a
+    v0[0] = __fadd_rn(__fadd_rn(e[0][0], e[1][0]), __fadd_rn(e[2][0], e[3][0]));
+    v1[0] = __fadd_rn(__fadd_rn(e[0][1], e[1][1]), __fadd_rn(e[2][1], e[3][1]));
+  } else {  // set 2 j + h = chain j of sequence c + 4 h
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      v0[h] = __fadd_rn(__fadd_rn(e[h][0], e[2 + h][0]), __fadd_rn(e[4 + h][0], e[6 + h][0]));
+      v1[h] = __fadd_rn(__fadd_rn(e[h][1], e[2 + h][1]), __fadd_rn(e[4 + h][1], e[6 + h][1]));
+    }
+  }
+}
+
 // ------------------------------------------------------------------ Q6_K (T6 units)
 // Unit = 16 rows x Kp columns, 105 Kp / 8 bytes: the fp16 d of each 256-weight super-
 // block for row pairs (g, g + 8) [Kp/256][8][2], the int8 scale of each 16-weight
@@ -938,11 +1295,13 @@ __device__ __forceinline__ void gemv_task_q6(const GemvDims& gd, uint32_t ubase,
 __device__ __forceinline__ uint16_t bf16r(float v) { return f2bf(v); }
 
 // epilogue of one row pair (positions g and g + 8 of unit u); Spark: the qkv stage's
-// partial RoPE and gate rows, the GELU * mul epilogue
-template <bool Spark>
+// partial RoPE and gate rows, the GELU * mul epilogue.  NB > 1: of sequence bq (outputs
+// at bq times their one-sequence size; rope_cs is that sequence's row, kvo its cache
+// offset)
+template <bool Spark, int NB = 1>
 __device__ __forceinline__ void gemv_epilogue(const SparkStage& st, const SparkStepIO& io, const long long* misc64,
                                               const uint16_t* rope_cs, int u, int g, float v0, float v1,
-                                              unsigned long long& best) {
+                                              unsigned long long& best, int bq = 0, long long kvo = 0) {
   const int rg = u / st.kp, kpi = u - rg * st.kp;
   int r0, r1;
   if constexpr (Spark) {
@@ -955,7 +1314,7 @@ __device__ __forceinline__ void gemv_epilogue(const SparkStage& st, const SparkS
   }
   switch (st.epi) {
     case SPARK_EPI_BF16: {
-      uint16_t* y = static_cast<uint16_t*>(st.out);
+      uint16_t* y = static_cast<uint16_t*>(st.out) + (NB > 1 ? (size_t)bq * st.n : 0);
       y[r0] = bf16r(v0);
       y[r1] = bf16r(v1);
       break;
@@ -979,7 +1338,7 @@ __device__ __forceinline__ void gemv_epilogue(const SparkStage& st, const SparkS
           yp[r1] = v1;
         }
       } else {
-        float* y = static_cast<float*>(st.out) + (size_t)kpi * st.n;
+        float* y = static_cast<float*>(st.out) + (size_t)((NB > 1 ? bq * st.kp : 0) + kpi) * st.n;
         y[r0] = v0;
         y[r1] = v1;
       }
@@ -988,7 +1347,7 @@ __device__ __forceinline__ void gemv_epilogue(const SparkStage& st, const SparkS
     case SPARK_EPI_SILU_MUL: {
       const float gf = bf2f(f2bf(v0)), uf = bf2f(f2bf(v1));
       const float act = bf2f(f2bf(__fdiv_rn(gf, __fadd_rn(1.0f, spark_exp(-gf)))));
-      static_cast<uint16_t*>(st.out)[r0] = f2bf(__fmul_rn(act, uf));
+      static_cast<uint16_t*>(st.out)[(NB > 1 ? (size_t)bq * (st.n >> 1) : 0) + r0] = f2bf(__fmul_rn(act, uf));
       break;
     }
     case SPARK_EPI_GELU_MUL: {
@@ -1001,8 +1360,9 @@ __device__ __forceinline__ void gemv_epilogue(const SparkStage& st, const SparkS
     case SPARK_EPI_ARGMAX: {
       const uint16_t b0 = f2bf(v0), b1 = f2bf(v1);
       if (st.out) {
-        static_cast<uint16_t*>(st.out)[r0] = b0;
-        static_cast<uint16_t*>(st.out)[r1] = b1;
+        uint16_t* y = static_cast<uint16_t*>(st.out) + (NB > 1 ? (size_t)bq * st.n : 0);
+        y[r0] = b0;
+        y[r1] = b1;
       }
       const unsigned long long k0 = argmax_key(b0, st.row0 + r0), k1 = argmax_key(b1, st.row0 + r1);
       const unsigned long long k = k0 > k1 ? k0 : k1;
@@ -1041,17 +1401,18 @@ __device__ __forceinline__ void gemv_epilogue(const SparkStage& st, const SparkS
       }
       const uint16_t ua = f2bf(a), ub = f2bf(b);
       if (hd < st.nq) {
-        uint16_t* q = static_cast<uint16_t*>(st.q) + (size_t)hd * D;
+        uint16_t* q = static_cast<uint16_t*>(st.q) + ((NB > 1 ? (size_t)bq * st.nq : 0) + hd) * D;
         q[i] = ua;
         q[i + half] = ub;
       } else {
         const int isv = hd >= st.nq + st.nkv;
         const int hk = hd - st.nq - isv * st.nkv;
         uint16_t* cache = static_cast<uint16_t*>(isv ? st.v_cache : st.k_cache);
-        uint16_t* dst = cache + misc64[1] + (int64_t)hk * st.block_size * D;
+        uint16_t* dst = cache + (NB > 1 ? kvo : misc64[1]) + (int64_t)hk * st.block_size * D;
         dst[i] = ua;
         dst[i + half] = ub;
-        uint16_t* kn = static_cast<uint16_t*>(st.kv_new) + ((size_t)isv * st.nkv + hk) * D;
+        uint16_t* kn =
+            static_cast<uint16_t*>(st.kv_new) + ((NB > 1 ? (size_t)bq * 2 * st.nkv : 0) + (size_t)isv * st.nkv + hk) * D;
         kn[i] = ua;
         kn[i + half] = ub;
       }
@@ -1218,6 +1579,126 @@ __device__ __forceinline__ bool gemv_stage(const StepParams& P, const SparkStage
   return true;
 }
 
+
+// A GEMV stage of a batch-NB program: the one-sequence stage's units, tasks and slot
+// handling, with NB staged inputs, the batch task and NB epilogues per row pair (lane
+// (g, c) runs those of its sequences c % NB, c < NB; NB = 8: c and c + 4).  Slice sums:
+// [slot][slice][sequence][16].
+template <int NB>
+__device__ __forceinline__ bool gemv_stage_b(const StepParams& P, const SparkStage& st, const Smem& s, uint32_t& seq_base,
+                                             int tid) {
+  constexpr int NV = BatchShape<NB>::NV;
+  const int ncta = gridDim.x, cta = blockIdx.x, warp = tid >> 5, lane = tid & 31, c = lane & 3;
+  int u0, ustride;
+  const int nl = local_units(st, cta, ncta, u0, ustride);
+  const bool part_x = !st.norm && st.kp > 1 && ncta % st.kp == 0;
+  const int kx = part_x ? st.k / st.kp : st.k;
+  unsigned long long* tr = (tid == 0 && P.io.trace)
+                               ? P.io.trace + ((size_t)cta * P.num_stages + s.flag[2]) * kTraceSlots
+                               : nullptr;
+  if (nl > 0 || (cta == 0 && st.res_out)) stage_x_batch<NB>(st, s, tid, tr, part_x ? (u0 % st.kp) * kx : 0, kx);
+  consumer_bar();
+  if (tr) tr[4] = gtimer();
+  const bool owner = NB >= 4 || c < NB;
+  int bqs[NV];
+#pragma unroll
+  for (int i = 0; i < NV; i++) bqs[i] = NB == 8 ? c + 4 * i : c % NB;
+  unsigned long long best[NV];
+#pragma unroll
+  for (int i = 0; i < NV; i++) best[i] = 0ull;
+  const int ks = st.ks;
+  GemvDims gd;
+  gd.kp = st.kp;
+  gd.kp_blocks = (st.k / st.kp) >> 5;
+  gd.tps = (gd.kp_blocks >> 1) / ks;
+  gd.xf = smem_u32(s.scratch);
+  gd.xm = gd.xf + 64 * (kx >> 5) * NB;
+  gd.xm2 = 0;
+  const bool rope = st.epi == SPARK_EPI_ROPE_KV;
+  auto epi = [&](int u, int g, int i, float v0, float v1) {
+    const int bq = bqs[i];
+    gemv_epilogue<false, NB>(st, P.io, s.misc64, rope ? s.rope_cs + 128 * bq : s.rope_cs, u, g, v0, v1, best[i], bq,
+                             rope ? s.bkvoff[bq] : 0ll);
+  };
+  for (int t = warp; t < nl * ks; t += kWarps) {
+    const int j = t / ks, sl = t - j * ks;
+    const uint32_t seq = seq_base + j;
+    if (!wait_unit(s, seq)) {  // abort: skip the work, keep the barriers
+      raise_abort(P, s, SPARK_ERR_LAUNCH);
+      continue;
+    }
+    const int u = u0 + j * ustride;
+    const uint32_t slot = seq % kDesc;
+    float v0[NV], v1[NV];
+    gemv_task_b<NB>(gd, smem_u32(s.ring) + s.desc_off[slot], part_x ? 0 : u % gd.kp, sl, lane, v0, v1);
+    if (ks == 1) {
+      if (owner)
+#pragma unroll
+        for (int i = 0; i < NV; i++) epi(u, lane >> 2, i, v0[i], v1[i]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(s.empty + slot));
+    } else {
+      float* pr = s.partial + slot * Layout<NB>::slices * 16 * NB;
+      if (owner) {
+#pragma unroll
+        for (int i = 0; i < NV; i++) {
+          pr[(sl * NB + bqs[i]) * 16 + (lane >> 2)] = v0[i];
+          pr[(sl * NB + bqs[i]) * 16 + (lane >> 2) + 8] = v1[i];
+        }
+      }
+      __syncwarp();
+      int last = 0;
+      if (lane == 0) {
+        int old;
+        asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], 1;" : "=r"(old) : "r"(smem_u32(s.done + slot))
+                     : "memory");
+        last = old == ks - 1;
+      }
+      last = __shfl_sync(0xffffffffu, last, 0);
+      __syncwarp();
+      if (last) {
+        if (owner) {
+#pragma unroll
+          for (int i = 0; i < NV; i++) {
+            const int g = lane >> 2, bq = bqs[i];
+            float a0 = pr[bq * 16 + g], a1 = pr[bq * 16 + g + 8];
+            for (int q = 1; q < ks; q++) {
+              a0 = __fadd_rn(a0, pr[(q * NB + bq) * 16 + g]);
+              a1 = __fadd_rn(a1, pr[(q * NB + bq) * 16 + g + 8]);
+            }
+            epi(u, g, i, a0, a1);
+          }
+        }
+        __syncwarp();
+        if (lane == 0) {
+          s.done[slot] = 0;
+          mbar_arrive(smem_u32(s.empty + slot));
+        }
+      }
+    }
+  }
+  if (tr) tr[5] = gtimer();
+  if (st.epi == SPARK_EPI_ARGMAX) {  // per sequence: over the lanes of the same c, the warps, the CTAs
+#pragma unroll
+    for (int i = 0; i < NV; i++) {
+#pragma unroll
+      for (int off = 16; off >= 4; off /= 2) {
+        const unsigned long long o = __shfl_xor_sync(0xffffffffu, best[i], off);
+        best[i] = o > best[i] ? o : best[i];
+      }
+      if (lane < 4 && owner) s.red64[warp * NB + bqs[i]] = best[i];
+    }
+    consumer_bar();
+    if (tid < NB) {
+      unsigned long long m = 0;
+      for (int w = 0; w < kWarps; w++) m = s.red64[w * NB + tid] > m ? s.red64[w * NB + tid] : m;
+      if (m) atomicMax(st.key + tid, m);
+    }
+  }
+  seq_base += nl;
+  return true;
+}
+
 // ------------------------------------------------------------------ consumers: attention
 // Task (kv head g, split j): tokens [t0, t1) of the context pos + 1 (Spark sliding
 // window: of its last `window` positions), T = split_len.  Head dim D = 128 (256 in the
@@ -1272,13 +1753,14 @@ __device__ __forceinline__ void release_runs(const Smem& s, uint32_t seq0, int r
 }
 
 // One task (kv head g, split j): the ranges' softmax and P V, their merge, the split's
-// partials.  false: the split is longer than the scratch holds (launch aborted).
-template <int D, bool Spark>
+// partials.  false: the split is longer than the scratch holds (launch aborted).  NB > 1:
+// of sequence bq (its position, q, kv_new and partials).
+template <int D, bool Spark, int NB = 1>
 __device__ __forceinline__ bool attn_split(const StepParams& P, const SparkStage& st, const Smem& s, uint32_t& seq_base,
-                                           int tid, int g, int j) {
+                                           int tid, int g, int j, int bq = 0) {
   const int warp = tid >> 5, lane = tid & 31;
   const int nq = st.nq, S = st.splits;
-  const int64_t pos = s.misc64[0], len = pos + 1;
+  const int64_t pos = NB > 1 ? s.bpos[bq] : s.misc64[0], len = pos + 1;
   // Spark sliding window: positions [lo, len); the splits start at lo rounded down to 16,
   // positions before lo score -inf
   const int64_t lo = Spark && st.window > 0 && len > st.window ? len - st.window : 0;
@@ -1290,9 +1772,9 @@ __device__ __forceinline__ bool attn_split(const StepParams& P, const SparkStage
   }
   const int64_t t0 = start + (int64_t)j * T, t1 = t0 + T < len ? t0 + T : len;
   const int n = t1 > t0 ? (int)(t1 - t0) : 0;
-  float* part_o = st.part_o;
-  float* part_lse = st.part_lse;
-  const uint16_t* kv_new = static_cast<const uint16_t*>(st.kv_new);
+  float* part_o = st.part_o + (NB > 1 ? (size_t)bq * S * nq * D : 0);
+  float* part_lse = st.part_lse + (NB > 1 ? (size_t)bq * S * nq : 0);
+  const uint16_t* kv_new = static_cast<const uint16_t*>(st.kv_new) + (NB > 1 ? (size_t)bq * 2 * st.nkv * D : 0);
   unsigned long long* tr = (tid == 0 && P.io.trace)
                                ? P.io.trace + ((size_t)blockIdx.x * P.num_stages + s.flag[2]) * kTraceSlots
                                : nullptr;
@@ -1321,7 +1803,7 @@ __device__ __forceinline__ bool attn_split(const StepParams& P, const SparkStage
   if (a < b) {
     float qf[4][16];
     {
-      const uint16_t* q = static_cast<const uint16_t*>(st.q) + (size_t)4 * g * D;
+      const uint16_t* q = static_cast<const uint16_t*>(st.q) + ((NB > 1 ? (size_t)bq * nq : 0) + (size_t)4 * g) * D;
 #pragma unroll
       for (int h = 0; h < 4; h++) {
         float lo8[8], hi8[8];
@@ -1590,9 +2072,9 @@ __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wai
 // accumulates its outputs over the splits in ascending order.  ToSmem: the outputs become
 // the staged (fixed-point digit) input of the following SPARK_PRO_ATTN o_proj stage; else
 // they go to attn_out.
-template <int D, bool Spark, bool ToSmem>
+template <int D, bool Spark, bool ToSmem, int NB = 1>
 __device__ __forceinline__ void attn_combine_all(const SparkStage& st, const Smem& s, int tid, int g,
-                                                 unsigned long long* tr) {
+                                                 unsigned long long* tr, int bq = 0) {
   const int warp = tid >> 5, lane = tid & 31;
   cstamp(tr, 18);
   const int nq = st.nq, S = st.splits;
@@ -1600,8 +2082,8 @@ __device__ __forceinline__ void attn_combine_all(const SparkStage& st, const Sme
   constexpr int PER = kCombineBytes / (16 * D);              // splits per round
   constexpr int CH = D;                                      // 16-byte chunks per split (4 D floats)
   const float ninf = __int_as_float(0xff800000);
-  const float* part_o = st.part_o;
-  const float* part_lse = st.part_lse;
+  const float* part_o = st.part_o + (NB > 1 ? (size_t)bq * S * nq * D : 0);
+  const float* part_lse = st.part_lse + (NB > 1 ? (size_t)bq * S * nq : 0);
   const float* pc = reinterpret_cast<const float*>(s.scratch);             // [PER][4 D]
   float* lse_s = reinterpret_cast<float*>(s.scratch + kCombineLseOff);      // [4][S]
   float* w_s = lse_s + 4 * S;                                               // [4][S]
@@ -1702,7 +2184,7 @@ __device__ __forceinline__ void attn_combine_all(const SparkStage& st, const Sme
       if constexpr (ToSmem) {
         xin[o] = ob;
       } else {
-        static_cast<uint16_t*>(st.attn_out)[(size_t)4 * g * D + o] = ob;
+        static_cast<uint16_t*>(st.attn_out)[((NB > 1 ? (size_t)bq * nq : 0) + (size_t)4 * g) * D + o] = ob;
       }
     }
   }
@@ -1736,10 +2218,12 @@ __device__ __forceinline__ bool attn_wait_head(const StepParams& P, const SparkS
 // so no CTA waits for another (several tasks per CTA cannot deadlock).  !Multi: at most
 // one task per CTA, in a form with no loop state (the usual program; a loop here costs
 // the GEMV stages registers in the same kernel).
-template <int D, bool Multi, bool Spark>
+// NB > 1: tasks (sequence b, kv head g, split j) = t / (nkv S), ..., never fused (the
+// host checks), each sequence's heads counted on its own counters.
+template <int D, bool Multi, bool Spark, int NB = 1>
 __device__ __forceinline__ bool attn_stage_d(const StepParams& P, const SparkStage& st, const Smem& s,
                                           uint32_t& seq_base, int tid, bool fused) {
-  const int S = st.splits, ntask = st.nkv * S;
+  const int S = st.splits, ntask = NB * st.nkv * S;
   unsigned long long* tr = (tid == 0 && P.io.trace)
                                ? P.io.trace + ((size_t)blockIdx.x * P.num_stages + s.flag[2]) * kTraceSlots
                                : nullptr;
@@ -1765,7 +2249,26 @@ __device__ __forceinline__ bool attn_stage_d(const StepParams& P, const SparkSta
     }
     if (tr) tr[7] = gtimer();
   };
-  if constexpr (!Multi) {
+  if constexpr (NB > 1) {
+    const int per = st.nkv * S;
+#pragma unroll 1
+    for (int t = blockIdx.x; t < ntask; t += gridDim.x) {
+      const int bq = t / per, tb = t - bq * per, g = tb / S;
+      if (!attn_split<D, Spark, NB>(P, st, s, seq_base, tid, g, tb - g * S, bq)) return false;
+      consumer_bar();  // the split's partials (all threads) before its count
+      if (tid == 0) {
+        int old;
+        asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;"
+                     : "=r"(old)
+                     : "l"(st.head_counters + (size_t)bq * st.nkv + g)
+                     : "memory");
+        s.flag[3] = old == st.splits * (int)(s.misc64[2] + 1) - 1;
+      }
+      consumer_bar();
+      if (s.flag[3]) attn_combine_all<D, Spark, false, NB>(st, s, tid, g, tr, bq);
+      if (t + (int)gridDim.x < ntask) consumer_bar();  // this task's shared memory before the next task's
+    }
+  } else if constexpr (!Multi) {
     if ((int)blockIdx.x >= ntask) return true;
     const int g = blockIdx.x / S, j = blockIdx.x - g * S;
     if (!attn_split<D, Spark>(P, st, s, seq_base, tid, g, j)) return false;
@@ -1783,10 +2286,12 @@ __device__ __forceinline__ bool attn_stage_d(const StepParams& P, const SparkSta
 
 // head_dim 256 in the Spark instantiation, 128 in the others (the host checks; one
 // attention body per kernel keeps its registers)
-template <bool Multi, bool Spark>
+template <bool Multi, bool Spark, int NB = 1>
 __device__ __forceinline__ bool attn_stage(const StepParams& P, const SparkStage& st, const Smem& s, uint32_t& seq_base,
                                         int tid, bool fused) {
-  if constexpr (Spark) {
+  if constexpr (NB > 1) {
+    return attn_stage_d<128, true, false, NB>(P, st, s, seq_base, tid, false);
+  } else if constexpr (Spark) {
     return attn_stage_d<256, Multi, true>(P, st, s, seq_base, tid, fused);
   } else {
     return attn_stage_d<128, Multi, false>(P, st, s, seq_base, tid, fused);
@@ -1812,12 +2317,15 @@ __device__ __forceinline__ bool wait_stage(const StepParams& P, const Smem& s, i
 
 // Q6: the program has Q6_K GEMV stages; Multi: an attention stage has more tasks than
 // CTAs; Spark: the program uses a Spark layer feature (head_dim 256, sliding window,
-// output gate, partial RoPE, GELU * mul).  Each is its own instantiation so the usual
-// program (Q4_0, one attention task per CTA) carries none of their registers.
-template <bool Q6, bool Multi, bool Spark, bool TP>
+// output gate, partial RoPE, GELU * mul); NB: sequences decoded together (batch
+// programs: Q4_0, head_dim 128, one GPU, any number of attention tasks).  Each is its
+// own instantiation so the usual program (Q4_0, one attention task per CTA, one
+// sequence) carries none of their registers.
+template <bool Q6, bool Multi, bool Spark, bool TP, int NB = 1>
 __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepParams P) {
+  static_assert(NB == 1 || (!Q6 && !Spark && !TP), "batch programs: Q4_0, head_dim 128, one GPU");
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  const Smem s = carve(smem_raw);
+  const Smem s = carve<NB>(smem_raw);
   const int tid = threadIdx.x;
   if (tid == 0) {
     for (int i = 0; i < kDesc; i++) {
@@ -1834,8 +2342,8 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepParams P) {
   __syncthreads();
   if (tid >= kConsumers) {
     if (tid == kConsumers) {
-      Producer pr(P, s);
-      pr.template run<Multi, Spark>();
+      Producer<NB> pr(P, s);
+      pr.template run<NB == 1 ? Multi : true, Spark>();
     }
     return;
   }
@@ -1855,7 +2363,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepParams P) {
       const bool rope = gemv && nx.epi == SPARK_EPI_ROPE_KV;
       if (gemv && nx.norm) {  // RMSNorm weight (a constant) next to the staging area
         const uint4* src = static_cast<const uint4*>(nx.gamma);
-        uint4* dst = reinterpret_cast<uint4*>(s.scratch + 72 * (nx.k >> 5) + 4 * nx.k);
+        uint4* dst = reinterpret_cast<uint4*>(s.scratch + (NB == 1 ? 72 * (nx.k >> 5) + 4 * nx.k : 4 * nx.k * NB));
         for (int q = tid; q < (nx.k >> 3); q += kConsumers) dst[q] = __ldg(src + q);
       }
       if (tid == 32) {  // touch the stage's activation buffers (value unused) to warm their translations
@@ -1869,7 +2377,24 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepParams P) {
       // of the key and a layer of the other type fetches its own row)
       const long long key = (long long)reinterpret_cast<uintptr_t>(nx.pos) ^
                             (Spark && rope ? (long long)reinterpret_cast<uintptr_t>(nx.cos_sin) : 0ll);
-      if ((rope || nx.kind == SPARK_STAGE_ATTN) && s.misc64[3] != key && tid < 32) {
+      if (NB > 1 && (rope || nx.kind == SPARK_STAGE_ATTN) && s.misc64[3] != key && tid < 32) {
+        // the NB sequences' positions, cache offsets of the decoded tokens and RoPE rows
+        if (tid < NB) {
+          const int64_t pos = __ldcg(nx.pos + tid);
+          s.bpos[tid] = pos;
+          if (rope) {
+            const int64_t blk = pos / nx.block_size, off = pos - blk * nx.block_size;
+            s.bkvoff[tid] =
+                ((int64_t)nx.block_table[(size_t)tid * nx.bt_stride + blk] * nx.nkv * nx.block_size + off) * 128;
+          }
+        }
+        __syncwarp();
+        if (rope)
+          for (int e = tid; e < NB * 128; e += 32)
+            s.rope_cs[e] = static_cast<const uint16_t*>(nx.cos_sin)[(size_t)s.bpos[e >> 7] * 128 + (e & 127)];
+        __syncwarp();
+        if (rope && tid == 0) s.misc64[3] = key;
+      } else if (NB == 1 && (rope || nx.kind == SPARK_STAGE_ATTN) && s.misc64[3] != key && tid < 32) {
         const int64_t pos = __ldcg(nx.pos);
         if (tid == 0) {
           s.misc64[0] = pos;
@@ -1905,8 +2430,13 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepParams P) {
     const bool fused = st.kind == SPARK_STAGE_ATTN && i + 1 < P.num_stages && stage_at(P, i + 1).pro == SPARK_PRO_ATTN;
     // both stage functions keep every consumer on the same barriers; a stage that
     // fails returns false in all threads (attention: a split longer than the scratch)
-    const bool ok = st.kind != SPARK_STAGE_ATTN ? gemv_stage<Q6, Spark, TP>(P, st, s, seq_base, tid)
-                                                : attn_stage<Multi, Spark>(P, st, s, seq_base, tid, fused);
+    bool ok;
+    if constexpr (NB > 1)
+      ok = st.kind != SPARK_STAGE_ATTN ? gemv_stage_b<NB>(P, st, s, seq_base, tid)
+                                       : attn_stage<true, false, NB>(P, st, s, seq_base, tid, false);
+    else
+      ok = st.kind != SPARK_STAGE_ATTN ? gemv_stage<Q6, Spark, TP>(P, st, s, seq_base, tid)
+                                       : attn_stage<Multi, Spark>(P, st, s, seq_base, tid, fused);
     consumer_bar();
     if (!ok) return;
     if (tid == 0 && tr) tr[2] = gtimer();
@@ -1952,14 +2482,19 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepParams P) {
       }
       if (ok) {
         if (io.key) {
-          const unsigned long long k = atomicAdd(io.key, 0ull);
-          const int32_t tok = (int32_t)(0xffffffffu - (uint32_t)(k & 0xffffffffull));
-          if (io.token_out) io.token_out[0] = tok;
-          if (io.token_log) io.token_log[io.step ? io.step[0] : 0] = tok;
-          *io.key = 0ull;
+#pragma unroll 1
+          for (int b = 0; b < NB; b++) {  // sequence b's token
+            const unsigned long long k = atomicAdd(io.key + b, 0ull);
+            const int32_t tok = (int32_t)(0xffffffffu - (uint32_t)(k & 0xffffffffull));
+            if (io.token_out) io.token_out[b] = tok;
+            if (io.token_log) io.token_log[(io.step ? io.step[0] : 0) * NB + b] = tok;
+            io.key[b] = 0ull;
+          }
         }
         if (io.step) io.step[0] += 1;
-        if (io.pos) io.pos[0] += 1;
+        if (io.pos)
+#pragma unroll 1
+          for (int b = 0; b < NB; b++) io.pos[b] += 1;
         if (!tp)
           for (int i = 0; i <= P.num_stages; i++) io.counters[i] = 0;
         io.counters[P.num_stages + 2] += 1;  // next launch's generation

@@ -48,6 +48,7 @@ SIGNATURES: dict[str, list] = {
     "spark_t16_bytes": [_I, _I, _I],
     "spark_q4_pack_t16": [_P, _P, _I, _I, _I, _I, _I, _P, _P],
     "spark_step_ring_bytes": [],
+    "spark_step_ring_bytes_batch": [_I],
     "spark_step_num_ctas": [],
     "spark_step_run": [_P, _P, _I, _P, _P],
     "spark_t6_bytes": [_I, _I],
@@ -64,7 +65,7 @@ RESTYPES = {"spark_t16_bytes": _I64, "spark_t6_bytes": _I64}
 
 
 class SparkStage(ctypes.Structure):
-    """Mirror of ``SparkStage`` in include/spark_b200.h (280 bytes)."""
+    """Mirror of ``SparkStage`` in include/spark_b200.h (288 bytes)."""
 
     _fields_ = [(n, ctypes.c_int32) for n in (
         "kind", "pro", "epi", "rowmap", "n", "k", "kp", "ks", "units", "rot", "wait", "norm", "a_parts",
@@ -73,7 +74,8 @@ class SparkStage(ctypes.Structure):
         (n, _P) for n in (
             "w", "a", "b", "embed", "token", "gamma", "res_out", "out", "cos_sin", "pos", "block_table", "k_cache",
             "v_cache", "q", "kv_new", "key", "part_o", "part_lse", "head_counters", "attn_out")] + [
-        ("rotary_dim", ctypes.c_int32), ("window", ctypes.c_int32), ("table", _P), ("gate", _P)]
+        ("rotary_dim", ctypes.c_int32), ("window", ctypes.c_int32), ("table", _P), ("gate", _P),
+        ("batch", ctypes.c_int32), ("bt_stride", ctypes.c_int32)]
 
 
 class SparkStepIO(ctypes.Structure):
@@ -84,7 +86,7 @@ class SparkStepIO(ctypes.Structure):
         ("window_bytes", ctypes.c_uint64), ("tp_size", ctypes.c_int32), ("tp_rank", ctypes.c_int32)]
 
 
-assert ctypes.sizeof(SparkStage) == 280
+assert ctypes.sizeof(SparkStage) == 288
 
 
 class SparkError(RuntimeError):

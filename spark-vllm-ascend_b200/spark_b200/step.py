@@ -101,9 +101,17 @@ def pick_ks(n: int, k: int, kp: int, want: int, ncta: int) -> int:
 
 
 class StepProgram:
-    """An ordered list of stages, its device copy, and the launch state."""
+    """An ordered list of stages, its device copy, and the launch state.
 
-    def __init__(self, device, ncta: int | None = None):
+    ``batch`` B > 1: a small-batch program (B in 2, 4, 8): every stage decodes B
+    sequences, its buffers holding B copies of their one-sequence layout, sequence-major;
+    ``bt_stride`` = entries per sequence row of the int32 [B][bt_stride] block table."""
+
+    def __init__(self, device, ncta: int | None = None, batch: int = 1, bt_stride: int = 0):
+        if batch not in (1, 2, 4, 8):
+            raise ValueError(f"batch {batch}: the step kernel decodes 1, 2, 4 or 8 sequences")
+        self.batch = batch
+        self.bt_stride = bt_stride
         self.device = torch.device(device)
         self.ncta = ncta or num_ctas()
         self.stages: list[SparkStage] = []
@@ -154,6 +162,11 @@ class StepProgram:
                                                    _p(rope["kv_new"]))
             s.block_size, s.nq, s.nkv = rope["block_size"], rope["nq"], rope["nkv"]
         self.keep.extend([w, a, b, embed, token, gamma, res_out, out, key, rope, gate, table])
+        return self._add(s)
+
+    def _add(self, s: SparkStage) -> int:
+        if self.batch > 1:
+            s.batch, s.bt_stride = self.batch, self.bt_stride
         self.stages.append(s)
         return len(self.stages) - 1
 
@@ -173,8 +186,7 @@ class StepProgram:
         s.window, s.gate = window, _p(gate)
         self.keep.extend([q, k_cache, v_cache, kv_new, block_table, pos, part_o, part_lse, head_counters, attn_out,
                           gate])
-        self.stages.append(s)
-        return len(self.stages) - 1
+        return self._add(s)
 
     # -- device copy
     def finalize(self, counters: torch.Tensor | None = None) -> "StepProgram":
@@ -254,7 +266,7 @@ def fuse_o_proj(cfg, ncta: int, splits: int) -> bool:
     return splits > 0 and cfg.num_kv_heads * splits <= ncta and cfg.head_dim == 128 and not cfg.spark_features
 
 
-def default_order(cfg, ncta: int, tp: int = 1, splits: int = 0) -> dict:
+def default_order(cfg, ncta: int, tp: int = 1, splits: int = 0, batch: int = 1) -> dict:
     """Slice / part counts of the decode program (the oracle's persistent-step order).
 
     ``cfg`` is the rank's local config (heads, intermediate size and vocab divided by
@@ -262,9 +274,9 @@ def default_order(cfg, ncta: int, tp: int = 1, splits: int = 0) -> dict:
     "kp_local" are the K parts of o_proj / down on one rank; "kp" the parts of the whole
     model (tp x kp_local: rank r's parts follow rank r - 1's), which is the order the
     oracle restates.  A fused o_proj (``fuse_o_proj``) is cut into one K part per kv head,
-    one slice per unit."""
+    one slice per unit.  Batch programs (``batch`` > 1) never fuse o_proj."""
     h, i, nq, D, v = cfg.hidden_size, cfg.intermediate_size, cfg.num_q_heads, cfg.head_dim, cfg.vocab_size
-    fused = fuse_o_proj(cfg, ncta, splits)
+    fused = batch == 1 and fuse_o_proj(cfg, ncta, splits)
     kp_o = cfg.num_kv_heads if fused else _pick_kp(nq * D, (2, 1), tp)
     kp_down = _pick_kp(i, (4, 2, 1), tp)
     qkv_n = (nq + 2 * cfg.num_kv_heads) * D
@@ -299,6 +311,18 @@ def splits_for(nkv: int, ncta: int, max_seq_len: int = 0, head_dim: int = 128) -
         return short
     rounds = max(1, -(-need * nkv // ncta))
     splits = max(need, rounds * ncta // nkv)
+    if splits > MAX_SPLITS:
+        raise ValueError(f"max_seq_len {max_seq_len} needs {splits} splits per kv head (limit {MAX_SPLITS})")
+    return splits
+
+
+def batch_splits(nkv: int, ncta: int, max_seq_len: int, batch: int) -> int:
+    """Splits per kv head of a batch-B program: the fewest that hold the context, rounded
+    up to whole rounds of the B x nkv x splits tasks over the CTAs."""
+    need = max(1, -(-max_seq_len // MAX_SPLIT_TOKENS))
+    pairs = nkv * batch
+    rounds = max(1, -(-need * pairs // ncta))
+    splits = max(need, rounds * ncta // pairs)
     if splits > MAX_SPLITS:
         raise ValueError(f"max_seq_len {max_seq_len} needs {splits} splits per kv head (limit {MAX_SPLITS})")
     return splits
