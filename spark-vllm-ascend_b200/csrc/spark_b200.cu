@@ -467,6 +467,10 @@ static int attn_launch(const uint16_t* q, const uint16_t* k_cache, const uint16_
   a.counters = counters;
   a.out = out;
   const int G = 4;
+  // the whole split in shared memory, 16 warps (pages of >= 64 tokens: at most 8 page segments)
+  if (a.t_alloc <= kWideMaxTokens && block_size >= 64 && (kWideMaxTokens + block_size - 1) / block_size + 1 <= kWideMaxSegs)
+    return launch(attn_decode_wide_kernel<128, 4>, dim3(splits, nkv), dim3(kWideThreads),
+                  attn_wide_smem(a.t_alloc), as_stream(stream), a);
   const size_t smem = (size_t)(G * a.t_alloc + 2 * G + G * kAttnMaxFusedSplits + 4) * sizeof(float) +
                       (size_t)a.kv_slots * kAttnChunk * (kKRowBytes + kVRowBytes);
   return launch(attn_decode_kernel<128, 4>, dim3(splits, nkv), dim3(kAttnThreads), smem, as_stream(stream), a);

@@ -28,9 +28,24 @@ def _run(world: int, *args: str, timeout: int = 600) -> list[dict]:
            f"--nproc-per-node={world}", "--master-addr=127.0.0.1", "--master-port=29533",
            os.path.join(HERE, "tp_worker.py"), *args]
     p = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=timeout + 60)
-    lines = [json.loads(l) for l in p.stdout.splitlines() if l.startswith("{")]
     assert p.returncode == 0, (p.returncode, p.stdout[-3000:], p.stderr[-3000:])
-    return lines
+    return _json_objects(p.stdout)
+
+
+def _json_objects(text: str) -> list[dict]:
+    """Every JSON object in the ranks' interleaved output (two ranks' lines can share a
+    line when they print at the same moment)."""
+    dec, out, i = json.JSONDecoder(), [], text.find("{")
+    while i >= 0:
+        try:
+            obj, end = dec.raw_decode(text, i)
+        except json.JSONDecodeError:
+            i = text.find("{", i + 1)
+            continue
+        if isinstance(obj, dict) and "rank" in obj:
+            out.append(obj)
+        i = text.find("{", end)
+    return out
 
 
 @pytest.mark.parametrize("world", [2])
