@@ -59,15 +59,16 @@ int spark_q4_dequantize_bf16(const uint8_t* qs, const uint16_t* d, int64_t rows,
 
 /* Prefill GEMM on the tensor cores: y[t][n] = bf16(sum_k W[n][k] * x[t][k]) for t < T
  * tokens, W the Q4_0 planes [n][k] dequantized to bf16 in shared memory (the same
- * rounding as spark_q4_dequantize_bf16), fp32 accumulation (tcgen05.mma).  Replaces the
- * prefill's dequantize -> bf16 matmul (integration/weights.py:28-31 and vLLM's torch
- * linear layers, integration/model.py:50-62) without the bf16 weight copy.  k % 64 == 0;
- * x [T][k] bf16 16-B aligned.  Each wait on the tensor cores is bounded by wait_ns
- * (< 0: the default 0.5 s; 0: give up at the first look, for testing the error path).
- * *error (caller-owned, required) becomes 1 when a wait ran out (y is then not
- * written); the CTA still waits, with a fixed 2 s bound, for the MMAs it issued before it
- * frees its tensor memory.  2 means that drain ran out too and the CTA kept its tensor
- * memory: the CUDA context must then be treated as unusable. */
+ * rounding as spark_q4_dequantize_bf16), fp32 accumulation (tcgen05.mma; activation and
+ * weight tiles brought in by TMA).  Replaces the prefill's dequantize -> bf16 matmul
+ * (integration/weights.py:28-31 and vLLM's torch linear layers,
+ * integration/model.py:50-62) without the bf16 weight copy.  k % 256 == 0; x [T][k]
+ * bf16, qs and d 16-B aligned.  Each wait inside the kernel is bounded by wait_ns
+ * (< 0: the default 0.5 s; 0: give up at the second look, for testing the error path).
+ * *error (caller-owned, required) becomes 1 when a wait ran out (y is then not valid);
+ * the CTA still waits, with a fixed 2 s bound, for the copies and MMAs it issued before
+ * it frees its shared and tensor memory.  2 means that drain ran out too and the CTA
+ * kept its tensor memory: the CUDA context must then be treated as unusable. */
 int spark_q4_gemm_tc(const uint16_t* x, const uint8_t* qs, const uint16_t* d, uint16_t* y, int t, int n, int k,
                      int* error, int64_t wait_ns, void* stream);
 

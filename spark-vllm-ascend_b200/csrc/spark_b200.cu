@@ -5,6 +5,8 @@
 // status codes.  Launches use cudaLaunchKernelEx with programmatic stream
 // serialization (PDL) so that consecutive kernels of a decode step overlap their
 // launch and prologue with the tail of the previous kernel.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -293,16 +295,63 @@ int spark_q4_dequantize_bf16(const uint8_t* qs, const uint16_t* d, int64_t rows,
   return cudaGetLastError() == cudaSuccess ? SPARK_OK : SPARK_ERR_LAUNCH;
 }
 
+// cuTensorMapEncodeTiled from the driver, through the runtime's entry-point query (no
+// link against libcuda)
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D tensor map: `inner` elements per row (row pitch `pitch` bytes), `outer` rows
+static bool encode_map(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
+                       uint64_t pitch, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle sw) {
+  auto fn = tensor_map_encoder();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {pitch};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 int spark_q4_gemm_tc(const uint16_t* x, const uint8_t* qs, const uint16_t* d, uint16_t* y, int t, int n, int k,
                      int* error, int64_t wait_ns, void* stream) {
   if (!x || !qs || !d || !y || !error) return SPARK_ERR_INVALID_ARG;
-  if (t <= 0 || n <= 0 || k <= 0 || k % tc::kBK || t > 65535 * tc::kBN) return SPARK_ERR_UNSUPPORTED_SHAPE;
-  if (!aligned(x, 16) || !aligned(qs, 16) || !aligned(d, 2) || !aligned(y, 2) || !aligned(error, 4))
+  if (t <= 0 || n <= 0 || k <= 0 || k % tc::kRK) return SPARK_ERR_UNSUPPORTED_SHAPE;
+  if (!aligned(x, 16) || !aligned(qs, 16) || !aligned(d, 16) || !aligned(y, 2) || !aligned(error, 4))
     return SPARK_ERR_ALIGNMENT;
   if (set_smem(reinterpret_cast<const void*>(&tc::q4_gemm_tc_kernel), tc::kSmemBytes)) return SPARK_ERR_LAUNCH;
-  const dim3 grid((unsigned)((n + tc::kBM - 1) / tc::kBM), (unsigned)((t + tc::kBN - 1) / tc::kBN));
+  // 256-token tiles unless 128 gives fewer partial waves (the 128-token tile dequantizes
+  // twice the weights per product, weighed at 1.25)
+  const int sms = num_sms();
+  const long long ntm = (n + tc::kBM - 1) / tc::kBM;
+  auto cost = [&](int bn) {
+    const long long tiles = ntm * ((t + bn - 1) / bn);
+    return (double)((tiles + sms - 1) / sms) * bn * (bn == 128 ? 1.25 : 1.0);
+  };
+  const int bn = cost(128) < cost(256) ? 128 : 256;
+  CUtensorMap mx, mq, md;
+  if (!encode_map(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)k, (uint64_t)t, (uint64_t)k * 2, tc::kBK,
+                  (uint32_t)bn, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_map(&mq, CU_TENSOR_MAP_DATA_TYPE_UINT8, qs, (uint64_t)k / 2, (uint64_t)n, (uint64_t)k / 2,
+                  tc::kRK / 2, tc::kBM, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_map(&md, CU_TENSOR_MAP_DATA_TYPE_UINT16, d, (uint64_t)k / 32, (uint64_t)n, (uint64_t)k / 16,
+                  tc::kRK / 32, tc::kBM, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return SPARK_ERR_LAUNCH;
+  const long long ntiles = ntm * ((t + bn - 1) / bn);
+  const int grid = (int)std::min<long long>(ntiles, sms);
   const unsigned long long limit = wait_ns < 0 ? tc::kWaitNs : (unsigned long long)wait_ns;
-  tc::q4_gemm_tc_kernel<<<grid, tc::kThreads, tc::kSmemBytes, as_stream(stream)>>>(x, qs, d, y, t, n, k, error, limit);
+  tc::q4_gemm_tc_kernel<<<grid, tc::kThreads, tc::kSmemBytes, as_stream(stream)>>>(mx, mq, md, y, t, n, k, bn,
+                                                                                   error, limit);
   return cudaGetLastError() == cudaSuccess ? SPARK_OK : SPARK_ERR_LAUNCH;
 }
 

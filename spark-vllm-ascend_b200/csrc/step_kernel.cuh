@@ -1724,6 +1724,16 @@ constexpr int kCombineLseOff = kCombineBytes;     // lse [4][S], weights [4][S],
 constexpr int kMaxCombineSplits = (kScratchBytes - kCombineLseOff - 16) / 32;
 constexpr int kXinOff = 32 * 1024;                // combined output (bf16) before the o_proj staging
 
+// the decoded token's K and V rows (2 x D bf16), copied from kv_new by the range that
+// holds it, past the split's scores and P
+constexpr int kKvNewOff = 24 * kMaxSplitTokens;
+static_assert(kKvNewOff % 16 == 0 && kKvNewOff + 4 * 256 <= kScratchBytes, "kv_new rows in the scratch");
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 __host__ __device__ __forceinline__ int warp_range(int n, int tpi) {
   const int c = (n + kWarps - 1) / kWarps;
   return (c + tpi - 1) / tpi * tpi;
@@ -1800,6 +1810,18 @@ __device__ __forceinline__ bool attn_split(const StepParams& P, const SparkStage
     for (int d = 0; d < DL; d++) acc[h][d] = 0.0f;
   bool ok = true;
   cstamp(tr, 12);
+  // The token being decoded (pos, the last token of the last split) is peeled off both
+  // loops: its K / V come from kv_new (this launch's qkv stage wrote them; the ring's copy
+  // of its run predates that), so the loops themselves read shared memory only.  Its two
+  // rows are copied into the scratch together with the q loads, so their L2 round trip
+  // overlaps the scores instead of following them.
+  const bool has_pos = a < b && pos >= t0 + a && pos < t0 + b;  // then pos = t0 + b - 1
+  if (has_pos) {
+    const uint32_t kvs = smem_u32(s.scratch + kKvNewOff);
+    const uint16_t* kr = kv_new + (size_t)g * D;
+    const uint16_t* vr = kv_new + ((size_t)st.nkv + g) * D;
+    for (int c = lane; c < 2 * (D / 8); c += 32) cp_async16(kvs + 16 * c, c < D / 8 ? kr + 8 * c : vr + 8 * (c - D / 8));
+  }
   if (a < b) {
     float qf[4][16];
     {
@@ -1816,10 +1838,6 @@ __device__ __forceinline__ bool attn_split(const StepParams& P, const SparkStage
         }
       }
     }
-    // The token being decoded (pos, the last token of the last split) is peeled off both
-    // loops: its K / V come from kv_new (this launch's qkv stage wrote them; the ring's copy
-    // of its run predates that), so the loops themselves read shared memory only.
-    const bool has_pos = pos >= t0 + a && pos < t0 + b;  // then pos = t0 + b - 1
     const int bl = has_pos ? b - 1 : b;                  // ring tokens of the range: [a, bl)
     // ---- scores (a TPI-token step never crosses a 64-token run: t0 and a are multiples of TPI)
     int waited = -1;
@@ -1870,10 +1888,14 @@ __device__ __forceinline__ bool attn_split(const StepParams& P, const SparkStage
         if (valid) mx[h] = sc[h] > mx[h] ? sc[h] : mx[h];
       if (jj == 0 && in) rec[i] = valid ? make_float4(sc[0], sc[1], sc[2], sc[3]) : make_float4(ninf, ninf, ninf, ninf);
     }
+    if (has_pos) {  // the warp's copies of the decoded token's rows
+      cp_async_wait_all();
+      __syncwarp();
+    }
     if (ok && has_pos) {  // every lane group scores the decoded token; group 0 stores it
-      const uint16_t* kr = kv_new + (size_t)g * D;
-      const uint4 k0 = __ldcg(reinterpret_cast<const uint4*>(kr + 8 * jj));
-      const uint4 k1 = __ldcg(reinterpret_cast<const uint4*>(kr + D / 2 + 8 * jj));
+      const unsigned char* kvn = s.scratch + kKvNewOff;
+      const uint4 k0 = *reinterpret_cast<const uint4*>(kvn + 16 * jj);
+      const uint4 k1 = *reinterpret_cast<const uint4*>(kvn + D + 16 * jj);
       float sc[4];
       dot4(k0, k1, sc);
 #pragma unroll
@@ -1971,16 +1993,7 @@ __device__ __forceinline__ bool attn_split(const StepParams& P, const SparkStage
       if (ok && has_pos) {
         const uint2 pw = pbf[b - 1];
         float v4[DL];
-        if constexpr (D == 128) {
-          const uint2 vv = __ldcg(reinterpret_cast<const uint2*>(kv_new + ((size_t)st.nkv + g) * D + 4 * lane));
-          v4[0] = bf_lo(vv.x);
-          v4[1] = bf_hi(vv.x);
-          v4[2] = bf_lo(vv.y);
-          v4[3] = bf_hi(vv.y);
-        } else {
-          const uint4 vv = __ldcg(reinterpret_cast<const uint4*>(kv_new + ((size_t)st.nkv + g) * D + 8 * lane));
-          unpack8(vv, v4);
-        }
+        v_load(smem_u32(s.scratch + kKvNewOff) + 2 * D + lane * (2 * DL), v4);
         pv_token(pw, v4);
       }
       if (ok) release_runs(s, seq_base + nruns, r0, r1, t0, t1, w0, C, lane);  // V runs
@@ -2061,10 +2074,6 @@ __device__ __forceinline__ bool attn_split(const StepParams& P, const SparkStage
   return true;
 }
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 // All 4 x D combined outputs of kv head g from its S published partials (the oracle's
 // combine order).  The partials come into the scratch with 16-byte asynchronous copies,

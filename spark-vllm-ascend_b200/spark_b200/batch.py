@@ -190,8 +190,8 @@ class BatchDecodeEngine:
         self.pos.copy_(torch.as_tensor(pos, dtype=torch.int64).reshape(self.batch))
 
     def prefill(self, prompts, chunk: int = 2048) -> torch.Tensor:
-        """Prefill each sequence's prompt (``spark_b200.prefill``: dequantized bf16 GEMMs,
-        causal attention, K / V into the sequence's own blocks).  Returns the first
+        """Prefill each sequence's prompt (``spark_b200.prefill``: tensor-core GEMMs over the
+        Q4_0 weights, causal attention, K / V into the sequence's own blocks).  Returns the first
         generated token of every sequence (int32 [B])."""
         from .prefill import prefill
         if len(prompts) != self.batch:

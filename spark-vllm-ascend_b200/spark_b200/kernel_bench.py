@@ -232,6 +232,34 @@ def bench_step_attn(ctx, reps, copies, device, gen, cfg):
     return {"us": round(us, 3), "bytes": byts, "gbs": round(byts / us / 1e3, 1), "splits": splits}
 
 
+def bench_prefill_gemm(tokens, reps, device, gen, cfg, only=None):
+    """The prefill GEMMs of one layer (qkv, o, gate_up, down) at ``tokens`` prompt tokens:
+    the tcgen05 Q4_0 GEMM (``spark_q4_gemm_tc``) against cuBLAS over a cached bf16
+    dequantization and against dequantize + cuBLAS.  µs per launch and TFLOP/s."""
+    h, i = cfg.hidden_size, cfg.intermediate_size
+    nh = cfg.num_q_heads + 2 * cfg.num_kv_heads
+    shapes = {"qkv": (nh * cfg.head_dim, h), "o": (h, cfg.num_q_heads * cfg.head_dim), "gate_up": (2 * i, h),
+              "down": (h, i)}
+    res = {}
+    for name, (n, k) in shapes.items():
+        if only and name not in only:
+            continue
+        qs, d = _q4(n, k, device, gen)
+        x = torch.randn((tokens, k), generator=gen, device=device).to(BF16)
+        err = torch.zeros(1, dtype=torch.int32, device=device)
+        wb = ops.q4_dequantize(qs, d)
+        flop = 2.0 * tokens * n * k
+        t_tc = _time(lambda _: ops.q4_gemm(x, qs, d, err), reps)
+        t_blas = _time(lambda _: x @ wb.t(), reps)
+        t_deq = _time(lambda _: x @ ops.q4_dequantize(qs, d).t(), reps)
+        torch.cuda.synchronize()
+        res[name] = {"shape": [tokens, n, k], "tc_us": round(t_tc, 1), "tc_tflops": round(flop / t_tc / 1e6, 1),
+                     "cublas_cached_bf16_us": round(t_blas, 1), "dequant_cublas_us": round(t_deq, 1),
+                     "error": int(err.item())}
+        del qs, d, x, wb
+    return res
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--kernels", default="gemv,qkv,o_proj,gate_up,down,head,attn")
@@ -239,6 +267,8 @@ def main(argv=None):
     ap.add_argument("--copies", type=int, default=16)
     ap.add_argument("--ctx", default="2048,4096,6144")
     ap.add_argument("--splits", type=int, default=16)
+    ap.add_argument("--tokens", type=int, default=2048, help="prompt tokens of --kernels prefill_gemm")
+    ap.add_argument("--gemm-shapes", default="", help="prefill_gemm: a subset of qkv,o,gate_up,down")
     ap.add_argument("--direct", action="store_true", help="register-direct GEMV instead of the weight ring")
     ap.add_argument("--step", action="store_true",
                     help="stages of the persistent decode-step kernel (one cooperative launch each)")
@@ -254,6 +284,9 @@ def main(argv=None):
             n, k, kind = cases[name]
             fn = bench_step_gemv if args.step else bench_gemv
             out[name] = fn(name, n, k, kind, args.reps, args.copies, device, gen, cfg)
+        elif name == "prefill_gemm":
+            out[name] = bench_prefill_gemm(args.tokens, args.reps, device, gen, cfg,
+                                           args.gemm_shapes.split(",") if args.gemm_shapes else None)
         elif name == "head_q6" and args.step:
             out[name] = bench_step_q6_head(args.reps, args.copies, device, gen)
         elif name == "attn":

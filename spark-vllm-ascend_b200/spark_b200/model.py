@@ -503,14 +503,15 @@ class DecodeEngine:
         # the last step's argmax is the first generated token
         return self.token.clone()
 
-    def prefill_batched(self, prompt: torch.Tensor | list[int], chunk: int = 2048) -> torch.Tensor:
-        """Prefill all prompt tokens of a chunk at once (``spark_b200.prefill``: dequantized
-        bf16 GEMMs and causal attention, the reference's standard prefill path) instead of
-        one decode step per token; single GPU.  Returns the first generated token."""
+    def prefill_batched(self, prompt: torch.Tensor | list[int], chunk: int = 2048, gemm: str = "q4") -> torch.Tensor:
+        """Prefill all prompt tokens of a chunk at once (``spark_b200.prefill``: tensor-core
+        GEMMs over the Q4_0 weights, or cuBLAS over cached bf16 ones with gemm="bf16", and
+        causal attention: the reference's standard prefill path) instead of one decode
+        step per token; single GPU.  Returns the first generated token."""
         if self.tp_size > 1:
             raise ValueError("batched prefill runs on one GPU")
         from .prefill import prefill
-        return prefill(self, prompt, chunk)
+        return prefill(self, prompt, chunk, gemm)
 
     def generate(self, prompt, max_new_tokens: int) -> list[int]:
         """Greedy decode: returns the generated token ids (host list)."""

@@ -85,7 +85,7 @@ def q4_dequantize(qs: torch.Tensor, d: torch.Tensor) -> torch.Tensor:
 def q4_gemm(x: torch.Tensor, qs: torch.Tensor, d: torch.Tensor, error: torch.Tensor,
             wait_ns: int = -1) -> torch.Tensor:
     """Prefill GEMM on the tensor cores: x bf16 [T, K] times the Q4_0 weight [N, K]
-    (dequantized in shared memory) -> bf16 [T, N].  K % 64 == 0.  ``error`` (int32 [1],
+    (dequantized in shared memory) -> bf16 [T, N].  K % 256 == 0.  ``error`` (int32 [1],
     required, on the device) becomes nonzero if a wait inside the kernel ran out, and y
     is then not valid: the caller owns the status word and must read it.  ``wait_ns``
     bounds each wait (-1: the kernel's 0.5 s; 0: give up at once, for tests)."""

@@ -2,19 +2,23 @@
 
 The reference keeps vLLM's standard PyTorch path for prefill and runs its megakernel
 for decode only (integration/model.py:50-62: query length > 1 falls back to the torch
-layer).  This is the same split on B200: each layer's Q4_0 weights are dequantized to
-bf16 by ``spark_q4_dequantize_bf16`` (the reference's ``dequantize(...).bfloat16()``,
-weights.py:28-31) and multiplied by the chunk's activations with bf16 tensor-core GEMMs
-(fp32 accumulation), attention is causal scaled-dot-product attention over the paged
-cache (the chunk's own K / V are written into it first), and the element-wise steps
-follow the decode engine's semantics (bf16 residual, fp32 RMSNorm, bf16-rounded inputs
-to the fp32 RoPE, SiLU / GELU of the bf16 gate, the Spark output gate and sliding
-window); add + RMSNorm, RoPE and the activation * mul run as row-batched kernels
-(``spark_add_rmsnorm_rows``, ``spark_rope_neox_rows``, ``spark_act_mul_rows``, the last
-with the decode epilogues' SiLU / GELU-table arithmetic).  Results agree with token-by-token decode within bf16 rounding, not bit for
-bit (the GEMM summation order is cuBLAS's).  The bf16 weights are made once per engine
-(2 bytes per weight of HBM, kept for later prompts).  After ``prefill`` the engine holds
-the prompt's K / V, ``pos`` = prompt length and ``token`` = the first generated token.
+layer); its linear layers multiply by the bf16 dequantization of each Q4_0 weight
+(``dequantize(...).bfloat16()``, weights.py:28-31).  This is the same split on B200.  The
+four projections of a layer run on the tensor cores straight from the Q4_0 planes
+(``gemm="q4"``, the default: ``spark_q4_gemm_tc``, weights dequantized to bf16 in shared
+memory, tcgen05 MMAs with fp32 accumulation; no bf16 copy of the weights in HBM), or, with
+``gemm="bf16"``, as cuBLAS bf16 GEMMs over a bf16 dequantization made once per engine (2
+bytes per weight of HBM, 4.5 GB for the 4B models; kept for later prompts).  Attention is
+causal scaled-dot-product attention over the paged cache (the chunk's own K / V are
+written into it first), and the element-wise steps follow the decode engine's semantics
+(bf16 residual, fp32 RMSNorm, bf16-rounded inputs to the fp32 RoPE, SiLU / GELU of the
+bf16 gate, the Spark output gate and sliding window); add + RMSNorm, RoPE and the
+activation * mul run as row-batched kernels (``spark_add_rmsnorm_rows``,
+``spark_rope_neox_rows``, ``spark_act_mul_rows``, the last with the decode epilogues'
+SiLU / GELU-table arithmetic).  Results agree with token-by-token decode within bf16
+rounding, not bit for bit (the GEMM summation order is the tensor cores').  After
+``prefill`` the engine holds the prompt's K / V, ``pos`` = prompt length and ``token`` =
+the first generated token.
 """
 from __future__ import annotations
 
@@ -49,6 +53,22 @@ def _bf16_weights(eng) -> list:
     return eng._prefill_w
 
 
+class _Q4Linear:
+    """x @ W^T for a Q4_0 weight on the tensor cores (``spark_q4_gemm_tc``); every call
+    reports into one device status word that ``check`` reads once per prefill."""
+
+    def __init__(self, device):
+        self.err = torch.zeros(1, dtype=torch.int32, device=device)
+
+    def __call__(self, x, q):
+        return ops.q4_gemm(x, q.qs, q.d, self.err)
+
+    def check(self):
+        e = int(self.err.item())
+        if e:
+            raise RuntimeError(f"spark_q4_gemm_tc: a wait inside the kernel ran out (status {e})")
+
+
 def _gather(cache: torch.Tensor, table: torch.Tensor, n: int, bs: int) -> torch.Tensor:
     """Positions [0, n) of one layer's paged cache [blocks, nkv, bs, D] -> [nkv, n, D]."""
     pos = torch.arange(n, device=cache.device)
@@ -56,9 +76,10 @@ def _gather(cache: torch.Tensor, table: torch.Tensor, n: int, bs: int) -> torch.
 
 
 @torch.no_grad()
-def prefill(eng, prompt: torch.Tensor, chunk: int = 2048) -> torch.Tensor:
+def prefill(eng, prompt: torch.Tensor, chunk: int = 2048, gemm: str = "q4") -> torch.Tensor:
     """Fill ``eng``'s KV cache with ``prompt`` (int32 [P]) from position 0 and set the
-    first generated token; returns it (int32 [1])."""
+    first generated token; returns it (int32 [1]).  ``gemm``: "q4" (tensor-core GEMMs
+    over the Q4_0 planes) or "bf16" (cuBLAS over a cached bf16 dequantization)."""
     cfg, w = eng.cfg, eng.w
     dev = eng.device
     prompt = torch.as_tensor(prompt, dtype=torch.int64).to(dev)
@@ -69,7 +90,14 @@ def prefill(eng, prompt: torch.Tensor, chunk: int = 2048) -> torch.Tensor:
                             cfg.head_dim, cfg.block_size)
     nh, eps, scale = nq + 2 * nkv, cfg.rms_norm_eps, cfg.attn_scale
     table = eng.block_table
-    wb = _bf16_weights(eng)
+    if gemm not in ("q4", "bf16"):
+        raise ValueError(f"gemm must be 'q4' or 'bf16', not {gemm!r}")
+    if gemm == "q4":
+        q4 = _Q4Linear(dev)
+        mats = [((lambda x, m=l.qkv: q4(x, m)), (lambda x, m=l.o: q4(x, m)), (lambda x, m=l.gate_up: q4(x, m)),
+                 (lambda x, m=l.down: q4(x, m))) for l in w.layers]
+    else:
+        mats = [tuple((lambda x, wt=wt: x @ wt.t()) for wt in ws) for ws in _bf16_weights(eng)]
     heads = torch.arange(nkv, device=dev)
     eng.reset(0)
     a_last = b_last = None
@@ -79,9 +107,9 @@ def prefill(eng, prompt: torch.Tensor, chunk: int = 2048) -> torch.Tensor:
         pos = torch.arange(p0, p1, device=dev)
         a = w.embed[prompt[p0:p1]]  # bf16 [n, h]
         b = None
-        for li, (lw, (w_qkv, w_o, w_gu, w_down)) in enumerate(zip(w.layers, wb)):
+        for li, (lw, (w_qkv, w_o, w_gu, w_down)) in enumerate(zip(w.layers, mats)):
             res, x = ops.add_rmsnorm_rows(a, b, lw.in_norm, eps)  # (norm of the fp32 sum a + b)
-            y = x @ w_qkv.t()
+            y = w_qkv(x)
             _, rot = cfg.layer_rope(li)
             cs = w.layer_cos_sin(li) if hasattr(w, "layer_cos_sin") else w.cos_sin
             ops.rope_rows_(y, nq + nkv, D, rot, cs, p0)  # q and k heads, in place
@@ -111,11 +139,11 @@ def prefill(eng, prompt: torch.Tensor, chunk: int = 2048) -> torch.Tensor:
             if cfg.attn_gate:
                 g = torch.sigmoid(y[:, nh * D:nh * D + nq].float()).to(BF16)
                 o = (o.float() * g.float()[:, :, None]).to(BF16)
-            oproj = o.reshape(n, nq * D) @ w_o.t()
+            oproj = w_o(o.reshape(n, nq * D))
             resmid, x2 = ops.add_rmsnorm_rows(oproj, res, lw.post_norm, eps)
-            gu = x2 @ w_gu.t()
+            gu = w_gu(x2)
             mid = ops.act_mul_rows(gu, getattr(eng, "gelu", None) if cfg.hidden_act == "gelu" else None)
-            a = mid @ w_down.t()
+            a = w_down(mid)
             b = resmid
         a_last, b_last = a[-1:], b[-1:]
     # LM head of the last position, greedy
@@ -131,6 +159,8 @@ def prefill(eng, prompt: torch.Tensor, chunk: int = 2048) -> torch.Tensor:
         logits[r0:r1] = (x @ wt.t())[0]
     eng.logits.copy_(logits)
     tok = torch.argmax(logits.float()).to(torch.int32).reshape(1)
+    if gemm == "q4":
+        q4.check()
     eng.token.copy_(tok)
     eng.pos.fill_(P)
     eng.step_idx.zero_()
@@ -150,28 +180,29 @@ def main(argv=None):
     ap.add_argument("--model", choices=["synthetic-4b", "spark-x26"], default="synthetic-4b")
     ap.add_argument("--tokens", type=int, default=2048)
     ap.add_argument("--profile", action="store_true")
+    ap.add_argument("--gemm", choices=["q4", "bf16"], default="q4")
     args = ap.parse_args(argv)
     cfg = spark_x26_config() if args.model == "spark-x26" else SparkConfig()
     w = SyntheticWeights(cfg, device="cuda", seed=0)
     eng = DecodeEngine(w, max_seq_len=args.tokens + 64, num_blocks=(args.tokens + 64) // 128 + 8, use_graph=False)
     prompt = torch.randint(0, cfg.vocab_size, (args.tokens,), generator=torch.Generator().manual_seed(0),
                            dtype=torch.int32)
-    eng.prefill_batched(prompt)
+    eng.prefill_batched(prompt, gemm=args.gemm)
     torch.cuda.synchronize()
     best = None
     for _ in range(3):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        eng.prefill_batched(prompt)
+        eng.prefill_batched(prompt, gemm=args.gemm)
         e1.record()
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1)
         best = ms if best is None else min(best, ms)
-    print(json.dumps({"model": cfg.name, "tokens": args.tokens, "ttft_ms": round(best, 3)}))
+    print(json.dumps({"model": cfg.name, "tokens": args.tokens, "gemm": args.gemm, "ttft_ms": round(best, 3)}))
     if args.profile:
         from torch.profiler import ProfilerActivity, profile
         with profile(activities=[ProfilerActivity.CUDA]) as prof:
-            eng.prefill_batched(prompt)
+            eng.prefill_batched(prompt, gemm=args.gemm)
             torch.cuda.synchronize()
         print(prof.key_averages().table(sort_by="cuda_time_total", row_limit=12, max_name_column_width=70))
 

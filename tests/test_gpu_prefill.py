@@ -1,7 +1,7 @@
-"""Batched prefill (spark_b200.prefill: dequantized bf16 GEMMs + causal attention, the
-reference's standard prefill path) against token-by-token decode of the same prompt:
+"""Batched prefill (spark_b200.prefill: tensor-core GEMMs over the Q4_0 planes, or cuBLAS
+over cached bf16 weights, + causal attention, the reference's standard prefill path) against token-by-token decode of the same prompt:
 the paged K / V of every prompt position and the first token's logits agree within
-bf16 rounding (not bit for bit: cuBLAS sums in its own order), for the synthetic
+bf16 rounding (not bit for bit: the GEMMs sum in their own order), for the synthetic
 architecture and the Spark one (gate, GELU, sliding window shorter than the prompt,
 partial RoPE, Q6_K head), with a prompt split over two chunks; decode continues from
 the batched state."""
@@ -19,8 +19,9 @@ def _cfgs():
                              vocab_size=4096, sliding_window=33, max_position=4096, name="spark-tiny")]
 
 
+@pytest.mark.parametrize("gemm", ["q4", "bf16"])
 @pytest.mark.parametrize("which", [0, 1])
-def test_batched_prefill_matches_decode(cuda, which):
+def test_batched_prefill_matches_decode(cuda, which, gemm):
     import torch
     from spark_b200.model import DecodeEngine, SyntheticWeights
     cfg = _cfgs()[which]
@@ -31,7 +32,7 @@ def test_batched_prefill_matches_decode(cuda, which):
     ref.prefill(prompt)
     torch.cuda.synchronize()
     eng = DecodeEngine(w, max_seq_len=256, num_blocks=8, seed=11)
-    eng.prefill_batched(prompt, chunk=64)  # two chunks: the second attends to the first's cache
+    eng.prefill_batched(prompt, chunk=64, gemm=gemm)  # two chunks: the second attends to the first's cache
     torch.cuda.synchronize()
     bs = cfg.block_size
     pos = torch.arange(P, device="cuda")

@@ -13,7 +13,7 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 SHAPES = [  # (tokens, rows, K)
-    (1, 128, 64),
+    (1, 128, 256),
     (77, 200, 2560),
     (128, 256, 4096),
     (300, 6144, 2560),
@@ -75,15 +75,15 @@ def test_q4_gemm_tc_identity_is_bit_exact_dequant(cuda, n, k):
 def test_q4_gemm_tc_rejects_bad_shapes(cuda):
     import torch
     from spark_b200 import ops
-    qs, d = _planes(128, 96, seed=1)  # K = 96: not a multiple of 64
-    x = torch.zeros((4, 96), dtype=torch.bfloat16, device="cuda")
+    qs, d = _planes(128, 320, seed=1)  # K = 320: not a multiple of 256
+    x = torch.zeros((4, 320), dtype=torch.bfloat16, device="cuda")
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
     with pytest.raises(Exception):
         ops.q4_gemm(x, qs, d, err)
 
 
 def test_q4_gemm_tc_wait_timeout_reports_and_recovers(cuda):
-    """A wait limit of 0 ns makes the first unfinished MMA wait give up: the kernel must
+    """A wait limit of 0 ns makes the first unfinished wait give up: the kernel must
     return (no hang), report 1 in the caller's status word (not 2: the issued MMAs drained
     and the tensor memory was freed), and the next call with the default limit must
     match the dequantize + fp32 product again on the same context."""
