@@ -9,8 +9,8 @@
 // bf16 operands, fp32 accumulators in tensor memory).
 //
 // Persistent, warp-specialized; one CTA per SM walks output tiles of 128 weight rows
-// (MMA M = TMEM lanes) x bn tokens (MMA N = TMEM columns, bn = 256, or 128 when that
-// gives fewer partial waves).  448 threads:
+// (MMA M = TMEM lanes) x bn tokens (MMA N = TMEM columns; the host passes bn = 256, the
+// kernel also takes 128).  448 threads:
 //   warp 0      TMA producer: per 64-wide K step the activation tile X[bn][64] (bf16,
 //               128-byte swizzle); per 256-wide K stage the weight rows' nibbles
 //               [128][128 B] (128-byte swizzle) and fp16 scales [128][8];
@@ -47,7 +47,7 @@ namespace spark {
 namespace tc {
 
 constexpr int kBM = 128;        // weight rows per tile (MMA M)
-constexpr int kBNMax = 256;     // tokens per tile (MMA N), 256 or 128
+constexpr int kBNMax = 256;     // tokens per tile (MMA N)
 constexpr int kBK = 64;         // K per MMA step: one 128-byte swizzle atom of bf16
 constexpr int kRK = 256;        // K per raw Q4_0 stage: 128 B of nibbles per row
 constexpr int kStepsPerR = kRK / kBK;

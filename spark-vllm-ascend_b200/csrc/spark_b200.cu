@@ -330,15 +330,12 @@ int spark_q4_gemm_tc(const uint16_t* x, const uint8_t* qs, const uint16_t* d, ui
   if (!aligned(x, 16) || !aligned(qs, 16) || !aligned(d, 16) || !aligned(y, 2) || !aligned(error, 4))
     return SPARK_ERR_ALIGNMENT;
   if (set_smem(reinterpret_cast<const void*>(&tc::q4_gemm_tc_kernel), tc::kSmemBytes)) return SPARK_ERR_LAUNCH;
-  // 256-token tiles unless 128 gives fewer partial waves (the 128-token tile dequantizes
-  // twice the weights per product, weighed at 1.25)
+  // 256-token tiles for every shape: 128-token tiles dequantize twice the weights per
+  // product and measured slower even where they fill the SMs better (o / down: 320
+  // tiles of 128 tokens 121 / 272 us, 160 tiles of 256 tokens 88 / 187 us)
   const int sms = num_sms();
   const long long ntm = (n + tc::kBM - 1) / tc::kBM;
-  auto cost = [&](int bn) {
-    const long long tiles = ntm * ((t + bn - 1) / bn);
-    return (double)((tiles + sms - 1) / sms) * bn * (bn == 128 ? 1.25 : 1.0);
-  };
-  const int bn = cost(128) < cost(256) ? 128 : 256;
+  const int bn = tc::kBNMax;
   CUtensorMap mx, mq, md;
   if (!encode_map(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)k, (uint64_t)t, (uint64_t)k * 2, tc::kBK,
                   (uint32_t)bn, CU_TENSOR_MAP_SWIZZLE_128B) ||
