@@ -5,7 +5,11 @@
 // outputs are bit-identical to the register-direct kernel and to the CPU oracle.
 // What changes is how the weights reach the SM:
 //
-//   * one CTA per SM (grid = number of SMs), 12 consumer warps + 1 producer warp;
+//   * one CTA per SM (grid = number of SMs), 12 consumer warps + 1 producer warp; at
+//     most 72 registers per thread (launch bounds of 2 CTAs per SM), so when the ring
+//     fits half the shared memory (the single-op GEMV of 9728 x 2560, qkv, o_proj) the
+//     next launch's CTA is resident beside this one and its producer streams weights
+//     while this CTA finishes (back-to-back 9728 x 2560: 5.9 -> 5.0 us);
 //   * the CTA owns a contiguous range of "units" (a unit is a row pair in pair mode,
 //     one row in single mode); units are processed in rounds of up to 24 (one per
 //     consumer half warp), each round in K-chunks of 16*CB blocks per row;
@@ -121,7 +125,7 @@ __device__ __forceinline__ void ring_finish(const GemvArgs& g, EpiState& st, uns
 
 // NB: blocks per row when known at compile time (0 = runtime, generic loop).
 template <class Pro, class Epi, int ROWS, int NB>
-__global__ void __launch_bounds__(kRingThreads, 1) q4_gemv_ring_kernel(const GemvArgs g, const RingPlan plan) {
+__global__ void __launch_bounds__(kRingThreads, 2) q4_gemv_ring_kernel(const GemvArgs g, const RingPlan plan) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   // staged x (xq: 64 B per block, xm: 8 B per block), reduction scratch, norm scratch
   const uint4* xq = reinterpret_cast<const uint4*>(smem_raw);

@@ -2105,12 +2105,12 @@ __device__ __forceinline__ void attn_combine_all(const SparkStage& st, const Sme
       cp_async16(pc_u + (uint32_t)(sp * CH + q) * 16, part_o + ((size_t)(s0 + sp) * nq + 4 * g) * D + 4 * q);
     }
   };
+  // the first round's partials stay in flight while the weights are computed from the lse
   fetch(0);
   for (int i = tid; i < 4 * S; i += kConsumers) {
     const int h = i / S, sp = i - h * S;
     lse_s[i] = __ldcg(part_lse + (size_t)sp * nq + 4 * g + h);
   }
-  cp_async_wait_all();
   consumer_bar();
   cstamp(tr, 19);
   if (warp < 4) {  // warp h: max, exp, the sequential denominator and w / den of head h
@@ -2141,7 +2141,8 @@ __device__ __forceinline__ void attn_combine_all(const SparkStage& st, const Sme
     for (int sp = lane; sp < S; sp += 32) w_s[h * S + sp] = __fdiv_rn(w_s[h * S + sp], den);
     if (lane == 0) mx_s[h] = m;
   }
-  consumer_bar();
+  cp_async_wait_all();
+  consumer_bar();  // the weights and the first round's partials
   cstamp(tr, 20);
   float a[NO];
 #pragma unroll
