@@ -212,6 +212,124 @@ __global__ void act_mul_rows_kernel(const uint16_t* __restrict__ gu, int64_t n, 
   }
 }
 
+// ------------------------------------------------------------------ 16-byte forms of the row kernels
+// The same per-element arithmetic as the three kernels above (RMSNorm: per-thread fma
+// partials, warp butterflies, the 8 warp totals in order), moved 8 bf16 values per
+// 16-byte load / store.  The host uses them when the row lengths are multiples of 8 and
+// the rows 16-byte aligned.
+__device__ __forceinline__ void unpack8_bf16(const uint4 u, float (&v)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int t = 0; t < 4; t++) {
+    v[2 * t] = bf_lo(w[t]);
+    v[2 * t + 1] = bf_hi(w[t]);
+  }
+}
+__device__ __forceinline__ uint4 pack8_bf16(const float (&v)[8]) {
+  uint32_t w[4];
+#pragma unroll
+  for (int t = 0; t < 4; t++) w[t] = (uint32_t)f2bf(v[2 * t]) | ((uint32_t)f2bf(v[2 * t + 1]) << 16);
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+constexpr int kRowGroupsPerThread = 4;  // add + RMSNorm: hidden <= 256 x 8 x 4 = 8192
+
+__global__ void __launch_bounds__(256) add_rmsnorm_rows_v8_kernel(const uint16_t* __restrict__ a,
+                                                                  const uint16_t* __restrict__ b,
+                                                                  const uint16_t* __restrict__ gamma, float eps,
+                                                                  float inv_h, int h, uint16_t* res_out, uint16_t* y) {
+  __shared__ float red[8];
+  const size_t off = (size_t)blockIdx.x * h;
+  const int ng = h >> 3;
+  float sv[kRowGroupsPerThread][8];
+  float part = 0.0f;
+#pragma unroll
+  for (int q = 0; q < kRowGroupsPerThread; q++) {
+    const int gi = threadIdx.x + q * 256;
+    if (gi < ng) {
+      unpack8_bf16(*reinterpret_cast<const uint4*>(a + off + 8 * gi), sv[q]);
+      if (b) {
+        float bv[8];
+        unpack8_bf16(*reinterpret_cast<const uint4*>(b + off + 8 * gi), bv);
+#pragma unroll
+        for (int j = 0; j < 8; j++) sv[q][j] = __fadd_rn(sv[q][j], bv[j]);
+      }
+      if (res_out) *reinterpret_cast<uint4*>(res_out + off + 8 * gi) = pack8_bf16(sv[q]);
+#pragma unroll
+      for (int j = 0; j < 8; j++) part = __fmaf_rn(sv[q][j], sv[q][j], part);
+    }
+  }
+  part = butterfly_sum<32>(part);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = part;
+  __syncthreads();
+  float tot = 0.0f;
+  for (int w = 0; w < (int)(blockDim.x >> 5); w++) tot += red[w];
+  const float inv = rsqrtf(__fadd_rn(__fmul_rn(tot, inv_h), eps));
+#pragma unroll
+  for (int q = 0; q < kRowGroupsPerThread; q++) {
+    const int gi = threadIdx.x + q * 256;
+    if (gi < ng) {
+      float gv[8], o[8];
+      unpack8_bf16(*reinterpret_cast<const uint4*>(gamma + 8 * gi), gv);
+#pragma unroll
+      for (int j = 0; j < 8; j++) o[j] = __fmul_rn(__fmul_rn(sv[q][j], inv), gv[j]);
+      *reinterpret_cast<uint4*>(y + off + 8 * gi) = pack8_bf16(o);
+    }
+  }
+}
+
+// pairs (i .. i + 7, i + half .. i + half + 7) of one head of one row per thread
+__global__ void rope_rows_v8_kernel(uint16_t* x, int64_t row_stride, int n, int nh, int dim, int rot,
+                                    const uint16_t* __restrict__ cos_sin, int64_t pos0) {
+  const int half = rot >> 1, hg = half >> 3;
+  const int64_t total = (int64_t)n * nh * hg;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = idx / (nh * hg);
+    const int rem = (int)(idx - r * nh * hg), h = rem / hg, i = 8 * (rem - h * hg);
+    uint16_t* v = x + r * row_stride + (int64_t)h * dim;
+    const uint16_t* cs = cos_sin + (pos0 + r) * rot;
+    float a[8], b[8], c[8], sn[8], o0[8], o1[8];
+    unpack8_bf16(*reinterpret_cast<const uint4*>(v + i), a);
+    unpack8_bf16(*reinterpret_cast<const uint4*>(v + i + half), b);
+    unpack8_bf16(*reinterpret_cast<const uint4*>(cs + i), c);
+    unpack8_bf16(*reinterpret_cast<const uint4*>(cs + i + half), sn);
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      o0[j] = __fsub_rn(__fmul_rn(a[j], c[j]), __fmul_rn(b[j], sn[j]));
+      o1[j] = __fadd_rn(__fmul_rn(b[j], c[j]), __fmul_rn(a[j], sn[j]));
+    }
+    *reinterpret_cast<uint4*>(v + i) = pack8_bf16(o0);
+    *reinterpret_cast<uint4*>(v + i + half) = pack8_bf16(o1);
+  }
+}
+
+// 8 consecutive intermediate columns of one row per thread: row blockIdx.y
+__global__ void act_mul_rows_v8_kernel(const uint16_t* __restrict__ gu, int inter, const uint16_t* __restrict__ table,
+                                       uint16_t* __restrict__ out) {
+  const int gi = blockIdx.x * blockDim.x + threadIdx.x;
+  if (gi >= (inter >> 3)) return;
+  const int64_t r = blockIdx.y;
+  const int i = 8 * gi;
+  const uint4 gw = *reinterpret_cast<const uint4*>(gu + r * 2 * inter + i);
+  float uf[8], o[8];
+  unpack8_bf16(*reinterpret_cast<const uint4*>(gu + r * 2 * inter + inter + i), uf);
+  const uint32_t g2[4] = {gw.x, gw.y, gw.z, gw.w};
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    const uint16_t gb = (uint16_t)((j & 1) ? (g2[j >> 1] >> 16) : (g2[j >> 1] & 0xffffu));
+    float act;
+    if (table) {
+      act = bf2f(spark_gelu_bf16(gb, table));
+    } else {
+      const float gf = bf2f(gb);
+      act = bf2f(f2bf(__fdiv_rn(gf, __fadd_rn(1.0f, spark_exp(-gf)))));
+    }
+    o[j] = __fmul_rn(act, uf[j]);
+  }
+  *reinterpret_cast<uint4*>(out + r * inter + i) = pack8_bf16(o);
+}
+
 // ------------------------------------------------------------------ slot mapping (integration/slot_mapping.py:8-22)
 __global__ void slot_mapping_kernel(int64_t n, int64_t max_tokens, const int32_t* __restrict__ query_start,
                                     const int64_t* __restrict__ positions, const int32_t* __restrict__ table,

@@ -646,6 +646,10 @@ int spark_add_rmsnorm_rows(const uint16_t* a, const uint16_t* b, const uint16_t*
                            int hidden, uint16_t* res_out, uint16_t* y, void* stream) {
   if (!a || !gamma || !y) return SPARK_ERR_INVALID_ARG;
   if (rows <= 0 || hidden <= 0 || hidden > 12288) return SPARK_ERR_UNSUPPORTED_SHAPE;
+  if (hidden % 8 == 0 && hidden <= 256 * 8 * kRowGroupsPerThread && aligned(a, 16) && (!b || aligned(b, 16)) &&
+      aligned(gamma, 16) && aligned(y, 16) && (!res_out || aligned(res_out, 16)))
+    return launch(add_rmsnorm_rows_v8_kernel, dim3((unsigned)rows), dim3(256), 0, as_stream(stream), a, b, gamma,
+                  eps, (float)(1.0 / (double)hidden), hidden, res_out, y);
   return launch(add_rmsnorm_rows_kernel, dim3((unsigned)rows), dim3(256), (size_t)(hidden + 8) * sizeof(float),
                 as_stream(stream), a, b, gamma, eps, (float)(1.0 / (double)hidden), hidden, res_out, y);
 }
@@ -656,6 +660,12 @@ int spark_rope_neox_rows(uint16_t* x, int64_t row_stride, int rows, int nh, int 
   if (rows <= 0 || nh <= 0 || head_dim <= 0 || rotary_dim <= 0 || rotary_dim > head_dim || rotary_dim % 2 ||
       pos0 < 0 || row_stride < (int64_t)nh * head_dim)
     return SPARK_ERR_UNSUPPORTED_SHAPE;
+  if (rotary_dim % 16 == 0 && head_dim % 8 == 0 && row_stride % 8 == 0 && aligned(x, 16) && aligned(cos_sin, 16)) {
+    const int64_t total8 = (int64_t)rows * nh * (rotary_dim / 16);
+    const int64_t grid8 = std::min<int64_t>((total8 + 255) / 256, 16LL * num_sms());
+    return launch(rope_rows_v8_kernel, dim3((unsigned)grid8), dim3(256), 0, as_stream(stream), x, row_stride, rows,
+                  nh, head_dim, rotary_dim, cos_sin, pos0);
+  }
   const int64_t total = (int64_t)rows * nh * (rotary_dim / 2);
   const int64_t grid = std::min<int64_t>((total + 255) / 256, 16LL * num_sms());
   return launch(rope_rows_kernel, dim3((unsigned)grid), dim3(256), 0, as_stream(stream), x, row_stride, rows, nh,
@@ -666,6 +676,9 @@ int spark_act_mul_rows(const uint16_t* gu, int rows, int inter, const uint16_t* 
                        void* stream) {
   if (!gu || !out) return SPARK_ERR_INVALID_ARG;
   if (rows <= 0 || inter <= 0) return SPARK_ERR_UNSUPPORTED_SHAPE;
+  if (inter % 8 == 0 && rows <= 65535 && aligned(gu, 16) && aligned(out, 16))
+    return launch(act_mul_rows_v8_kernel, dim3((unsigned)((inter / 8 + 255) / 256), (unsigned)rows), dim3(256), 0,
+                  as_stream(stream), gu, inter, gelu_table, out);
   const int64_t total = (int64_t)rows * inter;
   const int64_t grid = std::min<int64_t>((total + 255) / 256, 16LL * num_sms());
   return launch(act_mul_rows_kernel, dim3((unsigned)grid), dim3(256), 0, as_stream(stream), gu, (int64_t)rows,

@@ -135,11 +135,19 @@ def bench_attn(ctx, splits, reps, copies, device, gen, cfg):
         split(t)
         ops.attn_combine_out(po, pl, out)
 
+    counters = torch.zeros(nkv, device=device, dtype=torch.int32)
+
+    def fused(t):  # one launch: the last split of each kv head merges its heads
+        kc, vc, table = caches[t % copies]
+        ops.attn_decode_out(q, kc, vc, table, splits, T, scale, po, pl, counters, out, pos=pos)
+
     us_split = _time(split, reps)
     us_both = _time(both, reps)
+    us_fused = _time(fused, reps)
     byts = 2 * ctx * nkv * D * 2 + 2 * nq * D * 2
-    return {"us_split": round(us_split, 3), "us_split_combine": round(us_both, 3), "bytes": byts,
-            "gbs_split": round(byts / us_split / 1e3, 1), "gbs_split_combine": round(byts / us_both / 1e3, 1)}
+    return {"us_split": round(us_split, 3), "us_split_combine": round(us_both, 3), "us_fused": round(us_fused, 3),
+            "bytes": byts, "gbs_split": round(byts / us_split / 1e3, 1),
+            "gbs_split_combine": round(byts / us_both / 1e3, 1), "gbs_fused": round(byts / us_fused / 1e3, 1)}
 
 
 # ---------------------------------------------------------------- persistent-step stages

@@ -22,6 +22,8 @@ the first generated token.
 """
 from __future__ import annotations
 
+import warnings
+
 import torch
 import torch.nn.functional as F
 
@@ -31,13 +33,24 @@ BF16 = torch.bfloat16
 
 
 def _sdpa(q, K, V, scale, causal, mask=None):
-    """q [nq, n, D], K / V [nq, m, D] bf16 -> [nq, n, D]: a fused backend (flash, cuDNN,
-    memory-efficient) when one takes the shapes, else the math path."""
+    """q [nq, n, D], K / V [nkv, m, D] bf16 (nq a multiple of nkv) -> [nq, n, D]: a fused
+    backend (flash, cuDNN, memory-efficient) with grouped-query heads when one takes the
+    shapes, else the kv heads repeated for the fused backends, else the math path."""
     from torch.nn.attention import SDPBackend, sdpa_kernel
-    args = (q.unsqueeze(0).contiguous(), K.unsqueeze(0).contiguous(), V.unsqueeze(0).contiguous())
+    fused = [SDPBackend.FLASH_ATTENTION, SDPBackend.CUDNN_ATTENTION, SDPBackend.EFFICIENT_ATTENTION]
     kw = dict(is_causal=causal, scale=scale) if mask is None else dict(attn_mask=mask, scale=scale)
+    rep = q.shape[0] // K.shape[0]
+    if rep > 1:
+        try:
+            with sdpa_kernel(fused), warnings.catch_warnings():
+                warnings.simplefilter("ignore")  # (a backend that declines the shapes says why)
+                return F.scaled_dot_product_attention(q.unsqueeze(0), K.unsqueeze(0), V.unsqueeze(0),
+                                                      enable_gqa=True, **kw)[0]
+        except RuntimeError:
+            K, V = K.repeat_interleave(rep, 0), V.repeat_interleave(rep, 0)
+    args = (q.unsqueeze(0).contiguous(), K.unsqueeze(0).contiguous(), V.unsqueeze(0).contiguous())
     try:
-        with sdpa_kernel([SDPBackend.FLASH_ATTENTION, SDPBackend.CUDNN_ATTENTION, SDPBackend.EFFICIENT_ATTENTION]):
+        with sdpa_kernel(fused):
             return F.scaled_dot_product_attention(*args, **kw)[0]
     except RuntimeError:
         return F.scaled_dot_product_attention(*args, **kw)[0]
@@ -126,7 +139,6 @@ def prefill(eng, prompt: torch.Tensor, chunk: int = 2048, gemm: str = "q4") -> t
             else:
                 K = _gather(eng.k_cache[li], table, p1, bs)  # [nkv, p1, D]
                 V = _gather(eng.v_cache[li], table, p1, bs)
-            K, V = K.repeat_interleave(nq // nkv, 0), V.repeat_interleave(nq // nkv, 0)
             if p0 == 0 and (win == 0 or win >= n):  # plain causal: no mask
                 o = _sdpa(q.transpose(0, 1), K, V, scale, True)
             else:
@@ -149,14 +161,14 @@ def prefill(eng, prompt: torch.Tensor, chunk: int = 2048, gemm: str = "q4") -> t
     # LM head of the last position, greedy
     _, x = ops.add_rmsnorm_rows(a_last, b_last, w.final_norm, eps)
     logits = torch.empty(cfg.vocab_size, dtype=BF16, device=dev)
-    rows = 16384
-    for r0 in range(0, cfg.vocab_size, rows):
-        r1 = min(cfg.vocab_size, r0 + rows)
-        if getattr(w, "head_q6", None) is not None:
+    if getattr(w, "head_q6", None) is not None:  # Q6_K head: bf16 row chunks and matmul
+        rows = 16384
+        for r0 in range(0, cfg.vocab_size, rows):
+            r1 = min(cfg.vocab_size, r0 + rows)
             wt = ops.q6k_dequantize(w.head_q6[r0:r1].contiguous()).view(r1 - r0, h).to(BF16)
-        else:
-            wt = ops.q4_dequantize(w.head.qs[r0:r1].contiguous(), w.head.d[r0:r1].contiguous())
-        logits[r0:r1] = (x @ wt.t())[0]
+            logits[r0:r1] = (x @ wt.t())[0]
+    else:  # one position: the decode path's Q4_0 GEMV, not a dequantized copy of the head
+        ops.q4_gemv_out(x, w.head.qs, w.head.d, logits)
     eng.logits.copy_(logits)
     tok = torch.argmax(logits.float()).to(torch.int32).reshape(1)
     if gemm == "q4":

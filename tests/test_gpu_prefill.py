@@ -82,14 +82,15 @@ def test_prefill_row_kernels(cuda, oracle):
         assert np.array_equal(got[r, nh * D:], xs[r, nh * D:])  # the columns past the heads untouched
 
 
-def test_act_mul_rows_matches_decode_arithmetic(cuda, oracle):
+@pytest.mark.parametrize("i", [1024, 1020])  # 16-byte form, element form
+def test_act_mul_rows_matches_decode_arithmetic(cuda, oracle, i):
     """spark_act_mul_rows: bit for bit the oracle's SiLU * mul and GELU-table * mul (the
     decode epilogues' arithmetic), over gate values spanning every range of the table."""
     import numpy as np
     import torch
     from spark_b200 import ops, step
     g = torch.Generator(device="cuda").manual_seed(6)
-    n, i = 19, 1024
+    n = 19
     gu = (torch.randn((n, 2 * i), generator=g, device="cuda") *
           torch.exp2(torch.randint(-14, 9, (n, 2 * i), generator=g, device="cuda").float())).to(torch.bfloat16)
     u = gu.view(torch.int16).cpu().numpy().view(np.uint16)
