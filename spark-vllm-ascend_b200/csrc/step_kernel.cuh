@@ -1838,6 +1838,11 @@ __device__ __forceinline__ bool attn_split(const StepParams& P, const SparkStage
         }
       }
     }
+    if (tr) {  // trace: the q loads have returned (the clock read takes the last q value as input)
+      unsigned long long t;
+      asm volatile("mov.u64 %0, %%clock64;" : "=l"(t) : "f"(qf[3][15]));
+      tr[23] = t;
+    }
     const int bl = has_pos ? b - 1 : b;                  // ring tokens of the range: [a, bl)
     // ---- scores (a TPI-token step never crosses a 64-token run: t0 and a are multiples of TPI)
     int waited = -1;

@@ -52,7 +52,7 @@ def summarize(t: np.ndarray, kinds: list[str]) -> dict:
             ph.update({"ranges": c[has, 4] - c[has, 1], "merge": c[has, 5] - c[has, 4],
                        "publish": c[has, 6] - c[has, 5], "combine": c[has, 7] - c[has, 6],
                        "tail": c[has, 2] - c[has, 7]})
-            # SM-cycle checkpoints of thread 0 (clock64): q + scores, exp, P V, CTA barrier,
+            # SM-cycle checkpoints of thread 0 (clock64): q + scores (of which the q loads), exp, P V, CTA barrier,
             # merge factors, merge outputs; combine: loads, weights, accumulation, staging
             raw = d.setdefault("raw", {})
             names = ["cyc_q_scores", "cyc_exp", "cyc_pv", "cyc_bar", "cyc_fac", "cyc_merge_out"]
@@ -60,6 +60,9 @@ def summarize(t: np.ndarray, kinds: list[str]) -> dict:
                 ok = has & (c[:, 13 + q] > 0) & (c[:, 12 + q] > 0)
                 if ok.any():
                     raw.setdefault(nm, []).append(float(np.median(c[ok, 13 + q] - c[ok, 12 + q])))
+            ok = has & (c[:, 23] > 0) & (c[:, 12] > 0)  # q loads returned
+            if ok.any():
+                raw.setdefault("cyc_q_load", []).append(float(np.median(c[ok, 23] - c[ok, 12])))
             for q, nm in enumerate(["cyc_c_loads", "cyc_c_weights", "cyc_c_acc", "cyc_c_stage"]):
                 ok = has & (c[:, 19 + q] > 0) & (c[:, 18 + q] > 0) & (c[:, 19 + q] >= c[:, 18 + q])
                 if ok.any():
