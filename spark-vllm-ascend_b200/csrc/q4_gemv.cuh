@@ -35,11 +35,18 @@ namespace spark {
 //   xm  float2 [nb]:   (sx, C as int bits)
 constexpr float kStageMinMax = 7.888609052210118e-31f;  // 2^-100
 
-__device__ __forceinline__ void stage_block_q(const float (&v)[32], uint4* xq, float2* xm, int nb, int b) {
+// Stage block b (the canonical fixed point above) with its 32 elements spread over the 4
+// consecutive lanes of a quad (lane c: elements 8c .. 8c+7): every lane of the warp calls
+// it, a lane without a block with valid = false and zeros.  The maximum and the integer
+// sum are exact in any order, so the staged words do not depend on the split.
+__device__ __forceinline__ void stage_block_q4(const float (&v)[8], bool valid, uint4* xq, float2* xm, int nb, int b,
+                                               int c) {
   float M = 0.0f;
 #pragma unroll
-  for (int j = 0; j < 32; j++) M = fmaxf(M, fabsf(v[j]));
-  int X[32];
+  for (int j = 0; j < 8; j++) M = fmaxf(M, fabsf(v[j]));
+  M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 1));
+  M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 2));
+  int X[8];
   float sx = 1.0f;
   int sum = 0;
   if (M >= kStageMinMax && M != __int_as_float(0x7f800000)) {
@@ -47,29 +54,34 @@ __device__ __forceinline__ void stage_block_q(const float (&v)[32], uint4* xq, f
     const int S = 14 - e;
     const float sc = __uint_as_float((uint32_t)(S + 127) << 23);
 #pragma unroll
-    for (int j = 0; j < 32; j++) {
+    for (int j = 0; j < 8; j++) {
       X[j] = __float2int_rn(__fmul_rn(v[j], sc));
       sum += X[j];
     }
     sx = __uint_as_float((uint32_t)(127 - S) << 23);
   } else {
 #pragma unroll
-    for (int j = 0; j < 32; j++) X[j] = 0;
+    for (int j = 0; j < 8; j++) X[j] = 0;
   }
+  sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+  sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+  if (valid) {
+    // elements 4q .. 4q+3, q = 2c, 2c+1: word q (hi, lo halves) for q < 4, else the
+    // (hi, lo) halves of word q - 4 for elements 16 + 4 (q - 4) ..
 #pragma unroll
-  for (int w = 0; w < 4; w++) {
-    uint32_t hl = 0, ll = 0, hh = 0, lh = 0;
+    for (int t2 = 0; t2 < 2; t2++) {
+      const int q = 2 * c + t2;
+      uint32_t hi = 0, lo = 0;
 #pragma unroll
-    for (int t = 0; t < 4; t++) {
-      const int a = X[4 * w + t], c = X[16 + 4 * w + t];
-      hl |= (uint32_t)((a >> 8) & 0xff) << (8 * t);
-      ll |= (uint32_t)(a & 0xff) << (8 * t);
-      hh |= (uint32_t)((c >> 8) & 0xff) << (8 * t);
-      lh |= (uint32_t)(c & 0xff) << (8 * t);
+      for (int t = 0; t < 4; t++) {
+        const int a = X[4 * t2 + t];
+        hi |= (uint32_t)((a >> 8) & 0xff) << (8 * t);
+        lo |= (uint32_t)(a & 0xff) << (8 * t);
+      }
+      reinterpret_cast<uint2*>(xq + (q & 3) * nb + b)[q >> 2] = make_uint2(hi, lo);
     }
-    xq[w * nb + b] = make_uint4(hl, ll, hh, lh);
+    if (c == 0) xm[b] = make_float2(sx, __int_as_float(8 * sum));
   }
-  xm[b] = make_float2(sx, __int_as_float(8 * sum));
 }
 
 __device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
@@ -325,19 +337,28 @@ __device__ __forceinline__ void stage_x(const GemvArgs& g, unsigned char* smem, 
       uint4* xq = reinterpret_cast<uint4*>(smem + (size_t)bt * 72 * nb);
       float2* xm = reinterpret_cast<float2*>(smem + (size_t)bt * 72 * nb + 64 * nb);
       const uint4* src = reinterpret_cast<const uint4*>(g.x + (size_t)bt * k);
-      for (int b = tid; b < nb; b += nthreads) {
-        float v[32];
+      // item = 4 b + c: lane c of block b's quad (nthreads is a multiple of 32, so every
+      // lane of a warp takes the same number of rounds); the loads of 4 rounds first
+      for (int base = 0; base < 4 * nb; base += 4 * nthreads) {
+        uint4 u[4];
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-          const uint4 u = bt < g.batch ? src[b * 4 + i] : make_uint4(0, 0, 0, 0);
-          const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+        for (int rr = 0; rr < 4; rr++) {
+          const int item = base + rr * nthreads + tid;
+          u[rr] = (item < 4 * nb && bt < g.batch) ? src[item] : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int rr = 0; rr < 4; rr++) {
+          const int item = base + rr * nthreads + tid;
+          if (base + rr * nthreads >= 4 * nb) break;  // (warp-uniform)
+          float v[8];
+          const uint32_t w4[4] = {u[rr].x, u[rr].y, u[rr].z, u[rr].w};
 #pragma unroll
           for (int t = 0; t < 4; t++) {
-            v[8 * i + 2 * t] = bf_lo(w4[t]);
-            v[8 * i + 2 * t + 1] = bf_hi(w4[t]);
+            v[2 * t] = bf_lo(w4[t]);
+            v[2 * t + 1] = bf_hi(w4[t]);
           }
+          stage_block_q4(v, item < 4 * nb, xq, xm, nb, item >> 2, item & 3);
         }
-        stage_block_q(v, xq, xm, nb, b);
       }
     }
   } else {
@@ -375,16 +396,32 @@ __device__ __forceinline__ void stage_x(const GemvArgs& g, unsigned char* smem, 
     uint4* xq = reinterpret_cast<uint4*>(smem);
     float2* xm = reinterpret_cast<float2*>(smem + 64 * nb);
     const uint32_t* pg = reinterpret_cast<const uint32_t*>(g.gamma);
-    for (int b = tid; b < nb; b += nthreads) {
-      float v[32];
+    for (int base = 0; base < 4 * nb; base += 4 * nthreads) {  // 4 lanes per block, as above
+      uint32_t gw[4][4];  // gamma pairs of 4 rounds, loaded first
 #pragma unroll
-      for (int j = 0; j < 16; j++) {
-        const uint32_t gv = pg[b * 16 + j];
-        const float2 sv = reinterpret_cast<const float2*>(slin)[b * 16 + j];
-        v[2 * j] = bf2f(f2bf(__fmul_rn(__fmul_rn(sv.x, inv), bf_lo(gv))));
-        v[2 * j + 1] = bf2f(f2bf(__fmul_rn(__fmul_rn(sv.y, inv), bf_hi(gv))));
+      for (int rr = 0; rr < 4; rr++) {
+        const int item = base + rr * nthreads + tid;
+#pragma unroll
+        for (int j = 0; j < 4; j++) gw[rr][j] = item < 4 * nb ? pg[4 * item + j] : 0u;
       }
-      stage_block_q(v, xq, xm, nb, b);
+#pragma unroll
+      for (int rr = 0; rr < 4; rr++) {
+        const int item = base + rr * nthreads + tid;
+        if (base + rr * nthreads >= 4 * nb) break;  // (warp-uniform)
+        const bool valid = item < 4 * nb;
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          v[2 * j] = 0.0f;
+          v[2 * j + 1] = 0.0f;
+          if (valid) {
+            const float2 sv = reinterpret_cast<const float2*>(slin)[4 * item + j];
+            v[2 * j] = bf2f(f2bf(__fmul_rn(__fmul_rn(sv.x, inv), bf_lo(gw[rr][j]))));
+            v[2 * j + 1] = bf2f(f2bf(__fmul_rn(__fmul_rn(sv.y, inv), bf_hi(gw[rr][j]))));
+          }
+        }
+        stage_block_q4(v, valid, xq, xm, nb, item >> 2, item & 3);
+      }
     }
   }
   Pro::sync(nthreads);
