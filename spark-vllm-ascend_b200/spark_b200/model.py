@@ -232,8 +232,12 @@ class DecodeEngine:
             from . import step as _step
             self.ncta = _step.num_ctas()
             splits = splits or _step.attn_splits(cfg, self.ncta, max_seq_len)
-        if splits <= 0:  # auto: splits of at most 128 tokens (one K/V chunk), at least 16
-            splits = min(256, max(16, -(-max_seq_len // 128)))
+        if splits <= 0:
+            # auto (kernel chain): 16 splits while a split fits the wide attention kernel
+            # (at most 400 tokens: one CTA per split and kv head, the split's K / V in shared
+            # memory), measured best over ctx 2048 -> 6143 (16 / 24 / 49 splits: 650 / 596 /
+            # 546 tok/s); beyond, splits of at most 128 tokens (one K/V chunk)
+            splits = 16 if -(-max_seq_len // 16) <= 400 else min(256, max(16, -(-max_seq_len // 128)))
         self.splits = splits
         self.max_seq_len = max_seq_len
         bs = cfg.block_size
