@@ -34,8 +34,8 @@ Fixtures written next to this script:
   m = 4 (the tile heights the reference uses for qkv / o / gate_up and down,
   weights.py:62, 77).  ``pack`` asserts BF16-exact scales (weights.py:52), so the packed
   case uses blocks whose fp16 scales are bf16 values; the unpack case also covers the
-  seeded N(0, 0.02) weights quantized by gguf.  Needs the reference tree (path in
-  ``SPARK_REFERENCE_SRC``, default the mounted checkout); skipped when it is absent.
+  seeded N(0, 0.02) weights quantized by gguf.  Needs the reference tree: the ``src``
+  directory of its checkout in ``SPARK_REFERENCE_SRC``; skipped when that is unset.
 """
 from __future__ import annotations
 
@@ -152,8 +152,8 @@ def ref_pack_blocks(rng, n: int, k: int) -> np.ndarray:
 def make_ref_pack() -> bool:
     import os
     import sys
-    src = os.environ.get("SPARK_REFERENCE_SRC", "/root/reference/src")
-    if not Path(src, "spark_vllm_ascend", "integration", "weights.py").exists():
+    src = os.environ.get("SPARK_REFERENCE_SRC", "")
+    if not src or not Path(src, "spark_vllm_ascend", "integration", "weights.py").exists():
         print("reference tree not found: ref_pack_q4.npz not regenerated")
         return False
     sys.path.insert(0, src)
