@@ -624,6 +624,20 @@ def run_reference(args):
     }
 
 
+def resolve_mode(args, world: int) -> str:
+    """The engine of ``--mode auto``: the kernel chain for one batch-1 sequence of the
+    synthetic 4B model on one GPU whose context fits 16 splits of the wide attention kernel
+    (at most 400 tokens each; the chain engine's own split rule there), else the
+    persistent step (tensor parallelism, small batches and the Spark features run only
+    there).  An explicit ``--mode step|kernels`` is kept."""
+    if args.mode != "auto":
+        return args.mode
+    max_seq = args.prompt + max(args.steps, args.warmup) + 1
+    chain = (world == 1 and args.tp == 1 and args.batch == 1 and args.model == "synthetic-4b"
+             and -(-max_seq // 16) <= 400 and args.splits in (0, 16))
+    return "kernels" if chain else "step"
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -654,11 +668,7 @@ def main(argv=None):
     args = ap.parse_args(argv)
     if args.tp == 0:  # the multi-GPU bench measures tensor parallelism, not replicas
         args.tp = int(os.environ.get("WORLD_SIZE", "1"))
-    if args.mode == "auto":
-        max_seq = args.prompt + max(args.steps, args.warmup) + 1
-        chain = (int(os.environ.get("WORLD_SIZE", "1")) == 1 and args.tp == 1 and args.batch == 1
-                 and args.model == "synthetic-4b" and -(-max_seq // 16) <= 400 and args.splits in (0, 16))
-        args.mode = "kernels" if chain else "step"
+    args.mode = resolve_mode(args, int(os.environ.get("WORLD_SIZE", "1")))
     global PROMPT_LEN
     PROMPT_LEN = args.prompt
     if args.warmup < 3:

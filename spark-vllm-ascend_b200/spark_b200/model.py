@@ -189,6 +189,17 @@ def _vp(t):
     return None if t is None else ctypes.c_void_p(t.data_ptr())
 
 
+def chain_splits(max_seq_len: int) -> int:
+    """Attention splits of the kernel chain for contexts up to ``max_seq_len``: 16 while a
+    split fits the wide attention kernel (at most 400 tokens: one CTA per split and kv
+    head, the split's K / V in shared memory), measured best over ctx 2048 -> 6143 (16 / 24
+    / 49 splits: 650 / 596 / 546 tok/s); beyond, splits of at most 128 tokens (one K/V
+    chunk), 16 to 256 of them."""
+    if -(-max_seq_len // 16) <= 400:
+        return 16
+    return min(256, max(16, -(-max_seq_len // 128)))
+
+
 class DecodeEngine:
     """Batch-1 greedy decode of the synthetic model with a paged BF16 KV cache.
 
@@ -233,11 +244,7 @@ class DecodeEngine:
             self.ncta = _step.num_ctas()
             splits = splits or _step.attn_splits(cfg, self.ncta, max_seq_len)
         if splits <= 0:
-            # auto (kernel chain): 16 splits while a split fits the wide attention kernel
-            # (at most 400 tokens: one CTA per split and kv head, the split's K / V in shared
-            # memory), measured best over ctx 2048 -> 6143 (16 / 24 / 49 splits: 650 / 596 /
-            # 546 tok/s); beyond, splits of at most 128 tokens (one K/V chunk)
-            splits = 16 if -(-max_seq_len // 16) <= 400 else min(256, max(16, -(-max_seq_len // 128)))
+            splits = chain_splits(max_seq_len)
         self.splits = splits
         self.max_seq_len = max_seq_len
         bs = cfg.block_size
