@@ -81,3 +81,12 @@ def test_host_validation_rejects_bad_shapes_before_launch(libpath):
     assert L.spark_attn_splitkv(*args, 32, 4, 128, 128, 16, 256, ctypes.c_float(0.1), fake, fake, None, None) == 2
     assert L.spark_attn_splitkv(*args, 32, 8, 128, 128, 16, 4096, ctypes.c_float(0.1), fake, fake, None, None) == 5
     assert L.spark_slot_mapping(10, 5, fake, fake, fake, 128, fake, None) == 2
+    # tensor-core prefill GEMM: K a multiple of 256, 16-byte aligned x / qs / d, a status word
+    err = ctypes.c_void_p(0x2000)
+    assert L.spark_q4_gemm_tc(fake, fake, fake, fake, 4, 128, 320, err, -1, None) == 2
+    assert L.spark_q4_gemm_tc(fake, fake, fake, fake, 0, 128, 256, err, -1, None) == 2
+    assert L.spark_q4_gemm_tc(fake, fake, fake, fake, 4, 128, 256, None, -1, None) == 1
+    assert L.spark_q4_gemm_tc(fake, fake, ctypes.c_void_p(0x1008), fake, 4, 128, 256, err, -1, None) == 3
+    # prefill row kernels: shapes
+    assert L.spark_add_rmsnorm_rows(fake, None, fake, ctypes.c_float(1e-6), 4, 16384, None, fake, None) == 2
+    assert L.spark_act_mul_rows(fake, 0, 64, None, fake, None) == 2
